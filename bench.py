@@ -1,0 +1,386 @@
+"""Benchmark: routed sparse attention (router + block-sparse attention) for one chunk-layer.
+
+Workload (config 2): a 4680-query chunk against a 32760-token KV window, 12 heads, D=128,
+64-token router blocks, 25% block density (74 forced current-chunk blocks + 54 routed),
+seeded N(0,1) bf16 Q/K/V, N(0,1/128) router weights. One step = router + attention on inputs
+already resident in HBM. Two input sets alternate (215 MB each, larger than the 126 MB L2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N>1 runs under torchrun: every rank processes its own stream (weak scaling, no collective on
+the data path); ``value`` is the sum over ranks of effective FLOPs / the slowest rank's time.
+``--impl reference`` times the CPU restatement of the reference's path (oracle/) on the host
+cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+LQ, LK, H, D, BLOCK, DENSITY = 4680, 32760, 12, 128, 64, 0.25
+WORKLOAD = "config2 chunk-layer: 4680 q x 32760 KV tokens, 12 heads, D=128, block 64, 25% density, router+attention"
+METRIC = "routed sparse-attn effective TFLOP/s per chunk-layer (router + block-sparse attention)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", "attention_sm100_config2.md")
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+def make_inputs(seed: int, device):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn((LQ, H, D), generator=g).bfloat16()
+    k = torch.randn((LK, H, D), generator=g).bfloat16()
+    v = torch.randn((LK, H, D), generator=g).bfloat16()
+    wq = torch.randn((H, D, 64), generator=g) / math.sqrt(D)
+    wk = torch.randn((H, D, 64), generator=g) / math.sqrt(D)
+    if device is None:
+        return q, k, v, wq, wk
+    return tuple(t.to(device) for t in (q, k, v, wq, wk))
+
+
+def effective_flops(ids: np.ndarray, Lq: int = LQ, Lk: int = LK, block: int = BLOCK) -> float:
+    """4*D*sum over heads and query rows of the valid tokens in the row's selected blocks."""
+    valid = np.minimum(block, Lk - np.arange(math.ceil(Lk / block)) * block)
+    tok = np.where(ids >= 0, valid[np.clip(ids, 0, None)], 0).sum(-1)          # [H, qb]
+    rows = np.minimum(block, Lq - np.arange(ids.shape[1]) * block)             # [qb]
+    return float(4 * D * (tok * rows[None]).sum())
+
+
+class ClockSampler:
+    """NVML SM clock / throttle-reason samples taken while the timed region runs (read only)."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(0.002)
+
+    def sample(self):
+        if self.nvml is None:
+            return
+        try:
+            self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+            bits = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for b, name in self.REASONS.items():
+                if bits & b:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def __enter__(self):
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self.t.join()
+        self.sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU baseline (the oracle restatement of the reference's path, timed on the host cores)
+# ----------------------------------------------------------------------------------------------
+
+class CpuPort:
+    """The CPU restatement of the reference's path (oracle/: exact-fp32 C router + fp32 numpy
+    gather-softmax attention) on the config-2 workload, run on the host cores."""
+
+    def __init__(self):
+        import sys
+        sys.path.insert(0, ROOT)
+        from oracle import oracle as o
+        self.o = o
+        self.threads = len(os.sched_getaffinity(0))
+        q, k, v, wq, wk = make_inputs(0, None)
+        self.q, self.k, self.v = (t.float().numpy() for t in (q, k, v))
+        self.wq, self.wk = wq.numpy(), wk.numpy()
+        self.extra = o.budget(512, 74, density=DENSITY)
+        self.ids = None
+        self.order = None
+        self.pos = 0
+
+    def route(self) -> float:
+        t0 = time.perf_counter()
+        r = self.o.route(self.q, self.k, self.wq, self.wk, BLOCK, self.extra)
+        dt = time.perf_counter() - t0
+        self.ids = r["ids"]
+        if self.order is None:
+            self.order = [(h, i) for i in range(self.ids.shape[1]) for h in range(H)]
+            np.random.default_rng(0).shuffle(self.order)
+        return dt
+
+    def attend(self, seconds: float = 1e9, max_pairs: int | None = None):
+        """Attention over (head, query block) pairs until the budget is spent -> (flops, s, pairs)."""
+        flops, t_att, done = 0.0, 0.0, 0
+        while t_att < seconds and (max_pairs is None or done < max_pairs):
+            h, i = self.order[self.pos % len(self.order)]
+            self.pos += 1
+            t1 = time.perf_counter()
+            r0, r1 = i * BLOCK, min(LQ, (i + 1) * BLOCK)
+            self.o.attention_block(self.q, self.k, self.v, self.ids[h, i], h, r0, r1, BLOCK, 1.0 / math.sqrt(D),
+                                   dtype=np.float32)
+            t_att += time.perf_counter() - t1
+            sub = np.full_like(self.ids, -1)
+            sub[h, i] = self.ids[h, i]
+            flops += effective_flops(sub)
+            done += 1
+        return flops, t_att, done
+
+    def charged(self, flops, t_att, pairs, t_router):
+        """Time charged to a sample: its attention plus the router pro rata to its rows."""
+        t = t_att + t_router * pairs / len(self.order)
+        return flops / t / 1e12, t
+
+
+def cpu_baseline(seconds: float):
+    port = CpuPort()
+    t_router = port.route()
+    flops, t_att, pairs = port.attend(seconds=seconds)
+    val, _ = port.charged(flops, t_att, pairs, t_router)
+    return {"value": val, "unit": "TFLOP/s", "cores": port.threads, "kind": "port",
+            "sample": f"{pairs} (head, query-block) pairs of config 2 ({t_att:.1f} s of fp32 numpy attention) plus "
+                      f"the exact-fp32 C router charged pro rata ({t_router:.2f} s per full chunk-layer)"}
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    port = CpuPort()
+    times, vals = [], []
+    for s in range(args.warmup + args.steps):
+        t_router = port.route()
+        flops, t_att, pairs = port.attend(max_pairs=args.ref_pairs)
+        val, t = port.charged(flops, t_att, pairs, t_router)
+        if s >= args.warmup:
+            times.append(t)
+            vals.append(val)
+    value = statistics.median(vals)
+    sample = (f"per step: the full C router + {args.ref_pairs} (head, query-block) pairs of config-2 attention "
+              f"(fp32 numpy), router time charged pro rata")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "parallelism": "rank 0 host cores"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": port.threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ----------------------------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch.distributed as dist
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib_ok = ops.attention_max_ids(LK, BLOCK) >= 128
+    assert lib_ok
+    sets = [make_inputs(1000 * rank + s, dev) for s in range(2)]
+    extra = RouterConfig(density=DENSITY).extra(LQ, LK)
+    ws = ops.Workspace()
+    n_ids = ops.forced_count(LQ, LK, BLOCK) + extra
+    ids_buf = [torch.empty((H, math.ceil(LQ / BLOCK), n_ids), dtype=torch.int32, device=dev) for _ in sets]
+    out = torch.empty((LQ, H, D), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(s, ev=None):
+        q, k, v, wq, wk = sets[s]
+        if ev is not None:
+            ev[0].record(stream)
+        ops.route(q, k, wq, wk, block=BLOCK, extra=extra, workspace=ws, out=ids_buf[s])
+        if ev is not None:
+            ev[1].record(stream)
+        ops.sparse_attention(q, k, v, ids_buf[s], block=BLOCK, out=out)
+        if ev is not None:
+            ev[2].record(stream)
+
+    for s in range(max(3, args.warmup)):
+        step(s % 2)
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    flops = [effective_flops(b.cpu().numpy()) for b in ids_buf]
+    # router FLOPs (reported separately): pooled projections + block-score GEMM
+    qb, kb = math.ceil(LQ / BLOCK), math.ceil(LK / BLOCK)
+    router_flops = 2 * H * qb * kb * 64 + 2 * H * (qb + kb) * D * 64
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else 0) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            step(i % 2, evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    att_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    rt_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    my_flops = sum(flops[i % 2] for i in range(args.steps))
+    t = torch.tensor([elapsed_ms, my_flops], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm[1:], op=dist.ReduceOp.SUM)
+        elapsed_ms, total_flops = float(mx[0]), float(sm[1])
+    else:
+        total_flops = my_flops
+    value = total_flops / (elapsed_ms * 1e-3) / 1e12
+
+    # ---- e2e: the public plugin call with host buffers (pinned), copies inside the timed region
+    sparse = SparseAttention(sets[0][3], sets[0][4], RouterConfig(density=DENSITY), workspace=ws)
+    host = [tuple(t.cpu().pin_memory() for t in s_[:3]) for s_ in sets]
+    dev_in = [tuple(torch.empty_like(t) for t in s_[:3]) for s_ in sets]
+    host_out = torch.empty((1, LQ, H, D), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step(s):
+        for dst, src in zip(dev_in[s], host[s]):
+            dst.copy_(src, non_blocking=True)
+        q, k, v = dev_in[s]
+        res = sparse(q[None], k[None], v[None])
+        host_out.copy_(res, non_blocking=True)
+
+    for s in range(2):
+        e2e_step(s)
+    torch.cuda.synchronize()
+    e_steps = max(3, min(args.steps, 20))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(e_steps):
+        e2e_step(i % 2)
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    e2e_flops = sum(flops[i % 2] for i in range(e_steps))
+    te = torch.tensor([e2e_ms, e2e_flops], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = te.clone()
+        dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
+        sm = te.clone()
+        dist.all_reduce(sm[1:], op=dist.ReduceOp.SUM)
+        e2e_ms, e2e_flops = float(mx[0]), float(sm[1])
+    e2e_value = e2e_flops / (e2e_ms * 1e-3) / 1e12
+
+    if rank != 0:
+        return
+    peak, hbm, peak_kind = peaks()
+    att_avg = statistics.mean(att_ms)
+    achieved = (sum(flops) / 2) / (att_avg * 1e-3) / 1e12
+    traffic = profiled_traffic()
+    cpu = None if args.no_cpu_baseline else cpu_baseline(args.cpu_seconds)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "parallelism": f"streams x{world} (one replica per GPU)",
+                   "l2": "2 alternating input sets of 215 MB each (> 126 MB L2)", "density": DENSITY,
+                   "blocks_per_query_block": n_ids},
+        "us_per_chunk_layer": 1e3 * elapsed_ms / args.steps,
+        "attention_us": 1e3 * att_avg, "router_us": 1e3 * statistics.mean(rt_ms),
+        "effective_gflop_per_chunk_layer": statistics.mean(flops) / 1e9,
+        "router_gflop_per_chunk_layer": router_flops / 1e9,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "ss::attn::sparse_attention_kernel"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output"},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-pairs", type=int, default=48)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+/*
+ * ssparse.h -- C ABI of libssparse.so, the sm_100a routed block-sparse attention path for
+ * streaming (chunk-autoregressive) Wan-DiT video diffusion.
+ *
+ * Conventions shared by every entry point
+ *   - Plain pointers to device memory, sizes as int / int64_t, a cudaStream_t passed as void*.
+ *     No torch types cross this boundary.
+ *   - The caller allocates every buffer (inputs, outputs, workspace). The library never allocates,
+ *     frees or synchronises; work is enqueued on the caller's stream, so every entry point can be
+ *     captured into a CUDA graph once ss_prepare_device() has run on that device.
+ *   - Return value: 0 on success, a cudaError_t value (< 1000) if a CUDA call failed, or one of
+ *     the SS_ERR_* codes below for invalid arguments (checked on the host before any launch).
+ *   - Device-side faults (non-finite router score, a pipeline wait that timed out) are reported
+ *     by OR-ing SS_DEV_* bits into an optional device int (`status`), which the caller reads when
+ *     it chooses to synchronise. Kernels never trap.
+ *   - Layouts: one batch element (B = 1, as in the reference); token-major activations
+ *     q[Lq][H][D], k/v[Lk][H][D] in bf16 with row stride H*D elements; D = 128.
+ *
+ * Reference interfaces replaced (paths are inside the jurky123/streaming_sparse repository):
+ *   ss_router      <- project (migration/unified_router/opt8/projection.py:11-14),
+ *                     prototype pooling segment (migration/unified_router/opt19/prototype.py:43-49),
+ *                     block-score GEMM _coarse + top-k _top (migration/unified_router/opt16/route.py:34-55,
+ *                     route() :90-113), forced-set policy (local_experiments/video_runtime_v1/
+ *                     pipeline_graph.py:140-151) and fixed_page_select (local_experiments/
+ *                     video_runtime_v1/fixed_page_select.py:34-41)
+ *   ss_attention   <- exact(q,k,v,ids,workspace) (local_experiments/video_runtime_v1/attention.py:15-24)
+ *                     wrapping _attn_fwd (local_experiments/gap_exact_round_kernel.py:4-137), and the
+ *                     sm_80 C ABI `run` (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:407-409)
+ *   ss_lse_merge   <- merge (local_experiments/video_runtime_v1/attention.py:40-45),
+ *                     _merge_restore (migration/unified_router/opt21/attention.py:7-15)
+ *   ss_cache_append<- the cache roll + write in CausalWanSelfAttention.forward
+ *                     (wan/modules/causal_model.py:216-246) and commit_fixed15
+ *                     (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:453-458)
+ */
+#ifndef SSPARSE_H_
+#define SSPARSE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* host-side argument errors */
+#define SS_ERR_SHAPE 1001       /* inconsistent or unsupported sizes */
+#define SS_ERR_POINTER 1002     /* null or misaligned pointer */
+#define SS_ERR_WORKSPACE 1003   /* workspace too small */
+#define SS_ERR_BUDGET 1004      /* extra > number of unforced blocks */
+#define SS_ERR_SMEM 1005        /* the id lists do not fit the attention kernel's shared memory */
+#define SS_ERR_DRIVER 1006      /* cuTensorMapEncodeTiled unavailable or failed */
+
+/* device-side status bits (OR-ed into *status) */
+#define SS_DEV_NONFINITE 0x1    /* a router score was NaN or +-inf */
+#define SS_DEV_TIMEOUT 0x2      /* an mbarrier wait in the attention kernel ran out of budget */
+#define SS_DEV_BADID 0x4        /* a block id in the LUT was out of range */
+
+/* Library version (major*100 + minor). */
+int ss_version(void);
+
+/* One-time per-device setup (kernel attributes such as the dynamic shared memory size).
+   Call once per device before capturing any ss_* call into a CUDA graph. Idempotent. */
+int ss_prepare_device(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Router: mean-pooled query/key blocks -> per-head projections -> block scores -> top-k.       */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Bytes of workspace ss_router needs for these sizes (R = projection width, 64 in the reference). */
+int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes);
+
+/* Route one chunk-layer.
+ *   q       [Lq][H][128] bf16, the current chunk's queries (RoPE applied)
+ *   k       [Lk][H][128] bf16, the visible KV window; its last Lq rows are the current chunk
+ *   wq, wk  [H][128][R] fp32 per-head projections
+ *   block   query/KV block size in tokens (64 or 128); last blocks may be partial
+ *   sink_tokens  tokens at the start of the window that are always kept (0 = no sink)
+ *   extra   number of blocks chosen by score per query block, outside the forced set
+ *   ids     [H][qb][n_ids] int32 out, ascending block ids; n_ids must equal forced + extra
+ *           (forced = blocks overlapping [0, sink_tokens) or [Lk-Lq, Lk))
+ *   mask    [H][qb][kb] uint8 out (optional, may be NULL): 1 where a block is selected
+ *   scores  [H][qb][kb] fp32 out (optional, may be NULL): the block scores
+ * Scores are computed in exact fp32 with a fixed summation order (sequential token sums, one
+ * divide by the valid count, fmaf in ascending index order), -0 is canonicalised to +0, and
+ * ties go to the lower block index, so the ids are bit-identical to the CPU oracle. */
+int ss_router(const void *q, const void *k, const float *wq, const float *wk,
+              int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
+              int32_t *ids, int n_ids, uint8_t *mask, float *scores,
+              void *workspace, size_t workspace_bytes, int *status, void *stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Block-sparse attention (tcgen05 / TMEM / TMA, sm_100a).                                     */
+/* ------------------------------------------------------------------------------------------ */
+
+/* out[t][h][:] = softmax(q[t,h,:] . K_sel^T * scale) V_sel over the valid tokens of the blocks
+ * listed for t's query block in ids[h][t / block][0..n_ids) (ascending or not; entries < 0 are
+ * ignored). out_dtype: 0 = bf16, 1 = fp32. lse (optional): [H][Lq] fp32 natural-log
+ * log-sum-exp of the scaled scores. */
+int ss_attention(const void *q, const void *k, const void *v, const int32_t *ids,
+                 int H, int Lq, int Lk, int block, int n_ids, float scale,
+                 void *out, int out_dtype, float *lse, int *status, void *stream);
+
+/* Largest n_ids ss_attention accepts for these sizes (its block lists live in shared memory). */
+int ss_attention_max_ids(int Lk, int block, int *max_ids);
+
+/* ------------------------------------------------------------------------------------------ */
+/* Log-sum-exp merge of partial attention results.                                             */
+/* ------------------------------------------------------------------------------------------ */
+
+/* o_parts [P][Lq][H][128] fp32, lse_parts [P][H][Lq] fp32 (natural log; -inf = empty part).
+ * out [Lq][H][128] (out_dtype 0 = bf16, 1 = fp32) = sum_p exp(lse_p - L) o_p with
+ * L = logsumexp_p lse_p; lse_out [H][Lq] (optional) = L. */
+int ss_lse_merge(const float *o_parts, const float *lse_parts, int P, int H, int Lq,
+                 void *out, int out_dtype, float *lse_out, void *stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* KV cache append / evict.                                                                    */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Apply one chunk write to a [cap][H][128] bf16 K/V cache with the rolling-window semantics of
+ * CausalWanSelfAttention (sink kept, oldest non-sink tokens evicted by a left shift):
+ *   local_attn      nonzero if the model uses a local window (eviction enabled)
+ *   global_end, local_end  the cache's index state before the write
+ *   current_start, n_new   the chunk's absolute start token and length
+ *   sink_tokens     sink length in tokens
+ *   k_new, v_new    [n_new][H][128] bf16 with token stride new_stride (elements)
+ *   out_local_end   receives the new local end index (the window is [max(0,end-W), end))
+ * The shift moves rows in chunks no longer than the eviction distance, so it never reads a row
+ * that an earlier chunk of the same call has overwritten. All stores are 16-byte vectors. */
+int ss_cache_append(void *k_cache, void *v_cache, int cap, int H,
+                    const void *k_new, const void *v_new, int64_t new_stride, int n_new,
+                    int local_attn, int64_t global_end, int64_t local_end,
+                    int64_t current_start, int sink_tokens, int64_t *out_local_end,
+                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSPARSE_H_ */

@@ -1,0 +1,250 @@
+"""CPU oracle for the routed sparse-attention path -- TEST INFRASTRUCTURE, never the product.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import this
+module, and only as the checker / timed CPU baseline. The package ``streaming_sparse_b200``
+never imports it and has no CPU fallback.
+
+Pieces and the reference code each one restates (paths inside jurky123/streaming_sparse):
+
+* ``route``: exact-fp32 router in C (``ssparse_oracle.c``): block pooling
+  (migration/unified_router/opt19/prototype.py:11-49), projection (opt8/projection.py:4-14),
+  block-score GEMM (opt16/route.py:34-47), forced sink/current set
+  (local_experiments/video_runtime_v1/pipeline_graph.py:140-151), top-k with lower-index ties
+  (streaming_sparse/v05/primitives.py:35-56).
+* ``attention``: gather-softmax over the selected blocks' valid tokens, float64
+  (streaming_sparse/v08/attention.py:115-123 ``reference``; the page gather of
+  local_experiments/review_v1/runtime.py:106-121 ``SelectedAttention.fixed``); natural-log LSE as
+  returned by ``exact`` (local_experiments/video_runtime_v1/attention.py:15-24).
+* ``lse_merge``: local_experiments/video_runtime_v1/attention.py:40-45 ``merge`` generalised to
+  P parts (migration/unified_router/opt21/attention.py:7-15).
+* ``cache_append``: the roll + write of CausalWanSelfAttention.forward
+  (wan/modules/causal_model.py:216-253).
+
+Parity pins: tests/golden/ holds vectors produced by the reference's own pure-torch functions
+(script ``tests/golden/make_golden.py``); ``tests/test_oracle.py`` checks this module against
+them before any GPU result is compared with it.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+from functools import lru_cache
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "libssoracle.so")
+SRC = os.path.join(HERE, "ssparse_oracle.c")
+
+
+def build(force: bool = False) -> str:
+    """Compile the C restatement (strict IEEE fp32: no contraction, no fast-math)."""
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(SRC):
+        tmp = LIB + ".tmp"
+        subprocess.run(["gcc", "-O2", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
+                        "-o", tmp, SRC, "-lm"], check=True)
+        os.replace(tmp, LIB)
+    return LIB
+
+
+@lru_cache(None)
+def _lib():
+    lib = ctypes.CDLL(build())
+    P = ctypes.c_void_p
+    i, i64 = ctypes.c_int, ctypes.c_int64
+    lib.oracle_pool_project.argtypes = [P, i64, i, i, i, i, i, P, P, P]
+    lib.oracle_pool_project.restype = i
+    lib.oracle_scores.argtypes = [P, P, i, i, i, i, P]
+    lib.oracle_scores.restype = i64
+    lib.oracle_forced.argtypes = [i, i, i, i, P]
+    lib.oracle_forced.restype = i
+    lib.oracle_select.argtypes = [P, i, i, i, P, i, P, i, P]
+    lib.oracle_select.restype = i
+    return lib
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """Round float32 values to bfloat16 (round-to-nearest-even) and return them as float32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def nblocks(n: int, block: int) -> int:
+    return (n + block - 1) // block
+
+
+# ----------------------------------------------------------------------------------------------
+# router
+# ----------------------------------------------------------------------------------------------
+
+def pool_project(x: np.ndarray, w: np.ndarray, block: int):
+    """x [L,H,D] fp32 (bf16 values), w [H,D,R] fp32 -> (pooled [H,nb,D], proj [H,nb,R])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    L, H, D = x.shape
+    R = w.shape[2]
+    nb = nblocks(L, block)
+    pooled = np.empty((H, nb, D), np.float32)
+    proj = np.empty((H, nb, R), np.float32)
+    rc = _lib().oracle_pool_project(_ptr(x), H * D, L, H, D, R, block, _ptr(w), _ptr(pooled), _ptr(proj))
+    if rc:
+        raise MemoryError("oracle_pool_project failed")
+    return pooled, proj
+
+
+def scores(qh: np.ndarray, kh: np.ndarray):
+    """qh [H,qb,R], kh [H,kb,R] -> (S [H,qb,kb] fp32, number of non-finite scores)."""
+    qh = np.ascontiguousarray(qh, dtype=np.float32)
+    kh = np.ascontiguousarray(kh, dtype=np.float32)
+    H, qb, R = qh.shape
+    kb = kh.shape[1]
+    S = np.empty((H, qb, kb), np.float32)
+    bad = _lib().oracle_scores(_ptr(qh), _ptr(kh), H, qb, kb, R, _ptr(S))
+    return S, int(bad)
+
+
+def forced_blocks(Lq: int, Lk: int, block: int, sink_tokens: int = 0) -> np.ndarray:
+    kb = nblocks(Lk, block)
+    f = np.zeros(kb, np.uint8)
+    _lib().oracle_forced(Lq, Lk, block, sink_tokens, _ptr(f))
+    return f
+
+
+def select(S: np.ndarray, forced: np.ndarray, extra: int):
+    """Top-`extra` unforced blocks per row plus the forced set -> (ids ascending, mask)."""
+    S = np.ascontiguousarray(S, dtype=np.float32)
+    forced = np.ascontiguousarray(forced, dtype=np.uint8)
+    H, qb, kb = S.shape
+    n_ids = int(forced.sum()) + extra
+    ids = np.empty((H, qb, n_ids), np.int32)
+    mask = np.empty((H, qb, kb), np.uint8)
+    rc = _lib().oracle_select(_ptr(S), H, qb, kb, _ptr(forced), extra, _ptr(ids), n_ids, _ptr(mask))
+    if rc:
+        raise ValueError(f"oracle_select rejected extra={extra} (forced={int(forced.sum())}, kb={kb})")
+    return ids, mask.astype(bool)
+
+
+def route(q, k, wq, wk, block: int, extra: int, sink_tokens: int = 0):
+    """Full router: returns dict(ids, mask, scores, qh, kh, nonfinite)."""
+    Lq, Lk = q.shape[0], k.shape[0]
+    _, qh = pool_project(q, wq, block)
+    _, kh = pool_project(k, wk, block)
+    S, bad = scores(qh, kh)
+    f = forced_blocks(Lq, Lk, block, sink_tokens)
+    ids, mask = select(S, f, extra)
+    return dict(ids=ids, mask=mask, scores=S, qh=qh, kh=kh, nonfinite=bad, forced=f)
+
+
+def budget(kb: int, nforced: int, *, topk: int | None = None, density: float | None = None,
+           rule: str = "total") -> int:
+    """Number of score-chosen blocks per query block.
+
+    * ``topk``: a fixed count outside the forced set (config 1: 24).
+    * ``density`` with rule ``"total"``: the row keeps ceil(density*kb) blocks in all, forced
+      ones included (config 2).
+    * ``density`` with rule ``"rest"``: floor(density*(kb - forced)) extra blocks, the
+      ``chunk_history10`` policy of local_experiments/video_runtime_v1/pipeline_graph.py:143-146.
+    """
+    if topk is not None:
+        extra = topk
+    elif rule == "total":
+        extra = math.ceil(density * kb) - nforced
+    elif rule == "rest":
+        extra = math.floor(density * (kb - nforced))
+    else:
+        raise ValueError(rule)
+    return max(0, min(extra, kb - nforced))
+
+
+# ----------------------------------------------------------------------------------------------
+# attention
+# ----------------------------------------------------------------------------------------------
+
+def selected_tokens(ids_row: np.ndarray, Lk: int, block: int) -> np.ndarray:
+    blocks = np.unique(ids_row[ids_row >= 0])
+    tok = (blocks[:, None] * block + np.arange(block)[None, :]).reshape(-1)
+    return tok[tok < Lk]
+
+
+def attention_block(q, k, v, ids_row, h: int, r0: int, r1: int, block: int, scale: float, dtype=np.float64):
+    """One (head, query block): rows [r0, r1) of head h against the valid tokens of ids_row."""
+    tok = selected_tokens(ids_row, k.shape[0], block)
+    if len(tok) == 0:
+        n = r1 - r0
+        return np.zeros((n, q.shape[2]), dtype), np.full(n, -np.inf, dtype)
+    kk = np.asarray(k[tok, h, :], dtype)
+    vv = np.asarray(v[tok, h, :], dtype)
+    z = (np.asarray(q[r0:r1, h, :], dtype) @ kk.T) * dtype(scale)
+    m = z.max(axis=1, keepdims=True)
+    p = np.exp(z - m)
+    s = p.sum(axis=1, keepdims=True)
+    return (p @ vv) / s, (m + np.log(s))[:, 0]
+
+
+def attention(q, k, v, ids, block: int, scale: float | None = None, dtype=np.float64,
+              heads=None, qblocks=None):
+    """Gather-softmax attention. q [Lq,H,D], k/v [Lk,H,D], ids [H,qb,K] (entries <0 ignored).
+
+    Returns (out [Lq,H,D], lse [H,Lq]) in ``dtype``; rows of skipped heads/qblocks are NaN,
+    rows whose list is empty are 0 with LSE -inf.
+    """
+    Lq, H, D = q.shape
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    qb = nblocks(Lq, block)
+    out = np.full((Lq, H, D), np.nan, dtype)
+    lse = np.full((H, Lq), np.nan, dtype)
+    for h in (range(H) if heads is None else heads):
+        for i in (range(qb) if qblocks is None else qblocks):
+            r0, r1 = i * block, min(Lq, (i + 1) * block)
+            out[r0:r1, h, :], lse[h, r0:r1] = attention_block(q, k, v, ids[h, i], h, r0, r1, block, scale, dtype)
+    return out, lse
+
+
+def lse_merge(o_parts: np.ndarray, lse_parts: np.ndarray):
+    """o_parts [P,Lq,H,D], lse_parts [P,H,Lq] natural log -> (out [Lq,H,D], lse [H,Lq])."""
+    o = np.asarray(o_parts, np.float64)
+    l = np.asarray(lse_parts, np.float64)
+    mx = l.max(axis=0)
+    safe = np.where(np.isfinite(mx), mx, 0.0)
+    w = np.exp(l - safe[None])                      # [P,H,Lq]
+    tot = w.sum(axis=0)
+    lse = np.where(tot > 0, safe + np.log(np.where(tot > 0, tot, 1.0)), -np.inf)
+    wn = np.where(tot[None] > 0, w / np.where(tot > 0, tot, 1.0)[None], 0.0)
+    out = np.einsum("phl,plhd->lhd", wn, o)
+    return out, lse
+
+
+# ----------------------------------------------------------------------------------------------
+# cache
+# ----------------------------------------------------------------------------------------------
+
+def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end: int,
+                 local_end: int, current_start: int, sink_tokens: int):
+    """In-place roll + write on numpy caches [cap,H,D]; returns the new local end index.
+
+    Restates wan/modules/causal_model.py:216-246 (the branch taken when a kv_cache is given).
+    """
+    cap = k_cache.shape[0]
+    n = k_new.shape[0]
+    current_end = current_start + n
+    if local_attn and current_end > global_end and n + local_end > cap:
+        evicted = n + local_end - cap
+        rolled = local_end - evicted - sink_tokens
+        src = slice(sink_tokens + evicted, sink_tokens + evicted + rolled)
+        dst = slice(sink_tokens, sink_tokens + rolled)
+        k_cache[dst] = k_cache[src].copy()
+        v_cache[dst] = v_cache[src].copy()
+        new_local_end = local_end + current_end - global_end - evicted
+    else:
+        new_local_end = local_end + current_end - global_end
+    start = new_local_end - n
+    k_cache[start:new_local_end] = k_new
+    v_cache[start:new_local_end] = v_new
+    return new_local_end

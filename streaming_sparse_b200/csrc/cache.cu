@@ -1,0 +1,91 @@
+// cache.cu -- KV-cache append / evict for the streaming window.
+//
+// Semantics of the reference's CausalWanSelfAttention.forward (wan/modules/causal_model.py:
+// 216-246): when a local window is in use and the new chunk would overflow the cache, the
+// oldest non-sink tokens are evicted by shifting the rest of the window left onto the sink
+// boundary, then the chunk is written at [local_end - n, local_end). The reference does the
+// shift with a full `.clone()` of the rolled range; here it is a sequence of in-place 16-byte
+// vector copies, each moving at most `evicted` rows, so no copy reads rows an earlier copy
+// of the same call has already overwritten (stream order separates the copies). The chunk
+// write is one 16-byte-vector copy kernel (the reference's sm_80 commit_tile,
+// local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:417-458, also writes with uint4).
+#include "common.cuh"
+
+namespace ss {
+namespace cache {
+
+constexpr int D = 128;
+
+// copy n rows of `row_vec` uint4 each, for two tensors at once (K and V)
+__global__ void __launch_bounds__(256) copy_rows_kernel(const uint4 *__restrict__ src_k, const uint4 *__restrict__ src_v,
+                                                        int64_t src_stride_vec, uint4 *__restrict__ dst_k,
+                                                        uint4 *__restrict__ dst_v, int64_t dst_stride_vec,
+                                                        int64_t n, int row_vec) {
+    const int64_t total = n * row_vec;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / row_vec, c = i % row_vec;
+        const uint4 a = src_k[r * src_stride_vec + c];
+        const uint4 b = src_v[r * src_stride_vec + c];
+        dst_k[r * dst_stride_vec + c] = a;
+        dst_v[r * dst_stride_vec + c] = b;
+    }
+}
+
+static int launch_copy(const void *sk, const void *sv, int64_t src_stride, void *dk, void *dv, int64_t dst_stride,
+                       int64_t n, int H, cudaStream_t st) {
+    if (n <= 0) return 0;
+    const int row_vec = H * D / 8;  // uint4 = 8 bf16
+    const int64_t total = n * row_vec;
+    int sms = 148;
+    int dev;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = (total + 255) / 256;
+    const unsigned blocks = (unsigned)std::min<int64_t>(want, (int64_t)sms * 8);
+    copy_rows_kernel<<<blocks, 256, 0, st>>>((const uint4 *)sk, (const uint4 *)sv, src_stride / 8, (uint4 *)dk,
+                                            (uint4 *)dv, dst_stride / 8, n, row_vec);
+    return (int)cudaGetLastError();
+}
+
+}  // namespace cache
+}  // namespace ss
+
+extern "C" int ss_cache_append(void *k_cache, void *v_cache, int cap, int H, const void *k_new, const void *v_new,
+                               int64_t new_stride, int n_new, int local_attn, int64_t global_end, int64_t local_end,
+                               int64_t current_start, int sink_tokens, int64_t *out_local_end, void *stream) {
+    using namespace ss;
+    if (!k_cache || !v_cache || !k_new || !v_new || !out_local_end) return SS_ERR_POINTER;
+    if (cap <= 0 || H <= 0 || n_new <= 0 || n_new > cap || sink_tokens < 0 || global_end < 0 || local_end < 0 ||
+        local_end > cap || current_start < 0)
+        return SS_ERR_SHAPE;
+    if (new_stride % 8 != 0 || new_stride < (int64_t)H * cache::D) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+         reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15u)
+        return SS_ERR_POINTER;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t row = (int64_t)H * cache::D;  // elements per cache row
+    const int64_t current_end = current_start + n_new;
+    int64_t new_local_end;
+    if (local_attn && current_end > global_end && n_new + local_end > cap) {
+        const int64_t evicted = n_new + local_end - cap;
+        const int64_t rolled = local_end - evicted - sink_tokens;
+        if (rolled < 0) return SS_ERR_SHAPE;  // cache too small for the sink and the chunk
+        __nv_bfloat16 *kc = static_cast<__nv_bfloat16 *>(k_cache);
+        __nv_bfloat16 *vc = static_cast<__nv_bfloat16 *>(v_cache);
+        for (int64_t done = 0; done < rolled; done += evicted) {
+            const int64_t n = std::min<int64_t>(evicted, rolled - done);
+            const int64_t src = sink_tokens + evicted + done, dst = sink_tokens + done;
+            int rc = cache::launch_copy(kc + src * row, vc + src * row, row, kc + dst * row, vc + dst * row, row, n, H, st);
+            if (rc) return rc;
+        }
+        new_local_end = local_end + current_end - global_end - evicted;
+    } else {
+        new_local_end = local_end + current_end - global_end;
+    }
+    const int64_t start = new_local_end - n_new;
+    if (start < 0 || new_local_end > cap) return SS_ERR_SHAPE;
+    int rc = cache::launch_copy(k_new, v_new, new_stride, static_cast<__nv_bfloat16 *>(k_cache) + start * row,
+                                static_cast<__nv_bfloat16 *>(v_cache) + start * row, row, n_new, H, st);
+    if (rc) return rc;
+    *out_local_end = new_local_end;
+    return 0;
+}

@@ -1,0 +1,307 @@
+"""Op-level API: the reference's router / sparse-attention / merge / cache ops on libssparse.so.
+
+Every function takes CUDA tensors, enqueues work on the current stream through the C ABI and
+raises on a nonzero status; none has a CPU path. Mirrors of the reference's op signatures:
+
+* ``exact(q, k, v, ids, workspace)`` -> (O fp32 [1,N,H,D], natural LSE [H,N]) as
+  local_experiments/video_runtime_v1/attention.py:15-24.
+* ``merge(exact_output, exact_lse, approx, approx_lse)`` -> bf16 [1,N,H,D] as
+  local_experiments/video_runtime_v1/attention.py:40-45.
+* ``Workspace`` as local_experiments/video_runtime_v1/attention.py:7-13.
+* ``route(q, k, wq, wk, ...)`` replaces the router pipeline (project / pool / score / top-k of
+  migration/unified_router/opt16/route.py:90-113 with the forced set of
+  local_experiments/video_runtime_v1/pipeline_graph.py:140-151) and returns the page LUT
+  ``ids[H, qb, n]`` (ascending, as checked by migration/unified_router/opt28/
+  validate_selection.py:30) that ``exact`` consumes.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from ._lib import DEV_BADID, DEV_NONFINITE, DEV_TIMEOUT, check, lib
+
+HEAD_DIM = 128
+
+
+class Workspace:
+    """Named, shape-keyed device buffers reused across calls (no per-call allocation)."""
+
+    def __init__(self):
+        self.entries = {}
+
+    def tensor(self, name, shape, device, dtype):
+        key = (name, tuple(shape), str(device), dtype)
+        if key not in self.entries:
+            self.entries[key] = torch.empty(shape, device=device, dtype=dtype)
+        return self.entries[key]
+
+    def bytes(self):
+        return sum(x.numel() * x.element_size() for x in self.entries.values())
+
+
+_DEFAULT_WS: dict[str, Workspace] = {}
+
+
+def _ws(workspace, device) -> Workspace:
+    if workspace is not None:
+        return workspace
+    key = str(device)
+    if key not in _DEFAULT_WS:
+        _DEFAULT_WS[key] = Workspace()
+    return _DEFAULT_WS[key]
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _require(cond: bool, msg: str):
+    if not cond:
+        raise ValueError(msg)
+
+
+def _tokens(x: torch.Tensor, name: str) -> torch.Tensor:
+    """Accept [L,H,D] or [1,L,H,D] bf16 CUDA tensors; return the [L,H,D] view."""
+    if x.dim() == 4:
+        _require(x.shape[0] == 1, f"{name}: batch size must be 1 (got {x.shape[0]})")
+        x = x[0]
+    _require(x.dim() == 3 and x.shape[-1] == HEAD_DIM, f"{name}: expected [L,H,{HEAD_DIM}], got {tuple(x.shape)}")
+    _require(x.is_cuda, f"{name}: must be a CUDA tensor (libssparse has no CPU path)")
+    _require(x.dtype == torch.bfloat16, f"{name}: must be bfloat16")
+    _require(x.is_contiguous(), f"{name}: must be contiguous")
+    return x
+
+
+def nblocks(n: int, block: int) -> int:
+    return (n + block - 1) // block
+
+
+def forced_count(Lq: int, Lk: int, block: int, sink_tokens: int = 0) -> int:
+    """Blocks overlapping the sink [0, sink_tokens) or the current chunk [Lk-Lq, Lk)."""
+    return sum(1 for j in range(nblocks(Lk, block))
+               if j * block < sink_tokens or min((j + 1) * block, Lk) > Lk - Lq)
+
+
+def budget(kb: int, nforced: int, *, topk: int | None = None, density: float | None = None,
+           rule: str = "total") -> int:
+    """Score-chosen blocks per query block (outside the forced set).
+
+    ``topk``: fixed count (config 1: 24). ``density`` + ``rule="total"``: the row keeps
+    ceil(density*kb) blocks including the forced ones. ``density`` + ``rule="rest"``:
+    floor(density*(kb-forced)) extra blocks (local_experiments/video_runtime_v1/
+    pipeline_graph.py:143-146).
+    """
+    if topk is not None:
+        extra = topk
+    elif density is None:
+        raise ValueError("give topk or density")
+    elif rule == "total":
+        extra = math.ceil(density * kb) - nforced
+    elif rule == "rest":
+        extra = math.floor(density * (kb - nforced))
+    else:
+        raise ValueError(f"unknown budget rule {rule!r}")
+    return max(0, min(extra, kb - nforced))
+
+
+class DeviceStatus:
+    """Per-device int32 word the kernels OR their SS_DEV_* bits into."""
+
+    _words: dict[str, torch.Tensor] = {}
+
+    @classmethod
+    def word(cls, device) -> torch.Tensor:
+        key = str(device)
+        if key not in cls._words:
+            cls._words[key] = torch.zeros(1, dtype=torch.int32, device=device)
+        return cls._words[key]
+
+    @classmethod
+    def check(cls, device, reset: bool = True) -> None:
+        w = cls.word(device)
+        bits = int(w.item())
+        if reset:
+            w.zero_()
+        if bits & DEV_NONFINITE:
+            raise FloatingPointError("router produced a non-finite block score")
+        if bits & DEV_TIMEOUT:
+            raise RuntimeError("attention kernel pipeline wait timed out")
+        if bits & DEV_BADID:
+            raise IndexError("block id out of range in the attention LUT")
+
+
+# ----------------------------------------------------------------------------------------------
+# router
+# ----------------------------------------------------------------------------------------------
+
+def router_workspace_bytes(H: int, Lq: int, Lk: int, R: int = 64, block: int = 64) -> int:
+    n = ctypes.c_size_t()
+    check(lib().ss_router_workspace_bytes(H, Lq, Lk, R, block, ctypes.byref(n)), "ss_router_workspace_bytes")
+    return n.value
+
+
+def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, return_mask: bool = False,
+          return_scores: bool = False, workspace: Workspace | None = None, out: torch.Tensor | None = None,
+          validate: bool = False):
+    """Block ids per (head, query block): forced blocks plus the ``extra`` best-scoring others.
+
+    q [Lq,H,128] bf16 (current chunk), k [Lk,H,128] bf16 (visible window, current chunk last),
+    wq/wk [H,128,R] fp32. Returns ids int32 [H, qb, forced+extra] ascending, and optionally the
+    selection mask (bool [H,qb,kb]) and block scores (fp32 [H,qb,kb]).
+    """
+    q = _tokens(q, "q")
+    k = _tokens(k, "k")
+    Lq, H, _ = q.shape
+    Lk = k.shape[0]
+    _require(k.shape[1] == H and k.device == q.device, "q/k head count or device mismatch")
+    _require(wq.shape == wk.shape and wq.dim() == 3 and wq.shape[0] == H and wq.shape[1] == HEAD_DIM,
+             "wq/wk must be [H,128,R]")
+    wq = wq.to(device=q.device, dtype=torch.float32).contiguous()
+    wk = wk.to(device=q.device, dtype=torch.float32).contiguous()
+    R = wq.shape[2]
+    qb, kb = nblocks(Lq, block), nblocks(Lk, block)
+    n_ids = forced_count(Lq, Lk, block, sink_tokens) + extra
+    ws = _ws(workspace, q.device)
+    nbytes = router_workspace_bytes(H, Lq, Lk, R, block)
+    scratch = ws.tensor("router", (nbytes,), q.device, torch.uint8)
+    ids = out if out is not None else torch.empty((H, qb, n_ids), dtype=torch.int32, device=q.device)
+    _require(ids.shape == (H, qb, n_ids) and ids.dtype == torch.int32 and ids.is_contiguous(), "bad ids buffer")
+    mask = torch.empty((H, qb, kb), dtype=torch.uint8, device=q.device) if return_mask else None
+    scores = torch.empty((H, qb, kb), dtype=torch.float32, device=q.device) if return_scores else None
+    status = DeviceStatus.word(q.device)
+    rc = lib().ss_router(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra, _p(ids), n_ids,
+                         _p(mask), _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
+    check(rc, "ss_router")
+    if validate:
+        DeviceStatus.check(q.device)
+    res = [ids]
+    if return_mask:
+        res.append(mask.bool())
+    if return_scores:
+        res.append(scores)
+    return res[0] if len(res) == 1 else tuple(res)
+
+
+# ----------------------------------------------------------------------------------------------
+# attention
+# ----------------------------------------------------------------------------------------------
+
+def attention_max_ids(Lk: int, block: int = 64) -> int:
+    n = ctypes.c_int()
+    check(lib().ss_attention_max_ids(Lk, block, ctypes.byref(n)), "ss_attention_max_ids")
+    return n.value
+
+
+def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = None,
+                     out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False,
+                     out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False):
+    """softmax(scale q K_S^T) V_S over the valid tokens of the blocks in ids[h, t // block].
+
+    q [Lq,H,128], k/v [Lk,H,128] bf16; ids int32 [H, ceil(Lq/block), n] (entries < 0 ignored).
+    Returns out [Lq,H,128] in ``out_dtype`` (bf16 or fp32), plus the natural-log LSE [H,Lq] fp32
+    when ``return_lse``.
+    """
+    q = _tokens(q, "q")
+    k = _tokens(k, "k")
+    v = _tokens(v, "v")
+    Lq, H, D = q.shape
+    Lk = k.shape[0]
+    _require(v.shape == k.shape and k.shape[1] == H, "k/v shape mismatch")
+    _require(ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 3, "ids must be int32 CUDA [H,qb,n]")
+    _require(ids.shape[0] == H and ids.shape[1] == nblocks(Lq, block), f"ids must be [H,{nblocks(Lq, block)},n]")
+    ids = ids.contiguous()
+    _require(out_dtype in (torch.bfloat16, torch.float32), "out_dtype must be bf16 or fp32")
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    if out is None:
+        out = torch.empty((Lq, H, D), dtype=out_dtype, device=q.device)
+    _require(out.shape[-3:] == (Lq, H, D) and out.dtype == out_dtype and out.is_contiguous(), "bad out buffer")
+    if return_lse and lse is None:
+        lse = torch.empty((H, Lq), dtype=torch.float32, device=q.device)
+    status = DeviceStatus.word(q.device)
+    rc = lib().ss_attention(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
+                            1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None, _p(status),
+                            _stream(q.device))
+    check(rc, "ss_attention")
+    if validate:
+        DeviceStatus.check(q.device)
+    return (out, lse) if return_lse else out
+
+
+def exact(q, k, v, ids, workspace: Workspace | None = None):
+    """Reference mirror: q/k/v [1,N,H,D] bf16, ids [H, N//64, count] -> (O fp32 [1,N,H,D], lse [H,N])."""
+    ws = _ws(workspace, q.device)
+    _, n, h, d = q.shape
+    out = ws.tensor("exact", (1, n, h, d), q.device, torch.float32)
+    lse = ws.tensor("exact_lse", (h, n), q.device, torch.float32)
+    ids = ids.to(torch.int32)
+    sparse_attention(q, k, v, ids, block=64, out_dtype=torch.float32, return_lse=True, out=out[0], lse=lse)
+    return out, lse
+
+
+# ----------------------------------------------------------------------------------------------
+# merge
+# ----------------------------------------------------------------------------------------------
+
+def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor, *, out_dtype: torch.dtype = torch.bfloat16,
+              return_lse: bool = False):
+    """o_parts fp32 [P,Lq,H,128], lse_parts fp32 [P,H,Lq] natural log -> merged [Lq,H,128] (+ LSE)."""
+    _require(o_parts.is_cuda and o_parts.dtype == torch.float32 and o_parts.dim() == 4, "o_parts: fp32 CUDA [P,Lq,H,D]")
+    P, Lq, H, D = o_parts.shape
+    _require(D == HEAD_DIM and lse_parts.shape == (P, H, Lq) and lse_parts.dtype == torch.float32, "lse_parts: [P,H,Lq]")
+    o_parts = o_parts.contiguous()
+    lse_parts = lse_parts.contiguous()
+    out = torch.empty((Lq, H, D), dtype=out_dtype, device=o_parts.device)
+    lse = torch.empty((H, Lq), dtype=torch.float32, device=o_parts.device) if return_lse else None
+    rc = lib().ss_lse_merge(_p(o_parts), _p(lse_parts), P, H, Lq, _p(out), 1 if out_dtype == torch.float32 else 0,
+                            _p(lse), _stream(o_parts.device))
+    check(rc, "ss_lse_merge")
+    return (out, lse) if return_lse else out
+
+
+def merge(exact_output, exact_lse, approx, approx_lse):
+    """Reference mirror: exact [1,N,H,D] + LSE [H,N] with approx [H,N,D] + LSE [H,N] -> bf16 [1,N,H,D]."""
+    parts = torch.stack((exact_output[0].float(), approx.float().transpose(0, 1)))
+    lses = torch.stack((exact_lse.float(), approx_lse.float()))
+    return lse_merge(parts, lses, out_dtype=torch.bfloat16)[None]
+
+
+# ----------------------------------------------------------------------------------------------
+# cache
+# ----------------------------------------------------------------------------------------------
+
+def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end: int, local_end: int,
+                 current_start: int, sink_tokens: int) -> int:
+    """Roll (evict) + write one chunk into [cap,H,128] (or [1,cap,H,128]) bf16 caches in place.
+
+    Returns the new local end index; the visible window is cache[max(0, end - W) : end].
+    """
+    kc = k_cache[0] if k_cache.dim() == 4 else k_cache
+    vc = v_cache[0] if v_cache.dim() == 4 else v_cache
+    kn = k_new[0] if k_new.dim() == 4 else k_new
+    vn = v_new[0] if v_new.dim() == 4 else v_new
+    for name, t in (("k_cache", kc), ("v_cache", vc), ("k_new", kn), ("v_new", vn)):
+        _require(t.is_cuda and t.dtype == torch.bfloat16 and t.shape[-1] == HEAD_DIM, f"{name}: bf16 CUDA [...,128]")
+    _require(kc.is_contiguous() and vc.is_contiguous() and kc.shape == vc.shape, "caches must be contiguous and equal")
+    cap, H, _ = kc.shape
+    _require(kn.shape == vn.shape and kn.shape[1] == H and kn.stride() == vn.stride(), "k_new/v_new mismatch")
+    _require(kn.stride(2) == 1 and kn.stride(1) == HEAD_DIM, "k_new rows must be [H,128] contiguous")
+    new_end = ctypes.c_int64()
+    rc = lib().ss_cache_append(_p(kc), _p(vc), cap, H, _p(kn), _p(vn), kn.stride(0), kn.shape[0], int(bool(local_attn)),
+                               int(global_end), int(local_end), int(current_start), int(sink_tokens),
+                               ctypes.byref(new_end), _stream(kc.device))
+    check(rc, "ss_cache_append")
+    return new_end.value
+
+
+__all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "sparse_attention", "exact",
+           "attention_max_ids", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks"]
+
+# keep the status-bit names importable from here
+DEV_BITS = dict(nonfinite=DEV_NONFINITE, timeout=DEV_TIMEOUT, badid=DEV_BADID)

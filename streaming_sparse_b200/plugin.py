@@ -1,0 +1,142 @@
+"""Drop-in plugin: routed block-sparse attention behind the reference's ``attention(q, k, v)``.
+
+The reference swaps the module-level ``wan.modules.causal_model.attention`` symbol, which
+CausalWanSelfAttention.forward calls with the RoPE'd queries of the current chunk and the
+visible KV window (wan/modules/causal_model.py:247-251); ``SelfForcingAdapter.__enter__``
+(streaming_sparse/integration/self_forcing_adapter.py:104-125) does the swap, rejects extra
+positional/keyword options, refuses nested adapters and restores the symbol on exit.
+``SparsePlugin`` does the same around ``SparseAttention``, a callable with that exact
+signature: ``q [B,Lq,H,D]``, ``k, v [B,Lk,H,D]`` bf16 with the current chunk as the last
+``Lq`` rows of ``k``/``v`` -> ``[B,Lq,H,D]`` bf16.
+"""
+from __future__ import annotations
+
+import importlib
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+_PATCH_FLAG = "_streaming_sparse_b200_patch"
+
+
+@dataclass(frozen=True)
+class RouterConfig:
+    """Block size and budget of the learned block router.
+
+    Exactly one of ``topk`` (fixed count outside the forced set) or ``density`` is used;
+    ``rule`` picks how ``density`` becomes a count (see ``ops.budget``).
+    """
+
+    block: int = 64
+    topk: int | None = None
+    density: float | None = 0.25
+    rule: str = "total"
+    sink_tokens: int = 0
+    proj_dim: int = 64
+
+    def extra(self, Lq: int, Lk: int) -> int:
+        kb = ops.nblocks(Lk, self.block)
+        nf = ops.forced_count(Lq, Lk, self.block, self.sink_tokens)
+        return ops.budget(kb, nf, topk=self.topk, density=self.density, rule=self.rule)
+
+
+def init_router_weights(num_heads: int, head_dim: int = 128, proj_dim: int = 64, *, seed: int = 0,
+                        device="cuda"):
+    """W_q, W_k ~ N(0, 1/head_dim), [H, head_dim, proj_dim] fp32 (the benchmark's random init)."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    std = 1.0 / math.sqrt(head_dim)
+    wq = torch.randn((num_heads, head_dim, proj_dim), generator=g) * std
+    wk = torch.randn((num_heads, head_dim, proj_dim), generator=g) * std
+    return wq.to(device), wk.to(device)
+
+
+class SparseAttention:
+    """Router + block-sparse attention with the signature of the reference's ``attention``."""
+
+    def __init__(self, wq: torch.Tensor, wk: torch.Tensor, config: RouterConfig = RouterConfig(),
+                 workspace: ops.Workspace | None = None, validate: bool = False):
+        self.wq = wq.float().contiguous()
+        self.wk = wk.float().contiguous()
+        self.config = config
+        self.workspace = workspace if workspace is not None else ops.Workspace()
+        self.validate = validate
+        self.dense = False          # when True, every block is kept (the reference's context pass)
+        self.last_ids = None
+        self.calls = 0
+
+    def route(self, q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+        Lq, Lk = q.shape[-3], k.shape[-3]
+        c = self.config
+        return ops.route(q, k, self.wq, self.wk, block=c.block, extra=c.extra(Lq, Lk), sink_tokens=c.sink_tokens,
+                         workspace=self.workspace, validate=self.validate)
+
+    def _dense_ids(self, H: int, Lq: int, Lk: int, device) -> torch.Tensor:
+        c = self.config
+        qb, kb = ops.nblocks(Lq, c.block), ops.nblocks(Lk, c.block)
+        ids = self.workspace.tensor("dense_ids", (H, qb, kb), device, torch.int32)
+        ids.copy_(torch.arange(kb, device=device, dtype=torch.int32).expand(H, qb, kb))
+        return ids
+
+    def forward_one(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None):
+        """q [Lq,H,D], k/v [Lk,H,D] bf16 -> [Lq,H,D] bf16."""
+        Lq, H, _ = q.shape
+        Lk = k.shape[0]
+        if Lk < Lq:
+            raise ValueError("the KV window must contain the current chunk (Lk >= Lq)")
+        ids = self._dense_ids(H, Lq, Lk, q.device) if self.dense else self.route(q, k)
+        self.last_ids = ids
+        self.calls += 1
+        return ops.sparse_attention(q, k, v, ids, block=self.config.block, out=out, validate=self.validate)
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *args, **kwargs) -> torch.Tensor:
+        if args or kwargs:
+            raise ValueError("Unexpected attention options; audit upstream implementation")
+        if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+            raise ValueError("expected q [B,Lq,H,D] and k, v [B,Lk,H,D]")
+        q = q.to(torch.bfloat16).contiguous()
+        k = k.to(torch.bfloat16).contiguous()
+        v = v.to(torch.bfloat16).contiguous()
+        out = torch.empty_like(q)
+        for b in range(q.shape[0]):
+            self.forward_one(q[b], k[b], v[b], out=out[b])
+        return out
+
+
+class SparsePlugin:
+    """Context manager that routes ``<module>.attention`` through a ``SparseAttention``.
+
+    ``target`` is a module object or its import path (default ``wan.modules.causal_model``).
+    One plugin may be active per target; nested use raises, as in the reference adapter.
+    """
+
+    def __init__(self, sparse: SparseAttention, target="wan.modules.causal_model", attribute: str = "attention"):
+        self.sparse = sparse
+        self.target = target
+        self.attribute = attribute
+        self.module = None
+        self.original = None
+
+    def __enter__(self):
+        module = importlib.import_module(self.target) if isinstance(self.target, str) else self.target
+        current = getattr(module, self.attribute)
+        if getattr(current, _PATCH_FLAG, False):
+            raise RuntimeError("Nested/concurrent sparse plugins are unsupported")
+        self.module, self.original = module, current
+        sparse = self.sparse
+
+        def wrapped(q, k, v, *args, **kwargs):
+            return sparse(q, k, v, *args, **kwargs)
+
+        setattr(wrapped, _PATCH_FLAG, True)
+        wrapped.original = current
+        setattr(module, self.attribute, wrapped)
+        return self
+
+    def __exit__(self, *exc):
+        if self.module is not None:
+            setattr(self.module, self.attribute, self.original)
+        self.module = None
+        return False

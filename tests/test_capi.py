@@ -1,0 +1,75 @@
+"""The C ABI library loads, exports every entry point declared in include/ssparse.h, and rejects
+bad arguments on the host (none of these calls reaches a CUDA API)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "ssparse.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^int\s+(ss_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from streaming_sparse_b200 import build
+    build.build()
+    from streaming_sparse_b200._lib import lib as load
+    return load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from streaming_sparse_b200._lib import SIGNATURES
+    names = declared()
+    assert len(names) >= 8
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version(lib):
+    assert lib.ss_version() >= 100
+
+
+def test_workspace_and_capacity_queries(lib):
+    n = ctypes.c_size_t()
+    assert lib.ss_router_workspace_bytes(12, 4680, 32760, 64, 64, ctypes.byref(n)) == 0
+    # qh + kh + scores, fp32
+    assert n.value >= 4 * (12 * 74 * 64 + 12 * 512 * 64 + 12 * 74 * 512)
+    m = ctypes.c_int()
+    assert lib.ss_attention_max_ids(32760, 64, ctypes.byref(m)) == 0
+    assert m.value == 512          # config 2 fits with every block listed
+    assert lib.ss_attention_max_ids(98280, 64, ctypes.byref(m)) == 0
+    assert m.value >= 768          # config 5 at 50% density
+    assert lib.ss_attention_max_ids(100, 96, ctypes.byref(m)) == 1001
+
+
+def test_host_argument_errors(lib):
+    fake = ctypes.c_void_p(0x100000)  # never dereferenced: every call below fails its host checks first
+    # null pointers
+    assert lib.ss_attention(None, fake, fake, fake, 12, 64, 64, 64, 1, 0.1, fake, 0, None, None, None) == 1002
+    # unsupported block size / empty sizes
+    assert lib.ss_attention(fake, fake, fake, fake, 12, 64, 64, 96, 1, 0.1, fake, 0, None, None, None) == 1001
+    assert lib.ss_attention(fake, fake, fake, fake, 0, 64, 64, 64, 1, 0.1, fake, 0, None, None, None) == 1001
+    # misaligned base pointer (TMA needs 16-byte alignment)
+    odd = ctypes.c_void_p(0x100002)
+    assert lib.ss_attention(odd, fake, fake, fake, 12, 64, 64, 64, 1, 0.1, fake, 0, None, None, None) == 1002
+    # router: budget larger than the unforced blocks, n_ids inconsistent, workspace too small
+    ws = ctypes.c_size_t(1 << 30)
+    assert lib.ss_router(fake, fake, fake, fake, 12, 1560, 6240, 64, 64, 0, 74, fake, 99, None, None, fake, ws,
+                         None, None) == 1004
+    assert lib.ss_router(fake, fake, fake, fake, 12, 1560, 6240, 64, 64, 0, 24, fake, 48, None, None, fake, ws,
+                         None, None) == 1001
+    assert lib.ss_router(fake, fake, fake, fake, 12, 1560, 6240, 64, 64, 0, 24, fake, 49, None, None, fake,
+                         ctypes.c_size_t(16), None, None) == 1003
+    # merge / cache shape checks
+    assert lib.ss_lse_merge(fake, fake, 0, 12, 10, fake, 0, None, None) == 1001
+    end = ctypes.c_int64()
+    assert lib.ss_cache_append(fake, fake, 24, 1, fake, fake, 128, 30, 1, 0, 0, 0, 4, ctypes.byref(end), None) == 1001
+    assert lib.ss_cache_append(fake, fake, 24, 1, fake, fake, 100, 12, 1, 0, 0, 0, 4, ctypes.byref(end), None) == 1001

@@ -1,0 +1,111 @@
+"""Multi-rank host logic on CPU (gloo, world size 2): LSE merge of KV-block shards and the head
+all_gather, with the per-rank partial attention computed by the CPU oracle in the test."""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, fn, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        q.put((rank, fn(rank, world)))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, e))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(fn, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fn, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        if isinstance(v, Exception):
+            raise v
+    return res
+
+
+def _inputs():
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from oracle import oracle as o
+    rng = np.random.default_rng(5)
+    Lq, Lk, H = 130, 900, 3
+    q = o.bf16_round(rng.standard_normal((Lq, H, 128)).astype(np.float32))
+    k = o.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    v = o.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    kb = math.ceil(Lk / 64)
+    ids = np.stack([np.stack([np.sort(rng.choice(kb, 6, replace=False)) for _ in range(3)]) for _ in range(H)])
+    return o, q, k, v, ids.astype(np.int32)
+
+
+def kv_shard_rank(rank, world):
+    from streaming_sparse_b200.distributed import merge_partials, shard_ids
+    o, q, k, v, ids = _inputs()
+    mine = shard_ids(torch.from_numpy(ids), rank, world).numpy()
+    part, lse = o.attention(q, k, v, mine, 64)
+    lse = np.where(np.isnan(lse), -np.inf, lse)
+    empty = np.isneginf(lse).T[:, :, None]
+    part = np.where(empty, 0.0, part)
+    out, total = merge_partials(torch.from_numpy(part).float(), torch.from_numpy(lse).float(),
+                                out_dtype=torch.float32)
+    return out.numpy(), total.numpy()
+
+
+def head_shard_rank(rank, world):
+    from streaming_sparse_b200.distributed import gather_heads, head_range
+    o, q, k, v, ids = _inputs()
+    h0, h1 = head_range(q.shape[1], rank, world)
+    part, _ = o.attention(q[:, h0:h1], k[:, h0:h1], v[:, h0:h1], ids[h0:h1], 64)
+    return gather_heads(torch.from_numpy(part).float(), q.shape[1]).numpy()
+
+
+def test_kv_sharded_lse_merge_equals_full():
+    res = _run(kv_shard_rank)
+    o, q, k, v, ids = _inputs()
+    ref, ref_lse = o.attention(q, k, v, ids, 64)
+    for r in range(2):
+        np.testing.assert_allclose(res[r][0], ref, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(res[r][1], ref_lse, rtol=1e-6, atol=1e-6)
+
+
+def test_head_sharded_gather_equals_full():
+    res = _run(head_shard_rank)
+    o, q, k, v, ids = _inputs()
+    ref, _ = o.attention(q, k, v, ids, 64)
+    for r in range(2):
+        np.testing.assert_allclose(res[r], ref, rtol=1e-6, atol=1e-7)
+
+
+def test_head_range_and_shard_ids():
+    from streaming_sparse_b200.distributed import head_range, shard_ids
+    assert [head_range(12, r, 4) for r in range(4)] == [(0, 3), (3, 6), (6, 9), (9, 12)]
+    assert [head_range(12, r, 5) for r in range(5)] == [(0, 3), (3, 6), (6, 8), (8, 10), (10, 12)]
+    ids = torch.tensor([[[0, 1, 2, 3, 4, 5, 6, -1]]], dtype=torch.int32)
+    parts = [shard_ids(ids, r, 3) for r in range(3)]
+    assert parts[0].tolist() == [[[0, -1, -1, 3, -1, -1, 6, -1]]]
+    union = torch.stack(parts).max(0).values
+    assert union.tolist() == ids.tolist()

@@ -1,0 +1,154 @@
+"""tcgen05 block-sparse attention == the float64 gather-softmax oracle."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_attention_close, np32, qkv, router_weights
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _attend(q, k, v, ids, block, out_dtype=torch.bfloat16):
+    from streaming_sparse_b200 import ops
+    out, lse = ops.sparse_attention(q.to(DEV), k.to(DEV), v.to(DEV), torch.as_tensor(ids).to(DEV), block=block,
+                                    out_dtype=out_dtype, return_lse=True, validate=True)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy(), lse.cpu().numpy()
+
+
+def _random_ids(rng, H, qb, kb, n, pad=0, forced=()):
+    ids = np.full((H, qb, n + pad), -1, np.int32)
+    for h in range(H):
+        for i in range(qb):
+            rest = [j for j in range(kb) if j not in forced]
+            pick = sorted(set(forced) | set(rng.choice(rest, n - len(forced), replace=False).tolist()))
+            ids[h, i, :n] = pick
+    return ids
+
+
+@pytest.mark.parametrize("Lq,Lk,H,block,n,pad", [
+    (100, 333, 2, 64, 3, 2),       # partial query tile, partial last key block, -1 padding
+    (256, 1024, 3, 64, 7, 0),      # two full tiles
+    (300, 1000, 2, 128, 4, 1),     # 128-token router blocks
+    (64, 4096, 1, 64, 64, 0),      # one tile, all 64 blocks listed
+    (1, 65, 1, 64, 2, 0),          # a single query row, a 1-token last block
+])
+def test_attention_random_lists(oracle, Lq, Lk, H, block, n, pad):
+    q, k, v = qkv(11, Lq, Lk, H)
+    rng = np.random.default_rng(11)
+    qb, kb = math.ceil(Lq / block), math.ceil(Lk / block)
+    ids = _random_ids(rng, H, qb, kb, min(n, kb), pad, forced=(kb - 1,))
+    out, lse = _attend(q, k, v, ids, block)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids, block)
+    assert_attention_close(out, ref)
+    np.testing.assert_allclose(lse, ref_lse, rtol=0, atol=2e-3)
+
+
+def test_attention_fp32_output_and_lse(oracle):
+    Lq, Lk, H, block = 200, 2000, 2, 64
+    q, k, v = qkv(12, Lq, Lk, H)
+    rng = np.random.default_rng(12)
+    ids = _random_ids(rng, H, math.ceil(Lq / 64), math.ceil(Lk / 64), 9, forced=(31,))
+    out, lse = _attend(q, k, v, ids, block, torch.float32)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids, block)
+    err = np.abs(out - ref)
+    assert err.max() < 5e-3 and err.mean() < 5e-4
+    np.testing.assert_allclose(lse, ref_lse, rtol=0, atol=2e-3)
+
+
+def test_attention_config1_routed(oracle):
+    """Config 1 end to end: router ids from the GPU (bit-exact to the oracle), attention vs oracle."""
+    from streaming_sparse_b200 import ops
+    Lq, Lk, H = 1560, 6240, 12
+    q, k, v = qkv(1, Lq, Lk, H)
+    wq, wk = router_weights(1, H)
+    ids = ops.route(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), block=64, extra=24, validate=True)
+    ids_np = ids.cpu().numpy()
+    r = oracle.route(np32(q), np32(k), wq.numpy(), wk.numpy(), 64, 24)
+    np.testing.assert_array_equal(ids_np, r["ids"])
+    out, lse = _attend(q, k, v, ids_np, 64)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, 64)
+    assert_attention_close(out, ref)
+    np.testing.assert_allclose(lse, ref_lse, rtol=0, atol=2e-3)
+
+
+def test_attention_config2_sampled(oracle):
+    """Config 2 at full size; the float64 oracle checks a sample of heads and query blocks."""
+    from streaming_sparse_b200 import ops
+    Lq, Lk, H = 4680, 32760, 12
+    q, k, v = qkv(2, Lq, Lk, H)
+    wq, wk = router_weights(2, H)
+    ids = ops.route(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), block=64, extra=54, validate=True)
+    ids_np = ids.cpu().numpy()
+    assert ids_np.shape == (12, 74, 128)
+    out, lse = _attend(q, k, v, ids_np, 64)
+    heads, qblocks = [0, 5, 11], [0, 1, 36, 72, 73]
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, 64, heads=heads, qblocks=qblocks)
+    assert_attention_close(out, ref)
+    m = np.isfinite(ref_lse)
+    np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
+    assert np.isfinite(out).all()
+
+
+def test_all_selected_equals_sdpa():
+    """Every block listed == dense attention (local_experiments/review_v1/test_ops.py:19-23)."""
+    Lq, Lk, H = 192, 700, 2
+    q, k, v = qkv(13, Lq, Lk, H)
+    kb = math.ceil(Lk / 64)
+    ids = np.tile(np.arange(kb, dtype=np.int32), (H, math.ceil(Lq / 64), 1))
+    out, _ = _attend(q, k, v, ids, 64)
+    dense = torch.nn.functional.scaled_dot_product_attention(
+        q.float().permute(1, 0, 2), k.float().permute(1, 0, 2), v.float().permute(1, 0, 2)).permute(1, 0, 2)
+    assert_attention_close(out, dense.numpy())
+
+
+def test_golden_reference_gather(golden):
+    """Inputs and output of streaming_sparse/v08/attention.py:115-123 (bf16-valued inputs)."""
+    g = golden("attention_v08.npz")
+    for c in ("c0", "c1"):
+        f = lambda key: torch.from_numpy(g[f"{c}_{key}"].view(np.int16)).view(torch.bfloat16)
+        q, kh, vh, kc, vc = (f(x) for x in ("q", "kh", "vh", "kc", "vc"))
+        bm = g[f"{c}_block_mask"]
+        nh = kh.shape[0]
+        k = torch.cat([kh, kc])[:, None, :].contiguous()
+        v = torch.cat([vh, vc])[:, None, :].contiguous()
+        kb = math.ceil(k.shape[0] / 64)
+        ids = np.full((1, bm.shape[0], kb), -1, np.int32)
+        for i in range(bm.shape[0]):
+            sel = [j for j in range(nh // 64) if bm[i, j]] + list(range(nh // 64, kb))
+            ids[0, i, :len(sel)] = sel
+        out, _ = _attend(q[:, None, :].contiguous(), k, v, ids, 64)
+        assert_attention_close(out[:, 0, :], g[f"{c}_out"])
+
+
+def test_padded_reference_ids_are_ignored(oracle, golden):
+    """RouteOps.select LUTs pad with -1 (local_experiments/review_v1/ops.py:115-135): never read."""
+    g = golden("padded_ids.npz")
+    ids = g["ids"].astype(np.int32)              # [2, 3, 128] over 410 pages of 64 tokens
+    H, qb, _ = ids.shape
+    Lq, Lk = qb * 64, 410 * 64
+    q, k, v = qkv(14, Lq, Lk, H)
+    out, lse = _attend(q, k, v, ids, 64)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids, 64)
+    assert_attention_close(out, ref)
+
+
+def test_empty_list_gives_zero_and_neg_inf():
+    Lq, Lk, H = 128, 256, 1
+    q, k, v = qkv(15, Lq, Lk, H)
+    ids = np.full((1, 2, 2), -1, np.int32)
+    ids[0, 0] = [0, 3]                          # second query block has no blocks at all
+    out, lse = _attend(q, k, v, ids, 64)
+    assert (out[64:] == 0).all() and np.isneginf(lse[0, 64:]).all()
+    assert np.isfinite(out[:64]).all()
+
+
+def test_bad_block_id_is_reported():
+    from streaming_sparse_b200 import ops
+    q, k, v = qkv(16, 64, 128, 1)
+    ids = torch.tensor([[[0, 5]]], dtype=torch.int32, device=DEV)   # kb = 2
+    with pytest.raises(IndexError):
+        ops.sparse_attention(q.to(DEV), k.to(DEV), v.to(DEV), ids, block=64, validate=True)

@@ -1,0 +1,97 @@
+"""KV-cache append/evict and the LSE merge on the GPU against the oracle and reference fixtures."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import np32
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def test_cache_known_answer_on_gpu():
+    """evaluation/validate.py:57-88 schedule: visible positions [0..3] + [16..35] after 3 chunks."""
+    from streaming_sparse_b200.cache import KVCache
+    c = KVCache(24, num_heads=1, frame_tokens=4, local_attn_size=6, sink_size=1, device=DEV)
+    for chunk in range(3):
+        for _ in range(3):
+            start = chunk * 12
+            tok = torch.arange(start, start + 12, device=DEV, dtype=torch.float32)
+            kv = tok[:, None, None].expand(12, 1, 128).to(torch.bfloat16).contiguous()
+            vis, hist = c.append(kv, kv, start)
+    k, v = c.window()
+    expected = list(range(4)) + list(range(16, 36))
+    np.testing.assert_array_equal(k[:, 0, 0].float().cpu().numpy(), expected)
+    np.testing.assert_array_equal(vis, expected)
+    assert hist == 12
+
+
+@pytest.mark.parametrize("local,sink,frames_per_chunk,chunks", [(5, 1, 2, 9), (-1, 0, 3, 3), (4, 0, 1, 10)])
+def test_cache_matches_oracle(oracle, local, sink, frames_per_chunk, chunks):
+    from streaming_sparse_b200.cache import KVCache
+    H, ftok = 3, 70                      # 70-token frames: rows never align with 16-byte vector groups of rows
+    cap = (local if local != -1 else frames_per_chunk * chunks) * ftok
+    c = KVCache(cap, num_heads=H, frame_tokens=ftok, local_attn_size=local, sink_size=sink, device=DEV)
+    ok, ov = np.zeros((cap, H, 128), np.float32), np.zeros((cap, H, 128), np.float32)
+    ge = le = 0
+    g = torch.Generator().manual_seed(0)
+    n = frames_per_chunk * ftok
+    for chunk in range(chunks):
+        for step in range(2):
+            start = chunk * n
+            kn = torch.randn((n, H, 128), generator=g).bfloat16()
+            vn = torch.randn((n, H, 128), generator=g).bfloat16()
+            c.append(kn.to(DEV), vn.to(DEV), start)
+            le = oracle.cache_append(ok, ov, np32(kn), np32(vn), local_attn=local != -1, global_end=ge,
+                                     local_end=le, current_start=start, sink_tokens=sink * ftok)
+            ge = start + n
+            assert c.local_end == le and c.global_end == ge
+            np.testing.assert_array_equal(c.k[0].float().cpu().numpy()[:le], ok[:le])
+            np.testing.assert_array_equal(c.v[0].float().cpu().numpy()[:le], ov[:le])
+
+
+def test_merge_matches_reference_fixture(golden):
+    from streaming_sparse_b200 import ops
+    g = golden("merge_vr1.npz")
+    eo, el = torch.from_numpy(g["exact"]).to(DEV), torch.from_numpy(g["exact_lse"]).to(DEV)
+    ap, al = torch.from_numpy(g["approx"]).to(DEV), torch.from_numpy(g["approx_lse"]).to(DEV)
+    out = ops.merge(eo, el, ap, al).float().cpu().numpy()
+    np.testing.assert_allclose(out, g["out"], rtol=0, atol=1.6e-2)
+    assert np.abs(out - g["out"]).mean() < 1e-3
+
+
+def test_lse_merge_many_parts(oracle):
+    from streaming_sparse_b200 import ops
+    g = torch.Generator().manual_seed(2)
+    P, Lq, H = 5, 77, 3
+    o = torch.randn((P, Lq, H, 128), generator=g)
+    l = torch.randn((P, H, Lq), generator=g) * 4
+    l[2, 1, :10] = -float("inf")
+    l[:, 0, 5] = -float("inf")           # a row with every part empty
+    out, lse = ops.lse_merge(o.to(DEV), l.to(DEV), out_dtype=torch.float32, return_lse=True)
+    ref, ref_lse = oracle.lse_merge(o.numpy(), l.numpy())
+    ref[5, 0] = 0.0
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, rtol=1e-5, atol=1e-5)
+
+
+def test_split_blocks_then_merge_equals_whole(oracle):
+    """Attention over a block list == LSE merge of attention over a partition of that list
+    (the exchange step of KV-block sharding)."""
+    from helpers import qkv
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.distributed import shard_ids
+    Lq, Lk, H = 256, 4096, 2
+    q, k, v = qkv(21, Lq, Lk, H)
+    rng = np.random.default_rng(21)
+    ids = np.stack([np.stack([np.sort(rng.choice(64, 20, replace=False)) for _ in range(4)]) for _ in range(H)])
+    ids = torch.from_numpy(ids.astype(np.int32)).to(DEV)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    whole = ops.sparse_attention(qd, kd, vd, ids, out_dtype=torch.float32)
+    parts, lses = [], []
+    for r in range(3):
+        o, l = ops.sparse_attention(qd, kd, vd, shard_ids(ids, r, 3), out_dtype=torch.float32, return_lse=True)
+        parts.append(o)
+        lses.append(l)
+    merged = ops.lse_merge(torch.stack(parts), torch.stack(lses), out_dtype=torch.float32)
+    torch.testing.assert_close(merged, whole, rtol=2e-3, atol=2e-3)

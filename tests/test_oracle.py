@@ -1,0 +1,162 @@
+"""Pin the CPU oracle against vectors produced by the reference's own code (tests/golden/)."""
+import math
+
+import numpy as np
+import pytest
+
+
+def test_select_matches_reference_stable_select(oracle, golden):
+    """v05 select (streaming_sparse/v05/primitives.py:35-56): score desc, lower id on ties, -0 == +0."""
+    g = golden("select_v05.npz")
+    forced = g["forced"]
+    names = sorted({k.rsplit("_", 1)[0] for k in g.files if k.endswith("_scores")})
+    assert len(names) >= 40
+    for name in names:
+        scores = g[name + "_scores"][None]           # [1,Q,B]
+        extra = int(g[name + "_extra"])
+        ids, mask = oracle.select(scores, forced, extra)
+        np.testing.assert_array_equal(mask[0].astype(np.uint8), g[name + "_mask"], err_msg=name)
+        assert (np.diff(ids, axis=-1) > 0).all()
+
+
+def test_attention_matches_reference_gather(oracle, golden):
+    """v08 reference (streaming_sparse/v08/attention.py:115-123) == global-block gather over [history|current]."""
+    g = golden("attention_v08.npz")
+    for c in ("c0", "c1"):
+        f = lambda key: g[f"{c}_{key}"].astype(np.uint32) << 16
+        q, kh, vh, kc, vc = (f(k).view(np.float32) for k in ("q", "kh", "vh", "kc", "vc"))
+        bm = g[f"{c}_block_mask"]
+        nh, nc = len(kh), len(kc)
+        assert nh % 64 == 0
+        k = np.concatenate([kh, kc])[:, None, :]
+        v = np.concatenate([vh, vc])[:, None, :]
+        kb = math.ceil((nh + nc) / 64)
+        qb = bm.shape[0]
+        ids = np.full((1, qb, kb), -1, np.int32)
+        for i in range(qb):
+            sel = [j for j in range(nh // 64) if bm[i, j]] + list(range(nh // 64, kb))
+            ids[0, i, :len(sel)] = sel
+        out, lse = oracle.attention(q[:, None, :], k, v, ids, 64)
+        np.testing.assert_allclose(out[:, 0, :], g[f"{c}_out"], rtol=1e-5, atol=1e-6)
+        assert np.isfinite(lse).all()
+
+
+def test_all_selected_equals_dense(oracle):
+    """all-selected == dense softmax (local_experiments/review_v1/test_ops.py:19-23)."""
+    rng = np.random.default_rng(3)
+    q = oracle.bf16_round(rng.standard_normal((100, 2, 128)).astype(np.float32))
+    k = oracle.bf16_round(rng.standard_normal((300, 2, 128)).astype(np.float32))
+    v = oracle.bf16_round(rng.standard_normal((300, 2, 128)).astype(np.float32))
+    kb = math.ceil(300 / 64)
+    ids = np.tile(np.arange(kb, dtype=np.int32), (2, 2, 1))
+    out, lse = oracle.attention(q, k, v, ids, 64)
+    for h in range(2):
+        z = q[:, h].astype(np.float64) @ k[:, h].T.astype(np.float64) / math.sqrt(128)
+        p = np.exp(z - z.max(1, keepdims=True))
+        dense = (p / p.sum(1, keepdims=True)) @ v[:, h]
+        np.testing.assert_allclose(out[:, h], dense, rtol=1e-10, atol=1e-12)
+        ref_lse = np.log(np.exp(z - z.max(1, keepdims=True)).sum(1)) + z.max(1)
+        np.testing.assert_allclose(lse[h], ref_lse, rtol=1e-12)
+
+
+def test_merge_matches_reference(oracle, golden):
+    """merge (local_experiments/video_runtime_v1/attention.py:40-45); its output is bf16."""
+    g = golden("merge_vr1.npz")
+    parts = np.stack([g["exact"][0], g["approx"].transpose(1, 0, 2)])
+    lses = np.stack([g["exact_lse"], g["approx_lse"]])
+    out, _ = oracle.lse_merge(parts, lses)
+    np.testing.assert_allclose(oracle.bf16_round(out.astype(np.float32)), g["out"][0], rtol=0, atol=1e-2)
+    np.testing.assert_allclose(out, g["out"][0], rtol=8e-3, atol=1e-5)
+
+
+def test_positions_match_reference_adapter(golden):
+    """PositionTracker == SelfForcingAdapter._pre (streaming_sparse/integration/self_forcing_adapter.py:50-97)."""
+    from streaming_sparse_b200.cache import PositionTracker
+    g = golden("positions_adapter.npz")
+    for name in ("validate", "long", "global"):
+        ftok, local, sink, cache, n, chunks, steps, frame = (int(x) for x in g[f"{name}_meta"])
+        calls = g[f"{name}_calls"]
+        flat_all = g[f"{name}_positions"]
+        tr = PositionTracker(cache)
+        max_att = 32760 if local == -1 else local * frame
+        ge = le = off = 0
+        for start, nn, hist, count in calls:
+            vis, h = tr.update(start=int(start), n=int(nn), old_global=ge, old_local=le, local_attn=local != -1,
+                               sink_tokens=sink * ftok, max_attention_size=max_att)
+            np.testing.assert_array_equal(vis, flat_all[off:off + count], err_msg=f"{name} start={start}")
+            assert h == hist
+            off += count
+            end = int(start) + int(nn)
+            if local != -1 and end > ge and nn + le > cache:
+                le = le + end - ge - (nn + le - cache)
+            else:
+                le = le + end - ge
+            ge = end
+
+
+def test_cache_known_answer(oracle):
+    """evaluation/validate.py:57-88: after 3 chunks the visible positions are [0..3] + [16..35]."""
+    cap, n = 24, 12
+    kc = np.full((cap, 1, 2), -1.0)
+    vc = np.full((cap, 1, 2), -1.0)
+    ge = le = 0
+    for chunk in range(3):
+        for _ in range(3):
+            start = chunk * n
+            tok = np.arange(start, start + n, dtype=np.float64)[:, None, None].repeat(2, 2)
+            le = oracle.cache_append(kc, vc, tok, tok, local_attn=True, global_end=ge, local_end=le,
+                                     current_start=start, sink_tokens=4)
+            ge = start + n
+    np.testing.assert_array_equal(kc[:le, 0, 0], list(range(4)) + list(range(16, 36)))
+
+
+def test_budget_sizes_per_config(oracle):
+    # config 1: Lq 1560, Lk 6240, block 64 -> current-frame blocks 73..97 forced, extra 24
+    f = oracle.forced_blocks(1560, 6240, 64)
+    assert f.sum() == 25 and f[73:].all() and not f[:73].any()
+    # config 2: 74 forced current blocks (438..511), total ceil(.25*512)=128 -> extra 54
+    f = oracle.forced_blocks(4680, 32760, 64)
+    assert f.sum() == 74 and f[438:].all() and not f[:438].any()
+    assert oracle.budget(512, 74, density=0.25, rule="total") == 54
+    # config 4: window 34320 with one sink frame, block 128: 13 sink + 37/38 current blocks
+    f = oracle.forced_blocks(4680, 34320, 128, sink_tokens=1560)
+    kb = len(f)
+    assert kb == 269 and f[:13].all()
+    assert oracle.budget(kb, int(f.sum()), density=0.1, rule="rest") == math.floor(0.1 * (kb - f.sum()))
+
+
+def test_router_invariants(oracle):
+    """ids in range and strictly increasing (migration/unified_router/opt28/validate_selection.py:30);
+    forced blocks present; no unselected unforced block outranks a selected one."""
+    rng = np.random.default_rng(0)
+    Lq, Lk, H = 300, 1000, 3
+    q = oracle.bf16_round(rng.standard_normal((Lq, H, 128)).astype(np.float32))
+    k = oracle.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    wq = (rng.standard_normal((H, 128, 64)) / math.sqrt(128)).astype(np.float32)
+    wk = (rng.standard_normal((H, 128, 64)) / math.sqrt(128)).astype(np.float32)
+    r = oracle.route(q, k, wq, wk, 64, extra=4)
+    ids, mask, S, f = r["ids"], r["mask"], r["scores"], r["forced"].astype(bool)
+    kb = len(f)
+    assert ((ids >= 0) & (ids < kb)).all() and (np.diff(ids, axis=-1) > 0).all()
+    assert mask[..., f].all()
+    for h in range(H):
+        for i in range(ids.shape[1]):
+            sel = mask[h, i] & ~f
+            rest = ~mask[h, i] & ~f
+            assert sel.sum() == 4
+            assert S[h, i][sel].min() >= S[h, i][rest].max()
+
+
+def test_router_pooling_is_exact_fp32_order(oracle):
+    """The block mean is a sequential fp32 sum and one divide; projection is ascending fmaf."""
+    rng = np.random.default_rng(1)
+    x = oracle.bf16_round(rng.standard_normal((70, 1, 128)).astype(np.float32))
+    w = rng.standard_normal((1, 128, 64)).astype(np.float32)
+    pooled, proj = oracle.pool_project(x, w, 64)
+    for b, (t0, t1) in enumerate([(0, 64), (64, 70)]):
+        s = np.float32(0)
+        for t in range(t0, t1):
+            s = np.float32(s + x[t, 0])
+        np.testing.assert_array_equal(pooled[0, b], s / np.float32(t1 - t0))
+    # fma order: compare with float64 accumulation loosely, exact equality is checked on the GPU
+    np.testing.assert_allclose(proj[0], pooled[0].astype(np.float64) @ w[0], rtol=1e-4, atol=1e-5)
