@@ -11,23 +11,28 @@
 // Work decomposition
 //   One CTA per (head, 128-row query tile). With 64-token router blocks a tile holds two query
 //   blocks; the CTA walks the union of their block lists and masks, per 64-row half, the blocks
-//   that half did not select. With 128-token blocks a tile is exactly one query block.
-//   The union is walked in steps of 128 KV tokens (two 64-token sub-blocks, each gathered by
-//   its own TMA loads, so the two need not be adjacent). CTAs are ordered head-major so the
-//   CTAs resident at one time share a few heads' K/V in L2.
+//   that half did not select. With 128-token blocks a tile is exactly one query block and each
+//   block is walked as two 64-token sub-blocks. One step = one 64-token sub-block, gathered by
+//   TMA at its own row offset. CTAs are ordered head-major so the CTAs resident at one time
+//   share a few heads' K/V in L2.
 //
-// Warp roles (256 threads)
-//   warp 0      TMA producer: Q once, then K and V sub-blocks into a 2-stage ring
+// Warp roles (384 threads)
+//   warp 0      K producer: TMA loads of K sub-blocks into a 4-stage ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-3   block-list construction in the prologue, idle afterwards
-//   warps 4-7   softmax: thread r owns query row r (TMEM lane r); reads S from TMEM, applies the
-//               masks, keeps the running max/sum, writes P (bf16) to shared memory, rescales the
-//               O accumulator in TMEM when the running max grows by more than 2^8, and runs the
-//               epilogue.
+//   warp 2      Q + V producer: TMA loads of Q, then V sub-blocks into a 4-stage ring
+//   warp 3      block-list construction in the prologue, idle afterwards
+//   warps 4-7   softmax group 0 (even steps), warps 8-11 softmax group 1 (odd steps). Thread r of
+//               a group owns query row r (TMEM lane r). It copies its 64 scores from TMEM to
+//               registers and at once releases the S buffer (the next QK MMA of the group can
+//               start), keeps a running max/sum, writes P (bf16) to its group's P columns in
+//               TMEM (the PV MMA reads P from TMEM) and rescales the group's O accumulator when
+//               the running max grows by more than 2^8. The two groups' partial results are
+//               merged by log-sum-exp in the epilogue.
 //
-// TMEM (512 columns): S double buffer at columns [0,128) and [128,256); O at [256,384).
-// MMAs: S = Q K^T (M=128, N=128, K=128, both K-major, 128-byte swizzle) and
-//       O += P V   (M=128, N=128, K=128 tokens; P K-major, V MN-major).
+// TMEM (512 columns allocated): S of group g at [64g, 64g+64), P of group g at [128+32g,
+// 160+32g), O of group g at [256+128g, 384+128g).
+// MMAs: S = Q K^T (M=128, N=64, K=128; A and B K-major in shared memory, 128-byte swizzle),
+//       O += P V   (M=128, N=128, K=64 tokens; A = P in TMEM, B = V MN-major in shared memory).
 // Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its TMA loads and MMAs,
 // frees TMEM, sets SS_DEV_TIMEOUT in *status and exits.
 #include "common.cuh"
@@ -38,28 +43,41 @@ namespace attn {
 constexpr int D = 128;
 constexpr int TILE_M = 128;
 constexpr int SUB = 64;
-constexpr int STAGES = 2;
-constexpr int NTHREADS = 256;
-constexpr uint32_t REGION = 16384;                 // 128 rows x 128 B: one 64-column half
-constexpr uint32_t Q_BYTES = 2 * REGION;           // 128 rows x 128 dims bf16
-constexpr uint32_t KV_BYTES = 2 * REGION;          // 128 tokens x 128 dims bf16
-constexpr uint32_t P_BYTES = 2 * REGION;           // 128 rows x 128 tokens bf16
+constexpr int KSTAGES = 4;
+constexpr int VSTAGES = 4;
+constexpr int NTHREADS = 384;
+constexpr uint32_t QREGION = 16384;                // 128 rows x 128 B: one 64-column half of Q
+constexpr uint32_t REGION = 8192;                  // 64 rows x 128 B: one 64-column half of a sub-block
+constexpr uint32_t Q_BYTES = 2 * QREGION;          // 128 rows x 128 dims bf16
+constexpr uint32_t KV_BYTES = 2 * REGION;          // 64 tokens x 128 dims bf16
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
-constexpr uint32_t OFF_V = OFF_K + STAGES * KV_BYTES;
-constexpr uint32_t OFF_P = OFF_V + STAGES * KV_BYTES;
-constexpr uint32_t OFF_BAR = OFF_P + P_BYTES;
-constexpr int NBAR = 16;
+constexpr uint32_t OFF_V = OFF_K + KSTAGES * KV_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
+constexpr int NBAR = 32;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t OFF_DYN = OFF_MISC + 64;        // bitmaps, then the sub-block list
+constexpr uint32_t OFF_ML = OFF_MISC + 64;         // [2 groups][128 rows] (m, l) for the merge
+constexpr uint32_t OFF_DYN = OFF_ML + 2 * 128 * 8; // bitmaps, then the sub-block list
 constexpr uint32_t SMEM_LIMIT = 232448;            // 227 KB opt-in maximum per CTA
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_O = 256;
+constexpr uint32_t TMEM_S = 0, TMEM_P = 128, TMEM_O = 256;
 
-enum Bar { Q_FULL = 0, K_FULL = 1, V_FULL = 3, K_EMPTY = 5, V_EMPTY = 7, S_FULL = 9, S_FREE = 11,
-           P_FULL = 13, O_DONE = 14, DRAIN = 15 };
+enum Bar {
+    Q_FULL = 0,
+    K_FULL = 1,
+    K_EMPTY = K_FULL + KSTAGES,
+    V_FULL = K_EMPTY + KSTAGES,
+    V_EMPTY = V_FULL + VSTAGES,
+    S_FULL = V_EMPTY + VSTAGES,  // per softmax group: QK result ready
+    S_FREE = S_FULL + 2,         // per group: scores copied out of TMEM
+    P_FULL = S_FREE + 2,         // per group: P written (and O rescaled)
+    P_FREE = P_FULL + 2,         // per group: PV done reading P (and O updated)
+    DRAIN = P_FREE + 2,
+    NBAR_USED
+};
+static_assert(NBAR_USED <= NBAR, "barrier space");
 
-constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128, false, false);
+constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 64, false, false);
 constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, 128, false, true);
 
 // sub-block entry: bits 0-19 first token, bits 20-26 valid tokens (0..64), bits 27-28 row-half mask
@@ -80,19 +98,61 @@ struct Params {
 
 __device__ __forceinline__ bool warp_all_ok(bool ok) { return __all_sync(0xffffffffu, ok) != 0; }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float f2_lo(uint64_t x) { return __uint_as_float((uint32_t)x); }
+__device__ __forceinline__ float f2_hi(uint64_t x) { return __uint_as_float((uint32_t)(x >> 32)); }
+
+// D[tmem] (+)= A[tmem] * B[smem]
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 __global__ void __launch_bounds__(NTHREADS, 1)
 sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t sQ = sbase + OFF_Q, sK = sbase + OFF_K, sV = sbase + OFF_V, sP = sbase + OFF_P;
+    const uint32_t sQ = sbase + OFF_Q, sK = sbase + OFF_K, sV = sbase + OFF_V;
     const uint32_t bar0 = sbase + OFF_BAR;
     auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
     volatile int *nsub_slot = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
     volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 12);
+    float2 *ml = reinterpret_cast<float2 *>(smem + OFF_ML);
     uint32_t *bmA = reinterpret_cast<uint32_t *>(smem + OFF_DYN);
     uint32_t *bmB = bmA + p.nwords;
     uint32_t *steps = bmB + p.nwords;
@@ -109,18 +169,20 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
         *abort_flag = 0;
         *badid_flag = 0;
         mbar_init(bar(Q_FULL), 1);
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < KSTAGES; ++s) {
             mbar_init(bar(K_FULL + s), 1);
-            mbar_init(bar(V_FULL + s), 1);
             mbar_init(bar(K_EMPTY + s), 1);
+        }
+        for (int s = 0; s < VSTAGES; ++s) {
+            mbar_init(bar(V_FULL + s), 1);
             mbar_init(bar(V_EMPTY + s), 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(bar(S_FULL + b), 1);
-            mbar_init(bar(S_FREE + b), 128);
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(bar(S_FULL + g), 1);
+            mbar_init(bar(S_FREE + g), 128);
+            mbar_init(bar(P_FULL + g), 128);
+            mbar_init(bar(P_FREE + g), 1);
         }
-        mbar_init(bar(P_FULL), 128);
-        mbar_init(bar(O_DONE), 1);
         mbar_init(bar(DRAIN), 1);
         fence_mbar_init();
     }
@@ -150,7 +212,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
         }
     }
     __syncthreads();
-    if (warp == 2) {
+    if (warp == 3) {
         // ascending compaction of the union bitmap into sub-block entries
         const int per = p.block / SUB;  // sub-blocks per router block
         int carry = 0;
@@ -177,225 +239,268 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
             }
             carry += __shfl_sync(0xffffffffu, incl, 31);
         }
-        if (lane == 0) {
-            if (carry & 1) steps[carry++] = entry(0u, 0u, 0u);  // pad to whole 128-token steps
-            *nsub_slot = carry;
-        }
+        if (lane == 0) *nsub_slot = carry;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int nsteps = *nsub_slot / 2;
+    const int nsteps = *nsub_slot;
+    const int xh = h * D;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- K producer ----------------
         if (lane == 0 && nsteps > 0) {
-            const int q0 = tile * TILE_M;
-            const int xh = h * D;
-            mbar_arrive_expect_tx(bar(Q_FULL), Q_BYTES);
-            tma_load_2d(sQ, &tm_q, xh, q0, bar(Q_FULL));
-            tma_load_2d(sQ + REGION, &tm_q, xh + 64, q0, bar(Q_FULL));
             int issued = 0;
             bool ok = true;
-            for (int j = 0; j < nsteps && ok; ++j) {
-                const int st = j % STAGES, it = j / STAGES;
-                const int t0 = e_start(steps[2 * j]), t1 = e_start(steps[2 * j + 1]);
+            for (int j = 0; j < nsteps; ++j) {
+                const int st = j % KSTAGES, it = j / KSTAGES;
                 if (it > 0) ok = mbar_wait(bar(K_EMPTY + st), (it - 1) & 1, abort_flag);
                 if (!ok) break;
+                const int t0 = e_start(steps[j]);
                 const uint32_t dk = sK + st * KV_BYTES;
                 mbar_arrive_expect_tx(bar(K_FULL + st), KV_BYTES);
                 tma_load_2d(dk, &tm_k, xh, t0, bar(K_FULL + st));
                 tma_load_2d(dk + REGION, &tm_k, xh + 64, t0, bar(K_FULL + st));
-                tma_load_2d(dk + REGION / 2, &tm_k, xh, t1, bar(K_FULL + st));
-                tma_load_2d(dk + REGION + REGION / 2, &tm_k, xh + 64, t1, bar(K_FULL + st));
-                if (it > 0) ok = mbar_wait(bar(V_EMPTY + st), (it - 1) & 1, abort_flag);
-                const uint32_t dv = sV + st * KV_BYTES;
-                if (ok) {
-                    mbar_arrive_expect_tx(bar(V_FULL + st), KV_BYTES);
-                    tma_load_2d(dv, &tm_v, xh, t0, bar(V_FULL + st));
-                    tma_load_2d(dv + REGION, &tm_v, xh + 64, t0, bar(V_FULL + st));
-                    tma_load_2d(dv + REGION / 2, &tm_v, xh, t1, bar(V_FULL + st));
-                    tma_load_2d(dv + REGION + REGION / 2, &tm_v, xh + 64, t1, bar(V_FULL + st));
-                }
                 issued = j + 1;
             }
-            if (!ok) {
-                // drain: the loads of the last STAGES steps may still be landing in shared memory
+            if (!ok) {  // drain: loads still landing in shared memory
                 volatile int never = 0;
-                for (int j = max(0, issued - STAGES); j < issued; ++j) {
-                    const int st = j % STAGES, it = j / STAGES;
-                    mbar_wait(bar(K_FULL + st), it & 1, &never);
-                    mbar_wait(bar(V_FULL + st), it & 1, &never);
-                }
-                mbar_wait(bar(Q_FULL), 0, &never);
+                for (int j = max(0, issued - KSTAGES); j < issued; ++j)
+                    mbar_wait(bar(K_FULL + j % KSTAGES), (j / KSTAGES) & 1, &never);
             }
+        }
+    } else if (warp == 2) {
+        // ---------------- Q + V producer ----------------
+        if (lane == 0 && nsteps > 0) {
+            mbar_arrive_expect_tx(bar(Q_FULL), Q_BYTES);
+            tma_load_2d(sQ, &tm_q, xh, tile * TILE_M, bar(Q_FULL));
+            tma_load_2d(sQ + QREGION, &tm_q, xh + 64, tile * TILE_M, bar(Q_FULL));
+            int issued = 0;
+            bool ok = true;
+            for (int j = 0; j < nsteps; ++j) {
+                const int st = j % VSTAGES, it = j / VSTAGES;
+                if (it > 0) ok = mbar_wait(bar(V_EMPTY + st), (it - 1) & 1, abort_flag);
+                if (!ok) break;
+                const int t0 = e_start(steps[j]);
+                const uint32_t dv = sV + st * KV_BYTES;
+                mbar_arrive_expect_tx(bar(V_FULL + st), KV_BYTES);
+                tma_load_2d(dv, &tm_v, xh, t0, bar(V_FULL + st));
+                tma_load_2d(dv + REGION, &tm_v, xh + 64, t0, bar(V_FULL + st));
+                issued = j + 1;
+            }
+            volatile int never = 0;
+            if (!ok) {
+                for (int j = max(0, issued - VSTAGES); j < issued; ++j)
+                    mbar_wait(bar(V_FULL + j % VSTAGES), (j / VSTAGES) & 1, &never);
+            }
+            mbar_wait(bar(Q_FULL), 0, &never);  // Q has landed before this warp can exit
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0 && nsteps > 0) {
             bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
             tc_fence_after();
-            auto issue_pv = [&](int i) -> bool {
-                const int st = i % STAGES, it = i / STAGES;
-                if (!mbar_wait(bar(P_FULL), i & 1, abort_flag)) return false;
-                if (!mbar_wait(bar(V_FULL + st), it & 1, abort_flag)) return false;
-                tc_fence_after();
-                const uint32_t dv = sV + st * KV_BYTES;
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint64_t a = smem_desc_sw128(sP + (kk >> 2) * REGION + (kk & 3) * 32, 16, 1024);
-                    const uint64_t b = smem_desc_sw128(dv + kk * 2048, REGION, 1024);
-                    mma_bf16_ss(tmem + TMEM_O, a, b, IDESC_PV, (i > 0 || kk > 0) ? 1u : 0u);
-                }
-                tc_commit(bar(O_DONE));
-                tc_commit(bar(V_EMPTY + st));
-                return true;
-            };
-            for (int j = 0; j < nsteps && ok; ++j) {
-                const int st = j % STAGES, it = j / STAGES, b = j & 1;
-                ok = mbar_wait(bar(K_FULL + st), it & 1, abort_flag);
-                if (ok && j >= 2) ok = mbar_wait(bar(S_FREE + b), ((j - 2) >> 1) & 1, abort_flag);
-                if (!ok) break;
+            auto issue_qk = [&](int j) -> bool {  // S_g = Q K_j^T
+                const int st = j % KSTAGES, it = j / KSTAGES, g = j & 1;
+                if (!mbar_wait(bar(K_FULL + st), it & 1, abort_flag)) return false;
                 tc_fence_after();
                 const uint32_t dk = sK + st * KV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * REGION + (kk & 3) * 32;
-                    const uint64_t a = smem_desc_sw128(sQ + off, 16, 1024);
-                    const uint64_t bd = smem_desc_sw128(dk + off, 16, 1024);
-                    mma_bf16_ss(tmem + b * 128, a, bd, IDESC_QK, kk > 0 ? 1u : 0u);
+                    mma_bf16_ss(tmem + TMEM_S + 64 * g,
+                                smem_desc_sw128(sQ + (kk >> 2) * QREGION + (kk & 3) * 32, 16, 1024),
+                                smem_desc_sw128(dk + (kk >> 2) * REGION + (kk & 3) * 32, 16, 1024), IDESC_QK,
+                                kk > 0 ? 1u : 0u);
                 }
-                tc_commit(bar(S_FULL + b));
+                tc_commit(bar(S_FULL + g));
                 tc_commit(bar(K_EMPTY + st));
-                if (j >= 1) ok = issue_pv(j - 1);
+                return true;
+            };
+            auto issue_pv = [&](int j) -> bool {  // O_g += P_g V_j
+                const int st = j % VSTAGES, it = j / VSTAGES, g = j & 1;
+                if (!mbar_wait(bar(P_FULL + g), (j >> 1) & 1, abort_flag)) return false;
+                if (!mbar_wait(bar(V_FULL + st), it & 1, abort_flag)) return false;
+                tc_fence_after();
+                const uint32_t dv = sV + st * KV_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_bf16_ts(tmem + TMEM_O + 128 * g, tmem + TMEM_P + 32 * g + kk * 8,
+                                smem_desc_sw128(dv + kk * 2048, REGION, 1024), IDESC_PV,
+                                (j >= 2 || kk > 0) ? 1u : 0u);
+                tc_commit(bar(P_FREE + g));
+                tc_commit(bar(V_EMPTY + st));
+                return true;
+            };
+            if (ok) ok = issue_qk(0);
+            if (ok && nsteps > 1) ok = issue_qk(1);
+            for (int j = 0; j < nsteps && ok; ++j) {
+                if (j + 2 < nsteps) {
+                    // the group's S buffer is free once its softmax copied step j's scores out
+                    ok = mbar_wait(bar(S_FREE + (j & 1)), (j >> 1) & 1, abort_flag);
+                    if (ok) ok = issue_qk(j + 2);
+                }
+                if (ok) ok = issue_pv(j);
             }
-            if (ok) issue_pv(nsteps - 1);
             // every MMA issued above has completed once DRAIN fires
             tc_commit(bar(DRAIN));
             volatile int never = 0;
             mbar_wait(bar(DRAIN), 0, &never);
         }
     } else if (warp >= 4) {
-        // ---------------- softmax + epilogue ----------------
-        const int r = tid - 128;            // row within the tile == TMEM lane
+        // ---------------- softmax groups + epilogue ----------------
+        const int grp = (warp - 4) >> 2;    // 0: even steps, 1: odd steps
+        const int r = (tid - 128) & 127;    // row within the tile == TMEM lane
         const int half = r >> 6;            // which 64-row query block of the pair
-        const uint32_t lane_addr = tmem + ((uint32_t)((r >> 5) * 32) << 16);
+        const uint32_t lane_base = tmem + ((uint32_t)((r >> 5) * 32) << 16);
+        const uint32_t s_addr = lane_base + TMEM_S + 64 * grp;
+        const uint32_t p_addr = lane_base + TMEM_P + 32 * grp;
+        const uint32_t o_addr = lane_base + TMEM_O + 128 * grp;
         const float sl2 = p.scale_log2;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
         float m = -INFINITY, l = 0.f;
-        bool ok = nsteps > 0;
-        for (int j = 0; j < nsteps && ok; ++j) {
-            const int b = j & 1;
-            ok = warp_all_ok(mbar_wait(bar(S_FULL + b), (j >> 1) & 1, abort_flag));
+        int mine = 0;                        // steps processed by this group
+        bool ok = true;
+        for (int j = grp; j < nsteps && ok; j += 2, ++mine) {
+            ok = warp_all_ok(mbar_wait(bar(S_FULL + grp), mine & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            float s[128];
-            tmem_ld32(lane_addr + b * 128 + 0, s + 0);
-            tmem_ld32(lane_addr + b * 128 + 32, s + 32);
-            tmem_ld32(lane_addr + b * 128 + 64, s + 64);
-            tmem_ld32(lane_addr + b * 128 + 96, s + 96);
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(bar(S_FREE + b));
-
-            const uint32_t e0 = steps[2 * j], e1 = steps[2 * j + 1];
-            const bool sel0 = (e0 >> (27 + half)) & 1u, sel1 = (e1 >> (27 + half)) & 1u;
-            const int v0 = sel0 ? e_valid(e0) : 0, v1 = sel1 ? e_valid(e1) : 0;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                s[c] = c < v0 ? s[c] : -INFINITY;
-                s[64 + c] = c < v1 ? s[64 + c] : -INFINITY;
-                mx = fmaxf(mx, fmaxf(s[c], s[64 + c]));
+            const uint32_t e = steps[j];
+            const bool sel = (e >> (27 + half)) & 1u;   // warp-uniform (a warp is within one half)
+            const int valid = sel ? e_valid(e) : 0;
+            float s[64];
+            if (sel) {
+                tmem_ld32(s_addr, s);
+                tmem_ld32(s_addr + 32, s + 32);
+                tmem_wait_ld();
             }
-            const float mnew = mx * sl2;
-            // P and O are single-buffered: PV of the previous step must be complete
-            if (j > 0) {
-                ok = warp_all_ok(mbar_wait(bar(O_DONE), (j - 1) & 1, abort_flag));
-                if (!ok) break;
-                tc_fence_after();
+            tc_fence_before();
+            mbar_arrive(bar(S_FREE + grp));
+            // row max over the valid columns (four independent chains)
+            float mx = -INFINITY;
+            if (sel) {
+                if (valid == SUB) {
+                    float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
+#pragma unroll
+                    for (int c = 4; c < 64; c += 8) {
+                        m0 = max3(m0, s[c], s[c + 1]);
+                        m1 = max3(m1, s[c + 2], s[c + 3]);
+                        m2 = max3(m2, s[c + 4], s[c + 5]);
+                        m3 = max3(m3, s[c + 6], s[c + 7]);
+                    }
+                    mx = max3(fmaxf(m0, m1), m2, m3);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 64; ++c) {
+                        s[c] = c < valid ? s[c] : -INFINITY;
+                        mx = fmaxf(mx, s[c]);
+                    }
+                }
             }
             // lazy rescale: move the reference max only when the row max grew by more than 2^8
+            const float mnew = mx * sl2;
             float alpha = 1.f;
             if (mnew > m + 8.0f) {
                 alpha = (m == -INFINITY) ? 0.f : ex2(m - mnew);
                 l *= alpha;
                 m = mnew;
             }
+            // P and O of this group are free once the group's previous PV has completed
+            if (mine > 0) {
+                ok = warp_all_ok(mbar_wait(bar(P_FREE + grp), (mine - 1) & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+            }
             // tcgen05.ld/st are warp-collective: the whole warp rescales if any of its rows must
-            const bool rescale = (j > 0) && __any_sync(0xffffffffu, alpha != 1.f);
+            const bool rescale = (mine > 0) && __any_sync(0xffffffffu, alpha != 1.f);
             if (rescale) {
-#pragma unroll
+#pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tmem_ld32(lane_addr + TMEM_O + 32 * c, o);
+                    tmem_ld32(o_addr + 32 * c, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int x = 0; x < 32; ++x) o[x] *= alpha;
-                    tmem_st32(lane_addr + TMEM_O + 32 * c, o);
+                    tmem_st32(o_addr + 32 * c, o);
                 }
             }
-            const float base = (m == -INFINITY) ? 0.f : m;
-            float rs = 0.f;
-            // P row r: tokens 0-63 in region 0, 64-127 in region 1; 16-byte chunks swizzled by r&7
+            // P = 2^(s*sl2 - m) as bf16 pairs into the group's P columns
+            uint32_t pk[32];
+            if (sel) {
+                const float base = (m == -INFINITY) ? 0.f : m;
+                const uint64_t nbx2 = f2_pack(-base, -base);
+                uint64_t sa = 0, sb = 0;
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                const bool sel = c < 8 ? sel0 : sel1;
-                float pv[8];
+                for (int c = 0; c < 64; c += 4) {
+                    const uint64_t x0 = f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, nbx2);
+                    const uint64_t x1 = f2_fma(f2_pack(s[c + 2], s[c + 3]), sl2x2, nbx2);
+                    const float p0 = ex2(f2_lo(x0)), p1 = ex2(f2_hi(x0));
+                    const float p2 = ex2(f2_lo(x1)), p3 = ex2(f2_hi(x1));
+                    sa = f2_add(sa, f2_pack(p0, p1));
+                    sb = f2_add(sb, f2_pack(p2, p3));
+                    pk[c >> 1] = pack_bf16x2(p0, p1);
+                    pk[(c >> 1) + 1] = pack_bf16x2(p2, p3);
+                }
+                const uint64_t st2 = f2_add(sa, sb);
+                l += f2_lo(st2) + f2_hi(st2);
+            } else {
 #pragma unroll
-                for (int x = 0; x < 8; ++x) pv[x] = sel ? ex2(fmaf(s[8 * c + x], sl2, -base)) : 0.f;
-                rs += ((pv[0] + pv[1]) + (pv[2] + pv[3])) + ((pv[4] + pv[5]) + (pv[6] + pv[7]));
-                const uint32_t addr = sP + (c >> 3) * REGION + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pack_bf16x2(pv[0], pv[1])),
-                             "r"(pack_bf16x2(pv[2], pv[3])), "r"(pack_bf16x2(pv[4], pv[5])),
-                             "r"(pack_bf16x2(pv[6], pv[7]))
-                             : "memory");
+                for (int x = 0; x < 32; ++x) pk[x] = 0u;
             }
-            l += rs;
-            if (rescale) tmem_wait_st();
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tmem_st16(p_addr, pk);
+            tmem_st16(p_addr + 16, pk + 16);
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(P_FULL));
+            mbar_arrive(bar(P_FULL + grp));
         }
-        bool have = ok && nsteps > 0;
-        if (have) have = warp_all_ok(mbar_wait(bar(O_DONE), (nsteps - 1) & 1, abort_flag));
+        // epilogue: both groups' O are final once each group's last PV has completed
+        bool have = ok && mine > 0;
+        if (have) have = warp_all_ok(mbar_wait(bar(P_FREE + grp), (mine - 1) & 1, abort_flag));
+        ml[grp * 128 + r] = make_float2(have ? m : -INFINITY, have ? l : 0.f);
+        tc_fence_before();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        tc_fence_after();
+        const float2 ml0 = ml[r], ml1 = ml[128 + r];
+        const float mt = fmaxf(ml0.x, ml1.x);
+        const float a0 = ml0.x == -INFINITY ? 0.f : ex2(ml0.x - mt);
+        const float a1 = ml1.x == -INFINITY ? 0.f : ex2(ml1.x - mt);
+        const float lt = a0 * ml0.y + a1 * ml1.y;
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        const float w0 = a0 * inv, w1 = a1 * inv;
         const int row = tile * TILE_M + r;
         const bool live = row < p.Lq && (pair ? (half == 0 ? qblkA < p.qb : qblkB < p.qb) : true);
-        if (have || nsteps == 0) {
-            if (have) tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
+        // warp-uniform conditions only: tcgen05.ld is warp-collective
+        const bool fin = __all_sync(0xffffffffu, !*abort_flag) != 0;
+        const bool has0 = fin && (nsteps + 1) / 2 > 0, has1 = fin && nsteps / 2 > 0;
+        // group g writes output columns [64g, 64g + 64) of its row
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+            const int col = 64 * grp + 32 * c;
+            float o0[32], o1[32];
+            if (has0) tmem_ld32(lane_base + TMEM_O + col, o0);
+            if (has1) tmem_ld32(lane_base + TMEM_O + 128 + col, o1);
+            tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float o[32];
-                if (have) {
-                    tmem_ld32(lane_addr + TMEM_O + 32 * c, o);
-                    tmem_wait_ld();
+            for (int x = 0; x < 32; ++x) o0[x] = (has0 ? o0[x] * w0 : 0.f) + (has1 ? o1[x] * w1 : 0.f);
+            if (live && fin) {
+                if (p.out_fp32) {
+                    float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) +
+                                                             ((size_t)row * p.H + h) * D + col);
+#pragma unroll
+                    for (int x = 0; x < 8; ++x) dst[x] = make_float4(o0[4 * x], o0[4 * x + 1], o0[4 * x + 2], o0[4 * x + 3]);
                 } else {
+                    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) +
+                                                           ((size_t)row * p.H + h) * D + col);
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) o[x] = 0.f;
-                }
-                if (live) {
-                    if (p.out_fp32) {
-                        float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) +
-                                                                 ((size_t)row * p.H + h) * D + 32 * c);
-#pragma unroll
-                        for (int x = 0; x < 8; ++x)
-                            dst[x] = make_float4(o[4 * x] * inv, o[4 * x + 1] * inv, o[4 * x + 2] * inv, o[4 * x + 3] * inv);
-                    } else {
-                        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) +
-                                                               ((size_t)row * p.H + h) * D + 32 * c);
-#pragma unroll
-                        for (int x = 0; x < 4; ++x)
-                            dst[x] = make_uint4(pack_bf16x2(o[8 * x] * inv, o[8 * x + 1] * inv),
-                                                pack_bf16x2(o[8 * x + 2] * inv, o[8 * x + 3] * inv),
-                                                pack_bf16x2(o[8 * x + 4] * inv, o[8 * x + 5] * inv),
-                                                pack_bf16x2(o[8 * x + 6] * inv, o[8 * x + 7] * inv));
-                    }
+                    for (int x = 0; x < 4; ++x)
+                        dst[x] = make_uint4(pack_bf16x2(o0[8 * x], o0[8 * x + 1]), pack_bf16x2(o0[8 * x + 2], o0[8 * x + 3]),
+                                            pack_bf16x2(o0[8 * x + 4], o0[8 * x + 5]),
+                                            pack_bf16x2(o0[8 * x + 6], o0[8 * x + 7]));
                 }
             }
-            if (live && p.lse)
-                p.lse[(size_t)h * p.Lq + row] = l > 0.f ? (m + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
         }
+        if (live && fin && grp == 0 && p.lse)
+            p.lse[(size_t)h * p.Lq + row] = lt > 0.f ? (mt + __log2f(lt)) * 0.69314718055994530942f : -INFINITY;
     }
     tc_fence_before();
     __syncthreads();
@@ -414,7 +519,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
 int attention_smem_bytes(int Lk, int block, int n_ids, uint32_t *bytes) {
     const int kb = (Lk + block - 1) / block;
     const int nwords = (kb + 31) / 32;
-    long max_sub = (block == 64) ? (long)std::min(2 * n_ids, kb) + 1 : 2L * std::min(n_ids, kb);
+    long max_sub = (block == 64) ? (long)std::min(2 * n_ids, kb) : 2L * std::min(n_ids, kb);
     long total = 1024 + attn::OFF_DYN + 8L * nwords + 4L * (max_sub + 2);
     *bytes = (uint32_t)total;
     return total <= (long)attn::SMEM_LIMIT ? 0 : SS_ERR_SMEM;

@@ -1,17 +1,23 @@
 // router.cu -- learned KV-block router for sm_100a in exact fp32.
 //
-//   1. pool_project: per (head, block) the mean of the block's valid tokens (fp32 adds in token
-//      order, one correctly rounded divide) projected by the head's [128 x R] matrix with fmaf in
-//      ascending row order. Reference: block pooling of migration/unified_router/opt19/
-//      prototype.py:11-49 (one prototype = plain mean), projection opt8/projection.py:4-14.
-//   2. block_scores: S[h,i,j] = <qh_i, kh_j> with fmaf in ascending order, -0 -> +0, non-finite
-//      scores flagged. Reference: the block-score GEMM `_coarse` of opt16/route.py:34-47.
-//   3. select_topk: forced blocks (sink, current chunk) plus the `extra` highest-scoring others,
-//      ties to the lower block index, ids written ascending. Reference: `_chosen`/`_top`
-//      (opt16/route.py:13-24,49-55), fixed_page_select (local_experiments/video_runtime_v1/
-//      fixed_page_select.py:7-21) and the forced set of pipeline_graph.py:140-151.
-// The fixed summation order makes the result bit-identical to the CPU oracle; the score GEMM is
-// a few tens of MFMA per chunk-layer, so CUDA-core FFMA costs microseconds.
+//   1. pool: per (head, block) the mean of the block's valid tokens -- fp32 adds in token order,
+//      one correctly rounded divide. One CTA reads a whole block of token rows (all heads) with
+//      coalesced 16-byte loads; thread (h, 8 dims) keeps 8 running sums.
+//      Reference: block pooling of migration/unified_router/opt19/prototype.py:11-49 (one
+//      prototype = plain mean of the valid tokens).
+//   2. project: pooled [nb x 128] @ W [128 x R] per head with fmaf in ascending row order,
+//      W staged in shared memory. Reference: opt8/projection.py:4-14.
+//   3. score_select: one warp per (head, query block). Scores S[j] = <qh, kh_j> (fmaf in
+//      ascending order, -0 -> +0, non-finite flagged) for every key block; the order-preserving
+//      uint32 of each unforced score stays in registers. The `extra`-th largest score T is found
+//      exactly by a 32-step bisection with warp-wide counts; blocks above T are kept and ties at
+//      T go to the lowest block indices (ordered ballot scan). Forced blocks (sink, current
+//      chunk) are always kept and ids are written ascending. Reference: the block-score GEMM
+//      `_coarse` (opt16/route.py:34-47), `_chosen`/`_top` (opt16/route.py:13-24,49-55),
+//      fixed_page_select (local_experiments/video_runtime_v1/fixed_page_select.py:7-21) and the
+//      forced set of local_experiments/video_runtime_v1/pipeline_graph.py:140-151.
+// The fixed summation order makes every score bit-identical to the CPU oracle. The score GEMM is
+// tens of MFMA per chunk-layer, so CUDA-core FFMA keeps it exact at a cost of microseconds.
 #include <algorithm>
 
 #include "common.cuh"
@@ -21,72 +27,116 @@ namespace router {
 
 constexpr int D = 128;
 constexpr int MAX_R = 128;
-constexpr int TOPK_THREADS = 256;
-constexpr int MAX_KB = 8192;
+constexpr int MAX_KB = 2048;       // score bits of a row live in registers (64 per lane)
+constexpr int PROJ_ROWS = 32;       // pooled rows per projection CTA
+constexpr int TILE_J = 64;          // key blocks staged per score tile
 
-__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// grid (nb, H), 128 threads: thread d owns dimension d of the block mean.
-__global__ void __launch_bounds__(128) pool_project_kernel(const uint16_t *__restrict__ x, int64_t row_stride, int L,
-                                                           int H, int block, const float *__restrict__ W, int R,
-                                                           float *__restrict__ proj) {
-    __shared__ float mean[D];
-    const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+// grid (nq + nk), H*16 threads. Block b < nq pools q, otherwise k; means -> [H][nb][128].
+__global__ void pool_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k, int H, int Lq, int Lk,
+                            int block, int nq, float *__restrict__ qmean, float *__restrict__ kmean) {
+    const bool isq = (int)blockIdx.x < nq;
+    const int b = isq ? blockIdx.x : blockIdx.x - nq;
+    const uint16_t *x = isq ? q : k;
+    const int L = isq ? Lq : Lk;
+    const int nb = isq ? nq : (Lk + block - 1) / block;
+    float *out = isq ? qmean : kmean;
     const int t0 = b * block;
     const int n = min(block, L - t0);
-    const uint16_t *src = x + (int64_t)t0 * row_stride + (int64_t)h * D + d;
-    float s = 0.f;
+    const int tid = threadIdx.x;            // = h*16 + chunk of 8 dims
+    const int row_vec = H * D / 8;          // uint4 per token row
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t0 * H * D) + tid;
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i] = 0.f;
     int t = 0;
     for (; t + 8 <= n; t += 8) {
-        uint16_t v[8];
+        uint4 v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (int64_t)(t + u) * row_stride);
+        for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (size_t)(t + u) * row_vec);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) s = __fadd_rn(s, bf16_to_f32(v[u]));
-    }
-    for (; t < n; ++t) s = __fadd_rn(s, bf16_to_f32(__ldg(src + (int64_t)t * row_stride)));
-    mean[d] = __fdiv_rn(s, (float)n);
-    __syncthreads();
-    const float *w = W + (int64_t)h * D * R;
-    for (int e = d; e < R; e += 128) {
-        float acc = 0.f;
-#pragma unroll 8
-        for (int k = 0; k < D; ++k) acc = __fmaf_rn(mean[k], __ldg(w + (int64_t)k * R + e), acc);
-        proj[((int64_t)h * gridDim.x + b) * R + e] = acc;
-    }
-}
-
-// grid (ceil(kb/64), ceil(qb/16), H), 256 threads: a 16 x 64 tile of scores, 4 per thread.
-__global__ void __launch_bounds__(256) block_scores_kernel(const float *__restrict__ qh, const float *__restrict__ kh,
-                                                           int qb, int kb, int R, float *__restrict__ S, int *status) {
-    extern __shared__ float sm[];
-    float *sq = sm;            // [16][R]
-    float *sk = sm + 16 * R;   // [64][R+1]
-    const int h = blockIdx.z, i0 = blockIdx.y * 16, j0 = blockIdx.x * 64, tid = threadIdx.x;
-    for (int x = tid; x < 16 * R; x += 256) {
-        int i = i0 + x / R;
-        sq[x] = i < qb ? qh[((int64_t)h * qb + i) * R + x % R] : 0.f;
-    }
-    for (int x = tid; x < 64 * R; x += 256) {
-        int j = j0 + x / R;
-        sk[(x / R) * (R + 1) + x % R] = j < kb ? kh[((int64_t)h * kb + j) * R + x % R] : 0.f;
-    }
-    __syncthreads();
-    const int jj = tid & 63, ib = (tid >> 6) * 4;
-    const int j = j0 + jj;
-    bool bad = false;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int i = i0 + ib + u;
-        float acc = 0.f;
-        for (int e = 0; e < R; ++e) acc = __fmaf_rn(sq[(ib + u) * R + e], sk[jj * (R + 1) + e], acc);
-        if (acc == 0.f) acc = 0.f;  // -0 -> +0
-        if (i < qb && j < kb) {
-            bad |= !isfinite(acc);
-            S[((int64_t)h * qb + i) * kb + j] = acc;
+        for (int u = 0; u < 8; ++u) {
+            s[0] = __fadd_rn(s[0], bf16_lo(v[u].x));
+            s[1] = __fadd_rn(s[1], bf16_hi(v[u].x));
+            s[2] = __fadd_rn(s[2], bf16_lo(v[u].y));
+            s[3] = __fadd_rn(s[3], bf16_hi(v[u].y));
+            s[4] = __fadd_rn(s[4], bf16_lo(v[u].z));
+            s[5] = __fadd_rn(s[5], bf16_hi(v[u].z));
+            s[6] = __fadd_rn(s[6], bf16_lo(v[u].w));
+            s[7] = __fadd_rn(s[7], bf16_hi(v[u].w));
         }
     }
-    if (bad) report(status, SS_DEV_NONFINITE);
+    for (; t < n; ++t) {
+        const uint4 v = __ldg(src + (size_t)t * row_vec);
+        s[0] = __fadd_rn(s[0], bf16_lo(v.x));
+        s[1] = __fadd_rn(s[1], bf16_hi(v.x));
+        s[2] = __fadd_rn(s[2], bf16_lo(v.y));
+        s[3] = __fadd_rn(s[3], bf16_hi(v.y));
+        s[4] = __fadd_rn(s[4], bf16_lo(v.z));
+        s[5] = __fadd_rn(s[5], bf16_hi(v.z));
+        s[6] = __fadd_rn(s[6], bf16_lo(v.w));
+        s[7] = __fadd_rn(s[7], bf16_hi(v.w));
+    }
+    const int h = tid >> 4, d0 = (tid & 15) * 8;
+    const float fn = (float)n;
+    float4 *dst = reinterpret_cast<float4 *>(out + ((size_t)h * nb + b) * D + d0);
+    dst[0] = make_float4(__fdiv_rn(s[0], fn), __fdiv_rn(s[1], fn), __fdiv_rn(s[2], fn), __fdiv_rn(s[3], fn));
+    dst[1] = make_float4(__fdiv_rn(s[4], fn), __fdiv_rn(s[5], fn), __fdiv_rn(s[6], fn), __fdiv_rn(s[7], fn));
+}
+
+// grid (tq + tk, H), 256 threads; tiles [0, tq) project q means with wq, the rest k means with wk.
+// Thread t owns row t / (R/8) of the tile and 8 consecutive output columns: eight independent
+// fmaf chains (each in ascending d order) keep the FMA pipe busy.
+__global__ void __launch_bounds__(256) project_kernel(const float *__restrict__ qmean, const float *__restrict__ kmean,
+                                                      const float *__restrict__ wq, const float *__restrict__ wk,
+                                                      int qb, int kb, int tq, int R, float *__restrict__ qh,
+                                                      float *__restrict__ kh) {
+    extern __shared__ float sm[];
+    float *sw = sm;                      // [128][R]
+    float *sx = sm + D * R;              // [PROJ_ROWS][129]
+    const int h = blockIdx.y;
+    const bool isq = (int)blockIdx.x < tq;
+    const int tile = isq ? blockIdx.x : blockIdx.x - tq;
+    const int nb = isq ? qb : kb;
+    const float *mean = (isq ? qmean : kmean) + (size_t)h * nb * D;
+    const float *w = (isq ? wq : wk) + (size_t)h * D * R;
+    float *out = (isq ? qh : kh) + (size_t)h * nb * R;
+    const int r0 = tile * PROJ_ROWS, rows = min(PROJ_ROWS, nb - r0);
+    for (int x = threadIdx.x; x < D * R / 4; x += 256)
+        reinterpret_cast<float4 *>(sw)[x] = reinterpret_cast<const float4 *>(w)[x];
+    for (int x = threadIdx.x; x < PROJ_ROWS * D; x += 256) {
+        const int rr = x / D, d = x % D;
+        sx[rr * (D + 1) + d] = rr < rows ? mean[(size_t)(r0 + rr) * D + d] : 0.f;
+    }
+    __syncthreads();
+    const int groups = R / 8;            // 8-column groups per row
+    for (int o = threadIdx.x; o < PROJ_ROWS * groups; o += 256) {
+        const int rr = o / groups, e0 = (o % groups) * 8;
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < D; ++d) {
+            const float x = sx[rr * (D + 1) + d];
+            const float4 w0 = reinterpret_cast<const float4 *>(sw + d * R + e0)[0];
+            const float4 w1 = reinterpret_cast<const float4 *>(sw + d * R + e0)[1];
+            acc[0] = __fmaf_rn(x, w0.x, acc[0]);
+            acc[1] = __fmaf_rn(x, w0.y, acc[1]);
+            acc[2] = __fmaf_rn(x, w0.z, acc[2]);
+            acc[3] = __fmaf_rn(x, w0.w, acc[3]);
+            acc[4] = __fmaf_rn(x, w1.x, acc[4]);
+            acc[5] = __fmaf_rn(x, w1.y, acc[5]);
+            acc[6] = __fmaf_rn(x, w1.z, acc[6]);
+            acc[7] = __fmaf_rn(x, w1.w, acc[7]);
+        }
+        if (rr < rows) {
+            float4 *dst = reinterpret_cast<float4 *>(out + (size_t)(r0 + rr) * R + e0);
+            dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        }
+    }
 }
 
 __device__ __forceinline__ bool is_forced(int j, int block, int Lq, int Lk, int sink) {
@@ -94,81 +144,132 @@ __device__ __forceinline__ bool is_forced(int j, int block, int Lq, int Lk, int 
     return lo < sink || hi > Lk - Lq;
 }
 
-__device__ __forceinline__ uint64_t score_key(float f, int j) {
-    if (f == 0.f) f = 0.f;
-    uint32_t u = __float_as_uint(f);
-    uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((uint64_t)o << 32) | (uint64_t)(0xffffffffu - (uint32_t)j);
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// one CTA per (head, query block) row; dynamic smem: npow2 uint64 keys
-__global__ void __launch_bounds__(TOPK_THREADS) select_topk_kernel(const float *__restrict__ S, int qb, int kb,
-                                                                   int block, int Lq, int Lk, int sink, int extra,
-                                                                   int npow2, int32_t *__restrict__ ids, int n_ids,
-                                                                   uint8_t *__restrict__ mask) {
-    extern __shared__ uint64_t keys[];
-    __shared__ int warp_tot[TOPK_THREADS / 32];
-    const int row = blockIdx.x, tid = threadIdx.x;
-    const float *srow = S + (int64_t)row * kb;
-    for (int j = tid; j < npow2; j += TOPK_THREADS)
-        keys[j] = (j < kb && !is_forced(j, block, Lq, Lk, sink)) ? score_key(srow[j], j) : 0ull;
-    __syncthreads();
-    // bitonic sort, descending
-    for (int size = 2; size <= npow2; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int t = tid; t < npow2 / 2; t += TOPK_THREADS) {
-                const int lo = 2 * t - (t & (stride - 1));
-                const int hi = lo + stride;
-                const bool desc = (lo & size) == 0;
-                const uint64_t a = keys[lo], b = keys[hi];
-                if ((a < b) == desc) {
-                    keys[lo] = b;
-                    keys[hi] = a;
-                }
+// One warp per (head, query block) row; `rows` warps per CTA share staged tiles of kh[h].
+// Key order: (ordered score bits, lower block index first). Lane owns blocks j = 32*i + lane,
+// i < NPL, with the score bits in registers (0 = not a candidate: forced or past kb; every
+// finite score maps to >= 0x00800000).
+//   1. T = the extra-th largest score value among candidates (32-step bisection on the bits).
+//   2. Blocks scoring above T are kept; of the blocks scoring exactly T, the lowest-index ones
+//      fill the remaining slots (ordered ballot scan).
+template <int NPL>
+__global__ void score_select_kernel(const float *__restrict__ qh, const float *__restrict__ kh, int qb, int kb, int R,
+                                    int block, int Lq, int Lk, int sink, int extra, int32_t *__restrict__ ids,
+                                    int n_ids, uint8_t *__restrict__ mask, float *__restrict__ scores, int *status) {
+    extern __shared__ float sm[];
+    const int rows = blockDim.x / 32;
+    float *sq = sm;                      // [rows][R]
+    float *sk = sm + rows * R;           // [TILE_J][R+1]
+    const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x * rows + warp;
+    const bool row_ok = i < qb;
+    for (int x = threadIdx.x; x < rows * R; x += blockDim.x) {
+        const int ii = blockIdx.x * rows + x / R;
+        sq[x] = ii < qb ? qh[((size_t)h * qb + ii) * R + x % R] : 0.f;
+    }
+    const float *myq = sq + warp * R;
+    uint32_t hi[NPL];
+#pragma unroll
+    for (int u = 0; u < NPL; ++u) hi[u] = 0u;
+    bool bad = false;
+    for (int j0 = 0; j0 < kb; j0 += TILE_J) {
+        const int nj = min(TILE_J, kb - j0);
+        __syncthreads();
+        for (int x = threadIdx.x; x < nj * R; x += blockDim.x)
+            sk[(x / R) * (R + 1) + x % R] = kh[((size_t)h * kb + j0 + x / R) * R + x % R];
+        __syncthreads();
+        if (row_ok) {
+            // lanes own columns lane and lane + 32 of this tile: two independent fmaf chains
+            const float *k0 = sk + lane * (R + 1), *k1 = sk + (lane + 32) * (R + 1);
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll 8
+            for (int e = 0; e < R; ++e) {
+                const float qe = myq[e];
+                a0 = __fmaf_rn(qe, k0[e], a0);
+                a1 = __fmaf_rn(qe, k1[e], a1);
             }
-            __syncthreads();
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float acc = c ? a1 : a0;
+                const int jj = lane + 32 * c;
+                const int j = j0 + jj;
+                if (acc == 0.f) acc = 0.f;  // -0 -> +0
+                const bool live = jj < nj;
+                bad |= live && !isfinite(acc);
+                if (live && scores) scores[((size_t)h * qb + i) * kb + j] = acc;
+                const uint32_t o = (!live || is_forced(j, block, Lq, Lk, sink)) ? 0u : ordered_bits(acc);
+                const int slot = (j0 >> 5) + c;   // = j >> 5, the same for all lanes
+#pragma unroll
+                for (int u = 0; u < NPL; ++u)
+                    if (u == slot && live) hi[u] = o;
+            }
         }
     }
-    const uint64_t cutoff = extra > 0 ? keys[extra - 1] : ~0ull;
-    // ascending compaction: thread tid owns the contiguous range [c0, c1)
-    const int per = (kb + TOPK_THREADS - 1) / TOPK_THREADS;
-    const int c0 = min(kb, tid * per), c1 = min(kb, c0 + per);
-    int cnt = 0;
-    for (int j = c0; j < c1; ++j) {
-        const bool f = is_forced(j, block, Lq, Lk, sink);
-        const bool sel = f || (extra > 0 && score_key(srow[j], j) >= cutoff);
-        cnt += sel;
-    }
-    int incl = cnt;
-    const int lane = tid & 31, warp = tid >> 5;
+    if (bad) report(status, SS_DEV_NONFINITE);
+    if (!row_ok) return;
+    uint32_t T = 0xffffffffu;
+    int need = 0;
+    if (extra > 0) {
+        T = 0u;
+        for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t cand = T | (1u << bit);
+            int cnt = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
+            for (int u = 0; u < NPL; ++u) cnt += hi[u] >= cand;
+            if ((int)__reduce_add_sync(0xffffffffu, (unsigned)cnt) >= extra) T = cand;
+        }
+        int gt = 0;
+#pragma unroll
+        for (int u = 0; u < NPL; ++u) gt += hi[u] > T;
+        need = extra - (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);  // ties at T to keep, >= 1
     }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    int off = 0;
-    for (int w = 0; w < warp; ++w) off += warp_tot[w];
-    int pos = off + incl - cnt;
-    int32_t *out = ids + (int64_t)row * n_ids;
-    for (int j = c0; j < c1; ++j) {
-        const bool f = is_forced(j, block, Lq, Lk, sink);
-        const bool sel = f || (extra > 0 && score_key(srow[j], j) >= cutoff);
-        if (sel && pos < n_ids) out[pos++] = j;
-        if (mask) mask[(int64_t)row * kb + j] = sel ? 1 : 0;
+    // ascending compaction of forced | above T | the first `need` ties at T
+    int32_t *out = ids + ((size_t)h * qb + i) * n_ids;
+    int pos = 0, taken = 0;
+#pragma unroll
+    for (int u = 0; u < NPL; ++u) {
+        const int j = 32 * u + lane;
+        if (32 * u >= kb) continue;   // warp-uniform
+        const bool tie = extra > 0 && j < kb && hi[u] == T;
+        const unsigned tb = __ballot_sync(0xffffffffu, tie);
+        const bool keep_tie = tie && taken + __popc(tb & ((1u << lane) - 1u)) < need;
+        taken += __popc(tb);
+        const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && hi[u] > T) || keep_tie);
+        const unsigned bal = __ballot_sync(0xffffffffu, sel);
+        const int off = pos + __popc(bal & ((1u << lane) - 1u));
+        if (sel && off < n_ids) out[off] = j;
+        if (mask && j < kb) mask[((size_t)h * qb + i) * kb + j] = sel ? 1 : 0;
+        pos += __popc(bal);
     }
 }
 
 }  // namespace router
+
+static size_t select_smem(int rows, int R) {
+    return (size_t)rows * R * 4 + (size_t)router::TILE_J * (R + 1) * 4;
+}
+
+using SelectFn = void (*)(const float *, const float *, int, int, int, int, int, int, int, int, int32_t *, int,
+                          uint8_t *, float *, int *);
+
+static SelectFn select_kernel(int kb) {
+    if (kb <= 128) return router::score_select_kernel<4>;
+    if (kb <= 512) return router::score_select_kernel<16>;
+    if (kb <= 1024) return router::score_select_kernel<32>;
+    return router::score_select_kernel<64>;
+}
 
 static int g_router_configured[64] = {0};
 
 int router_prepare(int device) {
     if (device < 0 || device >= 64) return SS_ERR_SHAPE;
     if (g_router_configured[device]) return 0;
-    cudaError_t e = cudaFuncSetAttribute(router::select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         router::MAX_KB * 8);
+    cudaError_t e = cudaFuncSetAttribute(router::project_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
     if (e != cudaSuccess) return (int)e;
     g_router_configured[device] = 1;
     return 0;
@@ -177,18 +278,21 @@ int router_prepare(int device) {
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct RouterLayout {
-    size_t qh, kh, s, total;
+    size_t qmean, kmean, qh, kh, total;
 };
 
 static RouterLayout router_layout(int H, int Lq, int Lk, int R, int block) {
     const size_t qb = (size_t)((Lq + block - 1) / block), kb = (size_t)((Lk + block - 1) / block);
     RouterLayout L;
-    L.qh = 0;
+    L.qmean = 0;
+    L.kmean = align256(L.qmean + 4 * (size_t)H * qb * router::D);
+    L.qh = align256(L.kmean + 4 * (size_t)H * kb * router::D);
     L.kh = align256(L.qh + 4 * (size_t)H * qb * R);
-    L.s = align256(L.kh + 4 * (size_t)H * kb * R);
-    L.total = align256(L.s + 4 * (size_t)H * qb * kb);
+    L.total = align256(L.kh + 4 * (size_t)H * kb * R);
     return L;
 }
+
+size_t router_workspace_size(int H, int Lq, int Lk, int R, int block) { return router_layout(H, Lq, Lk, R, block).total; }
 
 static int count_forced(int Lq, int Lk, int block, int sink) {
     const int kb = (Lk + block - 1) / block;
@@ -200,49 +304,51 @@ static int count_forced(int Lq, int Lk, int block, int sink) {
     return n;
 }
 
-// Launch the three router kernels with the intermediate tensors at the given device addresses.
-int router_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
-                  int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores_out,
-                  float *qh, float *kh, float *S, int *status, cudaStream_t st) {
-    const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block;
-    int device;
-    cudaError_t e = cudaGetDevice(&device);
-    if (e != cudaSuccess) return (int)e;
-    int rc = router_prepare(device);
-    if (rc) return rc;
-    float *Sbuf = scores_out ? scores_out : S;
-    const int64_t stride = (int64_t)H * router::D;
-    router::pool_project_kernel<<<dim3(qb, H), 128, 0, st>>>((const uint16_t *)q, stride, Lq, H, block, wq, R, qh);
-    router::pool_project_kernel<<<dim3(kb, H), 128, 0, st>>>((const uint16_t *)k, stride, Lk, H, block, wk, R, kh);
-    const size_t sm_scores = sizeof(float) * (16 * R + 64 * (R + 1));
-    router::block_scores_kernel<<<dim3((kb + 63) / 64, (qb + 15) / 16, H), 256, sm_scores, st>>>(qh, kh, qb, kb, R,
-                                                                                               Sbuf, status);
-    int npow2 = 1;
-    while (npow2 < kb) npow2 <<= 1;
-    router::select_topk_kernel<<<H * qb, router::TOPK_THREADS, (size_t)npow2 * 8, st>>>(
-        Sbuf, qb, kb, block, Lq, Lk, sink_tokens, extra, npow2, ids, n_ids, mask);
-    return (int)cudaGetLastError();
-}
-
 int router_check(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
                  int block, int sink_tokens, int extra, const int32_t *ids, int n_ids) {
     if (!q || !k || !wq || !wk || !ids) return SS_ERR_POINTER;
-    if (H <= 0 || Lq <= 0 || Lk < Lq || R <= 0 || R > router::MAX_R || (block != 64 && block != 128) ||
-        sink_tokens < 0)
+    if (H <= 0 || H > 64 || Lq <= 0 || Lk < Lq || R <= 0 || R > router::MAX_R || (R & 7) ||
+        (block != 64 && block != 128) || sink_tokens < 0)
         return SS_ERR_SHAPE;
     const int kb = (Lk + block - 1) / block;
     if (kb > router::MAX_KB) return SS_ERR_SHAPE;
     const int nforced = count_forced(Lq, Lk, block, sink_tokens);
     if (extra < 0 || extra > kb - nforced) return SS_ERR_BUDGET;
     if (n_ids != nforced + extra) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15u) return SS_ERR_POINTER;
     return 0;
+}
+
+// Launch the router kernels with the intermediates at the given device addresses
+// (ws points at a buffer of router_workspace_size bytes, 256-byte aligned).
+int router_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
+                  int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores,
+                  uint8_t *ws, int *status, cudaStream_t st) {
+    const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block;
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    int rc = router_prepare(device);
+    if (rc) return rc;
+    const RouterLayout L = router_layout(H, Lq, Lk, R, block);
+    float *qmean = reinterpret_cast<float *>(ws + L.qmean), *kmean = reinterpret_cast<float *>(ws + L.kmean);
+    float *qh = reinterpret_cast<float *>(ws + L.qh), *kh = reinterpret_cast<float *>(ws + L.kh);
+    router::pool_kernel<<<qb + kb, H * 16, 0, st>>>((const uint16_t *)q, (const uint16_t *)k, H, Lq, Lk, block, qb,
+                                                   qmean, kmean);
+    const int tq = (qb + router::PROJ_ROWS - 1) / router::PROJ_ROWS, tk = (kb + router::PROJ_ROWS - 1) / router::PROJ_ROWS;
+    const size_t sm_proj = sizeof(float) * ((size_t)router::D * R + router::PROJ_ROWS * (router::D + 1));
+    router::project_kernel<<<dim3(tq + tk, H), 256, sm_proj, st>>>(qmean, kmean, wq, wk, qb, kb, tq, R, qh, kh);
+    const int rows = 4;
+    select_kernel(kb)<<<dim3((qb + rows - 1) / rows, H), rows * 32, select_smem(rows, R), st>>>(
+        qh, kh, qb, kb, R, block, Lq, Lk, sink_tokens, extra, ids, n_ids, mask, scores, status);
+    return (int)cudaGetLastError();
 }
 
 }  // namespace ss
 
 extern "C" int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes) {
     if (!bytes || H <= 0 || Lq <= 0 || Lk <= 0 || R <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
-    *bytes = ss::router_layout(H, Lq, Lk, R, block).total;
+    *bytes = ss::router_workspace_size(H, Lq, Lk, R, block);
     return 0;
 }
 
@@ -251,12 +357,9 @@ extern "C" int ss_router(const void *q, const void *k, const float *wq, const fl
                          void *workspace, size_t workspace_bytes, int *status, void *stream) {
     int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
     if (rc) return rc;
-    const ss::RouterLayout L = ss::router_layout(H, Lq, Lk, R, block);
     if (!workspace) return SS_ERR_POINTER;
-    if (workspace_bytes < L.total) return SS_ERR_WORKSPACE;
+    if (workspace_bytes < ss::router_workspace_size(H, Lq, Lk, R, block)) return SS_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return SS_ERR_POINTER;
-    uint8_t *ws = static_cast<uint8_t *>(workspace);
     return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
-                             reinterpret_cast<float *>(ws + L.qh), reinterpret_cast<float *>(ws + L.kh),
-                             reinterpret_cast<float *>(ws + L.s), status, static_cast<cudaStream_t>(stream));
+                             static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream));
 }
