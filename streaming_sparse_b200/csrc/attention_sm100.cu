@@ -11,28 +11,32 @@
 // Work decomposition
 //   One CTA per (head, 128-row query tile). With 64-token router blocks a tile holds two query
 //   blocks; the CTA walks the union of their block lists and masks, per 64-row half, the blocks
-//   that half did not select. With 128-token blocks a tile is exactly one query block and each
-//   block is walked as two 64-token sub-blocks. One step = one 64-token sub-block, gathered by
-//   TMA at its own row offset. CTAs are ordered head-major so the CTAs resident at one time
-//   share a few heads' K/V in L2.
+//   that half did not select. With 128-token blocks a tile is exactly one query block.
+//   The union is walked in steps of 128 KV tokens (two 64-token sub-blocks, each gathered by
+//   TMA at its own row offset, so the two need not be adjacent). CTAs are ordered head-major
+//   so the CTAs resident at one time share a few heads' K/V in L2.
 //
-// Warp roles (384 threads)
-//   warp 0      K producer: TMA loads of K sub-blocks into a 4-stage ring
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warp 2      Q + V producer: TMA loads of Q, then V sub-blocks into a 4-stage ring
+// Warp roles (384 threads; every role runs on a whole converged warp and issues its
+// single-thread instructions -- TMA, tcgen05.mma, tcgen05.commit -- from an elected lane)
+//   warp 0      K producer: TMA loads of K steps into a 3-stage ring
+//   warp 1      TMEM allocator + tcgen05.mma issuer
+//   warp 2      V producer: TMA loads of V steps into a 3-stage ring
 //   warp 3      block-list construction in the prologue, idle afterwards
-//   warps 4-7   softmax group 0 (even steps), warps 8-11 softmax group 1 (odd steps). Thread r of
-//               a group owns query row r (TMEM lane r). It copies its 64 scores from TMEM to
-//               registers and at once releases the S buffer (the next QK MMA of the group can
-//               start), keeps a running max/sum, writes P (bf16) to its group's P columns in
-//               TMEM (the PV MMA reads P from TMEM) and rescales the group's O accumulator when
-//               the running max grows by more than 2^8. The two groups' partial results are
-//               merged by log-sum-exp in the epilogue.
+//   warps 4-11  softmax: group g (warps 4+4g .. 7+4g) owns sub-block g of every step, i.e. score
+//               columns [64g, 64g+64). In the prologue the groups copy the Q tile into TMEM (the QK
+//               MMA reads Q from TMEM, so shared-memory bandwidth goes to K and V only). Thread r
+//               of a group owns query row r (TMEM lane r). Per step both groups read their 64
+//               scores, exchange the row maximum through shared memory, keep identical running
+//               maxima, write P (bf16) over the scores they consumed (the PV MMA reads P from
+//               TMEM) and each rescale their half of the shared O accumulator when the running
+//               max grows by more than 2^8.
 //
-// TMEM (512 columns allocated): S of group g at [64g, 64g+64), P of group g at [128+32g,
-// 160+32g), O of group g at [256+128g, 384+128g).
-// MMAs: S = Q K^T (M=128, N=64, K=128; A and B K-major in shared memory, 128-byte swizzle),
-//       O += P V   (M=128, N=128, K=64 tokens; A = P in TMEM, B = V MN-major in shared memory).
+// TMEM (512 columns): S of step parity b at [128b, 128b+128) with P written over columns
+// [128b+64g, 128b+64g+32) by group g; Q (bf16 pairs) at [256, 320); O at [384, 512).
+// MMAs: S = Q K^T (M=128, N=128, K=128; A = Q in TMEM, B = K K-major in shared memory, 128-byte
+//       swizzle), O += P V (M=128, N=128, K=128 tokens; A = P in TMEM, B = V MN-major in shared
+//       memory). tcgen05.mma instructions of one thread execute in order, so the QK MMA that
+//       reuses an S buffer (issued after the PV MMA that reads P from it) cannot overtake that read.
 // Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its TMA loads and MMAs,
 // frees TMEM, sets SS_DEV_TIMEOUT in *status and exits.
 #include "common.cuh"
@@ -43,41 +47,40 @@ namespace attn {
 constexpr int D = 128;
 constexpr int TILE_M = 128;
 constexpr int SUB = 64;
-constexpr int KSTAGES = 4;
-constexpr int VSTAGES = 4;
+constexpr int KSTAGES = 3;
+constexpr int VSTAGES = 3;
 constexpr int NTHREADS = 384;
-constexpr uint32_t QREGION = 16384;                // 128 rows x 128 B: one 64-column half of Q
-constexpr uint32_t REGION = 8192;                  // 64 rows x 128 B: one 64-column half of a sub-block
-constexpr uint32_t Q_BYTES = 2 * QREGION;          // 128 rows x 128 dims bf16
-constexpr uint32_t KV_BYTES = 2 * REGION;          // 64 tokens x 128 dims bf16
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+constexpr uint32_t REGION = 16384;                 // 128 rows x 128 B: one 64-column half of a step
+constexpr uint32_t KV_BYTES = 2 * REGION;          // 128 tokens x 128 dims bf16
+constexpr uint32_t OFF_K = 0;
 constexpr uint32_t OFF_V = OFF_K + KSTAGES * KV_BYTES;
 constexpr uint32_t OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
-constexpr int NBAR = 32;
+constexpr int NBAR = 24;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t OFF_ML = OFF_MISC + 64;         // [2 groups][128 rows] (m, l) for the merge
-constexpr uint32_t OFF_DYN = OFF_ML + 2 * 128 * 8; // bitmaps, then the sub-block list
+constexpr uint32_t OFF_RED = OFF_MISC + 64;        // [2 step parities][2 groups][128 rows] row maxima
+constexpr uint32_t OFF_LSUM = OFF_RED + 2 * 2 * 128 * 4; // [2 groups][128 rows] partial row sums
+constexpr uint32_t OFF_DYN = OFF_LSUM + 2 * 128 * 4;   // bitmaps, then the sub-block list
 constexpr uint32_t SMEM_LIMIT = 232448;            // 227 KB opt-in maximum per CTA
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_S = 0, TMEM_P = 128, TMEM_O = 256;
+constexpr uint32_t TMEM_S = 0, TMEM_Q = 256, TMEM_O = 384;
 
 enum Bar {
-    Q_FULL = 0,
+    Q_FULL = 0,                  // Q tile copied into TMEM (256 softmax threads)
     K_FULL = 1,
     K_EMPTY = K_FULL + KSTAGES,
     V_FULL = K_EMPTY + KSTAGES,
     V_EMPTY = V_FULL + VSTAGES,
-    S_FULL = V_EMPTY + VSTAGES,  // per softmax group: QK result ready
-    S_FREE = S_FULL + 2,         // per group: scores copied out of TMEM
-    P_FULL = S_FREE + 2,         // per group: P written (and O rescaled)
-    P_FREE = P_FULL + 2,         // per group: PV done reading P (and O updated)
-    DRAIN = P_FREE + 2,
+    S_FULL = V_EMPTY + VSTAGES,  // per S buffer (step parity): QK result ready
+    P_FULL = S_FULL + 2,         // per step parity: P written by both groups (256 arrivals)
+    O_DONE = P_FULL + 2,         // PV of a step completed (O up to date, P consumed)
+    XCHG = O_DONE + 1,           // per step parity: both groups' row maxima written (256 arrivals)
+    XSUM = XCHG + 2,             // epilogue: both groups' row sums written (256 arrivals)
+    DRAIN = XSUM + 1,
     NBAR_USED
 };
 static_assert(NBAR_USED <= NBAR, "barrier space");
 
-constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 64, false, false);
+constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128, false, false);
 constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, 128, false, true);
 
 // sub-block entry: bits 0-19 first token, bits 20-26 valid tokens (0..64), bits 27-28 row-half mask
@@ -88,6 +91,7 @@ __device__ __forceinline__ int e_start(uint32_t e) { return (int)(e & 0xFFFFFu);
 __device__ __forceinline__ int e_valid(uint32_t e) { return (int)((e >> 20) & 127u); }
 
 struct Params {
+    const __nv_bfloat16 *q;
     const int32_t *ids;
     void *out;
     float *lse;
@@ -140,19 +144,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1)
-sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const Params p) {
+sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                        const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t sQ = sbase + OFF_Q, sK = sbase + OFF_K, sV = sbase + OFF_V;
+    const uint32_t sK = sbase + OFF_K, sV = sbase + OFF_V;
     const uint32_t bar0 = sbase + OFF_BAR;
     auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
     volatile int *nsub_slot = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
     volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 12);
-    float2 *ml = reinterpret_cast<float2 *>(smem + OFF_ML);
+    float *red = reinterpret_cast<float *>(smem + OFF_RED);
+    float *lsum = reinterpret_cast<float *>(smem + OFF_LSUM);
     uint32_t *bmA = reinterpret_cast<uint32_t *>(smem + OFF_DYN);
     uint32_t *bmB = bmA + p.nwords;
     uint32_t *steps = bmB + p.nwords;
@@ -168,7 +173,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
     if (tid == 0) {
         *abort_flag = 0;
         *badid_flag = 0;
-        mbar_init(bar(Q_FULL), 1);
+        mbar_init(bar(Q_FULL), 256);
         for (int s = 0; s < KSTAGES; ++s) {
             mbar_init(bar(K_FULL + s), 1);
             mbar_init(bar(K_EMPTY + s), 1);
@@ -177,17 +182,17 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
             mbar_init(bar(V_FULL + s), 1);
             mbar_init(bar(V_EMPTY + s), 1);
         }
-        for (int g = 0; g < 2; ++g) {
-            mbar_init(bar(S_FULL + g), 1);
-            mbar_init(bar(S_FREE + g), 128);
-            mbar_init(bar(P_FULL + g), 128);
-            mbar_init(bar(P_FREE + g), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(S_FULL + b), 1);
+            mbar_init(bar(P_FULL + b), 256);
+            mbar_init(bar(XCHG + b), 256);
         }
+        mbar_init(bar(O_DONE), 1);
+        mbar_init(bar(XSUM), 256);
         mbar_init(bar(DRAIN), 1);
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
         prefetch_tmap(&tm_v);
     }
@@ -239,146 +244,151 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
             }
             carry += __shfl_sync(0xffffffffu, incl, 31);
         }
-        if (lane == 0) *nsub_slot = carry;
+        if (lane == 0) {
+            if (carry & 1) steps[carry++] = entry(0u, 0u, 0u);  // pad to whole 128-token steps
+            *nsub_slot = carry;
+        }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int nsteps = *nsub_slot;
+    const int nsteps = *nsub_slot / 2;
     const int xh = h * D;
 
-    if (warp == 0) {
-        // ---------------- K producer ----------------
-        if (lane == 0 && nsteps > 0) {
-            int issued = 0;
-            bool ok = true;
-            for (int j = 0; j < nsteps; ++j) {
-                const int st = j % KSTAGES, it = j / KSTAGES;
-                if (it > 0) ok = mbar_wait(bar(K_EMPTY + st), (it - 1) & 1, abort_flag);
-                if (!ok) break;
-                const int t0 = e_start(steps[j]);
-                const uint32_t dk = sK + st * KV_BYTES;
-                mbar_arrive_expect_tx(bar(K_FULL + st), KV_BYTES);
-                tma_load_2d(dk, &tm_k, xh, t0, bar(K_FULL + st));
-                tma_load_2d(dk + REGION, &tm_k, xh + 64, t0, bar(K_FULL + st));
-                issued = j + 1;
+    if (warp == 0 || warp == 2) {
+        // ---------------- K (warp 0) / V (warp 2) producer ----------------
+        const bool isk = warp == 0;
+        const CUtensorMap *tm = isk ? &tm_k : &tm_v;
+        const uint32_t ring = isk ? sK : sV;
+        const int stages = isk ? KSTAGES : VSTAGES;
+        const int full = isk ? K_FULL : V_FULL, empty = isk ? K_EMPTY : V_EMPTY;
+        int issued = 0;
+        bool ok = true;
+        for (int j = 0; j < nsteps; ++j) {
+            const int st = j % stages, it = j / stages;
+            if (it > 0) ok = warp_all_ok(mbar_wait(bar(empty + st), (it - 1) & 1, abort_flag));
+            if (!ok) break;
+            const int t0 = e_start(steps[2 * j]), t1 = e_start(steps[2 * j + 1]);
+            const uint32_t dst = ring + st * KV_BYTES;
+            if (elect_one()) {
+                mbar_arrive_expect_tx(bar(full + st), KV_BYTES);
+                tma_load_2d(dst, tm, xh, t0, bar(full + st));
+                tma_load_2d(dst + REGION, tm, xh + 64, t0, bar(full + st));
+                tma_load_2d(dst + REGION / 2, tm, xh, t1, bar(full + st));
+                tma_load_2d(dst + REGION + REGION / 2, tm, xh + 64, t1, bar(full + st));
             }
-            if (!ok) {  // drain: loads still landing in shared memory
-                volatile int never = 0;
-                for (int j = max(0, issued - KSTAGES); j < issued; ++j)
-                    mbar_wait(bar(K_FULL + j % KSTAGES), (j / KSTAGES) & 1, &never);
-            }
+            __syncwarp();
+            issued = j + 1;
         }
-    } else if (warp == 2) {
-        // ---------------- Q + V producer ----------------
-        if (lane == 0 && nsteps > 0) {
-            mbar_arrive_expect_tx(bar(Q_FULL), Q_BYTES);
-            tma_load_2d(sQ, &tm_q, xh, tile * TILE_M, bar(Q_FULL));
-            tma_load_2d(sQ + QREGION, &tm_q, xh + 64, tile * TILE_M, bar(Q_FULL));
-            int issued = 0;
-            bool ok = true;
-            for (int j = 0; j < nsteps; ++j) {
-                const int st = j % VSTAGES, it = j / VSTAGES;
-                if (it > 0) ok = mbar_wait(bar(V_EMPTY + st), (it - 1) & 1, abort_flag);
-                if (!ok) break;
-                const int t0 = e_start(steps[j]);
-                const uint32_t dv = sV + st * KV_BYTES;
-                mbar_arrive_expect_tx(bar(V_FULL + st), KV_BYTES);
-                tma_load_2d(dv, &tm_v, xh, t0, bar(V_FULL + st));
-                tma_load_2d(dv + REGION, &tm_v, xh + 64, t0, bar(V_FULL + st));
-                issued = j + 1;
-            }
+        if (!ok) {  // drain: loads still landing in shared memory
             volatile int never = 0;
-            if (!ok) {
-                for (int j = max(0, issued - VSTAGES); j < issued; ++j)
-                    mbar_wait(bar(V_FULL + j % VSTAGES), (j / VSTAGES) & 1, &never);
-            }
-            mbar_wait(bar(Q_FULL), 0, &never);  // Q has landed before this warp can exit
+            for (int j = max(0, issued - stages); j < issued; ++j)
+                mbar_wait(bar(full + j % stages), (j / stages) & 1, &never);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0 && nsteps > 0) {
-            bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag);
+        if (nsteps > 0) {
+            bool ok = warp_all_ok(mbar_wait(bar(Q_FULL), 0, abort_flag));
             tc_fence_after();
-            auto issue_qk = [&](int j) -> bool {  // S_g = Q K_j^T
-                const int st = j % KSTAGES, it = j / KSTAGES, g = j & 1;
-                if (!mbar_wait(bar(K_FULL + st), it & 1, abort_flag)) return false;
+            auto issue_qk = [&](int j) -> bool {  // S_(j&1) = Q K_j^T
+                const int st = j % KSTAGES, it = j / KSTAGES, b = j & 1;
+                if (!warp_all_ok(mbar_wait(bar(K_FULL + st), it & 1, abort_flag))) return false;
                 tc_fence_after();
                 const uint32_t dk = sK + st * KV_BYTES;
+                if (elect_one()) {
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    mma_bf16_ss(tmem + TMEM_S + 64 * g,
-                                smem_desc_sw128(sQ + (kk >> 2) * QREGION + (kk & 3) * 32, 16, 1024),
-                                smem_desc_sw128(dk + (kk >> 2) * REGION + (kk & 3) * 32, 16, 1024), IDESC_QK,
-                                kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_bf16_ts(tmem + TMEM_S + 128 * b, tmem + TMEM_Q + kk * 8,
+                                    smem_desc_sw128(dk + (kk >> 2) * REGION + (kk & 3) * 32, 16, 1024), IDESC_QK,
+                                    kk > 0 ? 1u : 0u);
+                    tc_commit(bar(S_FULL + b));
+                    tc_commit(bar(K_EMPTY + st));
                 }
-                tc_commit(bar(S_FULL + g));
-                tc_commit(bar(K_EMPTY + st));
+                __syncwarp();
                 return true;
             };
-            auto issue_pv = [&](int j) -> bool {  // O_g += P_g V_j
-                const int st = j % VSTAGES, it = j / VSTAGES, g = j & 1;
-                if (!mbar_wait(bar(P_FULL + g), (j >> 1) & 1, abort_flag)) return false;
-                if (!mbar_wait(bar(V_FULL + st), it & 1, abort_flag)) return false;
+            auto issue_pv = [&](int j) -> bool {  // O += P_j V_j
+                const int st = j % VSTAGES, it = j / VSTAGES, b = j & 1;
+                if (!warp_all_ok(mbar_wait(bar(P_FULL + b), (j >> 1) & 1, abort_flag))) return false;
+                if (!warp_all_ok(mbar_wait(bar(V_FULL + st), it & 1, abort_flag))) return false;
                 tc_fence_after();
                 const uint32_t dv = sV + st * KV_BYTES;
+                if (elect_one()) {
+                    // tokens 16kk.. of the step: P of sub-block kk/4 sits at columns 64*(kk/4) of S_b
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_bf16_ts(tmem + TMEM_O + 128 * g, tmem + TMEM_P + 32 * g + kk * 8,
-                                smem_desc_sw128(dv + kk * 2048, REGION, 1024), IDESC_PV,
-                                (j >= 2 || kk > 0) ? 1u : 0u);
-                tc_commit(bar(P_FREE + g));
-                tc_commit(bar(V_EMPTY + st));
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_bf16_ts(tmem + TMEM_O, tmem + TMEM_S + 128 * b + 64 * (kk >> 2) + 8 * (kk & 3),
+                                    smem_desc_sw128(dv + kk * 2048, REGION, 1024), IDESC_PV,
+                                    (j > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(bar(O_DONE));
+                    tc_commit(bar(V_EMPTY + st));
+                }
+                __syncwarp();
                 return true;
             };
             if (ok) ok = issue_qk(0);
             if (ok && nsteps > 1) ok = issue_qk(1);
             for (int j = 0; j < nsteps && ok; ++j) {
-                if (j + 2 < nsteps) {
-                    // the group's S buffer is free once its softmax copied step j's scores out
-                    ok = mbar_wait(bar(S_FREE + (j & 1)), (j >> 1) & 1, abort_flag);
-                    if (ok) ok = issue_qk(j + 2);
-                }
-                if (ok) ok = issue_pv(j);
+                ok = issue_pv(j);
+                if (ok && j + 2 < nsteps) ok = issue_qk(j + 2);
             }
             // every MMA issued above has completed once DRAIN fires
-            tc_commit(bar(DRAIN));
+            if (elect_one()) tc_commit(bar(DRAIN));
+            __syncwarp();
             volatile int never = 0;
             mbar_wait(bar(DRAIN), 0, &never);
         }
     } else if (warp >= 4) {
         // ---------------- softmax groups + epilogue ----------------
-        const int grp = (warp - 4) >> 2;    // 0: even steps, 1: odd steps
+        const int grp = (warp - 4) >> 2;    // sub-block (score columns [64g, 64g+64)) of each step
         const int r = (tid - 128) & 127;    // row within the tile == TMEM lane
         const int half = r >> 6;            // which 64-row query block of the pair
         const uint32_t lane_base = tmem + ((uint32_t)((r >> 5) * 32) << 16);
-        const uint32_t s_addr = lane_base + TMEM_S + 64 * grp;
-        const uint32_t p_addr = lane_base + TMEM_P + 32 * grp;
-        const uint32_t o_addr = lane_base + TMEM_O + 128 * grp;
+        const int row = tile * TILE_M + r;
+        // Q tile -> TMEM: group g copies dims [64g, 64g + 64) of row r as bf16 pairs
+        {
+            uint32_t qv[32];
+            if (row < p.Lq) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)row * p.H + h) * D + 64 * grp);
+#pragma unroll
+                for (int x = 0; x < 8; ++x) {
+                    const uint4 v = src[x];
+                    qv[4 * x] = v.x;
+                    qv[4 * x + 1] = v.y;
+                    qv[4 * x + 2] = v.z;
+                    qv[4 * x + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int x = 0; x < 32; ++x) qv[x] = 0u;
+            }
+            tmem_st32(lane_base + TMEM_Q + 32 * grp, reinterpret_cast<const float *>(qv));
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(Q_FULL));
+        }
+        const uint32_t o_addr = lane_base + TMEM_O + 64 * grp;   // this group's half of O
         const float sl2 = p.scale_log2;
         const uint64_t sl2x2 = f2_pack(sl2, sl2);
-        float m = -INFINITY, l = 0.f;
-        int mine = 0;                        // steps processed by this group
+        float m = -INFINITY, l = 0.f;        // m identical in both groups; l partial per group
         bool ok = true;
-        for (int j = grp; j < nsteps && ok; j += 2, ++mine) {
-            ok = warp_all_ok(mbar_wait(bar(S_FULL + grp), mine & 1, abort_flag));
+        int j = 0;
+        for (; j < nsteps && ok; ++j) {
+            const int b = j & 1;
+            ok = warp_all_ok(mbar_wait(bar(S_FULL + b), (j >> 1) & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            const uint32_t e = steps[j];
+            const uint32_t s_addr = lane_base + TMEM_S + 128 * b + 64 * grp;
+            const uint32_t e = steps[2 * j + grp];
             const bool sel = (e >> (27 + half)) & 1u;   // warp-uniform (a warp is within one half)
             const int valid = sel ? e_valid(e) : 0;
             float s[64];
+            float mx = -INFINITY;
             if (sel) {
                 tmem_ld32(s_addr, s);
                 tmem_ld32(s_addr + 32, s + 32);
                 tmem_wait_ld();
-            }
-            tc_fence_before();
-            mbar_arrive(bar(S_FREE + grp));
-            // row max over the valid columns (four independent chains)
-            float mx = -INFINITY;
-            if (sel) {
                 if (valid == SUB) {
                     float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
 #pragma unroll
@@ -397,6 +407,14 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
                     }
                 }
             }
+            // row max of the whole step: exchange with the other group (bounded mbarrier wait; a
+            // slot is rewritten two steps later, after every thread passed the next exchange)
+            float *rb = red + (b * 2) * 128;
+            rb[grp * 128 + r] = mx;
+            mbar_arrive(bar(XCHG + b));
+            ok = warp_all_ok(mbar_wait(bar(XCHG + b), (j >> 1) & 1, abort_flag));
+            if (!ok) break;
+            mx = fmaxf(mx, rb[(grp ^ 1) * 128 + r]);
             // lazy rescale: move the reference max only when the row max grew by more than 2^8
             const float mnew = mx * sl2;
             float alpha = 1.f;
@@ -405,17 +423,14 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
                 l *= alpha;
                 m = mnew;
             }
-            // P and O of this group are free once the group's previous PV has completed
-            if (mine > 0) {
-                ok = warp_all_ok(mbar_wait(bar(P_FREE + grp), (mine - 1) & 1, abort_flag));
+            // O changes only through PV of the previous step; tcgen05.ld/st are warp-collective, so
+            // the whole warp rescales its half of O if any of its rows must.
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                ok = warp_all_ok(mbar_wait(bar(O_DONE), (j - 1) & 1, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
-            }
-            // tcgen05.ld/st are warp-collective: the whole warp rescales if any of its rows must
-            const bool rescale = (mine > 0) && __any_sync(0xffffffffu, alpha != 1.f);
-            if (rescale) {
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     float o[32];
                     tmem_ld32(o_addr + 32 * c, o);
                     tmem_wait_ld();
@@ -424,7 +439,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
                     tmem_st32(o_addr + 32 * c, o);
                 }
             }
-            // P = 2^(s*sl2 - m) as bf16 pairs into the group's P columns
+            // P = 2^(s*sl2 - m) as bf16 pairs over the first 32 columns this group read
             uint32_t pk[32];
             if (sel) {
                 const float base = (m == -INFINITY) ? 0.f : m;
@@ -447,60 +462,54 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
 #pragma unroll
                 for (int x = 0; x < 32; ++x) pk[x] = 0u;
             }
-            tmem_st16(p_addr, pk);
-            tmem_st16(p_addr + 16, pk + 16);
+            tmem_st16(s_addr, pk);
+            tmem_st16(s_addr + 16, pk + 16);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(P_FULL + grp));
+            mbar_arrive(bar(P_FULL + b));
         }
-        // epilogue: both groups' O are final once each group's last PV has completed
-        bool have = ok && mine > 0;
-        if (have) have = warp_all_ok(mbar_wait(bar(P_FREE + grp), (mine - 1) & 1, abort_flag));
-        ml[grp * 128 + r] = make_float2(have ? m : -INFINITY, have ? l : 0.f);
-        tc_fence_before();
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        tc_fence_after();
-        const float2 ml0 = ml[r], ml1 = ml[128 + r];
-        const float mt = fmaxf(ml0.x, ml1.x);
-        const float a0 = ml0.x == -INFINITY ? 0.f : ex2(ml0.x - mt);
-        const float a1 = ml1.x == -INFINITY ? 0.f : ex2(ml1.x - mt);
-        const float lt = a0 * ml0.y + a1 * ml1.y;
+        // epilogue: O is final once the last PV has completed
+        bool have = ok && nsteps > 0;
+        if (have) have = warp_all_ok(mbar_wait(bar(O_DONE), (nsteps - 1) & 1, abort_flag));
+        if (have) tc_fence_after();
+        lsum[grp * 128 + r] = l;
+        mbar_arrive(bar(XSUM));
+        const bool summed = warp_all_ok(mbar_wait(bar(XSUM), 0, abort_flag));
+        const float lt = summed ? l + lsum[(grp ^ 1) * 128 + r] : 0.f;
         const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        const float w0 = a0 * inv, w1 = a1 * inv;
-        const int row = tile * TILE_M + r;
         const bool live = row < p.Lq && (pair ? (half == 0 ? qblkA < p.qb : qblkB < p.qb) : true);
         // warp-uniform conditions only: tcgen05.ld is warp-collective
-        const bool fin = __all_sync(0xffffffffu, !*abort_flag) != 0;
-        const bool has0 = fin && (nsteps + 1) / 2 > 0, has1 = fin && nsteps / 2 > 0;
+        const bool fin = __all_sync(0xffffffffu, have && summed && !*abort_flag) != 0;
         // group g writes output columns [64g, 64g + 64) of its row
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
             const int col = 64 * grp + 32 * c;
-            float o0[32], o1[32];
-            if (has0) tmem_ld32(lane_base + TMEM_O + col, o0);
-            if (has1) tmem_ld32(lane_base + TMEM_O + 128 + col, o1);
-            tmem_wait_ld();
+            float o[32];
+            if (fin) {
+                tmem_ld32(lane_base + TMEM_O + col, o);
+                tmem_wait_ld();
+            }
 #pragma unroll
-            for (int x = 0; x < 32; ++x) o0[x] = (has0 ? o0[x] * w0 : 0.f) + (has1 ? o1[x] * w1 : 0.f);
-            if (live && fin) {
+            for (int x = 0; x < 32; ++x) o[x] = fin ? o[x] * inv : 0.f;
+            if (live && (fin || nsteps == 0)) {
                 if (p.out_fp32) {
                     float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) +
                                                              ((size_t)row * p.H + h) * D + col);
 #pragma unroll
-                    for (int x = 0; x < 8; ++x) dst[x] = make_float4(o0[4 * x], o0[4 * x + 1], o0[4 * x + 2], o0[4 * x + 3]);
+                    for (int x = 0; x < 8; ++x) dst[x] = make_float4(o[4 * x], o[4 * x + 1], o[4 * x + 2], o[4 * x + 3]);
                 } else {
                     uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) +
                                                            ((size_t)row * p.H + h) * D + col);
 #pragma unroll
                     for (int x = 0; x < 4; ++x)
-                        dst[x] = make_uint4(pack_bf16x2(o0[8 * x], o0[8 * x + 1]), pack_bf16x2(o0[8 * x + 2], o0[8 * x + 3]),
-                                            pack_bf16x2(o0[8 * x + 4], o0[8 * x + 5]),
-                                            pack_bf16x2(o0[8 * x + 6], o0[8 * x + 7]));
+                        dst[x] = make_uint4(pack_bf16x2(o[8 * x], o[8 * x + 1]), pack_bf16x2(o[8 * x + 2], o[8 * x + 3]),
+                                            pack_bf16x2(o[8 * x + 4], o[8 * x + 5]),
+                                            pack_bf16x2(o[8 * x + 6], o[8 * x + 7]));
                 }
             }
         }
-        if (live && fin && grp == 0 && p.lse)
-            p.lse[(size_t)h * p.Lq + row] = lt > 0.f ? (mt + __log2f(lt)) * 0.69314718055994530942f : -INFINITY;
+        if (live && (fin || nsteps == 0) && grp == 0 && p.lse)
+            p.lse[(size_t)h * p.Lq + row] = lt > 0.f ? (m + __log2f(lt)) * 0.69314718055994530942f : -INFINITY;
     }
     tc_fence_before();
     __syncthreads();
@@ -519,7 +528,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_c
 int attention_smem_bytes(int Lk, int block, int n_ids, uint32_t *bytes) {
     const int kb = (Lk + block - 1) / block;
     const int nwords = (kb + 31) / 32;
-    long max_sub = (block == 64) ? (long)std::min(2 * n_ids, kb) : 2L * std::min(n_ids, kb);
+    long max_sub = (block == 64) ? (long)std::min(2 * n_ids, kb) + 1 : 2L * std::min(n_ids, kb);
     long total = 1024 + attn::OFF_DYN + 8L * nwords + 4L * (max_sub + 2);
     *bytes = (uint32_t)total;
     return total <= (long)attn::SMEM_LIMIT ? 0 : SS_ERR_SMEM;
@@ -572,13 +581,13 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
     rc = attention_prepare(device);
     if (rc) return rc;
 
-    CUtensorMap tq, tk, tv;
+    CUtensorMap tk, tv;
     const uint64_t row_bytes = (uint64_t)H * attn::D * 2;
-    if (encode_tmap_2d_bf16(&tq, q, (uint64_t)H * attn::D, (uint64_t)Lq, row_bytes, 64, 128)) return SS_ERR_DRIVER;
     if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
     if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
 
     attn::Params prm;
+    prm.q = static_cast<const __nv_bfloat16 *>(q);
     prm.ids = ids;
     prm.out = out;
     prm.lse = lse;
@@ -595,6 +604,6 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
     prm.out_fp32 = out_dtype;
     prm.scale_log2 = scale * 1.4426950408889634f;
     dim3 grid((unsigned)(prm.ntiles * H));
-    attn::sparse_attention_kernel<<<grid, attn::NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, prm);
+    attn::sparse_attention_kernel<<<grid, attn::NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tk, tv, prm);
     return (int)cudaGetLastError();
 }

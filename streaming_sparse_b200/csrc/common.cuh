@@ -178,6 +178,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
            | ((uint32_t)(M >> 4) << 24);     // M / 16
 }
 
+// One lane of a converged warp (elect.sync). Warp-specialised roles run their loops on the
+// whole, converged warp and issue single-thread instructions (tcgen05.mma, tcgen05.commit, TMA)
+// from the elected lane: issued from a lone diverged lane, each tcgen05.mma costs ~139 cycles
+// of issue time whatever its size (measured on B200), versus its math time when converged.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+    return pred != 0;
+}
+
 // ---------------------------------------------------------------------------------------------
 // misc math
 // ---------------------------------------------------------------------------------------------

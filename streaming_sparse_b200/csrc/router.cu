@@ -86,6 +86,25 @@ __global__ void pool_kernel(const uint16_t *__restrict__ q, const uint16_t *__re
     dst[1] = make_float4(__fdiv_rn(s[4], fn), __fdiv_rn(s[5], fn), __fdiv_rn(s[6], fn), __fdiv_rn(s[7], fn));
 }
 
+// Copy n rows of R floats from global (dense rows) to shared memory rows of stride `ld`,
+// eight loads in flight per thread (a plain loop would wait out one L2 round trip per element).
+__device__ __forceinline__ void stage_rows(float *dst, int ld, const float *__restrict__ src, int n, int R) {
+    const int total = n * R;
+    for (int x0 = threadIdx.x; x0 < total; x0 += 8 * blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int x = x0 + u * blockDim.x;
+            v[u] = x < total ? __ldg(src + x) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int x = x0 + u * blockDim.x;
+            if (x < total) dst[(x / R) * ld + x % R] = v[u];
+        }
+    }
+}
+
 // grid (tq + tk, H), 256 threads; tiles [0, tq) project q means with wq, the rest k means with wk.
 // Thread t owns row t / (R/8) of the tile and 8 consecutive output columns: eight independent
 // fmaf chains (each in ascending d order) keep the FMA pipe busy.
@@ -104,12 +123,10 @@ __global__ void __launch_bounds__(256) project_kernel(const float *__restrict__ 
     const float *w = (isq ? wq : wk) + (size_t)h * D * R;
     float *out = (isq ? qh : kh) + (size_t)h * nb * R;
     const int r0 = tile * PROJ_ROWS, rows = min(PROJ_ROWS, nb - r0);
-    for (int x = threadIdx.x; x < D * R / 4; x += 256)
-        reinterpret_cast<float4 *>(sw)[x] = reinterpret_cast<const float4 *>(w)[x];
-    for (int x = threadIdx.x; x < PROJ_ROWS * D; x += 256) {
-        const int rr = x / D, d = x % D;
-        sx[rr * (D + 1) + d] = rr < rows ? mean[(size_t)(r0 + rr) * D + d] : 0.f;
-    }
+    stage_rows(sw, R, w, D, R);
+    stage_rows(sx, D + 1, mean + (size_t)r0 * D, rows, D);
+    for (int x = threadIdx.x; x < (PROJ_ROWS - rows) * D; x += 256)   // zero the unused rows
+        sx[(rows + x / D) * (D + 1) + x % D] = 0.f;
     __syncthreads();
     const int groups = R / 8;            // 8-column groups per row
     for (int o = threadIdx.x; o < PROJ_ROWS * groups; o += 256) {
@@ -179,8 +196,7 @@ __global__ void score_select_kernel(const float *__restrict__ qh, const float *_
     for (int j0 = 0; j0 < kb; j0 += TILE_J) {
         const int nj = min(TILE_J, kb - j0);
         __syncthreads();
-        for (int x = threadIdx.x; x < nj * R; x += blockDim.x)
-            sk[(x / R) * (R + 1) + x % R] = kh[((size_t)h * kb + j0 + x / R) * R + x % R];
+        stage_rows(sk, R + 1, kh + ((size_t)h * kb + j0) * R, nj, R);
         __syncthreads();
         if (row_ok) {
             // lanes own columns lane and lane + 32 of this tile: two independent fmaf chains
