@@ -25,14 +25,15 @@
 //   warps 4-11  softmax: group g (warps 4+4g .. 7+4g) owns sub-block g of every step, i.e. score
 //               columns [64g, 64g+64). In the prologue the groups copy the Q tile into TMEM (the QK
 //               MMA reads Q from TMEM, so shared-memory bandwidth goes to K and V only). Thread r
-//               of a group owns query row r (TMEM lane r). Per step both groups read their 64
-//               scores, exchange the row maximum through shared memory, keep identical running
-//               maxima, write P (bf16) over the scores they consumed (the PV MMA reads P from
-//               TMEM) and each rescale their half of the shared O accumulator when the running
+//               of a group owns query row r (TMEM lane r). Per step both groups copy all 128 scores
+//               of their row to registers and release the S buffer at once (the QK MMA two steps
+//               ahead can start), derive the same running max (no exchange needed), exponentiate
+//               their 64 columns, write P (bf16) to their P columns in TMEM (the PV MMA reads P
+//               from TMEM) and rescale their half of the shared O accumulator when the running
 //               max grows by more than 2^8.
 //
-// TMEM (512 columns): S of step parity b at [128b, 128b+128) with P written over columns
-// [128b+64g, 128b+64g+32) by group g; Q (bf16 pairs) at [256, 320); O at [384, 512).
+// TMEM (512 columns): S of step parity b at [128b, 128b+128); Q (bf16 pairs) at [256, 320); P of
+// group g at [320+32g, 352+32g); O at [384, 512).
 // MMAs: S = Q K^T (M=128, N=128, K=128; A = Q in TMEM, B = K K-major in shared memory, 128-byte
 //       swizzle), O += P V (M=128, N=128, K=128 tokens; A = P in TMEM, B = V MN-major in shared
 //       memory). tcgen05.mma instructions of one thread execute in order, so the QK MMA that
@@ -57,12 +58,11 @@ constexpr uint32_t OFF_V = OFF_K + KSTAGES * KV_BYTES;
 constexpr uint32_t OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
 constexpr int NBAR = 24;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t OFF_RED = OFF_MISC + 64;        // [2 step parities][2 groups][128 rows] row maxima
-constexpr uint32_t OFF_LSUM = OFF_RED + 2 * 2 * 128 * 4; // [2 groups][128 rows] partial row sums
+constexpr uint32_t OFF_LSUM = OFF_MISC + 64;       // [2 groups][128 rows] partial row sums
 constexpr uint32_t OFF_DYN = OFF_LSUM + 2 * 128 * 4;   // bitmaps, then the sub-block list
 constexpr uint32_t SMEM_LIMIT = 232448;            // 227 KB opt-in maximum per CTA
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_S = 0, TMEM_Q = 256, TMEM_O = 384;
+constexpr uint32_t TMEM_S = 0, TMEM_Q = 256, TMEM_P = 320, TMEM_O = 384;
 
 enum Bar {
     Q_FULL = 0,                  // Q tile copied into TMEM (256 softmax threads)
@@ -71,10 +71,10 @@ enum Bar {
     V_FULL = K_EMPTY + KSTAGES,
     V_EMPTY = V_FULL + VSTAGES,
     S_FULL = V_EMPTY + VSTAGES,  // per S buffer (step parity): QK result ready
-    P_FULL = S_FULL + 2,         // per step parity: P written by both groups (256 arrivals)
+    S_FREE = S_FULL + 2,         // per S buffer: both groups copied the scores out (256 arrivals)
+    P_FULL = S_FREE + 2,         // per step parity: P written by both groups (256 arrivals)
     O_DONE = P_FULL + 2,         // PV of a step completed (O up to date, P consumed)
-    XCHG = O_DONE + 1,           // per step parity: both groups' row maxima written (256 arrivals)
-    XSUM = XCHG + 2,             // epilogue: both groups' row sums written (256 arrivals)
+    XSUM = O_DONE + 1,           // epilogue: both groups' row sums written (256 arrivals)
     DRAIN = XSUM + 1,
     NBAR_USED
 };
@@ -123,6 +123,25 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 __device__ __forceinline__ float f2_lo(uint64_t x) { return __uint_as_float((uint32_t)x); }
 __device__ __forceinline__ float f2_hi(uint64_t x) { return __uint_as_float((uint32_t)(x >> 32)); }
 
+// 2^x on the FMA pipe for a pair of arguments (x <= 8 here; x below -125 is clamped, giving
+// ~2^-125 instead of 0). x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f by the minimax cubic
+// for relative error on [-0.5, 0.5] (coefficients fitted by the Remez exchange algorithm, max
+// relative error 7.5e-5, below bf16 rounding of P); 2^n is added to the exponent bits.
+// Offloading a share of the exponentials from the MUFU unit keeps it from bounding the softmax.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float &y1) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer
+    const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+    const uint64_t t = f2_add(x, f2_pack(kRound, kRound));
+    const uint64_t n = f2_add(t, f2_pack(-kRound, -kRound));
+    const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);
+    uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f, f2_pack(0.2426111251f, 0.2426111251f));
+    p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
+    p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
+    const int n0 = (int)(uint32_t)t - 0x4B400000, n1 = (int)(uint32_t)(t >> 32) - 0x4B400000;
+    y0 = __int_as_float(__float_as_int(f2_lo(p)) + (n0 << 23));
+    y1 = __int_as_float(__float_as_int(f2_hi(p)) + (n1 << 23));
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -156,7 +175,6 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
     volatile int *nsub_slot = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
     volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 12);
-    float *red = reinterpret_cast<float *>(smem + OFF_RED);
     float *lsum = reinterpret_cast<float *>(smem + OFF_LSUM);
     uint32_t *bmA = reinterpret_cast<uint32_t *>(smem + OFF_DYN);
     uint32_t *bmB = bmA + p.nwords;
@@ -184,8 +202,8 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar(S_FULL + b), 1);
+            mbar_init(bar(S_FREE + b), 256);
             mbar_init(bar(P_FULL + b), 256);
-            mbar_init(bar(XCHG + b), 256);
         }
         mbar_init(bar(O_DONE), 1);
         mbar_init(bar(XSUM), 256);
@@ -315,10 +333,10 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 tc_fence_after();
                 const uint32_t dv = sV + st * KV_BYTES;
                 if (elect_one()) {
-                    // tokens 16kk.. of the step: P of sub-block kk/4 sits at columns 64*(kk/4) of S_b
+                    // tokens 16kk.. of the step: P of sub-block kk/4 sits in the P columns of group kk/4
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
-                        mma_bf16_ts(tmem + TMEM_O, tmem + TMEM_S + 128 * b + 64 * (kk >> 2) + 8 * (kk & 3),
+                        mma_bf16_ts(tmem + TMEM_O, tmem + TMEM_P + 8 * kk,
                                     smem_desc_sw128(dv + kk * 2048, REGION, 1024), IDESC_PV,
                                     (j > 0 || kk > 0) ? 1u : 0u);
                     tc_commit(bar(O_DONE));
@@ -330,8 +348,12 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             if (ok) ok = issue_qk(0);
             if (ok && nsteps > 1) ok = issue_qk(1);
             for (int j = 0; j < nsteps && ok; ++j) {
-                ok = issue_pv(j);
-                if (ok && j + 2 < nsteps) ok = issue_qk(j + 2);
+                if (j + 2 < nsteps) {
+                    // S_(j&1) is free once both groups copied step j's scores out
+                    ok = warp_all_ok(mbar_wait(bar(S_FREE + (j & 1)), (j >> 1) & 1, abort_flag));
+                    if (ok) ok = issue_qk(j + 2);
+                }
+                if (ok) ok = issue_pv(j);
             }
             // every MMA issued above has completed once DRAIN fires
             if (elect_one()) tc_commit(bar(DRAIN));
@@ -380,15 +402,43 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             if (!ok) break;
             tc_fence_after();
             const uint32_t s_addr = lane_base + TMEM_S + 128 * b + 64 * grp;
-            const uint32_t e = steps[2 * j + grp];
-            const bool sel = (e >> (27 + half)) & 1u;   // warp-uniform (a warp is within one half)
-            const int valid = sel ? e_valid(e) : 0;
+            const uint32_t e = steps[2 * j + grp], eo = steps[2 * j + (grp ^ 1)];
+            // selection and valid length, warp-uniform (a warp lies within one 64-row half)
+            const bool sel = (e >> (27 + half)) & 1u, selo = (eo >> (27 + half)) & 1u;
+            const int valid = sel ? e_valid(e) : 0, valido = selo ? e_valid(eo) : 0;
+            // row max over the whole step: both groups read all 128 columns, so both derive the
+            // same running max without exchanging it; each keeps the 64 scores it exponentiates.
             float s[64];
             float mx = -INFINITY;
             if (sel) {
                 tmem_ld32(s_addr, s);
                 tmem_ld32(s_addr + 32, s + 32);
+            }
+            if (selo) {
+                float t[64];
+                const uint32_t o_s = lane_base + TMEM_S + 128 * b + 64 * (grp ^ 1);
+                tmem_ld32(o_s, t);
+                tmem_ld32(o_s + 32, t + 32);
                 tmem_wait_ld();
+                if (valido == SUB) {
+                    float m0 = t[0], m1 = t[1], m2 = t[2], m3 = t[3];
+#pragma unroll
+                    for (int c = 4; c < 64; c += 8) {
+                        m0 = max3(m0, t[c], t[c + 1]);
+                        m1 = max3(m1, t[c + 2], t[c + 3]);
+                        m2 = max3(m2, t[c + 4], t[c + 5]);
+                        m3 = max3(m3, t[c + 6], t[c + 7]);
+                    }
+                    mx = max3(fmaxf(m0, m1), m2, m3);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 64; ++c) mx = fmaxf(mx, c < valido ? t[c] : -INFINITY);
+                }
+            }
+            if (sel) tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(bar(S_FREE + b));
+            if (sel) {
                 if (valid == SUB) {
                     float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
 #pragma unroll
@@ -398,7 +448,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                         m2 = max3(m2, s[c + 4], s[c + 5]);
                         m3 = max3(m3, s[c + 6], s[c + 7]);
                     }
-                    mx = max3(fmaxf(m0, m1), m2, m3);
+                    mx = max3(mx, fmaxf(m0, m1), fmaxf(m2, m3));
                 } else {
 #pragma unroll
                     for (int c = 0; c < 64; ++c) {
@@ -407,35 +457,31 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                     }
                 }
             }
-            // row max of the whole step: exchange with the other group (bounded mbarrier wait; a
-            // slot is rewritten two steps later, after every thread passed the next exchange)
-            float *rb = red + (b * 2) * 128;
-            rb[grp * 128 + r] = mx;
-            mbar_arrive(bar(XCHG + b));
-            ok = warp_all_ok(mbar_wait(bar(XCHG + b), (j >> 1) & 1, abort_flag));
-            if (!ok) break;
-            mx = fmaxf(mx, rb[(grp ^ 1) * 128 + r]);
             // lazy rescale: move the reference max only when the row max grew by more than 2^8
             const float mnew = mx * sl2;
             float alpha = 1.f;
+            bool grow = false;                   // an O row that is not all zeros must be scaled
             if (mnew > m + 8.0f) {
-                alpha = (m == -INFINITY) ? 0.f : ex2(m - mnew);
+                grow = m != -INFINITY;
+                alpha = grow ? ex2(m - mnew) : 0.f;
                 l *= alpha;
                 m = mnew;
             }
-            // O changes only through PV of the previous step; tcgen05.ld/st are warp-collective, so
-            // the whole warp rescales its half of O if any of its rows must.
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            // O and the P columns change through the previous step's PV; tcgen05.ld/st are
+            // warp-collective, so the whole warp rescales its half of O if any of its rows must.
+            bool o_ready = j == 0;
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
                 ok = warp_all_ok(mbar_wait(bar(O_DONE), (j - 1) & 1, abort_flag));
                 if (!ok) break;
                 tc_fence_after();
+                o_ready = true;
 #pragma unroll 1
                 for (int c = 0; c < 2; ++c) {
                     float o[32];
                     tmem_ld32(o_addr + 32 * c, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) o[x] *= alpha;
+                    for (int x = 0; x < 32; ++x) o[x] *= (grow ? alpha : 1.f);
                     tmem_st32(o_addr + 32 * c, o);
                 }
             }
@@ -449,8 +495,16 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 for (int c = 0; c < 64; c += 4) {
                     const uint64_t x0 = f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, nbx2);
                     const uint64_t x1 = f2_fma(f2_pack(s[c + 2], s[c + 3]), sl2x2, nbx2);
-                    const float p0 = ex2(f2_lo(x0)), p1 = ex2(f2_hi(x0));
-                    const float p2 = ex2(f2_lo(x1)), p3 = ex2(f2_hi(x1));
+                    float p0, p1, p2, p3;
+                    if (c < 48) {   // MUFU
+                        p0 = ex2(f2_lo(x0));
+                        p1 = ex2(f2_hi(x0));
+                        p2 = ex2(f2_lo(x1));
+                        p3 = ex2(f2_hi(x1));
+                    } else {        // FMA pipe (a quarter of the exponentials)
+                        exp2_poly2(f2_lo(x0), f2_hi(x0), p0, p1);
+                        exp2_poly2(f2_lo(x1), f2_hi(x1), p2, p3);
+                    }
                     sa = f2_add(sa, f2_pack(p0, p1));
                     sb = f2_add(sb, f2_pack(p2, p3));
                     pk[c >> 1] = pack_bf16x2(p0, p1);
@@ -462,8 +516,15 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
 #pragma unroll
                 for (int x = 0; x < 32; ++x) pk[x] = 0u;
             }
-            tmem_st16(s_addr, pk);
-            tmem_st16(s_addr + 16, pk + 16);
+            // the P columns are free once the previous step's PV has read them
+            if (!o_ready) {
+                ok = warp_all_ok(mbar_wait(bar(O_DONE), (j - 1) & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+            }
+            const uint32_t p_addr = lane_base + TMEM_P + 32 * grp;
+            tmem_st16(p_addr, pk);
+            tmem_st16(p_addr + 16, pk + 16);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(P_FULL + b));

@@ -51,25 +51,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Every wait in these kernels is bounded: after `kWaitLimitNs` (or once another thread of the
-// CTA has given up, signalled through *abort) the wait returns false, the caller reports
-// SS_DEV_TIMEOUT and unwinds. A healthy wait completes in microseconds.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Every wait in these kernels is bounded: after `kWaitLimitCycles` SM clocks (about 2 s), or once
+// another thread of the CTA has given up (signalled through *abort), the wait returns false,
+// the caller reports SS_DEV_TIMEOUT and unwinds. A healthy wait completes in microseconds.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = globaltimer_ns();
+    const long long t0 = clock64();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0u) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (clock64() - t0 > kWaitLimitCycles) {
                 *abort = 1;
                 return false;
             }
