@@ -1,21 +1,23 @@
 // router.cu -- learned KV-block router for sm_100a in exact fp32.
 //
-//   1. pool: per (head, block) the mean of the block's valid tokens -- fp32 adds in token order,
-//      one correctly rounded divide. One CTA reads a whole block of token rows (all heads) with
-//      coalesced 16-byte loads; thread (h, 8 dims) keeps 8 running sums.
+//   1. pool_project: one CTA per (head, group of 16 blocks). The head's [128 x R] projection is
+//      fetched into shared memory with one bulk copy; each thread sums 8 dimensions of one block
+//      over the block's valid tokens (fp32 adds in token order, one correctly rounded divide),
+//      then the block means are projected with fmaf in ascending row order. Query projections
+//      are stored [H][qb][R]; key projections transposed [H][R][kb] for the score stage.
 //      Reference: block pooling of migration/unified_router/opt19/prototype.py:11-49 (one
-//      prototype = plain mean of the valid tokens).
-//   2. project: pooled [nb x 128] @ W [128 x R] per head with fmaf in ascending row order,
-//      W staged in shared memory. Reference: opt8/projection.py:4-14.
-//   3. score_select: one warp per (head, query block). Scores S[j] = <qh, kh_j> (fmaf in
-//      ascending order, -0 -> +0, non-finite flagged) for every key block; the order-preserving
-//      uint32 of each unforced score stays in registers. The `extra`-th largest score T is found
-//      exactly by a 32-step bisection with warp-wide counts; blocks above T are kept and ties at
-//      T go to the lowest block indices (ordered ballot scan). Forced blocks (sink, current
-//      chunk) are always kept and ids are written ascending. Reference: the block-score GEMM
-//      `_coarse` (opt16/route.py:34-47), `_chosen`/`_top` (opt16/route.py:13-24,49-55),
-//      fixed_page_select (local_experiments/video_runtime_v1/fixed_page_select.py:7-21) and the
-//      forced set of local_experiments/video_runtime_v1/pipeline_graph.py:140-151.
+//      prototype = plain mean of the valid tokens) and the projection of opt8/projection.py:4-14.
+//   2. score_select: one warp per (head, query block), eight query blocks per CTA sharing the
+//      head's transposed key projections, staged into shared memory 256 key blocks at a time by
+//      bulk copies. Scores S[j] = <qh, kh_j> (fmaf in ascending order, -0 -> +0, non-finite
+//      flagged); the order-preserving uint32 of each unforced score is kept in shared memory.
+//      The `extra`-th largest score T is found exactly by a 32-step bisection with warp-wide
+//      counts; blocks above T are kept and ties at T go to the lowest block indices (ordered
+//      ballot scan). Forced blocks (sink, current chunk) are always kept; ids are written
+//      ascending. Reference: the block-score GEMM `_coarse` (opt16/route.py:34-47), `_chosen`/
+//      `_top` (opt16/route.py:13-24,49-55), fixed_page_select (local_experiments/
+//      video_runtime_v1/fixed_page_select.py:7-21) and the forced set of local_experiments/
+//      video_runtime_v1/pipeline_graph.py:140-151.
 // The fixed summation order makes every score bit-identical to the CPU oracle. The score GEMM is
 // tens of MFMA per chunk-layer, so CUDA-core FFMA keeps it exact at a cost of microseconds.
 #include <algorithm>
@@ -27,131 +29,120 @@ namespace router {
 
 constexpr int D = 128;
 constexpr int MAX_R = 128;
-constexpr int MAX_KB = 2048;       // score bits of a row live in registers (64 per lane)
-constexpr int PROJ_ROWS = 32;       // pooled rows per projection CTA
-constexpr int TILE_J = 64;          // key blocks staged per score tile
+constexpr int MAX_KB = 8192;
+constexpr int BG = 16;               // blocks per pool_project CTA
+constexpr int PP_THREADS = BG * 16;  // thread = (block, 8 dims)
+constexpr int ROWS = 8;              // query blocks (warps) per score_select CTA
+constexpr int TJ = 256;              // key blocks per staged tile
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// grid (nq + nk), H*16 threads. Block b < nq pools q, otherwise k; means -> [H][nb][128].
-__global__ void pool_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k, int H, int Lq, int Lk,
-                            int block, int nq, float *__restrict__ qmean, float *__restrict__ kmean) {
-    const bool isq = (int)blockIdx.x < nq;
-    const int b = isq ? blockIdx.x : blockIdx.x - nq;
-    const uint16_t *x = isq ? q : k;
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+// grid (tiles_q + tiles_k, H), BG*16 threads. Tiles [0, tiles_q) pool query blocks, the rest key
+// blocks. Dynamic shared memory: W [128][R], means [BG][128], mbarrier.
+__global__ void __launch_bounds__(PP_THREADS) pool_project_kernel(const uint16_t *__restrict__ q,
+                                                                  const uint16_t *__restrict__ k, int H, int Lq,
+                                                                  int Lk, int block, int R, int tiles_q,
+                                                                  const float *__restrict__ wq,
+                                                                  const float *__restrict__ wk,
+                                                                  float *__restrict__ qh, float *__restrict__ khT,
+                                                                  int kbp, int *status) {
+    extern __shared__ __align__(16) uint8_t smr[];
+    float *sw = reinterpret_cast<float *>(smr);                 // [128][R]
+    float *smean = sw + D * R;                                   // [BG][128]
+    uint64_t *mbar = reinterpret_cast<uint64_t *>(smean + BG * D);
+    const int h = blockIdx.y, tid = threadIdx.x;
+    const bool isq = (int)blockIdx.x < tiles_q;
+    const int tile = isq ? blockIdx.x : blockIdx.x - tiles_q;
     const int L = isq ? Lq : Lk;
-    const int nb = isq ? nq : (Lk + block - 1) / block;
-    float *out = isq ? qmean : kmean;
-    const int t0 = b * block;
-    const int n = min(block, L - t0);
-    const int tid = threadIdx.x;            // = h*16 + chunk of 8 dims
-    const int row_vec = H * D / 8;          // uint4 per token row
-    const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t0 * H * D) + tid;
-    float s[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i] = 0.f;
-    int t = 0;
-    for (; t + 8 <= n; t += 8) {
-        uint4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (size_t)(t + u) * row_vec);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            s[0] = __fadd_rn(s[0], bf16_lo(v[u].x));
-            s[1] = __fadd_rn(s[1], bf16_hi(v[u].x));
-            s[2] = __fadd_rn(s[2], bf16_lo(v[u].y));
-            s[3] = __fadd_rn(s[3], bf16_hi(v[u].y));
-            s[4] = __fadd_rn(s[4], bf16_lo(v[u].z));
-            s[5] = __fadd_rn(s[5], bf16_hi(v[u].z));
-            s[6] = __fadd_rn(s[6], bf16_lo(v[u].w));
-            s[7] = __fadd_rn(s[7], bf16_hi(v[u].w));
-        }
+    const int nb = (L + block - 1) / block;
+    const int b0 = tile * BG, nblk = min(BG, nb - b0);
+    const uint32_t bar = smem_u32(mbar);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
     }
-    for (; t < n; ++t) {
-        const uint4 v = __ldg(src + (size_t)t * row_vec);
-        s[0] = __fadd_rn(s[0], bf16_lo(v.x));
-        s[1] = __fadd_rn(s[1], bf16_hi(v.x));
-        s[2] = __fadd_rn(s[2], bf16_lo(v.y));
-        s[3] = __fadd_rn(s[3], bf16_hi(v.y));
-        s[4] = __fadd_rn(s[4], bf16_lo(v.z));
-        s[5] = __fadd_rn(s[5], bf16_hi(v.z));
-        s[6] = __fadd_rn(s[6], bf16_lo(v.w));
-        s[7] = __fadd_rn(s[7], bf16_hi(v.w));
-    }
-    const int h = tid >> 4, d0 = (tid & 15) * 8;
-    const float fn = (float)n;
-    float4 *dst = reinterpret_cast<float4 *>(out + ((size_t)h * nb + b) * D + d0);
-    dst[0] = make_float4(__fdiv_rn(s[0], fn), __fdiv_rn(s[1], fn), __fdiv_rn(s[2], fn), __fdiv_rn(s[3], fn));
-    dst[1] = make_float4(__fdiv_rn(s[4], fn), __fdiv_rn(s[5], fn), __fdiv_rn(s[6], fn), __fdiv_rn(s[7], fn));
-}
-
-// Copy n rows of R floats from global (dense rows) to shared memory rows of stride `ld`,
-// eight loads in flight per thread (a plain loop would wait out one L2 round trip per element).
-__device__ __forceinline__ void stage_rows(float *dst, int ld, const float *__restrict__ src, int n, int R) {
-    const int total = n * R;
-    for (int x0 = threadIdx.x; x0 < total; x0 += 8 * blockDim.x) {
-        float v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int x = x0 + u * blockDim.x;
-            v[u] = x < total ? __ldg(src + x) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int x = x0 + u * blockDim.x;
-            if (x < total) dst[(x / R) * ld + x % R] = v[u];
-        }
-    }
-}
-
-// grid (tq + tk, H), 256 threads; tiles [0, tq) project q means with wq, the rest k means with wk.
-// Thread t owns row t / (R/8) of the tile and 8 consecutive output columns: eight independent
-// fmaf chains (each in ascending d order) keep the FMA pipe busy.
-__global__ void __launch_bounds__(256) project_kernel(const float *__restrict__ qmean, const float *__restrict__ kmean,
-                                                      const float *__restrict__ wq, const float *__restrict__ wk,
-                                                      int qb, int kb, int tq, int R, float *__restrict__ qh,
-                                                      float *__restrict__ kh) {
-    extern __shared__ float sm[];
-    float *sw = sm;                      // [128][R]
-    float *sx = sm + D * R;              // [PROJ_ROWS][129]
-    const int h = blockIdx.y;
-    const bool isq = (int)blockIdx.x < tq;
-    const int tile = isq ? blockIdx.x : blockIdx.x - tq;
-    const int nb = isq ? qb : kb;
-    const float *mean = (isq ? qmean : kmean) + (size_t)h * nb * D;
-    const float *w = (isq ? wq : wk) + (size_t)h * D * R;
-    float *out = (isq ? qh : kh) + (size_t)h * nb * R;
-    const int r0 = tile * PROJ_ROWS, rows = min(PROJ_ROWS, nb - r0);
-    stage_rows(sw, R, w, D, R);
-    stage_rows(sx, D + 1, mean + (size_t)r0 * D, rows, D);
-    for (int x = threadIdx.x; x < (PROJ_ROWS - rows) * D; x += 256)   // zero the unused rows
-        sx[(rows + x / D) * (D + 1) + x % D] = 0.f;
     __syncthreads();
-    const int groups = R / 8;            // 8-column groups per row
-    for (int o = threadIdx.x; o < PROJ_ROWS * groups; o += 256) {
-        const int rr = o / groups, e0 = (o % groups) * 8;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(bar, (uint32_t)(D * R * 4));
+        bulk_g2s(smem_u32(sw), (isq ? wq : wk) + (size_t)h * D * R, (uint32_t)(D * R * 4), bar);
+    }
+    // pooling: thread (bi, c) sums dims [8c, 8c+8) of block b0+bi in token order
+    const int bi = tid >> 4, c = tid & 15;
+    if (bi < nblk) {
+        const int t0 = (b0 + bi) * block;
+        const int n = min(block, L - t0);
+        const uint16_t *x = isq ? q : k;
+        const size_t row_vec = (size_t)H * D / 8;
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + ((size_t)t0 * H + h) * D) + c;
+        float s[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i] = 0.f;
+        int t = 0;
+        for (; t + 8 <= n; t += 8) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (size_t)(t + u) * row_vec);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                s[0] = __fadd_rn(s[0], bf16_lo(v[u].x));
+                s[1] = __fadd_rn(s[1], bf16_hi(v[u].x));
+                s[2] = __fadd_rn(s[2], bf16_lo(v[u].y));
+                s[3] = __fadd_rn(s[3], bf16_hi(v[u].y));
+                s[4] = __fadd_rn(s[4], bf16_lo(v[u].z));
+                s[5] = __fadd_rn(s[5], bf16_hi(v[u].z));
+                s[6] = __fadd_rn(s[6], bf16_lo(v[u].w));
+                s[7] = __fadd_rn(s[7], bf16_hi(v[u].w));
+            }
+        }
+        for (; t < n; ++t) {
+            const uint4 v = __ldg(src + (size_t)t * row_vec);
+            s[0] = __fadd_rn(s[0], bf16_lo(v.x));
+            s[1] = __fadd_rn(s[1], bf16_hi(v.x));
+            s[2] = __fadd_rn(s[2], bf16_lo(v.y));
+            s[3] = __fadd_rn(s[3], bf16_hi(v.y));
+            s[4] = __fadd_rn(s[4], bf16_lo(v.z));
+            s[5] = __fadd_rn(s[5], bf16_hi(v.z));
+            s[6] = __fadd_rn(s[6], bf16_lo(v.w));
+            s[7] = __fadd_rn(s[7], bf16_hi(v.w));
+        }
+        const float fn = (float)n;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) smean[bi * D + 8 * c + i] = __fdiv_rn(s[i], fn);
+    }
+    // wait for W (bounded), then project: thread (bi, e-group) owns R/16 consecutive outputs
+    volatile int no_abort = 0;
+    const bool have_w = mbar_wait(bar, 0, &no_abort);
+    __syncthreads();
+    if (!have_w) {
+        if (tid == 0) report(status, SS_DEV_TIMEOUT);
+        return;
+    }
+    const int per = R / 16;  // 4 for R = 64 (R is a multiple of 16, at most 128)
+    if (bi < nblk) {
         float acc[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+        const int e0 = c * per;
 #pragma unroll 4
         for (int d = 0; d < D; ++d) {
-            const float x = sx[rr * (D + 1) + d];
-            const float4 w0 = reinterpret_cast<const float4 *>(sw + d * R + e0)[0];
-            const float4 w1 = reinterpret_cast<const float4 *>(sw + d * R + e0)[1];
-            acc[0] = __fmaf_rn(x, w0.x, acc[0]);
-            acc[1] = __fmaf_rn(x, w0.y, acc[1]);
-            acc[2] = __fmaf_rn(x, w0.z, acc[2]);
-            acc[3] = __fmaf_rn(x, w0.w, acc[3]);
-            acc[4] = __fmaf_rn(x, w1.x, acc[4]);
-            acc[5] = __fmaf_rn(x, w1.y, acc[5]);
-            acc[6] = __fmaf_rn(x, w1.z, acc[6]);
-            acc[7] = __fmaf_rn(x, w1.w, acc[7]);
+            const float xm = smean[bi * D + d];
+            const float *wr = sw + d * R + e0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (u < per) acc[u] = __fmaf_rn(xm, wr[u], acc[u]);
         }
-        if (rr < rows) {
-            float4 *dst = reinterpret_cast<float4 *>(out + (size_t)(r0 + rr) * R + e0);
-            dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        const int b = b0 + bi;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (u >= per) break;
+            if (isq) qh[((size_t)h * nb + b) * R + e0 + u] = acc[u];
+            else khT[((size_t)h * R + e0 + u) * kbp + b] = acc[u];
         }
     }
 }
@@ -166,67 +157,81 @@ __device__ __forceinline__ uint32_t ordered_bits(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// One warp per (head, query block) row; `rows` warps per CTA share staged tiles of kh[h].
-// Key order: (ordered score bits, lower block index first). Lane owns blocks j = 32*i + lane,
-// i < NPL, with the score bits in registers (0 = not a candidate: forced or past kb; every
-// finite score maps to >= 0x00800000).
-//   1. T = the extra-th largest score value among candidates (32-step bisection on the bits).
-//   2. Blocks scoring above T are kept; of the blocks scoring exactly T, the lowest-index ones
-//      fill the remaining slots (ordered ballot scan).
-template <int NPL>
-__global__ void score_select_kernel(const float *__restrict__ qh, const float *__restrict__ kh, int qb, int kb, int R,
-                                    int block, int Lq, int Lk, int sink, int extra, int32_t *__restrict__ ids,
-                                    int n_ids, uint8_t *__restrict__ mask, float *__restrict__ scores, int *status) {
-    extern __shared__ float sm[];
-    const int rows = blockDim.x / 32;
-    float *sq = sm;                      // [rows][R]
-    float *sk = sm + rows * R;           // [TILE_J][R+1]
+// grid (ceil(qb / ROWS), H), ROWS warps. khT rows have stride kbp (kb rounded up to a multiple of
+// 4). Dynamic shared memory: khT tile [R][TJ], qh rows [ROWS][R], keys [ROWS][kbp] (ordered score
+// bits; 0 = not a candidate, which no finite score maps to), mbarrier.
+__global__ void __launch_bounds__(ROWS * 32) score_select_kernel(const float *__restrict__ qh,
+                                                                 const float *__restrict__ khT, int qb, int kb,
+                                                                 int kbp, int R,
+                                                                 int block, int Lq, int Lk, int sink, int extra,
+                                                                 int32_t *__restrict__ ids, int n_ids,
+                                                                 uint8_t *__restrict__ mask,
+                                                                 float *__restrict__ scores, int *status) {
+    extern __shared__ __align__(16) uint8_t smr[];
+    float *sk = reinterpret_cast<float *>(smr);               // [R][TJ]
+    float *sq = sk + R * TJ;                                   // [ROWS][R]
+    uint32_t *keys = reinterpret_cast<uint32_t *>(sq + ROWS * R);  // [ROWS][kb]
+    uint64_t *mbar = reinterpret_cast<uint64_t *>(keys + (size_t)ROWS * kbp);
     const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x * rows + warp;
+    const int i = blockIdx.x * ROWS + warp;
     const bool row_ok = i < qb;
-    for (int x = threadIdx.x; x < rows * R; x += blockDim.x) {
-        const int ii = blockIdx.x * rows + x / R;
+    const uint32_t bar = smem_u32(mbar);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    for (int x = threadIdx.x; x < ROWS * R; x += blockDim.x) {
+        const int ii = blockIdx.x * ROWS + x / R;
         sq[x] = ii < qb ? qh[((size_t)h * qb + ii) * R + x % R] : 0.f;
     }
+    __syncthreads();
     const float *myq = sq + warp * R;
-    uint32_t hi[NPL];
-#pragma unroll
-    for (int u = 0; u < NPL; ++u) hi[u] = 0u;
-    bool bad = false;
-    for (int j0 = 0; j0 < kb; j0 += TILE_J) {
-        const int nj = min(TILE_J, kb - j0);
-        __syncthreads();
-        stage_rows(sk, R + 1, kh + ((size_t)h * kb + j0) * R, nj, R);
-        __syncthreads();
+    uint32_t *mykeys = keys + (size_t)warp * kbp;
+    bool bad = false, ok = true;
+    volatile int no_abort = 0;
+    for (int t = 0, j0 = 0; j0 < kb; ++t, j0 += TJ) {
+        const int nj = min(TJ, kb - j0);
+        if (threadIdx.x == 0) {
+            // rows e of the tile: khT[h][e][j0 .. j0+nj), 16-byte multiples (the host pads kb)
+            const uint32_t rb = (uint32_t)(((nj * 4) + 15) & ~15);
+            mbar_arrive_expect_tx(bar, rb * (uint32_t)R);
+            for (int e = 0; e < R; ++e)
+                bulk_g2s(smem_u32(sk + e * TJ), khT + ((size_t)h * R + e) * kbp + j0, rb, bar);
+        }
+        ok = mbar_wait(bar, t & 1, &no_abort);
+        if (!ok) break;
         if (row_ok) {
-            // lanes own columns lane and lane + 32 of this tile: two independent fmaf chains
-            const float *k0 = sk + lane * (R + 1), *k1 = sk + (lane + 32) * (R + 1);
-            float a0 = 0.f, a1 = 0.f;
-#pragma unroll 8
+            float acc[TJ / 32];
+#pragma unroll
+            for (int u = 0; u < TJ / 32; ++u) acc[u] = 0.f;
+#pragma unroll 2
             for (int e = 0; e < R; ++e) {
                 const float qe = myq[e];
-                a0 = __fmaf_rn(qe, k0[e], a0);
-                a1 = __fmaf_rn(qe, k1[e], a1);
+                const float *kr = sk + e * TJ + lane;
+#pragma unroll
+                for (int u = 0; u < TJ / 32; ++u) acc[u] = __fmaf_rn(qe, kr[32 * u], acc[u]);
             }
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                float acc = c ? a1 : a0;
-                const int jj = lane + 32 * c;
-                const int j = j0 + jj;
-                if (acc == 0.f) acc = 0.f;  // -0 -> +0
-                const bool live = jj < nj;
-                bad |= live && !isfinite(acc);
-                if (live && scores) scores[((size_t)h * qb + i) * kb + j] = acc;
-                const uint32_t o = (!live || is_forced(j, block, Lq, Lk, sink)) ? 0u : ordered_bits(acc);
-                const int slot = (j0 >> 5) + c;   // = j >> 5, the same for all lanes
-#pragma unroll
-                for (int u = 0; u < NPL; ++u)
-                    if (u == slot && live) hi[u] = o;
+            for (int u = 0; u < TJ / 32; ++u) {
+                const int j = j0 + lane + 32 * u;
+                if (j >= kb) continue;
+                float a = acc[u];
+                if (a == 0.f) a = 0.f;  // -0 -> +0
+                bad |= !isfinite(a);
+                if (scores) scores[((size_t)h * qb + i) * kb + j] = a;
+                mykeys[j] = is_forced(j, block, Lq, Lk, sink) ? 0u : ordered_bits(a);
             }
         }
+        __syncthreads();  // the tile buffer is refilled next iteration
     }
     if (bad) report(status, SS_DEV_NONFINITE);
+    if (!ok) {
+        if (threadIdx.x == 0) report(status, SS_DEV_TIMEOUT);
+        return;
+    }
     if (!row_ok) return;
+    __syncwarp();
+    // T = the extra-th largest candidate score (bisection on the order-preserving bits)
     uint32_t T = 0xffffffffu;
     int need = 0;
     if (extra > 0) {
@@ -234,27 +239,24 @@ __global__ void score_select_kernel(const float *__restrict__ qh, const float *_
         for (int bit = 31; bit >= 0; --bit) {
             const uint32_t cand = T | (1u << bit);
             int cnt = 0;
-#pragma unroll
-            for (int u = 0; u < NPL; ++u) cnt += hi[u] >= cand;
+            for (int j = lane; j < kb; j += 32) cnt += mykeys[j] >= cand;
             if ((int)__reduce_add_sync(0xffffffffu, (unsigned)cnt) >= extra) T = cand;
         }
         int gt = 0;
-#pragma unroll
-        for (int u = 0; u < NPL; ++u) gt += hi[u] > T;
+        for (int j = lane; j < kb; j += 32) gt += mykeys[j] > T;
         need = extra - (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);  // ties at T to keep, >= 1
     }
     // ascending compaction of forced | above T | the first `need` ties at T
     int32_t *out = ids + ((size_t)h * qb + i) * n_ids;
     int pos = 0, taken = 0;
-#pragma unroll
-    for (int u = 0; u < NPL; ++u) {
-        const int j = 32 * u + lane;
-        if (32 * u >= kb) continue;   // warp-uniform
-        const bool tie = extra > 0 && j < kb && hi[u] == T;
+    for (int j0 = 0; j0 < kb; j0 += 32) {
+        const int j = j0 + lane;
+        const uint32_t key = j < kb ? mykeys[j] : 0u;
+        const bool tie = extra > 0 && j < kb && key == T;
         const unsigned tb = __ballot_sync(0xffffffffu, tie);
         const bool keep_tie = tie && taken + __popc(tb & ((1u << lane) - 1u)) < need;
         taken += __popc(tb);
-        const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && hi[u] > T) || keep_tie);
+        const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && key > T) || keep_tie);
         const unsigned bal = __ballot_sync(0xffffffffu, sel);
         const int off = pos + __popc(bal & ((1u << lane) - 1u));
         if (sel && off < n_ids) out[off] = j;
@@ -265,18 +267,10 @@ __global__ void score_select_kernel(const float *__restrict__ qh, const float *_
 
 }  // namespace router
 
-static size_t select_smem(int rows, int R) {
-    return (size_t)rows * R * 4 + (size_t)router::TILE_J * (R + 1) * 4;
-}
+static size_t pp_smem(int R) { return (size_t)router::D * R * 4 + (size_t)router::BG * router::D * 4 + 16; }
 
-using SelectFn = void (*)(const float *, const float *, int, int, int, int, int, int, int, int, int32_t *, int,
-                          uint8_t *, float *, int *);
-
-static SelectFn select_kernel(int kb) {
-    if (kb <= 128) return router::score_select_kernel<4>;
-    if (kb <= 512) return router::score_select_kernel<16>;
-    if (kb <= 1024) return router::score_select_kernel<32>;
-    return router::score_select_kernel<64>;
+static size_t select_smem(int kb, int R) {
+    return (size_t)R * router::TJ * 4 + (size_t)router::ROWS * R * 4 + (size_t)router::ROWS * kb * 4 + 16;
 }
 
 static int g_router_configured[64] = {0};
@@ -284,8 +278,10 @@ static int g_router_configured[64] = {0};
 int router_prepare(int device) {
     if (device < 0 || device >= 64) return SS_ERR_SHAPE;
     if (g_router_configured[device]) return 0;
-    cudaError_t e = cudaFuncSetAttribute(router::project_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(router::pool_project_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaFuncSetAttribute(router::score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return (int)e;
     g_router_configured[device] = 1;
     return 0;
@@ -293,18 +289,21 @@ int router_prepare(int device) {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// key projections are stored transposed with rows padded to a multiple of 4 blocks, so every
+// bulk copy of a row segment starts and ends on a 16-byte boundary
+static int kb_padded(int kb) { return (kb + 3) & ~3; }
+
 struct RouterLayout {
-    size_t qmean, kmean, qh, kh, total;
+    size_t qh, khT, total;
 };
 
 static RouterLayout router_layout(int H, int Lq, int Lk, int R, int block) {
-    const size_t qb = (size_t)((Lq + block - 1) / block), kb = (size_t)((Lk + block - 1) / block);
+    const size_t qb = (size_t)((Lq + block - 1) / block);
+    const size_t kbp = (size_t)kb_padded((Lk + block - 1) / block);
     RouterLayout L;
-    L.qmean = 0;
-    L.kmean = align256(L.qmean + 4 * (size_t)H * qb * router::D);
-    L.qh = align256(L.kmean + 4 * (size_t)H * kb * router::D);
-    L.kh = align256(L.qh + 4 * (size_t)H * qb * R);
-    L.total = align256(L.kh + 4 * (size_t)H * kb * R);
+    L.qh = 0;
+    L.khT = align256(L.qh + 4 * (size_t)H * qb * R);
+    L.total = align256(L.khT + 4 * (size_t)H * R * kbp);
     return L;
 }
 
@@ -323,40 +322,39 @@ static int count_forced(int Lq, int Lk, int block, int sink) {
 int router_check(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
                  int block, int sink_tokens, int extra, const int32_t *ids, int n_ids) {
     if (!q || !k || !wq || !wk || !ids) return SS_ERR_POINTER;
-    if (H <= 0 || H > 64 || Lq <= 0 || Lk < Lq || R <= 0 || R > router::MAX_R || (R & 7) ||
+    if (H <= 0 || H > 65535 || Lq <= 0 || Lk < Lq || R <= 0 || R > router::MAX_R || (R % 16) ||
         (block != 64 && block != 128) || sink_tokens < 0)
         return SS_ERR_SHAPE;
     const int kb = (Lk + block - 1) / block;
-    if (kb > router::MAX_KB) return SS_ERR_SHAPE;
+    if (kb > router::MAX_KB || select_smem(kb_padded(kb), R) > 227 * 1024) return SS_ERR_SHAPE;
     const int nforced = count_forced(Lq, Lk, block, sink_tokens);
     if (extra < 0 || extra > kb - nforced) return SS_ERR_BUDGET;
     if (n_ids != nforced + extra) return SS_ERR_SHAPE;
-    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k)) & 15u) return SS_ERR_POINTER;
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(wq) |
+         reinterpret_cast<uintptr_t>(wk)) & 15u)
+        return SS_ERR_POINTER;
     return 0;
 }
 
-// Launch the router kernels with the intermediates at the given device addresses
-// (ws points at a buffer of router_workspace_size bytes, 256-byte aligned).
+// Launch the router kernels with the intermediates in `ws` (router_workspace_size bytes,
+// 256-byte aligned).
 int router_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
                   int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores,
                   uint8_t *ws, int *status, cudaStream_t st) {
-    const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block;
+    const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block, kbp = kb_padded(kb);
     int device;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return (int)e;
     int rc = router_prepare(device);
     if (rc) return rc;
     const RouterLayout L = router_layout(H, Lq, Lk, R, block);
-    float *qmean = reinterpret_cast<float *>(ws + L.qmean), *kmean = reinterpret_cast<float *>(ws + L.kmean);
-    float *qh = reinterpret_cast<float *>(ws + L.qh), *kh = reinterpret_cast<float *>(ws + L.kh);
-    router::pool_kernel<<<qb + kb, H * 16, 0, st>>>((const uint16_t *)q, (const uint16_t *)k, H, Lq, Lk, block, qb,
-                                                   qmean, kmean);
-    const int tq = (qb + router::PROJ_ROWS - 1) / router::PROJ_ROWS, tk = (kb + router::PROJ_ROWS - 1) / router::PROJ_ROWS;
-    const size_t sm_proj = sizeof(float) * ((size_t)router::D * R + router::PROJ_ROWS * (router::D + 1));
-    router::project_kernel<<<dim3(tq + tk, H), 256, sm_proj, st>>>(qmean, kmean, wq, wk, qb, kb, tq, R, qh, kh);
-    const int rows = 4;
-    select_kernel(kb)<<<dim3((qb + rows - 1) / rows, H), rows * 32, select_smem(rows, R), st>>>(
-        qh, kh, qb, kb, R, block, Lq, Lk, sink_tokens, extra, ids, n_ids, mask, scores, status);
+    float *qh = reinterpret_cast<float *>(ws + L.qh), *khT = reinterpret_cast<float *>(ws + L.khT);
+    const int tq = (qb + router::BG - 1) / router::BG, tk = (kb + router::BG - 1) / router::BG;
+    router::pool_project_kernel<<<dim3(tq + tk, H), router::PP_THREADS, pp_smem(R), st>>>(
+        (const uint16_t *)q, (const uint16_t *)k, H, Lq, Lk, block, R, tq, wq, wk, qh, khT, kbp, status);
+    router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::ROWS * 32,
+                                  select_smem(kbp, R), st>>>(qh, khT, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
+                                                             extra, ids, n_ids, mask, scores, status);
     return (int)cudaGetLastError();
 }
 

@@ -40,8 +40,8 @@ def test_version(lib):
 def test_workspace_and_capacity_queries(lib):
     n = ctypes.c_size_t()
     assert lib.ss_router_workspace_bytes(12, 4680, 32760, 64, 64, ctypes.byref(n)) == 0
-    # pooled means (128 wide) and projections (64 wide) of 74 query + 512 key blocks, fp32
-    assert n.value >= 4 * 12 * (74 + 512) * (128 + 64)
+    # 64-wide fp32 projections of the 74 query and 512 key blocks of every head
+    assert n.value >= 4 * 12 * (74 + 512) * 64
     m = ctypes.c_int()
     assert lib.ss_attention_max_ids(32760, 64, ctypes.byref(m)) == 0
     assert m.value == 512          # config 2 fits with every block listed
