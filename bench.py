@@ -218,6 +218,53 @@ def run_reference(args, rank: int):
 # GPU arm
 # ----------------------------------------------------------------------------------------------
 
+def cache_append_bench(dev, inputs, args):
+    """Time ss_cache_append writing the current chunk (4680 tokens of K and V) into a 32760-token
+    global cache; algorithmic bytes = chunk read + chunk written, for K and V. Four (chunk, cache)
+    pairs rotate, so each append's 57.5 MB come from and go to HBM rather than L2 (4 x 229 MB)."""
+    from streaming_sparse_b200 import ops
+    _, k, v, _, _ = inputs
+    start = LK - LQ
+    pairs = []
+    for r in range(4):
+        kc = torch.zeros((LK, H, D), dtype=torch.bfloat16, device=dev)
+        vc = torch.zeros_like(kc)
+        kn = torch.roll(k[start:], r, 0).contiguous()
+        vn = torch.roll(v[start:], r, 0).contiguous()
+        pairs.append((kc, vc, kn, vn))
+
+    def once(i):
+        kc, vc, kn, vn = pairs[i % len(pairs)]
+        ops.cache_append(kc, vc, kn, vn, local_attn=False, global_end=start, local_end=start,
+                         current_start=start, sink_tokens=0)
+
+    for i in range(4):
+        once(i)
+    torch.cuda.synchronize()
+    reps = 8
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            once(i)
+    g.replay()
+    n = max(5, args.steps // reps)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(n):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = 1e3 * a.elapsed_time(b) / (n * reps)
+    kc, vc, kn, vn = pairs[0]
+    nbytes = 2 * 2 * kn.numel() * kn.element_size()
+    assert torch.equal(kc[start:], kn) and torch.equal(vc[start:], vn)
+    del pairs
+    return {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
+            "note": "chunk of 4680 tokens x 12 heads x 128 (K and V, bf16) read + written; 4 rotating "
+                    "(chunk, cache) pairs larger than L2; CUDA-graph replay"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch.distributed as dist
     from streaming_sparse_b200 import ops
@@ -339,6 +386,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         e2e_ms, e2e_flops = float(mx[0]), float(sm[1])
     e2e_value = e2e_flops / (e2e_ms * 1e-3) / 1e12
 
+    # ---- cache append (the chunk write of config 2 into a 32760-token window), HBM-bound
+    cache = cache_append_bench(dev, sets[0], args)
+
     if rank != 0:
         return
     peak, hbm, peak_kind = peaks()
@@ -364,6 +414,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output"},
+        "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
         "gpu_launches": 4 * args.steps,
         "clocks": clk.summary(),
     }
