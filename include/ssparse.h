@@ -6,8 +6,9 @@
  *   - Plain pointers to device memory, sizes as int / int64_t, a cudaStream_t passed as void*.
  *     No torch types cross this boundary.
  *   - The caller allocates every buffer (inputs, outputs, workspace). The library never allocates,
- *     frees or synchronises; work is enqueued on the caller's stream, so every entry point can be
- *     captured into a CUDA graph once ss_prepare_device() has run on that device.
+ *     frees or synchronises; work is enqueued on the caller's stream, so the entry points that
+ *     take their buffers from the caller can be captured into a CUDA graph once
+ *     ss_prepare_device() has run on that device.
  *   - Return value: 0 on success, a cudaError_t value (< 1000) if a CUDA call failed, or one of
  *     the SS_ERR_* codes below for invalid arguments (checked on the host before any launch).
  *   - Device-side faults (non-finite router score, a pipeline wait that timed out) are reported
@@ -87,6 +88,32 @@ int ss_router(const void *q, const void *k, const float *wq, const float *wk,
               int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
               int32_t *ids, int n_ids, uint8_t *mask, float *scores,
               void *workspace, size_t workspace_bytes, int *status, void *stream);
+
+/* Bytes of the static device array used by ss_router_noalloc (8 MiB per device that loads the
+   library, held until the process exits). */
+#define SS_ROUTER_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* ss_router for callers that cannot allocate device memory: no workspace argument and no
+ * allocation. This entry point has no counterpart in the reference (whose router ops allocate
+ * their intermediates through torch). It serves hosts whose device memory is handed out by their
+ * own fixed pool (so a cudaMalloc or a torch allocation per call is unavailable or fails), and
+ * hosts binding the library from a language that has no device allocator of its own.
+ *   - The intermediates (ss_router_workspace_bytes for these sizes) live in one static device
+ *     array of SS_ROUTER_STATIC_SCRATCH_BYTES per device; larger problems return
+ *     SS_ERR_WORKSPACE before anything is launched (about 4.9 MB at a 98 280-token window with
+ *     12 heads and 64-token blocks).
+ *   - The first call on a device looks up that device's address of the array
+ *     (cudaGetSymbolAddress, with the device current); make that first call before capturing
+ *     any stream on that device.
+ *   - All calls on a device share the array: calls that overlap on the GPU (different streams
+ *     or host threads) race, so the caller serialises them. Nothing in the array needs to start
+ *     at zero: each call writes every value that affects its results (the few padding entries
+ *     it copies along with them are never used).
+ * Other arguments, results and status codes are those of ss_router. */
+int ss_router_noalloc(const void *q, const void *k, const float *wq, const float *wk,
+                      int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
+                      int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *status,
+                      void *stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Block-sparse attention (tcgen05 / TMEM / TMA, sm_100a).                                     */

@@ -21,6 +21,7 @@
 // The fixed summation order makes every score bit-identical to the CPU oracle. The score GEMM is
 // tens of MFMA per chunk-layer, so CUDA-core FFMA keeps it exact at a cost of microseconds.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -358,7 +359,54 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     return (int)cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------
+// ss_router_noalloc: the router with its intermediates in a static device array.
+// ---------------------------------------------------------------------------------------------
+// For callers that cannot allocate device memory per call. Every call on a device shares this
+// one array (it keeps the previous call's contents; nothing in it has to start at zero, because
+// each call writes every value that affects its results -- the few padding entries of the
+// transposed key rows are copied along but never used), so calls that may overlap on the GPU --
+// two streams, or two host threads -- race and must be serialised by the caller.
+static __device__ __align__(256) uint8_t g_router_scratch[SS_ROUTER_STATIC_SCRATCH_BYTES];
+
+static std::mutex g_router_scratch_mutex;
+static uint8_t *g_router_scratch_addr[64] = {nullptr};
+
+// Device address of g_router_scratch on the current device. In host code the symbol is only a
+// host-side stand-in; a kernel given it would fault (or, where the GPU can reach host memory,
+// silently use the wrong memory), so the address is looked up once per device, with that device
+// current, and cached.
+static int router_scratch_address(int device, uint8_t **addr) {
+    std::lock_guard<std::mutex> lock(g_router_scratch_mutex);
+    if (!g_router_scratch_addr[device]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
+        if (e != cudaSuccess) return (int)e;
+        if (!p) return SS_ERR_POINTER;
+        g_router_scratch_addr[device] = static_cast<uint8_t *>(p);
+    }
+    *addr = g_router_scratch_addr[device];
+    return 0;
+}
+
 }  // namespace ss
+
+extern "C" int ss_router_noalloc(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk,
+                                 int R, int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask,
+                                 float *scores, int *status, void *stream) {
+    int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
+    if (rc) return rc;
+    if (ss::router_workspace_size(H, Lq, Lk, R, block) > (size_t)SS_ROUTER_STATIC_SCRATCH_BYTES) return SS_ERR_WORKSPACE;
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    if (device < 0 || device >= 64) return SS_ERR_SHAPE;
+    uint8_t *scratch = nullptr;
+    rc = ss::router_scratch_address(device, &scratch);
+    if (rc) return rc;
+    return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores, scratch,
+                             status, static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes) {
     if (!bytes || H <= 0 || Lq <= 0 || Lk <= 0 || R <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
