@@ -9,74 +9,85 @@
 // csrc/fixed15_attention.cu:248-387); the design below is sm_100a-specific.
 //
 // Work decomposition
-//   One CTA per (head, 128-row query tile). With 64-token router blocks a tile holds two query
-//   blocks; the CTA walks the union of their block lists and masks, per 64-row half, the blocks
-//   that half did not select. With 128-token blocks a tile is exactly one query block.
-//   The union is walked in steps of 128 KV tokens (two 64-token sub-blocks, each gathered by
-//   TMA at its own row offset, so the two need not be adjacent). CTAs are ordered head-major
-//   so the CTAs resident at one time share a few heads' K/V in L2.
+//   A tile is 128 query rows of one head: two 64-token query blocks (router block 64; the tile
+//   walks the union of their block lists and masks, per 64-row half, the blocks that half did
+//   not select) or one 128-token query block. The union is walked in steps of 128 KV tokens
+//   (two 64-token sub-blocks, each gathered by TMA at its own row offset).
+//   The grid is persistent: G <= #SMs CTAs; CTA c runs tiles c, c+G, c+2G, ... of the
+//   head-major tile order, so at any time the CTAs of the grid share a few heads' K/V in L2.
+//   Both softmax warpgroups work on the same tile: warpgroup w takes the steps of parity w,
+//   with its own O accumulator and running max; the halves are merged by log-sum-exp at the
+//   end of the tile. Two independent softmax streams let the tensor pipe run one warpgroup's
+//   MMAs while the other exponentiates.
 //
 // Warp roles (384 threads; every role runs on a whole converged warp and issues its
 // single-thread instructions -- TMA, tcgen05.mma, tcgen05.commit -- from an elected lane)
-//   warp 0      K producer: TMA loads of K steps into a 3-stage ring
+//   warp 0      list construction (prologue), then the TMA producer of the K/V ring
 //   warp 1      TMEM allocator + tcgen05.mma issuer
-//   warp 2      V producer: TMA loads of V steps into a 3-stage ring
-//   warp 3      block-list construction in the prologue, idle afterwards
-//   warps 4-11  softmax: group g (warps 4+4g .. 7+4g) owns sub-block g of every step, i.e. score
-//               columns [64g, 64g+64). In the prologue the groups copy the Q tile into TMEM (the QK
-//               MMA reads Q from TMEM, so shared-memory bandwidth goes to K and V only). Thread r
-//               of a group owns query row r (TMEM lane r). Per step both groups copy all 128 scores
-//               of their row to registers and release the S buffer at once (the QK MMA two steps
-//               ahead can start), derive the same running max (no exchange needed), exponentiate
-//               their 64 columns, write P (bf16) to their P columns in TMEM (the PV MMA reads P
-//               from TMEM) and rescale their half of the shared O accumulator when the running
-//               max grows by more than 2^8.
+//   warps 2-3   idle after the prologue
+//   warps 4-7   softmax warpgroup 0,   warps 8-11  softmax warpgroup 1
+//               After the prologue the control warpgroup (warps 0-3) gives registers up
+//               (setmaxnreg 56) and the softmax warpgroups take them (224): a softmax thread
+//               holds the 128 scores of its row.
+//               Thread r (r = 32*(warp%4) + lane) owns query row r of the tile (TMEM lane r).
+//               Per step: copy the 128 scores of its row from TMEM and release S, mask, row
+//               max, lazy rescale (only when the running max grows by more than 2^8),
+//               exponentiate (a quarter on the FMA pipe), write P (bf16) once the previous PV
+//               has read the P buffer, release P.
 //
-// TMEM (512 columns): S of step parity b at [128b, 128b+128); Q (bf16 pairs) at [256, 320); P of
-// group g at [320+32g, 352+32g); O at [384, 512).
-// MMAs: S = Q K^T (M=128, N=128, K=128; A = Q in TMEM, B = K K-major in shared memory, 128-byte
-//       swizzle), O += P V (M=128, N=128, K=128 tokens; A = P in TMEM, B = V MN-major in shared
-//       memory). tcgen05.mma instructions of one thread execute in order, so the QK MMA that
-//       reuses an S buffer (issued after the PV MMA that reads P from it) cannot overtake that read.
+// TMEM (512 columns): S [0,128) (one buffer, used by the warpgroups' QKs in turn); P [128,192)
+// (bf16 pairs, one buffer in turn); Q [192,256) (bf16 pairs, the tile's queries, written by the
+// softmax threads); O of warpgroup w at [256+128w, 384+128w).
+// MMAs: S = Q K^T (M=128, N=128, K=128; A = Q in TMEM, B = K entry, K-major, 128-byte swizzle),
+//       O_w += P V (M=128, N=128, K=128 tokens; A = P in TMEM, B = V entry, MN-major).
+// MMA order per tile: QK0(0), QK1(0), then for each i: QK0(i+1), PV0(i), QK1(i+1), PV1(i). A
+// warpgroup's next QK needs only the S buffer (P has its own), so it is issued ahead of its PV and
+// the next scores are ready when the warpgroup finishes its exponentials.
+// Shared memory: barriers and tables, then a ring of NST K/V entries (128 tokens x 128 dims
+// bf16 each), the block bitmaps and the step lists.
 // Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its TMA loads and MMAs,
 // frees TMEM, sets SS_DEV_TIMEOUT in *status and exits.
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ss {
 namespace attn {
 
 constexpr int D = 128;
-constexpr int TILE_M = 128;
-constexpr int SUB = 64;
-constexpr int KSTAGES = 3;
-constexpr int VSTAGES = 3;
 constexpr int NTHREADS = 384;
-constexpr uint32_t REGION = 16384;                 // 128 rows x 128 B: one 64-column half of a step
-constexpr uint32_t KV_BYTES = 2 * REGION;          // 128 tokens x 128 dims bf16
-constexpr uint32_t OFF_K = 0;
-constexpr uint32_t OFF_V = OFF_K + KSTAGES * KV_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
-constexpr int NBAR = 24;
-constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t OFF_LSUM = OFF_MISC + 64;       // [2 groups][128 rows] partial row sums
-constexpr uint32_t OFF_DYN = OFF_LSUM + 2 * 128 * 4;   // bitmaps, then the sub-block list
+constexpr int REG_CTRL = 56, REG_SOFTMAX = 224;    // setmaxnreg split of the 384 x 168 launch registers
+static_assert(128 * REG_CTRL + 256 * REG_SOFTMAX <= NTHREADS * 168, "register split exceeds the launch");
+constexpr int NST = 6;                             // K/V ring entries
+constexpr int MAXT = 16;                           // tiles per CTA
+constexpr uint32_t REGION = 16384;                 // 128 rows x 128 B: one 64-column half of a tile
+constexpr uint32_t TILE_BYTES = 2 * REGION;        // 128 rows x 128 dims bf16
+constexpr uint32_t OFF_BAR = 0;
+constexpr int NBAR = 32;
+constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;  // flags and counters
+constexpr uint32_t OFF_TILES = OFF_MISC + 64;      // Tile table [MAXT]
+constexpr uint32_t OFF_XCH = 1024;                 // log-sum-exp merge: [2 wg][m, l][128 rows]
+constexpr uint32_t OFF_RING = OFF_XCH + 2 * 2 * 128 * 4;  // 1024-aligned
 constexpr uint32_t SMEM_LIMIT = 232448;            // 227 KB opt-in maximum per CTA
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TMEM_S = 0, TMEM_Q = 256, TMEM_P = 320, TMEM_O = 384;
+constexpr uint32_t TMEM_S = 0, TMEM_P = 128, TMEM_Q = 192, TMEM_O = 256;
+constexpr int POLY_FROM = 48;                      // columns [48, 64) of each sub-block: FMA-pipe exp2
+static_assert(OFF_TILES + MAXT * 16 <= OFF_XCH, "table space");
+static_assert(OFF_RING % 1024 == 0, "ring alignment");
 
 enum Bar {
-    Q_FULL = 0,                  // Q tile copied into TMEM (256 softmax threads)
-    K_FULL = 1,
-    K_EMPTY = K_FULL + KSTAGES,
-    V_FULL = K_EMPTY + KSTAGES,
-    V_EMPTY = V_FULL + VSTAGES,
-    S_FULL = V_EMPTY + VSTAGES,  // per S buffer (step parity): QK result ready
-    S_FREE = S_FULL + 2,         // per S buffer: both groups copied the scores out (256 arrivals)
-    P_FULL = S_FREE + 2,         // per step parity: P written by both groups (256 arrivals)
-    O_DONE = P_FULL + 2,         // PV of a step completed (O up to date, P consumed)
-    XSUM = O_DONE + 1,           // epilogue: both groups' row sums written (256 arrivals)
-    DRAIN = XSUM + 1,
-    NBAR_USED
+    Q_FULL = 0,                  // the tile's Q written to TMEM (256 arrivals)
+    S_FULL = 1,                  // per warpgroup: its QK completed
+    S_FREE = 3,                  // per warpgroup: S copied to registers (128 arrivals)
+    P_FULL = 5,                  // per warpgroup: P written (128 arrivals)
+    PV_DONE = 7,                 // per warpgroup: its PV completed
+    XSUM = 9,                    // tile end: both warpgroups posted m, l (256 arrivals)
+    XDONE = 10,                  // tile end: both warpgroups read both O accumulators (256 arrivals)
+    DRAIN = 11,
+    FULL = 12,                   // per ring entry
+    EMPTY = FULL + NST,
+    NBAR_USED = EMPTY + NST
 };
 static_assert(NBAR_USED <= NBAR, "barrier space");
 
@@ -90,13 +101,28 @@ __device__ __forceinline__ uint32_t entry(uint32_t start, uint32_t valid, uint32
 __device__ __forceinline__ int e_start(uint32_t e) { return (int)(e & 0xFFFFFu); }
 __device__ __forceinline__ int e_valid(uint32_t e) { return (int)((e >> 20) & 127u); }
 
+struct Tile {
+    int first, n, tile, pad;     // steps [first, first+n) of the step array (n even, >= 2); tile id
+};
+
+// Position in the K/V ring: entry index and the parity of its use.
+struct Ring {
+    int e = 0, ph = 0;
+    __device__ __forceinline__ void next() {
+        if (++e == NST) {
+            e = 0;
+            ph ^= 1;
+        }
+    }
+};
+
 struct Params {
     const __nv_bfloat16 *q;
     const int32_t *ids;
     void *out;
     float *lse;
     int *status;
-    int H, Lq, Lk, block, n_ids, qb, kb, ntiles, nwords, out_fp32;
+    int H, Lq, Lk, block, n_ids, qb, kb, ntiles, nwords, T, G, tmax, step_cap, out_fp32;
     float scale_log2;  // scale * log2(e)
 };
 
@@ -153,13 +179,55 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
+// Ascending compaction of the set bits of word(w) (w < nwords) into sub-block entries, run by
+// one warp; sub-block k of the output is stored at out[k]. Returns the number written.
+template <class W, class M>
+__device__ __forceinline__ int compact(int nwords, int block, int Lk, int lane, W &&word, M &&maskof, uint32_t *out) {
+    const int per = block / 64;
+    int carry = 0;
+    for (int w0 = 0; w0 < nwords; w0 += 32) {
+        const int w = w0 + lane;
+        uint32_t u = w < nwords ? word(w) : 0u;
+        const int cnt = __popc(u) * per;
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int pos = carry + incl - cnt;
+        while (u) {
+            const int bit = __ffs(u) - 1;
+            u &= u - 1;
+            const int j = w * 32 + bit;
+            const uint32_t m = maskof(w, bit);
+            for (int s = 0; s < per; ++s) {
+                const int t0 = j * block + s * 64;
+                const int valid = min(64, max(0, Lk - t0));
+                out[pos++] = entry((uint32_t)t0, (uint32_t)valid, m);
+            }
+        }
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    return carry;
+}
+
+// Q rows of the tile for one warpgroup: dims [64w, 64w + 64) of row `row` as 32 bf16 pairs.
+__device__ __forceinline__ void load_q(const Params &p, int h, int row, int w, uint32_t *qv) {
+    if (row < p.Lq) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)row * p.H + h) * D + 64 * w);
+#pragma unroll
+        for (int x = 0; x < 8; ++x) {
+            const uint4 v = src[x];
+            qv[4 * x] = v.x;
+            qv[4 * x + 1] = v.y;
+            qv[4 * x + 2] = v.z;
+            qv[4 * x + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) qv[x] = 0u;
+    }
 }
 
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -168,46 +236,39 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t sK = sbase + OFF_K, sV = sbase + OFF_V;
+    const uint32_t sRing = sbase + OFF_RING;
     const uint32_t bar0 = sbase + OFF_BAR;
     auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
-    volatile int *nsub_slot = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
-    volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 12);
-    float *lsum = reinterpret_cast<float *>(smem + OFF_LSUM);
-    uint32_t *bmA = reinterpret_cast<uint32_t *>(smem + OFF_DYN);
-    uint32_t *bmB = bmA + p.nwords;
-    uint32_t *steps = bmB + p.nwords;
+    volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
+    Tile *tiles = reinterpret_cast<Tile *>(smem + OFF_TILES);
+    float *xch = reinterpret_cast<float *>(smem + OFF_XCH);                              // [2][2][128]
+    uint32_t *bm = reinterpret_cast<uint32_t *>(smem + OFF_RING + NST * TILE_BYTES);     // [tmax][2][nwords]
+    uint2 *steps = reinterpret_cast<uint2 *>(bm + 2 * p.tmax * p.nwords);                // [step_cap]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.x / p.ntiles;
-    const int tile = blockIdx.x % p.ntiles;
-    const bool pair = (p.block == 64);
-    const int qblkA = pair ? 2 * tile : tile;
-    const int qblkB = pair ? 2 * tile + 1 : -1;
+    const int nt = (p.T - (int)blockIdx.x + p.G - 1) / p.G;    // tiles blockIdx.x + k*G < T
+    const bool pairq = (p.block == 64);
 
-    // ---------------- prologue: barriers, TMEM, the tile's sub-block list ----------------
+    // ---------------- prologue: barriers, TMEM, block bitmaps, step lists ----------------
     if (tid == 0) {
         *abort_flag = 0;
         *badid_flag = 0;
         mbar_init(bar(Q_FULL), 256);
-        for (int s = 0; s < KSTAGES; ++s) {
-            mbar_init(bar(K_FULL + s), 1);
-            mbar_init(bar(K_EMPTY + s), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(bar(S_FULL + s), 1);
+            mbar_init(bar(S_FREE + s), 128);
+            mbar_init(bar(P_FULL + s), 128);
+            mbar_init(bar(PV_DONE + s), 1);
         }
-        for (int s = 0; s < VSTAGES; ++s) {
-            mbar_init(bar(V_FULL + s), 1);
-            mbar_init(bar(V_EMPTY + s), 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(bar(S_FULL + b), 1);
-            mbar_init(bar(S_FREE + b), 256);
-            mbar_init(bar(P_FULL + b), 256);
-        }
-        mbar_init(bar(O_DONE), 1);
         mbar_init(bar(XSUM), 256);
+        mbar_init(bar(XDONE), 256);
         mbar_init(bar(DRAIN), 1);
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(bar(FULL + s), 1);
+            mbar_init(bar(EMPTY + s), 1);
+        }
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -218,228 +279,99 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         tmem_alloc(smem_u32((const void *)tmem_slot), TMEM_COLS);
         tmem_relinquish();
     }
-    for (int w = tid; w < 2 * p.nwords; w += NTHREADS) bmA[w] = 0u;
+    for (int w = tid; w < 2 * nt * p.nwords; w += NTHREADS) bm[w] = 0u;
     __syncthreads();
     {
-        const int32_t *la = p.ids + ((size_t)h * p.qb + qblkA) * p.n_ids;
-        const int32_t *lb = (qblkB >= 0 && qblkB < p.qb) ? p.ids + ((size_t)h * p.qb + qblkB) * p.n_ids : nullptr;
-        for (int i = tid; i < p.n_ids; i += NTHREADS) {
-            int a = la[i];
+        // bitmap (lt, half) <- ids of query block (pair ? 2*tile + half : tile) of head h
+        const int per_tile = (pairq ? 2 : 1) * p.n_ids;
+        for (int x = tid; x < nt * per_tile; x += NTHREADS) {
+            const int lt = x / per_tile, rem = x % per_tile, half = rem / p.n_ids, i = rem % p.n_ids;
+            const int t = (int)blockIdx.x + lt * p.G, h = t / p.ntiles, tile = t % p.ntiles;
+            const int qblk = pairq ? 2 * tile + half : tile;
+            if (qblk >= p.qb) continue;
+            const int a = p.ids[((size_t)h * p.qb + qblk) * p.n_ids + i];
             if (a >= p.kb) *badid_flag = 1;
-            else if (a >= 0) atomicOr(&bmA[a >> 5], 1u << (a & 31));
-            if (lb) {
-                int b = lb[i];
-                if (b >= p.kb) *badid_flag = 1;
-                else if (b >= 0) atomicOr(&bmB[b >> 5], 1u << (b & 31));
-            }
+            else if (a >= 0) atomicOr(&bm[(2 * lt + half) * p.nwords + (a >> 5)], 1u << (a & 31));
         }
     }
     __syncthreads();
-    if (warp == 3) {
-        // ascending compaction of the union bitmap into sub-block entries
-        const int per = p.block / SUB;  // sub-blocks per router block
-        int carry = 0;
-        for (int w0 = 0; w0 < p.nwords; w0 += 32) {
-            int w = w0 + lane;
-            uint32_t a = w < p.nwords ? bmA[w] : 0u, b = w < p.nwords ? bmB[w] : 0u, u = a | b;
-            int cnt = __popc(u) * per, incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
+    if (warp == 0) {
+        // per tile: ascending union sub-blocks, padded to a whole, even number (>= 2) of steps
+        uint32_t *sub = reinterpret_cast<uint32_t *>(steps);
+        int pos = 0;   // sub-blocks written
+        for (int lt = 0; lt < nt; ++lt) {
+            const uint32_t *A = bm + (2 * lt) * p.nwords, *B = A + p.nwords;
+            const int n = compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] | B[w]; },
+                                  [&](int w, int bit) -> uint32_t {
+                                      if (!pairq) return 3u;
+                                      return ((A[w] >> bit) & 1u) | (((B[w] >> bit) & 1u) << 1);
+                                  },
+                                  sub + pos);
+            const int padded = max(4, (n + 3) & ~3);
+            for (int k = n + lane; k < padded; k += 32) sub[pos + k] = entry(0u, 0u, 0u);
+            if (lane == 0) {
+                Tile tl;
+                tl.first = pos / 2;
+                tl.n = padded / 2;
+                tl.tile = (int)blockIdx.x + lt * p.G;
+                tl.pad = 0;
+                tiles[lt] = tl;
             }
-            int pos = carry + incl - cnt;
-            while (u) {
-                int bit = __ffs(u) - 1;
-                u &= u - 1;
-                int j = w * 32 + bit;
-                uint32_t m = pair ? (((a >> bit) & 1u) | (((b >> bit) & 1u) << 1)) : 3u;
-                for (int s = 0; s < per; ++s) {
-                    int t0 = j * p.block + s * SUB;
-                    int valid = min(SUB, max(0, p.Lk - t0));
-                    steps[pos++] = entry((uint32_t)t0, (uint32_t)valid, m);
-                }
-            }
-            carry += __shfl_sync(0xffffffffu, incl, 31);
-        }
-        if (lane == 0) {
-            if (carry & 1) steps[carry++] = entry(0u, 0u, 0u);  // pad to whole 128-token steps
-            *nsub_slot = carry;
+            pos += padded;
+            __syncwarp();
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int nsteps = *nsub_slot / 2;
-    const int xh = h * D;
 
-    if (warp == 0 || warp == 2) {
-        // ---------------- K (warp 0) / V (warp 2) producer ----------------
-        const bool isk = warp == 0;
-        const CUtensorMap *tm = isk ? &tm_k : &tm_v;
-        const uint32_t ring = isk ? sK : sV;
-        const int stages = isk ? KSTAGES : VSTAGES;
-        const int full = isk ? K_FULL : V_FULL, empty = isk ? K_EMPTY : V_EMPTY;
-        int issued = 0;
+    if (warp >= 4) {
+        // The softmax warpgroups and the control warpgroup run with different register budgets
+        // and never share code after this point (each branch ends with its own teardown).
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFTMAX));
+        // ---------------- softmax warpgroups + epilogues ----------------
+        const int wg = (warp - 4) >> 2;
+        const int q4 = warp & 3;
+        const int r = q4 * 32 + lane;                // row within the tile == TMEM lane
+        const int half = r >> 6;                     // which 64-row query block of the pair
+        const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+        const uint32_t s_addr = lane_base + TMEM_S, p_addr = lane_base + TMEM_P;
+        const uint32_t o_addr = lane_base + TMEM_O + 128 * wg;
+        const float sl2 = p.scale_log2;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
         bool ok = true;
-        for (int j = 0; j < nsteps; ++j) {
-            const int st = j % stages, it = j / stages;
-            if (it > 0) ok = warp_all_ok(mbar_wait(bar(empty + st), (it - 1) & 1, abort_flag));
-            if (!ok) break;
-            const int t0 = e_start(steps[2 * j]), t1 = e_start(steps[2 * j + 1]);
-            const uint32_t dst = ring + st * KV_BYTES;
-            if (elect_one()) {
-                mbar_arrive_expect_tx(bar(full + st), KV_BYTES);
-                tma_load_2d(dst, tm, xh, t0, bar(full + st));
-                tma_load_2d(dst + REGION, tm, xh + 64, t0, bar(full + st));
-                tma_load_2d(dst + REGION / 2, tm, xh, t1, bar(full + st));
-                tma_load_2d(dst + REGION + REGION / 2, tm, xh + 64, t1, bar(full + st));
-            }
-            __syncwarp();
-            issued = j + 1;
-        }
-        if (!ok) {  // drain: loads still landing in shared memory
-            volatile int never = 0;
-            for (int j = max(0, issued - stages); j < issued; ++j)
-                mbar_wait(bar(full + j % stages), (j / stages) & 1, &never);
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (nsteps > 0) {
-            bool ok = warp_all_ok(mbar_wait(bar(Q_FULL), 0, abort_flag));
-            tc_fence_after();
-            auto issue_qk = [&](int j) -> bool {  // S_(j&1) = Q K_j^T
-                const int st = j % KSTAGES, it = j / KSTAGES, b = j & 1;
-                if (!warp_all_ok(mbar_wait(bar(K_FULL + st), it & 1, abort_flag))) return false;
-                tc_fence_after();
-                const uint32_t dk = sK + st * KV_BYTES;
-                if (elect_one()) {
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_bf16_ts(tmem + TMEM_S + 128 * b, tmem + TMEM_Q + kk * 8,
-                                    smem_desc_sw128(dk + (kk >> 2) * REGION + (kk & 3) * 32, 16, 1024), IDESC_QK,
-                                    kk > 0 ? 1u : 0u);
-                    tc_commit(bar(S_FULL + b));
-                    tc_commit(bar(K_EMPTY + st));
-                }
-                __syncwarp();
-                return true;
-            };
-            auto issue_pv = [&](int j) -> bool {  // O += P_j V_j
-                const int st = j % VSTAGES, it = j / VSTAGES, b = j & 1;
-                if (!warp_all_ok(mbar_wait(bar(P_FULL + b), (j >> 1) & 1, abort_flag))) return false;
-                if (!warp_all_ok(mbar_wait(bar(V_FULL + st), it & 1, abort_flag))) return false;
-                tc_fence_after();
-                const uint32_t dv = sV + st * KV_BYTES;
-                if (elect_one()) {
-                    // tokens 16kk.. of the step: P of sub-block kk/4 sits in the P columns of group kk/4
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_bf16_ts(tmem + TMEM_O, tmem + TMEM_P + 8 * kk,
-                                    smem_desc_sw128(dv + kk * 2048, REGION, 1024), IDESC_PV,
-                                    (j > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(bar(O_DONE));
-                    tc_commit(bar(V_EMPTY + st));
-                }
-                __syncwarp();
-                return true;
-            };
-            if (ok) ok = issue_qk(0);
-            if (ok && nsteps > 1) ok = issue_qk(1);
-            for (int j = 0; j < nsteps && ok; ++j) {
-                if (j + 2 < nsteps) {
-                    // S_(j&1) is free once both groups copied step j's scores out
-                    ok = warp_all_ok(mbar_wait(bar(S_FREE + (j & 1)), (j >> 1) & 1, abort_flag));
-                    if (ok) ok = issue_qk(j + 2);
-                }
-                if (ok) ok = issue_pv(j);
-            }
-            // every MMA issued above has completed once DRAIN fires
-            if (elect_one()) tc_commit(bar(DRAIN));
-            __syncwarp();
-            volatile int never = 0;
-            mbar_wait(bar(DRAIN), 0, &never);
-        }
-    } else if (warp >= 4) {
-        // ---------------- softmax groups + epilogue ----------------
-        const int grp = (warp - 4) >> 2;    // sub-block (score columns [64g, 64g+64)) of each step
-        const int r = (tid - 128) & 127;    // row within the tile == TMEM lane
-        const int half = r >> 6;            // which 64-row query block of the pair
-        const uint32_t lane_base = tmem + ((uint32_t)((r >> 5) * 32) << 16);
-        const int row = tile * TILE_M + r;
-        // Q tile -> TMEM: group g copies dims [64g, 64g + 64) of row r as bf16 pairs
+        int k = 0;                                   // steps of this warpgroup so far
+        uint32_t qv[32];
         {
-            uint32_t qv[32];
-            if (row < p.Lq) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)row * p.H + h) * D + 64 * grp);
-#pragma unroll
-                for (int x = 0; x < 8; ++x) {
-                    const uint4 v = src[x];
-                    qv[4 * x] = v.x;
-                    qv[4 * x + 1] = v.y;
-                    qv[4 * x + 2] = v.z;
-                    qv[4 * x + 3] = v.w;
-                }
-            } else {
-#pragma unroll
-                for (int x = 0; x < 32; ++x) qv[x] = 0u;
-            }
-            tmem_st32(lane_base + TMEM_Q + 32 * grp, reinterpret_cast<const float *>(qv));
+            const int t0 = tiles[0].tile;
+            load_q(p, t0 / p.ntiles, (t0 % p.ntiles) * 128 + r, wg, qv);
+            tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(Q_FULL));
         }
-        const uint32_t o_addr = lane_base + TMEM_O + 64 * grp;   // this group's half of O
-        const float sl2 = p.scale_log2;
-        const uint64_t sl2x2 = f2_pack(sl2, sl2);
-        float m = -INFINITY, l = 0.f;        // m identical in both groups; l partial per group
-        bool ok = true;
-        int j = 0;
-        for (; j < nsteps && ok; ++j) {
-            const int b = j & 1;
-            ok = warp_all_ok(mbar_wait(bar(S_FULL + b), (j >> 1) & 1, abort_flag));
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t s_addr = lane_base + TMEM_S + 128 * b + 64 * grp;
-            const uint32_t e = steps[2 * j + grp], eo = steps[2 * j + (grp ^ 1)];
-            // selection and valid length, warp-uniform (a warp lies within one 64-row half)
-            const bool sel = (e >> (27 + half)) & 1u, selo = (eo >> (27 + half)) & 1u;
-            const int valid = sel ? e_valid(e) : 0, valido = selo ? e_valid(eo) : 0;
-            // row max over the whole step: both groups read all 128 columns, so both derive the
-            // same running max without exchanging it; each keeps the 64 scores it exponentiates.
-            float s[64];
-            float mx = -INFINITY;
-            if (sel) {
+        for (int lt = 0; lt < nt && ok; ++lt) {
+            const Tile tl = tiles[lt];
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < tl.n / 2; ++j, ++k) {
+                const uint2 st = steps[tl.first + 2 * j + wg];
+                ok = warp_all_ok(mbar_wait(bar(S_FULL + wg), k & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+                float s[128];
                 tmem_ld32(s_addr, s);
                 tmem_ld32(s_addr + 32, s + 32);
-            }
-            if (selo) {
-                float t[64];
-                const uint32_t o_s = lane_base + TMEM_S + 128 * b + 64 * (grp ^ 1);
-                tmem_ld32(o_s, t);
-                tmem_ld32(o_s + 32, t + 32);
+                tmem_ld32(s_addr + 64, s + 64);
+                tmem_ld32(s_addr + 96, s + 96);
+                // selection and valid length per sub-block, warp-uniform (a warp lies in one half)
+                const bool sel0 = (st.x >> (27 + half)) & 1u, sel1 = (st.y >> (27 + half)) & 1u;
+                const int v0 = sel0 ? e_valid(st.x) : 0, v1 = sel1 ? e_valid(st.y) : 0;
                 tmem_wait_ld();
-                if (valido == SUB) {
-                    float m0 = t[0], m1 = t[1], m2 = t[2], m3 = t[3];
-#pragma unroll
-                    for (int c = 4; c < 64; c += 8) {
-                        m0 = max3(m0, t[c], t[c + 1]);
-                        m1 = max3(m1, t[c + 2], t[c + 3]);
-                        m2 = max3(m2, t[c + 4], t[c + 5]);
-                        m3 = max3(m3, t[c + 6], t[c + 7]);
-                    }
-                    mx = max3(fmaxf(m0, m1), m2, m3);
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 64; ++c) mx = fmaxf(mx, c < valido ? t[c] : -INFINITY);
-                }
-            }
-            if (sel) tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(bar(S_FREE + b));
-            if (sel) {
-                if (valid == SUB) {
+                tc_fence_before();
+                mbar_arrive(bar(S_FREE + wg));       // the next QK may overwrite S
+                float mx = -INFINITY;
+                if (v0 == 64) {
                     float m0 = s[0], m1 = s[1], m2 = s[2], m3 = s[3];
 #pragma unroll
                     for (int c = 4; c < 64; c += 8) {
@@ -448,129 +380,289 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                         m2 = max3(m2, s[c + 4], s[c + 5]);
                         m3 = max3(m3, s[c + 6], s[c + 7]);
                     }
-                    mx = max3(mx, fmaxf(m0, m1), fmaxf(m2, m3));
-                } else {
+                    mx = max3(fmaxf(m0, m1), m2, m3);
+                } else if (v0 > 0) {
 #pragma unroll
                     for (int c = 0; c < 64; ++c) {
-                        s[c] = c < valid ? s[c] : -INFINITY;
+                        s[c] = c < v0 ? s[c] : -INFINITY;
                         mx = fmaxf(mx, s[c]);
                     }
                 }
-            }
-            // lazy rescale: move the reference max only when the row max grew by more than 2^8
-            const float mnew = mx * sl2;
-            float alpha = 1.f;
-            bool grow = false;                   // an O row that is not all zeros must be scaled
-            if (mnew > m + 8.0f) {
-                grow = m != -INFINITY;
-                alpha = grow ? ex2(m - mnew) : 0.f;
-                l *= alpha;
-                m = mnew;
-            }
-            // O and the P columns change through the previous step's PV; tcgen05.ld/st are
-            // warp-collective, so the whole warp rescales its half of O if any of its rows must.
-            bool o_ready = j == 0;
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
-                ok = warp_all_ok(mbar_wait(bar(O_DONE), (j - 1) & 1, abort_flag));
-                if (!ok) break;
-                tc_fence_after();
-                o_ready = true;
-#pragma unroll 1
-                for (int c = 0; c < 2; ++c) {
-                    float o[32];
-                    tmem_ld32(o_addr + 32 * c, o);
-                    tmem_wait_ld();
+                if (v1 == 64) {
+                    float m0 = s[64], m1 = s[65], m2 = s[66], m3 = s[67];
 #pragma unroll
-                    for (int x = 0; x < 32; ++x) o[x] *= (grow ? alpha : 1.f);
-                    tmem_st32(o_addr + 32 * c, o);
+                    for (int c = 68; c < 128; c += 8) {
+                        m0 = max3(m0, s[c], s[c + 1]);
+                        m1 = max3(m1, s[c + 2], s[c + 3]);
+                        m2 = max3(m2, s[c + 4], s[c + 5]);
+                        m3 = max3(m3, s[c + 6], s[c + 7]);
+                    }
+                    mx = max3(mx, fmaxf(m0, m1), fmaxf(m2, m3));
+                } else if (v1 > 0) {
+#pragma unroll
+                    for (int c = 64; c < 128; ++c) {
+                        s[c] = c - 64 < v1 ? s[c] : -INFINITY;
+                        mx = fmaxf(mx, s[c]);
+                    }
                 }
-            }
-            // P = 2^(s*sl2 - m) as bf16 pairs over the first 32 columns this group read
-            uint32_t pk[32];
-            if (sel) {
+                // lazy rescale: move the reference max only when the row max grew by more than 2^8
+                const float mnew = mx * sl2;
+                float alpha = 1.f;
+                bool grow = false;                   // an O row holding earlier steps must be scaled
+                if (mnew > m + 8.0f) {
+                    grow = m != -INFINITY;
+                    alpha = grow ? ex2(m - mnew) : 0.f;
+                    l *= alpha;
+                    m = mnew;
+                }
+                // O_w holds the previous steps once this warpgroup's previous PV completed;
+                // tcgen05.ld/st are warp-collective, so the whole warp rescales if any row must.
+                if (__any_sync(0xffffffffu, grow)) {
+                    ok = warp_all_ok(mbar_wait(bar(PV_DONE + wg), (k - 1) & 1, abort_flag));
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        float o[32];
+                        tmem_ld32(o_addr + 32 * c, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int x = 0; x < 32; ++x) o[x] *= (grow ? alpha : 1.f);
+                        tmem_st32(o_addr + 32 * c, o);
+                    }
+                }
+                // P = 2^(s*sl2 - m) as bf16 pairs
                 const float base = (m == -INFINITY) ? 0.f : m;
                 const uint64_t nbx2 = f2_pack(-base, -base);
                 uint64_t sa = 0, sb = 0;
+                uint32_t pk[64];
 #pragma unroll
-                for (int c = 0; c < 64; c += 4) {
-                    const uint64_t x0 = f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, nbx2);
-                    const uint64_t x1 = f2_fma(f2_pack(s[c + 2], s[c + 3]), sl2x2, nbx2);
-                    float p0, p1, p2, p3;
-                    if (c < 48) {   // MUFU
-                        p0 = ex2(f2_lo(x0));
-                        p1 = ex2(f2_hi(x0));
-                        p2 = ex2(f2_lo(x1));
-                        p3 = ex2(f2_hi(x1));
-                    } else {        // FMA pipe (a quarter of the exponentials)
-                        exp2_poly2(f2_lo(x0), f2_hi(x0), p0, p1);
-                        exp2_poly2(f2_lo(x1), f2_hi(x1), p2, p3);
+                for (int g = 0; g < 2; ++g) {
+                    const bool on = g == 0 ? v0 > 0 : v1 > 0;
+                    if (on) {
+#pragma unroll
+                        for (int c = 0; c < 64; c += 4) {
+                            const int cc = 64 * g + c;
+                            const uint64_t x0 = f2_fma(f2_pack(s[cc], s[cc + 1]), sl2x2, nbx2);
+                            const uint64_t x1 = f2_fma(f2_pack(s[cc + 2], s[cc + 3]), sl2x2, nbx2);
+                            float p0, p1, p2, p3;
+                            if (c < POLY_FROM) {   // MUFU
+                                p0 = ex2(f2_lo(x0));
+                                p1 = ex2(f2_hi(x0));
+                                p2 = ex2(f2_lo(x1));
+                                p3 = ex2(f2_hi(x1));
+                            } else {               // FMA pipe
+                                exp2_poly2(f2_lo(x0), f2_hi(x0), p0, p1);
+                                exp2_poly2(f2_lo(x1), f2_hi(x1), p2, p3);
+                            }
+                            sa = f2_add(sa, f2_pack(p0, p1));
+                            sb = f2_add(sb, f2_pack(p2, p3));
+                            pk[cc >> 1] = pack_bf16x2(p0, p1);
+                            pk[(cc >> 1) + 1] = pack_bf16x2(p2, p3);
+                        }
+                    } else {
+#pragma unroll
+                        for (int x = 0; x < 32; ++x) pk[32 * g + x] = 0u;
                     }
-                    sa = f2_add(sa, f2_pack(p0, p1));
-                    sb = f2_add(sb, f2_pack(p2, p3));
-                    pk[c >> 1] = pack_bf16x2(p0, p1);
-                    pk[(c >> 1) + 1] = pack_bf16x2(p2, p3);
                 }
                 const uint64_t st2 = f2_add(sa, sb);
                 l += f2_lo(st2) + f2_hi(st2);
-            } else {
-#pragma unroll
-                for (int x = 0; x < 32; ++x) pk[x] = 0u;
-            }
-            // the P columns are free once the previous step's PV has read them
-            if (!o_ready) {
-                ok = warp_all_ok(mbar_wait(bar(O_DONE), (j - 1) & 1, abort_flag));
+                // the P buffer is free once the PV issued before ours has read it: PV1(k-1) for
+                // warpgroup 0, PV0(k) for warpgroup 1
+                if (wg == 0) {
+                    if (k > 0) ok = warp_all_ok(mbar_wait(bar(PV_DONE + 1), (k - 1) & 1, abort_flag));
+                } else {
+                    ok = warp_all_ok(mbar_wait(bar(PV_DONE + 0), k & 1, abort_flag));
+                }
                 if (!ok) break;
                 tc_fence_after();
+                tmem_st32(p_addr, reinterpret_cast<const float *>(pk));
+                tmem_st32(p_addr + 32, reinterpret_cast<const float *>(pk + 32));
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar(P_FULL + wg));
             }
-            const uint32_t p_addr = lane_base + TMEM_P + 32 * grp;
-            tmem_st16(p_addr, pk);
-            tmem_st16(p_addr + 16, pk + 16);
-            tmem_wait_st();
+            if (!ok) break;
+            // ---------------- tile epilogue: merge the two halves, write, load the next Q ----------------
+            const int h = tl.tile / p.ntiles, row = (tl.tile % p.ntiles) * 128 + r;
+            const bool live = row < p.Lq;
+            const bool more = lt + 1 < nt;
+            if (more) {   // bring the next tile's Q row slice (128 B) into L2 while we wait
+                const int tn = tiles[lt + 1].tile, rn = (tn % p.ntiles) * 128 + r;
+                if (rn < p.Lq)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.q + ((size_t)rn * p.H + tn / p.ntiles) * D + 64 * wg));
+            }
+            ok = warp_all_ok(mbar_wait(bar(PV_DONE + wg), (k - 1) & 1, abort_flag));   // our last PV
+            if (!ok) break;
+            xch[(wg * 2 + 0) * 128 + r] = m;
+            xch[(wg * 2 + 1) * 128 + r] = l;
             tc_fence_before();
-            mbar_arrive(bar(P_FULL + b));
-        }
-        // epilogue: O is final once the last PV has completed
-        bool have = ok && nsteps > 0;
-        if (have) have = warp_all_ok(mbar_wait(bar(O_DONE), (nsteps - 1) & 1, abort_flag));
-        if (have) tc_fence_after();
-        lsum[grp * 128 + r] = l;
-        mbar_arrive(bar(XSUM));
-        const bool summed = warp_all_ok(mbar_wait(bar(XSUM), 0, abort_flag));
-        const float lt = summed ? l + lsum[(grp ^ 1) * 128 + r] : 0.f;
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        const bool live = row < p.Lq && (pair ? (half == 0 ? qblkA < p.qb : qblkB < p.qb) : true);
-        // warp-uniform conditions only: tcgen05.ld is warp-collective
-        const bool fin = __all_sync(0xffffffffu, have && summed && !*abort_flag) != 0;
-        // group g writes output columns [64g, 64g + 64) of its row
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-            const int col = 64 * grp + 32 * c;
-            float o[32];
-            if (fin) {
-                tmem_ld32(lane_base + TMEM_O + col, o);
-                tmem_wait_ld();
-            }
+            mbar_arrive(bar(XSUM));
+            ok = warp_all_ok(mbar_wait(bar(XSUM), lt & 1, abort_flag));   // every MMA of the tile done
+            if (!ok) break;
+            tc_fence_after();
+            const float mo = xch[((wg ^ 1) * 2 + 0) * 128 + r], lo = xch[((wg ^ 1) * 2 + 1) * 128 + r];
+            const float M = fmaxf(m, mo);
+            const float a_s = (m == -INFINITY) ? 0.f : ex2(m - M);
+            const float a_o = (mo == -INFINITY) ? 0.f : ex2(mo - M);
+            const float L = l * a_s + lo * a_o;
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            // warpgroup w writes output columns [64w, 64w + 64): O0 and O1 are both read here
+            const uint32_t o_self = o_addr, o_oth = lane_base + TMEM_O + 128 * (wg ^ 1);
+            float res[64];
 #pragma unroll
-            for (int x = 0; x < 32; ++x) o[x] = fin ? o[x] * inv : 0.f;
-            if (live && (fin || nsteps == 0)) {
+            for (int c = 0; c < 2; ++c) {
+                float o[32], t[32];
+                tmem_ld32(o_self + 64 * wg + 32 * c, o);
+                tmem_ld32(o_oth + 64 * wg + 32 * c, t);
+                tmem_wait_ld();
+#pragma unroll
+                for (int x = 0; x < 32; ++x)
+                    res[32 * c + x] = ((a_s > 0.f ? o[x] * a_s : 0.f) + (a_o > 0.f ? t[x] * a_o : 0.f)) * inv;
+            }
+            tc_fence_before();
+            mbar_arrive(bar(XDONE));
+            if (more) {
+                // all QKs of this tile completed (XSUM), so Q may be replaced
+                const int tn = tiles[lt + 1].tile;
+                load_q(p, tn / p.ntiles, (tn % p.ntiles) * 128 + r, wg, qv);
+                tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bar(Q_FULL));
+            }
+            if (live) {
                 if (p.out_fp32) {
                     float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) +
-                                                             ((size_t)row * p.H + h) * D + col);
+                                                             ((size_t)row * p.H + h) * D + 64 * wg);
 #pragma unroll
-                    for (int x = 0; x < 8; ++x) dst[x] = make_float4(o[4 * x], o[4 * x + 1], o[4 * x + 2], o[4 * x + 3]);
+                    for (int x = 0; x < 16; ++x)
+                        dst[x] = make_float4(res[4 * x], res[4 * x + 1], res[4 * x + 2], res[4 * x + 3]);
                 } else {
                     uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.out) +
-                                                           ((size_t)row * p.H + h) * D + col);
+                                                           ((size_t)row * p.H + h) * D + 64 * wg);
 #pragma unroll
-                    for (int x = 0; x < 4; ++x)
-                        dst[x] = make_uint4(pack_bf16x2(o[8 * x], o[8 * x + 1]), pack_bf16x2(o[8 * x + 2], o[8 * x + 3]),
-                                            pack_bf16x2(o[8 * x + 4], o[8 * x + 5]),
-                                            pack_bf16x2(o[8 * x + 6], o[8 * x + 7]));
+                    for (int x = 0; x < 8; ++x)
+                        dst[x] = make_uint4(pack_bf16x2(res[8 * x], res[8 * x + 1]),
+                                            pack_bf16x2(res[8 * x + 2], res[8 * x + 3]),
+                                            pack_bf16x2(res[8 * x + 4], res[8 * x + 5]),
+                                            pack_bf16x2(res[8 * x + 6], res[8 * x + 7]));
+                }
+                if (p.lse && wg == 0)
+                    p.lse[(size_t)h * p.Lq + row] = L > 0.f ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
+            }
+            // the next tile's first PV overwrites O: both warpgroups must have read it
+            ok = warp_all_ok(mbar_wait(bar(XDONE), lt & 1, abort_flag));
+        }
+        tc_fence_before();
+        __syncthreads();
+        return;
+    }
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (warp == 0) {
+        // ---------------- TMA producer: K/V steps in MMA order ----------------
+        // Per tile: K of QK0(0), K of QK1(0), then for each i and w: K of QKw(i+1), V of PVw(i).
+        Ring ring;
+        int loaded = 0;
+        bool ok = true;
+        auto load = [&](const CUtensorMap *tm, int h, uint2 st) -> bool {
+            if (loaded >= NST && !warp_all_ok(mbar_wait(bar(EMPTY + ring.e), ring.ph ^ 1, abort_flag))) return false;
+            const uint32_t dst = sRing + ring.e * TILE_BYTES, fb = bar(FULL + ring.e);
+            const int t0 = e_start(st.x), t1 = e_start(st.y);
+            if (elect_one()) {
+                mbar_arrive_expect_tx(fb, TILE_BYTES);
+                tma_load_2d(dst, tm, h * D, t0, fb);
+                tma_load_2d(dst + REGION, tm, h * D + 64, t0, fb);
+                tma_load_2d(dst + REGION / 2, tm, h * D, t1, fb);
+                tma_load_2d(dst + REGION + REGION / 2, tm, h * D + 64, t1, fb);
+            }
+            __syncwarp();
+            ring.next();
+            ++loaded;
+            return true;
+        };
+        for (int lt = 0; lt < nt && ok; ++lt) {
+            const Tile tl = tiles[lt];
+            const int h = tl.tile / p.ntiles, m = tl.n / 2;
+            const uint2 *sp = steps + tl.first;
+            ok = load(&tm_k, h, sp[0]) && load(&tm_k, h, sp[1]);
+            for (int j = 0; j < m && ok; ++j) {
+#pragma unroll
+                for (int w = 0; w < 2; ++w) {
+                    if (ok && j + 1 < m) ok = load(&tm_k, h, sp[2 * j + 2 + w]);
+                    if (ok) ok = load(&tm_v, h, sp[2 * j + w]);
                 }
             }
         }
-        if (live && (fin || nsteps == 0) && grp == 0 && p.lse)
-            p.lse[(size_t)h * p.Lq + row] = lt > 0.f ? (m + __log2f(lt)) * 0.69314718055994530942f : -INFINITY;
+        if (!ok) {  // drain: loads still landing in shared memory
+            volatile int never = 0;
+            for (int s = 0; s < NST && s < loaded; ++s) {
+                ring.e = ring.e == 0 ? NST - 1 : ring.e - 1;
+                if (ring.e == NST - 1) ring.ph ^= 1;
+                mbar_wait(bar(FULL + ring.e), ring.ph, &never);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        // The same order as the producer. The loop is kept short: this warp shares its SM
+        // sub-partition with two softmax warps, and every instruction it spends between MMAs
+        // delays the tensor pipe.
+        const uint64_t dk0 = smem_desc_sw128(sRing, 16, 1024), dv0 = smem_desc_sw128(sRing, REGION, 1024);
+        Ring ring;
+        int qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0;    // QKs and PVs issued per warpgroup
+        bool ok = true;
+        auto qk = [&](int w) -> bool {             // S = Q K^T into the shared S buffer
+            const int prev = w ? qc0 : qc1;        // S is free once the previous QK's warpgroup read it
+            if (qc0 + qc1 > 0 && !warp_all_ok(mbar_wait(bar(S_FREE + (w ^ 1)), (prev - 1) & 1, abort_flag)))
+                return false;
+            if (!warp_all_ok(mbar_wait(bar(FULL + ring.e), ring.ph, abort_flag))) return false;
+            tc_fence_after();
+            const uint64_t db = dk0 + (uint32_t)ring.e * (TILE_BYTES >> 4);
+            if (elect_one()) {
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_bf16_ts(tmem + TMEM_S, tmem + TMEM_Q + 8 * kk, db + ((((kk >> 2) * REGION) + (kk & 3) * 32) >> 4),
+                                IDESC_QK, kk > 0 ? 1u : 0u);
+                tc_commit(bar(S_FULL + w));
+                tc_commit(bar(EMPTY + ring.e));
+            }
+            __syncwarp();
+            ring.next();
+            if (w) ++qc1; else ++qc0;
+            return true;
+        };
+        auto pv = [&](int w, bool first) -> bool {  // O_w (+)= P V
+            if (!warp_all_ok(mbar_wait(bar(P_FULL + w), (w ? pc1 : pc0) & 1, abort_flag))) return false;
+            if (!warp_all_ok(mbar_wait(bar(FULL + ring.e), ring.ph, abort_flag))) return false;
+            tc_fence_after();
+            const uint64_t db = dv0 + (uint32_t)ring.e * (TILE_BYTES >> 4);
+            if (elect_one()) {
+                // tokens 16kk.. of the step: P columns 8kk.. (bf16 pairs)
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_bf16_ts(tmem + TMEM_O + 128 * w, tmem + TMEM_P + 8 * kk, db + ((kk * 2048) >> 4), IDESC_PV,
+                                (first && kk == 0) ? 0u : 1u);
+                tc_commit(bar(EMPTY + ring.e));
+                tc_commit(bar(PV_DONE + w));
+            }
+            __syncwarp();
+            ring.next();
+            if (w) ++pc1; else ++pc0;
+            return true;
+        };
+        for (int lt = 0; lt < nt && ok; ++lt) {
+            const int m = tiles[lt].n / 2;
+            ok = warp_all_ok(mbar_wait(bar(Q_FULL), lt & 1, abort_flag));   // the tile's Q is in TMEM
+            ok = ok && qk(0) && qk(1);
+            for (int j = 0; j < m && ok; ++j) {
+                ok = (j + 1 == m || qk(0)) && pv(0, j == 0) && (j + 1 == m || qk(1)) && pv(1, j == 0);
+            }
+        }
+        // every MMA issued above has completed once DRAIN fires
+        if (elect_one()) tc_commit(bar(DRAIN));
+        __syncwarp();
+        volatile int never = 0;
+        mbar_wait(bar(DRAIN), 0, &never);
     }
     tc_fence_before();
     __syncthreads();
@@ -586,23 +678,39 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
 
 }  // namespace attn
 
+// Steps of one tile: at most `sb_tile` sub-blocks, padded to an even number (>= 2) of steps.
+static long attention_tile_steps(long sb_tile) { return std::max(2L, ((sb_tile + 3) & ~3L) / 2); }
+
+static long attention_smem_for(int kb, int block, int n_ids, int tmax) {
+    const int nwords = (kb + 31) / 32;
+    const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)kb) : 2L * std::min(n_ids, kb);
+    const long cap = tmax * attention_tile_steps(sb_tile);
+    // alignment slack, fixed tables, ring, bitmaps, steps (8 B each)
+    return 1024 + attn::OFF_RING + (long)attn::NST * attn::TILE_BYTES + 8L * tmax * nwords + 8L * cap;
+}
+
 int attention_smem_bytes(int Lk, int block, int n_ids, uint32_t *bytes) {
     const int kb = (Lk + block - 1) / block;
-    const int nwords = (kb + 31) / 32;
-    long max_sub = (block == 64) ? (long)std::min(2 * n_ids, kb) + 1 : 2L * std::min(n_ids, kb);
-    long total = 1024 + attn::OFF_DYN + 8L * nwords + 4L * (max_sub + 2);
+    const long total = attention_smem_for(kb, block, n_ids, 1);
     *bytes = (uint32_t)total;
     return total <= (long)attn::SMEM_LIMIT ? 0 : SS_ERR_SMEM;
 }
 
 static int g_attn_configured[64] = {0};
+static int g_num_sms[64] = {0};
+static std::mutex g_attn_mutex;
 
 int attention_prepare(int device) {
     if (device < 0 || device >= 64) return SS_ERR_SHAPE;
+    std::lock_guard<std::mutex> lock(g_attn_mutex);
     if (g_attn_configured[device]) return 0;
     cudaError_t e = cudaFuncSetAttribute(attn::sparse_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)attn::SMEM_LIMIT);
     if (e != cudaSuccess) return (int)e;
+    int nsm = 0;
+    e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return (int)e;
+    g_num_sms[device] = nsm;
     g_attn_configured[device] = 1;
     return 0;
 }
@@ -633,19 +741,14 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
          reinterpret_cast<uintptr_t>(out)) & 15u)
         return SS_ERR_POINTER;
     if (out_dtype != 0 && out_dtype != 1) return SS_ERR_SHAPE;
-    uint32_t smem;
-    int rc = attention_smem_bytes(Lk, block, n_ids, &smem);
+    uint32_t smem1;
+    int rc = attention_smem_bytes(Lk, block, n_ids, &smem1);
     if (rc) return rc;
     int device;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return (int)e;
     rc = attention_prepare(device);
     if (rc) return rc;
-
-    CUtensorMap tk, tv;
-    const uint64_t row_bytes = (uint64_t)H * attn::D * 2;
-    if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
-    if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
 
     attn::Params prm;
     prm.q = static_cast<const __nv_bfloat16 *>(q);
@@ -660,11 +763,33 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
     prm.n_ids = n_ids;
     prm.qb = (Lq + block - 1) / block;
     prm.kb = (Lk + block - 1) / block;
-    prm.ntiles = (block == 64) ? (prm.qb + 1) / 2 : prm.qb;
+    prm.ntiles = (Lq + 127) / 128;
     prm.nwords = (prm.kb + 31) / 32;
+    prm.T = prm.ntiles * H;
+    // one CTA per SM running ceil(T / G) tiles; fewer tiles per CTA (more CTAs) where the step
+    // lists need the room
+    const int nsm = g_num_sms[device] > 0 ? g_num_sms[device] : 148;
+    int G = std::max(std::min(prm.T, nsm), (prm.T + attn::MAXT - 1) / attn::MAXT);
+    while (attention_smem_for(prm.kb, block, n_ids, (prm.T + G - 1) / G) > (long)attn::SMEM_LIMIT &&
+           (prm.T + G - 1) / G > 1) {
+        const int tmax = (prm.T + G - 1) / G;
+        G = (prm.T + tmax - 2) / (tmax - 1);   // one tile fewer per CTA
+    }
+    prm.G = G;
+    prm.tmax = (prm.T + G - 1) / G;
+    const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)prm.kb) : 2L * std::min(n_ids, prm.kb);
+    prm.step_cap = (int)(prm.tmax * attention_tile_steps(sb_tile));
     prm.out_fp32 = out_dtype;
     prm.scale_log2 = scale * 1.4426950408889634f;
-    dim3 grid((unsigned)(prm.ntiles * H));
-    attn::sparse_attention_kernel<<<grid, attn::NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(tk, tv, prm);
+    const long smem = attention_smem_for(prm.kb, block, n_ids, prm.tmax);
+    if (smem > (long)attn::SMEM_LIMIT) return SS_ERR_SMEM;
+
+    CUtensorMap tk, tv;
+    const uint64_t row_bytes = (uint64_t)H * attn::D * 2;
+    if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
+    if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
+
+    attn::sparse_attention_kernel<<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem,
+                                    static_cast<cudaStream_t>(stream)>>>(tk, tv, prm);
     return (int)cudaGetLastError();
 }

@@ -42,12 +42,25 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                  ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// With SS_MBAR_SUSPEND_NS > 0, a thread whose phase has not completed is suspended in try_wait
+// until the phase completes or about that many nanoseconds pass. Off by default: on B200 the
+// attention kernel measured slower with a suspend hint (1 us to 500 us) than with plain polling.
+#ifndef SS_MBAR_SUSPEND_NS
+#define SS_MBAR_SUSPEND_NS 0
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
+#if SS_MBAR_SUSPEND_NS > 0
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity), "n"(SS_MBAR_SUSPEND_NS) : "memory");
+#else
     asm volatile("{\n\t.reg .pred p;\n\t"
                  "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                  "selp.u32 %0, 1, 0, p;\n\t}"
                  : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+#endif
     return ok != 0;
 }
 
@@ -79,6 +92,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+
+// Brings the box at {x, y} of a tensor map into L2 (no shared memory, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y)
+                 : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {

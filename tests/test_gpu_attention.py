@@ -152,3 +152,29 @@ def test_bad_block_id_is_reported():
     ids = torch.tensor([[[0, 5]]], dtype=torch.int32, device=DEV)   # kb = 2
     with pytest.raises(IndexError):
         ops.sparse_attention(q.to(DEV), k.to(DEV), v.to(DEV), ids, block=64, validate=True)
+
+
+@pytest.mark.parametrize("Lq,Lk,H,n", [
+    (6400, 2048, 4, 12),     # 200 tiles: CTAs of one and two tiles (split / pair jobs)
+    (25600, 4096, 4, 16),    # 800 tiles: CTAs of five and six tiles (pair, pair, split)
+])
+def test_attention_many_tiles_per_cta(oracle, Lq, Lk, H, n):
+    """The persistent grid's jobs (pairs with shared blocks, Q-slot reloads, splits merged by
+    log-sum-exp, tile ranges that cross heads) against the oracle on sampled query blocks."""
+    q, k, v = qkv(17, Lq, Lk, H)
+    rng = np.random.default_rng(17)
+    qb, kb = math.ceil(Lq / 64), math.ceil(Lk / 64)
+    ids = np.zeros((H, qb, n), np.int32)
+    forced = list(range(kb - 4, kb)) + [0]
+    for h in range(H):
+        for i in range(qb):
+            rest = rng.choice(np.arange(1, kb - 4), n - len(forced), replace=False)
+            ids[h, i] = np.sort(np.concatenate([forced, rest]))
+    out, lse = _attend(q, k, v, ids, 64)
+    qblocks = sorted(set([0, 1, 2, 3, qb // 2, qb // 2 + 1, qb - 2, qb - 1] + rng.choice(qb, 8).tolist()))
+    heads = list(range(H))
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids, 64, heads=heads, qblocks=qblocks)
+    assert_attention_close(out, ref)
+    m = np.isfinite(ref_lse)
+    np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
+    assert np.isfinite(out).all()
