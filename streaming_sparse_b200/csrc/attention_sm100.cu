@@ -23,8 +23,9 @@
 // Warp roles (384 threads; every role runs on a whole converged warp and issues its
 // single-thread instructions -- TMA, tcgen05.mma, tcgen05.commit -- from an elected lane)
 //   warp 0      list construction (prologue), then the TMA producer of the K/V ring
-//   warp 1      TMEM allocator + tcgen05.mma issuer
-//   warps 2-3   idle after the prologue
+//   warp 1      TMEM allocator + tcgen05.mma issuer for warpgroup 0's QKs and PVs
+//   warp 2      tcgen05.mma issuer for warpgroup 1
+//   warp 3      idle after the prologue
 //   warps 4-7   softmax warpgroup 0,   warps 8-11  softmax warpgroup 1
 //               After the prologue the control warpgroup (warps 0-3) gives registers up
 //               (setmaxnreg 56) and the softmax warpgroups take them (224): a softmax thread
@@ -32,7 +33,7 @@
 //               Thread r (r = 32*(warp%4) + lane) owns query row r of the tile (TMEM lane r).
 //               Per step: copy the 128 scores of its row from TMEM and release S, mask, row
 //               max, lazy rescale (only when the running max grows by more than 2^8),
-//               exponentiate (a quarter on the FMA pipe), write P (bf16) once the previous PV
+//               exponentiate (MUFU ex2), write P (bf16) once the previous PV
 //               has read the P buffer, release P.
 //
 // TMEM (512 columns): S [0,128) (one buffer, used by the warpgroups' QKs in turn); P [128,192)
@@ -40,9 +41,10 @@
 // softmax threads); O of warpgroup w at [256+128w, 384+128w).
 // MMAs: S = Q K^T (M=128, N=128, K=128; A = Q in TMEM, B = K entry, K-major, 128-byte swizzle),
 //       O_w += P V (M=128, N=128, K=128 tokens; A = P in TMEM, B = V entry, MN-major).
-// MMA order per tile: QK0(0), QK1(0), then for each i: QK0(i+1), PV0(i), QK1(i+1), PV1(i). A
-// warpgroup's next QK needs only the S buffer (P has its own), so it is issued ahead of its PV and
-// the next scores are ready when the warpgroup finishes its exponentials.
+// Each warpgroup's MMAs are issued by its own warp in the order QK(0), QK(1), PV(0), QK(2), PV(1),
+// ...: a warpgroup's next QK needs only the S buffer (P has its own), so it is issued ahead of its
+// PV and the next scores are ready when the warpgroup finishes its exponentials. The K/V ring is
+// filled in the interleaved order K0(0), K1(0), K0(1), V0(0), K1(1), V1(0), ...
 // Shared memory: barriers and tables, then a ring of NST K/V entries (128 tokens x 128 dims
 // bf16 each), the block bitmaps and the step lists.
 // Every mbarrier wait is bounded (common.cuh); on timeout the CTA drains its TMA loads and MMAs,
@@ -72,7 +74,6 @@ constexpr uint32_t OFF_RING = OFF_XCH + 2 * 2 * 128 * 4;  // 1024-aligned
 constexpr uint32_t SMEM_LIMIT = 232448;            // 227 KB opt-in maximum per CTA
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TMEM_S = 0, TMEM_P = 128, TMEM_Q = 192, TMEM_O = 256;
-constexpr int POLY_FROM = 48;                      // columns [48, 64) of each sub-block: FMA-pipe exp2
 static_assert(OFF_TILES + MAXT * 16 <= OFF_XCH, "table space");
 static_assert(OFF_RING % 1024 == 0, "ring alignment");
 
@@ -149,25 +150,6 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 __device__ __forceinline__ float f2_lo(uint64_t x) { return __uint_as_float((uint32_t)x); }
 __device__ __forceinline__ float f2_hi(uint64_t x) { return __uint_as_float((uint32_t)(x >> 32)); }
 
-// 2^x on the FMA pipe for a pair of arguments (x <= 8 here; x below -125 is clamped, giving
-// ~2^-125 instead of 0). x = n + f with n = round(x), f in [-0.5, 0.5]; 2^f by the minimax cubic
-// for relative error on [-0.5, 0.5] (coefficients fitted by the Remez exchange algorithm, max
-// relative error 7.5e-5, below bf16 rounding of P); 2^n is added to the exponent bits.
-// Offloading a share of the exponentials from the MUFU unit keeps it from bounding the softmax.
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &y0, float &y1) {
-    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer
-    const uint64_t x = f2_pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-    const uint64_t t = f2_add(x, f2_pack(kRound, kRound));
-    const uint64_t n = f2_add(t, f2_pack(-kRound, -kRound));
-    const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), x);
-    uint64_t p = f2_fma(f2_pack(0.0551716685f, 0.0551716685f), f, f2_pack(0.2426111251f, 0.2426111251f));
-    p = f2_fma(p, f, f2_pack(0.6932609677f, 0.6932609677f));
-    p = f2_fma(p, f, f2_pack(0.9999280572f, 0.9999280572f));
-    const int n0 = (int)(uint32_t)t - 0x4B400000, n1 = (int)(uint32_t)(t >> 32) - 0x4B400000;
-    y0 = __int_as_float(__float_as_int(f2_lo(p)) + (n0 << 23));
-    y1 = __int_as_float(__float_as_int(f2_hi(p)) + (n1 << 23));
-}
-
 // D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
@@ -230,6 +212,71 @@ __device__ __forceinline__ void load_q(const Params &p, int h, int row, int w, u
     }
 }
 
+// MMA issuer of warpgroup W. The ring order (shared with the producer) per tile of m steps per
+// warpgroup: K0(0), K1(0), then for j < m-1: K0(j+1), V0(j), K1(j+1), V1(j), then V0(m-1), V1(m-1)
+// (4m entries). Warpgroup W's operations sit at fixed positions of that order.
+template <int W>
+__device__ __forceinline__ bool mma_issuer(uint32_t tmem, uint32_t sRing, uint32_t bar0, const Tile *tiles, int nt,
+                                        volatile int *abort_flag) {
+    auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+    const uint64_t dk0 = smem_desc_sw128(sRing, 16, 1024), dv0 = smem_desc_sw128(sRing, REGION, 1024);
+    int qc = 0, pc = 0;     // QKs and PVs issued by this warpgroup
+    int base = 0;           // ring position of the tile's first entry
+    auto qk = [&](int pos) -> bool {         // S = Q K^T into the shared S buffer
+        // the QK before ours in the alternating QK order belongs to the other warpgroup:
+        // S is free once that warpgroup copied its scores out
+        if (W == 1 || qc > 0) {
+            const int other = W == 0 ? qc - 1 : qc;
+            if (!warp_all_ok(mbar_wait(bar(S_FREE + (W ^ 1)), other & 1, abort_flag))) return false;
+        }
+        const int e = pos % NST;
+        if (!warp_all_ok(mbar_wait(bar(FULL + e), (pos / NST) & 1, abort_flag))) return false;
+        tc_fence_after();
+        const uint64_t db = dk0 + (uint32_t)e * (TILE_BYTES >> 4);
+        if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                mma_bf16_ts(tmem + TMEM_S, tmem + TMEM_Q + 8 * kk, db + ((((kk >> 2) * REGION) + (kk & 3) * 32) >> 4),
+                            IDESC_QK, kk > 0 ? 1u : 0u);
+            tc_commit(bar(S_FULL + W));
+            tc_commit(bar(EMPTY + e));
+        }
+        __syncwarp();
+        ++qc;
+        return true;
+    };
+    auto pv = [&](int pos, bool first) -> bool {   // O_W (+)= P V
+        if (!warp_all_ok(mbar_wait(bar(P_FULL + W), pc & 1, abort_flag))) return false;
+        const int e = pos % NST;
+        if (!warp_all_ok(mbar_wait(bar(FULL + e), (pos / NST) & 1, abort_flag))) return false;
+        tc_fence_after();
+        const uint64_t db = dv0 + (uint32_t)e * (TILE_BYTES >> 4);
+        if (elect_one()) {
+            // tokens 16kk.. of the step: P columns 8kk.. (bf16 pairs)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                mma_bf16_ts(tmem + TMEM_O + 128 * W, tmem + TMEM_P + 8 * kk, db + ((kk * 2048) >> 4), IDESC_PV,
+                            (first && kk == 0) ? 0u : 1u);
+            tc_commit(bar(EMPTY + e));
+            tc_commit(bar(PV_DONE + W));
+        }
+        __syncwarp();
+        ++pc;
+        return true;
+    };
+    bool ok = true;
+    for (int lt = 0; lt < nt && ok; ++lt) {
+        const int m = tiles[lt].n / 2;
+        ok = warp_all_ok(mbar_wait(bar(Q_FULL), lt & 1, abort_flag));   // the tile's Q is in TMEM
+        ok = ok && qk(base + W);
+        for (int j = 0; j + 1 < m && ok; ++j)
+            ok = qk(base + 2 + 2 * W + 4 * j) && pv(base + 3 + 2 * W + 4 * j, j == 0);
+        ok = ok && pv(base + 4 * m - 2 + W, m == 1);
+        base += 4 * m;
+    }
+    return ok;
+}
+
 __global__ void __launch_bounds__(NTHREADS, 1)
 sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const Params p) {
@@ -264,7 +311,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         }
         mbar_init(bar(XSUM), 256);
         mbar_init(bar(XDONE), 256);
-        mbar_init(bar(DRAIN), 1);
+        mbar_init(bar(DRAIN), 2);
         for (int s = 0; s < NST; ++s) {
             mbar_init(bar(FULL + s), 1);
             mbar_init(bar(EMPTY + s), 1);
@@ -431,7 +478,10 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                         tmem_st32(o_addr + 32 * c, o);
                     }
                 }
-                // P = 2^(s*sl2 - m) as bf16 pairs
+                // P = 2^(s*sl2 - m) as bf16 pairs, all on MUFU ex2: measured on B200, moving a
+                // share of the exponentials to an FMA-pipe polynomial (a quarter or a half,
+                // grouped or interleaved) made the step slower, the extra instructions costing
+                // more issue slots than the MUFU time they saved.
                 const float base = (m == -INFINITY) ? 0.f : m;
                 const uint64_t nbx2 = f2_pack(-base, -base);
                 uint64_t sa = 0, sb = 0;
@@ -445,16 +495,8 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                             const int cc = 64 * g + c;
                             const uint64_t x0 = f2_fma(f2_pack(s[cc], s[cc + 1]), sl2x2, nbx2);
                             const uint64_t x1 = f2_fma(f2_pack(s[cc + 2], s[cc + 3]), sl2x2, nbx2);
-                            float p0, p1, p2, p3;
-                            if (c < POLY_FROM) {   // MUFU
-                                p0 = ex2(f2_lo(x0));
-                                p1 = ex2(f2_hi(x0));
-                                p2 = ex2(f2_lo(x1));
-                                p3 = ex2(f2_hi(x1));
-                            } else {               // FMA pipe
-                                exp2_poly2(f2_lo(x0), f2_hi(x0), p0, p1);
-                                exp2_poly2(f2_lo(x1), f2_hi(x1), p2, p3);
-                            }
+                            const float p0 = ex2(f2_lo(x0)), p1 = ex2(f2_hi(x0));
+                            const float p2 = ex2(f2_lo(x1)), p3 = ex2(f2_hi(x1));
                             sa = f2_add(sa, f2_pack(p0, p1));
                             sb = f2_add(sb, f2_pack(p2, p3));
                             pk[cc >> 1] = pack_bf16x2(p0, p1);
@@ -602,63 +644,16 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 mbar_wait(bar(FULL + ring.e), ring.ph, &never);
             }
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        // The same order as the producer. The loop is kept short: this warp shares its SM
-        // sub-partition with two softmax warps, and every instruction it spends between MMAs
-        // delays the tensor pipe.
-        const uint64_t dk0 = smem_desc_sw128(sRing, 16, 1024), dv0 = smem_desc_sw128(sRing, REGION, 1024);
-        Ring ring;
-        int qc0 = 0, qc1 = 0, pc0 = 0, pc1 = 0;    // QKs and PVs issued per warpgroup
-        bool ok = true;
-        auto qk = [&](int w) -> bool {             // S = Q K^T into the shared S buffer
-            const int prev = w ? qc0 : qc1;        // S is free once the previous QK's warpgroup read it
-            if (qc0 + qc1 > 0 && !warp_all_ok(mbar_wait(bar(S_FREE + (w ^ 1)), (prev - 1) & 1, abort_flag)))
-                return false;
-            if (!warp_all_ok(mbar_wait(bar(FULL + ring.e), ring.ph, abort_flag))) return false;
-            tc_fence_after();
-            const uint64_t db = dk0 + (uint32_t)ring.e * (TILE_BYTES >> 4);
-            if (elect_one()) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_bf16_ts(tmem + TMEM_S, tmem + TMEM_Q + 8 * kk, db + ((((kk >> 2) * REGION) + (kk & 3) * 32) >> 4),
-                                IDESC_QK, kk > 0 ? 1u : 0u);
-                tc_commit(bar(S_FULL + w));
-                tc_commit(bar(EMPTY + ring.e));
-            }
-            __syncwarp();
-            ring.next();
-            if (w) ++qc1; else ++qc0;
-            return true;
-        };
-        auto pv = [&](int w, bool first) -> bool {  // O_w (+)= P V
-            if (!warp_all_ok(mbar_wait(bar(P_FULL + w), (w ? pc1 : pc0) & 1, abort_flag))) return false;
-            if (!warp_all_ok(mbar_wait(bar(FULL + ring.e), ring.ph, abort_flag))) return false;
-            tc_fence_after();
-            const uint64_t db = dv0 + (uint32_t)ring.e * (TILE_BYTES >> 4);
-            if (elect_one()) {
-                // tokens 16kk.. of the step: P columns 8kk.. (bf16 pairs)
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_bf16_ts(tmem + TMEM_O + 128 * w, tmem + TMEM_P + 8 * kk, db + ((kk * 2048) >> 4), IDESC_PV,
-                                (first && kk == 0) ? 0u : 1u);
-                tc_commit(bar(EMPTY + ring.e));
-                tc_commit(bar(PV_DONE + w));
-            }
-            __syncwarp();
-            ring.next();
-            if (w) ++pc1; else ++pc0;
-            return true;
-        };
-        for (int lt = 0; lt < nt && ok; ++lt) {
-            const int m = tiles[lt].n / 2;
-            ok = warp_all_ok(mbar_wait(bar(Q_FULL), lt & 1, abort_flag));   // the tile's Q is in TMEM
-            ok = ok && qk(0) && qk(1);
-            for (int j = 0; j < m && ok; ++j) {
-                ok = (j + 1 == m || qk(0)) && pv(0, j == 0) && (j + 1 == m || qk(1)) && pv(1, j == 0);
-            }
-        }
-        // every MMA issued above has completed once DRAIN fires
+    } else if (warp == 1 || warp == 2) {
+        // ---------------- MMA issuers: warp 1 for warpgroup 0, warp 2 for warpgroup 1 ----------------
+        // tcgen05.mma blocks its issuing thread while the pipe holds an earlier MMA, so a single
+        // issuer leaves the pipe idle for every instruction it spends between two operations.
+        // With one issuer per warpgroup, one warp's waits overlap the other's MMAs. Everything
+        // ordering the two streams is an explicit barrier: S_FREE (the shared S buffer), P_FULL
+        // and PV_DONE (the shared P buffer, via the softmax), Q_FULL (the tile's queries).
+        if (warp == 1) mma_issuer<0>(tmem, sRing, bar0, tiles, nt, abort_flag);
+        else mma_issuer<1>(tmem, sRing, bar0, tiles, nt, abort_flag);
+        // every MMA this warp issued has completed once DRAIN fires (two arrivals: both issuers)
         if (elect_one()) tc_commit(bar(DRAIN));
         __syncwarp();
         volatile int never = 0;
