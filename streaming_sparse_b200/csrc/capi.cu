@@ -25,9 +25,8 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D bf16 tensor map over a row-major [outer][inner] view, 128-byte swizzle, zero fill outside.
-int encode_tmap_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
-                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+static int encode_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                          uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return SS_ERR_DRIVER;
     cuuint64_t dims[2] = {inner, outer};
@@ -35,9 +34,21 @@ int encode_tmap_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : SS_ERR_DRIVER;
+}
+
+// 2-D bf16 tensor map over a row-major [outer][inner] view, 128-byte swizzle, zero fill outside.
+int encode_tmap_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+    return encode_2d_bf16(map, base, inner, outer, row_stride_bytes, box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// The same without swizzle: a box lands in shared memory as plain rows of box_inner elements.
+int encode_tmap_2d_bf16_rows(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                             uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+    return encode_2d_bf16(map, base, inner, outer, row_stride_bytes, box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace ss

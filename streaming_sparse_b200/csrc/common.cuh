@@ -221,4 +221,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 namespace ss {
 int encode_tmap_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+int encode_tmap_2d_bf16_rows(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                             uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 }

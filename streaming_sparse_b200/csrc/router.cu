@@ -1,23 +1,24 @@
 // router.cu -- learned KV-block router for sm_100a in exact fp32.
 //
-//   1. pool_project: one CTA per (head, group of 16 blocks). The head's [128 x R] projection is
-//      fetched into shared memory with one bulk copy; each thread sums 8 dimensions of one block
-//      over the block's valid tokens (fp32 adds in token order, one correctly rounded divide),
-//      then the block means are projected with fmaf in ascending row order. Query projections
-//      are stored [H][qb][R]; key projections transposed [H][R][kb] for the score stage.
+//   1. pool_project: one CTA per SM, each pooling a tile of blocks of one head (query or key).
+//      The head's [128 x R] projection is transposed into shared memory; the blocks' tokens
+//      arrive by TMA, one block per 64-thread group at a time; each thread sums 2 dimensions over
+//      the block's valid tokens (fp32 adds in token order, one correctly rounded divide), then
+//      the block means are projected with fmaf in ascending row order. Query projections are
+//      stored [H][qb][R]; key projections transposed [H][R][kb] for the score stage.
 //      Reference: block pooling of migration/unified_router/opt19/prototype.py:11-49 (one
 //      prototype = plain mean of the valid tokens) and the projection of opt8/projection.py:4-14.
-//   2. score_select: one warp per (head, query block), eight query blocks per CTA sharing the
-//      head's transposed key projections, staged into shared memory 256 key blocks at a time by
-//      bulk copies. Scores S[j] = <qh, kh_j> (fmaf in ascending order, -0 -> +0, non-finite
-//      flagged); the order-preserving uint32 of each unforced score is kept in shared memory.
-//      The `extra`-th largest score T is found exactly by a 32-step bisection with warp-wide
-//      counts; blocks above T are kept and ties at T go to the lowest block indices (ordered
-//      ballot scan). Forced blocks (sink, current chunk) are always kept; ids are written
-//      ascending. Reference: the block-score GEMM `_coarse` (opt16/route.py:34-47), `_chosen`/
-//      `_top` (opt16/route.py:13-24,49-55), fixed_page_select (local_experiments/
-//      video_runtime_v1/fixed_page_select.py:7-21) and the forced set of local_experiments/
-//      video_runtime_v1/pipeline_graph.py:140-151.
+//   2. score_select: eight query blocks per CTA. Every thread scores its key blocks against the
+//      eight query blocks, reading the head's transposed key projections straight from L2 (each
+//      value used eight times); scores S[j] = <qh, kh_j> accumulate with fmaf in ascending order,
+//      -0 -> +0, non-finite flagged; the order-preserving uint32 of each unforced score is kept
+//      in shared memory. Then one warp per query block finds the `extra`-th largest score T
+//      exactly by a 32-step bisection with warp-wide counts (keys in registers); blocks above T
+//      are kept and ties at T go to the lowest block indices (ordered ballot scan). Forced blocks
+//      (sink, current chunk) are always kept; ids are written ascending. Reference: the
+//      block-score GEMM `_coarse` (opt16/route.py:34-47), `_chosen`/`_top` (opt16/route.py:13-24,
+//      49-55), fixed_page_select (local_experiments/video_runtime_v1/fixed_page_select.py:7-21)
+//      and the forced set of local_experiments/video_runtime_v1/pipeline_graph.py:140-151.
 // The fixed summation order makes every score bit-identical to the CPU oracle. The score GEMM is
 // tens of MFMA per chunk-layer, so CUDA-core FFMA keeps it exact at a cost of microseconds.
 #include <algorithm>
@@ -31,10 +32,9 @@ namespace router {
 constexpr int D = 128;
 constexpr int MAX_R = 128;
 constexpr int MAX_KB = 8192;
-constexpr int BG = 16;               // blocks per pool_project CTA
-constexpr int PP_THREADS = BG * 16;  // thread = (block, 8 dims)
-constexpr int ROWS = 8;              // query blocks (warps) per score_select CTA
-constexpr int TJ = 256;              // key blocks per staged tile
+constexpr int PP_MAX_GROUPS = 12;    // 64-thread groups per pool_project CTA (one TMA stage each)
+constexpr int WT_STRIDE = 132;       // padded row of the transposed projection in shared memory
+constexpr int ROWS = 8;              // query blocks per score_select CTA (one warp each in the selection)
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -44,106 +44,115 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
-// grid (tiles_q + tiles_k, H), BG*16 threads. Tiles [0, tiles_q) pool query blocks, the rest key
-// blocks. Dynamic shared memory: W [128][R], means [BG][128], mbarrier.
-__global__ void __launch_bounds__(PP_THREADS) pool_project_kernel(const uint16_t *__restrict__ q,
-                                                                  const uint16_t *__restrict__ k, int H, int Lq,
-                                                                  int Lk, int block, int R, int tiles_q,
-                                                                  const float *__restrict__ wq,
-                                                                  const float *__restrict__ wk,
-                                                                  float *__restrict__ qh, float *__restrict__ khT,
-                                                                  int kbp, int *status) {
-    extern __shared__ __align__(16) uint8_t smr[];
-    float *sw = reinterpret_cast<float *>(smr);                 // [128][R]
-    float *smean = sw + D * R;                                   // [BG][128]
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(smean + BG * D);
-    const int h = blockIdx.y, tid = threadIdx.x;
+// grid (tiles_q + tiles_k, H), 64 * ng threads = ng groups of 64 (one CTA per SM). Tiles
+// [0, tiles_q) pool query blocks, the rest key blocks, bg blocks per tile. Group g pools blocks
+// g, g + ng, ... of the tile: the group's leader TMA-loads a block (block tokens x 128 dims of
+// head h, plain rows) into the group's stage, the 64 threads sum 2 dimensions each in token
+// order, the leader starts the next block's load, and the group projects the block mean (thread
+// e: outputs e, e + 64) against W transposed in shared memory (rows padded to WT_STRIDE floats, so
+// the float4 reads of 32 threads hit every bank the same number of times). ng stages of 16 KB keep
+// about 190 KB in flight per SM. Dynamic shared memory: stages [ng][block][128] bf16,
+// W^T [R][WT_STRIDE] fp32, means [ng][128] fp32, mbarriers, abort flag.
+__global__ void __launch_bounds__(PP_MAX_GROUPS * 64, 1)
+pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
+                    int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
+                    const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ khT, int kbp,
+                    int *status) {
+    extern __shared__ uint8_t smr_raw[];
+    uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
+    const int ng = blockDim.x / 64;
+    const uint32_t stage_bytes = (uint32_t)block * D * 2;
+    float *swt = reinterpret_cast<float *>(smr + ng * stage_bytes);   // [R][WT_STRIDE]
+    float *smean = swt + R * WT_STRIDE;                                // [ng][128]
+    uint64_t *mb = reinterpret_cast<uint64_t *>(smean + ng * D);      // full[ng]
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(mb + ng);
+    const int h = blockIdx.y, tid = threadIdx.x, g = tid >> 6, gt = tid & 63;
     const bool isq = (int)blockIdx.x < tiles_q;
     const int tile = isq ? blockIdx.x : blockIdx.x - tiles_q;
     const int L = isq ? Lq : Lk;
     const int nb = (L + block - 1) / block;
-    const int b0 = tile * BG, nblk = min(BG, nb - b0);
-    const uint32_t bar = smem_u32(mbar);
+    const int b0 = tile * bg, nblk = min(bg, nb - b0);
+    const uint32_t full = smem_u32(mb + g);
+    const uint32_t stage = smem_u32(smr) + g * stage_bytes;
+    const CUtensorMap *tm = isq ? &tm_q : &tm_k;
     if (tid == 0) {
-        mbar_init(bar, 1);
+        *abort_flag = 0;
+        for (int i = 0; i < ng; ++i) mbar_init(smem_u32(mb + i), 1);
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        mbar_arrive_expect_tx(bar, (uint32_t)(D * R * 4));
-        bulk_g2s(smem_u32(sw), (isq ? wq : wk) + (size_t)h * D * R, (uint32_t)(D * R * 4), bar);
+    if (gt == 0 && g < nblk) {
+        mbar_arrive_expect_tx(full, stage_bytes);
+        tma_load_2d(stage, tm, h * D, (b0 + g) * block, full);
     }
-    // pooling: thread (bi, c) sums dims [8c, 8c+8) of block b0+bi in token order
-    const int bi = tid >> 4, c = tid & 15;
-    if (bi < nblk) {
-        const int t0 = (b0 + bi) * block;
-        const int n = min(block, L - t0);
-        const uint16_t *x = isq ? q : k;
-        const size_t row_vec = (size_t)H * D / 8;
-        const uint4 *src = reinterpret_cast<const uint4 *>(x + ((size_t)t0 * H + h) * D) + c;
-        float s[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) s[i] = 0.f;
-        int t = 0;
-        for (; t + 8 <= n; t += 8) {
-            uint4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (size_t)(t + u) * row_vec);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                s[0] = __fadd_rn(s[0], bf16_lo(v[u].x));
-                s[1] = __fadd_rn(s[1], bf16_hi(v[u].x));
-                s[2] = __fadd_rn(s[2], bf16_lo(v[u].y));
-                s[3] = __fadd_rn(s[3], bf16_hi(v[u].y));
-                s[4] = __fadd_rn(s[4], bf16_lo(v[u].z));
-                s[5] = __fadd_rn(s[5], bf16_hi(v[u].z));
-                s[6] = __fadd_rn(s[6], bf16_lo(v[u].w));
-                s[7] = __fadd_rn(s[7], bf16_hi(v[u].w));
+    {   // W [128][R] of head h, transposed into shared memory while the first loads are in flight
+        const float *w = (isq ? wq : wk) + (size_t)h * D * R;
+        for (int x = tid; x < D * R; x += blockDim.x) swt[(x % R) * WT_STRIDE + x / R] = __ldg(w + x);
+    }
+    __syncthreads();
+    // Every thread of a group runs every group barrier (bar.sync is not bounded): after a failed
+    // wait the work is skipped but the barriers are kept, and the shared abort flag makes the
+    // remaining waits of the CTA return at once.
+    bool ok = true;
+    int issued = g < nblk ? 1 : 0, seen = 0;   // the leader's loads into the stage, and those waited on
+    for (int it = 0; g + ng * it < nblk; ++it) {
+        const int bi = g + ng * it;
+        if (ok) {
+            ok = mbar_wait(full, it & 1, abort_flag);
+            seen = it + 1;
+        }
+        const int t0 = (b0 + bi) * block, n = min(block, L - t0);
+        float s0 = 0.f, s1 = 0.f;
+        if (ok) {
+            // thread gt sums dimensions 2gt, 2gt+1 over the block's valid tokens, in token order
+            const uint32_t *rows = reinterpret_cast<const uint32_t *>(smr + g * stage_bytes) + gt;
+#pragma unroll 8
+            for (int t = 0; t < n; ++t) {
+                const uint32_t w = rows[t * (D / 2)];
+                s0 = __fadd_rn(s0, bf16_lo(w));
+                s1 = __fadd_rn(s1, bf16_hi(w));
             }
         }
-        for (; t < n; ++t) {
-            const uint4 v = __ldg(src + (size_t)t * row_vec);
-            s[0] = __fadd_rn(s[0], bf16_lo(v.x));
-            s[1] = __fadd_rn(s[1], bf16_hi(v.x));
-            s[2] = __fadd_rn(s[2], bf16_lo(v.y));
-            s[3] = __fadd_rn(s[3], bf16_hi(v.y));
-            s[4] = __fadd_rn(s[4], bf16_lo(v.z));
-            s[5] = __fadd_rn(s[5], bf16_hi(v.z));
-            s[6] = __fadd_rn(s[6], bf16_lo(v.w));
-            s[7] = __fadd_rn(s[7], bf16_hi(v.w));
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");   // the stage has been read
+        if (ok && gt == 0 && bi + ng < nblk) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(full, stage_bytes);
+            tma_load_2d(stage, tm, h * D, (b0 + bi + ng) * block, full);
+            ++issued;
         }
         const float fn = (float)n;
+        smean[g * D + 2 * gt] = __fdiv_rn(s0, fn);
+        smean[g * D + 2 * gt + 1] = __fdiv_rn(s1, fn);
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");
+        if (ok) {
+            // projection: outputs gt and gt + 64, fmaf over the 128 rows in ascending order
+            const int b = b0 + bi;
+            const float4 *m4 = reinterpret_cast<const float4 *>(smean + g * D);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) smean[bi * D + 8 * c + i] = __fdiv_rn(s[i], fn);
-    }
-    // wait for W (bounded), then project: thread (bi, e-group) owns R/16 consecutive outputs
-    volatile int no_abort = 0;
-    const bool have_w = mbar_wait(bar, 0, &no_abort);
-    __syncthreads();
-    if (!have_w) {
-        if (tid == 0) report(status, SS_DEV_TIMEOUT);
-        return;
-    }
-    const int per = R / 16;  // 4 for R = 64 (R is a multiple of 16, at most 128)
-    if (bi < nblk) {
-        float acc[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u] = 0.f;
-        const int e0 = c * per;
-#pragma unroll 4
-        for (int d = 0; d < D; ++d) {
-            const float xm = smean[bi * D + d];
-            const float *wr = sw + d * R + e0;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (u < per) acc[u] = __fmaf_rn(xm, wr[u], acc[u]);
+            for (int e = gt; e < MAX_R; e += 64) {
+                if (e >= R) break;
+                const float4 *w4 = reinterpret_cast<const float4 *>(swt + e * WT_STRIDE);
+                float acc = 0.f;
+#pragma unroll 8
+                for (int d4 = 0; d4 < D / 4; ++d4) {
+                    const float4 mv = m4[d4], wv = w4[d4];
+                    acc = __fmaf_rn(mv.x, wv.x, acc);
+                    acc = __fmaf_rn(mv.y, wv.y, acc);
+                    acc = __fmaf_rn(mv.z, wv.z, acc);
+                    acc = __fmaf_rn(mv.w, wv.w, acc);
+                }
+                if (isq) qh[((size_t)h * nb + b) * R + e] = acc;
+                else khT[((size_t)h * R + e) * kbp + b] = acc;
+            }
         }
-        const int b = b0 + bi;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            if (u >= per) break;
-            if (isq) qh[((size_t)h * nb + b) * R + e0 + u] = acc[u];
-            else khT[((size_t)h * R + e0 + u) * kbp + b] = acc[u];
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");   // smean is rewritten next block
+    }
+    if (*abort_flag) {
+        // a copy may still be landing: the leader's last load
+        volatile int never = 0;
+        if (gt == 0) {
+            for (int j = seen; j < issued; ++j) mbar_wait(full, j & 1, &never);
+            if (g == 0) report(status, SS_DEV_TIMEOUT);
         }
     }
 }
@@ -158,94 +167,110 @@ __device__ __forceinline__ uint32_t ordered_bits(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// grid (ceil(qb / ROWS), H), ROWS warps. khT rows have stride kbp (kb rounded up to a multiple of
-// 4). Dynamic shared memory: khT tile [R][TJ], qh rows [ROWS][R], keys [ROWS][kbp] (ordered score
-// bits; 0 = not a candidate, which no finite score maps to), mbarrier.
-__global__ void __launch_bounds__(ROWS * 32) score_select_kernel(const float *__restrict__ qh,
-                                                                 const float *__restrict__ khT, int qb, int kb,
-                                                                 int kbp, int R,
-                                                                 int block, int Lq, int Lk, int sink, int extra,
-                                                                 int32_t *__restrict__ ids, int n_ids,
-                                                                 uint8_t *__restrict__ mask,
-                                                                 float *__restrict__ scores, int *status) {
-    extern __shared__ __align__(16) uint8_t smr[];
-    float *sk = reinterpret_cast<float *>(smr);               // [R][TJ]
-    float *sq = sk + R * TJ;                                   // [ROWS][R]
-    uint32_t *keys = reinterpret_cast<uint32_t *>(sq + ROWS * R);  // [ROWS][kb]
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(keys + (size_t)ROWS * kbp);
-    const int h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x * ROWS + warp;
-    const bool row_ok = i < qb;
-    const uint32_t bar = smem_u32(mbar);
-    if (threadIdx.x == 0) {
-        mbar_init(bar, 1);
-        fence_mbar_init();
+// Threshold of one query block's selection: T = the extra-th largest candidate key (bisection on
+// the order-preserving bits) and `need` = how many keys equal to T are kept, run by one warp. NK
+// keys per lane are held in registers (NK = 0: read from shared memory at every step).
+template <int NK>
+__device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t &T,
+                                                 int &need) {
+    uint32_t kr[NK > 0 ? NK : 1];
+#pragma unroll
+    for (int u = 0; u < NK; ++u) {
+        const int j = lane + 32 * u;
+        kr[u] = j < kb ? mykeys[j] : 0u;
     }
-    for (int x = threadIdx.x; x < ROWS * R; x += blockDim.x) {
-        const int ii = blockIdx.x * ROWS + x / R;
-        sq[x] = ii < qb ? qh[((size_t)h * qb + ii) * R + x % R] : 0.f;
+    auto count = [&](uint32_t c, bool strict) -> int {
+        int n = 0;
+        if (NK > 0) {
+#pragma unroll
+            for (int u = 0; u < NK; ++u) n += strict ? (kr[u] > c) : (kr[u] >= c);
+        } else {
+            for (int j = lane; j < kb; j += 32) n += strict ? (mykeys[j] > c) : (mykeys[j] >= c);
+        }
+        return (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
+    };
+    T = 0u;
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = T | (1u << bit);
+        if (count(cand, false) >= extra) T = cand;
+    }
+    need = extra - count(T, true);   // ties at T to keep, >= 1
+}
+
+// grid (ceil(qb / ROWS), H), 256 threads, ROWS = 8 query blocks per CTA.
+// Phase 1: thread t scores key blocks t, t + 256, ... against the CTA's 8 query blocks: the R
+// projections of a key block come from khT (row e of all threads' key blocks is one coalesced
+// read, 32 rows in flight per thread), each reused for the 8 query blocks, whose projections are
+// read from shared memory ([R][8], two broadcast float4 per row). Scores accumulate with fmaf in
+// ascending e, -0 becomes +0, non-finite scores are flagged; the order-preserving uint32 of each
+// unforced score goes to shared memory (0 = not a candidate, which no finite score maps to).
+// Phase 2: warp w selects for query block w: the `extra`-th largest key T (keys in registers for
+// kb <= 1024), blocks above T kept, ties at T to the lowest block indices (ordered ballot scan),
+// forced blocks always kept, ids written ascending.
+__global__ void __launch_bounds__(256) score_select_kernel(const float *__restrict__ qh, const float *__restrict__ khT,
+                                                           int qb, int kb, int kbp, int R, int block, int Lq, int Lk,
+                                                           int sink, int extra, int32_t *__restrict__ ids, int n_ids,
+                                                           uint8_t *__restrict__ mask, float *__restrict__ scores,
+                                                           int *status) {
+    extern __shared__ __align__(16) uint8_t smr[];
+    float *sqT = reinterpret_cast<float *>(smr);                       // [R][ROWS]
+    uint32_t *keys = reinterpret_cast<uint32_t *>(sqT + R * ROWS);     // [ROWS][kbp]
+    const int h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int i0 = blockIdx.x * ROWS;
+    for (int x = tid; x < ROWS * R; x += blockDim.x) {
+        const int ii = x / R, e = x % R;
+        sqT[e * ROWS + ii] = i0 + ii < qb ? qh[((size_t)h * qb + i0 + ii) * R + e] : 0.f;
     }
     __syncthreads();
-    const float *myq = sq + warp * R;
-    uint32_t *mykeys = keys + (size_t)warp * kbp;
-    bool bad = false, ok = true;
-    volatile int no_abort = 0;
-    for (int t = 0, j0 = 0; j0 < kb; ++t, j0 += TJ) {
-        const int nj = min(TJ, kb - j0);
-        if (threadIdx.x == 0) {
-            // rows e of the tile: khT[h][e][j0 .. j0+nj), 16-byte multiples (the host pads kb)
-            const uint32_t rb = (uint32_t)(((nj * 4) + 15) & ~15);
-            mbar_arrive_expect_tx(bar, rb * (uint32_t)R);
-            for (int e = 0; e < R; ++e)
-                bulk_g2s(smem_u32(sk + e * TJ), khT + ((size_t)h * R + e) * kbp + j0, rb, bar);
-        }
-        ok = mbar_wait(bar, t & 1, &no_abort);
-        if (!ok) break;
-        if (row_ok) {
-            float acc[TJ / 32];
+    static_assert(ROWS == 8, "two float4 of query projections per row");
+    const float4 *q4 = reinterpret_cast<const float4 *>(sqT);
+    const float *kc = khT + (size_t)h * R * kbp;
+    bool bad = false;
+    for (int j = tid; j < kb; j += blockDim.x) {
+        float acc[ROWS];
 #pragma unroll
-            for (int u = 0; u < TJ / 32; ++u) acc[u] = 0.f;
-#pragma unroll 2
-            for (int e = 0; e < R; ++e) {
-                const float qe = myq[e];
-                const float *kr = sk + e * TJ + lane;
+        for (int r = 0; r < ROWS; ++r) acc[r] = 0.f;
+        for (int e0 = 0; e0 < R; e0 += 32) {   // R is a multiple of 16
+            float kv[32];
 #pragma unroll
-                for (int u = 0; u < TJ / 32; ++u) acc[u] = __fmaf_rn(qe, kr[32 * u], acc[u]);
-            }
+            for (int u = 0; u < 32; ++u) kv[u] = e0 + u < R ? __ldg(kc + (size_t)(e0 + u) * kbp + j) : 0.f;
 #pragma unroll
-            for (int u = 0; u < TJ / 32; ++u) {
-                const int j = j0 + lane + 32 * u;
-                if (j >= kb) continue;
-                float a = acc[u];
-                if (a == 0.f) a = 0.f;  // -0 -> +0
-                bad |= !isfinite(a);
-                if (scores) scores[((size_t)h * qb + i) * kb + j] = a;
-                mykeys[j] = is_forced(j, block, Lq, Lk, sink) ? 0u : ordered_bits(a);
+            for (int u = 0; u < 32; ++u) {
+                if (e0 + u >= R) break;
+                const float4 qa = q4[2 * (e0 + u)], qb4 = q4[2 * (e0 + u) + 1];
+                acc[0] = __fmaf_rn(qa.x, kv[u], acc[0]);
+                acc[1] = __fmaf_rn(qa.y, kv[u], acc[1]);
+                acc[2] = __fmaf_rn(qa.z, kv[u], acc[2]);
+                acc[3] = __fmaf_rn(qa.w, kv[u], acc[3]);
+                acc[4] = __fmaf_rn(qb4.x, kv[u], acc[4]);
+                acc[5] = __fmaf_rn(qb4.y, kv[u], acc[5]);
+                acc[6] = __fmaf_rn(qb4.z, kv[u], acc[6]);
+                acc[7] = __fmaf_rn(qb4.w, kv[u], acc[7]);
             }
         }
-        __syncthreads();  // the tile buffer is refilled next iteration
+        const bool forced = is_forced(j, block, Lq, Lk, sink);
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+            if (i0 + r >= qb) break;
+            float a = acc[r];
+            if (a == 0.f) a = 0.f;  // -0 -> +0
+            bad |= !isfinite(a);
+            if (scores) scores[((size_t)h * qb + i0 + r) * kb + j] = a;
+            keys[(size_t)r * kbp + j] = forced ? 0u : ordered_bits(a);
+        }
     }
     if (bad) report(status, SS_DEV_NONFINITE);
-    if (!ok) {
-        if (threadIdx.x == 0) report(status, SS_DEV_TIMEOUT);
-        return;
-    }
-    if (!row_ok) return;
-    __syncwarp();
-    // T = the extra-th largest candidate score (bisection on the order-preserving bits)
+    __syncthreads();
+    const int i = i0 + warp;
+    if (warp >= ROWS || i >= qb) return;
+    const uint32_t *mykeys = keys + (size_t)warp * kbp;
     uint32_t T = 0xffffffffu;
     int need = 0;
     if (extra > 0) {
-        T = 0u;
-        for (int bit = 31; bit >= 0; --bit) {
-            const uint32_t cand = T | (1u << bit);
-            int cnt = 0;
-            for (int j = lane; j < kb; j += 32) cnt += mykeys[j] >= cand;
-            if ((int)__reduce_add_sync(0xffffffffu, (unsigned)cnt) >= extra) T = cand;
-        }
-        int gt = 0;
-        for (int j = lane; j < kb; j += 32) gt += mykeys[j] > T;
-        need = extra - (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);  // ties at T to keep, >= 1
+        if (kb <= 256) select_threshold<8>(mykeys, kb, extra, lane, T, need);
+        else if (kb <= 512) select_threshold<16>(mykeys, kb, extra, lane, T, need);
+        else if (kb <= 1024) select_threshold<32>(mykeys, kb, extra, lane, T, need);
+        else select_threshold<0>(mykeys, kb, extra, lane, T, need);
     }
     // ascending compaction of forced | above T | the first `need` ties at T
     int32_t *out = ids + ((size_t)h * qb + i) * n_ids;
@@ -268,10 +293,22 @@ __global__ void __launch_bounds__(ROWS * 32) score_select_kernel(const float *__
 
 }  // namespace router
 
-static size_t pp_smem(int R) { return (size_t)router::D * R * 4 + (size_t)router::BG * router::D * 4 + 16; }
+// pool_project: groups per CTA (one 16 KB / 32 KB stage each) that fit beside W^T and the means
+static int pp_groups(int R, int block) {
+    const size_t fixed = 1024 + (size_t)R * router::WT_STRIDE * 4 + 64;
+    const size_t per = (size_t)block * router::D * 2 + router::D * 4 + 8;
+    const size_t budget = 227 * 1024;
+    int ng = budget > fixed ? (int)((budget - fixed) / per) : 0;
+    return std::min(ng, router::PP_MAX_GROUPS);
+}
+
+static size_t pp_smem(int R, int block, int ng) {
+    return 1024 + (size_t)ng * block * router::D * 2 + (size_t)R * router::WT_STRIDE * 4 + (size_t)ng * router::D * 4 +
+           8 * (size_t)ng + 16;
+}
 
 static size_t select_smem(int kb, int R) {
-    return (size_t)R * router::TJ * 4 + (size_t)router::ROWS * R * 4 + (size_t)router::ROWS * kb * 4 + 16;
+    return (size_t)R * router::ROWS * 4 + (size_t)router::ROWS * kb * 4 + 16;
 }
 
 static int g_router_configured[64] = {0};
@@ -350,10 +387,22 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     if (rc) return rc;
     const RouterLayout L = router_layout(H, Lq, Lk, R, block);
     float *qh = reinterpret_cast<float *>(ws + L.qh), *khT = reinterpret_cast<float *>(ws + L.khT);
-    const int tq = (qb + router::BG - 1) / router::BG, tk = (kb + router::BG - 1) / router::BG;
-    router::pool_project_kernel<<<dim3(tq + tk, H), router::PP_THREADS, pp_smem(R), st>>>(
-        (const uint16_t *)q, (const uint16_t *)k, H, Lq, Lk, block, R, tq, wq, wk, qh, khT, kbp, status);
-    router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::ROWS * 32,
+    // blocks per pool_project tile: the fewest that keep the grid within one wave
+    int nsm = 148;
+    if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) nsm = 148;
+    int bg = std::max(1, (H * (qb + kb) + nsm - 1) / nsm);
+    while (H * ((qb + bg - 1) / bg + (kb + bg - 1) / bg) > nsm && bg < std::max(qb, kb)) ++bg;
+    const int tq = (qb + bg - 1) / bg, tk = (kb + bg - 1) / bg;
+    const int ng = pp_groups(R, block);
+    CUtensorMap tmq, tmk;
+    const uint64_t row_bytes = (uint64_t)H * router::D * 2;
+    if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D, (uint32_t)block))
+        return SS_ERR_DRIVER;
+    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)Lk, row_bytes, router::D, (uint32_t)block))
+        return SS_ERR_DRIVER;
+    router::pool_project_kernel<<<dim3(tq + tk, H), 64 * ng, pp_smem(R, block, ng), st>>>(
+        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, khT, kbp, status);
+    router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), 256,
                                   select_smem(kbp, R), st>>>(qh, khT, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
                                                              extra, ids, n_ids, mask, scores, status);
     return (int)cudaGetLastError();
