@@ -107,8 +107,7 @@ int ss_router(const void *q, const void *k, const float *wq, const float *wk,
  *     any stream on that device.
  *   - All calls on a device share the array: calls that overlap on the GPU (different streams
  *     or host threads) race, so the caller serialises them. Nothing in the array needs to start
- *     at zero: each call writes every value that affects its results (the few padding entries
- *     it copies along with them are never used).
+ *     at zero: each call writes every value it reads.
  * Other arguments, results and status codes are those of ss_router. */
 int ss_router_noalloc(const void *q, const void *k, const float *wq, const float *wk,
                       int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,

@@ -5,12 +5,12 @@
 //      arrive by TMA, one block per 64-thread group at a time; each thread sums 2 dimensions over
 //      the block's valid tokens (fp32 adds in token order, one correctly rounded divide), then
 //      the block means are projected with fmaf in ascending row order. Query projections are
-//      stored [H][qb][R]; key projections transposed [H][R][kb] for the score stage.
+//      stored [H][qb][R], key projections [H][kbp][R] (kbp = kb rounded up to 4).
 //      Reference: block pooling of migration/unified_router/opt19/prototype.py:11-49 (one
 //      prototype = plain mean of the valid tokens) and the projection of opt8/projection.py:4-14.
 //   2. score_select: eight query blocks per CTA. Every thread scores its key blocks against the
-//      eight query blocks, reading the head's transposed key projections straight from L2 (each
-//      value used eight times); scores S[j] = <qh, kh_j> accumulate with fmaf in ascending order,
+//      eight query blocks, reading its key blocks' projections straight from L2 (each value used
+//      eight times); scores S[j] = <qh, kh_j> accumulate with fmaf in ascending order,
 //      -0 -> +0, non-finite flagged; the order-preserving uint32 of each unforced score is kept
 //      in shared memory. Then one warp per query block finds the `extra`-th largest score T
 //      exactly by a 32-step bisection with warp-wide counts (keys in registers); blocks above T
@@ -35,6 +35,7 @@ constexpr int MAX_KB = 8192;
 constexpr int PP_MAX_GROUPS = 12;    // 64-thread groups per pool_project CTA (one TMA stage each)
 constexpr int WT_STRIDE = 132;       // padded row of the transposed projection in shared memory
 constexpr int ROWS = 8;              // query blocks per score_select CTA (one warp each in the selection)
+constexpr int SS_THREADS = 512;      // score_select threads (one key block each up to 512 key blocks)
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -56,7 +57,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
 __global__ void __launch_bounds__(PP_MAX_GROUPS * 64, 1)
 pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
                     int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
-                    const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ khT, int kbp,
+                    const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kbp,
                     int *status) {
     extern __shared__ uint8_t smr_raw[];
     uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
@@ -142,7 +143,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     acc = __fmaf_rn(mv.w, wv.w, acc);
                 }
                 if (isq) qh[((size_t)h * nb + b) * R + e] = acc;
-                else khT[((size_t)h * R + e) * kbp + b] = acc;
+                else kh[((size_t)h * kbp + b) * R + e] = acc;
             }
         }
         asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");   // smean is rewritten next block
@@ -182,8 +183,10 @@ __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb,
     auto count = [&](uint32_t c, bool strict) -> int {
         int n = 0;
         if (NK > 0) {
+            int n4[4] = {0, 0, 0, 0};   // independent partial counts keep the add chains short
 #pragma unroll
-            for (int u = 0; u < NK; ++u) n += strict ? (kr[u] > c) : (kr[u] >= c);
+            for (int u = 0; u < NK; ++u) n4[u & 3] += strict ? (kr[u] > c) : (kr[u] >= c);
+            n = (n4[0] + n4[1]) + (n4[2] + n4[3]);
         } else {
             for (int j = lane; j < kb; j += 32) n += strict ? (mykeys[j] > c) : (mykeys[j] >= c);
         }
@@ -197,17 +200,17 @@ __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb,
     need = extra - count(T, true);   // ties at T to keep, >= 1
 }
 
-// grid (ceil(qb / ROWS), H), 256 threads, ROWS = 8 query blocks per CTA.
-// Phase 1: thread t scores key blocks t, t + 256, ... against the CTA's 8 query blocks: the R
-// projections of a key block come from khT (row e of all threads' key blocks is one coalesced
-// read, 32 rows in flight per thread), each reused for the 8 query blocks, whose projections are
+// grid (ceil(qb / ROWS), H), SS_THREADS threads, ROWS = 8 query blocks per CTA.
+// Phase 1: thread t scores key blocks t, t + SS_THREADS, ... against the CTA's 8 query blocks: the R
+// projections of a key block are one contiguous row of kh (16 float4 loads in flight per thread),
+// each value reused for the 8 query blocks, whose projections are
 // read from shared memory ([R][8], two broadcast float4 per row). Scores accumulate with fmaf in
 // ascending e, -0 becomes +0, non-finite scores are flagged; the order-preserving uint32 of each
 // unforced score goes to shared memory (0 = not a candidate, which no finite score maps to).
 // Phase 2: warp w selects for query block w: the `extra`-th largest key T (keys in registers for
 // kb <= 1024), blocks above T kept, ties at T to the lowest block indices (ordered ballot scan),
 // forced blocks always kept, ids written ascending.
-__global__ void __launch_bounds__(256) score_select_kernel(const float *__restrict__ qh, const float *__restrict__ khT,
+__global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *__restrict__ qh, const float *__restrict__ kh,
                                                            int qb, int kb, int kbp, int R, int block, int Lq, int Lk,
                                                            int sink, int extra, int32_t *__restrict__ ids, int n_ids,
                                                            uint8_t *__restrict__ mask, float *__restrict__ scores,
@@ -224,28 +227,29 @@ __global__ void __launch_bounds__(256) score_select_kernel(const float *__restri
     __syncthreads();
     static_assert(ROWS == 8, "two float4 of query projections per row");
     const float4 *q4 = reinterpret_cast<const float4 *>(sqT);
-    const float *kc = khT + (size_t)h * R * kbp;
     bool bad = false;
     for (int j = tid; j < kb; j += blockDim.x) {
         float acc[ROWS];
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) acc[r] = 0.f;
-        for (int e0 = 0; e0 < R; e0 += 32) {   // R is a multiple of 16
-            float kv[32];
+        const float4 *krow = reinterpret_cast<const float4 *>(kh + ((size_t)h * kbp + j) * R);
+        for (int e0 = 0; e0 < R; e0 += 64) {   // R is a multiple of 16
+            float4 kv[16];
 #pragma unroll
-            for (int u = 0; u < 32; ++u) kv[u] = e0 + u < R ? __ldg(kc + (size_t)(e0 + u) * kbp + j) : 0.f;
+            for (int u = 0; u < 16; ++u) kv[u] = e0 + 4 * u < R ? __ldg(krow + e0 / 4 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < 32; ++u) {
+            for (int u = 0; u < 64; ++u) {
                 if (e0 + u >= R) break;
+                const float k = (u & 3) == 0 ? kv[u >> 2].x : (u & 3) == 1 ? kv[u >> 2].y : (u & 3) == 2 ? kv[u >> 2].z : kv[u >> 2].w;
                 const float4 qa = q4[2 * (e0 + u)], qb4 = q4[2 * (e0 + u) + 1];
-                acc[0] = __fmaf_rn(qa.x, kv[u], acc[0]);
-                acc[1] = __fmaf_rn(qa.y, kv[u], acc[1]);
-                acc[2] = __fmaf_rn(qa.z, kv[u], acc[2]);
-                acc[3] = __fmaf_rn(qa.w, kv[u], acc[3]);
-                acc[4] = __fmaf_rn(qb4.x, kv[u], acc[4]);
-                acc[5] = __fmaf_rn(qb4.y, kv[u], acc[5]);
-                acc[6] = __fmaf_rn(qb4.z, kv[u], acc[6]);
-                acc[7] = __fmaf_rn(qb4.w, kv[u], acc[7]);
+                acc[0] = __fmaf_rn(qa.x, k, acc[0]);
+                acc[1] = __fmaf_rn(qa.y, k, acc[1]);
+                acc[2] = __fmaf_rn(qa.z, k, acc[2]);
+                acc[3] = __fmaf_rn(qa.w, k, acc[3]);
+                acc[4] = __fmaf_rn(qb4.x, k, acc[4]);
+                acc[5] = __fmaf_rn(qb4.y, k, acc[5]);
+                acc[6] = __fmaf_rn(qb4.z, k, acc[6]);
+                acc[7] = __fmaf_rn(qb4.w, k, acc[7]);
             }
         }
         const bool forced = is_forced(j, block, Lq, Lk, sink);
@@ -327,12 +331,12 @@ int router_prepare(int device) {
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// key projections are stored transposed with rows padded to a multiple of 4 blocks, so every
-// bulk copy of a row segment starts and ends on a 16-byte boundary
+// key-block count rounded up to a multiple of 4: the stride of the per-query-block key rows of
+// score_select in shared memory and the row count of the key projections
 static int kb_padded(int kb) { return (kb + 3) & ~3; }
 
 struct RouterLayout {
-    size_t qh, khT, total;
+    size_t qh, kh, total;
 };
 
 static RouterLayout router_layout(int H, int Lq, int Lk, int R, int block) {
@@ -340,8 +344,8 @@ static RouterLayout router_layout(int H, int Lq, int Lk, int R, int block) {
     const size_t kbp = (size_t)kb_padded((Lk + block - 1) / block);
     RouterLayout L;
     L.qh = 0;
-    L.khT = align256(L.qh + 4 * (size_t)H * qb * R);
-    L.total = align256(L.khT + 4 * (size_t)H * R * kbp);
+    L.kh = align256(L.qh + 4 * (size_t)H * qb * R);
+    L.total = align256(L.kh + 4 * (size_t)H * R * kbp);
     return L;
 }
 
@@ -386,7 +390,7 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     int rc = router_prepare(device);
     if (rc) return rc;
     const RouterLayout L = router_layout(H, Lq, Lk, R, block);
-    float *qh = reinterpret_cast<float *>(ws + L.qh), *khT = reinterpret_cast<float *>(ws + L.khT);
+    float *qh = reinterpret_cast<float *>(ws + L.qh), *kh = reinterpret_cast<float *>(ws + L.kh);
     // blocks per pool_project tile: the fewest that keep the grid within one wave
     int nsm = 148;
     if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) nsm = 148;
@@ -401,9 +405,9 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)Lk, row_bytes, router::D, (uint32_t)block))
         return SS_ERR_DRIVER;
     router::pool_project_kernel<<<dim3(tq + tk, H), 64 * ng, pp_smem(R, block, ng), st>>>(
-        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, khT, kbp, status);
-    router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), 256,
-                                  select_smem(kbp, R), st>>>(qh, khT, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
+        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kbp, status);
+    router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::SS_THREADS,
+                                  select_smem(kbp, R), st>>>(qh, kh, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
                                                              extra, ids, n_ids, mask, scores, status);
     return (int)cudaGetLastError();
 }
@@ -413,9 +417,8 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
 // ---------------------------------------------------------------------------------------------
 // For callers that cannot allocate device memory per call. Every call on a device shares this
 // one array (it keeps the previous call's contents; nothing in it has to start at zero, because
-// each call writes every value that affects its results -- the few padding entries of the
-// transposed key rows are copied along but never used), so calls that may overlap on the GPU --
-// two streams, or two host threads -- race and must be serialised by the caller.
+// each call writes every value it reads), so calls that may overlap on the GPU -- two streams,
+// or two host threads -- race and must be serialised by the caller.
 static __device__ __align__(256) uint8_t g_router_scratch[SS_ROUTER_STATIC_SCRATCH_BYTES];
 
 static std::mutex g_router_scratch_mutex;
