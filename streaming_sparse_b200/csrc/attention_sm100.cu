@@ -162,9 +162,9 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 }
 
 // Ascending compaction of the set bits of word(w) (w < nwords) into sub-block entries, run by
-// one warp; sub-block k of the output is stored at out[k]. Returns the number written.
-template <class W, class M>
-__device__ __forceinline__ int compact(int nwords, int block, int Lk, int lane, W &&word, M &&maskof, uint32_t *out) {
+// one warp; sub-block k of the output is stored by put(k, entry). Returns the number written.
+template <class W, class M, class P>
+__device__ __forceinline__ int compact(int nwords, int block, int Lk, int lane, W &&word, M &&maskof, P &&put) {
     const int per = block / 64;
     int carry = 0;
     for (int w0 = 0; w0 < nwords; w0 += 32) {
@@ -186,12 +186,20 @@ __device__ __forceinline__ int compact(int nwords, int block, int Lk, int lane, 
             for (int s = 0; s < per; ++s) {
                 const int t0 = j * block + s * 64;
                 const int valid = min(64, max(0, Lk - t0));
-                out[pos++] = entry((uint32_t)t0, (uint32_t)valid, m);
+                put(pos++, entry((uint32_t)t0, (uint32_t)valid, m));
             }
         }
         carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     return carry;
+}
+
+__device__ __forceinline__ int warp_count_bits(int nwords, int lane, int per, const uint32_t *a, const uint32_t *b,
+                                               uint32_t ka, uint32_t kb_) {
+    // number of set bits of (a ^ ka) & (b ^ kb_) over nwords words, times per (warp reduction)
+    int c = 0;
+    for (int w = lane; w < nwords; w += 32) c += __popc((a[w] ^ ka) & (b[w] ^ kb_));
+    return (int)__reduce_add_sync(0xffffffffu, (unsigned)c) * per;
 }
 
 // Q rows of the tile for one warpgroup: dims [64w, 64w + 64) of row `row` as 32 bf16 pairs.
@@ -343,17 +351,33 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     }
     __syncthreads();
     if (warp == 0) {
-        // per tile: ascending union sub-blocks, padded to a whole, even number (>= 2) of steps
+        // Per tile, the union's sub-blocks, padded to a whole, even number (>= 2) of steps. A
+        // 64-row half of the tile runs on two fixed SM sub-partitions (TMEM lane quarters), so a
+        // step whose sub-blocks only one half selected keeps the other half's sub-partitions
+        // idle while the first exponentiate 128 columns per row. The blocks only the first
+        // half selected are therefore paired with blocks only the second half selected (each
+        // row then exponentiates 64 columns), followed by the unpaired rest and the blocks
+        // both halves selected, each group ascending.
         uint32_t *sub = reinterpret_cast<uint32_t *>(steps);
         int pos = 0;   // sub-blocks written
         for (int lt = 0; lt < nt; ++lt) {
             const uint32_t *A = bm + (2 * lt) * p.nwords, *B = A + p.nwords;
-            const int n = compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] | B[w]; },
-                                  [&](int w, int bit) -> uint32_t {
-                                      if (!pairq) return 3u;
-                                      return ((A[w] >> bit) & 1u) | (((B[w] >> bit) & 1u) << 1);
-                                  },
-                                  sub + pos);
+            const int per = p.block / 64;
+            auto maskof = [&](int w, int bit) -> uint32_t {
+                if (!pairq) return 3u;
+                return ((A[w] >> bit) & 1u) | (((B[w] >> bit) & 1u) << 1);
+            };
+            const int na = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0xffffffffu);   // A only
+            const int nb = warp_count_bits(p.nwords, lane, per, B, A, 0u, 0xffffffffu);   // B only
+            const int mp = min(na, nb);
+            uint32_t *base = sub + pos;
+            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
+                    [&](int k, uint32_t e) { base[k < mp ? 2 * k : mp + k] = e; });
+            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
+                    [&](int k, uint32_t e) { base[k < mp ? 2 * k + 1 : mp + k] = e; });
+            const int nboth = compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & B[w]; }, maskof,
+                                      [&](int k, uint32_t e) { base[na + nb + k] = e; });
+            const int n = na + nb + nboth;
             const int padded = max(4, (n + 3) & ~3);
             for (int k = n + lane; k < padded; k += 32) sub[pos + k] = entry(0u, 0u, 0u);
             if (lane == 0) {
