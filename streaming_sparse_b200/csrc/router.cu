@@ -86,9 +86,20 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_arrive_expect_tx(full, stage_bytes);
         tma_load_2d(stage, tm, h * D, (b0 + g) * block, full);
     }
-    {   // W [128][R] of head h, transposed into shared memory while the first loads are in flight
+    {   // W [128][R] of head h, transposed into shared memory while the first loads are in flight;
+        // each thread's loads are all issued before any is stored (one round trip, not one each)
         const float *w = (isq ? wq : wk) + (size_t)h * D * R;
-        for (int x = tid; x < D * R; x += blockDim.x) swt[(x % R) * WT_STRIDE + x / R] = __ldg(w + x);
+        const int nw = D * R, step = blockDim.x;
+        for (int x0 = tid; x0 < nw; x0 += 16 * step) {
+            float v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = x0 + u * step < nw ? __ldg(w + x0 + u * step) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int x = x0 + u * step;
+                if (x < nw) swt[(x % R) * WT_STRIDE + x / R] = v[u];
+            }
+        }
     }
     __syncthreads();
     // Every thread of a group runs every group barrier (bar.sync is not bounded): after a failed
