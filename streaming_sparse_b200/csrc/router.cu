@@ -1,10 +1,11 @@
 // router.cu -- learned KV-block router for sm_100a in exact fp32.
 //
 //   1. pool_project: one CTA per SM, each pooling a tile of blocks of one head (query or key).
-//      The head's [128 x R] projection is transposed into shared memory; the blocks' tokens
-//      arrive by TMA, one block per 64-thread group at a time; each thread sums 2 dimensions over
-//      the block's valid tokens (fp32 adds in token order, one correctly rounded divide), then
-//      the block means are projected with fmaf in ascending row order. Query projections are
+//      The head's [128 x R] projection is bulk-copied into shared memory first; the blocks' tokens
+//      arrive by TMA, one block per warp at a time; each lane sums 4 dimensions over the block's
+//      valid tokens (fp32 adds in token order, one correctly rounded divide), then the means of
+//      two blocks are projected together with fmaf in ascending row order (f32x2 instructions:
+//      two independent IEEE operations each, so every value is the scalar chain's). Query projections are
 //      stored [H][qb][R], key projections [H][kbp][R] (kbp = kb rounded up to 4).
 //      Reference: block pooling of migration/unified_router/opt19/prototype.py:11-49 (one
 //      prototype = plain mean of the valid tokens) and the projection of opt8/projection.py:4-14.
@@ -32,8 +33,7 @@ namespace router {
 constexpr int D = 128;
 constexpr int MAX_R = 128;
 constexpr int MAX_KB = 8192;
-constexpr int PP_MAX_GROUPS = 12;    // 64-thread groups per pool_project CTA (one TMA stage each)
-constexpr int WT_STRIDE = 132;       // padded row of the transposed projection in shared memory
+constexpr int PP_MAX_WARPS = 16;     // warps per pool_project CTA (one TMA stage each)
 constexpr int ROWS = 8;              // query blocks per score_select CTA (one warp each in the selection)
 constexpr int SS_THREADS = 512;      // score_select threads (one key block each up to 512 key blocks)
 
@@ -45,126 +45,149 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
-// grid (tiles_q + tiles_k, H), 64 * ng threads = ng groups of 64 (one CTA per SM). Tiles
-// [0, tiles_q) pool query blocks, the rest key blocks, bg blocks per tile. Group g pools blocks
-// g, g + ng, ... of the tile: the group's leader TMA-loads a block (block tokens x 128 dims of
-// head h, plain rows) into the group's stage, the 64 threads sum 2 dimensions each in token
-// order, the leader starts the next block's load, and the group projects the block mean (thread
-// e: outputs e, e + 64) against W transposed in shared memory (rows padded to WT_STRIDE floats, so
-// the float4 reads of 32 threads hit every bank the same number of times). ng stages of 16 KB keep
-// about 190 KB in flight per SM. Dynamic shared memory: stages [ng][block][128] bf16,
-// W^T [R][WT_STRIDE] fp32, means [ng][128] fp32, mbarriers, abort flag.
-__global__ void __launch_bounds__(PP_MAX_GROUPS * 64, 1)
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t r) {
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+    return v;
+}
+// two independent IEEE fp32 operations (round to nearest) on the halves of a register pair
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// grid (tiles_q + tiles_k, H), 32 * nw threads (one CTA per SM). Tiles [0, tiles_q) pool query
+// blocks, the rest key blocks, bg blocks per tile. Thread 0 first starts one bulk copy of the
+// head's projection W [128][R] into shared memory (ahead of the token loads, so the small copy is
+// not queued behind megabytes of them). Warp w owns one TMA stage and pools blocks w, w + nw, ...
+// of the tile in pairs: lane 0 TMA-loads a block (block tokens x 128 dims of head h, plain rows),
+// lane l sums dimensions 4l..4l+3 over the valid tokens in token order (two f32x2 adds per token),
+// lane 0 reloads the stage with the warp's next block, and once both blocks of a pair are summed
+// the warp projects both means with one pass over W (lane l: outputs 2l, 2l+1 (+64 ...), one
+// f32x2 fma per block per row, rows ascending). Dynamic shared memory: stages [nw][block][128]
+// bf16, W [128][R] fp32, means [nw][128] x {A, A, B, B} fp32, mbarriers full[nw] and w, abort.
+__global__ void __launch_bounds__(PP_MAX_WARPS * 32, 1)
 pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
                     int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
                     const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kbp,
                     int *status) {
     extern __shared__ uint8_t smr_raw[];
     uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
-    const int ng = blockDim.x / 64;
+    const int nw = blockDim.x / 32;
     const uint32_t stage_bytes = (uint32_t)block * D * 2;
-    float *swt = reinterpret_cast<float *>(smr + ng * stage_bytes);   // [R][WT_STRIDE]
-    float *smean = swt + R * WT_STRIDE;                                // [ng][128]
-    uint64_t *mb = reinterpret_cast<uint64_t *>(smean + ng * D);      // full[ng]
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(mb + ng);
-    const int h = blockIdx.y, tid = threadIdx.x, g = tid >> 6, gt = tid & 63;
+    float *sw = reinterpret_cast<float *>(smr + nw * stage_bytes);   // [128][R]
+    float4 *smean = reinterpret_cast<float4 *>(sw + D * R);          // [nw][128]
+    uint64_t *mb = reinterpret_cast<uint64_t *>(smean + nw * D);     // full[nw], w
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(mb + nw + 1);
+    const int h = blockIdx.y, tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
     const bool isq = (int)blockIdx.x < tiles_q;
     const int tile = isq ? blockIdx.x : blockIdx.x - tiles_q;
     const int L = isq ? Lq : Lk;
     const int nb = (L + block - 1) / block;
     const int b0 = tile * bg, nblk = min(bg, nb - b0);
-    const uint32_t full = smem_u32(mb + g);
-    const uint32_t stage = smem_u32(smr) + g * stage_bytes;
+    const uint32_t full = smem_u32(mb + w), wbar = smem_u32(mb + nw);
+    const uint32_t stage = smem_u32(smr) + w * stage_bytes;
+    const uint8_t *stage_p = smr + w * stage_bytes;
+    float4 *md = smean + w * D;
     const CUtensorMap *tm = isq ? &tm_q : &tm_k;
     if (tid == 0) {
         *abort_flag = 0;
-        for (int i = 0; i < ng; ++i) mbar_init(smem_u32(mb + i), 1);
+        for (int i = 0; i <= nw; ++i) mbar_init(smem_u32(mb + i), 1);
         fence_mbar_init();
+        const uint32_t wbytes = (uint32_t)(D * R * 4);
+        mbar_arrive_expect_tx(wbar, wbytes);
+        bulk_g2s(smem_u32(sw), (isq ? wq : wk) + (size_t)h * D * R, wbytes, wbar);
     }
     __syncthreads();
-    if (gt == 0 && g < nblk) {
+    int issued = 0, seen = 0;   // lane 0's loads into the stage, and those waited on
+    if (lane == 0 && w < nblk) {
         mbar_arrive_expect_tx(full, stage_bytes);
-        tma_load_2d(stage, tm, h * D, (b0 + g) * block, full);
+        tma_load_2d(stage, tm, h * D, (b0 + w) * block, full);
+        issued = 1;
     }
-    {   // W [128][R] of head h, transposed into shared memory while the first loads are in flight;
-        // each thread's loads are all issued before any is stored (one round trip, not one each)
-        const float *w = (isq ? wq : wk) + (size_t)h * D * R;
-        const int nw = D * R, step = blockDim.x;
-        for (int x0 = tid; x0 < nw; x0 += 16 * step) {
-            float v[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) v[u] = x0 + u * step < nw ? __ldg(w + x0 + u * step) : 0.f;
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int x = x0 + u * step;
-                if (x < nw) swt[(x % R) * WT_STRIDE + x / R] = v[u];
-            }
-        }
-    }
-    __syncthreads();
-    // Every thread of a group runs every group barrier (bar.sync is not bounded): after a failed
-    // wait the work is skipped but the barriers are kept, and the shared abort flag makes the
-    // remaining waits of the CTA return at once.
-    bool ok = true;
-    int issued = g < nblk ? 1 : 0, seen = 0;   // the leader's loads into the stage, and those waited on
-    for (int it = 0; g + ng * it < nblk; ++it) {
-        const int bi = g + ng * it;
+    bool ok = true, w_seen = false;
+    // sum block bi from the stage (the k-th load), then reload the stage with block `next`
+    auto pool = [&](int bi, int k, int next, bool hi_half) {
         if (ok) {
-            ok = mbar_wait(full, it & 1, abort_flag);
-            seen = it + 1;
+            ok = mbar_wait(full, k & 1, abort_flag);
+            seen = k + 1;
         }
         const int t0 = (b0 + bi) * block, n = min(block, L - t0);
-        float s0 = 0.f, s1 = 0.f;
+        uint64_t s01 = 0, s23 = 0;
         if (ok) {
-            // thread gt sums dimensions 2gt, 2gt+1 over the block's valid tokens, in token order
-            const uint32_t *rows = reinterpret_cast<const uint32_t *>(smr + g * stage_bytes) + gt;
+            const uint2 *rows = reinterpret_cast<const uint2 *>(stage_p) + lane;
 #pragma unroll 8
             for (int t = 0; t < n; ++t) {
-                const uint32_t w = rows[t * (D / 2)];
-                s0 = __fadd_rn(s0, bf16_lo(w));
-                s1 = __fadd_rn(s1, bf16_hi(w));
+                const uint2 v = rows[t * (D / 4)];
+                s01 = add2(s01, pack2(bf16_lo(v.x), bf16_hi(v.x)));
+                s23 = add2(s23, pack2(bf16_lo(v.y), bf16_hi(v.y)));
             }
         }
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");   // the stage has been read
-        if (ok && gt == 0 && bi + ng < nblk) {
+        __syncwarp();
+        if (ok && lane == 0 && next < nblk) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive_expect_tx(full, stage_bytes);
-            tma_load_2d(stage, tm, h * D, (b0 + bi + ng) * block, full);
+            tma_load_2d(stage, tm, h * D, (b0 + next) * block, full);
             ++issued;
         }
         const float fn = (float)n;
-        smean[g * D + 2 * gt] = __fdiv_rn(s0, fn);
-        smean[g * D + 2 * gt + 1] = __fdiv_rn(s1, fn);
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");
-        if (ok) {
-            // projection: outputs gt and gt + 64, fmaf over the 128 rows in ascending order
-            const int b = b0 + bi;
-            const float4 *m4 = reinterpret_cast<const float4 *>(smean + g * D);
+        const float2 a = unpack2(s01), b = unpack2(s23);
+        const float m[4] = {__fdiv_rn(a.x, fn), __fdiv_rn(a.y, fn), __fdiv_rn(b.x, fn), __fdiv_rn(b.y, fn)};
 #pragma unroll
-            for (int e = gt; e < MAX_R; e += 64) {
-                if (e >= R) break;
-                const float4 *w4 = reinterpret_cast<const float4 *>(swt + e * WT_STRIDE);
-                float acc = 0.f;
+        for (int i = 0; i < 4; ++i) {
+            float2 *p = reinterpret_cast<float2 *>(md + 4 * lane + i) + (hi_half ? 1 : 0);
+            *p = make_float2(m[i], m[i]);
+        }
+    };
+    int k = 0;
+    for (int bA = w; bA < nblk; bA += 2 * nw, k += 2) {
+        const int bB = bA + nw;
+        const bool hasB = bB < nblk;
+        pool(bA, k, bB, false);
+        if (hasB) pool(bB, k + 1, bB + nw, true);
+        if (!w_seen && ok) {
+            ok = mbar_wait(wbar, 0, abort_flag);
+            w_seen = ok;
+        }
+        __syncwarp();
+        if (ok) {
+            // projection of both means: fmaf over the 128 rows in ascending order per output
+            for (int e = 2 * lane; e < R; e += 64) {
+                const float *wc = sw + e;
+                uint64_t accA = 0, accB = 0;
 #pragma unroll 8
-                for (int d4 = 0; d4 < D / 4; ++d4) {
-                    const float4 mv = m4[d4], wv = w4[d4];
-                    acc = __fmaf_rn(mv.x, wv.x, acc);
-                    acc = __fmaf_rn(mv.y, wv.y, acc);
-                    acc = __fmaf_rn(mv.z, wv.z, acc);
-                    acc = __fmaf_rn(mv.w, wv.w, acc);
+                for (int d = 0; d < D; ++d) {
+                    const float4 mv = md[d];
+                    const uint64_t wv = *reinterpret_cast<const uint64_t *>(wc + d * R);
+                    accA = fma2(pack2(mv.x, mv.y), wv, accA);
+                    accB = fma2(pack2(mv.z, mv.w), wv, accB);
                 }
-                if (isq) qh[((size_t)h * nb + b) * R + e] = acc;
-                else kh[((size_t)h * kbp + b) * R + e] = acc;
+                const float2 ra = unpack2(accA), rb = unpack2(accB);
+                float *dst = isq ? qh + ((size_t)h * nb + b0) * R : kh + ((size_t)h * kbp + b0) * R;
+                *reinterpret_cast<float2 *>(dst + (size_t)bA * R + e) = ra;
+                if (hasB) *reinterpret_cast<float2 *>(dst + (size_t)bB * R + e) = rb;
             }
         }
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + g) : "memory");   // smean is rewritten next block
+        __syncwarp();   // the means are rewritten by the next pair
     }
     if (*abort_flag) {
-        // a copy may still be landing: the leader's last load
+        // copies may still be landing: W, and lane 0's last load
         volatile int never = 0;
-        if (gt == 0) {
+        if (tid == 0 && !w_seen) mbar_wait(wbar, 0, &never);
+        if (lane == 0) {
             for (int j = seen; j < issued; ++j) mbar_wait(full, j & 1, &never);
-            if (g == 0) report(status, SS_DEV_TIMEOUT);
+            if (w == 0) report(status, SS_DEV_TIMEOUT);
         }
     }
 }
@@ -308,18 +331,18 @@ __global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *_
 
 }  // namespace router
 
-// pool_project: groups per CTA (one 16 KB / 32 KB stage each) that fit beside W^T and the means
-static int pp_groups(int R, int block) {
-    const size_t fixed = 1024 + (size_t)R * router::WT_STRIDE * 4 + 64;
-    const size_t per = (size_t)block * router::D * 2 + router::D * 4 + 8;
+// pool_project: warps per CTA (one 16 KB / 32 KB stage and 2 KB of means each) beside W
+static int pp_warps(int R, int block) {
+    const size_t fixed = 1024 + (size_t)R * router::D * 4 + 64;
+    const size_t per = (size_t)block * router::D * 2 + router::D * 16 + 8;
     const size_t budget = 227 * 1024;
-    int ng = budget > fixed ? (int)((budget - fixed) / per) : 0;
-    return std::min(ng, router::PP_MAX_GROUPS);
+    int nw = budget > fixed ? (int)((budget - fixed) / per) : 0;
+    return std::min(nw, router::PP_MAX_WARPS);
 }
 
-static size_t pp_smem(int R, int block, int ng) {
-    return 1024 + (size_t)ng * block * router::D * 2 + (size_t)R * router::WT_STRIDE * 4 + (size_t)ng * router::D * 4 +
-           8 * (size_t)ng + 16;
+static size_t pp_smem(int R, int block, int nw) {
+    return 1024 + (size_t)nw * block * router::D * 2 + (size_t)R * router::D * 4 + (size_t)nw * router::D * 16 +
+           8 * ((size_t)nw + 1) + 16;
 }
 
 static size_t select_smem(int kb, int R) {
@@ -408,14 +431,14 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     int bg = std::max(1, (H * (qb + kb) + nsm - 1) / nsm);
     while (H * ((qb + bg - 1) / bg + (kb + bg - 1) / bg) > nsm && bg < std::max(qb, kb)) ++bg;
     const int tq = (qb + bg - 1) / bg, tk = (kb + bg - 1) / bg;
-    const int ng = pp_groups(R, block);
+    const int nw = pp_warps(R, block);
     CUtensorMap tmq, tmk;
     const uint64_t row_bytes = (uint64_t)H * router::D * 2;
     if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D, (uint32_t)block))
         return SS_ERR_DRIVER;
     if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)Lk, row_bytes, router::D, (uint32_t)block))
         return SS_ERR_DRIVER;
-    router::pool_project_kernel<<<dim3(tq + tk, H), 64 * ng, pp_smem(R, block, ng), st>>>(
+    router::pool_project_kernel<<<dim3(tq + tk, H), 32 * nw, pp_smem(R, block, nw), st>>>(
         tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kbp, status);
     router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::SS_THREADS,
                                   select_smem(kbp, R), st>>>(qh, kh, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
