@@ -32,6 +32,13 @@
  *   ss_cache_append<- the cache roll + write in CausalWanSelfAttention.forward
  *                     (wan/modules/causal_model.py:216-246) and commit_fixed15
  *                     (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:453-458)
+ *   ss_qkv_norm_rope <- the fused projection hook project_cached_rotary
+ *                     (wan/modules/causal_model.py:116-128, 241-246; local_experiments/
+ *                     video_runtime_v1/rms_mean.py:38-72): q/k RMSNorm + RoPE, k/v into the cache
+ *   ss_adaln       <- WanLayerNorm + modulation (wan/modules/causal_model.py:332, 344-345, 383)
+ *                     and the affine norm3 (wan/modules/causal_model.py:285-287)
+ *   ss_rms_norm    <- WanRMSNorm (wan/modules/model.py:70-86) of the cross-attention query (:172)
+ *   ss_gate_residual <- the gated residual adds (wan/modules/causal_model.py:337, 348-349)
  */
 #ifndef SSPARSE_H_
 #define SSPARSE_H_
@@ -158,6 +165,40 @@ int ss_cache_append(void *k_cache, void *v_cache, int cap, int H,
                     int local_attn, int64_t global_end, int64_t local_end,
                     int64_t current_start, int sink_tokens, int64_t *out_local_end,
                     void *stream);
+
+/* ---- per-token kernels of the DiT layer around the attention (one CTA per token row) ---- */
+
+/* q/k/v rows of one chunk from a fused [n][>= 3*d] projection (q at column 0, k at d, v at 2d;
+ * d = H*128; row stride qkv_ld elements). For q and k: RMSNorm over the d columns (fp32 mean of
+ * squares, + eps, rsqrt), rounded to bf16, times the bf16 norm weight (rounded), then rotated
+ * pairwise (2i, 2i+1) by the row's table cos_t/sin_t [n][64] fp32 (pair index = column % 128 / 2).
+ * q goes to q_out (row stride q_ld); k and the untouched v go to k_out / v_out (row stride kv_ld),
+ * which may be the cache rows the chunk occupies. All pointers 16-byte aligned, strides multiples
+ * of 8 elements, d/8 <= 1024. */
+int ss_qkv_norm_rope(const void *qkv, int64_t qkv_ld, int n, int H, const void *norm_q,
+                     const void *norm_k, float eps, const float *cos_t, const float *sin_t,
+                     void *q_out, int64_t q_ld, void *k_out, void *v_out, int64_t kv_ld,
+                     void *stream);
+
+/* LayerNorm of the n rows of x [n][d] bf16 (no affine, fp32 statistics, rounded to bf16), then
+ * EITHER modulation with the row's frame f = row / frame_tokens:
+ *     out = bf16(ln * (1 + scale[f*mod_ld + c]) + shift[f*mod_ld + c])   (shift/scale fp32)
+ * OR affine: out = bf16(((x - mean) * rstd) * weight + bias) (weight/bias bf16 [d]).
+ * Exactly one of (shift, scale) and (weight, bias) is given. d a multiple of 8, d/8 <= 1024. */
+int ss_adaln(const void *x, int n, int d, int frame_tokens, const float *shift, const float *scale,
+             int64_t mod_ld, const void *weight, const void *bias, float eps, void *out,
+             void *stream);
+
+/* out [n][d] bf16 = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * weight), x rows at stride x_ld,
+ * weight bf16 [d]. */
+int ss_rms_norm(const void *x, int64_t x_ld, int n, int d, const void *weight, float eps, void *out,
+                void *stream);
+
+/* In place on x [n][d] bf16 (contiguous rows): x = bf16(x + bf16(y * gate[f])) with
+ * f = row / frame_tokens and gate fp32 rows of stride gate_ld, or x = bf16(x + y) when gate is
+ * NULL. y rows at stride y_ld elements. */
+int ss_gate_residual(void *x, const void *y, int64_t y_ld, int n, int d, int frame_tokens,
+                     const float *gate, int64_t gate_ld, void *stream);
 
 #ifdef __cplusplus
 }

@@ -98,6 +98,28 @@ class KVCache:
         self.commits += 1
         return vis
 
+    def reserve(self, n: int, current_start: int):
+        """Claim the rows a chunk of n tokens occupies, for a producer that writes them itself.
+
+        Returns (k rows, v rows) as [n,H,D] views of the cache and advances the index state as
+        ``append`` would, when the write needs no roll of the window; returns None (state
+        unchanged) when it does, in which case the caller writes through ``append``.
+        """
+        end = current_start + n
+        if self.local_attn_size != -1 and end > self.global_end and n + self.local_end > self.capacity:
+            return None
+        if self.positions is not None:
+            self.positions.update(start=current_start, n=n, old_global=self.global_end, old_local=self.local_end,
+                                  local_attn=self.local_attn_size != -1, sink_tokens=self.sink_tokens,
+                                  max_attention_size=self.max_attention_size)
+        local_end = self.local_end + end - self.global_end
+        start = local_end - n
+        if start < 0 or local_end > self.capacity:
+            raise ValueError("Invalid KV cache bounds; reduce length or use local attention")
+        self.local_end, self.global_end = local_end, end
+        self.commits += 1
+        return self.k[0, start:local_end], self.v[0, start:local_end]
+
     def window(self):
         """Visible K/V window [Lk,H,D] (views into the cache): the last tokens are the current chunk."""
         a = max(0, self.local_end - self.max_attention_size)

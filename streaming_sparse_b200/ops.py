@@ -300,8 +300,99 @@ def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end
     return new_end.value
 
 
+# ----------------------------------------------------------------------------------------------
+# per-token kernels of the DiT layer around the attention (csrc/dit.cu), used by the rollout
+# ----------------------------------------------------------------------------------------------
+def _rows(t: torch.Tensor, name: str, width: int) -> int:
+    """Row stride of a CUDA tensor whose last dim holds `width` contiguous values per row."""
+    _require(t.is_cuda, f"{name}: must be a CUDA tensor")
+    _require(t.stride(-1) == 1 and t.shape[-1] >= width, f"{name}: rows of {width} contiguous values expected")
+    return t.stride(-2) if t.dim() >= 2 else width
+
+
+def qkv_norm_rope(qkv: torch.Tensor, norm_q: torch.Tensor, norm_k: torch.Tensor, eps: float, cos: torch.Tensor,
+                  sin: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor) -> torch.Tensor:
+    """q/k RMSNorm + weight + 3-D RoPE, v copied, from one fused projection (`ss_qkv_norm_rope`).
+
+    qkv [n, >=3d] bf16 (q | k | v columns, d = H*128); norm_q/norm_k [d] bf16; cos/sin [n, 64]
+    fp32; q_out [n, H, 128] bf16; k_out/v_out [n, H, 128] bf16 with equal row strides (for
+    example the cache rows of the chunk). Returns q_out.
+    """
+    n, H = q_out.shape[0], q_out.shape[1]
+    d = H * HEAD_DIM
+    _require(qkv.dtype == torch.bfloat16 and qkv.dim() == 2 and qkv.shape[0] == n, "qkv: bf16 [n, 3d]")
+    ld = _rows(qkv, "qkv", 3 * d)
+    for name, t in (("q_out", q_out), ("k_out", k_out), ("v_out", v_out)):
+        _require(t.dtype == torch.bfloat16 and t.shape == (n, H, HEAD_DIM) and t.stride(2) == 1 and
+                 t.stride(1) == HEAD_DIM, f"{name}: bf16 [n, H, 128] rows")
+    _require(k_out.stride(0) == v_out.stride(0), "k_out and v_out must share a row stride")
+    for name, t in (("norm_q", norm_q), ("norm_k", norm_k)):
+        _require(t.dtype == torch.bfloat16 and t.is_contiguous() and t.numel() == d, f"{name}: bf16 [{d}]")
+    for name, t in (("cos", cos), ("sin", sin)):
+        _require(t.dtype == torch.float32 and t.is_contiguous() and t.shape == (n, HEAD_DIM // 2),
+                 f"{name}: fp32 [n, 64]")
+    rc = lib().ss_qkv_norm_rope(_p(qkv), ld, n, H, _p(norm_q), _p(norm_k), float(eps), _p(cos), _p(sin), _p(q_out),
+                                q_out.stride(0), _p(k_out), _p(v_out), k_out.stride(0), _stream(qkv.device))
+    check(rc, "ss_qkv_norm_rope")
+    return q_out
+
+
+def adaln(x: torch.Tensor, *, eps: float, shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
+          frame_tokens: int = 0, weight: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+          out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm of x [n, d] bf16 with per-frame modulation (shift/scale fp32 rows [frames, d],
+    any row stride) or with an affine bf16 weight/bias (`ss_adaln`)."""
+    _require(x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous() and x.is_cuda,
+             "x: contiguous bf16 [n, d]")
+    n, d = x.shape
+    out = torch.empty_like(x) if out is None else out
+    _require(out.shape == x.shape and out.dtype == x.dtype and out.is_contiguous(), "bad out buffer")
+    mod_ld = 0
+    if shift is not None or scale is not None:
+        _require(shift is not None and scale is not None, "shift and scale go together")
+        _require(shift.dtype == scale.dtype == torch.float32, "shift/scale: fp32")
+        mod_ld = _rows(shift, "shift", d)
+        _require(_rows(scale, "scale", d) == mod_ld, "shift and scale must share a row stride")
+        _require(frame_tokens > 0 and shift.shape[-2] * frame_tokens >= n, "frame_tokens must cover the rows")
+    rc = lib().ss_adaln(_p(x), n, d, int(frame_tokens), _p(shift), _p(scale), mod_ld, _p(weight), _p(bias), float(eps),
+                        _p(out), _stream(x.device))
+    check(rc, "ss_adaln")
+    return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """WanRMSNorm of the rows of x [n, d] bf16 (any row stride) with a bf16 weight (`ss_rms_norm`)."""
+    _require(x.dtype == torch.bfloat16 and x.dim() == 2, "x: bf16 [n, d]")
+    n, d = x.shape
+    x_ld = _rows(x, "x", d)
+    _require(weight.dtype == torch.bfloat16 and weight.is_contiguous() and weight.numel() == d, f"weight: bf16 [{d}]")
+    out = torch.empty((n, d), dtype=x.dtype, device=x.device) if out is None else out
+    _require(out.shape == (n, d) and out.dtype == x.dtype and out.is_contiguous(), "bad out buffer")
+    rc = lib().ss_rms_norm(_p(x), x_ld, n, d, _p(weight), float(eps), _p(out), _stream(x.device))
+    check(rc, "ss_rms_norm")
+    return out
+
+
+def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None = None,
+                  frame_tokens: int = 0) -> torch.Tensor:
+    """In place: x = x + y * gate[frame] (or x + y), bf16 [n, d] (`ss_gate_residual`)."""
+    _require(x.dtype == y.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(), "x: contiguous bf16 [n, d]")
+    n, d = x.shape
+    _require(y.shape == x.shape, "y must match x")
+    y_ld = _rows(y, "y", d)
+    g_ld = 0
+    if gate is not None:
+        _require(gate.dtype == torch.float32, "gate: fp32")
+        g_ld = _rows(gate, "gate", d)
+        _require(frame_tokens > 0 and gate.shape[-2] * frame_tokens >= n, "frame_tokens must cover the rows")
+    rc = lib().ss_gate_residual(_p(x), _p(y), y_ld, n, d, int(frame_tokens), _p(gate), g_ld, _stream(x.device))
+    check(rc, "ss_gate_residual")
+    return x
+
+
 __all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "sparse_attention", "exact",
-           "attention_max_ids", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks"]
+           "attention_max_ids", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
+           "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
 
 # keep the status-bit names importable from here
 DEV_BITS = dict(nonfinite=DEV_NONFINITE, timeout=DEV_TIMEOUT, badid=DEV_BADID)

@@ -197,8 +197,51 @@ class Block(nn.Module):
         v = self.cv(context).view(1, -1, H, HEAD_DIM)
         return k, v
 
-    def forward(self, x, e0, rope, cache: KVCache, cross, current_start: int):
-        """x [n, dim] bf16 (n = frames * frame_tokens), e0 [frames, 6, dim] fp32."""
+    def forward(self, x, e0, rope, cache: KVCache, cross, current_start: int, fused: bool = True):
+        """x [n, dim] bf16 (n = frames * frame_tokens), e0 [frames, 6, dim] fp32 -> new x.
+
+        ``fused`` (CUDA only): the per-token work between the GEMMs runs in the library's
+        kernels (AdaLN, q/k RMSNorm + RoPE with k/v written into the cache rows, RMSNorm, gated
+        residual adds, in place on x); otherwise as the PyTorch expressions below, which state
+        the same arithmetic.
+        """
+        if fused and x.is_cuda:
+            return self._forward_fused(x, e0, rope, cache, cross, current_start)
+        return self._forward_torch(x, e0, rope, cache, cross, current_start)
+
+    def _forward_fused(self, x, e0, rope, cache: KVCache, cross, current_start: int):
+        cfg, H = self.cfg, self.cfg.num_heads
+        n, d = x.shape
+        ft = n // e0.shape[0]
+        em = self.modulation.float() + e0                                 # [frames, 6, dim]
+        x = x.contiguous()
+
+        h = ops.adaln(x, eps=cfg.eps, shift=em[:, 0], scale=em[:, 1], frame_tokens=ft)
+        qkv = self.qkv(h)
+        q = torch.empty((n, H, HEAD_DIM), device=x.device, dtype=x.dtype)
+        rows = cache.reserve(n, current_start)
+        if rows is not None:
+            ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, rows[0], rows[1])
+        else:   # the write rolls the window: stage k/v, then the cache kernel rolls and writes
+            k = torch.empty_like(q)
+            v = torch.empty_like(q)
+            ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, k, v)
+            cache.append(k, v, current_start)
+        kw, vw = cache.window()
+        y = _module_attention()(q[None], kw[None], vw[None])[0]
+        ops.gate_residual(x, self.o(y.reshape(n, d)), gate=em[:, 2], frame_tokens=ft)
+
+        hq = ops.rms_norm(self.cq(ops.adaln(x, eps=cfg.eps, weight=self.norm3_w, bias=self.norm3_b)), self.cnorm_q,
+                          cfg.eps)
+        ck, cv = cross
+        y = dense_attention(hq.view(1, n, H, HEAD_DIM), ck, cv)[0]
+        ops.gate_residual(x, self.co(y.reshape(n, d)))
+
+        h = ops.adaln(x, eps=cfg.eps, shift=em[:, 3], scale=em[:, 4], frame_tokens=ft)
+        ops.gate_residual(x, self.ffn2(F.gelu(self.ffn1(h), approximate="tanh")), gate=em[:, 5], frame_tokens=ft)
+        return x
+
+    def _forward_torch(self, x, e0, rope, cache: KVCache, cross, current_start: int):
         cfg, H = self.cfg, self.cfg.num_heads
         n, d = x.shape
         fr = e0.shape[0]
@@ -306,7 +349,8 @@ class CausalWanDiT(nn.Module):
         u = torch.einsum("fhwpqrc->cfphqwr", u)
         return u.reshape(cfg.out_dim, Fr, cfg.latent_h, cfg.latent_w)
 
-    def forward_chunk(self, x: torch.Tensor, t, caches, cross, start_frame: int, rope) -> torch.Tensor:
+    def forward_chunk(self, x: torch.Tensor, t, caches, cross, start_frame: int, rope,
+                      fused: bool = True) -> torch.Tensor:
         """x [C, F, Hl, Wl] latents of one chunk -> flow prediction [C, F, Hl, Wl]."""
         cfg = self.cfg
         Fr = x.shape[1]
@@ -314,11 +358,14 @@ class CausalWanDiT(nn.Module):
         h = self.patchify(x)
         current_start = start_frame * cfg.frame_tokens
         for blk, cache, cr in zip(self.blocks, caches, cross):
-            h = blk(h, e0, rope, cache, cr, current_start)
-        m = (self.head_modulation.float() + e.unsqueeze(1)).chunk(2, dim=1)   # [F, 1, dim] x 2
+            h = blk(h, e0, rope, cache, cr, current_start, fused=fused)
+        m = self.head_modulation.float() + e.unsqueeze(1)                     # [F, 2, dim]
         d = cfg.dim
-        hn = layer_norm(h, cfg.eps).view(Fr, -1, d).float() * (1 + m[1]) + m[0]
-        out = self.head(hn.to(h.dtype).view(-1, d))
+        if fused and h.is_cuda:
+            hn = ops.adaln(h, eps=cfg.eps, shift=m[:, 0], scale=m[:, 1], frame_tokens=h.shape[0] // Fr)
+        else:
+            hn = (layer_norm(h, cfg.eps).view(Fr, -1, d).float() * (1 + m[:, 1:2]) + m[:, 0:1]).to(h.dtype)
+        out = self.head(hn.view(-1, d))
         return self.unpatchify(out, Fr)
 
 
@@ -332,6 +379,8 @@ class Rollout:
     module for the denoising passes; its ``dense`` switch lists every block for the clean
     context pass. ``sparse=None`` runs the dense model (the unpatched ``attention``).
 
+    ``fused`` selects the library's per-token kernels between the GEMMs (see ``Block.forward``).
+
     ``graphs=True``: the first ``run`` executes eagerly (it also warms up the libraries); from
     the second on, every model call (one chunk, one phase: 30 layers of GEMMs, norms, cache
     writes, routing and attention) is captured once into a CUDA graph and replayed, so the host
@@ -340,7 +389,8 @@ class Rollout:
     exactly; the cross-attention K/V and the inputs live in static buffers.
     """
 
-    def __init__(self, model: CausalWanDiT, sparse=None, scheduler: FlowMatch | None = None, graphs: bool = False):
+    def __init__(self, model: CausalWanDiT, sparse=None, scheduler: FlowMatch | None = None, graphs: bool = False,
+                 fused: bool = True):
         self.model = model
         self.cfg = model.cfg
         self.sparse = sparse
@@ -353,6 +403,7 @@ class Rollout:
         self.device = dev
         self._rope = {}
         self.graphs = graphs
+        self.fused = fused
         self._runs = 0
         self._graph = {}          # (start_frame, frames, phase) -> (graph, x_in, t_in, flow_out)
         self._pool = None
@@ -423,7 +474,7 @@ class Rollout:
         """One model call on latents x [C, F, Hl, Wl] (any float dtype) -> flow prediction."""
         model = self.model
         if not use_graphs:
-            return model.forward_chunk(x.to(torch.bfloat16), t, self.caches, cross, c0, rope)
+            return model.forward_chunk(x.to(torch.bfloat16), t, self.caches, cross, c0, rope, fused=self.fused)
         key = (c0, nf, phase)
         ent = self._graph.get(key)
         if ent is None:
@@ -435,7 +486,7 @@ class Rollout:
                 self._pool = torch.cuda.graph_pool_handle()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, pool=self._pool):
-                flow = model.forward_chunk(x_in, t_in, self.caches, cross, c0, rope)
+                flow = model.forward_chunk(x_in, t_in, self.caches, cross, c0, rope, fused=self.fused)
             ent = self._graph[key] = (g, x_in, t_in, flow)
         g, x_in, t_in, flow = ent
         x_in.copy_(x)

@@ -138,3 +138,21 @@ def test_rollout_graph_replay_matches_eager():
     assert torch.equal(captured, replayed)
     assert (captured - eager).abs().max() < 1e-2
     ro.release_graphs()
+
+
+@pytest.mark.gpu
+def test_rollout_fused_kernels_match_torch_layer():
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+
+    dev = torch.device("cuda:0")
+    m = R.build_model(TINY, device=dev)
+    g = torch.Generator(device=dev)
+    noise = torch.randn(TINY.frames, 16, 16, 16, device=dev, generator=g.manual_seed(3))
+    text = torch.randn(10, TINY.text_dim, device=dev, generator=g.manual_seed(4))
+    wq, wk = init_router_weights(TINY.num_heads, device=dev)
+    outs = []
+    for fused in (False, True):
+        sp = SparseAttention(wq, wk, RouterConfig(density=1.0))
+        outs.append(R.Rollout(m, sparse=sp, fused=fused).run(noise, text, generator=g.manual_seed(5)))
+    err = (outs[0] - outs[1]).abs()
+    assert err.max() < 0.15 and err.mean() < 5e-3, (err.max().item(), err.mean().item())
