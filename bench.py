@@ -11,6 +11,10 @@ N>1 runs under torchrun: every rank processes its own stream (weak scaling, no c
 the data path); ``value`` is the sum over ranks of effective FLOPs / the slowest rank's time.
 ``--impl reference`` times the CPU restatement of the reference's path (oracle/) on the host
 cores, rank 0 only.
+
+The line also carries ``rollout`` (config 3, unless ``--no-rollout``): latent frames/s of one
+Self-Forcing rollout stream per GPU through a random-init Wan-1.3B DiT with the plugin in every
+self-attention layer, next to the same model with dense attention.
 """
 from __future__ import annotations
 
@@ -265,6 +269,75 @@ def cache_append_bench(dev, inputs, args):
                     "(chunk, cache) pairs larger than L2; CUDA-graph replay"}
 
 
+def rollout_bench(dev, args, world: int):
+    """Config 3: one Self-Forcing rollout stream per GPU (21 latent frames = 7 chunks x (4 denoising
+    + 1 clean pass) x 30 layers of a random-init Wan-1.3B DiT), the sparse plugin (25% density) in
+    every self-attention layer, CUDA-graph replay per (chunk, phase). Timed region per rollout:
+    pinned-host noise and text -> device, the rollout, latents -> pinned host. Streams are
+    independent (weak scaling); the time is the max over ranks. The same model with dense
+    attention (scaled-dot-product, no plugin) is timed beside it."""
+    import torch.distributed as dist
+    from streaming_sparse_b200 import rollout as R
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+
+    cfg = R.WanConfig()
+    rank = dist.get_rank() if world > 1 else 0
+    model = R.build_model(cfg, device=dev, seed=0)
+    g = torch.Generator(device="cpu").manual_seed(100 + rank)
+    noise_h = torch.randn((cfg.frames, cfg.in_dim, cfg.latent_h, cfg.latent_w), generator=g).pin_memory()
+    text_h = torch.randn((cfg.text_len, cfg.text_dim), generator=g).pin_memory()
+    out_h = torch.empty_like(noise_h).pin_memory()
+    noise_d, text_d = torch.empty_like(noise_h, device=dev), torch.empty_like(text_h, device=dev)
+    wq, wk = init_router_weights(cfg.num_heads, device=dev)
+    dg = torch.Generator(device=dev)
+    res = {}
+    for name, sparse in (("sparse", SparseAttention(wq, wk, RouterConfig(density=DENSITY))), ("dense", None)):
+        ro = R.Rollout(model, sparse=sparse, graphs=True)
+
+        def once():
+            noise_d.copy_(noise_h, non_blocking=True)
+            text_d.copy_(text_h, non_blocking=True)
+            out = ro.run(noise_d, text_d, generator=dg.manual_seed(7))
+            out_h.copy_(out, non_blocking=True)
+
+        for _ in range(2):      # eager warm-up, then capture of every (chunk, phase) graph
+            once()
+        torch.cuda.synchronize()
+        reps = max(1, min(3, args.steps // 50))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            once()
+        b.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ok = bool(torch.isfinite(out_h).all())
+        res[name] = (float(ms), ok)
+        ro.release_graphs()
+        del ro
+    del model
+    torch.cuda.empty_cache()
+    ms_s, ok_s = res["sparse"]
+    ms_d, ok_d = res["dense"]
+    frames = cfg.frames * world
+    return {"metric": "latent frames/s (config 3 rollout, all streams)", "value": frames / (ms_s * 1e-3),
+            "unit": "frames/s", "streams": world, "frames_per_stream": cfg.frames, "ms_per_rollout": ms_s,
+            "dense_value": frames / (ms_d * 1e-3), "dense_ms_per_rollout": ms_d, "speedup_vs_dense": ms_d / ms_s,
+            "finite": ok_s and ok_d, "reps": reps,
+            "h2d_bytes_per_rollout": noise_h.numel() * 4 + text_h.numel() * 4,
+            "d2h_bytes_per_rollout": out_h.numel() * 4,
+            "model": "random-init Wan-1.3B causal DiT (30 blocks, dim 1536, 12 heads, FFN 8960), bf16",
+            "note": "7 chunks x 3 latent frames (60x104), 4 denoising steps + 1 clean pass per chunk, global "
+                    "KV cache 32760 tokens, text 512 x 4096 N(0,1); routed at 25% density in the denoising "
+                    "passes, dense (every block) in the clean pass; dense_value: same model with "
+                    "scaled-dot-product attention; timed region includes host<->device copies"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch.distributed as dist
     from streaming_sparse_b200 import ops
@@ -389,6 +462,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # ---- cache append (the chunk write of config 2 into a 32760-token window), HBM-bound
     cache = cache_append_bench(dev, sets[0], args)
 
+    # ---- config 3: streaming rollout of the DiT with the plugin in every layer (latent frames/s)
+    rollout = None
+    if not args.no_rollout:
+        rollout = rollout_bench(dev, args, world)
+
     if rank != 0:
         return
     peak, hbm, peak_kind = peaks()
@@ -415,6 +493,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output"},
         "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
+        "rollout": rollout,
         "gpu_launches": 4 * args.steps,
         "clocks": clk.summary(),
     }
@@ -430,6 +509,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-pairs", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-rollout", action="store_true", help="skip the config-3 rollout measurement")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
