@@ -519,3 +519,88 @@ def model_flops_per_call(cfg: WanConfig, Lk: int, attended_per_query: float | No
 __all__ = ["WanConfig", "FlowMatch", "CausalWanDiT", "Rollout", "build_model", "attention", "dense_attention",
            "apply_rope",
            "rope_angles", "rope_tables", "sinusoidal_embedding", "model_flops_per_call"]
+
+
+def main(argv=None):
+    """python -m streaming_sparse_b200.rollout [--density D | --dense] [--profile] ...
+
+    Times full rollouts of one stream on cuda:0 (CUDA-graph replay after a warm-up), or with
+    --profile prints the per-kernel GPU time (torch profiler) of one denoising and one clean call
+    of the last chunk, after a rollout has filled the cache.
+    """
+    import argparse
+    import time
+
+    from .plugin import RouterConfig, SparseAttention, SparsePlugin, init_router_weights
+
+    ap = argparse.ArgumentParser(prog="python -m streaming_sparse_b200.rollout")
+    ap.add_argument("--density", type=float, default=0.25)
+    ap.add_argument("--dense", action="store_true", help="no plugin: dense attention everywhere")
+    ap.add_argument("--unfused", action="store_true", help="PyTorch per-token ops instead of csrc/dit.cu")
+    ap.add_argument("--layers", type=int, default=30)
+    ap.add_argument("--frames", type=int, default=21)
+    ap.add_argument("--runs", type=int, default=2)
+    ap.add_argument("--profile", action="store_true")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda:0")
+    cfg = WanConfig(num_layers=a.layers, frames=a.frames, cache_frames=a.frames)
+    model = build_model(cfg, device=dev)
+    g = torch.Generator(device=dev)
+    noise = torch.randn(cfg.frames, cfg.in_dim, cfg.latent_h, cfg.latent_w, device=dev, generator=g.manual_seed(0))
+    text = torch.randn(cfg.text_len, cfg.text_dim, device=dev, generator=g.manual_seed(1))
+    sparse = None
+    if not a.dense:
+        wq, wk = init_router_weights(cfg.num_heads, device=dev)
+        sparse = SparseAttention(wq, wk, RouterConfig(density=a.density))
+    fused = not a.unfused
+    if a.profile:
+        from torch.profiler import ProfilerActivity, profile
+
+        ro = Rollout(model, sparse=sparse, fused=fused)
+        ro.run(noise, text, generator=g.manual_seed(2))
+        c0 = cfg.frames - cfg.frames_per_chunk
+        ctx = model.embed_text(text.bfloat16())
+        cross = [b.cross_kv(ctx) for b in model.blocks]
+        x = noise[c0:].transpose(0, 1).bfloat16()
+        rope = ro.rope(c0, cfg.frames_per_chunk)
+        import sys
+        plugin = SparsePlugin(sparse, target=sys.modules[__name__]) if sparse is not None else None
+        if plugin is not None:
+            plugin.__enter__()
+        try:
+            with torch.no_grad():
+                for phase in ("denoise", "clean"):
+                    if sparse is not None:
+                        sparse.dense = phase == "clean"
+                    t = 0.0 if phase == "clean" else ro.sched.denoising[1]
+                    model.forward_chunk(x, t, ro.caches, cross, c0, rope, fused=fused)
+                    torch.cuda.synchronize()
+                    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                        model.forward_chunk(x, t, ro.caches, cross, c0, rope, fused=fused)
+                        torch.cuda.synchronize()
+                    print(f"== {phase} call, chunk at frame {c0}, window {ro.caches[0].local_end} tokens")
+                    print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=16,
+                                                    max_name_column_width=60))
+        finally:
+            if plugin is not None:
+                plugin.__exit__(None, None, None)
+        return
+    ro = Rollout(model, sparse=sparse, graphs=True, fused=fused)
+    for _ in range(2):
+        ro.run(noise, text, generator=g.manual_seed(2))
+    torch.cuda.synchronize()
+    for _ in range(a.runs):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        e0.record()
+        out = ro.run(noise, text, generator=g.manual_seed(2))
+        e1.record()
+        w1 = time.perf_counter()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        print(f"rollout {cfg.frames} frames: {ms:.1f} ms GPU, {1e3 * (w1 - w0):.1f} ms host enqueue, "
+              f"{cfg.frames / (ms * 1e-3):.2f} latent frames/s, finite={bool(torch.isfinite(out).all())}")
+
+
+if __name__ == "__main__":
+    main()
