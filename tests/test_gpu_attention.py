@@ -93,6 +93,52 @@ def test_attention_config2_sampled(oracle):
     assert np.isfinite(out).all()
 
 
+def test_attention_config4_routed_sampled(oracle):
+    """Config 4 shape: 128-token router blocks, a one-frame sink, 10 % of the unforced blocks;
+    router bit-exact to the oracle, attention checked on sampled query blocks."""
+    from streaming_sparse_b200 import ops
+    Lq, Lk, H, block, sink = 4680, 34320, 4, 128, 1560
+    kb = ops.nblocks(Lk, block)
+    nf = ops.forced_count(Lq, Lk, block, sink)
+    extra = (kb - nf) // 10
+    assert (kb, nf, extra) == (269, 51, 21)
+    q, k, v = qkv(4, Lq, Lk, H)
+    wq, wk = router_weights(4, H)
+    ids = ops.route(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), block=block, extra=extra, sink_tokens=sink,
+                    validate=True)
+    ids_np = ids.cpu().numpy()
+    r = oracle.route(np32(q), np32(k), wq.numpy(), wk.numpy(), block, extra, sink_tokens=sink)
+    np.testing.assert_array_equal(ids_np, r["ids"])
+    out, lse = _attend(q, k, v, ids_np, block)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, block, heads=[0, 3], qblocks=[0, 17, 36])
+    assert_attention_close(out, ref)
+    m = np.isfinite(ref_lse)
+    np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
+
+
+@pytest.mark.parametrize("block,density", [(64, 0.5), (128, 0.05)])
+def test_attention_config5_longest_window_sampled(oracle, block, density):
+    """Config 5's longest window (63 latent frames, 98280 tokens) at the sweep's densest and
+    sparsest points; routed lists from the GPU router, attention on sampled query blocks."""
+    from streaming_sparse_b200 import ops
+    Lq, Lk, H = 4680, 98280, 2
+    kb = ops.nblocks(Lk, block)
+    nf = ops.forced_count(Lq, Lk, block)
+    extra = ops.budget(kb, nf, density=density)
+    q, k, v = qkv(5, Lq, Lk, H)
+    wq, wk = router_weights(5, H)
+    ids = ops.route(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), block=block, extra=extra, validate=True)
+    ids_np = ids.cpu().numpy()
+    assert ids_np.shape[-1] == nf + extra
+    out, lse = _attend(q, k, v, ids_np, block)
+    qbs = ops.nblocks(Lq, block)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, block, heads=[0, 1],
+                                    qblocks=[0, qbs // 2, qbs - 1])
+    assert_attention_close(out, ref)
+    m = np.isfinite(ref_lse)
+    np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
+
+
 def test_all_selected_equals_sdpa():
     """Every block listed == dense attention (local_experiments/review_v1/test_ops.py:19-23)."""
     Lq, Lk, H = 192, 700, 2
