@@ -235,6 +235,76 @@ __global__ void __launch_bounds__(1024) rms_norm_kernel(const __nv_bfloat16 *__r
     *reinterpret_cast<uint4 *>(out + row * d + t * VEC) = pack8(o);
 }
 
+// The same LayerNorm + modulation / affine with one warp per row, for rows of d = 256 * NV
+// (lane l holds vectors l, l + 32, ...; butterfly reductions, no shared memory or block barrier).
+template <int NV>
+__global__ void __launch_bounds__(256) adaln_warp_kernel(const __nv_bfloat16 *__restrict__ x, int n, int frame_tokens,
+                                                         const float *__restrict__ shift,
+                                                         const float *__restrict__ scale, int64_t mod_ld,
+                                                         const __nv_bfloat16 *__restrict__ weight,
+                                                         const __nv_bfloat16 *__restrict__ bias, float eps,
+                                                         __nv_bfloat16 *__restrict__ out) {
+    constexpr int d = 256 * NV;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    float v[NV][VEC];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        unpack8(*reinterpret_cast<const uint4 *>(x + row * d + (k * 32 + lane) * VEC), v[k]);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) s = __fadd_rn(s, v[k][i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = __fdiv_rn(s, (float)d);
+    float s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            const float c = __fsub_rn(v[k][i], mean);
+            s2 = __fadd_rn(s2, __fmul_rn(c, c));
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(s2, (float)d), eps));
+    const int64_t f = weight ? 0 : row / frame_tokens;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int c0 = (k * 32 + lane) * VEC;
+        float o[VEC];
+        if (weight) {
+            float w[VEC], b[VEC];
+            unpack8(*reinterpret_cast<const uint4 *>(weight + c0), w);
+            unpack8(*reinterpret_cast<const uint4 *>(bias + c0), b);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i)
+                o[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[k][i], mean), rstd), w[i]), b[i]);
+        } else {
+            const float4 *sh = reinterpret_cast<const float4 *>(shift + f * mod_ld + c0);
+            const float4 *sc = reinterpret_cast<const float4 *>(scale + f * mod_ld + c0);
+            const float4 a0 = sh[0], a1 = sh[1], g0 = sc[0], g1 = sc[1];
+            const float shv[VEC] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float scv[VEC] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                const float y = round_bf16(__fmul_rn(__fsub_rn(v[k][i], mean), rstd));
+                o[i] = __fadd_rn(__fmul_rn(y, __fadd_rn(1.f, scv[i])), shv[i]);
+            }
+        }
+        *reinterpret_cast<uint4 *>(out + row * d + c0) = pack8(o);
+    }
+}
+
+template <int NV>
+static void launch_adaln_warp(const __nv_bfloat16 *x, int n, int frame_tokens, const float *shift, const float *scale,
+                              int64_t mod_ld, const __nv_bfloat16 *w, const __nv_bfloat16 *b, float eps,
+                              __nv_bfloat16 *out, cudaStream_t st) {
+    adaln_warp_kernel<NV><<<(n + 7) / 8, 256, 0, st>>>(x, n, frame_tokens, shift, scale, mod_ld, w, b, eps, out);
+}
+
 static bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
 static int row_threads(int d) { return ((d / VEC + 31) / 32) * 32; }
@@ -277,6 +347,23 @@ extern "C" int ss_adaln(const void *x, int n, int d, int frame_tokens, const flo
         (modulate && (dit::misaligned(shift) || dit::misaligned(scale))))
         return SS_ERR_POINTER;
     if (n == 0) return 0;
+    {
+        const auto *xb = static_cast<const __nv_bfloat16 *>(x);
+        const auto *wb = static_cast<const __nv_bfloat16 *>(weight);
+        const auto *bb = static_cast<const __nv_bfloat16 *>(bias);
+        auto *ob = static_cast<__nv_bfloat16 *>(out);
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        bool warp_rows = true;   // rows of 256 * NV: one warp per row
+        switch (d) {
+            case 256: dit::launch_adaln_warp<1>(xb, n, frame_tokens, shift, scale, mod_ld, wb, bb, eps, ob, st); break;
+            case 512: dit::launch_adaln_warp<2>(xb, n, frame_tokens, shift, scale, mod_ld, wb, bb, eps, ob, st); break;
+            case 1024: dit::launch_adaln_warp<4>(xb, n, frame_tokens, shift, scale, mod_ld, wb, bb, eps, ob, st); break;
+            case 1536: dit::launch_adaln_warp<6>(xb, n, frame_tokens, shift, scale, mod_ld, wb, bb, eps, ob, st); break;
+            case 2048: dit::launch_adaln_warp<8>(xb, n, frame_tokens, shift, scale, mod_ld, wb, bb, eps, ob, st); break;
+            default: warp_rows = false;
+        }
+        if (warp_rows) return (int)cudaGetLastError();
+    }
     dit::adaln_kernel<<<n, dit::row_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16 *>(x), d, frame_tokens, shift, scale, mod_ld,
         static_cast<const __nv_bfloat16 *>(weight), static_cast<const __nv_bfloat16 *>(bias), eps,

@@ -238,7 +238,10 @@ class Block(nn.Module):
         ops.gate_residual(x, self.co(y.reshape(n, d)))
 
         h = ops.adaln(x, eps=cfg.eps, shift=em[:, 3], scale=em[:, 4], frame_tokens=ft)
-        ops.gate_residual(x, self.ffn2(F.gelu(self.ffn1(h), approximate="tanh")), gate=em[:, 5], frame_tokens=ft)
+        # bias + tanh-GELU in the GEMM's epilogue (cuBLASLt GELU_BIAS; checked against
+        # F.gelu(approximate="tanh") in tests/test_gpu_dit.py)
+        f1 = torch._addmm_activation(self.ffn1.bias, h, self.ffn1.weight.t(), use_gelu=True)
+        ops.gate_residual(x, self.ffn2(f1), gate=em[:, 5], frame_tokens=ft)
         return x
 
     def _forward_torch(self, x, e0, rope, cache: KVCache, cross, current_start: int):
