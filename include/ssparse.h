@@ -32,6 +32,9 @@
  *   ss_cache_append<- the cache roll + write in CausalWanSelfAttention.forward
  *                     (wan/modules/causal_model.py:216-246) and commit_fixed15
  *                     (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:453-458)
+ *   ss_cache_rope_shift <- the anchor rebase shift_temporal_ (local_experiments/anchor_rebase.py:8-18)
+ *                     as applied to the cache's first frame by set_phase
+ *                     (reproduction/vbench_current/phase.py:4-9)
  *   ss_qkv_norm_rope <- the fused projection hook project_cached_rotary
  *                     (wan/modules/causal_model.py:116-128, 241-246; local_experiments/
  *                     video_runtime_v1/rms_mean.py:38-72): q/k RMSNorm + RoPE, k/v into the cache
@@ -165,6 +168,15 @@ int ss_cache_append(void *k_cache, void *v_cache, int cap, int H,
                     int local_attn, int64_t global_end, int64_t local_end,
                     int64_t current_start, int sink_tokens, int64_t *out_local_end,
                     void *stream);
+
+/* Rotate the first `pairs` complex pairs (elements 2p, 2p+1) of every head of rows [0, n) of a
+ * key tensor [n][H][128] bf16 by phase[p] = (cos, sin) (float64 [pairs][2], device memory):
+ * float64 products and sums, then double -> float -> bf16. src rows at stride src_ld elements,
+ * dst rows at dst_ld; dst may equal src (in place); when it does not, the rows are copied first
+ * so the other pairs come through unchanged. Used to re-rotate a snapshot of the anchor (sink)
+ * frame's keys to a new temporal position. */
+int ss_cache_rope_shift(const void *src, int64_t src_ld, void *dst, int64_t dst_ld, int n, int H,
+                        int pairs, const double *phase, void *stream);
 
 /* ---- per-token kernels of the DiT layer around the attention (one CTA per token row) ---- */
 

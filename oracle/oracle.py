@@ -19,6 +19,8 @@ Pieces and the reference code each one restates (paths inside jurky123/streaming
   P parts (migration/unified_router/opt21/attention.py:7-15).
 * ``cache_append``: the roll + write of CausalWanSelfAttention.forward
   (wan/modules/causal_model.py:216-253).
+* ``rope_shift``: the anchor rebase ``shift_temporal_`` (local_experiments/anchor_rebase.py:8-18):
+  the temporal RoPE pairs of the first tokens rotated by a frame offset in float64.
 
 Parity pins: tests/golden/ holds vectors produced by the reference's own pure-torch functions
 (script ``tests/golden/make_golden.py``); ``tests/test_oracle.py`` checks this module against
@@ -248,3 +250,33 @@ def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end
     k_cache[start:new_local_end] = k_new
     v_cache[start:new_local_end] = v_new
     return new_local_end
+
+
+# ----------------------------------------------------------------------------------------------
+
+def rope_phase(offset: int, pairs: int = 22, head_dim: int = 128) -> np.ndarray:
+    """[pairs, 2] float64 (cos, sin) of offset * theta_p, theta_p = 10000^(-2p / (head_dim - 4*(head_dim//6))):
+    the temporal part of the model's RoPE table (wan/modules/model.py:29-37 rope_params with the
+    split of causal_model.py:500-505), row `offset`."""
+    n = head_dim - 4 * (head_dim // 6)
+    theta = 1.0 / np.power(10000.0, np.arange(0, n, 2, dtype=np.float64) / n)
+    ang = offset * theta[:pairs]
+    return np.stack([np.cos(ang), np.sin(ang)], axis=-1)
+
+
+def rope_shift(keys: np.ndarray, tokens: int, phase: np.ndarray) -> np.ndarray:
+    """keys [..., T, H, D] (bf16 values as float32) -> copy with the first `tokens` rows' first
+    `pairs` complex pairs multiplied by phase (float64), rounded to float32 then bf16, as
+    ``shift_temporal_`` does (local_experiments/anchor_rebase.py:8-18; the double -> bf16 cast
+    goes through float). Spatial pairs and later rows are unchanged."""
+    out = np.array(keys, dtype=np.float32, copy=True)
+    pairs = phase.shape[0]
+    part = out[..., :tokens, :, :2 * pairs].astype(np.float64)
+    x, y = part[..., 0::2], part[..., 1::2]
+    c, s = phase[:, 0], phase[:, 1]
+    re = x * c - y * s
+    im = x * s + y * c
+    rot = np.empty_like(part)
+    rot[..., 0::2], rot[..., 1::2] = re, im
+    out[..., :tokens, :, :2 * pairs] = bf16_round(rot.astype(np.float32))
+    return out

@@ -36,6 +36,7 @@ SIGNATURES = {
     "ss_attention_max_ids": ([_I, _I, ctypes.POINTER(_I)], _I),
     "ss_lse_merge": ([_P, _P, _I, _I, _I, _P, _I, _P, _P], _I),
     "ss_cache_append": ([_P, _P, _I, _I, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _I, ctypes.POINTER(_I64), _P], _I),
+    "ss_cache_rope_shift": ([_P, _I64, _P, _I64, _I, _I, _I, _P, _P], _I),
     "ss_qkv_norm_rope": ([_P, _I64, _I, _I, _P, _P, _F, _P, _P, _P, _I64, _P, _P, _I64, _P], _I),
     "ss_adaln": ([_P, _I, _I, _I, _P, _P, _I64, _P, _P, _F, _P, _P], _I),
     "ss_rms_norm": ([_P, _I64, _I, _I, _P, _F, _P, _P], _I),

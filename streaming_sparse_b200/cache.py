@@ -6,6 +6,13 @@ chunk write with the rolling-window semantics of CausalWanSelfAttention.forward
 (wan/modules/causal_model.py:216-253) through ``ss_cache_append``. The index state is mirrored
 on the host, so no device->host read is needed per call (the reference calls ``.item()``).
 
+Snapshots: ``snapshot``/``restore`` copy a layer's whole state (K/V rows and the index state) on
+the device, so a stream can be forked or rewound. ``save_anchor``/``rebase_anchor`` keep a
+canonical copy of the anchor (sink) frame's keys and rewrite the cache's anchor rows with their
+temporal RoPE pairs rotated to a new frame position -- the reference's long-horizon "anchor
+rebase" (``set_phase``, reproduction/vbench_current/phase.py:4-9, with ``shift_temporal_``,
+local_experiments/anchor_rebase.py:8-18), through ``ss_cache_rope_shift``.
+
 ``PositionTracker`` restates the adapter's absolute-position bookkeeping
 (streaming_sparse/integration/self_forcing_adapter.py:50-97): the absolute token index held in
 every cache slot through roll/evict, and the positions of the visible window.
@@ -15,7 +22,18 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .ops import cache_append
+from .ops import cache_append, rope_shift
+
+
+def temporal_phase(offset: int, device, head_dim: int = 128) -> torch.Tensor:
+    """(cos, sin) of offset * theta_p for the temporal RoPE pairs, float64 [P, 2] on `device`:
+    row `offset` of the model's RoPE table (wan/modules/model.py:29-37, temporal part of the
+    split in causal_model.py:500-505), built with torch.polar as the reference builds it."""
+    n = head_dim - 4 * (head_dim // 6)
+    theta = 1.0 / torch.pow(10000, torch.arange(0, n, 2, dtype=torch.float64).div(n))
+    ang = float(offset) * theta
+    z = torch.polar(torch.ones_like(ang), ang)
+    return torch.view_as_real(z).contiguous().to(device)
 
 
 class PositionTracker:
@@ -71,6 +89,7 @@ class KVCache:
         self.local_end = 0
         self.positions = PositionTracker(capacity) if track_positions else None
         self.commits = 0
+        self.anchor = None
 
     @property
     def sink_tokens(self) -> int:
@@ -119,6 +138,38 @@ class KVCache:
         self.local_end, self.global_end = local_end, end
         self.commits += 1
         return self.k[0, start:local_end], self.v[0, start:local_end]
+
+    def snapshot(self) -> dict:
+        """Device copy of the K/V rows in use and the index state (see ``restore``)."""
+        n = self.local_end
+        return {"k": self.k[0, :n].clone(), "v": self.v[0, :n].clone(), "global_end": self.global_end,
+                "local_end": self.local_end, "commits": self.commits,
+                "positions": None if self.positions is None else self.positions.flat.copy()}
+
+    def restore(self, snap: dict) -> None:
+        """Put back a ``snapshot`` of this cache (same capacity and heads)."""
+        n = snap["local_end"]
+        self.k[0, :n].copy_(snap["k"])
+        self.v[0, :n].copy_(snap["v"])
+        self.global_end, self.local_end, self.commits = snap["global_end"], n, snap["commits"]
+        if self.positions is not None and snap["positions"] is not None:
+            self.positions.flat[:] = snap["positions"]
+
+    def save_anchor(self, tokens: int | None = None) -> None:
+        """Keep the canonical (unshifted) keys of the first `tokens` rows (default: the sink
+        frames, else one frame)."""
+        t = tokens if tokens is not None else (self.sink_tokens or self.frame_tokens)
+        if t <= 0 or t > self.local_end:
+            raise ValueError("the anchor rows must be written before they are saved")
+        self.anchor = self.k[0, :t].clone()
+
+    def rebase_anchor(self, offset: int) -> None:
+        """Rewrite the anchor rows from the saved canonical keys with their temporal RoPE pairs
+        rotated by `offset` frames (offset 0 restores them as saved)."""
+        if getattr(self, "anchor", None) is None:
+            raise RuntimeError("save_anchor() first")
+        t = self.anchor.shape[0]
+        rope_shift(self.anchor, self.k[0, :t], temporal_phase(offset, self.k.device, self.D))
 
     def window(self):
         """Visible K/V window [Lk,H,D] (views into the cache): the last tokens are the current chunk."""

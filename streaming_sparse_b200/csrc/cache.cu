@@ -46,8 +46,57 @@ static int launch_copy(const void *sk, const void *sv, int64_t src_stride, void 
     return (int)cudaGetLastError();
 }
 
+// Rotation of the first `pairs` complex pairs of every (row, head) by phase[p] = (cos, sin), in
+// float64 with separately rounded products and sums, then double -> float -> bf16 (round to
+// nearest even each time), as the reference's float64 complex multiply and `.to(bfloat16)` do.
+__global__ void __launch_bounds__(256) rope_shift_kernel(const uint32_t *__restrict__ src, int64_t src_ld2,
+                                                         uint32_t *__restrict__ dst, int64_t dst_ld2, int64_t n, int H,
+                                                         int pairs, const double *__restrict__ phase) {
+    const int64_t total = n * H * pairs;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / ((int64_t)H * pairs);
+        const int rem = (int)(i % ((int64_t)H * pairs));
+        const int h = rem / pairs, p = rem % pairs;
+        const uint32_t w = src[r * src_ld2 + h * (D / 2) + p];
+        const double x = (double)__uint_as_float(w << 16), y = (double)__uint_as_float(w & 0xffff0000u);
+        const double c = phase[2 * p], sn = phase[2 * p + 1];
+        const double re = __dsub_rn(__dmul_rn(x, c), __dmul_rn(y, sn));
+        const double im = __dadd_rn(__dmul_rn(x, sn), __dmul_rn(y, c));
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(__double2float_rn(re)));
+        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(__double2float_rn(im)));
+        dst[r * dst_ld2 + h * (D / 2) + p] = lo | (hi << 16);
+    }
+}
+
 }  // namespace cache
 }  // namespace ss
+
+extern "C" int ss_cache_rope_shift(const void *src, int64_t src_ld, void *dst, int64_t dst_ld, int n, int H, int pairs,
+                                   const double *phase, void *stream) {
+    using namespace ss;
+    if (!src || !dst || !phase) return SS_ERR_POINTER;
+    if (n < 0 || H <= 0 || pairs < 0 || pairs > cache::D / 2 || src_ld < (int64_t)H * cache::D ||
+        dst_ld < (int64_t)H * cache::D || (src_ld % 2) || (dst_ld % 2))
+        return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 3u ||
+        (reinterpret_cast<uintptr_t>(phase) & 7u))
+        return SS_ERR_POINTER;
+    // rows the rotation leaves alone are still copied when dst is another buffer
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (src != dst && n > 0) {
+        cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dst_ld * 2, src, (size_t)src_ld * 2, (size_t)H * cache::D * 2,
+                                          (size_t)n, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return (int)e;
+    }
+    const int64_t total = (int64_t)n * H * pairs;
+    if (total == 0) return 0;
+    int sms = 148, dev;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8);
+    cache::rope_shift_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint32_t *>(src), src_ld / 2,
+                                                     static_cast<uint32_t *>(dst), dst_ld / 2, n, H, pairs, phase);
+    return (int)cudaGetLastError();
+}
 
 extern "C" int ss_cache_append(void *k_cache, void *v_cache, int cap, int H, const void *k_new, const void *v_new,
                                int64_t new_stride, int n_new, int local_attn, int64_t global_end, int64_t local_end,

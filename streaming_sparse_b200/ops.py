@@ -300,6 +300,23 @@ def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end
     return new_end.value
 
 
+def rope_shift(src: torch.Tensor, dst: torch.Tensor, phase: torch.Tensor) -> torch.Tensor:
+    """dst = src with the first P complex pairs of every head rotated by phase [P, 2] float64
+    (cos, sin) on the device (`ss_cache_rope_shift`). src/dst [n, H, 128] bf16 (rows may be
+    strided; dst may be src). The anchor rebase of local_experiments/anchor_rebase.py:8-18."""
+    for name, t in (("src", src), ("dst", dst)):
+        _require(t.is_cuda and t.dtype == torch.bfloat16 and t.dim() == 3 and t.shape[-1] == HEAD_DIM and
+                 t.stride(2) == 1 and t.stride(1) == HEAD_DIM, f"{name}: bf16 CUDA [n, H, 128] rows")
+    _require(src.shape == dst.shape, "src and dst must have the same shape")
+    _require(phase.is_cuda and phase.dtype == torch.float64 and phase.is_contiguous() and phase.dim() == 2 and
+             phase.shape[1] == 2, "phase: float64 CUDA [P, 2]")
+    n, H, _ = src.shape
+    rc = lib().ss_cache_rope_shift(_p(src), src.stride(0), _p(dst), dst.stride(0), n, H, phase.shape[0], _p(phase),
+                                   _stream(src.device))
+    check(rc, "ss_cache_rope_shift")
+    return dst
+
+
 # ----------------------------------------------------------------------------------------------
 # per-token kernels of the DiT layer around the attention (csrc/dit.cu), used by the rollout
 # ----------------------------------------------------------------------------------------------
@@ -392,7 +409,7 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None
 
 __all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "sparse_attention", "exact",
            "attention_max_ids", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
-           "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
+           "rope_shift", "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
 
 # keep the status-bit names importable from here
 DEV_BITS = dict(nonfinite=DEV_NONFINITE, timeout=DEV_TIMEOUT, badid=DEV_BADID)

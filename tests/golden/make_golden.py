@@ -16,6 +16,11 @@ committed). Each fixture names the reference function that produced it:
 * merge_vr1.npz       local_experiments/video_runtime_v1/attention.py:40-45 ``merge``.
 * positions_adapter.npz  streaming_sparse/integration/self_forcing_adapter.py:50-97 ``_pre``
                       (absolute position of every visible cache slot through roll/evict).
+* anchor_rebase.npz   local_experiments/anchor_rebase.py:8-18 ``shift_temporal_`` (temporal RoPE
+                      pairs of the anchor frame rotated by a frame offset, float64, back to bf16),
+                      with the RoPE table built as wan/modules/model.py:29-37 ``rope_params``
+                      concatenated as causal_model.py:500-505 (``wan`` itself is not importable
+                      here, so the table is rebuilt from that formula).
 """
 import argparse
 import inspect
@@ -164,6 +169,27 @@ def positions_case(SelfForcingAdapter):
     np.savez_compressed(os.path.join(OUT, "positions_adapter.npz"), **cases)
 
 
+def anchor_rebase_case(shift_temporal_):
+    d = 128
+
+    def rope_params(max_seq_len, dim, theta=10000):
+        freqs = torch.outer(torch.arange(max_seq_len),
+                            1.0 / torch.pow(theta, torch.arange(0, dim, 2).to(torch.float64).div(dim)))
+        return torch.polar(torch.ones_like(freqs), freqs)
+
+    freqs = torch.cat([rope_params(1024, d - 4 * (d // 6)), rope_params(1024, 2 * (d // 6)),
+                       rope_params(1024, 2 * (d // 6))], dim=1)
+    g = torch.Generator().manual_seed(909)
+    keys = (3 * torch.randn(2, 64, 2, d, generator=g)).bfloat16()
+    bits = lambda t: t.view(torch.int16).numpy()   # bf16 bit patterns
+    cases = {"keys": bits(keys)}
+    for offset, tokens in ((0, 64), (1, 64), (3, 0), (15, 40), (42, 64), (1023, 64)):
+        k = keys.clone()
+        shift_temporal_(k, tokens, freqs, offset)
+        cases[f"out_{offset}_{tokens}"] = bits(k)
+    np.savez_compressed(os.path.join(OUT, "anchor_rebase.npz"), **cases)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -174,6 +200,7 @@ def main():
     from local_experiments.review_v1.ops import RouteOps, Config
     from local_experiments.video_runtime_v1.attention import merge
     from streaming_sparse.integration.self_forcing_adapter import SelfForcingAdapter
+    from local_experiments.anchor_rebase import shift_temporal_
     assert "kv_cache" in inspect.signature(_FakeAttention.forward).parameters
     torch.set_num_threads(4)
     select_cases(select)
@@ -181,6 +208,7 @@ def main():
     padded_ids_case(RouteOps, Config)
     merge_case(merge)
     positions_case(SelfForcingAdapter)
+    anchor_rebase_case(shift_temporal_)
     for f in sorted(os.listdir(OUT)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(OUT, f)))

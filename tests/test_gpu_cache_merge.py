@@ -95,3 +95,53 @@ def test_split_blocks_then_merge_equals_whole(oracle):
         lses.append(l)
     merged = ops.lse_merge(torch.stack(parts), torch.stack(lses), out_dtype=torch.float32)
     torch.testing.assert_close(merged, whole, rtol=2e-3, atol=2e-3)
+
+
+def _bf16_bits(a):
+    return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+
+
+def test_rope_shift_matches_reference_fixture(golden):
+    """ss_cache_rope_shift == the reference's shift_temporal_ (anchor_rebase.npz), bit for bit."""
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.cache import temporal_phase
+    g = golden("anchor_rebase.npz")
+    keys = _bf16_bits(g["keys"]).cuda()                       # [2, 64, 2, 128]
+    for name in g.files:
+        if not name.startswith("out_"):
+            continue
+        _, offset, tokens = name.split("_")
+        t = int(tokens)
+        out = keys.clone()
+        for layer in range(keys.shape[0]):
+            if t:
+                ops.rope_shift(keys[layer, :t], out[layer, :t], temporal_phase(int(offset), "cuda"))
+        exp = _bf16_bits(g[name])
+        assert torch.equal(out.cpu().view(torch.int16), exp.view(torch.int16)), name
+
+
+def test_anchor_rebase_and_snapshot_restore():
+    from streaming_sparse_b200.cache import KVCache
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(5)
+    c = KVCache(64 * 8, 2, 128, frame_tokens=64, local_attn_size=6, sink_size=1, device=dev)
+    for start in range(0, 64 * 6, 64):
+        k = torch.randn(64, 2, 128, device=dev, generator=g).bfloat16()
+        c.append(k, k.neg(), start)
+    snap = c.snapshot()
+    c.save_anchor()
+    canonical = c.anchor.clone()
+    assert canonical.shape[0] == 64                      # the sink frame
+    c.rebase_anchor(9)
+    moved = c.k[0, :64].clone()
+    assert not torch.equal(moved, canonical)
+    assert torch.equal(moved[..., 44:], canonical[..., 44:])   # spatial pairs untouched
+    c.rebase_anchor(0)
+    assert torch.equal(c.k[0, :64], canonical)
+    # one more chunk, then restore brings back the rows and the index state
+    k = torch.randn(64, 2, 128, device=dev, generator=g).bfloat16()
+    c.append(k, k, 64 * 6)
+    assert c.global_end == 64 * 7
+    c.restore(snap)
+    assert (c.global_end, c.local_end) == (snap["global_end"], snap["local_end"])
+    assert torch.equal(c.k[0, :c.local_end], snap["k"]) and torch.equal(c.v[0, :c.local_end], snap["v"])

@@ -160,3 +160,25 @@ def test_router_pooling_is_exact_fp32_order(oracle):
         np.testing.assert_array_equal(pooled[0, b], s / np.float32(t1 - t0))
     # fma order: compare with float64 accumulation loosely, exact equality is checked on the GPU
     np.testing.assert_allclose(proj[0], pooled[0].astype(np.float64) @ w[0], rtol=1e-4, atol=1e-5)
+
+
+def _bf16_bits_to_f32(a):
+    return (a.astype(np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_rope_shift_matches_reference_anchor_rebase(oracle, golden):
+    """local_experiments/anchor_rebase.py:8-18 shift_temporal_: bit for bit, every case."""
+    g = golden("anchor_rebase.npz")
+    keys = _bf16_bits_to_f32(g["keys"])
+    for name in g.files:
+        if not name.startswith("out_"):
+            continue
+        _, offset, tokens = name.split("_")
+        got = oracle.rope_shift(keys, int(tokens), oracle.rope_phase(int(offset)))
+        np.testing.assert_array_equal(got.view(np.uint32), _bf16_bits_to_f32(g[name]).view(np.uint32), err_msg=name)
+
+
+def test_temporal_phase_table_matches_oracle(oracle):
+    from streaming_sparse_b200.cache import temporal_phase
+    for off in (0, 1, 15, 1023):
+        np.testing.assert_allclose(temporal_phase(off, "cpu").numpy(), oracle.rope_phase(off), rtol=0, atol=1e-15)
