@@ -14,7 +14,8 @@ cores, rank 0 only.
 
 The line also carries ``rollout`` (config 3, unless ``--no-rollout``): latent frames/s of one
 Self-Forcing rollout stream per GPU through a random-init Wan-1.3B DiT with the plugin in every
-self-attention layer, next to the same model with dense attention.
+self-attention layer, next to the same model with dense attention; and ``other_configs`` (unless
+``--no-configs``): router + attention at the shapes of configs 1, 4 and a grid of config 5.
 """
 from __future__ import annotations
 
@@ -269,6 +270,69 @@ def cache_append_bench(dev, inputs, args):
                     "(chunk, cache) pairs larger than L2; CUDA-graph replay"}
 
 
+def configs_bench(dev, args):
+    """Router + attention at the other shapes of the reference's configs, one graph replay per
+    timed step with a 256 MB L2 flush between steps: config 1, config 4 (128-token blocks, a
+    one-frame sink, 10 % of the unforced blocks) and a grid of config 5's sweep (window 2..21 frames
+    of 4680 tokens and 98280, densities 5/25/50 %, blocks 64 and 128). Seeded N(0,1) inputs."""
+    from streaming_sparse_b200 import ops
+
+    pts = [("config1", 1560, 6240, 64, 0, dict(topk=24)),
+           ("config4", 4680, 34320, 128, 1560, dict(density=0.10, rule="rest"))]
+    for lk in (9360, 65520, 98280):
+        for dens in (0.05, 0.25, 0.5):
+            pts.append((f"config5 Lk={lk} d={dens:g} b=64", 4680, lk, 64, 0, dict(density=dens)))
+    for dens in (0.05, 0.5):
+        pts.append((f"config5 Lk=98280 d={dens:g} b=128", 4680, 98280, 128, 0, dict(density=dens)))
+    peak, _, _ = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(55)
+    out = []
+    reps = max(5, min(20, args.steps // 10))
+    for name, lq, lk, block, sink, rule in pts:
+        q = torch.randn((lq, H, D), device=dev, generator=g).bfloat16()
+        k = torch.randn((lk, H, D), device=dev, generator=g).bfloat16()
+        v = torch.randn((lk, H, D), device=dev, generator=g).bfloat16()
+        wq = torch.randn((H, D, 64), device=dev, generator=g) / math.sqrt(D)
+        wk = torch.randn((H, D, 64), device=dev, generator=g) / math.sqrt(D)
+        kb = ops.nblocks(lk, block)
+        nf = ops.forced_count(lq, lk, block, sink)
+        extra = ops.budget(kb, nf, **rule)
+        ws = ops.Workspace()
+        ids = torch.empty((H, ops.nblocks(lq, block), nf + extra), dtype=torch.int32, device=dev)
+        o = torch.empty_like(q)
+
+        def step():
+            ops.route(q, k, wq, wk, block=block, extra=extra, sink_tokens=sink, workspace=ws, out=ids)
+            ops.sparse_attention(q, k, v, ids, block=block, out=o)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        ops.DeviceStatus.check(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step()
+        ms = []
+        for _ in range(reps):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            gr.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms.append(a.elapsed_time(b))
+        us = 1e3 * statistics.median(ms)
+        fl = effective_flops(ids.cpu().numpy(), lq, lk, block)
+        out.append({"name": name, "Lq": lq, "Lk": lk, "block": block, "sink_tokens": sink, "blocks_per_query_block":
+                    nf + extra, "us": us, "effective_gflop": fl / 1e9, "tflops": fl / (us * 1e-6) / 1e12,
+                    "frac_of_peak": fl / (us * 1e-6) / 1e12 / peak})
+        del gr, q, k, v, ids, o, ws
+    del flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def rollout_bench(dev, args, world: int):
     """Config 3: one Self-Forcing rollout stream per GPU (21 latent frames = 7 chunks x (4 denoising
     + 1 clean pass) x 30 layers of a random-init Wan-1.3B DiT), the sparse plugin (25% density) in
@@ -466,6 +530,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     rollout = None
     if not args.no_rollout:
         rollout = rollout_bench(dev, args, world)
+    # ---- the other configs' shapes (router + attention, per shape)
+    other = None if args.no_configs else configs_bench(dev, args)
 
     if rank != 0:
         return
@@ -494,6 +560,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output"},
         "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
         "rollout": rollout,
+        "other_configs": other,
         "gpu_launches": 4 * args.steps,
         "clocks": clk.summary(),
     }
@@ -510,6 +577,7 @@ def main():
     ap.add_argument("--ref-pairs", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rollout", action="store_true", help="skip the config-3 rollout measurement")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-shape measurements of configs 1, 4, 5")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
