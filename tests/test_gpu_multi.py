@@ -1,0 +1,83 @@
+"""The multi-GPU layouts on real GPUs: NCCL ranks (one process per GPU, spawned), KV-block sharding
+with the LSE merge and head sharding with the all_gather, each against the single-GPU result.
+Skipped where fewer than two GPUs are visible."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LQ, LK, H = 1024, 8192, 4
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _inputs():
+    from helpers import qkv, router_weights
+    q, k, v = qkv(31, LQ, LK, H)
+    wq, wk = router_weights(31, H)
+    return q, k, v, wq, wk
+
+
+def _worker(rank, world, port, q_out):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        from streaming_sparse_b200.distributed import HeadShardedAttention, KVShardedAttention, head_shard
+        from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
+        q, k, v, wq, wk = (t.to(dev) for t in _inputs())
+        cfg = RouterConfig(density=0.25)
+        kv = KVShardedAttention(SparseAttention(wq, wk, cfg))(q[None], k[None], v[None])
+        hs = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg),
+                                  H)(head_shard(q, rank, world), head_shard(k, rank, world), head_shard(v, rank, world))
+        torch.cuda.synchronize()
+        q_out.put((rank, kv.float().cpu().numpy(), hs.float().cpu().numpy()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:   # report to the parent instead of hanging it
+        q_out.put((rank, repr(e), None))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
+    import torch.multiprocessing as mp
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
+    from helpers import assert_attention_close
+
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        rank, kv, hs = q_out.get(timeout=240)
+        results[rank] = (kv, hs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, (kv, hs) in results.items():
+        assert not isinstance(kv, str), f"rank {rank}: {kv}"
+    # the single-GPU path, same inputs
+    dev = torch.device("cuda:0")
+    q, k, v, wq, wk = (t.to(dev) for t in _inputs())
+    whole = SparseAttention(wq, wk, RouterConfig(density=0.25))(q[None], k[None], v[None])[0].float().cpu().numpy()
+    for rank, (kv, hs) in results.items():
+        assert_attention_close(kv, whole)                       # KV-block shards merged by LSE
+        np.testing.assert_array_equal(hs, whole)               # heads are independent: identical bits
