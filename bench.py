@@ -389,6 +389,7 @@ def rollout_bench(dev, args, world: int):
     ms_s, ok_s = res["sparse"]
     ms_d, ok_d = res["dense"]
     frames = cfg.frames * world
+    c4 = rollout4_bench(dev, args) if world == 1 else None
     return {"metric": "latent frames/s (config 3 rollout, all streams)", "value": frames / (ms_s * 1e-3),
             "unit": "frames/s", "streams": world, "frames_per_stream": cfg.frames, "ms_per_rollout": ms_s,
             "dense_value": frames / (ms_d * 1e-3), "dense_ms_per_rollout": ms_d, "speedup_vs_dense": ms_d / ms_s,
@@ -399,7 +400,42 @@ def rollout_bench(dev, args, world: int):
             "note": "7 chunks x 3 latent frames (60x104), 4 denoising steps + 1 clean pass per chunk, global "
                     "KV cache 32760 tokens, text 512 x 4096 N(0,1); routed at 25% density in the denoising "
                     "passes, dense (every block) in the clean pass; dense_value: same model with "
-                    "scaled-dot-product attention; timed region includes host<->device copies"}
+                    "scaled-dot-product attention; timed region includes host<->device copies",
+            "config4_long_horizon": c4}
+
+
+def rollout4_bench(dev, args):
+    """Config 4's stream on one GPU: 120 latent frames in 40 chunks through a rolling window of 21
+    frames + 1 sink frame (34320 tokens), 128-token router blocks at 10 % of the unforced blocks;
+    the window rolls on every chunk's first call from chunk 7 on. One timed rollout after an eager
+    warm-up and a capture run (routed only; the dense model is timed by
+    `python -m streaming_sparse_b200.rollout --config4 --dense`)."""
+    from streaming_sparse_b200 import rollout as R
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+
+    cfg = R.WanConfig(frames=120, cache_frames=22, local_attn_frames=22, sink_frames=1)
+    model = R.build_model(cfg, device=dev, seed=0)
+    g = torch.Generator(device=dev)
+    noise = torch.randn((cfg.frames, cfg.in_dim, cfg.latent_h, cfg.latent_w), device=dev, generator=g.manual_seed(3))
+    text = torch.randn((cfg.text_len, cfg.text_dim), device=dev, generator=g.manual_seed(4))
+    wq, wk = init_router_weights(cfg.num_heads, device=dev)
+    sp = SparseAttention(wq, wk, RouterConfig(block=128, density=0.10, rule="rest", sink_tokens=cfg.frame_tokens))
+    ro = R.Rollout(model, sparse=sp, graphs=True)
+    for _ in range(2):
+        ro.run(noise, text, generator=g.manual_seed(5))
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    out = ro.run(noise, text, generator=g.manual_seed(5))
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    res = {"value": cfg.frames / (ms * 1e-3), "unit": "frames/s", "ms_per_rollout": ms, "frames": cfg.frames,
+           "graphs": len(ro._graph), "finite": bool(torch.isfinite(out).all())}
+    ro.release_graphs()
+    del ro, model
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_ours(args, rank: int, world: int, local_rank: int):

@@ -101,20 +101,43 @@ class KVCache:
         return {"k": self.k, "v": self.v, "global_end_index": torch.tensor([self.global_end], device=dev),
                 "local_end_index": torch.tensor([self.local_end], device=dev)}
 
-    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, current_start: int):
-        """Write a chunk (post-RoPE K, V: [n,H,D] or [1,n,H,D]); returns (visible positions, history)."""
-        n = k_new.shape[-3]
-        local_attn = self.local_attn_size != -1
+    def _rolls(self, n: int, current_start: int) -> bool:
+        end = current_start + n
+        return self.local_attn_size != -1 and end > self.global_end and n + self.local_end > self.capacity
+
+    def write_plan(self, n: int, current_start: int) -> tuple[bool, int, int]:
+        """(rolls, evicted tokens, local end after) of writing n tokens at current_start."""
+        end = current_start + n
+        rolls = self._rolls(n, current_start)
+        evicted = n + self.local_end - self.capacity if rolls else 0
+        return rolls, evicted, self.local_end + end - self.global_end - evicted
+
+    def advance(self, n: int, current_start: int):
+        """Host-side index update of one chunk write (what ``append`` does besides the copy);
+        for a caller whose write already happened on the device (a replayed CUDA graph).
+        Returns (visible positions, history) when positions are tracked."""
         vis = None
         if self.positions is not None:
             vis = self.positions.update(start=current_start, n=n, old_global=self.global_end, old_local=self.local_end,
-                                        local_attn=local_attn, sink_tokens=self.sink_tokens,
+                                        local_attn=self.local_attn_size != -1, sink_tokens=self.sink_tokens,
                                         max_attention_size=self.max_attention_size)
-        new_end = cache_append(self.k, self.v, k_new, v_new, local_attn=local_attn, global_end=self.global_end,
-                               local_end=self.local_end, current_start=current_start, sink_tokens=self.sink_tokens)
-        self.local_end = new_end
-        self.global_end = current_start + n
+        end = current_start + n
+        _, _, local_end = self.write_plan(n, current_start)
+        if local_end - n < 0 or local_end > self.capacity:
+            raise ValueError("Invalid KV cache bounds; reduce length or use local attention")
+        self.local_end, self.global_end = local_end, end
         self.commits += 1
+        return vis
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, current_start: int):
+        """Write a chunk (post-RoPE K, V: [n,H,D] or [1,n,H,D]); returns (visible positions, history)."""
+        n = k_new.shape[-3]
+        old_global, old_local = self.global_end, self.local_end
+        vis = self.advance(n, current_start)
+        new_end = cache_append(self.k, self.v, k_new, v_new, local_attn=self.local_attn_size != -1,
+                               global_end=old_global, local_end=old_local, current_start=current_start,
+                               sink_tokens=self.sink_tokens)
+        assert new_end == self.local_end
         return vis
 
     def reserve(self, n: int, current_start: int):
@@ -124,20 +147,10 @@ class KVCache:
         ``append`` would, when the write needs no roll of the window; returns None (state
         unchanged) when it does, in which case the caller writes through ``append``.
         """
-        end = current_start + n
-        if self.local_attn_size != -1 and end > self.global_end and n + self.local_end > self.capacity:
+        if self._rolls(n, current_start):
             return None
-        if self.positions is not None:
-            self.positions.update(start=current_start, n=n, old_global=self.global_end, old_local=self.local_end,
-                                  local_attn=self.local_attn_size != -1, sink_tokens=self.sink_tokens,
-                                  max_attention_size=self.max_attention_size)
-        local_end = self.local_end + end - self.global_end
-        start = local_end - n
-        if start < 0 or local_end > self.capacity:
-            raise ValueError("Invalid KV cache bounds; reduce length or use local attention")
-        self.local_end, self.global_end = local_end, end
-        self.commits += 1
-        return self.k[0, start:local_end], self.v[0, start:local_end]
+        self.advance(n, current_start)
+        return self.k[0, self.local_end - n:self.local_end], self.v[0, self.local_end - n:self.local_end]
 
     def snapshot(self) -> dict:
         """Device copy of the K/V rows in use and the index state (see ``restore``)."""

@@ -64,7 +64,9 @@ class WanConfig:
     latent_w: int = 104
     frames: int = 21              # latent frames generated per rollout
     frames_per_chunk: int = 3
-    cache_frames: int = 21        # KV cache capacity in frames (global attention: no eviction)
+    cache_frames: int = 21        # KV cache capacity in frames
+    local_attn_frames: int = -1   # rolling window in frames (-1: global cache, no eviction)
+    sink_frames: int = 0          # frames kept at the front when the window rolls
 
     @property
     def frame_tokens(self) -> int:
@@ -387,9 +389,12 @@ class Rollout:
     ``graphs=True``: the first ``run`` executes eagerly (it also warms up the libraries); from
     the second on, every model call (one chunk, one phase: 30 layers of GEMMs, norms, cache
     writes, routing and attention) is captured once into a CUDA graph and replayed, so the host
-    enqueues one launch per call instead of ~1500. Within a rollout every call of a chunk writes
-    the same cache slots (global cache, no eviction), so a graph replays that chunk's writes
-    exactly; the cross-attention K/V and the inputs live in static buffers.
+    enqueues one launch per call instead of ~1500. A call's device work is fixed by its shape,
+    phase and cache write plan (whether the window rolls, by how much, where the chunk ends), so
+    graphs are keyed by those: the calls of a chunk that rewrite the same rows share a graph, and
+    with a rolling window (``local_attn_frames``) every steady-state chunk reuses the same three
+    (rolling first call, later calls, clean pass). The cross-attention K/V, the inputs and the
+    RoPE tables live in static buffers.
     """
 
     def __init__(self, model: CausalWanDiT, sparse=None, scheduler: FlowMatch | None = None, graphs: bool = False,
@@ -401,7 +406,8 @@ class Rollout:
         dev = next(model.parameters()).device
         cfg = self.cfg
         self.caches = [KVCache(cfg.cache_frames * cfg.frame_tokens, cfg.num_heads, HEAD_DIM,
-                               frame_tokens=cfg.frame_tokens, device=dev, track_positions=False)
+                               frame_tokens=cfg.frame_tokens, local_attn_size=cfg.local_attn_frames,
+                               sink_size=cfg.sink_frames, device=dev, track_positions=False)
                        for _ in range(cfg.num_layers)]
         self.device = dev
         self._rope = {}
@@ -411,6 +417,7 @@ class Rollout:
         self._graph = {}          # (start_frame, frames, phase) -> (graph, x_in, t_in, flow_out)
         self._pool = None
         self._cross = None        # static cross-attention K/V per layer
+        self._rope_in = {}        # frames -> static (cos, sin) buffers read by the graphs
 
     def reset(self):
         for c in self.caches:
@@ -478,8 +485,18 @@ class Rollout:
         model = self.model
         if not use_graphs:
             return model.forward_chunk(x.to(torch.bfloat16), t, self.caches, cross, c0, rope, fused=self.fused)
-        key = (c0, nf, phase)
+        # A call's device work is fixed by its shape, phase and the caches' index state (where
+        # the chunk lands, whether the window rolls); the RoPE table comes through a static
+        # buffer. So one graph serves every call with the same key -- with a rolling window, every
+        # steady-state chunk -- and the host index mirrors are advanced after each replay.
+        start = c0 * self.cfg.frame_tokens
+        key = (nf, phase) + self.caches[0].write_plan(x.shape[1] * self.cfg.frame_tokens, start)
         ent = self._graph.get(key)
+        if nf not in self._rope_in:
+            self._rope_in[nf] = (torch.empty_like(rope[0]), torch.empty_like(rope[1]))
+        rope_in = self._rope_in[nf]
+        rope_in[0].copy_(rope[0])
+        rope_in[1].copy_(rope[1])
         if ent is None:
             x_in = torch.empty(x.shape, device=self.device, dtype=torch.bfloat16)
             t_in = torch.zeros(1, device=self.device, dtype=torch.float64)
@@ -488,18 +505,26 @@ class Rollout:
             if self._pool is None:
                 self._pool = torch.cuda.graph_pool_handle()
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, pool=self._pool):
-                flow = model.forward_chunk(x_in, t_in, self.caches, cross, c0, rope, fused=self.fused)
+            with torch.cuda.graph(g, pool=self._pool):   # the host mirrors advance here, once
+                flow = model.forward_chunk(x_in, t_in, self.caches, cross, c0, rope_in, fused=self.fused)
             ent = self._graph[key] = (g, x_in, t_in, flow)
+            advance = False
+        else:
+            advance = True
         g, x_in, t_in, flow = ent
         x_in.copy_(x)
         t_in.fill_(t)
         g.replay()
+        if advance:
+            n = x.shape[1] * self.cfg.frame_tokens
+            for cache in self.caches:
+                cache.advance(n, start)
         return flow
 
     def release_graphs(self):
         self._graph.clear()
         self._pool = None
+        self._rope_in.clear()
 
 
 def build_model(cfg: WanConfig = WanConfig(), device="cuda", seed: int = 0) -> CausalWanDiT:
@@ -537,6 +562,9 @@ def main(argv=None):
     from .plugin import RouterConfig, SparseAttention, SparsePlugin, init_router_weights
 
     ap = argparse.ArgumentParser(prog="python -m streaming_sparse_b200.rollout")
+    ap.add_argument("--config4", action="store_true",
+                    help="config 4's long-horizon stream: 120 frames, 21-frame window + 1 sink frame, "
+                         "128-token router blocks at 10%% of the unforced blocks")
     ap.add_argument("--density", type=float, default=0.25)
     ap.add_argument("--dense", action="store_true", help="no plugin: dense attention everywhere")
     ap.add_argument("--unfused", action="store_true", help="PyTorch per-token ops instead of csrc/dit.cu")
@@ -546,7 +574,12 @@ def main(argv=None):
     ap.add_argument("--profile", action="store_true")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
-    cfg = WanConfig(num_layers=a.layers, frames=a.frames, cache_frames=a.frames)
+    if a.config4:
+        cfg = WanConfig(num_layers=a.layers, frames=120, cache_frames=22, local_attn_frames=22, sink_frames=1)
+        rcfg = RouterConfig(block=128, density=0.10, rule="rest", sink_tokens=cfg.frame_tokens)
+    else:
+        cfg = WanConfig(num_layers=a.layers, frames=a.frames, cache_frames=a.frames)
+        rcfg = RouterConfig(density=a.density)
     model = build_model(cfg, device=dev)
     g = torch.Generator(device=dev)
     noise = torch.randn(cfg.frames, cfg.in_dim, cfg.latent_h, cfg.latent_w, device=dev, generator=g.manual_seed(0))
@@ -554,7 +587,7 @@ def main(argv=None):
     sparse = None
     if not a.dense:
         wq, wk = init_router_weights(cfg.num_heads, device=dev)
-        sparse = SparseAttention(wq, wk, RouterConfig(density=a.density))
+        sparse = SparseAttention(wq, wk, rcfg)
     fused = not a.unfused
     if a.profile:
         from torch.profiler import ProfilerActivity, profile

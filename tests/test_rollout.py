@@ -156,3 +156,37 @@ def test_rollout_fused_kernels_match_torch_layer():
         outs.append(R.Rollout(m, sparse=sp, fused=fused).run(noise, text, generator=g.manual_seed(5)))
     err = (outs[0] - outs[1]).abs()
     assert err.max() < 0.15 and err.mean() < 5e-3, (err.max().item(), err.mean().item())
+
+
+TINY_WINDOW = R.WanConfig(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_dim=64, text_len=16, latent_h=16,
+                          latent_w=16, frames=15, cache_frames=7, local_attn_frames=7, sink_frames=1)
+
+
+@pytest.mark.gpu
+def test_rolling_window_rollout_graphs_match_eager():
+    """A rolling window with a sink frame (config 4's cache policy, small): chunks from the third
+    on roll the window; graphs keyed by the write plan replay every roll and write exactly."""
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+
+    dev = torch.device("cuda:0")
+    cfg = TINY_WINDOW
+    m = R.build_model(cfg, device=dev)
+    g = torch.Generator(device=dev)
+    noise = torch.randn(cfg.frames, 16, 16, 16, device=dev, generator=g.manual_seed(3))
+    text = torch.randn(10, cfg.text_dim, device=dev, generator=g.manual_seed(4))
+    wq, wk = init_router_weights(cfg.num_heads, device=dev)
+    sp = SparseAttention(wq, wk, RouterConfig(density=0.5, sink_tokens=cfg.frame_tokens))
+    ro = R.Rollout(m, sparse=sp, graphs=True)
+    eager = ro.run(noise, text, generator=g.manual_seed(5))
+    state = [(c.global_end, c.local_end) for c in ro.caches]
+    k_eager = ro.caches[1].k.clone()
+    captured = ro.run(noise, text, generator=g.manual_seed(5))
+    replayed = ro.run(noise, text, generator=g.manual_seed(5))
+    assert [(c.global_end, c.local_end) for c in ro.caches] == state == [(cfg.frames * 64, 7 * 64)] * 2
+    assert torch.equal(captured, replayed)
+    assert (captured - eager).abs().max() < 1e-2
+    assert (ro.caches[1].k - k_eager).abs().max() < 1e-2
+    # chunks 0 and 1 fill the window, chunk 2 rolls from a partial window, chunks 3-4 share the
+    # steady-state graphs: (roll, rewrite, clean) x 1 + per-chunk (first, clean) x 2 + 3 + ...
+    assert len(ro._graph) < 3 * math.ceil(cfg.frames / cfg.frames_per_chunk)
+    ro.release_graphs()
