@@ -162,6 +162,9 @@ class KVCache:
     def restore(self, snap: dict) -> None:
         """Put back a ``snapshot`` of this cache (same capacity and heads)."""
         n = snap["local_end"]
+        if not (0 <= n <= self.capacity and tuple(snap["k"].shape) == (n, self.H, self.D) and
+                snap["v"].shape == snap["k"].shape):
+            raise ValueError("snapshot does not match this cache's geometry")
         self.k[0, :n].copy_(snap["k"])
         self.v[0, :n].copy_(snap["v"])
         self.global_end, self.local_end, self.commits = snap["global_end"], n, snap["commits"]

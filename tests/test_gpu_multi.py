@@ -67,11 +67,16 @@ def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
     for p in procs:
         p.start()
     results = {}
-    for _ in procs:
-        rank, kv, hs = q_out.get(timeout=240)
-        results[rank] = (kv, hs)
-    for p in procs:
-        p.join(timeout=60)
+    try:
+        for _ in procs:
+            rank, kv, hs = q_out.get(timeout=240)
+            results[rank] = (kv, hs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():      # a rank that never reported: end it rather than leave it running
+                p.terminate()
+                p.join(timeout=30)
     for rank, (kv, hs) in results.items():
         assert not isinstance(kv, str), f"rank {rank}: {kv}"
     # the single-GPU path, same inputs
