@@ -190,3 +190,26 @@ def test_rolling_window_rollout_graphs_match_eager():
     # steady-state graphs: (roll, rewrite, clean) x 1 + per-chunk (first, clean) x 2 + 3 + ...
     assert len(ro._graph) < 3 * math.ceil(cfg.frames / cfg.frames_per_chunk)
     ro.release_graphs()
+
+
+@pytest.mark.gpu
+def test_rollout_with_a_short_last_chunk():
+    """7 frames in chunks of 3: the last chunk has one frame (its own RoPE table, graphs and a
+    64-token query chunk); graph replay equals the eager run."""
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+
+    dev = torch.device("cuda:0")
+    cfg = R.WanConfig(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_dim=64, text_len=16, latent_h=16,
+                      latent_w=16, frames=7, cache_frames=7)
+    m = R.build_model(cfg, device=dev)
+    g = torch.Generator(device=dev)
+    noise = torch.randn(cfg.frames, 16, 16, 16, device=dev, generator=g.manual_seed(3))
+    text = torch.randn(10, cfg.text_dim, device=dev, generator=g.manual_seed(4))
+    wq, wk = init_router_weights(cfg.num_heads, device=dev)
+    ro = R.Rollout(m, sparse=SparseAttention(wq, wk, RouterConfig(density=0.5)), graphs=True)
+    eager = ro.run(noise, text, generator=g.manual_seed(5))
+    ro.run(noise, text, generator=g.manual_seed(5))
+    replayed = ro.run(noise, text, generator=g.manual_seed(5))
+    assert torch.isfinite(eager).all() and ro.caches[0].local_end == 7 * 64
+    assert (replayed - eager).abs().max() < 1e-2
+    ro.release_graphs()
