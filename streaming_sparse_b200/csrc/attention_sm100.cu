@@ -419,6 +419,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             load_q(p, t0 / p.ntiles, (t0 % p.ntiles) * 128 + r, wg, qv);
             tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
             tmem_wait_st();
+            tmem_st_fence32(reinterpret_cast<const float *>(qv));
             tc_fence_before();
             mbar_arrive(bar(Q_FULL));
         }
@@ -439,6 +440,10 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 const bool sel0 = (st.x >> (27 + half)) & 1u, sel1 = (st.y >> (27 + half)) & 1u;
                 const int v0 = sel0 ? e_valid(st.x) : 0, v1 = sel1 ? e_valid(st.y) : 0;
                 tmem_wait_ld();
+                tmem_ld_fence32(s);
+                tmem_ld_fence32(s + 32);
+                tmem_ld_fence32(s + 64);
+                tmem_ld_fence32(s + 96);
                 tc_fence_before();
                 mbar_arrive(bar(S_FREE + wg));       // the next QK may overwrite S
                 float mx = -INFINITY;
@@ -497,9 +502,12 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                         float o[32];
                         tmem_ld32(o_addr + 32 * c, o);
                         tmem_wait_ld();
+                        tmem_ld_fence32(o);
 #pragma unroll
                         for (int x = 0; x < 32; ++x) o[x] *= (grow ? alpha : 1.f);
                         tmem_st32(o_addr + 32 * c, o);
+                        tmem_wait_st();            // o is reloaded by the next chunk
+                        tmem_st_fence32(o);
                     }
                 }
                 // P = 2^(s*sl2 - m) as bf16 pairs, all on MUFU ex2: measured on B200, moving a
@@ -545,6 +553,8 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 tmem_st32(p_addr, reinterpret_cast<const float *>(pk));
                 tmem_st32(p_addr + 32, reinterpret_cast<const float *>(pk + 32));
                 tmem_wait_st();
+                tmem_st_fence32(reinterpret_cast<const float *>(pk));
+                tmem_st_fence32(reinterpret_cast<const float *>(pk + 32));
                 tc_fence_before();
                 mbar_arrive(bar(P_FULL + wg));
             }
@@ -582,6 +592,8 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 tmem_ld32(o_self + 64 * wg + 32 * c, o);
                 tmem_ld32(o_oth + 64 * wg + 32 * c, t);
                 tmem_wait_ld();
+                tmem_ld_fence32(o);
+                tmem_ld_fence32(t);
 #pragma unroll
                 for (int x = 0; x < 32; ++x)
                     res[32 * c + x] = ((a_s > 0.f ? o[x] * a_s : 0.f) + (a_o > 0.f ? t[x] * a_o : 0.f)) * inv;
@@ -594,6 +606,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 load_q(p, tn / p.ntiles, (tn % p.ntiles) * 128 + r, wg, qv);
                 tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
                 tmem_wait_st();
+                tmem_st_fence32(reinterpret_cast<const float *>(qv));
                 tc_fence_before();
                 mbar_arrive(bar(Q_FULL));
             }

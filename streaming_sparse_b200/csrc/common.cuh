@@ -154,6 +154,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
+// tcgen05.ld writes its destination registers asynchronously: they hold the loaded values only
+// after tcgen05.wait::ld. The compiler does not know that, and may read those registers -- or
+// spill them to local memory -- anywhere after the load instruction. Call this on every 32-register
+// block loaded by tmem_ld32, after tmem_wait_ld(): it claims to rewrite the registers, so no use of
+// them can be placed before it (asm volatile statements keep their order).
+__device__ __forceinline__ void tmem_ld_fence32(float *v) {
+    uint32_t *r = reinterpret_cast<uint32_t *>(v);
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+// tcgen05.st reads its source registers asynchronously, until tcgen05.wait::st; the compiler
+// does not know that and may reuse (or reload from a spill slot into) those registers right
+// after the store instruction. Call this on every 32-register block stored by tmem_st32, after
+// tmem_wait_st(): it reads the registers, so they keep their values until the wait is past.
+__device__ __forceinline__ void tmem_st_fence32(const float *v) {
+    const uint32_t *r = reinterpret_cast<const uint32_t *>(v);
+    asm volatile("" ::"r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+                 "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+                 "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+                 "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
     const uint32_t *r = reinterpret_cast<const uint32_t *>(v);
     asm volatile(
