@@ -182,3 +182,34 @@ def test_temporal_phase_table_matches_oracle(oracle):
     from streaming_sparse_b200.cache import temporal_phase
     for off in (0, 1, 15, 1023):
         np.testing.assert_allclose(temporal_phase(off, "cpu").numpy(), oracle.rope_phase(off), rtol=0, atol=1e-15)
+
+
+def test_cache_index_plan_matches_oracle_roll(oracle):
+    """KVCache.write_plan/advance (host-only index arithmetic, which keys the rollout's graphs)
+    against the oracle's restatement of the cache roll + write, over random chunk sequences with
+    rewrites of the same chunk and rolling windows with sink frames."""
+    import numpy as np
+    from streaming_sparse_b200.cache import KVCache
+    rng = np.random.default_rng(5)
+    for local, sink, ft in [(-1, 0, 8), (6, 1, 8), (5, 2, 4), (4, 0, 16)]:
+        cap = (local if local > 0 else 12) * ft
+        c = KVCache(cap, 1, 128, frame_tokens=ft, local_attn_size=local, sink_size=sink, device="cpu",
+                    track_positions=False)
+        kc = np.zeros((cap, 1, 1), np.float32)
+        vc = np.zeros((cap, 1, 1), np.float32)
+        g_end, l_end, start = 0, 0, 0
+        total = 0
+        while total < (3 * cap if local > 0 else cap - 3 * ft):
+            n = int(rng.integers(1, 3)) * ft
+            for rep in range(int(rng.integers(1, 4))):          # the same chunk written 1-3 times
+                new = np.full((n, 1, 1), start + rep, np.float32)
+                rolls, evicted, end_after = c.write_plan(n, start)
+                l_ref = oracle.cache_append(kc, vc, new, new, local_attn=local != -1, global_end=g_end,
+                                            local_end=l_end, current_start=start, sink_tokens=sink * ft)
+                assert end_after == l_ref
+                assert rolls == (evicted > 0) and (rolls == (local != -1 and start + n > g_end and n + l_end > cap))
+                c.advance(n, start)
+                g_end, l_end = start + n, l_ref
+                assert (c.global_end, c.local_end) == (g_end, l_end)
+            start += n
+            total += n
