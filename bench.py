@@ -625,7 +625,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
         "rollout": rollout,
         "other_configs": other,
-        "gpu_launches": 4 * args.steps,
+        # per timed step: the router graph (pool_project + score_select) and the attention graph
+        "gpu_launches": 3 * args.steps,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
