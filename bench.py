@@ -15,7 +15,8 @@ cores, rank 0 only.
 The line also carries ``rollout`` (config 3, unless ``--no-rollout``): latent frames/s of one
 Self-Forcing rollout stream per GPU through a random-init Wan-1.3B DiT with the plugin in every
 self-attention layer, next to the same model with dense attention; and ``other_configs`` (unless
-``--no-configs``): router + attention at the shapes of configs 1, 4 and a grid of config 5.
+``--no-configs``): router + attention at the shapes of configs 1, 4 and a grid of config 5; and
+``hbm_kernels``: the rolling cache append, the 8-part LSE merge and the anchor rebase, each alone.
 """
 from __future__ import annotations
 
@@ -228,14 +229,19 @@ def cache_append_bench(dev, inputs, args):
     global cache; algorithmic bytes = chunk read + chunk written, for K and V. Four (chunk, cache)
     pairs rotate, so each append's 57.5 MB come from and go to HBM rather than L2 (4 x 229 MB)."""
     from streaming_sparse_b200 import ops
-    _, k, v, _, _ = inputs
     start = LK - LQ
+    if inputs is not None:
+        _, k, v, _, _ = inputs
+        k, v = k[start:], v[start:]
+    else:
+        k = torch.randn((LQ, H, D), device=dev).to(torch.bfloat16)
+        v = torch.randn((LQ, H, D), device=dev).to(torch.bfloat16)
     pairs = []
     for r in range(4):
         kc = torch.zeros((LK, H, D), dtype=torch.bfloat16, device=dev)
         vc = torch.zeros_like(kc)
-        kn = torch.roll(k[start:], r, 0).contiguous()
-        vn = torch.roll(v[start:], r, 0).contiguous()
+        kn = torch.roll(k, r, 0).contiguous()
+        vn = torch.roll(v, r, 0).contiguous()
         pairs.append((kc, vc, kn, vn))
 
     def once(i):
@@ -268,6 +274,116 @@ def cache_append_bench(dev, inputs, args):
     return {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
             "note": "chunk of 4680 tokens x 12 heads x 128 (K and V, bf16) read + written; 4 rotating "
                     "(chunk, cache) pairs larger than L2; CUDA-graph replay"}
+
+
+def _graph_us(fn, reps: int, steps: int) -> float:
+    """Mean us per call of fn(i), i = 0..reps-1 captured in one CUDA graph, replayed back to back
+    (eager warm-up first)."""
+    for i in range(reps):
+        fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            fn(i)
+    g.replay()
+    n = max(5, steps // reps)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(n):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return 1e3 * a.elapsed_time(b) / (n * reps)
+
+
+def hbm_kernels_bench(dev, args, hbm_gbs: float) -> dict:
+    """The HBM-bound kernels beside the attention, each timed alone with CUDA events over graph
+    replays, inputs rotating over buffers larger than L2 where the kernel's traffic allows:
+
+    * ``cache_append_roll``: a chunk write into a full rolling window (config 4: 22 frames of
+      1560 tokens with a 1-frame sink, 4680-token chunk): 28080 rows shifted left by 4680 in six
+      copies, then the chunk written; (28080 + 4680) rows x 3 KB x (K, V) read + written.
+    * ``lse_merge_8``: the KV-sharded merge of 8 partial outputs (fp32 [8, 4680, 12, 128] + LSE)
+      into bf16, the combine step of 8-GPU KV-block sharding.
+    * ``anchor_rebase``: one layer's anchor rebase (1560 canonical key rows copied into the
+      cache, their 22 temporal RoPE pairs rotated); L2-resident, so latency-bound.
+    Each is checked once against a torch expression before it is timed."""
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.cache import temporal_phase
+    out = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    row_bytes = H * D * 2
+
+    # ---- rolling append, config-4 window
+    ft, sink, n = 1560, 1560, LQ
+    cap = 22 * ft
+    evicted, rolled = n, cap - n - sink
+    caches = [(torch.randn((cap, H, D), generator=gen, device=dev).to(torch.bfloat16),
+               torch.randn((cap, H, D), generator=gen, device=dev).to(torch.bfloat16)) for _ in range(2)]
+    chunks = [(torch.randn((n, H, D), generator=gen, device=dev).to(torch.bfloat16),
+               torch.randn((n, H, D), generator=gen, device=dev).to(torch.bfloat16)) for _ in range(2)]
+    g_end = 10 * n
+
+    def roll(i):
+        (kc, vc), (kn, vn) = caches[i % 2], chunks[i % 2]
+        ops.cache_append(kc, vc, kn, vn, local_attn=True, global_end=g_end, local_end=cap, current_start=g_end,
+                         sink_tokens=sink)
+
+    kc, vc = caches[0]
+    want_k = torch.cat((kc[:sink], kc[sink + evicted:], chunks[0][0]))
+    want_v = torch.cat((vc[:sink], vc[sink + evicted:], chunks[0][1]))
+    roll(0)
+    torch.cuda.synchronize()
+    assert torch.equal(kc, want_k) and torch.equal(vc, want_v), "rolling append differs from the window roll"
+    del want_k, want_v
+    us = _graph_us(roll, 2, args.steps)
+    nbytes = (rolled + n) * row_bytes * 2 * 2
+    out["cache_append_roll"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
+                                "frac": nbytes / (us * 1e-6) / 1e9 / hbm_gbs, "launches": rolled // evicted + 1}
+    del caches, chunks
+
+    # ---- 8-part LSE merge
+    P = 8
+    parts = [(torch.randn((P, LQ, H, D), generator=gen, device=dev),
+              4.0 * torch.randn((P, H, LQ), generator=gen, device=dev)) for _ in range(2)]
+    o, l = parts[0]
+    ref = (torch.softmax(l, 0).permute(0, 2, 1)[..., None] * o).sum(0)
+    got = ops.lse_merge(o, l, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.allclose(got.float(), ref, atol=2e-2, rtol=1e-2), "lse_merge differs from the softmax-weighted sum"
+    del ref, got
+
+    def merge(i):
+        ops.lse_merge(*parts[i % 2], out_dtype=torch.bfloat16)
+
+    us = _graph_us(merge, 2, args.steps)
+    nbytes = P * LQ * H * D * 4 + P * H * LQ * 4 + LQ * H * D * 2
+    out["lse_merge_8"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
+                          "frac": nbytes / (us * 1e-6) / 1e9 / hbm_gbs}
+    del parts
+
+    # ---- anchor rebase of one layer (canonical rows -> cache rows, temporal pairs rotated)
+    anchor = torch.randn((ft, H, D), generator=gen, device=dev).to(torch.bfloat16)
+    kc = torch.zeros((cap, H, D), dtype=torch.bfloat16, device=dev)
+    phase = temporal_phase(5 * 3, dev, D)
+    ops.rope_shift(anchor, kc[:ft], temporal_phase(0, dev, D))
+    torch.cuda.synchronize()
+    assert torch.equal(kc[:ft], anchor), "a zero-offset rebase must restore the saved rows"
+
+    def rebase(i):
+        ops.rope_shift(anchor, kc[:ft], phase)
+
+    us = _graph_us(rebase, 4, args.steps)
+    pairs = phase.shape[0]
+    nbytes = 2 * ft * row_bytes + 2 * ft * H * pairs * 4
+    out["anchor_rebase"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
+                            "note": "rows copied + temporal pairs rotated in place; L2-resident"}
+    out["hbm_peak_gbs"] = hbm_gbs
+    return out
 
 
 def configs_bench(dev, args):
@@ -447,6 +563,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(dev)
     lib_ok = ops.attention_max_ids(LK, BLOCK) >= 128
     assert lib_ok
+    if args.only_hbm_kernels:   # the cache / merge kernels alone (e.g. under a profiler), rank 0
+        if rank == 0:
+            _, hbm, _ = peaks()
+            hbm_k = hbm_kernels_bench(dev, args, hbm)   # first: its first 7 copy launches are one rolling append
+            cache = cache_append_bench(dev, None, args)
+            line = {"cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm), "hbm_kernels": hbm_k}
+            print(json.dumps(line), flush=True)
+        return
     sets = [make_inputs(1000 * rank + s, dev) for s in range(2)]
     extra = RouterConfig(density=DENSITY).extra(LQ, LK)
     ws = ops.Workspace()
@@ -588,6 +712,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     # ---- cache append (the chunk write of config 2 into a 32760-token window), HBM-bound
     cache = cache_append_bench(dev, sets[0], args)
+    _, hbm_gbs, _ = peaks()
+    hbm_k = hbm_kernels_bench(dev, args, hbm_gbs)
 
     # ---- config 3: streaming rollout of the DiT with the plugin in every layer (latent frames/s)
     rollout = None
@@ -623,6 +749,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output; "
                 "step i+1's upload overlaps step i (separate copy streams for upload and readback)"},
         "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
+        "hbm_kernels": hbm_k,
         "rollout": rollout,
         "other_configs": other,
         # per timed step: the router graph (pool_project + score_select) and the attention graph
@@ -643,6 +770,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rollout", action="store_true", help="skip the config-3 rollout measurement")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-shape measurements of configs 1, 4, 5")
+    ap.add_argument("--only-hbm-kernels", action="store_true",
+                    help="measure only the cache append / roll, LSE merge and anchor rebase kernels")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -16,18 +16,67 @@ namespace cache {
 
 constexpr int D = 128;
 
-// copy n rows of `row_vec` uint4 each, for two tensors at once (K and V)
+// Copy n rows of `row_vec` uint4 each, for two tensors at once (K and V). A thread takes
+// CP_UNROLL vectors of each tensor (grid-stride apart) and issues all of its loads before its
+// stores, so 2 x CP_UNROLL 16-byte loads per thread are in flight; the sources are read once
+// (evict-first), the destinations stay in L2 for the attention that reads them next. Source and
+// destination ranges of one launch never overlap (the roll moves at most `evicted` rows a launch).
+constexpr int CP_UNROLL = 4;
+
+// Flat form: both sides are contiguous rows (stride == row_vec) and the copy has fewer than 2^31
+// vectors, so vector i sits at offset i on both sides and 32-bit offsets from one base suffice.
+__global__ void __launch_bounds__(256) copy_flat_kernel(const uint4 *__restrict__ src_k, const uint4 *__restrict__ src_v,
+                                                        uint4 *__restrict__ dst_k, uint4 *__restrict__ dst_v,
+                                                        int total) {
+    const int stride = gridDim.x * blockDim.x;
+    for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * CP_UNROLL) {
+        uint4 a[CP_UNROLL], b[CP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < CP_UNROLL; ++u) {
+            const int i = i0 + u * stride;
+            if (i < total) {
+                a[u] = __ldcs(src_k + i);
+                b[u] = __ldcs(src_v + i);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CP_UNROLL; ++u) {
+            const int i = i0 + u * stride;
+            if (i < total) {
+                dst_k[i] = a[u];
+                dst_v[i] = b[u];
+            }
+        }
+    }
+}
+
+// General form: rows of row_vec vectors at independent strides on the two sides.
 __global__ void __launch_bounds__(256) copy_rows_kernel(const uint4 *__restrict__ src_k, const uint4 *__restrict__ src_v,
                                                         int64_t src_stride_vec, uint4 *__restrict__ dst_k,
                                                         uint4 *__restrict__ dst_v, int64_t dst_stride_vec,
                                                         int64_t n, int row_vec) {
     const int64_t total = n * row_vec;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / row_vec, c = i % row_vec;
-        const uint4 a = src_k[r * src_stride_vec + c];
-        const uint4 b = src_v[r * src_stride_vec + c];
-        dst_k[r * dst_stride_vec + c] = a;
-        dst_v[r * dst_stride_vec + c] = b;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * CP_UNROLL) {
+        uint4 a[CP_UNROLL], b[CP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < CP_UNROLL; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < total) {
+                const int64_t s = (i / row_vec) * src_stride_vec + i % row_vec;
+                a[u] = __ldcs(src_k + s);
+                b[u] = __ldcs(src_v + s);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CP_UNROLL; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < total) {
+                const int64_t d = (i / row_vec) * dst_stride_vec + i % row_vec;
+                dst_k[d] = a[u];
+                dst_v[d] = b[u];
+            }
+        }
     }
 }
 
@@ -39,10 +88,23 @@ static int launch_copy(const void *sk, const void *sv, int64_t src_stride, void 
     int sms = 148;
     int dev;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int64_t want = (total + 255) / 256;
-    const unsigned blocks = (unsigned)std::min<int64_t>(want, (int64_t)sms * 8);
-    copy_rows_kernel<<<blocks, 256, 0, st>>>((const uint4 *)sk, (const uint4 *)sv, src_stride / 8, (uint4 *)dk,
-                                            (uint4 *)dv, dst_stride / 8, n, row_vec);
+    const int64_t want = (total + 256 * CP_UNROLL - 1) / (256 * CP_UNROLL);
+    // at most one wave of resident CTAs; the grid-stride loop covers the rest
+    const bool flat = src_stride / 8 == row_vec && dst_stride / 8 == row_vec &&
+                      total < ((int64_t)1 << 31) - (int64_t)sms * 8 * 256 * CP_UNROLL;
+    int per_sm = 0;
+    if (flat)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, copy_flat_kernel, 256, 0);
+    else
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, copy_rows_kernel, 256, 0);
+    per_sm = std::min(std::max(per_sm, 1), 8);
+    const unsigned blocks = (unsigned)std::min<int64_t>(want, (int64_t)sms * per_sm);
+    if (flat)
+        copy_flat_kernel<<<blocks, 256, 0, st>>>((const uint4 *)sk, (const uint4 *)sv, (uint4 *)dk, (uint4 *)dv,
+                                                 (int)total);
+    else
+        copy_rows_kernel<<<blocks, 256, 0, st>>>((const uint4 *)sk, (const uint4 *)sv, src_stride / 8, (uint4 *)dk,
+                                                (uint4 *)dv, dst_stride / 8, n, row_vec);
     return (int)cudaGetLastError();
 }
 

@@ -13,7 +13,12 @@ namespace merge {
 
 constexpr int D = 128;
 
-// one thread per (row, head, 4 consecutive dims)
+// One thread per (row, head, 4 consecutive dims). For up to PMAX parts every part's LSE and
+// float4 are loaded before any is used, so a thread has all of its loads in flight at once (a
+// dependent loop over the parts kept one or two per thread in flight and left DRAM half idle);
+// the parts are read once, so their loads are marked evict-first. PMAX = 0: any P, one part at a
+// time. The arithmetic and its order are the same for every PMAX.
+template <int PMAX>
 __global__ void __launch_bounds__(256) lse_merge_kernel(const float *__restrict__ o, const float *__restrict__ lse,
                                                         int P, int H, int Lq, void *out, int out_fp32,
                                                         float *__restrict__ lse_out) {
@@ -24,19 +29,49 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const float *__restrict_
     const int64_t rh = gid / (D / 4);  // row * H + h
     const int h = (int)(rh % H);
     const int row = (int)(rh / H);
-    float mx = -INFINITY;
-    for (int p = 0; p < P; ++p) mx = fmaxf(mx, lse[((int64_t)p * H + h) * Lq + row]);
+    const float *lp = lse + (int64_t)h * Lq + row;                          // part p at lp[p * H * Lq]
+    const float4 *op = reinterpret_cast<const float4 *>(o + rh * D) + quad;  // part p at op[p * Lq * H * D / 4]
+    const int64_t lstride = (int64_t)H * Lq, ostride = (int64_t)Lq * H * (D / 4);
+    float mx = -INFINITY, wsum = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float wsum = 0.f;
-    if (mx != -INFINITY) {
-        for (int p = 0; p < P; ++p) {
-            const float w = __expf(lse[((int64_t)p * H + h) * Lq + row] - mx);
-            const float4 v = reinterpret_cast<const float4 *>(o + (((int64_t)p * Lq + row) * H + h) * D)[quad];
-            acc.x = fmaf(w, v.x, acc.x);
-            acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z);
-            acc.w = fmaf(w, v.w, acc.w);
-            wsum += w;
+    if constexpr (PMAX > 0) {
+        float l[PMAX];
+        float4 v[PMAX];
+#pragma unroll
+        for (int p = 0; p < PMAX; ++p) {
+            if (p < P) {
+                l[p] = __ldcs(lp + p * lstride);
+                v[p] = __ldcs(op + p * ostride);
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < PMAX; ++p)
+            if (p < P) mx = fmaxf(mx, l[p]);
+        if (mx != -INFINITY) {
+#pragma unroll
+            for (int p = 0; p < PMAX; ++p) {
+                if (p < P) {
+                    const float w = __expf(l[p] - mx);
+                    acc.x = fmaf(w, v[p].x, acc.x);
+                    acc.y = fmaf(w, v[p].y, acc.y);
+                    acc.z = fmaf(w, v[p].z, acc.z);
+                    acc.w = fmaf(w, v[p].w, acc.w);
+                    wsum += w;
+                }
+            }
+        }
+    } else {
+        for (int p = 0; p < P; ++p) mx = fmaxf(mx, lp[p * lstride]);
+        if (mx != -INFINITY) {
+            for (int p = 0; p < P; ++p) {
+                const float w = __expf(lp[p * lstride] - mx);
+                const float4 v = op[p * ostride];
+                acc.x = fmaf(w, v.x, acc.x);
+                acc.y = fmaf(w, v.y, acc.y);
+                acc.z = fmaf(w, v.z, acc.z);
+                acc.w = fmaf(w, v.w, acc.w);
+                wsum += w;
+            }
         }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
@@ -64,7 +99,14 @@ extern "C" int ss_lse_merge(const float *o_parts, const float *lse_parts, int P,
     if ((reinterpret_cast<uintptr_t>(o_parts) | reinterpret_cast<uintptr_t>(out)) & 15u) return SS_ERR_POINTER;
     const int64_t total = (int64_t)Lq * H * (ss::merge::D / 4);
     const unsigned blocks = (unsigned)((total + 255) / 256);
-    ss::merge::lse_merge_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(o_parts, lse_parts, P, H, Lq,
-                                                                                     out, out_dtype, lse_out);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (P <= 2)
+        ss::merge::lse_merge_kernel<2><<<blocks, 256, 0, st>>>(o_parts, lse_parts, P, H, Lq, out, out_dtype, lse_out);
+    else if (P <= 4)
+        ss::merge::lse_merge_kernel<4><<<blocks, 256, 0, st>>>(o_parts, lse_parts, P, H, Lq, out, out_dtype, lse_out);
+    else if (P <= 8)
+        ss::merge::lse_merge_kernel<8><<<blocks, 256, 0, st>>>(o_parts, lse_parts, P, H, Lq, out, out_dtype, lse_out);
+    else
+        ss::merge::lse_merge_kernel<0><<<blocks, 256, 0, st>>>(o_parts, lse_parts, P, H, Lq, out, out_dtype, lse_out);
     return (int)cudaGetLastError();
 }
