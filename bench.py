@@ -15,8 +15,10 @@ cores, rank 0 only.
 The line also carries ``rollout`` (config 3, unless ``--no-rollout``): latent frames/s of one
 Self-Forcing rollout stream per GPU through a random-init Wan-1.3B DiT with the plugin in every
 self-attention layer, next to the same model with dense attention; and ``other_configs`` (unless
-``--no-configs``): router + attention at the shapes of configs 1, 4 and a grid of config 5; and
-``hbm_kernels``: the rolling cache append, the 8-part LSE merge and the anchor rebase, each alone.
+``--no-configs``): router + attention at the shapes of configs 1, 4 and a grid of config 5;
+``hbm_kernels``: the rolling cache append, the 8-part LSE merge and the anchor rebase, each alone;
+``e2e`` (the plugin call with the whole KV window uploaded from the host every step) and
+``e2e_streaming`` (the window resident in a KVCache, only the chunk's q/k/v uploaded per step).
 """
 from __future__ import annotations
 
@@ -554,6 +556,93 @@ def rollout4_bench(dev, args):
     return res
 
 
+def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> dict:
+    """The config-2 chunk-layer as a streaming caller makes it (the reference's per-layer
+    ``self_attn.forward(..., kv_cache, current_start)``, wan/modules/causal_model.py:216-253):
+    the 32760-token window is resident in a ``KVCache`` kept across calls, and every step uploads
+    only the chunk's q, k, v from pinned host memory, writes k/v into the window
+    (``KVCache.append``; a denoising call rewrites its chunk's rows, no roll), routes and attends
+    over the window, and reads the output back. Pipelined like ``e2e``: step i+1's upload overlaps
+    step i. One window per input set; the output of a warm-up step is checked bit for bit against
+    the plugin call on the same q/k/v."""
+    import torch.distributed as dist
+    from streaming_sparse_b200.cache import KVCache
+    start = LK - LQ
+    caches = []
+    for q, k, v, _, _ in sets:
+        c = KVCache(LK, H, D, local_attn_size=-1, device=dev, track_positions=False)
+        c.append(k, v, 0)                       # the history (and this chunk) written once, outside timing
+        caches.append(c)
+    host = [tuple(t.cpu().pin_memory() for t in (q, k[start:], v[start:])) for q, k, v, _, _ in sets]
+    dev_in = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in h) for h in host]
+    outs = [torch.empty((LQ, H, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    d2h = outs[0].numel() * outs[0].element_size()
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(i):
+        s_ = i % 2
+        with torch.cuda.stream(up):
+            if i >= 2:
+                up.wait_event(done[s_])
+            for dst, src in zip(dev_in[s_], host[s_]):
+                dst.copy_(src, non_blocking=True)
+            copied[s_].record(up)
+
+    def compute(i):
+        s_ = i % 2
+        stream.wait_event(copied[s_])
+        q, k_new, v_new = dev_in[s_]
+        cache = caches[s_]
+        cache.append(k_new, v_new, start)
+        kw, vw = cache.window()
+        res = sparse.forward_one(q, kw, vw)
+        done[s_].record(stream)
+        with torch.cuda.stream(down):
+            down.wait_event(done[s_])
+            outs[s_].copy_(res, non_blocking=True)
+        res.record_stream(down)
+
+    def run(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            compute(i)
+
+    run(2)
+    torch.cuda.synchronize()
+    ref = sparse(sets[0][0][None], sets[0][1][None], sets[0][2][None])[0].cpu()
+    assert torch.equal(outs[0], ref), "streaming call differs from the plugin call on the same inputs"
+    n = max(3, min(args.steps, 20))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(up)
+    run(n)
+    down.wait_stream(stream)
+    b.record(down)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    fl = sum(flops[i % 2] for i in range(n))
+    t = torch.tensor([ms, fl], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx[:1], op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm[1:], op=dist.ReduceOp.SUM)
+        ms, fl = float(mx[0]), float(sm[1])
+    else:
+        ms, fl = float(t[0]), float(t[1])
+    return {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": ms / n,
+            "api": "KVCache.append(k_new, v_new, current_start) + SparseAttention.forward_one(q, *cache.window()) "
+                   "with pinned host q / chunk k, v and output; the window stays resident across calls"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch.distributed as dist
     from streaming_sparse_b200 import ops
@@ -709,6 +798,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(sm[1:], op=dist.ReduceOp.SUM)
         e2e_ms, e2e_flops = float(mx[0]), float(sm[1])
     e2e_value = e2e_flops / (e2e_ms * 1e-3) / 1e12
+    streaming = e2e_streaming_bench(dev, sets, sparse, flops, args, world, stream)
 
     # ---- cache append (the chunk write of config 2 into a 32760-token window), HBM-bound
     cache = cache_append_bench(dev, sets[0], args)
@@ -748,6 +838,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output; "
                 "step i+1's upload overlaps step i (separate copy streams for upload and readback)"},
+        "e2e_streaming": streaming,
         "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
         "hbm_kernels": hbm_k,
         "rollout": rollout,
