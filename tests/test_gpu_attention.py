@@ -75,6 +75,27 @@ def test_attention_config1_routed(oracle):
     np.testing.assert_allclose(lse, ref_lse, rtol=0, atol=2e-3)
 
 
+@pytest.mark.parametrize("rho", [0.0, 0.1, 0.3, 1.0])
+def test_attention_history_budgets(oracle, rho):
+    """History budgets floor(rho * pages) from the GPU router, budget 0 (the current chunk alone)
+    and the whole history included, against the oracle (streaming_sparse/v07/tests.py:24-37)."""
+    from streaming_sparse_b200 import ops
+    H, Lq, hist_blocks = 3, 256, 16
+    Lk = hist_blocks * 64 + Lq
+    q, k, v = qkv(11, Lq, Lk, H)
+    wq, wk = router_weights(11, H)
+    extra = math.floor(rho * hist_blocks)
+    ids = ops.route(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), block=64, extra=extra, validate=True)
+    ids_np = ids.cpu().numpy()
+    r = oracle.route(np32(q), np32(k), wq.numpy(), wk.numpy(), 64, extra)
+    np.testing.assert_array_equal(ids_np, r["ids"])
+    assert ((ids_np < hist_blocks).sum(-1) == extra).all()
+    out, lse = _attend(q, k, v, ids_np, 64)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, 64)
+    assert_attention_close(out, ref)
+    np.testing.assert_allclose(lse, ref_lse, rtol=0, atol=2e-3)
+
+
 def test_attention_config2_sampled(oracle):
     """Config 2 at full size; the float64 oracle checks a sample of heads and query blocks."""
     from streaming_sparse_b200 import ops

@@ -15,6 +15,7 @@ CASES = [
     (100, 333, 2, 64, 0, 2),            # ragged: partial query and key blocks
     (64, 64, 1, 64, 0, 0),              # single block, everything forced
     (130, 4000, 3, 128, 200, 5),        # sink not block-aligned
+    (64, 26240, 2, 64, 0, 102),         # 410 key blocks, own block forced: 103 kept (review_v1/test_ops.py:39-47)
 ]
 
 

@@ -125,6 +125,58 @@ def test_budget_sizes_per_config(oracle):
     assert oracle.budget(kb, int(f.sum()), density=0.1, rule="rest") == math.floor(0.1 * (kb - f.sum()))
 
 
+def test_count_rule_known_answer(oracle):
+    """The count known answer of local_experiments/review_v1/test_ops.py:39-47: 410 pages at the
+    25 % "total" rule keep ceil(0.25 * 410) = 103 blocks, the forced own page included, and drop
+    the other 307; the kept mask has exactly that many entries and contains the own page."""
+    rng = np.random.default_rng(410)
+    kb, own = 410, 339
+    S = rng.random((2, 3, kb)).astype(np.float32)
+    forced = np.zeros(kb, np.uint8)
+    forced[own] = 1
+    extra = oracle.budget(kb, 1, density=0.25, rule="total")
+    assert extra + 1 == 103
+    ids, mask = oracle.select(S, forced, extra)
+    assert ids.shape == (2, 3, 103) and (mask.sum(-1) == 103).all() and ((~mask).sum(-1) == 307).all()
+    assert mask[..., own].all() and (np.diff(ids, axis=-1) > 0).all()
+    # the 102 others are the best-scoring unforced pages
+    for h in range(2):
+        for i in range(3):
+            rest = np.delete(S[h, i], own)
+            assert S[h, i][mask[h, i]].sum() - S[h, i, own] == pytest.approx(np.sort(rest)[-102:].sum(), rel=1e-6)
+
+
+@pytest.mark.parametrize("rho", [0.0, 0.1, 0.2, 0.3, 1.0])
+def test_budgets_match_direct_gather(oracle, rho):
+    """streaming_sparse/v07/tests.py:24-37 restated: for history budgets floor(rho * pages), the
+    routed output of a query row equals exact softmax attention over the directly gathered tokens
+    (the selected history blocks, then the current chunk), budget 0 (current chunk only) and the
+    whole history (dense) included."""
+    rng = np.random.default_rng(7)
+    H, Lq, hist_blocks, block = 2, 128, 16, 64
+    Lk = hist_blocks * block + Lq
+    q = oracle.bf16_round(rng.standard_normal((Lq, H, 128)).astype(np.float32))
+    k = oracle.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    v = oracle.bf16_round(rng.standard_normal((Lk, H, 128)).astype(np.float32))
+    wq = (rng.standard_normal((H, 128, 64)) / math.sqrt(128)).astype(np.float32)
+    wk = (rng.standard_normal((H, 128, 64)) / math.sqrt(128)).astype(np.float32)
+    extra = math.floor(rho * hist_blocks)
+    ids = oracle.route(q, k, wq, wk, block, extra)["ids"]
+    out, _ = oracle.attention(q, k, v, ids, block)
+    for h in range(H):
+        for row in (0, 63, 64, Lq - 1):
+            i = row // block
+            hist = [j for j in ids[h, i] if j < hist_blocks]
+            assert len(hist) == extra
+            tokens = [t for j in hist for t in range(j * block, (j + 1) * block)] + list(range(Lk - Lq, Lk))
+            kk = k[tokens, h].astype(np.float64)
+            vv = v[tokens, h].astype(np.float64)
+            s = kk @ q[row, h].astype(np.float64) / math.sqrt(128)
+            p = np.exp(s - s.max())
+            direct = (p / p.sum()) @ vv
+            np.testing.assert_allclose(out[row, h], direct, rtol=1e-5, atol=1e-6)
+
+
 def test_router_invariants(oracle):
     """ids in range and strictly increasing (migration/unified_router/opt28/validate_selection.py:30);
     forced blocks present; no unselected unforced block outranks a selected one."""
