@@ -562,8 +562,8 @@ def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> d
     the 32760-token window is resident in a ``KVCache`` kept across calls, and every step uploads
     only the chunk's q, k, v from pinned host memory, writes k/v into the window
     (``KVCache.append``; a denoising call rewrites its chunk's rows, no roll), routes and attends
-    over the window, and reads the output back. Pipelined like ``e2e``: step i+1's upload overlaps
-    step i. One window per input set; the output of a warm-up step is checked bit for bit against
+    over the window, and reads the output back. The chunk's q, k, v are staged in one pinned
+    buffer, so a step is one upload; pipelined like ``e2e``: step i+1's upload overlaps step i. One window per input set; the output of a warm-up step is checked bit for bit against
     the plugin call on the same q/k/v."""
     import torch.distributed as dist
     from streaming_sparse_b200.cache import KVCache
@@ -573,10 +573,11 @@ def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> d
         c = KVCache(LK, H, D, local_attn_size=-1, device=dev, track_positions=False)
         c.append(k, v, 0)                       # the history (and this chunk) written once, outside timing
         caches.append(c)
-    host = [tuple(t.cpu().pin_memory() for t in (q, k[start:], v[start:])) for q, k, v, _, _ in sets]
-    dev_in = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in h) for h in host]
+    # the chunk's q, k, v staged in one pinned buffer [3, Lq, H, D]: one upload per step
+    host = [torch.stack((q, k[start:], v[start:])).cpu().pin_memory() for q, k, v, _, _ in sets]
+    dev_in = [torch.empty(h.shape, dtype=h.dtype, device=dev) for h in host]
     outs = [torch.empty((LQ, H, D), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    h2d = sum(t.numel() * t.element_size() for t in host[0])
+    h2d = host[0].numel() * host[0].element_size()
     d2h = outs[0].numel() * outs[0].element_size()
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     copied = [torch.cuda.Event() for _ in range(2)]
@@ -587,14 +588,13 @@ def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> d
         with torch.cuda.stream(up):
             if i >= 2:
                 up.wait_event(done[s_])
-            for dst, src in zip(dev_in[s_], host[s_]):
-                dst.copy_(src, non_blocking=True)
+            dev_in[s_].copy_(host[s_], non_blocking=True)
             copied[s_].record(up)
 
     def compute(i):
         s_ = i % 2
         stream.wait_event(copied[s_])
-        q, k_new, v_new = dev_in[s_]
+        q, k_new, v_new = dev_in[s_].unbind(0)
         cache = caches[s_]
         cache.append(k_new, v_new, start)
         kw, vw = cache.window()
@@ -640,7 +640,8 @@ def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> d
     return {"value": fl / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": n, "ms_per_step": ms / n,
             "api": "KVCache.append(k_new, v_new, current_start) + SparseAttention.forward_one(q, *cache.window()) "
-                   "with pinned host q / chunk k, v and output; the window stays resident across calls"}
+                   "with the chunk's q, k, v in one pinned host buffer and a pinned output; the window stays "
+                   "resident across calls"}
 
 
 def run_ours(args, rank: int, world: int, local_rank: int):

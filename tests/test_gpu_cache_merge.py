@@ -26,8 +26,12 @@ def test_cache_known_answer_on_gpu():
     assert hist == 12
 
 
-@pytest.mark.parametrize("local,sink,frames_per_chunk,chunks", [(5, 1, 2, 9), (-1, 0, 3, 3), (4, 0, 1, 10)])
-def test_cache_matches_oracle(oracle, local, sink, frames_per_chunk, chunks):
+@pytest.mark.parametrize("local,sink,frames_per_chunk,chunks,strided",
+                         [(5, 1, 2, 9, False), (-1, 0, 3, 3, False), (4, 0, 1, 10, False), (5, 1, 2, 9, True)])
+def test_cache_matches_oracle(oracle, local, sink, frames_per_chunk, chunks, strided):
+    """Append/evict against the oracle's roll. `strided`: the chunk's k/v are row-strided views
+    (slices of a fused [n, 3, H, 128] projection output), so the chunk write takes the strided copy
+    while the window shifts take the contiguous one."""
     from streaming_sparse_b200.cache import KVCache
     H, ftok = 3, 70                      # 70-token frames: rows never align with 16-byte vector groups of rows
     cap = (local if local != -1 else frames_per_chunk * chunks) * ftok
@@ -41,7 +45,12 @@ def test_cache_matches_oracle(oracle, local, sink, frames_per_chunk, chunks):
             start = chunk * n
             kn = torch.randn((n, H, 128), generator=g).bfloat16()
             vn = torch.randn((n, H, 128), generator=g).bfloat16()
-            c.append(kn.to(DEV), vn.to(DEV), start)
+            if strided:
+                fused = torch.zeros((n, 3, H, 128), dtype=torch.bfloat16, device=DEV)
+                fused[:, 1], fused[:, 2] = kn.to(DEV), vn.to(DEV)
+                c.append(fused[:, 1], fused[:, 2], start)
+            else:
+                c.append(kn.to(DEV), vn.to(DEV), start)
             le = oracle.cache_append(ok, ov, np32(kn), np32(vn), local_attn=local != -1, global_end=ge,
                                      local_end=le, current_start=start, sink_tokens=sink * ftok)
             ge = start + n
