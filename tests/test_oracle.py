@@ -265,3 +265,25 @@ def test_cache_index_plan_matches_oracle_roll(oracle):
                 assert (c.global_end, c.local_end) == (g_end, l_end)
             start += n
             total += n
+
+
+def test_window_retention_matches_reference_first_chunk_policy():
+    """The retention known answers of local_experiments/test_kv_history.py:11-24 for the policy
+    that keeps the first chunk and the latest frames ("A_first_chunk": 3-frame chunks, 15 frames
+    kept), which is the rolling window with sink frames: a KVCache with a 3-frame sink and a
+    15-frame window, one token per frame, so visible positions are frame indices. After every
+    chunk the visible frames are min(15, 3 * chunks) sorted distinct frames drawn from the
+    previous set and the new chunk; after 20 chunks they are 0..2 and 48..59."""
+    from streaming_sparse_b200.cache import KVCache
+    c = KVCache(15, 1, 128, frame_tokens=1, local_attn_size=15, sink_size=3, device="cpu")
+    old = []
+    for completed in range(1, 43):
+        for _ in range(2):                       # a chunk's denoising passes rewrite it in place
+            vis, _ = c.advance(3, (completed - 1) * 3)
+        chosen = vis.tolist()
+        assert len(chosen) == min(15, completed * 3)
+        assert chosen == sorted(set(chosen))
+        assert set(chosen) <= set(old + list(range((completed - 1) * 3, completed * 3)))
+        old = chosen
+        if completed == 20:
+            assert chosen == list(range(3)) + list(range(48, 60))
