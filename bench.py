@@ -391,14 +391,17 @@ def hbm_kernels_bench(dev, args, hbm_gbs: float) -> dict:
 def configs_bench(dev, args):
     """Router + attention at the other shapes of the reference's configs, one graph replay per
     timed step with a 256 MB L2 flush between steps: config 1, config 4 (128-token blocks, a
-    one-frame sink, 10 % of the unforced blocks) and a grid of config 5's sweep (window 2..21 frames
-    of 4680 tokens and 98280, densities 5/25/50 %, blocks 64 and 128). Seeded N(0,1) inputs."""
+    one-frame sink, 10 % of the unforced blocks) and a grid of config 5's sweep (windows of c = 1, 2,
+    14 and 21 chunks of 4680 tokens, densities 5/10/25/50 %, blocks 64 and 128). Seeded N(0,1)
+    inputs."""
     from streaming_sparse_b200 import ops
 
     pts = [("config1", 1560, 6240, 64, 0, dict(topk=24)),
            ("config4", 4680, 34320, 128, 1560, dict(density=0.10, rule="rest"))]
+    # c = 1 (the window is the chunk: every block forced, dense), then c = 2, 14, 21
+    pts.append(("config5 Lk=4680 (all forced) b=64", 4680, 4680, 64, 0, dict(density=0.25)))
     for lk in (9360, 65520, 98280):
-        for dens in (0.05, 0.25, 0.5):
+        for dens in (0.05, 0.10, 0.25, 0.5):
             pts.append((f"config5 Lk={lk} d={dens:g} b=64", 4680, lk, 64, 0, dict(density=dens)))
     for dens in (0.05, 0.5):
         pts.append((f"config5 Lk=98280 d={dens:g} b=128", 4680, 98280, 128, 0, dict(density=dens)))
