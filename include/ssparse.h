@@ -60,6 +60,10 @@ extern "C" {
 #define SS_ERR_BUDGET 1004      /* extra > number of unforced blocks */
 #define SS_ERR_SMEM 1005        /* the id lists do not fit the attention kernel's shared memory */
 #define SS_ERR_DRIVER 1006      /* cuTensorMapEncodeTiled unavailable or failed */
+#define SS_ERR_DEVICE 1007      /* current device ordinal >= SS_MAX_DEVICES */
+
+/* Devices per process the library keeps per-device state for (ordinals 0 .. 63). */
+#define SS_MAX_DEVICES 64
 
 /* device-side status bits (OR-ed into *status) */
 #define SS_DEV_NONFINITE 0x1    /* a router score was NaN or +-inf */
@@ -114,10 +118,16 @@ int ss_router(const void *q, const void *k, const float *wq, const float *wk,
  *     12 heads and 64-token blocks).
  *   - The first call on a device looks up that device's address of the array
  *     (cudaGetSymbolAddress, with the device current); make that first call before capturing
- *     any stream on that device.
+ *     any stream on that device. The address is kept per (device, CUDA context): after
+ *     cudaDeviceReset the next call sees a new context and looks the address up again, so that
+ *     call, too, must come before any capture.
  *   - All calls on a device share the array: calls that overlap on the GPU (different streams
  *     or host threads) race, so the caller serialises them. Nothing in the array needs to start
- *     at zero: each call writes every value it reads.
+ *     at zero: a call that completes writes every value it reads.
+ *   - Whenever *status comes back non-zero, ids, mask and scores of that call are undefined:
+ *     a pooling wait that timed out leaves projections unwritten, and the scoring then reads the
+ *     previous call's values from the shared array.
+ *   - Device ordinals >= SS_MAX_DEVICES are refused with SS_ERR_DEVICE.
  * Other arguments, results and status codes are those of ss_router. */
 int ss_router_noalloc(const void *q, const void *k, const float *wq, const float *wk,
                       int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,

@@ -21,6 +21,7 @@ SS_ERRORS = {
     1004: "extra exceeds the number of unforced blocks",
     1005: "block lists do not fit the attention kernel's shared memory",
     1006: "cuTensorMapEncodeTiled unavailable or failed",
+    1007: "device ordinal beyond the library's 64-device table",
 }
 DEV_NONFINITE, DEV_TIMEOUT, DEV_BADID = 0x1, 0x2, 0x4
 

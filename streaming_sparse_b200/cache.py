@@ -53,19 +53,19 @@ class PositionTracker:
             evicted = n + old_local - size
             rolled = old_local - evicted - sink_tokens
             if rolled < 0:
-                raise ValueError("Cache too small for sink and current chunk")
+                raise ValueError(f"a {n}-token chunk and a {sink_tokens}-token sink do not fit a {size}-slot cache")
             flat[sink_tokens:sink_tokens + rolled] = flat[sink_tokens + evicted:sink_tokens + evicted + rolled].copy()
         local_end = old_local + end - old_global - evicted
         local_start = local_end - n
         if local_start < 0 or local_end > size:
-            raise ValueError("Invalid KV cache bounds; reduce length or use local attention")
+            raise ValueError(f"chunk rows [{local_start}, {local_end}) fall outside the {size}-slot cache")
         flat[local_start:local_end] = np.arange(start, end)
         visible_start = max(0, local_end - max_attention_size)
         if visible_start > local_start:
-            raise ValueError("Attention window must contain the entire current chunk")
+            raise ValueError(f"the {max_attention_size}-token visible window is shorter than the {n}-token chunk")
         visible = flat[visible_start:local_end].copy()
         if (visible < 0).any():
-            raise ValueError("Uninitialized visible cache positions")
+            raise ValueError("the visible window reaches cache slots that were never written")
         return visible, local_start - visible_start
 
 
@@ -124,7 +124,7 @@ class KVCache:
         end = current_start + n
         _, _, local_end = self.write_plan(n, current_start)
         if local_end - n < 0 or local_end > self.capacity:
-            raise ValueError("Invalid KV cache bounds; reduce length or use local attention")
+            raise ValueError(f"chunk rows [{local_end - n}, {local_end}) fall outside the {self.capacity}-slot cache")
         self.local_end, self.global_end = local_end, end
         self.commits += 1
         return vis

@@ -728,14 +728,21 @@ int attention_smem_bytes(int Lk, int block, int n_ids, uint32_t *bytes) {
     return total <= (long)attn::SMEM_LIMIT ? 0 : SS_ERR_SMEM;
 }
 
-static int g_attn_configured[64] = {0};
-static int g_num_sms[64] = {0};
+static int g_attn_configured[SS_MAX_DEVICES] = {0};
+static int g_num_sms[SS_MAX_DEVICES] = {0};
 static std::mutex g_attn_mutex;
 
+static void *g_attn_ctx[SS_MAX_DEVICES] = {nullptr};
+
+// Per (device, context): the kernel's shared-memory attribute and the SM count. A new context on
+// the device (after cudaDeviceReset) is configured again.
 int attention_prepare(int device) {
-    if (device < 0 || device >= 64) return SS_ERR_SHAPE;
+    if (device < 0 || device >= SS_MAX_DEVICES) return SS_ERR_DEVICE;
+    void *ctx = nullptr;
+    int rc = current_context(&ctx);
+    if (rc) return rc;
     std::lock_guard<std::mutex> lock(g_attn_mutex);
-    if (g_attn_configured[device]) return 0;
+    if (g_attn_configured[device] && g_attn_ctx[device] == ctx) return 0;
     cudaError_t e = cudaFuncSetAttribute(attn::sparse_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)attn::SMEM_LIMIT);
     if (e != cudaSuccess) return (int)e;
@@ -743,6 +750,7 @@ int attention_prepare(int device) {
     e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) return (int)e;
     g_num_sms[device] = nsm;
+    g_attn_ctx[device] = ctx;
     g_attn_configured[device] = 1;
     return 0;
 }

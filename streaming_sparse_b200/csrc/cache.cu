@@ -9,6 +9,9 @@
 // of the same call has already overwritten (stream order separates the copies). The chunk
 // write is one 16-byte-vector copy kernel (the reference's sm_80 commit_tile,
 // local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:417-458, also writes with uint4).
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace ss {
@@ -80,24 +83,48 @@ __global__ void __launch_bounds__(256) copy_rows_kernel(const uint4 *__restrict_
     }
 }
 
+// Launch geometry of the copy kernels on one device: SM count and resident CTAs per SM of each
+// form, queried once per device (a rolling append makes up to seven launches).
+struct CopyGeometry {
+    int sms = 0, per_sm_flat = 1, per_sm_rows = 1;
+};
+static CopyGeometry g_copy_geo[SS_MAX_DEVICES];
+static std::mutex g_copy_mutex;
+
+static int copy_geometry(CopyGeometry *out) {
+    int dev;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= SS_MAX_DEVICES) return SS_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(g_copy_mutex);
+    CopyGeometry &g = g_copy_geo[dev];
+    if (g.sms == 0) {
+        int sms = 0, a = 0, b = 0;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return (int)e;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, copy_flat_kernel, 256, 0)) != cudaSuccess) return (int)e;
+        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, copy_rows_kernel, 256, 0)) != cudaSuccess) return (int)e;
+        g.per_sm_flat = std::min(std::max(a, 1), 8);
+        g.per_sm_rows = std::min(std::max(b, 1), 8);
+        g.sms = std::max(sms, 1);
+    }
+    *out = g;
+    return 0;
+}
+
 static int launch_copy(const void *sk, const void *sv, int64_t src_stride, void *dk, void *dv, int64_t dst_stride,
                        int64_t n, int H, cudaStream_t st) {
     if (n <= 0) return 0;
     const int row_vec = H * D / 8;  // uint4 = 8 bf16
     const int64_t total = n * row_vec;
-    int sms = 148;
-    int dev;
-    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    CopyGeometry geo;
+    int rc = copy_geometry(&geo);
+    if (rc) return rc;
+    const int sms = geo.sms;
     const int64_t want = (total + 256 * CP_UNROLL - 1) / (256 * CP_UNROLL);
     // at most one wave of resident CTAs; the grid-stride loop covers the rest
     const bool flat = src_stride / 8 == row_vec && dst_stride / 8 == row_vec &&
                       total < ((int64_t)1 << 31) - (int64_t)sms * 8 * 256 * CP_UNROLL;
-    int per_sm = 0;
-    if (flat)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, copy_flat_kernel, 256, 0);
-    else
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, copy_rows_kernel, 256, 0);
-    per_sm = std::min(std::max(per_sm, 1), 8);
+    const int per_sm = flat ? geo.per_sm_flat : geo.per_sm_rows;
     const unsigned blocks = (unsigned)std::min<int64_t>(want, (int64_t)sms * per_sm);
     if (flat)
         copy_flat_kernel<<<blocks, 256, 0, st>>>((const uint4 *)sk, (const uint4 *)sv, (uint4 *)dk, (uint4 *)dv,

@@ -51,9 +51,30 @@ int encode_tmap_2d_bf16_rows(CUtensorMap *map, const void *base, uint64_t inner,
     return encode_2d_bf16(map, base, inner, outer, row_stride_bytes, box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+
+// The calling thread's current CUDA context (nullptr if none), through the driver entry point so
+// the library does not link libcuda directly.
+int current_context(void **ctx) {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    if (!fn) return SS_ERR_DRIVER;
+    CUcontext c = nullptr;
+    if (fn(&c) != CUDA_SUCCESS) return SS_ERR_DRIVER;
+    *ctx = static_cast<void *>(c);
+    return 0;
+}
+
 }  // namespace ss
 
-extern "C" int ss_version(void) { return 100; }
+extern "C" int ss_version(void) { return 101; }
 
 extern "C" int ss_prepare_device(void) {
     int device;

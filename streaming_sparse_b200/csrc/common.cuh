@@ -250,4 +250,5 @@ int encode_tmap_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint
                         uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 int encode_tmap_2d_bf16_rows(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
                              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+int current_context(void **ctx);
 }

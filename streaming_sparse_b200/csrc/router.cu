@@ -349,16 +349,29 @@ static size_t select_smem(int kb, int R) {
     return (size_t)R * router::ROWS * 4 + (size_t)router::ROWS * kb * 4 + 16;
 }
 
-static int g_router_configured[64] = {0};
+static int g_router_configured[SS_MAX_DEVICES] = {0};
+static void *g_router_ctx[SS_MAX_DEVICES] = {nullptr};
+static int g_router_sms[SS_MAX_DEVICES] = {0};
+static std::mutex g_router_mutex;
 
+// Per (device, context): the kernels' shared-memory attributes and the SM count.
 int router_prepare(int device) {
-    if (device < 0 || device >= 64) return SS_ERR_SHAPE;
-    if (g_router_configured[device]) return 0;
+    if (device < 0 || device >= SS_MAX_DEVICES) return SS_ERR_DEVICE;
+    void *ctx = nullptr;
+    int rc = current_context(&ctx);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lock(g_router_mutex);
+    if (g_router_configured[device] && g_router_ctx[device] == ctx) return 0;
     cudaError_t e = cudaFuncSetAttribute(router::pool_project_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
     if (e != cudaSuccess) return (int)e;
     e = cudaFuncSetAttribute(router::score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return (int)e;
+    int nsm = 0;
+    e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return (int)e;
+    g_router_sms[device] = nsm;
+    g_router_ctx[device] = ctx;
     g_router_configured[device] = 1;
     return 0;
 }
@@ -426,8 +439,7 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     const RouterLayout L = router_layout(H, Lq, Lk, R, block);
     float *qh = reinterpret_cast<float *>(ws + L.qh), *kh = reinterpret_cast<float *>(ws + L.kh);
     // blocks per pool_project tile: the fewest that keep the grid within one wave
-    int nsm = 148;
-    if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) nsm = 148;
+    const int nsm = g_router_sms[device] > 0 ? g_router_sms[device] : 148;
     int bg = std::max(1, (H * (qb + kb) + nsm - 1) / nsm);
     while (H * ((qb + bg - 1) / bg + (kb + bg - 1) / bg) > nsm && bg < std::max(qb, kb)) ++bg;
     const int tq = (qb + bg - 1) / bg, tk = (kb + bg - 1) / bg;
@@ -456,20 +468,26 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
 static __device__ __align__(256) uint8_t g_router_scratch[SS_ROUTER_STATIC_SCRATCH_BYTES];
 
 static std::mutex g_router_scratch_mutex;
-static uint8_t *g_router_scratch_addr[64] = {nullptr};
+static uint8_t *g_router_scratch_addr[SS_MAX_DEVICES] = {nullptr};
+static void *g_router_scratch_ctx[SS_MAX_DEVICES] = {nullptr};
 
 // Device address of g_router_scratch on the current device. In host code the symbol is only a
 // host-side stand-in; a kernel given it would fault (or, where the GPU can reach host memory,
-// silently use the wrong memory), so the address is looked up once per device, with that device
-// current, and cached.
+// silently use the wrong memory), so the address is looked up with the device current and kept
+// together with the context it belongs to. A new context on the device (after cudaDeviceReset the
+// module is loaded again and the array may sit elsewhere) triggers a fresh lookup.
 static int router_scratch_address(int device, uint8_t **addr) {
+    void *ctx = nullptr;
+    int rc = current_context(&ctx);
+    if (rc) return rc;
     std::lock_guard<std::mutex> lock(g_router_scratch_mutex);
-    if (!g_router_scratch_addr[device]) {
+    if (!g_router_scratch_addr[device] || g_router_scratch_ctx[device] != ctx) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_router_scratch);
         if (e != cudaSuccess) return (int)e;
         if (!p) return SS_ERR_POINTER;
         g_router_scratch_addr[device] = static_cast<uint8_t *>(p);
+        g_router_scratch_ctx[device] = ctx;
     }
     *addr = g_router_scratch_addr[device];
     return 0;
@@ -486,7 +504,7 @@ extern "C" int ss_router_noalloc(const void *q, const void *k, const float *wq, 
     int device;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return (int)e;
-    if (device < 0 || device >= 64) return SS_ERR_SHAPE;
+    if (device < 0 || device >= SS_MAX_DEVICES) return SS_ERR_DEVICE;
     uint8_t *scratch = nullptr;
     rc = ss::router_scratch_address(device, &scratch);
     if (rc) return rc;

@@ -226,8 +226,9 @@ def test_bad_block_id_is_reported():
     (25600, 4096, 4, 16),    # 800 tiles: CTAs of five and six tiles (pair, pair, split)
 ])
 def test_attention_many_tiles_per_cta(oracle, Lq, Lk, H, n):
-    """The persistent grid's jobs (pairs with shared blocks, Q-slot reloads, splits merged by
-    log-sum-exp, tile ranges that cross heads) against the oracle on sampled query blocks."""
+    """A persistent CTA that runs several tiles in turn (each tile's Q reloaded into TMEM while the
+    previous tile's output is written, tile ranges that cross heads, per-CTA step lists that fill
+    most of the shared-memory budget) against the oracle on sampled query blocks."""
     q, k, v = qkv(17, Lq, Lk, H)
     rng = np.random.default_rng(17)
     qb, kb = math.ceil(Lq / 64), math.ceil(Lk / 64)

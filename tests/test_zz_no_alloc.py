@@ -86,3 +86,34 @@ def test_router_noalloc_refuses_oversized_problem():
     rc = lib.ss_router_noalloc(fake, fake, fake, fake, H, Lq, Lk, 64, block, 0, 1, fake, n_ids, None, None, None,
                                None)
     assert rc == 1003  # SS_ERR_WORKSPACE
+
+
+def test_router_noalloc_near_the_array_limit():
+    """A problem whose intermediates fill ~98 % of the static array (98 280-token window, 20
+    heads, 64-token blocks) gives ss_router's results bit for bit; one more head no longer fits
+    and is refused on the host before anything is launched."""
+    from streaming_sparse_b200 import build, ops
+    build.build()
+    from streaming_sparse_b200._lib import lib as load
+    lib = load()
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    Lq, Lk, block, extra = 4680, 98280, 64, 3
+    limit = 8 << 20
+    assert 0.95 * limit < ops.router_workspace_bytes(20, Lq, Lk, 64, block) <= limit
+    assert ops.router_workspace_bytes(21, Lq, Lk, 64, block) > limit
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    q, k, wq, wk = _inputs(5, Lq, Lk, 20, dev)
+    n_ids = ops.forced_count(Lq, Lk, block) + extra
+    ws = torch.empty(ops.router_workspace_bytes(20, Lq, Lk, 64, block), dtype=torch.uint8, device=dev)
+    ref = _call(lib, False, q, k, wq, wk, block, 0, extra, n_ids, ws, status, dev)
+    got = _call(lib, True, q, k, wq, wk, block, 0, extra, n_ids, None, status, dev)
+    np.testing.assert_array_equal(got[0], ref[0])
+    np.testing.assert_array_equal(got[1], ref[1])
+    np.testing.assert_array_equal(got[2].view(np.uint32), ref[2].view(np.uint32))
+    assert int(status.item()) == 0
+    del q, k, ws
+    fake = ctypes.c_void_p(0x100000)                     # never dereferenced: refused on the host
+    rc = lib.ss_router_noalloc(fake, fake, fake, fake, 21, Lq, Lk, 64, block, 0, extra, fake, n_ids, None, None,
+                               None, None)
+    assert rc == 1003  # SS_ERR_WORKSPACE
