@@ -27,7 +27,6 @@ import datetime
 import json
 import math
 import os
-import re
 import statistics
 import threading
 import time
@@ -50,14 +49,10 @@ def peaks():
         return 1590.0, 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """Per-launch DRAM bytes of the attention kernel from the committed ncu summary (or None)."""
-    path = os.path.join(ROOT, "profiles", "attention_sm100_config2.md")
-    try:
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
-        return float(m.group(1)) if m else None
-    except OSError:
-        return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention launch at config 2,
+# from the ncu capture summarised in profiles/attention_sm100_config2.md (same command given there).
+ATTN_TRAFFIC_BYTES = 229491200
+ATTN_TRAFFIC_SOURCE = "ncu --set full capture of one config-2 attention launch (profiles/attention_sm100_config2.md)"
 
 
 def make_inputs(seed: int, device):
@@ -301,6 +296,20 @@ def _graph_us(fn, reps: int, steps: int) -> float:
     return 1e3 * a.elapsed_time(b) / (n * reps)
 
 
+def _replay_ms(graphs, n: int) -> float:
+    """Mean ms per replay of the given graphs replayed round-robin n times (after one warm-up round)."""
+    for g in graphs:
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n):
+        graphs[i % len(graphs)].replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n
+
+
 def hbm_kernels_bench(dev, args, hbm_gbs: float) -> dict:
     """The HBM-bound kernels beside the attention, each timed alone with CUDA events over graph
     replays, inputs rotating over buffers larger than L2 where the kernel's traffic allows:
@@ -388,29 +397,53 @@ def hbm_kernels_bench(dev, args, hbm_gbs: float) -> dict:
     return out
 
 
-def configs_bench(dev, args):
-    """Router + attention at the other shapes of the reference's configs, one graph replay per
-    timed step with a 256 MB L2 flush between steps: config 1, config 4 (128-token blocks, a
-    one-frame sink, 10 % of the unforced blocks) and a grid of config 5's sweep (windows of c = 1, 2,
-    14 and 21 chunks of 4680 tokens, densities 5/10/25/50 %, blocks 64 and 128). Seeded N(0,1)
-    inputs."""
-    from streaming_sparse_b200 import ops
-
-    pts = [("config1", 1560, 6240, 64, 0, dict(topk=24)),
-           ("config4", 4680, 34320, 128, 1560, dict(density=0.10, rule="rest"))]
+def config_points():
+    """(short name, long name, Lq, Lk, block, sink tokens, budget rule) of every shape the bench
+    times besides the headline: config 1, config 4 and a grid of config 5's sweep."""
+    pts = [("c1", "config1", 1560, 6240, 64, 0, dict(topk=24)),
+           ("c4", "config4", 4680, 34320, 128, 1560, dict(density=0.10, rule="rest"))]
     # c = 1 (the window is the chunk: every block forced, dense), then c = 2, 14, 21
-    pts.append(("config5 Lk=4680 (all forced) b=64", 4680, 4680, 64, 0, dict(density=0.25)))
+    pts.append(("c5/4680", "config5 Lk=4680 (all forced) b=64", 4680, 4680, 64, 0, dict(density=0.25)))
     for lk in (9360, 65520, 98280):
         for dens in (0.05, 0.10, 0.25, 0.5):
-            pts.append((f"config5 Lk={lk} d={dens:g} b=64", 4680, lk, 64, 0, dict(density=dens)))
+            pts.append((f"c5/{lk}/{round(dens * 100)}", f"config5 Lk={lk} d={dens:g} b=64", 4680, lk, 64, 0,
+                        dict(density=dens)))
     for dens in (0.05, 0.5):
-        pts.append((f"config5 Lk=98280 d={dens:g} b=128", 4680, 98280, 128, 0, dict(density=dens)))
+        pts.append((f"c5/98280/{round(dens * 100)}/b128", f"config5 Lk=98280 d={dens:g} b=128", 4680, 98280, 128, 0,
+                    dict(density=dens)))
+    return pts
+
+
+def configs_bench(dev, args):
+    """Router + attention at the other shapes of the reference's configs: config 1, config 4
+    (128-token blocks, a one-frame sink, 10 % of the unforced blocks) and a grid of config 5's
+    sweep (windows of c = 1, 2, 14 and 21 chunks of 4680 tokens, densities 5/10/25/50 %, blocks 64
+    and 128). Seeded N(0,1) inputs. As in the headline step, the history's key blocks are pooled at
+    commit and a routed call pools the rest: per point, the median of graph replays of (cached
+    route + attention) with a 256 MB L2 flush before each, plus a quarter of the commit's median
+    (one commit per four denoising calls). The cached route's ids are checked against the full
+    route's, bit for bit, at every point."""
+    from streaming_sparse_b200 import ops
+
     peak, _, _ = peaks()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     g = torch.Generator(device=dev).manual_seed(55)
     out = []
     reps = max(5, min(20, args.steps // 10))
-    for name, lq, lk, block, sink, rule in pts:
+
+    def median_us(graph):
+        ms = []
+        for _ in range(reps):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms.append(a.elapsed_time(b))
+        return 1e3 * statistics.median(ms)
+
+    for short, name, lq, lk, block, sink, rule in config_points():
         q = torch.randn((lq, H, D), device=dev, generator=g).bfloat16()
         k = torch.randn((lk, H, D), device=dev, generator=g).bfloat16()
         v = torch.randn((lk, H, D), device=dev, generator=g).bfloat16()
@@ -422,33 +455,38 @@ def configs_bench(dev, args):
         ws = ops.Workspace()
         ids = torch.empty((H, ops.nblocks(lq, block), nf + extra), dtype=torch.int32, device=dev)
         o = torch.empty_like(q)
+        keys = ops.RouterKeys(H, lk, block=block, device=dev)
+        n_hist = ops.history_blocks(lq, lk, block)
+
+        def commit():
+            ops.pool_keys(k, wk, keys, j0=0, j1=n_hist)
 
         def step():
-            ops.route(q, k, wq, wk, block=block, extra=extra, sink_tokens=sink, workspace=ws, out=ids)
+            ops.route(q, k, wq, wk, block=block, extra=extra, sink_tokens=sink, workspace=ws, out=ids, keys=keys,
+                      n_cached=n_hist)
             ops.sparse_attention(q, k, v, ids, block=block, out=o)
 
+        commit()
         for _ in range(3):
             step()
         torch.cuda.synchronize()
         ops.DeviceStatus.check(dev)
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr):
+        full = ops.route(q, k, wq, wk, block=block, extra=extra, sink_tokens=sink, workspace=ws)
+        assert torch.equal(full, ids), f"{name}: cached route differs from the full route"
+        gs = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gs):
             step()
-        ms = []
-        for _ in range(reps):
-            flush.fill_(1)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            gr.replay()
-            b.record()
-            torch.cuda.synchronize()
-            ms.append(a.elapsed_time(b))
-        us = 1e3 * statistics.median(ms)
+        gc = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gc):
+            commit()
+        step_us, commit_us = median_us(gs), median_us(gc)
+        us = step_us + commit_us / 4
         fl = effective_flops(ids.cpu().numpy(), lq, lk, block)
-        out.append({"name": name, "Lq": lq, "Lk": lk, "block": block, "sink_tokens": sink, "blocks_per_query_block":
-                    nf + extra, "us": us, "effective_gflop": fl / 1e9, "tflops": fl / (us * 1e-6) / 1e12,
+        out.append({"short": short, "name": name, "Lq": lq, "Lk": lk, "block": block, "sink_tokens": sink,
+                    "blocks_per_query_block": nf + extra, "us": us, "step_us": step_us, "commit_us": commit_us,
+                    "effective_gflop": fl / 1e9, "tflops": fl / (us * 1e-6) / 1e12,
                     "frac_of_peak": fl / (us * 1e-6) / 1e12 / peak})
-        del gr, q, k, v, ids, o, ws
+        del gs, gc, q, k, v, ids, o, ws, keys, full
     del flush
     torch.cuda.empty_cache()
     return out
@@ -576,6 +614,7 @@ def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> d
         c = KVCache(LK, H, D, local_attn_size=-1, device=dev, track_positions=False)
         c.append(k, v, 0)                       # the history (and this chunk) written once, outside timing
         caches.append(c)
+        sparse.attach(c)                        # history key projections pooled once, reused per call
     # the chunk's q, k, v staged in one pinned buffer [3, Lq, H, D]: one upload per step
     host = [torch.stack((q, k[start:], v[start:])).cpu().pin_memory() for q, k, v, _, _ in sets]
     dev_in = [torch.empty(h.shape, dtype=h.dtype, device=dev) for h in host]
@@ -670,8 +709,22 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     n_ids = ops.forced_count(LQ, LK, BLOCK) + extra
     ids_buf = [torch.empty((H, math.ceil(LQ / BLOCK), n_ids), dtype=torch.int32, device=dev) for _ in sets]
     out = torch.empty((LQ, H, D), dtype=torch.bfloat16, device=dev)
+    # Each input set is one layer's window: its history key blocks are pooled at commit
+    # (ss_router_pool_keys) and every routed call pools only the query blocks and the key blocks
+    # from the chunk boundary on (ss_router_cached), as the reference's streaming pipeline does
+    # (refresh_history once per chunk, current per call: migration/unified_router/opt23/pipeline.py).
+    n_hist = ops.history_blocks(LQ, LK, BLOCK)
+    keys = [ops.RouterKeys(H, LK, block=BLOCK, device=dev) for _ in sets]
+
+    def commit(s):
+        _, k, _, _, wk = sets[s]
+        ops.pool_keys(k, wk, keys[s], j0=0, j1=n_hist)
 
     def route(s):
+        q, k, v, wq, wk = sets[s]
+        ops.route(q, k, wq, wk, block=BLOCK, extra=extra, workspace=ws, out=ids_buf[s], keys=keys[s], n_cached=n_hist)
+
+    def route_uncached(s):
         q, k, v, wq, wk = sets[s]
         ops.route(q, k, wq, wk, block=BLOCK, extra=extra, workspace=ws, out=ids_buf[s])
 
@@ -679,29 +732,42 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         q, k, v, wq, wk = sets[s]
         ops.sparse_attention(q, k, v, ids_buf[s], block=BLOCK, out=out)
 
+    for s in range(2):
+        commit(s)
     for s in range(max(3, args.warmup)):
         route(s % 2)
         attend(s % 2)
     torch.cuda.synchronize()
     ops.DeviceStatus.check(dev)
+    cached_ids = [b.clone() for b in ids_buf]
+    for s in range(2):
+        route_uncached(s)
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, b) for a, b in zip(cached_ids, ids_buf)), "cached route differs from the full route"
     flops = [effective_flops(b.cpu().numpy()) for b in ids_buf]
     # router FLOPs (reported separately): pooled projections + block-score GEMM
     qb, kb = math.ceil(LQ / BLOCK), math.ceil(LK / BLOCK)
     router_flops = 2 * H * qb * kb * 64 + 2 * H * (qb + kb) * D * 64
 
-    # one CUDA graph per (stage, input set): a step replays the router graph, then the attention graph
-    g_route, g_attn = [], []
+    # one CUDA graph per (stage, input set): a step replays the router graph (after the commit
+    # graph on the set's every fourth call: a chunk's four denoising calls share one commit), then
+    # the attention graph
+    g_commit, g_route, g_attn, g_full = [], [], [], []
     for s in range(2):
-        for fn, lst in ((route, g_route), (attend, g_attn)):
+        for fn, lst in ((commit, g_commit), (route, g_route), (attend, g_attn), (route_uncached, g_full)):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn(s)
             lst.append(g)
     for s in range(2):
+        g_commit[s].replay()
         g_route[s].replay()
         g_attn[s].replay()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
+
+    def is_commit(i):
+        return (i // 2) % 4 == 0
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     if world > 1:
@@ -714,6 +780,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         for i in range(args.steps):
             e = evs[i]
             e[0].record(stream)
+            if is_commit(i):
+                g_commit[i % 2].replay()
             g_route[i % 2].replay()
             e[1].record(stream)
             g_attn[i % 2].replay()
@@ -736,6 +804,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     else:
         total_flops = my_flops
     value = total_flops / (elapsed_ms * 1e-3) / 1e12
+    launches = sum(3 + (1 if is_commit(i) else 0) for i in range(args.steps))
+    # untimed beside it: the commit-time pooling alone and the router that pools every key block
+    commit_us = 1e3 * _replay_ms(g_commit, 20)
+    route_full_us = 1e3 * _replay_ms(g_full, 20)
+    route_cached_us = 1e3 * _replay_ms(g_route, 20)
+    del g_commit, g_full
 
     # ---- e2e: the public plugin call with host buffers (pinned), copies inside the timed region
     sparse = SparseAttention(sets[0][3], sets[0][4], RouterConfig(density=DENSITY), workspace=ws)
@@ -821,35 +895,48 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     peak, hbm, peak_kind = peaks()
     att_avg = statistics.mean(att_ms)
     achieved = (sum(flops) / 2) / (att_avg * 1e-3) / 1e12
-    traffic = profiled_traffic()
     cpu = None if args.no_cpu_baseline else cpu_baseline(args.cpu_seconds)
+    # Detail records first, one JSON object per line; the last line is the bench line proper,
+    # short enough that a reader keeping only the tail of stdout still sees every headline figure.
+    details = {"e2e_streaming": streaming, "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
+               "hbm_kernels": hbm_k, "rollout": rollout, "other_configs": other}
+    for name, rec in details.items():
+        if rec is not None:
+            print(json.dumps({"detail": name, "record": rec}), flush=True)
+
+    def r(x, nd=1):
+        return None if x is None else round(float(x), nd)
+
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD, "parallelism": f"streams x{world} (one replica per GPU)",
-                   "timing": "CUDA-graph replay of router and attention per step (events between replays)",
+                   "timing": "CUDA-graph replays, events between them; history keys pooled at commit (every 4th "
+                             "call of a window), current chunk pooled per call",
                    "l2": "2 alternating input sets of 215 MB each (> 126 MB L2)", "density": DENSITY,
                    "blocks_per_query_block": n_ids},
-        "us_per_chunk_layer": 1e3 * elapsed_ms / args.steps,
-        "attention_us": 1e3 * att_avg, "router_us": 1e3 * statistics.mean(rt_ms),
-        "effective_gflop_per_chunk_layer": statistics.mean(flops) / 1e9,
-        "router_gflop_per_chunk_layer": router_flops / 1e9,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "ss::attn::sparse_attention_kernel"},
+                     "frac": achieved / peak, "traffic": ATTN_TRAFFIC_BYTES, "peak_kind": peak_kind,
+                     "kernel": "ss::attn::sparse_attention_kernel", "traffic_source": ATTN_TRAFFIC_SOURCE},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e_steps, "api": "plugin.SparseAttention(q,k,v) with pinned host q/k/v and output; "
-                "step i+1's upload overlaps step i (separate copy streams for upload and readback)"},
-        "e2e_streaming": streaming,
-        "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
-        "hbm_kernels": hbm_k,
-        "rollout": rollout,
-        "other_configs": other,
-        # per timed step: the router graph (pool_project + score_select) and the attention graph
-        "gpu_launches": 3 * args.steps,
+                "steps": e_steps, "api": "plugin.SparseAttention(q,k,v), pinned host q/k/v (whole window) and output"},
+        # per timed step: pool_project + score_select + attention, plus pool_project at each commit
+        "gpu_launches": launches,
         "clocks": clk.summary(),
+        "us_per_chunk_layer": r(1e3 * elapsed_ms / args.steps),
+        "attention_us": r(1e3 * att_avg), "router_us": r(1e3 * statistics.mean(rt_ms)),
+        "router": {"cached_us": r(route_cached_us), "commit_pool_us": r(commit_us), "full_us": r(route_full_us)},
+        "effective_gflop": r(statistics.mean(flops) / 1e9), "router_gflop": r(router_flops / 1e9, 3),
+        "e2e_streaming": {"value": r(streaming["value"]), "ms_per_step": r(streaming["ms_per_step"], 3),
+                          "h2d_bytes_per_step": streaming["h2d_bytes_per_step"]},
+        "rollout": None if rollout is None else {
+            "frames_s": r(rollout["value"], 2), "dense_frames_s": r(rollout["dense_value"], 2),
+            "streams": rollout["streams"],
+            "config4_frames_s": None if rollout["config4_long_horizon"] is None else
+            r(rollout["config4_long_horizon"]["value"], 2)},
+        "configs_frac": None if other is None else {o["short"]: [r(o["us"]), r(o["frac_of_peak"], 3)] for o in other},
     }
     print(json.dumps(line), flush=True)
 

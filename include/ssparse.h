@@ -24,6 +24,9 @@
  *                     route() :90-113), forced-set policy (local_experiments/video_runtime_v1/
  *                     pipeline_graph.py:140-151) and fixed_page_select (local_experiments/
  *                     video_runtime_v1/fixed_page_select.py:34-41)
+ *   ss_router_pool_keys, ss_router_cached <- Cache.refresh_history / Cache.current
+ *                     (migration/unified_router/opt23/pipeline.py:22-34): history pooled once per
+ *                     commit, the current chunk pooled per call
  *   ss_attention   <- exact(q,k,v,ids,workspace) (local_experiments/video_runtime_v1/attention.py:15-24)
  *                     wrapping _attn_fwd (local_experiments/gap_exact_round_kernel.py:4-137), and the
  *                     sm_80 C ABI `run` (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:407-409)
@@ -102,6 +105,28 @@ int ss_router(const void *q, const void *k, const float *wq, const float *wk,
               int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
               int32_t *ids, int n_ids, uint8_t *mask, float *scores,
               void *workspace, size_t workspace_bytes, int *status, void *stream);
+
+/* Pool and project key blocks [j0, j1) of the window k into rows j0 .. j1-1 of kh
+ * [H][kh_rows][R] fp32 (kh_rows >= the window's block count), with the arithmetic of ss_router.
+ * Replaces the commit-time history pooling `Cache.refresh_history`
+ * (migration/unified_router/opt23/pipeline.py:22-29): the history's key blocks change only when
+ * the window is committed (a new chunk, a roll, a rewrite of sink rows), so they are pooled once
+ * per commit and reused by every denoising call of the chunk through ss_router_cached. */
+int ss_router_pool_keys(const void *k, const float *wk, int H, int Lk, int R, int block, int j0, int j1,
+                        float *kh, int kh_rows, int *status, void *stream);
+
+/* ss_router with the first n_cached key blocks' projections taken from kh [H][kh_rows][R]
+ * (written by ss_router_pool_keys or an earlier ss_router_cached on the same window rows): only
+ * the query blocks and key blocks [n_cached, kb) are pooled, and their key projections are
+ * written into kh rows n_cached .. kb-1. Results are bit-identical to ss_router whenever rows
+ * [0, n_cached) of kh hold the projections of this window's blocks. Replaces the per-call
+ * `Cache.current` pooling of the current chunk (migration/unified_router/opt23/pipeline.py:30-34).
+ * workspace: ss_router_workspace_bytes for these sizes (only its query half is used). */
+int ss_router_cached(const void *q, const void *k, const float *wq, const float *wk,
+                     int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
+                     float *kh, int kh_rows, int n_cached,
+                     int32_t *ids, int n_ids, uint8_t *mask, float *scores,
+                     void *workspace, size_t workspace_bytes, int *status, void *stream);
 
 /* Bytes of the static device array used by ss_router_noalloc (8 MiB per device that loads the
    library, held until the process exits). */

@@ -33,6 +33,9 @@ SIGNATURES = {
     "ss_router_workspace_bytes": ([_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)], _I),
     "ss_router": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _SZ, _P, _P], _I),
     "ss_router_noalloc": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P], _I),
+    "ss_router_pool_keys": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P], _I),
+    "ss_router_cached": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I, _P, _P, _P, _SZ, _P, _P],
+                         _I),
     "ss_attention": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P], _I),
     "ss_attention_max_ids": ([_I, _I, ctypes.POINTER(_I)], _I),
     "ss_lse_merge": ([_P, _P, _I, _I, _I, _P, _I, _P, _P], _I),

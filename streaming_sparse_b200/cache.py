@@ -90,6 +90,11 @@ class KVCache:
         self.positions = PositionTracker(capacity) if track_positions else None
         self.commits = 0
         self.anchor = None
+        # Bumped whenever rows that stay in the window change place or content outside the
+        # current chunk (a roll, a restore, an anchor rebase): a router key table pooled from
+        # the old rows is then stale.
+        self.epoch = 0
+        self._router_keys = None
 
     @property
     def sink_tokens(self) -> int:
@@ -122,12 +127,37 @@ class KVCache:
                                         local_attn=self.local_attn_size != -1, sink_tokens=self.sink_tokens,
                                         max_attention_size=self.max_attention_size)
         end = current_start + n
-        _, _, local_end = self.write_plan(n, current_start)
+        rolls, _, local_end = self.write_plan(n, current_start)
         if local_end - n < 0 or local_end > self.capacity:
             raise ValueError(f"chunk rows [{local_end - n}, {local_end}) fall outside the {self.capacity}-slot cache")
         self.local_end, self.global_end = local_end, end
         self.commits += 1
+        if rolls:
+            self.epoch += 1
         return vis
+
+    def window_start(self, local_end: int | None = None) -> int:
+        """First cache row of the visible window (for the given local end, default the current)."""
+        end = self.local_end if local_end is None else local_end
+        return max(0, end - self.max_attention_size)
+
+    def history_tag(self):
+        """Names the rows of the current window for a router key table (``ops.RouterKeys``): two
+        calls with the same tag see the same history rows at the same block alignment."""
+        return (id(self), self.epoch, self.window_start())
+
+    def tag_after(self, n: int, current_start: int):
+        """``history_tag`` as it will be once a write of n tokens at current_start is applied."""
+        rolls, _, local_end = self.write_plan(n, current_start)
+        return (id(self), self.epoch + (1 if rolls else 0), self.window_start(local_end))
+
+    def router_keys(self, block: int = 64, R: int = 64):
+        """This layer's router key table (created on first use, sized for the whole cache)."""
+        from .ops import RouterKeys
+        rk = self._router_keys
+        if rk is None or rk.block != block or rk.R != R:
+            rk = self._router_keys = RouterKeys(self.H, self.capacity, block=block, R=R, device=self.k.device)
+        return rk
 
     def append(self, k_new: torch.Tensor, v_new: torch.Tensor, current_start: int):
         """Write a chunk (post-RoPE K, V: [n,H,D] or [1,n,H,D]); returns (visible positions, history)."""
@@ -168,6 +198,7 @@ class KVCache:
         self.k[0, :n].copy_(snap["k"])
         self.v[0, :n].copy_(snap["v"])
         self.global_end, self.local_end, self.commits = snap["global_end"], n, snap["commits"]
+        self.epoch += 1
         if self.positions is not None and snap["positions"] is not None:
             self.positions.flat[:] = snap["positions"]
 
@@ -186,6 +217,14 @@ class KVCache:
             raise RuntimeError("save_anchor() first")
         t = self.anchor.shape[0]
         rope_shift(self.anchor, self.k[0, :t], temporal_phase(offset, self.k.device, self.D))
+        self.epoch += 1
+
+    def reset(self) -> None:
+        """Empty the cache (index state only; rows are overwritten by the next writes)."""
+        self.global_end = self.local_end = 0
+        self.epoch += 1
+        if self.positions is not None:
+            self.positions.flat[:] = -1
 
     def window(self):
         """Visible K/V window [Lk,H,D] (views into the cache): the last tokens are the current chunk."""

@@ -68,7 +68,9 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 }
 
 // grid (tiles_q + tiles_k, H), 32 * nw threads (one CTA per SM). Tiles [0, tiles_q) pool query
-// blocks, the rest key blocks, bg blocks per tile. Thread 0 first starts one bulk copy of the
+// blocks [0, qb), the rest key blocks [kj0, kj1), bg blocks per tile; key block j goes to row
+// h * kh_ld + j of kh, so a caller can keep the history's rows from an earlier call and pool only
+// the blocks after them. Thread 0 first starts one bulk copy of the
 // head's projection W [128][R] into shared memory (ahead of the token loads, so the small copy is
 // not queued behind megabytes of them). Warp w owns one TMA stage and pools blocks w, w + nw, ...
 // of the tile in pairs: lane 0 TMA-loads a block (block tokens x 128 dims of head h, plain rows),
@@ -80,8 +82,8 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 __global__ void __launch_bounds__(PP_MAX_WARPS * 32, 1)
 pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
                     int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
-                    const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kbp,
-                    int *status) {
+                    const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kh_ld,
+                    int kj0, int kj1, int *status) {
     extern __shared__ uint8_t smr_raw[];
     uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
     const int nw = blockDim.x / 32;
@@ -95,7 +97,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int tile = isq ? blockIdx.x : blockIdx.x - tiles_q;
     const int L = isq ? Lq : Lk;
     const int nb = (L + block - 1) / block;
-    const int b0 = tile * bg, nblk = min(bg, nb - b0);
+    const int b0 = (isq ? 0 : kj0) + tile * bg, nblk = min(bg, (isq ? nb : kj1) - b0);
     const uint32_t full = smem_u32(mb + w), wbar = smem_u32(mb + nw);
     const uint32_t stage = smem_u32(smr) + w * stage_bytes;
     const uint8_t *stage_p = smr + w * stage_bytes;
@@ -174,7 +176,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                     accB = fma2(pack2(mv.z, mv.w), wv, accB);
                 }
                 const float2 ra = unpack2(accA), rb = unpack2(accB);
-                float *dst = isq ? qh + ((size_t)h * nb + b0) * R : kh + ((size_t)h * kbp + b0) * R;
+                float *dst = isq ? qh + ((size_t)h * nb + b0) * R : kh + ((size_t)h * kh_ld + b0) * R;
                 *reinterpret_cast<float2 *>(dst + (size_t)bA * R + e) = ra;
                 if (hasB) *reinterpret_cast<float2 *>(dst + (size_t)bB * R + e) = rb;
             }
@@ -245,7 +247,7 @@ __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb,
 // kb <= 1024), blocks above T kept, ties at T to the lowest block indices (ordered ballot scan),
 // forced blocks always kept, ids written ascending.
 __global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *__restrict__ qh, const float *__restrict__ kh,
-                                                           int qb, int kb, int kbp, int R, int block, int Lq, int Lk,
+                                                           int kh_ld, int qb, int kb, int kbp, int R, int block, int Lq, int Lk,
                                                            int sink, int extra, int32_t *__restrict__ ids, int n_ids,
                                                            uint8_t *__restrict__ mask, float *__restrict__ scores,
                                                            int *status) {
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *_
         float acc[ROWS];
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) acc[r] = 0.f;
-        const float4 *krow = reinterpret_cast<const float4 *>(kh + ((size_t)h * kbp + j) * R);
+        const float4 *krow = reinterpret_cast<const float4 *>(kh + ((size_t)h * kh_ld + j) * R);
         for (int e0 = 0; e0 < R; e0 += 64) {   // R is a multiple of 16
             float4 kv[16];
 #pragma unroll
@@ -425,11 +427,42 @@ int router_check(const void *q, const void *k, const float *wq, const float *wk,
     return 0;
 }
 
-// Launch the router kernels with the intermediates in `ws` (router_workspace_size bytes,
-// 256-byte aligned).
+// Pool and project query blocks [0, qb) (when with_q) and key blocks [kj0, kj1) in one launch of
+// pool_project_kernel: blocks per CTA tile chosen as the fewest that keep the grid within one wave.
+static int pool_launch(int device, const void *q, const void *k, const float *wq, const float *wk, int H, int Lq,
+                       int Lk, int R, int block, bool with_q, float *qh, float *kh, int kh_ld, int kj0, int kj1,
+                       int *status, cudaStream_t st) {
+    const int qb = with_q ? (Lq + block - 1) / block : 0, nk = kj1 - kj0;
+    if (qb + nk <= 0) return 0;
+    const int nsm = g_router_sms[device] > 0 ? g_router_sms[device] : 148;
+    int bg = std::max(1, (H * (qb + nk) + nsm - 1) / nsm);
+    while (H * ((qb + bg - 1) / bg + (nk + bg - 1) / bg) > nsm && bg < std::max(qb, nk)) ++bg;
+    const int tq = (qb + bg - 1) / bg, tk = (nk + bg - 1) / bg;
+    const int nw = pp_warps(R, block);
+    CUtensorMap tmq, tmk;
+    const uint64_t row_bytes = (uint64_t)H * router::D * 2;
+    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)Lk, row_bytes, router::D, (uint32_t)block))
+        return SS_ERR_DRIVER;
+    if (with_q) {
+        if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D,
+                                     (uint32_t)block))
+            return SS_ERR_DRIVER;
+    } else {
+        tmq = tmk;   // no query tiles: the map is never read
+    }
+    router::pool_project_kernel<<<dim3(tq + tk, H), 32 * nw, pp_smem(R, block, nw), st>>>(
+        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kh_ld, kj0, kj1, status);
+    return (int)cudaGetLastError();
+}
+
+// Launch the router kernels with the query projections in `ws` (router_workspace_size bytes,
+// 256-byte aligned). The key projections go to the workspace too (kh_ext == nullptr), or to the
+// caller's table kh_ext [H][kh_ld][R], whose rows [0, n_cached) already hold this window's first
+// n_cached key blocks: only blocks [n_cached, kb) are pooled.
 int router_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
                   int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores,
-                  uint8_t *ws, int *status, cudaStream_t st) {
+                  uint8_t *ws, int *status, cudaStream_t st, float *kh_ext = nullptr, int kh_ld_ext = 0,
+                  int n_cached = 0) {
     const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block, kbp = kb_padded(kb);
     int device;
     cudaError_t e = cudaGetDevice(&device);
@@ -437,23 +470,14 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     int rc = router_prepare(device);
     if (rc) return rc;
     const RouterLayout L = router_layout(H, Lq, Lk, R, block);
-    float *qh = reinterpret_cast<float *>(ws + L.qh), *kh = reinterpret_cast<float *>(ws + L.kh);
-    // blocks per pool_project tile: the fewest that keep the grid within one wave
-    const int nsm = g_router_sms[device] > 0 ? g_router_sms[device] : 148;
-    int bg = std::max(1, (H * (qb + kb) + nsm - 1) / nsm);
-    while (H * ((qb + bg - 1) / bg + (kb + bg - 1) / bg) > nsm && bg < std::max(qb, kb)) ++bg;
-    const int tq = (qb + bg - 1) / bg, tk = (kb + bg - 1) / bg;
-    const int nw = pp_warps(R, block);
-    CUtensorMap tmq, tmk;
-    const uint64_t row_bytes = (uint64_t)H * router::D * 2;
-    if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D, (uint32_t)block))
-        return SS_ERR_DRIVER;
-    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)Lk, row_bytes, router::D, (uint32_t)block))
-        return SS_ERR_DRIVER;
-    router::pool_project_kernel<<<dim3(tq + tk, H), 32 * nw, pp_smem(R, block, nw), st>>>(
-        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kbp, status);
+    float *qh = reinterpret_cast<float *>(ws + L.qh);
+    float *kh = kh_ext ? kh_ext : reinterpret_cast<float *>(ws + L.kh);
+    const int kh_ld = kh_ext ? kh_ld_ext : kbp;
+    rc = pool_launch(device, q, k, wq, wk, H, Lq, Lk, R, block, true, qh, kh, kh_ld, kh_ext ? n_cached : 0, kb,
+                     status, st);
+    if (rc) return rc;
     router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::SS_THREADS,
-                                  select_smem(kbp, R), st>>>(qh, kh, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
+                                  select_smem(kbp, R), st>>>(qh, kh, kh_ld, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
                                                              extra, ids, n_ids, mask, scores, status);
     return (int)cudaGetLastError();
 }
@@ -528,4 +552,40 @@ extern "C" int ss_router(const void *q, const void *k, const float *wq, const fl
     if (reinterpret_cast<uintptr_t>(workspace) & 255u) return SS_ERR_POINTER;
     return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
                              static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ss_router_pool_keys(const void *k, const float *wk, int H, int Lk, int R, int block, int j0, int j1,
+                                   float *kh, int kh_rows, int *status, void *stream) {
+    using namespace ss;
+    if (!k || !wk || !kh) return SS_ERR_POINTER;
+    if (H <= 0 || H > 65535 || Lk <= 0 || R <= 0 || R > router::MAX_R || (R % 16) || (block != 64 && block != 128))
+        return SS_ERR_SHAPE;
+    const int kb = (Lk + block - 1) / block;
+    if (j0 < 0 || j1 < j0 || j1 > kb || kh_rows < kb) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(wk) | reinterpret_cast<uintptr_t>(kh)) & 15u)
+        return SS_ERR_POINTER;
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    int rc = router_prepare(device);
+    if (rc) return rc;
+    return pool_launch(device, nullptr, k, nullptr, wk, H, 0, Lk, R, block, false, nullptr, kh, kh_rows, j0, j1,
+                       status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ss_router_cached(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk,
+                                int R, int block, int sink_tokens, int extra, float *kh, int kh_rows, int n_cached,
+                                int32_t *ids, int n_ids, uint8_t *mask, float *scores, void *workspace,
+                                size_t workspace_bytes, int *status, void *stream) {
+    int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
+    if (rc) return rc;
+    if (!workspace || !kh) return SS_ERR_POINTER;
+    const int kb = (Lk + block - 1) / block;
+    if (kh_rows < kb || n_cached < 0 || n_cached > kb) return SS_ERR_SHAPE;
+    if (workspace_bytes < ss::router_workspace_size(H, Lq, Lk, R, block)) return SS_ERR_WORKSPACE;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) || (reinterpret_cast<uintptr_t>(kh) & 15u))
+        return SS_ERR_POINTER;
+    return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
+                             static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream), kh,
+                             kh_rows, n_cached);
 }

@@ -149,12 +149,16 @@ def router_workspace_bytes(H: int, Lq: int, Lk: int, R: int = 64, block: int = 6
 
 def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, return_mask: bool = False,
           return_scores: bool = False, workspace: Workspace | None = None, out: torch.Tensor | None = None,
-          validate: bool = False):
+          validate: bool = False, keys: RouterKeys | None = None, n_cached: int = 0):
     """Block ids per (head, query block): forced blocks plus the ``extra`` best-scoring others.
 
     q [Lq,H,128] bf16 (current chunk), k [Lk,H,128] bf16 (visible window, current chunk last),
     wq/wk [H,128,R] fp32. Returns ids int32 [H, qb, forced+extra] ascending, and optionally the
     selection mask (bool [H,qb,kb]) and block scores (fp32 [H,qb,kb]).
+
+    ``keys``: a ``RouterKeys`` table whose first ``n_cached`` rows hold this window's key-block
+    projections (``ss_router_cached``): only the query blocks and key blocks [n_cached, kb) are
+    pooled, their projections written into the table. The ids are those of the uncached call.
     """
     q = _tokens(q, "q")
     k = _tokens(k, "k")
@@ -176,9 +180,18 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
     mask = torch.empty((H, qb, kb), dtype=torch.uint8, device=q.device) if return_mask else None
     scores = torch.empty((H, qb, kb), dtype=torch.float32, device=q.device) if return_scores else None
     status = DeviceStatus.word(q.device)
-    rc = lib().ss_router(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra, _p(ids), n_ids,
-                         _p(mask), _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
-    check(rc, "ss_router")
+    if keys is None:
+        rc = lib().ss_router(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra, _p(ids), n_ids,
+                             _p(mask), _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
+        check(rc, "ss_router")
+    else:
+        _require(keys.block == block and keys.R == R and keys.kh.shape[0] == H and keys.kh.device == q.device,
+                 "RouterKeys geometry differs from this call")
+        _require(0 <= n_cached <= kb and keys.kh.shape[1] >= kb, "n_cached or RouterKeys rows out of range")
+        rc = lib().ss_router_cached(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra,
+                                    _p(keys.kh), keys.kh.shape[1], int(n_cached), _p(ids), n_ids, _p(mask),
+                                    _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
+        check(rc, "ss_router_cached")
     if validate:
         DeviceStatus.check(q.device)
     res = [ids]
@@ -187,6 +200,57 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
     if return_scores:
         res.append(scores)
     return res[0] if len(res) == 1 else tuple(res)
+
+
+class RouterKeys:
+    """One layer's table of key-block projections ``kh [H, rows, R]`` fp32, kept across calls.
+
+    The history's key blocks change only when the window is committed, so their projections are
+    pooled once (``pool_keys``, the commit-time ``refresh_history`` of migration/unified_router/
+    opt23/pipeline.py:22-29) and reused by every routed call of the chunk, which pools only the
+    query blocks and the key blocks from the first one that reaches the current chunk
+    (``route(..., keys=...)``, ``Cache.current`` at :30-34). ``tag`` names the window rows the
+    first ``n_valid`` rows were pooled from (for a ``KVCache``: its row epoch and window start);
+    a different tag means nothing is reusable.
+    """
+
+    def __init__(self, H: int, max_tokens: int, *, block: int = 64, R: int = 64, device="cuda"):
+        rows = (nblocks(max_tokens, block) + 3) // 4 * 4
+        self.block, self.R = block, R
+        self.kh = torch.empty((H, rows, R), dtype=torch.float32, device=device)
+        self.n_valid = 0
+        self.tag = None
+
+    def cached(self, tag) -> int:
+        """Leading key blocks whose projections are valid for the window named by ``tag``."""
+        return self.n_valid if tag is not None and tag == self.tag else 0
+
+    def mark(self, tag, n_valid: int) -> None:
+        self.tag, self.n_valid = tag, int(n_valid)
+
+    def invalidate(self) -> None:
+        self.tag, self.n_valid = None, 0
+
+
+def history_blocks(Lq: int, Lk: int, block: int) -> int:
+    """Key blocks that lie wholly in the history [0, Lk - Lq): their projections do not change
+    while the chunk is denoised."""
+    return (Lk - Lq) // block
+
+
+def pool_keys(k, wk, keys: RouterKeys, *, j0: int = 0, j1: int | None = None) -> None:
+    """Pool and project key blocks [j0, j1) of the window k [Lk,H,128] into ``keys.kh``
+    (``ss_router_pool_keys``)."""
+    k = _tokens(k, "k")
+    Lk, H, _ = k.shape
+    wk = wk.to(device=k.device, dtype=torch.float32).contiguous()
+    _require(wk.shape == (H, HEAD_DIM, keys.R), f"wk must be [H,128,{keys.R}]")
+    kb = nblocks(Lk, keys.block)
+    j1 = kb if j1 is None else j1
+    _require(0 <= j0 <= j1 <= kb and keys.kh.shape[0] == H and keys.kh.shape[1] >= kb, "key range or table size")
+    rc = lib().ss_router_pool_keys(_p(k), _p(wk), H, Lk, keys.R, keys.block, j0, j1, _p(keys.kh), keys.kh.shape[1],
+                                   _p(DeviceStatus.word(k.device)), _stream(k.device))
+    check(rc, "ss_router_pool_keys")
 
 
 # ----------------------------------------------------------------------------------------------
@@ -407,7 +471,8 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None
     return x
 
 
-__all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "sparse_attention", "exact",
+__all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "RouterKeys", "pool_keys",
+           "history_blocks", "sparse_attention", "exact",
            "attention_max_ids", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
            "rope_shift", "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
 

@@ -66,12 +66,39 @@ class SparseAttention:
         self.dense = False          # when True, every block is kept (the reference's context pass)
         self.last_ids = None
         self.calls = 0
+        self._caches = {}           # k-cache storage address -> attached KVCache
 
-    def route(self, q: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    def attach(self, cache) -> None:
+        """Let calls whose k is this ``KVCache``'s visible window reuse its history's pooled key
+        projections (``KVCache.router_keys``): pooled once per commit, not once per call."""
+        self._caches[cache.k.untyped_storage().data_ptr()] = cache
+
+    def detach_all(self) -> None:
+        self._caches.clear()
+
+    def cache_of(self, k: torch.Tensor):
+        """The attached cache whose current window is exactly ``k`` [Lk,H,D] (else None)."""
+        cache = self._caches.get(k.untyped_storage().data_ptr()) if self._caches else None
+        if cache is None:
+            return None
+        kw = cache.window()[0]
+        return cache if (kw.data_ptr() == k.data_ptr() and kw.shape == k.shape) else None
+
+    def route(self, q: torch.Tensor, k: torch.Tensor, cache=None) -> torch.Tensor:
+        """Router ids for q against the window k. With ``cache`` (a ``KVCache`` whose window is k),
+        the history's key projections come from the cache's key table when they are still valid
+        for its rows, and the table is marked valid for this window's history afterwards."""
         Lq, Lk = q.shape[-3], k.shape[-3]
         c = self.config
-        return ops.route(q, k, self.wq, self.wk, block=c.block, extra=c.extra(Lq, Lk), sink_tokens=c.sink_tokens,
-                         workspace=self.workspace, validate=self.validate)
+        if cache is None:
+            return ops.route(q, k, self.wq, self.wk, block=c.block, extra=c.extra(Lq, Lk), sink_tokens=c.sink_tokens,
+                             workspace=self.workspace, validate=self.validate)
+        keys = cache.router_keys(c.block, self.wq.shape[2])
+        tag = cache.history_tag()
+        ids = ops.route(q, k, self.wq, self.wk, block=c.block, extra=c.extra(Lq, Lk), sink_tokens=c.sink_tokens,
+                        workspace=self.workspace, validate=self.validate, keys=keys, n_cached=keys.cached(tag))
+        keys.mark(tag, ops.history_blocks(Lq, Lk, c.block))
+        return ids
 
     def _dense_ids(self, H: int, Lq: int, Lk: int, device) -> torch.Tensor:
         c = self.config
@@ -80,13 +107,17 @@ class SparseAttention:
         ids.copy_(torch.arange(kb, device=device, dtype=torch.int32).expand(H, qb, kb))
         return ids
 
-    def forward_one(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None):
-        """q [Lq,H,D], k/v [Lk,H,D] bf16 -> [Lq,H,D] bf16."""
+    def forward_one(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
+                    cache=None):
+        """q [Lq,H,D], k/v [Lk,H,D] bf16 -> [Lq,H,D] bf16. ``cache``: the ``KVCache`` whose window
+        k/v are (found among the attached caches when not given)."""
         Lq, H, _ = q.shape
         Lk = k.shape[0]
         if Lk < Lq:
             raise ValueError("the KV window must contain the current chunk (Lk >= Lq)")
-        ids = self._dense_ids(H, Lq, Lk, q.device) if self.dense else self.route(q, k)
+        if cache is None:
+            cache = self.cache_of(k)
+        ids = self._dense_ids(H, Lq, Lk, q.device) if self.dense else self.route(q, k, cache)
         self.last_ids = ids
         self.calls += 1
         return ops.sparse_attention(q, k, v, ids, block=self.config.block, out=out, validate=self.validate)

@@ -421,8 +421,7 @@ class Rollout:
 
     def reset(self):
         for c in self.caches:
-            c.global_end = 0
-            c.local_end = 0
+            c.reset()
 
     def rope(self, start_frame: int, frames: int):
         key = (start_frame, frames)
@@ -453,6 +452,8 @@ class Rollout:
         out = torch.empty_like(noise)
         plugin = SparsePlugin(self.sparse, target=sys.modules[__name__]) if self.sparse is not None else None
         if plugin is not None:
+            for c in self.caches:     # routed calls reuse each layer's pooled history keys
+                self.sparse.attach(c)
             plugin.__enter__()
         try:
             for c0 in range(0, cfg.frames, cfg.frames_per_chunk):
@@ -490,7 +491,15 @@ class Rollout:
         # buffer. So one graph serves every call with the same key -- with a rolling window, every
         # steady-state chunk -- and the host index mirrors are advanced after each replay.
         start = c0 * self.cfg.frame_tokens
-        key = (nf, phase) + self.caches[0].write_plan(x.shape[1] * self.cfg.frame_tokens, start)
+        n = x.shape[1] * self.cfg.frame_tokens
+        # a routed call also depends on how many history key blocks the layers' router tables
+        # hold for the window this write leaves (pooled at the chunk's first call, reused after)
+        routed = self.sparse is not None and phase == "denoise"
+        cached = None
+        if routed:
+            c = self.sparse.config
+            cached = self.caches[0].router_keys(c.block, self.sparse.wq.shape[2]).cached(self.caches[0].tag_after(n, start))
+        key = (nf, phase, cached) + self.caches[0].write_plan(n, start)
         ent = self._graph.get(key)
         if nf not in self._rope_in:
             self._rope_in[nf] = (torch.empty_like(rope[0]), torch.empty_like(rope[1]))
@@ -516,9 +525,13 @@ class Rollout:
         t_in.fill_(t)
         g.replay()
         if advance:
-            n = x.shape[1] * self.cfg.frame_tokens
             for cache in self.caches:
                 cache.advance(n, start)
+                if routed:   # what the captured route marked in each layer's key table
+                    c = self.sparse.config
+                    lk = cache.local_end - cache.window_start()
+                    cache.router_keys(c.block, self.sparse.wq.shape[2]).mark(cache.history_tag(),
+                                                                             ops.history_blocks(n, lk, c.block))
         return flow
 
     def release_graphs(self):

@@ -46,3 +46,9 @@ def test_effective_flops_match_token_count(Lq, Lk, extra, per_row):
     tok = _tokens_per_row(ids, Lq, Lk)
     assert (tok == per_row).all()
     assert bench.effective_flops(ids, Lq, Lk, B) == 4 * D * tok.sum() == 4 * D * H * Lq * per_row
+
+
+def test_config_points_have_unique_short_names():
+    pts = bench.config_points()
+    assert len({p[0] for p in pts}) == len(pts) == 17
+    assert all(p[2] <= p[3] for p in pts)          # Lq <= Lk everywhere
