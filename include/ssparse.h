@@ -121,8 +121,11 @@ int ss_router_pool_keys(const void *k, const float *wk, int H, int Lk, int R, in
  * written into kh rows n_cached .. kb-1. Results are bit-identical to ss_router whenever rows
  * [0, n_cached) of kh hold the projections of this window's blocks. Replaces the per-call
  * `Cache.current` pooling of the current chunk (migration/unified_router/opt23/pipeline.py:30-34).
+ * k holds window rows [k_row0, Lk) (k_row0 <= n_cached * block): a rank of a KV-sharded group,
+ * which stores only its own history blocks, passes the window's tail (the history rows of the
+ * block the current chunk starts in, then the chunk) with the gathered history projections in kh.
  * workspace: ss_router_workspace_bytes for these sizes (only its query half is used). */
-int ss_router_cached(const void *q, const void *k, const float *wq, const float *wk,
+int ss_router_cached(const void *q, const void *k, int k_row0, const float *wq, const float *wk,
                      int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
                      float *kh, int kh_rows, int n_cached,
                      int32_t *ids, int n_ids, uint8_t *mask, float *scores,
@@ -183,6 +186,46 @@ int ss_attention_max_ids(int Lk, int block, int *max_ids);
  * L = logsumexp_p lse_p; lse_out [H][Lq] (optional) = L. */
 int ss_lse_merge(const float *o_parts, const float *lse_parts, int P, int H, int Lq,
                  void *out, int out_dtype, float *lse_out, void *stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* KV-block sharding across the GPUs of a node: partials merged over peer memory.              */
+/* ------------------------------------------------------------------------------------------ */
+/* With the window split block-cyclically over P ranks (one GPU each), every rank attends over its
+ * own blocks (ss_attention with lse) and the partials are combined by the LSE merge of
+ * ss_lse_merge. These entry points do that combine with the partials left where they were
+ * written: each rank opens the others' buffers once (CUDA IPC), and per call a flag barrier makes
+ * the partials visible, then one kernel reads all P of them through peer pointers and writes the
+ * merged rows. No counterpart in the reference, whose runtime runs one video per GPU
+ * (local_experiments/video_runtime_v1/batch.py:29-37) and merges splits inside one GPU
+ * (migration/unified_router/opt21/attention.py:7-15). The caller allocates every buffer. */
+
+#define SS_MAX_PEERS 8
+#define SS_IPC_HANDLE_BYTES 64
+
+/* Export the allocation holding device pointer ptr: handle (SS_IPC_HANDLE_BYTES bytes) and the
+   offset of ptr inside that allocation, to be sent to the other processes of the node. */
+int ss_ipc_handle(const void *ptr, void *handle, size_t *offset);
+/* Map another process's exported allocation into the current device's context (peer access
+   enabled); *ptr = mapped base + offset. */
+int ss_ipc_open(const void *handle, size_t offset, void **ptr);
+/* Unmap a pointer returned by ss_ipc_open (same offset). */
+int ss_ipc_close(void *ptr, size_t offset);
+
+/* flags: P device pointers (flags[p] = rank p's int array of >= P entries, the others opened
+ * with ss_ipc_open). Posts epoch into slot `rank` of every rank's array, then waits until this
+ * rank's slots 0..P-1 all hold epoch or later. Epochs must increase from call to call. Writes
+ * enqueued before the barrier on each rank are visible to every rank's work enqueued after it.
+ * A wait that runs out (about 2 s) sets SS_DEV_TIMEOUT in *status instead of hanging. */
+int ss_peer_barrier(int *const *flags, int rank, int P, int epoch, int *status, void *stream);
+
+/* Rows [row0, row1) of out [Lq][H][128] (out_dtype 0 = bf16, 1 = fp32) =
+ * sum_p exp(lse_p - L) o_p with L = logsumexp_p lse_p, where o_parts[p] is part p's [Lq][H][128]
+ * output (part_dtype 0 = bf16, 1 = fp32) and lse_parts[p] its [H][Lq] natural-log LSE (-inf = the
+ * part saw no token), both device pointers that may live on other GPUs (ss_ipc_open). lse_out
+ * [H][Lq] (optional) receives L for those rows. P <= SS_MAX_PEERS. Arithmetic of ss_lse_merge. */
+int ss_lse_merge_peers(const void *const *o_parts, const float *const *lse_parts, int P, int part_dtype,
+                       int H, int Lq, int row0, int row1, void *out, int out_dtype, float *lse_out,
+                       void *stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* KV cache append / evict.                                                                    */

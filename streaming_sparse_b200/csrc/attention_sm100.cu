@@ -25,7 +25,7 @@
 //   warp 0      list construction (prologue), then the TMA producer of the K/V ring
 //   warp 1      TMEM allocator + tcgen05.mma issuer for warpgroup 0's QKs and PVs
 //   warp 2      tcgen05.mma issuer for warpgroup 1
-//   warp 3      idle after the prologue
+//   warp 3      after the prologue, L2 prefetch of the next tile's first K/V steps
 //   warps 4-7   softmax warpgroup 0,   warps 8-11  softmax warpgroup 1
 //               After the prologue the control warpgroup (warps 0-3) gives registers up
 //               (setmaxnreg 56) and the softmax warpgroups take them (224): a softmax thread
@@ -297,6 +297,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(smem + OFF_MISC);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
     volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
+    volatile int *progress = reinterpret_cast<volatile int *>(smem + OFF_MISC + 12);   // (tile << 16) | half-way
     Tile *tiles = reinterpret_cast<Tile *>(smem + OFF_TILES);
     float *xch = reinterpret_cast<float *>(smem + OFF_XCH);                              // [2][2][128]
     uint32_t *bm = reinterpret_cast<uint32_t *>(smem + OFF_RING + NST * TILE_BYTES);     // [tmax][2][nwords]
@@ -310,6 +311,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     if (tid == 0) {
         *abort_flag = 0;
         *badid_flag = 0;
+        *progress = 0;
         mbar_init(bar(Q_FULL), 256);
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar(S_FULL + s), 1);
@@ -356,8 +358,11 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         // step whose sub-blocks only one half selected keeps the other half's sub-partitions
         // idle while the first exponentiate 128 columns per row. The blocks only the first
         // half selected are therefore paired with blocks only the second half selected (each
-        // row then exponentiates 64 columns), followed by the unpaired rest and the blocks
-        // both halves selected, each group ascending.
+        // row then exponentiates 64 columns). The blocks both halves selected come first: they
+        // are mostly the forced current-chunk blocks, the same for every tile of a head, so the
+        // start of a tile reads K/V that the head's other tiles (and warp 3's L2 prefetch) have
+        // already brought into L2. Order: both (an even count), the pairs, the unpaired rest, the
+        // odd "both" sub-block if there is one; each group ascending.
         uint32_t *sub = reinterpret_cast<uint32_t *>(steps);
         int pos = 0;   // sub-blocks written
         for (int lt = 0; lt < nt; ++lt) {
@@ -369,15 +374,16 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             };
             const int na = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0xffffffffu);   // A only
             const int nb = warp_count_bits(p.nwords, lane, per, B, A, 0u, 0xffffffffu);   // B only
-            const int mp = min(na, nb);
-            uint32_t *base = sub + pos;
-            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
-                    [&](int k, uint32_t e) { base[k < mp ? 2 * k : mp + k] = e; });
-            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
-                    [&](int k, uint32_t e) { base[k < mp ? 2 * k + 1 : mp + k] = e; });
-            const int nboth = compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & B[w]; }, maskof,
-                                      [&](int k, uint32_t e) { base[na + nb + k] = e; });
+            const int nboth = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0u);         // both
+            const int mp = min(na, nb), nb2 = nboth & ~1;
             const int n = na + nb + nboth;
+            uint32_t *base = sub + pos;
+            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & B[w]; }, maskof,
+                    [&](int k, uint32_t e) { base[k < nb2 ? k : n - 1] = e; });
+            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
+                    [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k : mp + k)] = e; });
+            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
+                    [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k + 1 : mp + k)] = e; });
             const int padded = max(4, (n + 3) & ~3);
             for (int k = n + lane; k < padded; k += 32) sub[pos + k] = entry(0u, 0u, 0u);
             if (lane == 0) {
@@ -425,8 +431,16 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         }
         for (int lt = 0; lt < nt && ok; ++lt) {
             const Tile tl = tiles[lt];
+            const bool more = lt + 1 < nt;
+            if (more) {   // the next tile's Q row slice (128 B) into L2, a whole tile ahead of its use
+                const int tn = tiles[lt + 1].tile, rn = (tn % p.ntiles) * 128 + r;
+                if (rn < p.Lq)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.q + ((size_t)rn * p.H + tn / p.ntiles) * D + 64 * wg));
+            }
+            if (warp == 4 && lane == 0) *progress = lt << 16;
             float m = -INFINITY, l = 0.f;
             for (int j = 0; j < tl.n / 2; ++j, ++k) {
+                if (warp == 4 && lane == 0 && j == tl.n / 4) *progress = (lt << 16) | 1;   // half-way
                 const uint2 st = steps[tl.first + 2 * j + wg];
                 ok = warp_all_ok(mbar_wait(bar(S_FULL + wg), k & 1, abort_flag));
                 if (!ok) break;
@@ -559,15 +573,23 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 mbar_arrive(bar(P_FULL + wg));
             }
             if (!ok) break;
-            // ---------------- tile epilogue: merge the two halves, write, load the next Q ----------------
+            if (more) {
+                // The next tile's Q goes into TMEM as soon as this tile's last QK (warpgroup 1's)
+                // has completed, so its first QKs run while the epilogue below merges and writes.
+                const int tn = tiles[lt + 1].tile;
+                load_q(p, tn / p.ntiles, (tn % p.ntiles) * 128 + r, wg, qv);
+                ok = warp_all_ok(mbar_wait(bar(S_FULL + 1), (k - 1) & 1, abort_flag));
+                if (!ok) break;
+                tc_fence_after();
+                tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
+                tmem_wait_st();
+                tmem_st_fence32(reinterpret_cast<const float *>(qv));
+                tc_fence_before();
+                mbar_arrive(bar(Q_FULL));
+            }
+            // ---------------- tile epilogue: merge the two halves, write ----------------
             const int h = tl.tile / p.ntiles, row = (tl.tile % p.ntiles) * 128 + r;
             const bool live = row < p.Lq;
-            const bool more = lt + 1 < nt;
-            if (more) {   // bring the next tile's Q row slice (128 B) into L2 while we wait
-                const int tn = tiles[lt + 1].tile, rn = (tn % p.ntiles) * 128 + r;
-                if (rn < p.Lq)
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.q + ((size_t)rn * p.H + tn / p.ntiles) * D + 64 * wg));
-            }
             ok = warp_all_ok(mbar_wait(bar(PV_DONE + wg), (k - 1) & 1, abort_flag));   // our last PV
             if (!ok) break;
             xch[(wg * 2 + 0) * 128 + r] = m;
@@ -600,16 +622,6 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             }
             tc_fence_before();
             mbar_arrive(bar(XDONE));
-            if (more) {
-                // all QKs of this tile completed (XSUM), so Q may be replaced
-                const int tn = tiles[lt + 1].tile;
-                load_q(p, tn / p.ntiles, (tn % p.ntiles) * 128 + r, wg, qv);
-                tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
-                tmem_wait_st();
-                tmem_st_fence32(reinterpret_cast<const float *>(qv));
-                tc_fence_before();
-                mbar_arrive(bar(Q_FULL));
-            }
             if (live) {
                 if (p.out_fp32) {
                     float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) +
@@ -679,6 +691,37 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                 ring.e = ring.e == 0 ? NST - 1 : ring.e - 1;
                 if (ring.e == NST - 1) ring.ph ^= 1;
                 mbar_wait(bar(FULL + ring.e), ring.ph, &never);
+            }
+        }
+    } else if (warp == 3) {
+        // ---------------- L2 prefetch of the next tile's first steps ----------------
+        // Once the softmax warpgroups are half-way through tile lt, the K and V boxes of the first
+        // PF_STEPS steps of tile lt+1 are prefetched into L2 (no shared memory, no completion
+        // tracking). Those steps are the blocks both query blocks selected -- mostly the forced
+        // current-chunk blocks, shared by all tiles of a head -- so a head change at a tile
+        // boundary starts on L2 hits instead of every CTA waiting on HBM at once.
+        constexpr int PF_STEPS = 32;
+        for (int lt = 0; lt + 1 < nt; ++lt) {
+            const int want = (lt << 16) | 1;
+            const long long t0 = clock64();
+            bool go = true;
+            while (*progress < want) {
+                if (*abort_flag || clock64() - t0 > kWaitLimitCycles) {
+                    go = false;
+                    break;
+                }
+                __nanosleep(256);
+            }
+            if (!go) break;
+            const Tile tn = tiles[lt + 1];
+            const int h = tn.tile / p.ntiles, nst = min(PF_STEPS, tn.n);
+            for (int i = lane; i < 4 * nst; i += 32) {
+                const uint2 st = steps[tn.first + i / 4];
+                const int which = i & 3;   // K x, K y, V x, V y
+                const int t0s = e_start((which & 1) ? st.y : st.x);
+                const CUtensorMap *tm = which < 2 ? &tm_k : &tm_v;
+                tma_prefetch_2d(tm, h * D, t0s);
+                tma_prefetch_2d(tm, h * D + 64, t0s);
             }
         }
     } else if (warp == 1 || warp == 2) {

@@ -1,0 +1,229 @@
+// peer.cu -- the cross-GPU step of KV-block sharding, over peer memory (NVLink / NVSwitch).
+//
+// With the KV window split block-cyclically over the GPUs of a node, every rank attends over the
+// blocks it owns and holds a partial result (o_r, lse_r) for every query row. The partials are
+// combined by log-sum-exp, the arithmetic of `merge` (local_experiments/video_runtime_v1/
+// attention.py:40-45) and of the split merge `_merge_restore` (migration/unified_router/opt21/
+// attention.py:7-15). Here the exchange and the merge are one kernel: each rank reads the other
+// ranks' partials straight from their memory (peer loads through buffers the ranks opened to
+// each other with CUDA IPC) and writes the merged rows, so the partials cross NVLink once and
+// there is no separate collective or weighting pass.
+//
+//   ss_ipc_handle / ss_ipc_open / ss_ipc_close  export a caller-allocated device buffer to the
+//       other ranks of the node and map theirs (no allocation by the library)
+//   ss_peer_barrier      every rank posts an epoch into each peer's flag array, then waits
+//       (bounded) until every peer has posted it into its own: after it, the partials the peers
+//       wrote before their barrier are visible
+//   ss_lse_merge_peers   merged rows [row0, row1) from P partials given as P peer pointers
+#include <string.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ss {
+namespace peer {
+
+constexpr int D = 128;
+
+struct Parts {
+    const void *o[SS_MAX_PEERS];
+    const float *lse[SS_MAX_PEERS];
+};
+struct Flags {
+    int *f[SS_MAX_PEERS];
+};
+
+__device__ __forceinline__ void st_release_sys(int *p, int v) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One warp. Lane p < P posts `epoch` into slot `rank` of peer p's flags, then waits until slot p
+// of this rank's flags holds epoch (or later). Every wait is bounded: after ~2 s the kernel sets
+// SS_DEV_TIMEOUT in *status and returns.
+__global__ void __launch_bounds__(32) barrier_kernel(Flags fl, int rank, int P, int epoch, int *status) {
+    const int p = threadIdx.x;
+    if (p < P) {
+        __threadfence_system();                  // this rank's earlier writes before the post
+        st_release_sys(fl.f[p] + rank, epoch);
+        const int *mine = fl.f[rank] + p;
+        const long long t0 = clock64();
+        bool ok = true;
+        while (ld_acquire_sys(mine) - epoch < 0) {
+            if (clock64() - t0 > kWaitLimitCycles) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (!ok) report(status, SS_DEV_TIMEOUT);
+    }
+}
+
+__device__ __forceinline__ float4 load4(const void *base, int64_t idx4, bool bf16) {
+    // four consecutive values of part p (element offset 4*idx4), read once through L2
+    if (bf16) {
+        const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(base) + idx4);
+        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+    }
+    return __ldcg(reinterpret_cast<const float4 *>(base) + idx4);
+}
+
+// One thread per (row, head, 4 dims) of rows [row0, row1). Every part's LSE and values are loaded
+// before any is used (all of a thread's peer loads in flight at once); arithmetic and order are
+// those of ss_lse_merge: L = max + log(sum w), w_p = exp(lse_p - max), out = sum w_p o_p / sum w.
+template <int PMAX>
+__global__ void __launch_bounds__(256) merge_peers_kernel(Parts parts, int P, int part_bf16, int H, int Lq, int row0,
+                                                          int row1, void *out, int out_fp32, float *lse_out) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)(row1 - row0) * H * (D / 4);
+    if (gid >= total) return;
+    const int quad = (int)(gid % (D / 4));
+    const int64_t rh = (int64_t)row0 * H + gid / (D / 4);   // row * H + h
+    const int h = (int)(rh % H);
+    const int row = (int)(rh / H);
+    const int64_t idx4 = rh * (D / 4) + quad;
+    float l[PMAX];
+    float4 v[PMAX];
+#pragma unroll
+    for (int p = 0; p < PMAX; ++p) {
+        if (p < P) {
+            l[p] = __ldcg(parts.lse[p] + (int64_t)h * Lq + row);
+            v[p] = load4(parts.o[p], idx4, part_bf16 != 0);
+        }
+    }
+    float mx = -INFINITY, wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < PMAX; ++p)
+        if (p < P) mx = fmaxf(mx, l[p]);
+    if (mx != -INFINITY) {
+#pragma unroll
+        for (int p = 0; p < PMAX; ++p) {
+            if (p < P) {
+                const float w = __expf(l[p] - mx);
+                acc.x = fmaf(w, v[p].x, acc.x);
+                acc.y = fmaf(w, v[p].y, acc.y);
+                acc.z = fmaf(w, v[p].z, acc.z);
+                acc.w = fmaf(w, v[p].w, acc.w);
+                wsum += w;
+            }
+        }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    acc.x *= inv;
+    acc.y *= inv;
+    acc.z *= inv;
+    acc.w *= inv;
+    const int64_t base = rh * D + quad * 4;
+    if (out_fp32) {
+        reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + base)[0] = acc;
+    } else {
+        const uint2 pk = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+        reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + base)[0] = pk;
+    }
+    if (lse_out && quad == 0) lse_out[(int64_t)h * Lq + row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+}
+
+using AddressRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+static AddressRangeFn address_range_fn() {
+    static AddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddressRangeFn>(p);
+    });
+    return fn;
+}
+
+}  // namespace peer
+}  // namespace ss
+
+extern "C" int ss_ipc_handle(const void *ptr, void *handle, size_t *offset) {
+    using namespace ss;
+    if (!ptr || !handle || !offset) return SS_ERR_POINTER;
+    peer::AddressRangeFn fn = peer::address_range_fn();
+    if (!fn) return SS_ERR_DRIVER;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return SS_ERR_DRIVER;
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+    if (e != cudaSuccess) return (int)e;
+    static_assert(sizeof(cudaIpcMemHandle_t) == SS_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    *offset = (size_t)(reinterpret_cast<uintptr_t>(ptr) - (uintptr_t)base);
+    return 0;
+}
+
+extern "C" int ss_ipc_open(const void *handle, size_t offset, void **ptr) {
+    if (!handle || !ptr) return SS_ERR_POINTER;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void *base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return (int)e;
+    *ptr = static_cast<uint8_t *>(base) + offset;
+    return 0;
+}
+
+extern "C" int ss_ipc_close(void *ptr, size_t offset) {
+    if (!ptr) return SS_ERR_POINTER;
+    return (int)cudaIpcCloseMemHandle(static_cast<uint8_t *>(ptr) - offset);
+}
+
+extern "C" int ss_peer_barrier(int *const *flags, int rank, int P, int epoch, int *status, void *stream) {
+    using namespace ss;
+    if (!flags) return SS_ERR_POINTER;
+    if (P <= 0 || P > SS_MAX_PEERS || rank < 0 || rank >= P) return SS_ERR_SHAPE;
+    peer::Flags fl;
+    for (int p = 0; p < SS_MAX_PEERS; ++p) fl.f[p] = p < P ? flags[p] : nullptr;
+    for (int p = 0; p < P; ++p)
+        if (!fl.f[p] || (reinterpret_cast<uintptr_t>(fl.f[p]) & 3u)) return SS_ERR_POINTER;
+    peer::barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, rank, P, epoch, status);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ss_lse_merge_peers(const void *const *o_parts, const float *const *lse_parts, int P, int part_dtype,
+                                  int H, int Lq, int row0, int row1, void *out, int out_dtype, float *lse_out,
+                                  void *stream) {
+    using namespace ss;
+    if (!o_parts || !lse_parts || !out) return SS_ERR_POINTER;
+    if (P <= 0 || P > SS_MAX_PEERS || H <= 0 || Lq <= 0 || row0 < 0 || row1 < row0 || row1 > Lq ||
+        (part_dtype != 0 && part_dtype != 1) || (out_dtype != 0 && out_dtype != 1))
+        return SS_ERR_SHAPE;
+    peer::Parts parts;
+    for (int p = 0; p < SS_MAX_PEERS; ++p) {
+        parts.o[p] = p < P ? o_parts[p] : nullptr;
+        parts.lse[p] = p < P ? lse_parts[p] : nullptr;
+    }
+    for (int p = 0; p < P; ++p) {
+        if (!parts.o[p] || !parts.lse[p]) return SS_ERR_POINTER;
+        if ((reinterpret_cast<uintptr_t>(parts.o[p]) & (part_dtype ? 15u : 7u)) ||
+            (reinterpret_cast<uintptr_t>(parts.lse[p]) & 3u))
+            return SS_ERR_POINTER;
+    }
+    if (reinterpret_cast<uintptr_t>(out) & 15u) return SS_ERR_POINTER;
+    if (row1 == row0) return 0;
+    const int64_t total = (int64_t)(row1 - row0) * H * (peer::D / 4);
+    const unsigned blocks = (unsigned)((total + 255) / 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int bf = part_dtype == 0;
+    if (P <= 2)
+        peer::merge_peers_kernel<2><<<blocks, 256, 0, st>>>(parts, P, bf, H, Lq, row0, row1, out, out_dtype, lse_out);
+    else if (P <= 4)
+        peer::merge_peers_kernel<4><<<blocks, 256, 0, st>>>(parts, P, bf, H, Lq, row0, row1, out, out_dtype, lse_out);
+    else
+        peer::merge_peers_kernel<8><<<blocks, 256, 0, st>>>(parts, P, bf, H, Lq, row0, row1, out, out_dtype, lse_out);
+    return (int)cudaGetLastError();
+}

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(PP_MAX_WARPS * 32, 1)
 pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
                     int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
                     const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kh_ld,
-                    int kj0, int kj1, int *status) {
+                    int kj0, int kj1, int krow0, int *status) {
     extern __shared__ uint8_t smr_raw[];
     uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
     const int nw = blockDim.x / 32;
@@ -103,6 +103,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const uint8_t *stage_p = smr + w * stage_bytes;
     float4 *md = smean + w * D;
     const CUtensorMap *tm = isq ? &tm_q : &tm_k;
+    const int row0 = isq ? 0 : krow0;   // window row of the tensor map's first row
     if (tid == 0) {
         *abort_flag = 0;
         for (int i = 0; i <= nw; ++i) mbar_init(smem_u32(mb + i), 1);
@@ -115,7 +116,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     int issued = 0, seen = 0;   // lane 0's loads into the stage, and those waited on
     if (lane == 0 && w < nblk) {
         mbar_arrive_expect_tx(full, stage_bytes);
-        tma_load_2d(stage, tm, h * D, (b0 + w) * block, full);
+        tma_load_2d(stage, tm, h * D, (b0 + w) * block - row0, full);
         issued = 1;
     }
     bool ok = true, w_seen = false;
@@ -140,7 +141,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (ok && lane == 0 && next < nblk) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive_expect_tx(full, stage_bytes);
-            tma_load_2d(stage, tm, h * D, (b0 + next) * block, full);
+            tma_load_2d(stage, tm, h * D, (b0 + next) * block - row0, full);
             ++issued;
         }
         const float fn = (float)n;
@@ -431,7 +432,7 @@ int router_check(const void *q, const void *k, const float *wq, const float *wk,
 // pool_project_kernel: blocks per CTA tile chosen as the fewest that keep the grid within one wave.
 static int pool_launch(int device, const void *q, const void *k, const float *wq, const float *wk, int H, int Lq,
                        int Lk, int R, int block, bool with_q, float *qh, float *kh, int kh_ld, int kj0, int kj1,
-                       int *status, cudaStream_t st) {
+                       int *status, cudaStream_t st, int krow0 = 0) {
     const int qb = with_q ? (Lq + block - 1) / block : 0, nk = kj1 - kj0;
     if (qb + nk <= 0) return 0;
     const int nsm = g_router_sms[device] > 0 ? g_router_sms[device] : 148;
@@ -441,7 +442,8 @@ static int pool_launch(int device, const void *q, const void *k, const float *wq
     const int nw = pp_warps(R, block);
     CUtensorMap tmq, tmk;
     const uint64_t row_bytes = (uint64_t)H * router::D * 2;
-    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)Lk, row_bytes, router::D, (uint32_t)block))
+    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)(Lk - krow0), row_bytes, router::D,
+                                 (uint32_t)block))
         return SS_ERR_DRIVER;
     if (with_q) {
         if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D,
@@ -451,7 +453,7 @@ static int pool_launch(int device, const void *q, const void *k, const float *wq
         tmq = tmk;   // no query tiles: the map is never read
     }
     router::pool_project_kernel<<<dim3(tq + tk, H), 32 * nw, pp_smem(R, block, nw), st>>>(
-        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kh_ld, kj0, kj1, status);
+        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kh_ld, kj0, kj1, krow0, status);
     return (int)cudaGetLastError();
 }
 
@@ -462,7 +464,7 @@ static int pool_launch(int device, const void *q, const void *k, const float *wq
 int router_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
                   int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores,
                   uint8_t *ws, int *status, cudaStream_t st, float *kh_ext = nullptr, int kh_ld_ext = 0,
-                  int n_cached = 0) {
+                  int n_cached = 0, int krow0 = 0) {
     const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block, kbp = kb_padded(kb);
     int device;
     cudaError_t e = cudaGetDevice(&device);
@@ -474,7 +476,7 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     float *kh = kh_ext ? kh_ext : reinterpret_cast<float *>(ws + L.kh);
     const int kh_ld = kh_ext ? kh_ld_ext : kbp;
     rc = pool_launch(device, q, k, wq, wk, H, Lq, Lk, R, block, true, qh, kh, kh_ld, kh_ext ? n_cached : 0, kb,
-                     status, st);
+                     status, st, krow0);
     if (rc) return rc;
     router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::SS_THREADS,
                                   select_smem(kbp, R), st>>>(qh, kh, kh_ld, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
@@ -573,19 +575,20 @@ extern "C" int ss_router_pool_keys(const void *k, const float *wk, int H, int Lk
                        status, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int ss_router_cached(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk,
-                                int R, int block, int sink_tokens, int extra, float *kh, int kh_rows, int n_cached,
-                                int32_t *ids, int n_ids, uint8_t *mask, float *scores, void *workspace,
+extern "C" int ss_router_cached(const void *q, const void *k, int k_row0, const float *wq, const float *wk, int H,
+                                int Lq, int Lk, int R, int block, int sink_tokens, int extra, float *kh, int kh_rows,
+                                int n_cached, int32_t *ids, int n_ids, uint8_t *mask, float *scores, void *workspace,
                                 size_t workspace_bytes, int *status, void *stream) {
     int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
     if (rc) return rc;
     if (!workspace || !kh) return SS_ERR_POINTER;
     const int kb = (Lk + block - 1) / block;
     if (kh_rows < kb || n_cached < 0 || n_cached > kb) return SS_ERR_SHAPE;
+    if (k_row0 < 0 || k_row0 > n_cached * block || k_row0 >= Lk) return SS_ERR_SHAPE;
     if (workspace_bytes < ss::router_workspace_size(H, Lq, Lk, R, block)) return SS_ERR_WORKSPACE;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) || (reinterpret_cast<uintptr_t>(kh) & 15u))
         return SS_ERR_POINTER;
     return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
                              static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream), kh,
-                             kh_rows, n_cached);
+                             kh_rows, n_cached, k_row0);
 }

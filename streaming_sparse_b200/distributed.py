@@ -1,28 +1,38 @@
 """Partitioning the routed sparse-attention path across the GPUs of one node.
 
-Three layouts, one process per GPU, ``torch.distributed`` (NCCL over NVLink/NVSwitch) for the
-exchanges. The reference runs one video per GPU in separate worker processes
-(local_experiments/video_runtime_v1/batch.py:29-37) and has no cross-GPU split of one
-attention call; its in-GPU split-K LSE merge (migration/unified_router/opt21/attention.py:7-15)
-is the exchange used here for KV-block sharding.
+Three layouts, one process per GPU, ``torch.distributed`` (NCCL) for set-up collectives. The
+reference runs one video per GPU in separate worker processes
+(local_experiments/video_runtime_v1/batch.py:29-37) and has no cross-GPU split of one attention
+call; its in-GPU split merge (migration/unified_router/opt21/attention.py:7-15) is the combine
+used here for KV-block sharding.
 
 * streams (replicas): every rank runs its own stream; no collective at all.
 * heads: rank r owns a contiguous range of heads. Router and attention are per head, so the
   call itself needs no exchange; ``gather_heads`` assembles the full [Lq,H,D] output for the
   o-projection (one all_gather).
-* KV blocks: rank r owns the blocks with ``id % world == r`` (block-cyclic, which spreads the
-  always-kept sink and current-chunk blocks evenly). Every rank computes the same router
-  selection (the exact-fp32 router is deterministic), attends over the blocks it owns, and the
-  partial results are merged by log-sum-exp: all_gather of the per-rank LSE, then an all_reduce
-  (sum) of the weighted fp32 partial outputs.
+* KV blocks (``KVShardedAttention``): rank r stores only the window blocks j with
+  ``j % world == r`` (block-cyclic, which spreads the always-kept sink and current-chunk blocks
+  evenly), packed into a local window. The history's pooled key projections are computed by
+  their owners and all-gathered once per commit; every rank then routes with the same exact-fp32
+  router (bit-identical ids everywhere), pooling the current chunk itself from the window's tail.
+  Each rank attends over its own selected blocks into buffers the other ranks have mapped (CUDA
+  IPC), and one kernel per rank (``ss_lse_merge_peers``, after the flag barrier
+  ``ss_peer_barrier``) reads all partials over NVLink and writes the merged rows.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 
 from . import ops
+from ._lib import check, lib
 
+
+# ----------------------------------------------------------------------------------------------
+# heads
+# ----------------------------------------------------------------------------------------------
 
 def head_range(H: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous head range [h0, h1) of ``rank`` (the first H % world ranks get one more)."""
@@ -51,48 +61,6 @@ def gather_heads(local: torch.Tensor, H: int, group=None) -> torch.Tensor:
     return torch.cat([b[:, :h1 - h0] for b, (h0, h1) in zip(bufs, sizes)], dim=1)
 
 
-def shard_ids(ids: torch.Tensor, rank: int, world: int) -> torch.Tensor:
-    """Keep the block ids this rank owns (block-cyclic ``id % world == rank``); others become -1."""
-    own = (ids >= 0) & (torch.remainder(ids, world) == rank)
-    return torch.where(own, ids, torch.full_like(ids, -1))
-
-
-def merge_partials(o_local: torch.Tensor, lse_local: torch.Tensor, group=None, out_dtype=torch.bfloat16):
-    """LSE merge of per-rank partial attention results over a process group.
-
-    o_local fp32 [Lq,H,D] (normalised over the rank's own blocks), lse_local fp32 [H,Lq]
-    (natural log, -inf where the rank saw no block). Returns (merged [Lq,H,D], global LSE [H,Lq]).
-    """
-    world = dist.get_world_size(group)
-    lses = [torch.empty_like(lse_local) for _ in range(world)]
-    dist.all_gather(lses, lse_local.contiguous(), group=group)
-    stacked = torch.stack(lses)                               # [W,H,Lq]
-    total = torch.logsumexp(stacked, dim=0)                   # [H,Lq]
-    safe = torch.where(torch.isfinite(total), total, torch.zeros_like(total))
-    w = torch.exp(lse_local - safe)                           # [H,Lq], 0 for empty parts
-    w = torch.where(torch.isfinite(total), w, torch.zeros_like(w))
-    weighted = o_local.float() * w.transpose(0, 1)[:, :, None]
-    dist.all_reduce(weighted, op=dist.ReduceOp.SUM, group=group)
-    return weighted.to(out_dtype), total
-
-
-class KVShardedAttention:
-    """Routed sparse attention with the KV blocks split block-cyclically over a process group."""
-
-    def __init__(self, sparse, group=None):
-        self.sparse = sparse          # a plugin.SparseAttention (router weights + config)
-        self.group = group
-
-    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-        rank, world = dist.get_rank(self.group), dist.get_world_size(self.group)
-        ids = self.sparse.route(q, k)
-        mine = shard_ids(ids, rank, world)
-        o, lse = ops.sparse_attention(q, k, v, mine, block=self.sparse.config.block, out_dtype=torch.float32,
-                                      return_lse=True)
-        out, _ = merge_partials(o, lse, self.group)
-        return out
-
-
 class HeadShardedAttention:
     """Routed sparse attention over this rank's heads; ``gather`` returns all heads."""
 
@@ -104,3 +72,224 @@ class HeadShardedAttention:
     def __call__(self, q_local, k_local, v_local, gather: bool = True):
         out = self.sparse.forward_one(q_local, k_local, v_local)
         return gather_heads(out, self.H, self.group) if gather else out
+
+
+# ----------------------------------------------------------------------------------------------
+# KV blocks: ownership and the local window
+# ----------------------------------------------------------------------------------------------
+
+def owned_blocks(kb: int, rank: int, world: int) -> range:
+    """Window blocks rank ``rank`` stores: j = rank, rank + world, ... (< kb)."""
+    return range(rank, kb, world)
+
+
+def local_len(Lk: int, block: int, rank: int, world: int) -> int:
+    """Tokens of rank ``rank``'s local window: its blocks packed in order. Only the window's last
+    block can be partial, and it is the last block of its owner, so every local block keeps the
+    valid-token count of the window block it holds."""
+    own = owned_blocks(ops.nblocks(Lk, block), rank, world)
+    if len(own) == 0:
+        return 0
+    return (len(own) - 1) * block + min(block, Lk - own[-1] * block)
+
+
+def local_rows(Lk: int, block: int, rank: int, world: int) -> torch.Tensor:
+    """Window row of each local row (int64, ascending)."""
+    own = torch.tensor(list(owned_blocks(ops.nblocks(Lk, block), rank, world)), dtype=torch.int64)
+    rows = (own[:, None] * block + torch.arange(block)[None]).reshape(-1)
+    return rows[rows < Lk]
+
+
+def shard_ids(ids: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """Keep the block ids this rank owns (window numbering); others become -1."""
+    own = (ids >= 0) & (torch.remainder(ids, world) == rank)
+    return torch.where(own, ids, torch.full_like(ids, -1))
+
+
+def local_ids(ids: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """The block ids this rank owns, renumbered into its local window (j -> j // world); others -1."""
+    own = (ids >= 0) & (torch.remainder(ids, world) == rank)
+    return torch.where(own, torch.div(ids, world, rounding_mode="floor"), torch.full_like(ids, -1))
+
+
+def assemble_keys(parts, world: int, n_blocks: int) -> torch.Tensor:
+    """Window key table [H, n_blocks, R] from the ranks' tables of their own blocks
+    (parts[r] [H, >= len(owned_blocks(n_blocks, r, world)), R]): window block j = jl*world + r is
+    row jl of parts[r]."""
+    H, _, R = parts[0].shape
+    out = parts[0].new_empty((H, n_blocks, R))
+    for r, part in enumerate(parts):
+        n = len(owned_blocks(n_blocks, r, world))
+        if n:
+            out[:, r::world][:, :n] = part[:, :n]
+    return out
+
+
+# ----------------------------------------------------------------------------------------------
+# buffers the ranks of a node read from each other (CUDA IPC through libssparse)
+# ----------------------------------------------------------------------------------------------
+
+class PeerBuffers:
+    """Device buffers that every rank of a group can read: each rank allocates its own (torch),
+    exports them (``ss_ipc_handle``) and maps everyone else's (``ss_ipc_open``) once.
+    ``ptrs[name][r]`` is rank r's buffer as a device address valid on this rank's GPU."""
+
+    def __init__(self, specs: dict, device, group=None):
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.local = {name: torch.zeros(shape, dtype=dtype, device=device) for name, (shape, dtype) in specs.items()}
+        torch.cuda.synchronize(device)
+        mine = {}
+        for name, t in self.local.items():
+            handle = (ctypes.c_char * 64)()
+            off = ctypes.c_size_t()
+            check(lib().ss_ipc_handle(ctypes.c_void_p(t.data_ptr()), handle, ctypes.byref(off)), "ss_ipc_handle")
+            mine[name] = (bytes(handle), off.value)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.ptrs, self._opened = {}, []
+        for name, t in self.local.items():
+            row = []
+            for r in range(self.world):
+                if r == self.rank:
+                    row.append(t.data_ptr())
+                    continue
+                handle, off = everyone[r][name]
+                buf = (ctypes.c_char * 64).from_buffer_copy(handle)
+                p = ctypes.c_void_p()
+                check(lib().ss_ipc_open(buf, off, ctypes.byref(p)), "ss_ipc_open")
+                row.append(p.value)
+                self._opened.append((p.value, off))
+            self.ptrs[name] = row
+        dist.barrier(group=group)        # every mapping exists before anyone writes through it
+
+    def close(self):
+        """Unmap the peers' buffers (every rank calls it; the buffers stay alive until all did)."""
+        for p, off in self._opened:
+            lib().ss_ipc_close(ctypes.c_void_p(p), off)
+        self._opened = []
+        dist.barrier(group=self.group)
+
+
+def _ptr_array(ptrs, offset: int = 0):
+    arr = (ctypes.c_void_p * len(ptrs))()
+    for i, p in enumerate(ptrs):
+        arr[i] = p + offset
+    return arr
+
+
+class KVShardedAttention:
+    """Routed sparse attention with the KV window split block-cyclically over a process group.
+
+    One instance serves one layer's window geometry (chunk of ``Lq`` tokens at the end of an
+    ``Lk``-token window). ``commit(k, v)`` takes a full window (post-RoPE K/V as the model's cache
+    holds it), keeps this rank's blocks, pools the projections of its history blocks and
+    all-gathers them (the commit-time pooling of the reference's streaming pipeline,
+    migration/unified_router/opt23/pipeline.py:22-29). ``__call__(q, k_chunk, v_chunk)`` is one
+    routed chunk-layer call: every rank passes the same chunk (its q/k/v come from the replicated
+    activations) and gets the merged bf16 output [Lq, H, D].
+    """
+
+    def __init__(self, sparse, Lq: int, Lk: int, device, group=None, part_dtype=torch.bfloat16):
+        self.sparse, self.group = sparse, group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the peer merge takes at most 8 ranks")
+        c = sparse.config
+        self.block, self.Lq, self.Lk = c.block, Lq, Lk
+        self.H = sparse.wq.shape[0]
+        self.R = sparse.wq.shape[2]
+        self.extra = c.extra(Lq, Lk)
+        self.kb = ops.nblocks(Lk, self.block)
+        self.n_hist = ops.history_blocks(Lq, Lk, self.block)      # blocks wholly before the chunk
+        self.row0 = self.n_hist * self.block                      # window row where the tail starts
+        self.Lk_local = local_len(Lk, self.block, self.rank, self.world)
+        rows = local_rows(Lk, self.block, self.rank, self.world)
+        self.rows = rows.to(device)
+        chunk0 = Lk - Lq
+        in_chunk = rows >= chunk0
+        self.chunk_src = (rows[in_chunk] - chunk0).to(device)     # chunk rows this rank stores
+        self.chunk_dst = torch.nonzero(in_chunk).reshape(-1).to(device)
+        D = ops.HEAD_DIM
+        self.k_local = torch.zeros((max(self.Lk_local, 1), self.H, D), dtype=torch.bfloat16, device=device)
+        self.v_local = torch.zeros_like(self.k_local)
+        self.k_tail = torch.zeros((Lk - self.row0, self.H, D), dtype=torch.bfloat16, device=device)
+        self.keys = ops.RouterKeys(self.H, Lk, block=self.block, R=self.R, device=device)
+        self.ws = ops.Workspace()
+        self.part_fp32 = part_dtype == torch.float32
+        self.peer = PeerBuffers({"o": ((2, Lq, self.H, D), part_dtype), "lse": ((2, self.H, Lq), torch.float32),
+                                 "flags": ((self.world,), torch.int32)}, device, group)
+        self.o_bytes = Lq * self.H * D * (4 if self.part_fp32 else 2)
+        self.lse_bytes = self.H * Lq * 4
+        self.epoch = 0
+        self.calls = 0
+        self.device = device
+        self.last_ids = None
+
+    def commit(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Take the window [Lk, H, D] (the history rows matter; the chunk rows are rewritten by
+        every call): keep this rank's blocks, pool the projections of its history blocks, and
+        all-gather them into the window key table shared by every rank's router."""
+        assert k.shape == (self.Lk, self.H, ops.HEAD_DIM) and v.shape == k.shape
+        if self.Lk_local:
+            self.k_local[:self.Lk_local] = k.index_select(0, self.rows)
+            self.v_local[:self.Lk_local] = v.index_select(0, self.rows)
+        self.k_tail.copy_(k[self.row0:])
+        n_own = len(owned_blocks(self.n_hist, self.rank, self.world))
+        n_max = len(owned_blocks(self.n_hist, 0, self.world))
+        mine = torch.zeros((self.H, max(n_max, 1), self.R), dtype=torch.float32, device=self.device)
+        if n_own:
+            part = ops.RouterKeys(self.H, self.Lk_local, block=self.block, R=self.R, device=self.device)
+            ops.pool_keys(self.k_local[:self.Lk_local], self.sparse.wk, part, j0=0, j1=n_own)
+            mine[:, :n_own] = part.kh[:, :n_own]
+        gathered = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(gathered, mine, group=self.group)
+        if self.n_hist:
+            self.keys.kh[:, :self.n_hist] = assemble_keys(gathered, self.world, self.n_hist)
+        self.keys.mark(("kv-shard", id(self), self.epoch), self.n_hist)
+
+    def route(self, q: torch.Tensor) -> torch.Tensor:
+        c = self.sparse.config
+        return ops.route(q, self.k_tail, self.sparse.wq, self.sparse.wk, block=self.block, extra=self.extra,
+                         sink_tokens=c.sink_tokens, workspace=self.ws, keys=self.keys, n_cached=self.n_hist,
+                         k_row0=self.row0)
+
+    def __call__(self, q: torch.Tensor, k_chunk: torch.Tensor, v_chunk: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        Lq, H, D = q.shape
+        assert Lq == self.Lq and k_chunk.shape == q.shape and v_chunk.shape == q.shape
+        # this rank's rows of the chunk into its local window; the whole chunk into the tail
+        if self.chunk_dst.numel():
+            self.k_local.index_copy_(0, self.chunk_dst, k_chunk.index_select(0, self.chunk_src))
+            self.v_local.index_copy_(0, self.chunk_dst, v_chunk.index_select(0, self.chunk_src))
+        self.k_tail[self.Lk - Lq - self.row0:].copy_(k_chunk)
+        ids = self.route(q)                        # identical on every rank (exact-fp32 router)
+        self.last_ids = ids
+        slot = self.calls % 2
+        o_part = self.peer.local["o"][slot]
+        lse_part = self.peer.local["lse"][slot]
+        if self.Lk_local:
+            ops.sparse_attention(q, self.k_local[:self.Lk_local], self.v_local[:self.Lk_local],
+                                 local_ids(ids, self.rank, self.world), block=self.block,
+                                 out_dtype=torch.float32 if self.part_fp32 else torch.bfloat16, return_lse=True,
+                                 out=o_part, lse=lse_part)
+        else:
+            o_part.zero_()
+            lse_part.fill_(float("-inf"))
+        # every rank's partial is written -> merged rows over peer memory
+        self.epoch += 1
+        stream = ops._stream(self.device)
+        status = ops.DeviceStatus.word(self.device)
+        check(lib().ss_peer_barrier(_ptr_array(self.peer.ptrs["flags"]), self.rank, self.world, self.epoch,
+                                    ops._p(status), stream), "ss_peer_barrier")
+        if out is None:
+            out = torch.empty((Lq, H, D), dtype=torch.bfloat16, device=self.device)
+        check(lib().ss_lse_merge_peers(_ptr_array(self.peer.ptrs["o"], slot * self.o_bytes),
+                                       _ptr_array(self.peer.ptrs["lse"], slot * self.lse_bytes), self.world,
+                                       1 if self.part_fp32 else 0, H, Lq, 0, Lq, ops._p(out), 0, None, stream),
+              "ss_lse_merge_peers")
+        self.calls += 1
+        return out
+
+    def close(self):
+        self.peer.close()

@@ -149,7 +149,7 @@ def router_workspace_bytes(H: int, Lq: int, Lk: int, R: int = 64, block: int = 6
 
 def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, return_mask: bool = False,
           return_scores: bool = False, workspace: Workspace | None = None, out: torch.Tensor | None = None,
-          validate: bool = False, keys: RouterKeys | None = None, n_cached: int = 0):
+          validate: bool = False, keys: RouterKeys | None = None, n_cached: int = 0, k_row0: int = 0):
     """Block ids per (head, query block): forced blocks plus the ``extra`` best-scoring others.
 
     q [Lq,H,128] bf16 (current chunk), k [Lk,H,128] bf16 (visible window, current chunk last),
@@ -159,11 +159,14 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
     ``keys``: a ``RouterKeys`` table whose first ``n_cached`` rows hold this window's key-block
     projections (``ss_router_cached``): only the query blocks and key blocks [n_cached, kb) are
     pooled, their projections written into the table. The ids are those of the uncached call.
+    ``k_row0`` (with ``keys``): k holds only the window rows [k_row0, Lk), k_row0 <= n_cached*block
+    (a KV-sharded rank: the tail of the window, the history before it represented by ``keys``).
     """
     q = _tokens(q, "q")
     k = _tokens(k, "k")
     Lq, H, _ = q.shape
-    Lk = k.shape[0]
+    Lk = k.shape[0] + k_row0
+    _require(k_row0 == 0 or (keys is not None and 0 <= k_row0 <= n_cached * block), "k_row0 needs keys covering it")
     _require(k.shape[1] == H and k.device == q.device, "q/k head count or device mismatch")
     _require(wq.shape == wk.shape and wq.dim() == 3 and wq.shape[0] == H and wq.shape[1] == HEAD_DIM,
              "wq/wk must be [H,128,R]")
@@ -188,7 +191,7 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
         _require(keys.block == block and keys.R == R and keys.kh.shape[0] == H and keys.kh.device == q.device,
                  "RouterKeys geometry differs from this call")
         _require(0 <= n_cached <= kb and keys.kh.shape[1] >= kb, "n_cached or RouterKeys rows out of range")
-        rc = lib().ss_router_cached(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra,
+        rc = lib().ss_router_cached(_p(q), _p(k), int(k_row0), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra,
                                     _p(keys.kh), keys.kh.shape[1], int(n_cached), _p(ids), n_ids, _p(mask),
                                     _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
         check(rc, "ss_router_cached")

@@ -73,11 +73,11 @@ def test_host_argument_errors(lib):
     assert lib.ss_router_pool_keys(fake, fake, 12, 32760, 64, 64, 10, 5, fake, 512, None, None) == 1001
     assert lib.ss_router_pool_keys(fake, fake, 12, 32760, 64, 64, 0, 438, fake, 511, None, None) == 1001
     assert lib.ss_router_pool_keys(fake, None, 12, 32760, 64, 64, 0, 438, fake, 512, None, None) == 1002
-    assert lib.ss_router_cached(fake, fake, fake, fake, 12, 4680, 32760, 64, 64, 0, 54, fake, 511, 438, fake, 128,
+    assert lib.ss_router_cached(fake, fake, 0, fake, fake, 12, 4680, 32760, 64, 64, 0, 54, fake, 511, 438, fake, 128,
                                 None, None, fake, ws, None, None) == 1001
-    assert lib.ss_router_cached(fake, fake, fake, fake, 12, 4680, 32760, 64, 64, 0, 54, fake, 512, 513, fake, 128,
+    assert lib.ss_router_cached(fake, fake, 0, fake, fake, 12, 4680, 32760, 64, 64, 0, 54, fake, 512, 513, fake, 128,
                                 None, None, fake, ws, None, None) == 1001
-    assert lib.ss_router_cached(fake, fake, fake, fake, 12, 4680, 32760, 64, 64, 0, 54, None, 512, 438, fake, 128,
+    assert lib.ss_router_cached(fake, fake, 0, fake, fake, 12, 4680, 32760, 64, 64, 0, 54, None, 512, 438, fake, 128,
                                 None, None, fake, ws, None, None) == 1002
     # merge / cache shape checks
     assert lib.ss_lse_merge(fake, fake, 0, 12, 10, fake, 0, None, None) == 1001

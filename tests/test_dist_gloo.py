@@ -63,16 +63,43 @@ def _inputs():
 
 
 def kv_shard_rank(rank, world):
-    from streaming_sparse_b200.distributed import merge_partials, shard_ids
+    """This rank's partial over its local window (its own blocks, packed) with the ids renumbered
+    into it -- the layout KVShardedAttention gives the attention kernel -- gathered to every rank
+    and combined by the LSE merge."""
+    from streaming_sparse_b200.distributed import local_ids, local_len, local_rows
     o, q, k, v, ids = _inputs()
-    mine = shard_ids(torch.from_numpy(ids), rank, world).numpy()
-    part, lse = o.attention(q, k, v, mine, 64)
+    Lk = k.shape[0]
+    rows = local_rows(Lk, 64, rank, world).numpy()
+    assert len(rows) == local_len(Lk, 64, rank, world)
+    mine = local_ids(torch.from_numpy(ids), rank, world).numpy()
+    part, lse = o.attention(q, k[rows], v[rows], mine, 64)
     lse = np.where(np.isnan(lse), -np.inf, lse)
-    empty = np.isneginf(lse).T[:, :, None]
-    part = np.where(empty, 0.0, part)
-    out, total = merge_partials(torch.from_numpy(part).float(), torch.from_numpy(lse).float(),
-                                out_dtype=torch.float32)
-    return out.numpy(), total.numpy()
+    part = np.where(np.isneginf(lse).T[:, :, None], 0.0, part)
+    parts = [torch.empty(0)] * world
+    dist.all_gather_object(parts, (part.astype(np.float32), lse.astype(np.float32)))
+    return o.lse_merge(np.stack([p_[0] for p_ in parts]), np.stack([p_[1] for p_ in parts]))
+
+
+def kv_keys_rank(rank, world):
+    """Every rank pools the history blocks it owns from its local window; the all-gathered tables
+    assembled into window order must equal the projections of the whole window's blocks."""
+    from streaming_sparse_b200.distributed import assemble_keys, local_len, local_rows, owned_blocks
+    o, q, k, v, ids = _inputs()
+    Lk = k.shape[0]
+    wk = np.random.default_rng(8).standard_normal((k.shape[1], 128, 64)).astype(np.float32) / math.sqrt(128)
+    n_hist = (Lk - q.shape[0]) // 64
+    rows = local_rows(Lk, 64, rank, world).numpy()
+    n_own = len(owned_blocks(n_hist, rank, world))
+    n_max = len(owned_blocks(n_hist, 0, world))
+    mine = np.zeros((k.shape[1], max(n_max, 1), 64), np.float32)
+    if n_own:
+        _, kh = o.pool_project(k[rows][:n_own * 64], wk, 64)
+        mine[:, :n_own] = kh
+    parts = [None] * world
+    dist.all_gather_object(parts, mine)
+    table = assemble_keys([torch.from_numpy(p_) for p_ in parts], world, n_hist).numpy()
+    _, whole = o.pool_project(k, wk, 64)
+    return table, whole[:, :n_hist], local_len(Lk, 64, rank, world)
 
 
 def head_shard_rank(rank, world):
@@ -85,13 +112,28 @@ def head_shard_rank(rank, world):
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_kv_sharded_lse_merge_equals_full(world):
-    """World 3: block-cyclic ownership leaves some ranks without blocks for some rows (LSE -inf)."""
+    """World 3: block-cyclic ownership leaves some ranks without blocks for some rows (LSE -inf);
+    the window's partial last block (900 = 14 x 64 + 4 tokens) is the last local block of its
+    owner."""
     res = _run(kv_shard_rank, world)
     o, q, k, v, ids = _inputs()
     ref, ref_lse = o.attention(q, k, v, ids, 64)
     for r in range(world):
         np.testing.assert_allclose(res[r][0], ref, rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(res[r][1], ref_lse, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_kv_sharded_history_keys_gather(world):
+    """The history's key projections pooled by their owners and all-gathered are the whole
+    window's, bit for bit (the router then runs identically on every rank)."""
+    res = _run(kv_keys_rank, world)
+    lens = []
+    for r in range(world):
+        table, whole, n = res[r]
+        np.testing.assert_array_equal(table.view(np.uint32), whole.view(np.uint32))
+        lens.append(n)
+    assert sum(lens) == 900
 
 
 @pytest.mark.parametrize("world", [2, 3])
@@ -101,6 +143,20 @@ def test_head_sharded_gather_equals_full(world):
     ref, _ = o.attention(q, k, v, ids, 64)
     for r in range(world):
         np.testing.assert_allclose(res[r], ref, rtol=1e-6, atol=1e-7)
+
+
+def test_local_window_geometry():
+    from streaming_sparse_b200.distributed import local_ids, local_len, local_rows, owned_blocks
+    # config 4 at 8 ranks: 34320 tokens in 128-token blocks -> 269 blocks, the last one 16 tokens
+    Lk, block = 34320, 128
+    assert sum(local_len(Lk, block, r, 8) for r in range(8)) == Lk
+    last_owner = (268) % 8
+    assert local_len(Lk, block, last_owner, 8) == (len(owned_blocks(269, last_owner, 8)) - 1) * 128 + 16
+    rows = [local_rows(Lk, block, r, 8) for r in range(8)]
+    assert torch.equal(torch.sort(torch.cat(rows)).values, torch.arange(Lk))
+    ids = torch.tensor([[[0, 5, 8, 13, -1]]], dtype=torch.int32)
+    assert local_ids(ids, 0, 8).tolist() == [[[0, -1, 1, -1, -1]]]
+    assert local_ids(ids, 5, 8).tolist() == [[[-1, 0, -1, 1, -1]]]
 
 
 def test_head_range_and_shard_ids():

@@ -1,5 +1,6 @@
 """The multi-GPU layouts on real GPUs: NCCL ranks (one process per GPU, spawned), KV-block sharding
-with the LSE merge and head sharding with the all_gather, each against the single-GPU result.
+(each rank stores its own blocks, the history keys all-gathered at commit, the partials merged
+over peer memory) and head sharding with the all_gather, each against the single-GPU result.
 Skipped where fewer than two GPUs are visible."""
 import datetime
 import os
@@ -39,16 +40,24 @@ def _worker(rank, world, port, q_out):
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=dev)
+        from streaming_sparse_b200 import ops
         from streaming_sparse_b200.distributed import HeadShardedAttention, KVShardedAttention, head_shard
         from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
         q, k, v, wq, wk = (t.to(dev) for t in _inputs())
         cfg = RouterConfig(density=0.25)
-        kv = KVShardedAttention(SparseAttention(wq, wk, cfg))(q[None], k[None], v[None])
+        shard = KVShardedAttention(SparseAttention(wq, wk, cfg), LQ, LK, dev)
+        shard.commit(k, v)
+        c0 = LK - LQ
+        outs = [shard(q, k[c0:], v[c0:]) for _ in range(3)]      # both partial slots, then the first again
+        ids = shard.last_ids.cpu().numpy()
         hs = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg),
                                   H)(head_shard(q, rank, world), head_shard(k, rank, world), head_shard(v, rank, world))
         torch.cuda.synchronize()
-        q_out.put((rank, kv.float().cpu().numpy(), hs.float().cpu().numpy()))
+        ops.DeviceStatus.check(dev)
+        same = all(torch.equal(outs[0], o_) for o_ in outs[1:])
+        q_out.put((rank, (outs[0].float().cpu().numpy(), ids, same), hs.float().cpu().numpy()))
         dist.barrier()
+        shard.close()
         dist.destroy_process_group()
     except Exception as e:   # report to the parent instead of hanging it
         q_out.put((rank, repr(e), None))
@@ -77,12 +86,17 @@ def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
             if p.is_alive():      # a rank that never reported: end it rather than leave it running
                 p.terminate()
                 p.join(timeout=30)
+    assert len(results) == 2
     for rank, (kv, hs) in results.items():
         assert not isinstance(kv, str), f"rank {rank}: {kv}"
     # the single-GPU path, same inputs
     dev = torch.device("cuda:0")
     q, k, v, wq, wk = (t.to(dev) for t in _inputs())
-    whole = SparseAttention(wq, wk, RouterConfig(density=0.25))(q[None], k[None], v[None])[0].float().cpu().numpy()
-    for rank, (kv, hs) in results.items():
+    sp = SparseAttention(wq, wk, RouterConfig(density=0.25))
+    whole = sp(q[None], k[None], v[None])[0].float().cpu().numpy()
+    whole_ids = sp.last_ids.cpu().numpy()
+    for rank, ((kv, ids, same), hs) in results.items():
+        np.testing.assert_array_equal(ids, whole_ids)          # the sharded router: same ids, bit for bit
+        assert same                                            # repeated calls through both partial slots
         assert_attention_close(kv, whole)                       # KV-block shards merged by LSE
         np.testing.assert_array_equal(hs, whole)               # heads are independent: identical bits
