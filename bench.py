@@ -597,6 +597,114 @@ def rollout4_bench(dev, args):
     return res
 
 
+def sharded_bench(dev, args, rank: int, world: int) -> dict:
+    """Config 4's chunk-layer (4680 queries against a 34320-token window with a sink frame,
+    128-token blocks, 10 % of the unforced blocks) split over the N GPUs, next to the same call on
+    one GPU (every rank builds the same seeded window):
+
+    * ``kv``: KV-block sharding. Each rank stores its own blocks, the history keys are pooled by
+      their owners and all-gathered at commit (outside the timed region, once per chunk), and a
+      call routes, attends over the rank's blocks and merges all ranks' partials over peer memory
+      (flag barrier + one merge kernel).
+    * ``heads``: head sharding, each rank routing and attending over its heads, then one NCCL
+      all_gather of the outputs.
+    Each is checked once against the single-GPU output (router ids bit for bit for ``kv``; max-abs,
+    mean-abs and NMSE of the output), then timed as CUDA-graph replays (two calls per graph),
+    max over ranks. ``merge_share``: the part of a KV-sharded call that a graph without the
+    barrier and merge does not take."""
+    import torch.distributed as dist
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.distributed import HeadShardedAttention, KVShardedAttention, head_shard, local_ids
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
+
+    lq, lk, block, sink = 4680, 34320, 128, 1560
+    cfg = RouterConfig(block=block, density=0.10, rule="rest", sink_tokens=sink)
+    g = torch.Generator().manual_seed(404)
+    q = torch.randn((lq, H, D), generator=g).bfloat16().to(dev)
+    k = torch.randn((lk, H, D), generator=g).bfloat16().to(dev)
+    v = torch.randn((lk, H, D), generator=g).bfloat16().to(dev)
+    wq = (torch.randn((H, D, 64), generator=g) / math.sqrt(D)).to(dev)
+    wk = (torch.randn((H, D, 64), generator=g) / math.sqrt(D)).to(dev)
+    sp = SparseAttention(wq, wk, cfg)
+    whole = sp.forward_one(q, k, v)
+    whole_ids = sp.last_ids.clone()
+    reps = max(10, min(50, args.steps))
+
+    def graph_us(calls):
+        """us per call: a graph of two calls, replayed `reps` times after warm-up, max over ranks."""
+        for _ in range(2):
+            calls()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            calls()
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            gr.replay()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) * 1e3 / (2 * reps)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        del gr
+        return float(t)
+
+    def err(x):
+        d = (x.float() - whole.float()).abs()
+        return {"max_abs": float(d.max()), "mean_abs": float(d.mean()),
+                "nmse": float((d.double() ** 2).sum() / (whole.double() ** 2).sum())}
+
+    o1 = torch.empty_like(q)
+    single = graph_us(lambda: (sp.forward_one(q, k, v, out=o1), sp.forward_one(q, k, v, out=o1)))
+    res = {"config": "config4 chunk-layer: 4680 q x 34320 KV (21 frames + 1 sink frame), b128, 10% of unforced",
+           "single_gpu_us": single}
+
+    # ---- KV blocks
+    shard = KVShardedAttention(SparseAttention(wq, wk, cfg), lq, lk, dev)
+    shard.commit(k, v)
+    c0 = lk - lq
+    kc, vc = k[c0:].clone(), v[c0:].clone()
+    out = shard(q, kc, vc)
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    kv = dict(err(out), ids_equal=bool(torch.equal(shard.last_ids, whole_ids)))
+    ob = torch.empty_like(q)
+    kv["us"] = graph_us(lambda: (shard(q, kc, vc, out=ob), shard(q, kc, vc, out=ob)))
+
+    def local_part():
+        ids = shard.route(q)
+        ops.sparse_attention(q, shard.k_local[:shard.Lk_local], shard.v_local[:shard.Lk_local],
+                             local_ids(ids, rank, world), block=block, return_lse=True,
+                             out=shard.peer.local["o"][0], lse=shard.peer.local["lse"][0])
+    kv["local_us"] = graph_us(lambda: (local_part(), local_part()))
+    kv["merge_share"] = max(0.0, 1.0 - kv["local_us"] / kv["us"])
+    kv["speedup_vs_1gpu"] = single / kv["us"]
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    dist.barrier()
+    shard.close()
+    res["kv"] = kv
+
+    # ---- heads
+    sph = SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg)
+    hq, hk, hv = head_shard(q, rank, world), head_shard(k, rank, world), head_shard(v, rank, world)
+    hs = HeadShardedAttention(sph, H)
+    hout = hs(hq, hk, hv)
+    torch.cuda.synchronize()
+    heads = dict(err(hout), bit_exact=bool(torch.equal(hout, whole)))
+    heads["us"] = graph_us(lambda: (hs(hq, hk, hv), hs(hq, hk, hv)))
+    heads["speedup_vs_1gpu"] = single / heads["us"]
+    res["heads"] = heads
+    del shard, hs
+    torch.cuda.empty_cache()
+    return res
+
+
 def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> dict:
     """The config-2 chunk-layer as a streaming caller makes it (the reference's per-layer
     ``self_attn.forward(..., kv_cache, current_start)``, wan/modules/causal_model.py:216-253):
@@ -883,6 +991,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     _, hbm_gbs, _ = peaks()
     hbm_k = hbm_kernels_bench(dev, args, hbm_gbs)
 
+    # ---- config 4's chunk-layer split over the GPUs (KV blocks / heads), N > 1
+    sharded = sharded_bench(dev, args, rank, world) if world > 1 and not args.no_sharded else None
+
     # ---- config 3: streaming rollout of the DiT with the plugin in every layer (latent frames/s)
     rollout = None
     if not args.no_rollout:
@@ -899,7 +1010,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # Detail records first, one JSON object per line; the last line is the bench line proper,
     # short enough that a reader keeping only the tail of stdout still sees every headline figure.
     details = {"e2e_streaming": streaming, "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
-               "hbm_kernels": hbm_k, "rollout": rollout, "other_configs": other}
+               "hbm_kernels": hbm_k, "rollout": rollout, "other_configs": other, "sharded": sharded}
     for name, rec in details.items():
         if rec is not None:
             print(json.dumps({"detail": name, "record": rec}), flush=True)
@@ -937,6 +1048,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "config4_frames_s": None if rollout["config4_long_horizon"] is None else
             r(rollout["config4_long_horizon"]["value"], 2)},
         "configs_frac": None if other is None else {o["short"]: [r(o["us"]), r(o["frac_of_peak"], 3)] for o in other},
+        "sharded": None if sharded is None else {
+            "c4_1gpu_us": r(sharded["single_gpu_us"]),
+            "kv": {"us": r(sharded["kv"]["us"]), "x": r(sharded["kv"]["speedup_vs_1gpu"], 2),
+                   "merge_share": r(sharded["kv"]["merge_share"], 3), "ids_equal": sharded["kv"]["ids_equal"],
+                   "max_abs": r(sharded["kv"]["max_abs"], 5), "nmse": sharded["kv"]["nmse"]},
+            "heads": {"us": r(sharded["heads"]["us"]), "x": r(sharded["heads"]["speedup_vs_1gpu"], 2),
+                      "bit_exact": sharded["heads"]["bit_exact"]}},
     }
     print(json.dumps(line), flush=True)
 
@@ -952,6 +1070,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rollout", action="store_true", help="skip the config-3 rollout measurement")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-shape measurements of configs 1, 4, 5")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the KV-block / head sharded config-4 chunk-layer")
     ap.add_argument("--only-hbm-kernels", action="store_true",
                     help="measure only the cache append / roll, LSE merge and anchor rebase kernels")
     args = ap.parse_args()

@@ -211,12 +211,15 @@ int ss_ipc_open(const void *handle, size_t offset, void **ptr);
 /* Unmap a pointer returned by ss_ipc_open (same offset). */
 int ss_ipc_close(void *ptr, size_t offset);
 
-/* flags: P device pointers (flags[p] = rank p's int array of >= P entries, the others opened
- * with ss_ipc_open). Posts epoch into slot `rank` of every rank's array, then waits until this
- * rank's slots 0..P-1 all hold epoch or later. Epochs must increase from call to call. Writes
- * enqueued before the barrier on each rank are visible to every rank's work enqueued after it.
- * A wait that runs out (about 2 s) sets SS_DEV_TIMEOUT in *status instead of hanging. */
-int ss_peer_barrier(int *const *flags, int rank, int P, int epoch, int *status, void *stream);
+/* flags: P device pointers (flags[p] = rank p's int array of >= P entries, zeroed before first
+ * use, the others opened with ss_ipc_open); epoch: this rank's device int counter (zeroed before
+ * first use), advanced by one per call on the device, so a call captured in a CUDA graph posts a
+ * new epoch at every replay. Posts the epoch into slot `rank` of every rank's array, then waits
+ * until this rank's slots 0..P-1 all hold it or a later one. Every rank makes the same number of
+ * calls. Writes enqueued before the barrier on each rank are visible to every rank's work
+ * enqueued after it. A wait that runs out (about 2 s) sets SS_DEV_TIMEOUT in *status instead of
+ * hanging. */
+int ss_peer_barrier(int *const *flags, int rank, int P, int *epoch, int *status, void *stream);
 
 /* Rows [row0, row1) of out [Lq][H][128] (out_dtype 0 = bf16, 1 = fp32) =
  * sum_p exp(lse_p - L) o_p with L = logsumexp_p lse_p, where o_parts[p] is part p's [Lq][H][128]

@@ -43,11 +43,16 @@ __device__ __forceinline__ int ld_acquire_sys(const int *p) {
     return v;
 }
 
-// One warp. Lane p < P posts `epoch` into slot `rank` of peer p's flags, then waits until slot p
-// of this rank's flags holds epoch (or later). Every wait is bounded: after ~2 s the kernel sets
+// One warp. The epoch is this rank's counter + 1 (the counter lives in device memory and is
+// advanced here, so a captured and replayed barrier still posts a new epoch each time). Lane
+// p < P posts the epoch into slot `rank` of peer p's flags, then waits until slot p of this
+// rank's flags holds it (or a later one). Every wait is bounded: after ~2 s the kernel sets
 // SS_DEV_TIMEOUT in *status and returns.
-__global__ void __launch_bounds__(32) barrier_kernel(Flags fl, int rank, int P, int epoch, int *status) {
+__global__ void __launch_bounds__(32) barrier_kernel(Flags fl, int rank, int P, int *counter, int *status) {
     const int p = threadIdx.x;
+    const int epoch = *counter + 1;
+    __syncwarp();
+    if (p == 0) *counter = epoch;
     if (p < P) {
         __threadfence_system();                  // this rank's earlier writes before the post
         st_release_sys(fl.f[p] + rank, epoch);
@@ -182,9 +187,9 @@ extern "C" int ss_ipc_close(void *ptr, size_t offset) {
     return (int)cudaIpcCloseMemHandle(static_cast<uint8_t *>(ptr) - offset);
 }
 
-extern "C" int ss_peer_barrier(int *const *flags, int rank, int P, int epoch, int *status, void *stream) {
+extern "C" int ss_peer_barrier(int *const *flags, int rank, int P, int *epoch, int *status, void *stream) {
     using namespace ss;
-    if (!flags) return SS_ERR_POINTER;
+    if (!flags || !epoch) return SS_ERR_POINTER;
     if (P <= 0 || P > SS_MAX_PEERS || rank < 0 || rank >= P) return SS_ERR_SHAPE;
     peer::Flags fl;
     for (int p = 0; p < SS_MAX_PEERS; ++p) fl.f[p] = p < P ? flags[p] : nullptr;

@@ -130,37 +130,40 @@ def assemble_keys(parts, world: int, n_blocks: int) -> torch.Tensor:
 # ----------------------------------------------------------------------------------------------
 
 class PeerBuffers:
-    """Device buffers that every rank of a group can read: each rank allocates its own (torch),
-    exports them (``ss_ipc_handle``) and maps everyone else's (``ss_ipc_open``) once.
+    """Device buffers that every rank of a group can read: each rank allocates its own (one torch
+    allocation, carved into the named buffers at 256-byte boundaries), exports it
+    (``ss_ipc_handle``) and maps everyone else's (``ss_ipc_open``) once.
     ``ptrs[name][r]`` is rank r's buffer as a device address valid on this rank's GPU."""
 
     def __init__(self, specs: dict, device, group=None):
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
-        self.local = {name: torch.zeros(shape, dtype=dtype, device=device) for name, (shape, dtype) in specs.items()}
+        offsets, total = {}, 0
+        for name, (shape, dtype) in specs.items():
+            offsets[name] = total
+            n = torch.Size(shape).numel() * torch.empty((), dtype=dtype).element_size()
+            total += (n + 255) // 256 * 256
+        self.storage = torch.zeros(total, dtype=torch.uint8, device=device)
+        self.local = {name: self.storage[offsets[name]:].view(dtype)[:torch.Size(shape).numel()].view(shape)
+                      for name, (shape, dtype) in specs.items()}
         torch.cuda.synchronize(device)
-        mine = {}
-        for name, t in self.local.items():
-            handle = (ctypes.c_char * 64)()
-            off = ctypes.c_size_t()
-            check(lib().ss_ipc_handle(ctypes.c_void_p(t.data_ptr()), handle, ctypes.byref(off)), "ss_ipc_handle")
-            mine[name] = (bytes(handle), off.value)
+        handle = (ctypes.c_char * 64)()
+        off = ctypes.c_size_t()
+        check(lib().ss_ipc_handle(ctypes.c_void_p(self.storage.data_ptr()), handle, ctypes.byref(off)),
+              "ss_ipc_handle")
         everyone = [None] * self.world
-        dist.all_gather_object(everyone, mine, group=group)
-        self.ptrs, self._opened = {}, []
-        for name, t in self.local.items():
-            row = []
-            for r in range(self.world):
-                if r == self.rank:
-                    row.append(t.data_ptr())
-                    continue
-                handle, off = everyone[r][name]
-                buf = (ctypes.c_char * 64).from_buffer_copy(handle)
-                p = ctypes.c_void_p()
-                check(lib().ss_ipc_open(buf, off, ctypes.byref(p)), "ss_ipc_open")
-                row.append(p.value)
-                self._opened.append((p.value, off))
-            self.ptrs[name] = row
+        dist.all_gather_object(everyone, (bytes(handle), off.value), group=group)
+        bases, self._opened = [], []
+        for r in range(self.world):
+            if r == self.rank:
+                bases.append(self.storage.data_ptr())
+                continue
+            h, o = everyone[r]
+            p = ctypes.c_void_p()
+            check(lib().ss_ipc_open((ctypes.c_char * 64).from_buffer_copy(h), o, ctypes.byref(p)), "ss_ipc_open")
+            bases.append(p.value)
+            self._opened.append((p.value, o))
+        self.ptrs = {name: [b + offsets[name] for b in bases] for name in specs}
         dist.barrier(group=group)        # every mapping exists before anyone writes through it
 
     def close(self):
@@ -187,7 +190,9 @@ class KVShardedAttention:
     all-gathers them (the commit-time pooling of the reference's streaming pipeline,
     migration/unified_router/opt23/pipeline.py:22-29). ``__call__(q, k_chunk, v_chunk)`` is one
     routed chunk-layer call: every rank passes the same chunk (its q/k/v come from the replicated
-    activations) and gets the merged bf16 output [Lq, H, D].
+    activations) and gets the merged bf16 output [Lq, H, D]. A call has no host synchronisation
+    and can be captured in a CUDA graph (capture calls in pairs: they alternate between two
+    partial buffers); every rank makes the same calls in the same order.
     """
 
     def __init__(self, sparse, Lq: int, Lk: int, device, group=None, part_dtype=torch.bfloat16):
@@ -219,9 +224,9 @@ class KVShardedAttention:
         self.part_fp32 = part_dtype == torch.float32
         self.peer = PeerBuffers({"o": ((2, Lq, self.H, D), part_dtype), "lse": ((2, self.H, Lq), torch.float32),
                                  "flags": ((self.world,), torch.int32)}, device, group)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)   # advanced by the barrier kernel
         self.o_bytes = Lq * self.H * D * (4 if self.part_fp32 else 2)
         self.lse_bytes = self.H * Lq * 4
-        self.epoch = 0
         self.calls = 0
         self.device = device
         self.last_ids = None
@@ -246,7 +251,7 @@ class KVShardedAttention:
         dist.all_gather(gathered, mine, group=self.group)
         if self.n_hist:
             self.keys.kh[:, :self.n_hist] = assemble_keys(gathered, self.world, self.n_hist)
-        self.keys.mark(("kv-shard", id(self), self.epoch), self.n_hist)
+        self.keys.mark(("kv-shard", id(self)), self.n_hist)
 
     def route(self, q: torch.Tensor) -> torch.Tensor:
         c = self.sparse.config
@@ -277,10 +282,9 @@ class KVShardedAttention:
             o_part.zero_()
             lse_part.fill_(float("-inf"))
         # every rank's partial is written -> merged rows over peer memory
-        self.epoch += 1
         stream = ops._stream(self.device)
         status = ops.DeviceStatus.word(self.device)
-        check(lib().ss_peer_barrier(_ptr_array(self.peer.ptrs["flags"]), self.rank, self.world, self.epoch,
+        check(lib().ss_peer_barrier(_ptr_array(self.peer.ptrs["flags"]), self.rank, self.world, ops._p(self.epoch),
                                     ops._p(status), stream), "ss_peer_barrier")
         if out is None:
             out = torch.empty((Lq, H, D), dtype=torch.bfloat16, device=self.device)
