@@ -33,6 +33,36 @@ def test_every_declared_symbol_is_exported(lib):
         assert name in SIGNATURES, f"{name} has no ctypes signature"
 
 
+def _declarations():
+    """{name: [parameter declarations]} of every entry point in include/ssparse.h."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"^int\s+(ss_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M):
+        params = [p.strip() for p in m.group(2).replace("\n", " ").split(",") if p.strip() and p.strip() != "void"]
+        out[m.group(1)] = params
+    return out
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every ctypes argtype has the kind of the header's parameter: pointers as pointers, and
+    int / int64_t / size_t / float as those widths."""
+    import ctypes
+    from streaming_sparse_b200._lib import SIGNATURES
+    decls = _declarations()
+    assert set(decls) == set(SIGNATURES)
+    scalar = {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t, "float": ctypes.c_float}
+    for name, params in decls.items():
+        args, _ = SIGNATURES[name]
+        assert len(args) == len(params), f"{name}: {len(args)} argtypes for {len(params)} parameters"
+        for i, (decl, a) in enumerate(zip(params, args)):
+            if "*" in decl:
+                assert a is ctypes.c_void_p or hasattr(a, "_type_") and issubclass(a, ctypes._Pointer), \
+                    f"{name} parameter {i} ({decl}) is a pointer, argtype {a}"
+            else:
+                typ = decl.rsplit(" ", 1)[0].replace("const ", "").strip()
+                assert a is scalar[typ], f"{name} parameter {i} ({decl}): argtype {a}, want {scalar[typ]}"
+
+
 def test_version(lib):
     assert lib.ss_version() >= 100
 
