@@ -224,8 +224,9 @@ int ss_peer_barrier(int *const *flags, int rank, int P, int *epoch, int *status,
 /* Rows [row0, row1) of out [Lq][H][128] (out_dtype 0 = bf16, 1 = fp32) =
  * sum_p exp(lse_p - L) o_p with L = logsumexp_p lse_p, where o_parts[p] is part p's [Lq][H][128]
  * output (part_dtype 0 = bf16, 1 = fp32) and lse_parts[p] its [H][Lq] natural-log LSE (-inf = the
- * part saw no token), both device pointers that may live on other GPUs (ss_ipc_open). lse_out
- * [H][Lq] (optional) receives L for those rows. P <= SS_MAX_PEERS. Arithmetic of ss_lse_merge. */
+ * part saw no token), both device pointers that may live on other GPUs (ss_ipc_open); the o_parts
+ * and out 16-byte aligned. lse_out [H][Lq] (optional) receives L for those rows.
+ * P <= SS_MAX_PEERS. Arithmetic of ss_lse_merge (the same values, bit for bit). */
 int ss_lse_merge_peers(const void *const *o_parts, const float *const *lse_parts, int P, int part_dtype,
                        int H, int Lq, int row0, int row1, void *out, int out_dtype, float *lse_out,
                        void *stream);

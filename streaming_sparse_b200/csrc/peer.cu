@@ -70,41 +70,53 @@ __global__ void __launch_bounds__(32) barrier_kernel(Flags fl, int rank, int P, 
     }
 }
 
-__device__ __forceinline__ float4 load4(const void *base, int64_t idx4, bool bf16) {
-    // four consecutive values of part p (element offset 4*idx4), read once through L2
+// Eight consecutive values of a part (element offset 8*idx8) as two float4, one 16-byte load
+// (bf16) or two (fp32), read through L2: peer data crosses NVLink in whole 16-byte pieces.
+__device__ __forceinline__ void load8(const void *base, int64_t idx8, bool bf16, float4 &a, float4 &b) {
     if (bf16) {
-        const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(base) + idx4);
-        return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
-                           __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+        const uint4 u = __ldcg(reinterpret_cast<const uint4 *>(base) + idx8);
+        a = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+        b = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u),
+                        __uint_as_float(u.w << 16), __uint_as_float(u.w & 0xffff0000u));
+    } else {
+        a = __ldcg(reinterpret_cast<const float4 *>(base) + 2 * idx8);
+        b = __ldcg(reinterpret_cast<const float4 *>(base) + 2 * idx8 + 1);
     }
-    return __ldcg(reinterpret_cast<const float4 *>(base) + idx4);
 }
 
-// One thread per (row, head, 4 dims) of rows [row0, row1). Every part's LSE and values are loaded
+__device__ __forceinline__ void fma4(float w, const float4 &v, float4 &acc) {
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+}
+
+// One thread per (row, head, 8 dims) of rows [row0, row1). Every part's LSE and values are loaded
 // before any is used (all of a thread's peer loads in flight at once); arithmetic and order are
 // those of ss_lse_merge: L = max + log(sum w), w_p = exp(lse_p - max), out = sum w_p o_p / sum w.
 template <int PMAX>
 __global__ void __launch_bounds__(256) merge_peers_kernel(Parts parts, int P, int part_bf16, int H, int Lq, int row0,
                                                           int row1, void *out, int out_fp32, float *lse_out) {
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t total = (int64_t)(row1 - row0) * H * (D / 4);
+    const int64_t total = (int64_t)(row1 - row0) * H * (D / 8);
     if (gid >= total) return;
-    const int quad = (int)(gid % (D / 4));
-    const int64_t rh = (int64_t)row0 * H + gid / (D / 4);   // row * H + h
+    const int oct = (int)(gid % (D / 8));
+    const int64_t rh = (int64_t)row0 * H + gid / (D / 8);   // row * H + h
     const int h = (int)(rh % H);
     const int row = (int)(rh / H);
-    const int64_t idx4 = rh * (D / 4) + quad;
+    const int64_t idx8 = rh * (D / 8) + oct;
     float l[PMAX];
-    float4 v[PMAX];
+    float4 va[PMAX], vb[PMAX];
 #pragma unroll
     for (int p = 0; p < PMAX; ++p) {
         if (p < P) {
             l[p] = __ldcg(parts.lse[p] + (int64_t)h * Lq + row);
-            v[p] = load4(parts.o[p], idx4, part_bf16 != 0);
+            load8(parts.o[p], idx8, part_bf16 != 0, va[p], vb[p]);
         }
     }
     float mx = -INFINITY, wsum = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
 #pragma unroll
     for (int p = 0; p < PMAX; ++p)
         if (p < P) mx = fmaxf(mx, l[p]);
@@ -113,27 +125,25 @@ __global__ void __launch_bounds__(256) merge_peers_kernel(Parts parts, int P, in
         for (int p = 0; p < PMAX; ++p) {
             if (p < P) {
                 const float w = __expf(l[p] - mx);
-                acc.x = fmaf(w, v[p].x, acc.x);
-                acc.y = fmaf(w, v[p].y, acc.y);
-                acc.z = fmaf(w, v[p].z, acc.z);
-                acc.w = fmaf(w, v[p].w, acc.w);
+                fma4(w, va[p], a);
+                fma4(w, vb[p], b);
                 wsum += w;
             }
         }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    acc.x *= inv;
-    acc.y *= inv;
-    acc.z *= inv;
-    acc.w *= inv;
-    const int64_t base = rh * D + quad * 4;
+    const float r[8] = {a.x * inv, a.y * inv, a.z * inv, a.w * inv, b.x * inv, b.y * inv, b.z * inv, b.w * inv};
+    const int64_t base = rh * D + oct * 8;
     if (out_fp32) {
-        reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + base)[0] = acc;
+        float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + base);
+        dst[0] = make_float4(r[0], r[1], r[2], r[3]);
+        dst[1] = make_float4(r[4], r[5], r[6], r[7]);
     } else {
-        const uint2 pk = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
-        reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + base)[0] = pk;
+        reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(out) + base)[0] =
+            make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]), pack_bf16x2(r[4], r[5]),
+                       pack_bf16x2(r[6], r[7]));
     }
-    if (lse_out && quad == 0) lse_out[(int64_t)h * Lq + row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+    if (lse_out && oct == 0) lse_out[(int64_t)h * Lq + row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
 }
 
 using AddressRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
@@ -214,13 +224,13 @@ extern "C" int ss_lse_merge_peers(const void *const *o_parts, const float *const
     }
     for (int p = 0; p < P; ++p) {
         if (!parts.o[p] || !parts.lse[p]) return SS_ERR_POINTER;
-        if ((reinterpret_cast<uintptr_t>(parts.o[p]) & (part_dtype ? 15u : 7u)) ||
+        if ((reinterpret_cast<uintptr_t>(parts.o[p]) & 15u) ||
             (reinterpret_cast<uintptr_t>(parts.lse[p]) & 3u))
             return SS_ERR_POINTER;
     }
     if (reinterpret_cast<uintptr_t>(out) & 15u) return SS_ERR_POINTER;
     if (row1 == row0) return 0;
-    const int64_t total = (int64_t)(row1 - row0) * H * (peer::D / 4);
+    const int64_t total = (int64_t)(row1 - row0) * H * (peer::D / 8);
     const unsigned blocks = (unsigned)((total + 255) / 256);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int bf = part_dtype == 0;

@@ -16,6 +16,12 @@ committed). Each fixture names the reference function that produced it:
 * merge_vr1.npz       local_experiments/video_runtime_v1/attention.py:40-45 ``merge``.
 * positions_adapter.npz  streaming_sparse/integration/self_forcing_adapter.py:50-97 ``_pre``
                       (absolute position of every visible cache slot through roll/evict).
+* score_cached.npz    migration/unified_router/fast_route.py:10-34 ``prepare`` + ``score_cached``
+                      (block scores: one prototype per key block = the plain mean of its valid
+                      tokens, projected by the shared basis; q . k / sqrt(128) + log(count)). The
+                      block means are computed here in float64 (the reference builds them with
+                      its Triton ``segment`` kernel, opt19/prototype.py:11-49, which reduces to the
+                      plain mean with one prototype and does not run without a GPU).
 * anchor_rebase.npz   local_experiments/anchor_rebase.py:8-18 ``shift_temporal_`` (temporal RoPE
                       pairs of the anchor frame rotated by a frame offset, float64, back to bf16),
                       with the RoPE table built as wan/modules/model.py:29-37 ``rope_params``
@@ -190,11 +196,48 @@ def anchor_rebase_case(shift_temporal_):
     np.savez_compressed(os.path.join(OUT, "anchor_rebase.npz"), **cases)
 
 
+def score_cached_case(prepare, score_cached):
+    from types import SimpleNamespace
+    g = torch.Generator().manual_seed(811)
+    Lq, Lk, H, block = 320, 2000, 3, 64           # 32 key blocks, the last one 16 tokens
+    q = torch.randn((Lq, H, 128), generator=g).bfloat16().float()
+    k = torch.randn((Lk, H, 128), generator=g).bfloat16().float()
+    basis = torch.randn((H, 128, 64), generator=g) / math.sqrt(128)
+
+    def means(x):
+        L = x.shape[0]
+        nb = -(-L // block)
+        m = torch.zeros((H, nb, 128), dtype=torch.float64)
+        cnt = torch.zeros((H, nb), dtype=torch.float64)
+        for j in range(nb):
+            rows = x[j * block:min(L, (j + 1) * block)].double()
+            m[:, j] = rows.mean(0)
+            cnt[:, j] = rows.shape[0]
+        return m.float(), cnt.float()
+
+    qm, _ = means(q)
+    km, kcount = means(k)
+    sketch = SimpleNamespace(key_basis=basis, parts=[SimpleNamespace(key=km[:, :, None], count=kcount[:, :, None],
+                                                                      value=None)])
+    _, projected = prepare(sketch, "U-Sol")
+    score, _ = score_cached(qm, basis, projected)
+    # q, k are bf16 values: stored as their bf16 bit patterns (int16)
+    np.savez_compressed(os.path.join(OUT, "score_cached.npz"), q_bf16=q.bfloat16().view(torch.int16).numpy(),
+                        k_bf16=k.bfloat16().view(torch.int16).numpy(), basis=basis.numpy(),
+                        block=block, score=score.numpy(), logcount=kcount.log().numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", default=None, help="write just this fixture (file name without .npz)")
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
+    if a.only == "score_cached":
+        from migration.unified_router.fast_route import prepare, score_cached
+        torch.set_num_threads(4)
+        score_cached_case(prepare, score_cached)
+        return
     from streaming_sparse.v05.primitives import select
     from streaming_sparse.v08.attention import reference
     from local_experiments.review_v1.ops import RouteOps, Config
@@ -209,6 +252,8 @@ def main():
     merge_case(merge)
     positions_case(SelfForcingAdapter)
     anchor_rebase_case(shift_temporal_)
+    from migration.unified_router.fast_route import prepare, score_cached
+    score_cached_case(prepare, score_cached)
     for f in sorted(os.listdir(OUT)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(OUT, f)))

@@ -97,7 +97,9 @@ def test_attention_history_budgets(oracle, rho):
 
 
 def test_attention_config2_sampled(oracle):
-    """Config 2 at full size; the float64 oracle checks a sample of heads and query blocks."""
+    """Config 2 at full size; the float64 oracle checks every head on 16 query blocks (both ends,
+    the partial last block, and every sixth block between): 192 of the 888 (head, query-block)
+    pairs."""
     from streaming_sparse_b200 import ops
     Lq, Lk, H = 4680, 32760, 12
     q, k, v = qkv(2, Lq, Lk, H)
@@ -106,7 +108,8 @@ def test_attention_config2_sampled(oracle):
     ids_np = ids.cpu().numpy()
     assert ids_np.shape == (12, 74, 128)
     out, lse = _attend(q, k, v, ids_np, 64)
-    heads, qblocks = [0, 5, 11], [0, 1, 36, 72, 73]
+    heads, qblocks = list(range(12)), sorted({0, 1, 72, 73} | set(range(3, 72, 6)))
+    assert len(qblocks) >= 16
     ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, 64, heads=heads, qblocks=qblocks)
     assert_attention_close(out, ref)
     m = np.isfinite(ref_lse)
@@ -155,6 +158,42 @@ def test_attention_config5_longest_window_sampled(oracle, block, density):
     qbs = ops.nblocks(Lq, block)
     ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, block, heads=[0, 1],
                                     qblocks=[0, qbs // 2, qbs - 1])
+    assert_attention_close(out, ref)
+    m = np.isfinite(ref_lse)
+    np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
+
+
+CONFIG5_GRID = [(4680, 64, 0.25)] + [(lk, 64, d) for lk in (9360, 65520, 98280) for d in (0.05, 0.10, 0.25, 0.5)] + \
+    [(98280, 128, 0.05), (98280, 128, 0.5)]
+
+
+@pytest.mark.parametrize("Lk,block,density", CONFIG5_GRID)
+def test_config5_grid_point(oracle, Lk, block, density):
+    """Every config-5 point the bench times (4680 queries, windows of 1, 2, 14 and 21 chunks,
+    densities 5-50 %, blocks 64 and 128), 2 heads: the router -- full, and with the history keys
+    pooled at commit -- bit for bit against the oracle, then the attention on the router's ids
+    against the float64 oracle on a sample of query blocks of both heads."""
+    from streaming_sparse_b200 import ops
+    Lq, H = 4680, 2
+    q, k, v = qkv(55, Lq, Lk, H)
+    wq, wk = router_weights(55, H)
+    kb = ops.nblocks(Lk, block)
+    nf = ops.forced_count(Lq, Lk, block)
+    extra = ops.budget(kb, nf, density=density)
+    qd, kd, vd, wqd, wkd = (t.to(DEV) for t in (q, k, v, wq, wk))
+    ids = ops.route(qd, kd, wqd, wkd, block=block, extra=extra, validate=True)
+    keys = ops.RouterKeys(H, Lk, block=block, device=DEV)
+    n_hist = ops.history_blocks(Lq, Lk, block)
+    ops.pool_keys(kd, wkd, keys, j0=0, j1=n_hist)
+    cached = ops.route(qd, kd, wqd, wkd, block=block, extra=extra, validate=True, keys=keys, n_cached=n_hist)
+    r = oracle.route(np32(q), np32(k), wq.numpy(), wk.numpy(), block, extra)
+    ids_np = ids.cpu().numpy()
+    np.testing.assert_array_equal(ids_np, r["ids"])
+    np.testing.assert_array_equal(cached.cpu().numpy(), r["ids"])
+    out, lse = _attend(q, k, v, ids_np, block)
+    qbs = ops.nblocks(Lq, block)
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids_np, block, heads=[0, 1],
+                                    qblocks=[0, qbs // 3, qbs // 2, qbs - 1])
     assert_attention_close(out, ref)
     m = np.isfinite(ref_lse)
     np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)

@@ -154,3 +154,50 @@ def test_anchor_rebase_and_snapshot_restore():
     c.restore(snap)
     assert (c.global_end, c.local_end) == (snap["global_end"], snap["local_end"])
     assert torch.equal(c.k[0, :c.local_end], snap["k"]) and torch.equal(c.v[0, :c.local_end], snap["v"])
+
+
+@pytest.mark.parametrize("P,part_dtype,rows", [(3, torch.float32, (0, 700)), (2, torch.bfloat16, (100, 333)),
+                                               (8, torch.bfloat16, (0, 700))])
+def test_lse_merge_peers_equals_lse_merge(P, part_dtype, rows):
+    """ss_lse_merge_peers with every part local (the pointers a rank passes for its own part): the
+    values of ss_lse_merge bit for bit, for the rows asked and nothing else; empty parts (-inf)
+    and a row with every part empty included."""
+    import ctypes
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200._lib import lib
+    Lq, H = 700, 3
+    g = torch.Generator(device=DEV).manual_seed(9)
+    o = torch.randn((P, Lq, H, 128), generator=g, device=DEV).to(part_dtype)
+    lse = 3 * torch.randn((P, H, Lq), generator=g, device=DEV)
+    lse[0, :, 5] = float("-inf")
+    lse[:, 1, 7] = float("-inf")
+    want, want_lse = ops.lse_merge(o.float(), lse, out_dtype=torch.float32, return_lse=True)
+    out = torch.full((Lq, H, 128), 7.0, device=DEV)
+    lse_out = torch.full((H, Lq), 7.0, device=DEV)
+    optr = (ctypes.c_void_p * P)(*[o[p].data_ptr() for p in range(P)])
+    lptr = (ctypes.c_void_p * P)(*[lse[p].data_ptr() for p in range(P)])
+    r0, r1 = rows
+    rc = lib().ss_lse_merge_peers(optr, lptr, P, 1 if part_dtype == torch.float32 else 0, H, Lq, r0, r1,
+                                  ctypes.c_void_p(out.data_ptr()), 1, ctypes.c_void_p(lse_out.data_ptr()),
+                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out[r0:r1], want[r0:r1])
+    assert torch.equal(lse_out[:, r0:r1], want_lse[:, r0:r1])
+    assert (out[:r0] == 7).all() and (out[r1:] == 7).all()
+
+
+def test_peer_barrier_single_rank_advances_epoch():
+    """A one-rank barrier posts into its own flags only (no wait on another launch): the device
+    epoch counter advances by one per call and the status word stays clear."""
+    import ctypes
+    from streaming_sparse_b200._lib import lib
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    epoch = torch.zeros(1, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ptrs = (ctypes.c_void_p * 1)(flags.data_ptr())
+    for _ in range(3):
+        assert lib().ss_peer_barrier(ptrs, 0, 1, ctypes.c_void_p(epoch.data_ptr()), ctypes.c_void_p(status.data_ptr()),
+                                     ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    torch.cuda.synchronize()
+    assert int(epoch.item()) == 3 and int(flags.item()) == 3 and int(status.item()) == 0

@@ -287,3 +287,35 @@ def test_window_retention_matches_reference_first_chunk_policy():
         old = chosen
         if completed == 20:
             assert chosen == list(range(3)) + list(range(48, 60))
+
+
+def test_router_scores_match_reference_score_cached(oracle, golden):
+    """The exact-fp32 router scores against the reference's own block scores
+    (migration/unified_router/fast_route.py:25-34 ``score_cached`` with one mean prototype per key
+    block, golden from tests/golden/make_golden.py): with W_q = W_k = the reference's basis,
+    score_ref = score / sqrt(128) + log(count). The ids agree wherever the selection margin (the
+    extra-th against the next unforced score) is wider than the arithmetic tolerance."""
+    g = golden("score_cached.npz")
+    bits = lambda a: (a.astype(np.int32) << 16).view(np.float32)   # bf16 bit patterns -> float32
+    q, k = bits(g["q_bf16"].astype(np.uint16)), bits(g["k_bf16"].astype(np.uint16))
+    basis, block = g["basis"], int(g["block"])
+    Lq, Lk = q.shape[0], k.shape[0]
+    extra = 6
+    r = oracle.route(q, k, basis, basis, block, extra)
+    ours = r["scores"].astype(np.float64) / np.sqrt(128.0) + g["logcount"][:, None, :]
+    tol = 2e-6                               # measured difference: 2.4e-7 on scores of magnitude ~4
+    np.testing.assert_allclose(ours, g["score"], rtol=0, atol=tol)
+    # selection on the reference's scores: forced current blocks, then the extra best unforced
+    forced = oracle.forced_blocks(Lq, Lk, block)
+    ref = g["score"]
+    checked = 0
+    for h in range(ref.shape[0]):
+        for i in range(ref.shape[1]):
+            cand = [j for j in range(ref.shape[2]) if not forced[j]]
+            order = sorted(cand, key=lambda j: (-ref[h, i, j], j))
+            if extra < len(order) and ref[h, i, order[extra - 1]] - ref[h, i, order[extra]] <= 2 * tol:
+                continue
+            want = sorted(order[:extra] + [j for j in range(ref.shape[2]) if forced[j]])
+            np.testing.assert_array_equal(r["ids"][h, i], want)
+            checked += 1
+    assert checked == ref.shape[0] * ref.shape[1]
