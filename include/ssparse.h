@@ -177,6 +177,21 @@ int ss_attention(const void *q, const void *k, const void *v, const int32_t *ids
 /* Largest n_ids ss_attention accepts for these sizes (its block lists live in shared memory). */
 int ss_attention_max_ids(int Lk, int block, int *max_ids);
 
+/* ss_attention with a caller workspace that balances a problem of one to two tiles per SM: when
+ * the 128-row tiles (ceil(Lq/128) * H) are at least as many as the SMs and fewer than twice as
+ * many, each CTA takes an equal share of the tiles' work, a tile shared by several CTAs is cut at its step list, every piece leaves
+ * its normalised partial and LSE in the workspace, and a second kernel merges the pieces (the
+ * arithmetic of ss_lse_merge). Larger problems run exactly as ss_attention. Same arguments and
+ * results as ss_attention (within fp32 rounding of the merge for split tiles). workspace:
+ * ss_attention_workspace_bytes bytes (0 = this size never splits), 256-byte aligned; it keeps
+ * nothing between calls. No counterpart in the reference (its kernel launches one program per
+ * query block and page group). */
+int ss_attention_workspace_bytes(int H, int Lq, size_t *bytes);
+int ss_attention_ws(const void *q, const void *k, const void *v, const int32_t *ids,
+                    int H, int Lq, int Lk, int block, int n_ids, float scale,
+                    void *out, int out_dtype, float *lse, int *status,
+                    void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial attention results.                                             */
 /* ------------------------------------------------------------------------------------------ */

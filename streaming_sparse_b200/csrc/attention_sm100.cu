@@ -103,7 +103,9 @@ __device__ __forceinline__ int e_start(uint32_t e) { return (int)(e & 0xFFFFFu);
 __device__ __forceinline__ int e_valid(uint32_t e) { return (int)((e >> 20) & 127u); }
 
 struct Tile {
-    int first, n, tile, pad;     // steps [first, first+n) of the step array (n even, >= 2); tile id
+    int first, n, tile, slot;    // steps [first, first+n) of the step array (n even, >= 2); tile id;
+                                 // slot: -1 = the whole tile (written to out), else the workspace
+                                 // slot of this CTA's piece of a split tile
 };
 
 // Position in the K/V ring: entry index and the parity of its use.
@@ -125,7 +127,24 @@ struct Params {
     int *status;
     int H, Lq, Lk, block, n_ids, qb, kb, ntiles, nwords, T, G, tmax, step_cap, out_fp32;
     float scale_log2;  // scale * log2(e)
+    // split mode (fewer than two tiles per CTA): CTA c takes tile-units [c*T, (c+1)*T) of the
+    // T*G units (G per tile); a tile spanning several CTAs is split at step pairs in proportion,
+    // each piece writing its normalised partial and LSE to slot 2c (the first tile of c's range)
+    // or 2c + 1 (the last) of ws_o [2G][128][128] / ws_lse [2G][128], merged by split_merge_kernel
+    int split;
+    float *ws_o, *ws_lse;
 };
+
+// Pieces of one tile at most in split mode: the grid has at most 8 CTAs per tile, and a tile
+// meets at most one more CTA than that.
+constexpr int MAXSPLIT_PIECES = 9;
+
+// Tile range of CTA c in split mode: tiles [first, last] meet its units [c*T, (c+1)*T).
+__host__ __device__ __forceinline__ int split_first(int c, int T, int G) { return (int)(((long)c * T) / G); }
+__host__ __device__ __forceinline__ int split_last(int c, int T, int G) { return (int)(((long)(c + 1) * T - 1) / G); }
+__host__ __device__ __forceinline__ int split_slot(int c, int t, int T, int G) {
+    return 2 * c + (t == split_first(c, T, G) ? 0 : 1);
+}
 
 __device__ __forceinline__ bool warp_all_ok(bool ok) { return __all_sync(0xffffffffu, ok) != 0; }
 
@@ -298,13 +317,18 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
     volatile int *badid_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 8);
     volatile int *progress = reinterpret_cast<volatile int *>(smem + OFF_MISC + 12);   // (tile << 16) | half-way
+    volatile int *nt_slot = reinterpret_cast<volatile int *>(smem + OFF_MISC + 16);    // pieces with steps
     Tile *tiles = reinterpret_cast<Tile *>(smem + OFF_TILES);
     float *xch = reinterpret_cast<float *>(smem + OFF_XCH);                              // [2][2][128]
     uint32_t *bm = reinterpret_cast<uint32_t *>(smem + OFF_RING + NST * TILE_BYTES);     // [tmax][2][nwords]
     uint2 *steps = reinterpret_cast<uint2 *>(bm + 2 * p.tmax * p.nwords);                // [step_cap]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nt = (p.T - (int)blockIdx.x + p.G - 1) / p.G;    // tiles blockIdx.x + k*G < T
+    // candidate tiles of this CTA: blockIdx.x + k*G < T, or in split mode the tiles its units meet
+    const int c_first = p.split ? split_first((int)blockIdx.x, p.T, p.G) : 0;
+    const int ntc = p.split ? split_last((int)blockIdx.x, p.T, p.G) - c_first + 1
+                            : (p.T - (int)blockIdx.x + p.G - 1) / p.G;
+    auto cand_tile = [&](int lt) { return p.split ? c_first + lt : (int)blockIdx.x + lt * p.G; };
     const bool pairq = (p.block == 64);
 
     // ---------------- prologue: barriers, TMEM, block bitmaps, step lists ----------------
@@ -336,14 +360,14 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         tmem_alloc(smem_u32((const void *)tmem_slot), TMEM_COLS);
         tmem_relinquish();
     }
-    for (int w = tid; w < 2 * nt * p.nwords; w += NTHREADS) bm[w] = 0u;
+    for (int w = tid; w < 2 * ntc * p.nwords; w += NTHREADS) bm[w] = 0u;
     __syncthreads();
     {
         // bitmap (lt, half) <- ids of query block (pair ? 2*tile + half : tile) of head h
         const int per_tile = (pairq ? 2 : 1) * p.n_ids;
-        for (int x = tid; x < nt * per_tile; x += NTHREADS) {
+        for (int x = tid; x < ntc * per_tile; x += NTHREADS) {
             const int lt = x / per_tile, rem = x % per_tile, half = rem / p.n_ids, i = rem % p.n_ids;
-            const int t = (int)blockIdx.x + lt * p.G, h = t / p.ntiles, tile = t % p.ntiles;
+            const int t = cand_tile(lt), h = t / p.ntiles, tile = t % p.ntiles;
             const int qblk = pairq ? 2 * tile + half : tile;
             if (qblk >= p.qb) continue;
             const int a = p.ids[((size_t)h * p.qb + qblk) * p.n_ids + i];
@@ -365,7 +389,8 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         // odd "both" sub-block if there is one; each group ascending.
         uint32_t *sub = reinterpret_cast<uint32_t *>(steps);
         int pos = 0;   // sub-blocks written
-        for (int lt = 0; lt < nt; ++lt) {
+        int nout = 0;  // table entries (pieces with steps)
+        for (int lt = 0; lt < ntc; ++lt) {
             const uint32_t *A = bm + (2 * lt) * p.nwords, *B = A + p.nwords;
             const int per = p.block / 64;
             auto maskof = [&](int w, int bit) -> uint32_t {
@@ -386,22 +411,43 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                     [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k + 1 : mp + k)] = e; });
             const int padded = max(4, (n + 3) & ~3);
             for (int k = n + lane; k < padded; k += 32) sub[pos + k] = entry(0u, 0u, 0u);
-            if (lane == 0) {
-                Tile tl;
-                tl.first = pos / 2;
-                tl.n = padded / 2;
-                tl.tile = (int)blockIdx.x + lt * p.G;
-                tl.pad = 0;
-                tiles[lt] = tl;
+            // the steps this CTA runs: the whole list, or in split mode its share of the tile's
+            // step pairs (the same cut for every CTA holding a piece of the tile)
+            const int t = cand_tile(lt), tsteps = padded / 2;
+            int s0 = 0, s1 = tsteps, slot = -1;
+            if (p.split) {
+                const long g0 = (long)t * p.G, u0 = (long)blockIdx.x * p.T;
+                const long a = max(u0, g0) - g0, b = min(u0 + p.T, g0 + p.G) - g0;
+                if (a > 0 || b < p.G) {
+                    const long pairs = tsteps / 2;
+                    s0 = 2 * (int)(a * pairs / p.G);
+                    s1 = 2 * (int)(b * pairs / p.G);
+                    slot = split_slot((int)blockIdx.x, t, p.T, p.G);
+                }
+            }
+            if (s1 > s0) {
+                if (lane == 0) {
+                    Tile tl;
+                    tl.first = pos / 2 + s0;
+                    tl.n = s1 - s0;
+                    tl.tile = t;
+                    tl.slot = slot;
+                    tiles[nout] = tl;
+                }
+                ++nout;
+            } else {   // a piece without steps: an empty partial for the merge
+                for (int r = lane; r < 128; r += 32) p.ws_lse[(size_t)slot * 128 + r] = -INFINITY;
             }
             pos += padded;
             __syncwarp();
         }
+        if (lane == 0) *nt_slot = nout;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const int nt = *nt_slot;
 
     if (warp >= 4) {
         // The softmax warpgroups and the control warpgroup run with different register budgets
@@ -420,7 +466,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         bool ok = true;
         int k = 0;                                   // steps of this warpgroup so far
         uint32_t qv[32];
-        {
+        if (nt > 0) {   // (a CTA whose split pieces all came out empty has no tile at all)
             const int t0 = tiles[0].tile;
             load_q(p, t0 / p.ntiles, (t0 % p.ntiles) * 128 + r, wg, qv);
             tmem_st32(lane_base + TMEM_Q + 32 * wg, reinterpret_cast<const float *>(qv));
@@ -622,7 +668,16 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             }
             tc_fence_before();
             mbar_arrive(bar(XDONE));
-            if (live) {
+            if (tl.slot >= 0) {
+                // a piece of a split tile: the normalised partial and its LSE, merged later
+                float4 *dst = reinterpret_cast<float4 *>(p.ws_o + ((size_t)tl.slot * 128 + r) * D + 64 * wg);
+#pragma unroll
+                for (int x = 0; x < 16; ++x)
+                    dst[x] = make_float4(res[4 * x], res[4 * x + 1], res[4 * x + 2], res[4 * x + 3]);
+                if (wg == 0)
+                    p.ws_lse[(size_t)tl.slot * 128 + r] =
+                        L > 0.f ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
+            } else if (live) {
                 if (p.out_fp32) {
                     float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) +
                                                              ((size_t)row * p.H + h) * D + 64 * wg);
@@ -751,6 +806,63 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
     }
 }
 
+// Split mode: the rows of every split tile from its pieces. Grid (T, 16): CTA (t, y) takes rows
+// [8y, 8y + 8) of tile t, one thread per (row, 4 dims), every piece's LSE and values loaded before
+// any is used; CTAs of whole tiles return at once. Arithmetic of ss_lse_merge: L = max + log(sum
+// w), w_p = exp(lse_p - max), out = sum w_p o_p / sum w; pieces without a token (lse -inf) take no
+// part.
+constexpr int MERGE_MAXP = MAXSPLIT_PIECES;
+__global__ void __launch_bounds__(256) split_merge_kernel(const float *__restrict__ ws_o,
+                                                          const float *__restrict__ ws_lse, int T, int G, int ntiles,
+                                                          int H, int Lq, void *out, int out_fp32, float *lse) {
+    const int t = blockIdx.x;
+    const int ca = (int)(((long)t * G) / T), cb = (int)(((long)(t + 1) * G - 1) / T);
+    if (ca == cb) return;                       // the whole tile is one CTA's: already written
+    const int r = blockIdx.y * 8 + threadIdx.x / (D / 4), quad = threadIdx.x % (D / 4);
+    const int h = t / ntiles, row = (t % ntiles) * 128 + r;
+    if (row >= Lq) return;
+    const int np = min(cb - ca + 1, MERGE_MAXP);
+    float l[MERGE_MAXP];
+    float4 v[MERGE_MAXP];
+#pragma unroll
+    for (int i = 0; i < MERGE_MAXP; ++i) {
+        if (i < np) {
+            const int slot = split_slot(ca + i, t, T, G);
+            l[i] = ws_lse[(size_t)slot * 128 + r];
+            v[i] = reinterpret_cast<const float4 *>(ws_o + ((size_t)slot * 128 + r) * D)[quad];
+        }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MERGE_MAXP; ++i)
+        if (i < np) mx = fmaxf(mx, l[i]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (mx != -INFINITY) {
+#pragma unroll
+        for (int i = 0; i < MERGE_MAXP; ++i) {
+            if (i < np && l[i] != -INFINITY) {
+                const float w = __expf(l[i] - mx);
+                acc.x = fmaf(w, v[i].x, acc.x);
+                acc.y = fmaf(w, v[i].y, acc.y);
+                acc.z = fmaf(w, v[i].z, acc.z);
+                acc.w = fmaf(w, v[i].w, acc.w);
+                wsum += w;
+            }
+        }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    const size_t base = ((size_t)row * H + h) * D + quad * 4;
+    if (out_fp32) {
+        reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + base)[0] =
+            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    } else {
+        reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + base)[0] =
+            make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+    }
+    if (lse && quad == 0) lse[(size_t)h * Lq + row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+}
+
 }  // namespace attn
 
 // Steps of one tile: at most `sb_tile` sub-blocks, padded to an even number (>= 2) of steps.
@@ -812,10 +924,22 @@ extern "C" int ss_attention_max_ids(int Lk, int block, int *max_ids) {
     return 0;
 }
 
-extern "C" int ss_attention(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq, int Lk,
+namespace ss {
+
+// CTAs per tile at most, in split mode (the grid is min(#SMs, MAXSPLIT * T) CTAs).
+constexpr int MAXSPLIT = 8;
+static_assert(attn::MAXSPLIT_PIECES >= MAXSPLIT + 1, "pieces per tile");
+
+// Measured on B200 (kernel alone): 156 tiles 77.8 -> 74.9 us and 222 tiles 144.9 -> 136.2 us with
+// the split, but 111 tiles 74.1 -> 86.5 us: below one tile per SM each piece's fixed start-up and
+// epilogue cost outweighs the balance gained, so only between one and two tiles per SM.
+static bool split_wanted(int T, int nsm) { return T >= nsm && T < 2 * nsm; }
+static int split_grid(int T, int nsm) { return std::min(nsm, MAXSPLIT * T); }
+static size_t split_ws_bytes(int G) { return (size_t)2 * G * 128 * (attn::D + 1) * sizeof(float); }
+
+static int attention_launch(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq, int Lk,
                             int block, int n_ids, float scale, void *out, int out_dtype, float *lse, int *status,
-                            void *stream) {
-    using namespace ss;
+                            void *ws, size_t ws_bytes, cudaStream_t stream) {
     if (!q || !k || !v || !ids || !out) return SS_ERR_POINTER;
     if (H <= 0 || Lq <= 0 || Lk <= 0 || n_ids <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
     if (Lk >= (1 << 20) - 128 || (long)Lq * H * attn::D >= (1L << 31) || (long)Lk * H * attn::D >= (1L << 31))
@@ -824,6 +948,7 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
          reinterpret_cast<uintptr_t>(out)) & 15u)
         return SS_ERR_POINTER;
     if (out_dtype != 0 && out_dtype != 1) return SS_ERR_SHAPE;
+    if (ws && (reinterpret_cast<uintptr_t>(ws) & 255u)) return SS_ERR_POINTER;
     uint32_t smem1;
     int rc = attention_smem_bytes(Lk, block, n_ids, &smem1);
     if (rc) return rc;
@@ -849,18 +974,34 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
     prm.ntiles = (Lq + 127) / 128;
     prm.nwords = (prm.kb + 31) / 32;
     prm.T = prm.ntiles * H;
-    // one CTA per SM running ceil(T / G) tiles; fewer tiles per CTA (more CTAs) where the step
-    // lists need the room
+    prm.split = 0;
+    prm.ws_o = prm.ws_lse = nullptr;
     const int nsm = g_num_sms[device] > 0 ? g_num_sms[device] : 148;
-    int G = std::max(std::min(prm.T, nsm), (prm.T + attn::MAXT - 1) / attn::MAXT);
-    while (attention_smem_for(prm.kb, block, n_ids, (prm.T + G - 1) / G) > (long)attn::SMEM_LIMIT &&
-           (prm.T + G - 1) / G > 1) {
-        const int tmax = (prm.T + G - 1) / G;
-        G = (prm.T + tmax - 2) / (tmax - 1);   // one tile fewer per CTA
+    const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)prm.kb) : 2L * std::min(n_ids, prm.kb);
+    int G;
+    if (ws && split_wanted(prm.T, nsm)) {
+        // split mode: every CTA's units meet at most ceil(T/G) + 1 tiles
+        G = split_grid(prm.T, nsm);
+        const int tmax = (prm.T + G - 1) / G + 1;
+        if (ws_bytes >= split_ws_bytes(G) && attention_smem_for(prm.kb, block, n_ids, tmax) <= (long)attn::SMEM_LIMIT) {
+            prm.split = 1;
+            prm.tmax = tmax;
+            prm.ws_o = static_cast<float *>(ws);
+            prm.ws_lse = prm.ws_o + (size_t)2 * G * 128 * attn::D;
+        }
+    }
+    if (!prm.split) {
+        // one CTA per SM running ceil(T / G) tiles; fewer tiles per CTA (more CTAs) where the step
+        // lists need the room
+        G = std::max(std::min(prm.T, nsm), (prm.T + attn::MAXT - 1) / attn::MAXT);
+        while (attention_smem_for(prm.kb, block, n_ids, (prm.T + G - 1) / G) > (long)attn::SMEM_LIMIT &&
+               (prm.T + G - 1) / G > 1) {
+            const int tmax = (prm.T + G - 1) / G;
+            G = (prm.T + tmax - 2) / (tmax - 1);   // one tile fewer per CTA
+        }
+        prm.tmax = (prm.T + G - 1) / G;
     }
     prm.G = G;
-    prm.tmax = (prm.T + G - 1) / G;
-    const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)prm.kb) : 2L * std::min(n_ids, prm.kb);
     prm.step_cap = (int)(prm.tmax * attention_tile_steps(sb_tile));
     prm.out_fp32 = out_dtype;
     prm.scale_log2 = scale * 1.4426950408889634f;
@@ -872,7 +1013,38 @@ extern "C" int ss_attention(const void *q, const void *k, const void *v, const i
     if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
     if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
 
-    attn::sparse_attention_kernel<<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem,
-                                    static_cast<cudaStream_t>(stream)>>>(tk, tv, prm);
+    attn::sparse_attention_kernel<<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem, stream>>>(tk, tv, prm);
+    if (prm.split)
+        attn::split_merge_kernel<<<dim3((unsigned)prm.T, 16), 256, 0, stream>>>(prm.ws_o, prm.ws_lse, prm.T, G,
+                                                                                 prm.ntiles, H, Lq, out, out_dtype, lse);
     return (int)cudaGetLastError();
+}
+
+}  // namespace ss
+
+extern "C" int ss_attention(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq, int Lk,
+                            int block, int n_ids, float scale, void *out, int out_dtype, float *lse, int *status,
+                            void *stream) {
+    return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status, nullptr, 0,
+                                static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ss_attention_workspace_bytes(int H, int Lq, size_t *bytes) {
+    if (!bytes || H <= 0 || Lq <= 0) return SS_ERR_SHAPE;
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    int rc = ss::attention_prepare(device);
+    if (rc) return rc;
+    const int nsm = ss::g_num_sms[device] > 0 ? ss::g_num_sms[device] : 148;
+    const int T = (Lq + 127) / 128 * H;
+    *bytes = ss::split_wanted(T, nsm) ? ss::split_ws_bytes(ss::split_grid(T, nsm)) : 0;
+    return 0;
+}
+
+extern "C" int ss_attention_ws(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq, int Lk,
+                               int block, int n_ids, float scale, void *out, int out_dtype, float *lse, int *status,
+                               void *workspace, size_t workspace_bytes, void *stream) {
+    return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status, workspace,
+                                workspace_bytes, static_cast<cudaStream_t>(stream));
 }

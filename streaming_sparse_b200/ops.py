@@ -266,14 +266,29 @@ def attention_max_ids(Lk: int, block: int = 64) -> int:
     return n.value
 
 
+_ATTN_WS: dict[tuple, int] = {}
+
+
+def attention_workspace_bytes(H: int, Lq: int) -> int:
+    """Workspace ``ss_attention_ws`` uses to split a small problem's tiles across the SMs (0: none)."""
+    key = (H, Lq, torch.cuda.current_device())
+    if key not in _ATTN_WS:
+        n = ctypes.c_size_t()
+        check(lib().ss_attention_workspace_bytes(H, Lq, ctypes.byref(n)), "ss_attention_workspace_bytes")
+        _ATTN_WS[key] = n.value
+    return _ATTN_WS[key]
+
+
 def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = None,
                      out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False,
-                     out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False):
+                     out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False,
+                     workspace: Workspace | None = None, split: bool = True):
     """softmax(scale q K_S^T) V_S over the valid tokens of the blocks in ids[h, t // block].
 
     q [Lq,H,128], k/v [Lk,H,128] bf16; ids int32 [H, ceil(Lq/block), n] (entries < 0 ignored).
     Returns out [Lq,H,128] in ``out_dtype`` (bf16 or fp32), plus the natural-log LSE [H,Lq] fp32
-    when ``return_lse``.
+    when ``return_lse``. With ``split`` (default) a problem of fewer 128-row tiles than twice the
+    SMs splits its tiles across the SMs (``ss_attention_ws``, workspace from ``workspace``).
     """
     q = _tokens(q, "q")
     k = _tokens(k, "k")
@@ -292,10 +307,18 @@ def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = Non
     if return_lse and lse is None:
         lse = torch.empty((H, Lq), dtype=torch.float32, device=q.device)
     status = DeviceStatus.word(q.device)
-    rc = lib().ss_attention(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
-                            1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None, _p(status),
-                            _stream(q.device))
-    check(rc, "ss_attention")
+    nws = attention_workspace_bytes(H, Lq) if split else 0
+    if nws:
+        ws = _ws(workspace, q.device).tensor("attention_split", (nws,), q.device, torch.uint8)
+        rc = lib().ss_attention_ws(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
+                                   1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
+                                   _p(status), _p(ws), nws, _stream(q.device))
+        check(rc, "ss_attention_ws")
+    else:
+        rc = lib().ss_attention(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
+                                1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None, _p(status),
+                                _stream(q.device))
+        check(rc, "ss_attention")
     if validate:
         DeviceStatus.check(q.device)
     return (out, lse) if return_lse else out
@@ -476,7 +499,7 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None
 
 __all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "RouterKeys", "pool_keys",
            "history_blocks", "sparse_attention", "exact",
-           "attention_max_ids", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
+           "attention_max_ids", "attention_workspace_bytes", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
            "rope_shift", "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
 
 # keep the status-bit names importable from here

@@ -285,3 +285,39 @@ def test_attention_many_tiles_per_cta(oracle, Lq, Lk, H, n):
     m = np.isfinite(ref_lse)
     np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
     assert np.isfinite(out).all()
+
+
+@pytest.mark.parametrize("Lq,Lk,H,block,n", [
+    (1560, 6240, 12, 64, 49),       # config 1's shape: 156 tiles on 148 SMs
+    (4680, 34320, 6, 128, 72),      # config 4 with 6 heads (a 2-way head shard): 222 tiles
+    (3600, 6000, 10, 64, 2),        # 290 tiles with two-step lists: pieces without steps
+    (3650, 3000, 10, 128, 3),       # partial last tile of every head, 128-token blocks
+])
+def test_split_tiles_match_unsplit_and_oracle(oracle, Lq, Lk, H, block, n):
+    """ss_attention_ws on problems of one to two tiles per SM (tiles cut across CTAs,
+    pieces merged by log-sum-exp) against ss_attention (whole tiles) and, with the north-star
+    tolerance, against the float64 oracle; fp32 output and LSE too, twice in a row (the
+    workspace keeps nothing between calls)."""
+    from streaming_sparse_b200 import ops
+    q, k, v = qkv(61, Lq, Lk, H)
+    rng = np.random.default_rng(61)
+    qb, kb = math.ceil(Lq / block), math.ceil(Lk / block)
+    ids = _random_ids(rng, H, qb, kb, min(n, kb), 1, forced=(kb - 1,))
+    assert ops.attention_workspace_bytes(H, Lq) > 0
+    qd, kd, vd, idd = q.to(DEV), k.to(DEV), v.to(DEV), torch.from_numpy(ids).to(DEV)
+    whole, whole_lse = ops.sparse_attention(qd, kd, vd, idd, block=block, out_dtype=torch.float32, return_lse=True,
+                                            split=False, validate=True)
+    for rep in range(2):
+        split, split_lse = ops.sparse_attention(qd, kd, vd, idd, block=block, out_dtype=torch.float32, return_lse=True,
+                                                validate=True)
+        torch.cuda.synchronize()
+        # each piece exponentiates against its own running max, so P's bf16 rounding differs
+        # from the whole tile's: agreement at that level (relative 2^-9 of P), not fp32 rounding
+        d = (split - whole).abs()
+        assert d.max().item() < 2e-3 and d.mean().item() < 2 ** -8 * whole.abs().mean().item()
+        assert (split_lse - whole_lse).abs().max().item() < 1e-4
+    ref, ref_lse = oracle.attention(np32(q), np32(k), np32(v), ids, block)
+    out, lse = _attend(q, k, v, ids, block)
+    assert_attention_close(out, ref)
+    m = np.isfinite(ref_lse)
+    np.testing.assert_allclose(lse[m], ref_lse[m], rtol=0, atol=2e-3)
