@@ -169,7 +169,8 @@ int ss_router_noalloc(const void *q, const void *k, const float *wq, const float
 /* out[t][h][:] = softmax(q[t,h,:] . K_sel^T * scale) V_sel over the valid tokens of the blocks
  * listed for t's query block in ids[h][t / block][0..n_ids) (ascending or not; entries < 0 are
  * ignored). out_dtype: 0 = bf16, 1 = fp32. lse (optional): [H][Lq] fp32 natural-log
- * log-sum-exp of the scaled scores. */
+ * log-sum-exp of the scaled scores. q, k, v 16-byte aligned and out 32-byte aligned
+ * (SS_ERR_POINTER otherwise). */
 int ss_attention(const void *q, const void *k, const void *v, const int32_t *ids,
                  int H, int Lq, int Lk, int block, int n_ids, float scale,
                  void *out, int out_dtype, float *lse, int *status, void *stream);

@@ -90,6 +90,9 @@ def test_host_argument_errors(lib):
     # misaligned base pointer (TMA needs 16-byte alignment)
     odd = ctypes.c_void_p(0x100002)
     assert lib.ss_attention(odd, fake, fake, fake, 12, 64, 64, 64, 1, 0.1, fake, 0, None, None, None) == 1002
+    # out 16-byte but not 32-byte aligned (the output rows leave in 32-byte stores)
+    out16 = ctypes.c_void_p(0x100010)
+    assert lib.ss_attention(fake, fake, fake, fake, 12, 64, 64, 64, 1, 0.1, out16, 0, None, None, None) == 1002
     # router: budget larger than the unforced blocks, n_ids inconsistent, workspace too small
     ws = ctypes.c_size_t(1 << 30)
     assert lib.ss_router(fake, fake, fake, fake, 12, 1560, 6240, 64, 64, 0, 74, fake, 99, None, None, fake, ws,
