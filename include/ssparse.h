@@ -27,6 +27,8 @@
  *   ss_router_pool_keys, ss_router_cached <- Cache.refresh_history / Cache.current
  *                     (migration/unified_router/opt23/pipeline.py:22-34): history pooled once per
  *                     commit, the current chunk pooled per call
+ *   ss_router_fast <- the tensor-core projection/score GEMM (migration/unified_router/opt8/
+ *                     projection.py:4-14, `_coarse` in opt16/route.py:34-47)
  *   ss_attention   <- exact(q,k,v,ids,workspace) (local_experiments/video_runtime_v1/attention.py:15-24)
  *                     wrapping _attn_fwd (local_experiments/gap_exact_round_kernel.py:4-137), and the
  *                     sm_80 C ABI `run` (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:407-409)
@@ -84,7 +86,8 @@ int ss_prepare_device(void);
 /* Router: mean-pooled query/key blocks -> per-head projections -> block scores -> top-k.       */
 /* ------------------------------------------------------------------------------------------ */
 
-/* Bytes of workspace ss_router needs for these sizes (R = projection width, 64 in the reference). */
+/* Bytes of workspace ss_router, ss_router_cached and ss_router_fast need for these sizes
+ * (R = projection width, 64 in the reference). */
 int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes);
 
 /* Route one chunk-layer.
@@ -130,6 +133,56 @@ int ss_router_cached(const void *q, const void *k, int k_row0, const float *wq, 
                      float *kh, int kh_rows, int n_cached,
                      int32_t *ids, int n_ids, uint8_t *mask, float *scores,
                      void *workspace, size_t workspace_bytes, int *status, void *stream);
+
+/* The router with its block-score GEMM on the tensor cores (tcgen05 kind::tf32, each fp32
+ * operand split into a tf32 part and its remainder, three products accumulated in fp32), for
+ * R = 32 or 64. The fast scores are within 2^-13 * |qh_i| * |kh_j| of the exact mode's; a query
+ * block whose threshold is tied, or whose lowest selected score minus that bound does not exceed
+ * the highest unselected candidate's score plus it, is scored again in exact fp32 with
+ * ss_router's arithmetic, so ids and mask are bit-identical to ss_router / ss_router_cached.
+ * Arguments as ss_router_cached, except:
+ *   kh      may be NULL (with n_cached = k_row0 = 0): every key block pooled into the workspace
+ *   scores  (optional) receives the tensor-core scores
+ *   rescored (optional) device int, incremented once per query block scored again
+ *   workspace  ss_router_workspace_bytes for these sizes (the fast mode's scores live there too)
+ * Replaces the tensor-core projection and score GEMM of the reference's Triton router
+ * (migration/unified_router/opt8/projection.py:4-14, `_coarse` in migration/unified_router/
+ * opt16/route.py:34-47) with its top-k (`_top`, :49-55). */
+int ss_router_fast(const void *q, const void *k, int k_row0, const float *wq, const float *wk,
+                   int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
+                   float *kh, int kh_rows, int n_cached,
+                   int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *rescored,
+                   void *workspace, size_t workspace_bytes, int *status, void *stream);
+
+/* ---- ring-buffer KV cache (O(chunk) eviction) ----------------------------------------------- *
+ * A ring cache keeps the window's first S = ring_sink rows at physical rows [0, S) and the rest
+ * in a ring of C = ring_cap rows at [S, S + C): window row t >= S sits at physical row
+ * S + ((t - S + ring_head) mod C). A roll of the window then moves only the ring's head instead
+ * of the rows. The cache also holds rows [S + C, S + C + 64) = a copy of ring rows [0, 64), and,
+ * when S is not a multiple of 64, a copy of the sink's last S mod 64 rows at ring rows
+ * ring_head - S mod 64 .. ring_head - 1, so that every 64-row sub-block of the window is one
+ * contiguous physical range (kept by ss_cache_append_ring / ss_cache_ring_refresh). Physical rows:
+ * S + C + 64; the window (Lk rows, starting at the cache's row 0) needs Lk - S + S mod 64 <= C.
+ * The reference's paged store advances the same kind of cursor over whole pages
+ * (`PageStore.commit`: write = sink + (end - sink) % (history_pages - sink),
+ * local_experiments/review_v1/runtime.py:38-46); here it runs per token, because the frames
+ * (1560 tokens) are not whole 64-token sub-blocks, and the window's block grid, and so every
+ * block id, stays that of the shifted cache. */
+
+/* ss_router_pool_keys over a ring cache k (S + C + 64 rows). */
+int ss_router_pool_keys_ring(const void *k, const float *wk, int H, int Lk, int R, int block, int j0, int j1,
+                             float *kh, int kh_rows, int ring_sink, int ring_cap, int ring_head,
+                             int *status, void *stream);
+
+/* The router over a ring cache k: the exact mode (fast = 0, ss_router / ss_router_cached) or the
+ * tensor-core mode (fast != 0, ss_router_fast), the first n_cached key blocks' projections from kh
+ * when kh is not NULL. Results equal those of the same call on the shifted (contiguous) window. */
+int ss_router_ring(const void *q, const void *k, const float *wq, const float *wk,
+                   int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
+                   float *kh, int kh_rows, int n_cached,
+                   int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *rescored, int fast,
+                   int ring_sink, int ring_cap, int ring_head,
+                   void *workspace, size_t workspace_bytes, int *status, void *stream);
 
 /* Bytes of the static device array used by ss_router_noalloc (8 MiB per device that loads the
    library, held until the process exits). */
@@ -192,6 +245,13 @@ int ss_attention_ws(const void *q, const void *k, const void *v, const int32_t *
                     int H, int Lq, int Lk, int block, int n_ids, float scale,
                     void *out, int out_dtype, float *lse, int *status,
                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* ss_attention_ws over a ring cache k, v (S + C + 64 rows each; see ss_router_ring). */
+int ss_attention_ring(const void *q, const void *k, const void *v, const int32_t *ids,
+                      int H, int Lq, int Lk, int block, int n_ids, float scale,
+                      void *out, int out_dtype, float *lse, int *status,
+                      int ring_sink, int ring_cap, int ring_head,
+                      void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial attention results.                                             */
@@ -266,6 +326,23 @@ int ss_cache_append(void *k_cache, void *v_cache, int cap, int H,
                     int local_attn, int64_t global_end, int64_t local_end,
                     int64_t current_start, int sink_tokens, int64_t *out_local_end,
                     void *stream);
+
+/* ss_cache_append on a ring cache (see ss_router_ring): the same window, index arithmetic and
+ * results, but a roll moves the ring's head by the evicted row count instead of shifting the
+ * window's rows, so a call writes only the chunk's n_new rows, their copies among the mirrored
+ * rows, and the sink's last S mod 64 rows before the new head. cap = the window's capacity in
+ * rows (the cache holds sink_tokens + ring_cap + 64 physical rows), ring_cap >= cap -
+ * sink_tokens + sink_tokens mod 64. *out_ring_head receives the head after the call. */
+int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H,
+                         const void *k_new, const void *v_new, int64_t new_stride, int n_new,
+                         int local_attn, int64_t global_end, int64_t local_end,
+                         int64_t current_start, int sink_tokens, int ring_cap, int ring_head,
+                         int64_t *out_local_end, int *out_ring_head, void *stream);
+
+/* Rewrite the copy of the sink's last sink_tokens mod 64 rows before the ring's head (and its
+ * mirrored rows), after the sink rows changed outside ss_cache_append_ring (an anchor rebase). */
+int ss_cache_ring_refresh(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap, int ring_head,
+                          void *stream);
 
 /* Rotate the first `pairs` complex pairs (elements 2p, 2p+1) of every head of rows [0, n) of a
  * key tensor [n][H][128] bf16 by phase[p] = (cos, sin) (float64 [pairs][2], device memory):

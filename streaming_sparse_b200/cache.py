@@ -22,7 +22,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .ops import cache_append, rope_shift
+from .ops import Ring, cache_append, cache_append_ring, ring_refresh, rope_shift
 
 
 def temporal_phase(offset: int, device, head_dim: int = 128) -> torch.Tensor:
@@ -74,16 +74,35 @@ class KVCache:
 
     ``local_attn_size`` / ``sink_size`` are in frames as in CausalWanSelfAttention; a value of -1
     for ``local_attn_size`` means a global cache (no eviction, window of 32760 tokens).
+
+    ``ring``: keep the rows after the sink in a ring buffer (``ops.Ring``): a roll then moves the
+    ring's head instead of shifting the window's rows, and a write costs only the chunk's rows.
+    ``k``/``v`` are then the physical rows [1, S + C + 64, H, D] (C = capacity - S + 64) and
+    ``window()`` returns them with ``ring`` and ``window_rows()`` describing the window; the
+    attention and router calls take them as they are (``ops.sparse_attention/route(..., ring=,
+    Lk=)``), ``window_logical()`` gathers the window in order. The window must cover the whole
+    cache. The index state, window contents and block grid are those of the shifting cache.
     """
 
     def __init__(self, capacity: int, num_heads: int = 12, head_dim: int = 128, *, frame_tokens: int = 1560,
                  local_attn_size: int = -1, sink_size: int = 0, device="cuda", dtype=torch.bfloat16,
-                 track_positions: bool = True):
+                 track_positions: bool = True, ring: bool = False):
         self.capacity, self.H, self.D = capacity, num_heads, head_dim
         self.frame_tokens = frame_tokens
         self.local_attn_size, self.sink_size = local_attn_size, sink_size
         self.max_attention_size = 32760 if local_attn_size == -1 else local_attn_size * frame_tokens
-        self.k = torch.zeros((1, capacity, num_heads, head_dim), device=device, dtype=dtype)
+        self.ring_mode = bool(ring)
+        self.ring = None
+        rows = capacity
+        if self.ring_mode:
+            if self.max_attention_size < capacity:
+                raise ValueError("a ring cache needs a visible window that covers the whole cache")
+            S = self.sink_tokens
+            if S >= capacity:
+                raise ValueError("the sink must leave room for the ring")
+            self.ring = Ring(S, capacity - S + 64, 0)
+            rows = self.ring.phys_rows()
+        self.k = torch.zeros((1, rows, num_heads, head_dim), device=device, dtype=dtype)
         self.v = torch.zeros_like(self.k)
         self.global_end = 0
         self.local_end = 0
@@ -164,9 +183,16 @@ class KVCache:
         n = k_new.shape[-3]
         old_global, old_local = self.global_end, self.local_end
         vis = self.advance(n, current_start)
-        new_end = cache_append(self.k, self.v, k_new, v_new, local_attn=self.local_attn_size != -1,
-                               global_end=old_global, local_end=old_local, current_start=current_start,
-                               sink_tokens=self.sink_tokens)
+        if self.ring_mode:
+            new_end, head = cache_append_ring(self.k, self.v, k_new, v_new, cap=self.capacity,
+                                              local_attn=self.local_attn_size != -1, global_end=old_global,
+                                              local_end=old_local, current_start=current_start,
+                                              sink_tokens=self.sink_tokens, ring=self.ring)
+            self.ring = Ring(self.ring.sink, self.ring.cap, head)
+        else:
+            new_end = cache_append(self.k, self.v, k_new, v_new, local_attn=self.local_attn_size != -1,
+                                   global_end=old_global, local_end=old_local, current_start=current_start,
+                                   sink_tokens=self.sink_tokens)
         assert new_end == self.local_end
         return vis
 
@@ -177,27 +203,30 @@ class KVCache:
         ``append`` would, when the write needs no roll of the window; returns None (state
         unchanged) when it does, in which case the caller writes through ``append``.
         """
-        if self._rolls(n, current_start):
+        if self.ring_mode or self._rolls(n, current_start):
             return None
         self.advance(n, current_start)
         return self.k[0, self.local_end - n:self.local_end], self.v[0, self.local_end - n:self.local_end]
 
     def snapshot(self) -> dict:
         """Device copy of the K/V rows in use and the index state (see ``restore``)."""
-        n = self.local_end
+        n = self.k.shape[1] if self.ring_mode else self.local_end
         return {"k": self.k[0, :n].clone(), "v": self.v[0, :n].clone(), "global_end": self.global_end,
-                "local_end": self.local_end, "commits": self.commits,
+                "local_end": self.local_end, "commits": self.commits, "ring": self.ring,
                 "positions": None if self.positions is None else self.positions.flat.copy()}
 
     def restore(self, snap: dict) -> None:
         """Put back a ``snapshot`` of this cache (same capacity and heads)."""
-        n = snap["local_end"]
-        if not (0 <= n <= self.capacity and tuple(snap["k"].shape) == (n, self.H, self.D) and
-                snap["v"].shape == snap["k"].shape):
+        le = snap["local_end"]
+        n = self.k.shape[1] if self.ring_mode else le
+        if not (0 <= le <= self.capacity and tuple(snap["k"].shape) == (n, self.H, self.D) and
+                snap["v"].shape == snap["k"].shape and (snap.get("ring") is None) != self.ring_mode):
             raise ValueError("snapshot does not match this cache's geometry")
         self.k[0, :n].copy_(snap["k"])
         self.v[0, :n].copy_(snap["v"])
-        self.global_end, self.local_end, self.commits = snap["global_end"], n, snap["commits"]
+        if self.ring_mode:
+            self.ring = snap["ring"]
+        self.global_end, self.local_end, self.commits = snap["global_end"], le, snap["commits"]
         self.epoch += 1
         if self.positions is not None and snap["positions"] is not None:
             self.positions.flat[:] = snap["positions"]
@@ -208,6 +237,8 @@ class KVCache:
         t = tokens if tokens is not None else (self.sink_tokens or self.frame_tokens)
         if t <= 0 or t > self.local_end:
             raise ValueError("the anchor rows must be written before they are saved")
+        if self.ring_mode and t > self.sink_tokens:
+            raise ValueError("a ring cache keeps only its sink rows in place: the anchor must lie in the sink")
         self.anchor = self.k[0, :t].clone()
 
     def rebase_anchor(self, offset: int) -> None:
@@ -217,16 +248,43 @@ class KVCache:
             raise RuntimeError("save_anchor() first")
         t = self.anchor.shape[0]
         rope_shift(self.anchor, self.k[0, :t], temporal_phase(offset, self.k.device, self.D))
+        if self.ring_mode:
+            ring_refresh(self.k, self.v, self.ring)   # the sink's copy before the ring's head
         self.epoch += 1
 
     def reset(self) -> None:
         """Empty the cache (index state only; rows are overwritten by the next writes)."""
         self.global_end = self.local_end = 0
+        if self.ring_mode:
+            self.ring = Ring(self.ring.sink, self.ring.cap, 0)
         self.epoch += 1
         if self.positions is not None:
             self.positions.flat[:] = -1
 
     def window(self):
-        """Visible K/V window [Lk,H,D] (views into the cache): the last tokens are the current chunk."""
+        """Visible K/V window [Lk,H,D] (views into the cache): the last tokens are the current chunk.
+        A ring cache returns its physical rows (see ``ring``, ``window_rows``)."""
+        if self.ring_mode:
+            return self.k[0], self.v[0]
         a = max(0, self.local_end - self.max_attention_size)
         return self.k[0, a:self.local_end], self.v[0, a:self.local_end]
+
+    def window_rows(self) -> int:
+        """Rows of the visible window."""
+        return self.local_end - self.window_start()
+
+    def physical_rows(self, n: int | None = None) -> torch.Tensor:
+        """Physical cache row of each of the window's first n rows (default: all), int64 on the device."""
+        n = self.window_rows() if n is None else n
+        t = torch.arange(n, device=self.k.device)
+        if not self.ring_mode:
+            return t + self.window_start()
+        S, C, head = self.ring
+        return torch.where(t < S, t, S + torch.remainder(t - S + head, C))
+
+    def window_logical(self):
+        """The visible window gathered in order (a copy; a plain cache returns its views)."""
+        if not self.ring_mode:
+            return self.window()
+        rows = self.physical_rows()
+        return self.k[0].index_select(0, rows), self.v[0].index_select(0, rows)

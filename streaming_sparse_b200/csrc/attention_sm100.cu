@@ -133,6 +133,7 @@ struct Params {
     // or 2c + 1 (the last) of ws_o [2G][128][128] / ws_lse [2G][128], merged by split_merge_kernel
     int split;
     float *ws_o, *ws_lse;
+    KvRing ring;   // where K/V rows live (C = 0: the window's rows in order)
 };
 
 // Pieces of one tile at most in split mode: the grid has at most 8 CTAs per tile, and a tile
@@ -183,7 +184,8 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 // Ascending compaction of the set bits of word(w) (w < nwords) into sub-block entries, run by
 // one warp; sub-block k of the output is stored by put(k, entry). Returns the number written.
 template <class W, class M, class P>
-__device__ __forceinline__ int compact(int nwords, int block, int Lk, int lane, W &&word, M &&maskof, P &&put) {
+__device__ __forceinline__ int compact(int nwords, int block, int Lk, const KvRing &ring, int lane, W &&word,
+                                       M &&maskof, P &&put) {
     const int per = block / 64;
     int carry = 0;
     for (int w0 = 0; w0 < nwords; w0 += 32) {
@@ -205,7 +207,7 @@ __device__ __forceinline__ int compact(int nwords, int block, int Lk, int lane, 
             for (int s = 0; s < per; ++s) {
                 const int t0 = j * block + s * 64;
                 const int valid = min(64, max(0, Lk - t0));
-                put(pos++, entry((uint32_t)t0, (uint32_t)valid, m));
+                put(pos++, entry((uint32_t)ring.sub_row(t0), (uint32_t)valid, m));
             }
         }
         carry += __shfl_sync(0xffffffffu, incl, 31);
@@ -410,11 +412,11 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             const int mp = min(na, nb), nb2 = nboth & ~1;
             const int n = na + nb + nboth;
             uint32_t *base = sub + pos;
-            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & B[w]; }, maskof,
+            compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & B[w]; }, maskof,
                     [&](int k, uint32_t e) { base[k < nb2 ? k : n - 1] = e; });
-            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
+            compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
                     [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k : mp + k)] = e; });
-            compact(p.nwords, p.block, p.Lk, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
+            compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
                     [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k + 1 : mp + k)] = e; });
             const int padded = max(4, (n + 3) & ~3);
             for (int k = n + lane; k < padded; k += 32) sub[pos + k] = entry(0u, 0u, 0u);
@@ -941,9 +943,19 @@ static bool split_wanted(int T, int nsm) { return T >= nsm && T < 2 * nsm; }
 static int split_grid(int T, int nsm) { return std::min(nsm, MAXSPLIT * T); }
 static size_t split_ws_bytes(int G) { return (size_t)2 * G * 128 * (attn::D + 1) * sizeof(float); }
 
+// A ring geometry the kernels can follow for a window of Lk rows: the window's ring rows and the
+// repeated sink rows fit the ring, and every physical row fits the 20-bit row field of a step.
+int ring_check(const KvRing &r, int Lk) {
+    if (r.C == 0) return r.S == 0 && r.head == 0 ? 0 : SS_ERR_SHAPE;
+    if (r.S < 0 || r.C < 64 || r.head < 0 || r.head >= r.C) return SS_ERR_SHAPE;
+    if ((int64_t)r.S + r.C + 64 >= (1 << 20) - 128) return SS_ERR_SHAPE;
+    if (Lk > r.S && (int64_t)(Lk - r.S) + (r.S % 64) > r.C) return SS_ERR_SHAPE;
+    return 0;
+}
+
 static int attention_launch(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq, int Lk,
                             int block, int n_ids, float scale, void *out, int out_dtype, float *lse, int *status,
-                            void *ws, size_t ws_bytes, cudaStream_t stream) {
+                            void *ws, size_t ws_bytes, cudaStream_t stream, KvRing ring = KvRing()) {
     if (!q || !k || !v || !ids || !out) return SS_ERR_POINTER;
     if (H <= 0 || Lq <= 0 || Lk <= 0 || n_ids <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
     if (Lk >= (1 << 20) - 128 || (long)Lq * H * attn::D >= (1L << 31) || (long)Lk * H * attn::D >= (1L << 31))
@@ -952,6 +964,7 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
         return SS_ERR_POINTER;
     if (reinterpret_cast<uintptr_t>(out) & 31u) return SS_ERR_POINTER;   // 32-byte row stores
     if (out_dtype != 0 && out_dtype != 1) return SS_ERR_SHAPE;
+    if (ring_check(ring, Lk)) return SS_ERR_SHAPE;
     if (ws && (reinterpret_cast<uintptr_t>(ws) & 255u)) return SS_ERR_POINTER;
     uint32_t smem1;
     int rc = attention_smem_bytes(Lk, block, n_ids, &smem1);
@@ -980,6 +993,7 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
     prm.T = prm.ntiles * H;
     prm.split = 0;
     prm.ws_o = prm.ws_lse = nullptr;
+    prm.ring = ring;
     const int nsm = g_num_sms[device] > 0 ? g_num_sms[device] : 148;
     const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)prm.kb) : 2L * std::min(n_ids, prm.kb);
     int G;
@@ -1014,8 +1028,9 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
 
     CUtensorMap tk, tv;
     const uint64_t row_bytes = (uint64_t)H * attn::D * 2;
-    if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
-    if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, (uint64_t)Lk, row_bytes, 64, 64)) return SS_ERR_DRIVER;
+    const uint64_t rows = (uint64_t)ring.phys_rows(Lk);
+    if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, rows, row_bytes, 64, 64)) return SS_ERR_DRIVER;
+    if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, rows, row_bytes, 64, 64)) return SS_ERR_DRIVER;
 
     attn::sparse_attention_kernel<<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem, stream>>>(tk, tv, prm);
     if (prm.split)
@@ -1051,4 +1066,17 @@ extern "C" int ss_attention_ws(const void *q, const void *k, const void *v, cons
                                void *workspace, size_t workspace_bytes, void *stream) {
     return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status, workspace,
                                 workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ss_attention_ring(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq,
+                                 int Lk, int block, int n_ids, float scale, void *out, int out_dtype, float *lse,
+                                 int *status, int ring_sink, int ring_cap, int ring_head, void *workspace,
+                                 size_t workspace_bytes, void *stream) {
+    ss::KvRing ring;
+    ring.S = ring_sink;
+    ring.C = ring_cap;
+    ring.head = ring_head;
+    if (ring_cap <= 0) return SS_ERR_SHAPE;
+    return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status, workspace,
+                                workspace_bytes, static_cast<cudaStream_t>(stream), ring);
 }

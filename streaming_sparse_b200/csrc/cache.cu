@@ -157,6 +157,39 @@ __global__ void __launch_bounds__(256) rope_shift_kernel(const uint32_t *__restr
     }
 }
 
+// Write n rows (K and V, source rows `src_stride` elements apart) to ring rows [pos0, pos0 + n) mod C
+// of a ring cache (ring row p at physical row S + p), and the rows that land on ring rows
+// [0, 64) once more at S + C + p: at most three contiguous copies plus the mirrored part.
+static int ring_write(const __nv_bfloat16 *sk, const __nv_bfloat16 *sv, int64_t src_stride, __nv_bfloat16 *kc,
+                      __nv_bfloat16 *vc, int H, int S, int C, int64_t pos0, int64_t n, cudaStream_t st) {
+    const int64_t row = (int64_t)H * D;
+    int64_t done = 0;
+    while (done < n) {
+        const int64_t pos = (pos0 + done) % C;
+        const int64_t m = std::min<int64_t>(n - done, C - pos);   // up to the ring's end
+        int rc = launch_copy(sk + done * src_stride, sv + done * src_stride, src_stride, kc + (S + pos) * row,
+                             vc + (S + pos) * row, row, m, H, st);
+        if (rc) return rc;
+        if (pos < 64) {   // the mirror of ring rows [0, 64)
+            const int64_t mm = std::min<int64_t>(m, 64 - pos);
+            rc = launch_copy(sk + done * src_stride, sv + done * src_stride, src_stride, kc + (S + C + pos) * row,
+                             vc + (S + C + pos) * row, row, mm, H, st);
+            if (rc) return rc;
+        }
+        done += m;
+    }
+    return 0;
+}
+
+// The sink's last S mod 64 rows repeated just before the ring's head (ring rows head - a .. head - 1).
+static int ring_refresh_tail(__nv_bfloat16 *kc, __nv_bfloat16 *vc, int H, int S, int C, int head, cudaStream_t st) {
+    const int a = S % 64;
+    if (a == 0) return 0;
+    const int64_t row = (int64_t)H * D;
+    return ring_write(kc + (int64_t)(S - a) * row, vc + (int64_t)(S - a) * row, row, kc, vc, H, S, C,
+                      ((int64_t)head - a + C) % C, a, st);
+}
+
 }  // namespace cache
 }  // namespace ss
 
@@ -226,4 +259,67 @@ extern "C" int ss_cache_append(void *k_cache, void *v_cache, int cap, int H, con
     if (rc) return rc;
     *out_local_end = new_local_end;
     return 0;
+}
+
+extern "C" int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H, const void *k_new,
+                                    const void *v_new, int64_t new_stride, int n_new, int local_attn,
+                                    int64_t global_end, int64_t local_end, int64_t current_start, int sink_tokens,
+                                    int ring_cap, int ring_head, int64_t *out_local_end, int *out_ring_head,
+                                    void *stream) {
+    using namespace ss;
+    if (!k_cache || !v_cache || !k_new || !v_new || !out_local_end || !out_ring_head) return SS_ERR_POINTER;
+    if (cap <= 0 || H <= 0 || n_new <= 0 || n_new > cap || sink_tokens < 0 || sink_tokens > cap || global_end < 0 ||
+        local_end < 0 || local_end > cap || current_start < 0)
+        return SS_ERR_SHAPE;
+    const int S = sink_tokens, C = ring_cap;
+    if (C < 64 || (int64_t)C < (int64_t)cap - S + S % 64 || ring_head < 0 || ring_head >= C) return SS_ERR_SHAPE;
+    if (new_stride % 8 != 0 || new_stride < (int64_t)H * cache::D) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+         reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15u)
+        return SS_ERR_POINTER;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t row = (int64_t)H * cache::D;
+    const int64_t current_end = current_start + n_new;
+    int64_t new_local_end;
+    int head = ring_head;
+    if (local_attn && current_end > global_end && n_new + local_end > cap) {
+        // the roll: the window's rows after the sink move down by `evicted`, which in the ring is
+        // only its head moving on by that many rows
+        const int64_t evicted = n_new + local_end - cap;
+        if (local_end - evicted - S < 0) return SS_ERR_SHAPE;   // cache too small for the sink and the chunk
+        head = (int)(((int64_t)head + evicted) % C);
+        new_local_end = local_end + current_end - global_end - evicted;
+    } else {
+        new_local_end = local_end + current_end - global_end;
+    }
+    const int64_t start = new_local_end - n_new;
+    if (start < 0 || new_local_end > cap) return SS_ERR_SHAPE;
+    __nv_bfloat16 *kc = static_cast<__nv_bfloat16 *>(k_cache), *vc = static_cast<__nv_bfloat16 *>(v_cache);
+    const __nv_bfloat16 *kn = static_cast<const __nv_bfloat16 *>(k_new), *vn = static_cast<const __nv_bfloat16 *>(v_new);
+    // chunk rows in the sink: their own rows; the rest: the ring from the window row's ring position
+    const int64_t ns = std::max<int64_t>(0, std::min<int64_t>(S, new_local_end) - start);
+    int rc = 0;
+    if (ns > 0) rc = cache::launch_copy(kn, vn, new_stride, kc + start * row, vc + start * row, row, ns, H, st);
+    if (rc) return rc;
+    if (n_new > ns) {
+        const int64_t t0 = start + ns;   // first window row of the chunk at or after S
+        rc = cache::ring_write(kn + ns * new_stride, vn + ns * new_stride, new_stride, kc, vc, H, S, C,
+                               (t0 - S + head) % C, n_new - ns, st);
+        if (rc) return rc;
+    }
+    rc = cache::ring_refresh_tail(kc, vc, H, S, C, head, st);   // after the chunk: it may hold the sink's rows
+    if (rc) return rc;
+    *out_local_end = new_local_end;
+    *out_ring_head = head;
+    return 0;
+}
+
+extern "C" int ss_cache_ring_refresh(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap, int ring_head,
+                                     void *stream) {
+    using namespace ss;
+    if (!k_cache || !v_cache) return SS_ERR_POINTER;
+    if (H <= 0 || sink_tokens < 0 || ring_cap < 64 || ring_head < 0 || ring_head >= ring_cap) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) return SS_ERR_POINTER;
+    return cache::ring_refresh_tail(static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), H,
+                                    sink_tokens, ring_cap, ring_head, static_cast<cudaStream_t>(stream));
 }

@@ -242,6 +242,32 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
+// ---------------------------------------------------------------------------------------------
+// KV ring: where a window row lives in a ring-buffer cache
+// ---------------------------------------------------------------------------------------------
+// A ring cache keeps the window's first S (sink) rows at physical rows [0, S) and the rest in a
+// ring of C rows at [S, S + C): window row t >= S sits at S + ((t - S + head) mod C). Two copies
+// make every 64-row sub-block of the window (rows [64s, 64s + 64)) one contiguous physical range,
+// so K/V still load as one box per sub-block:
+//   - rows [S + C, S + C + 64) repeat ring rows [0, 64) (a sub-block that runs past the ring's end);
+//   - when S is not a multiple of 64, the sink's last S mod 64 rows are repeated just before the
+//     ring's head, at ring rows head - S mod 64 .. head - 1 (the sub-block that starts in the sink).
+// C = 0 means a plain contiguous window (physical row = window row).
+struct KvRing {
+    int S = 0, C = 0, head = 0;
+    // physical row of the first row of the 64-row sub-block starting at window row t0 (t0 % 64 == 0)
+    __host__ __device__ __forceinline__ int sub_row(int t0) const {
+        if (C == 0 || t0 + 64 <= S) return t0;
+        int x = (t0 - S + head) % C;
+        if (x < 0) x += C;
+        return S + x;
+    }
+    // physical rows the cache needs for a window of `rows` rows
+    __host__ __device__ __forceinline__ int64_t phys_rows(int64_t rows) const {
+        return C == 0 ? rows : (int64_t)S + C + 64;
+    }
+};
+
 }  // namespace ss
 
 // host helpers (defined in capi.cu)
@@ -251,4 +277,5 @@ int encode_tmap_2d_bf16(CUtensorMap *map, const void *base, uint64_t inner, uint
 int encode_tmap_2d_bf16_rows(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
                              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 int current_context(void **ctx);
+int ring_check(const KvRing &ring, int Lk);   // attention_sm100.cu: a geometry the kernels can follow
 }

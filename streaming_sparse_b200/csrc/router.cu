@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(PP_MAX_WARPS * 32, 1)
 pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
                     int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
                     const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kh_ld,
-                    int kj0, int kj1, int krow0, int *status) {
+                    int kj0, int kj1, int krow0, KvRing ring, int *status) {
     extern __shared__ uint8_t smr_raw[];
     uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
     const int nw = blockDim.x / 32;
@@ -114,9 +114,16 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     __syncthreads();
     int issued = 0, seen = 0;   // lane 0's loads into the stage, and those waited on
-    if (lane == 0 && w < nblk) {
+    // a block arrives as block / 64 boxes of 64 rows, each from its sub-block's physical row
+    auto load_block = [&](int bi) {
         mbar_arrive_expect_tx(full, stage_bytes);
-        tma_load_2d(stage, tm, h * D, (b0 + w) * block - row0, full);
+        for (int sb = 0; sb < block / 64; ++sb) {
+            const int t = (b0 + bi) * block + 64 * sb;
+            tma_load_2d(stage + (uint32_t)sb * 64 * D * 2, tm, h * D, (isq ? t : ring.sub_row(t)) - row0, full);
+        }
+    };
+    if (lane == 0 && w < nblk) {
+        load_block(w);
         issued = 1;
     }
     bool ok = true, w_seen = false;
@@ -140,8 +147,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         __syncwarp();
         if (ok && lane == 0 && next < nblk) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive_expect_tx(full, stage_bytes);
-            tma_load_2d(stage, tm, h * D, (b0 + next) * block - row0, full);
+            load_block(next);
             ++issued;
         }
         const float fn = (float)n;
@@ -237,6 +243,38 @@ __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb,
     need = extra - count(T, true);   // ties at T to keep, >= 1
 }
 
+// select_threshold with the keys per lane chosen by the key-block count.
+__device__ __forceinline__ void find_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t &T,
+                                               int &need) {
+    if (kb <= 256) select_threshold<8>(mykeys, kb, extra, lane, T, need);
+    else if (kb <= 512) select_threshold<16>(mykeys, kb, extra, lane, T, need);
+    else if (kb <= 1024) select_threshold<32>(mykeys, kb, extra, lane, T, need);
+    else select_threshold<0>(mykeys, kb, extra, lane, T, need);
+}
+
+// One query block's ids, run by one warp: the ascending compaction of forced blocks, keys above
+// T and the first `need` keys equal to T (lowest block indices first) into out[0, n_ids); mrow
+// (optional) receives the 0/1 selection of every key block.
+__device__ __forceinline__ void write_selection(const uint32_t *mykeys, int kb, int extra, uint32_t T, int need,
+                                                int lane, int block, int Lq, int Lk, int sink, int32_t *out, int n_ids,
+                                                uint8_t *mrow) {
+    int pos = 0, taken = 0;
+    for (int j0 = 0; j0 < kb; j0 += 32) {
+        const int j = j0 + lane;
+        const uint32_t key = j < kb ? mykeys[j] : 0u;
+        const bool tie = extra > 0 && j < kb && key == T;
+        const unsigned tb = __ballot_sync(0xffffffffu, tie);
+        const bool keep_tie = tie && taken + __popc(tb & ((1u << lane) - 1u)) < need;
+        taken += __popc(tb);
+        const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && key > T) || keep_tie);
+        const unsigned bal = __ballot_sync(0xffffffffu, sel);
+        const int off = pos + __popc(bal & ((1u << lane) - 1u));
+        if (sel && off < n_ids) out[off] = j;
+        if (mrow && j < kb) mrow[j] = sel ? 1 : 0;
+        pos += __popc(bal);
+    }
+}
+
 // grid (ceil(qb / ROWS), H), SS_THREADS threads, ROWS = 8 query blocks per CTA.
 // Phase 1: thread t scores key blocks t, t + SS_THREADS, ... against the CTA's 8 query blocks: the R
 // projections of a key block are one contiguous row of kh (16 float4 loads in flight per thread),
@@ -307,29 +345,444 @@ __global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *_
     const uint32_t *mykeys = keys + (size_t)warp * kbp;
     uint32_t T = 0xffffffffu;
     int need = 0;
-    if (extra > 0) {
-        if (kb <= 256) select_threshold<8>(mykeys, kb, extra, lane, T, need);
-        else if (kb <= 512) select_threshold<16>(mykeys, kb, extra, lane, T, need);
-        else if (kb <= 1024) select_threshold<32>(mykeys, kb, extra, lane, T, need);
-        else select_threshold<0>(mykeys, kb, extra, lane, T, need);
+    if (extra > 0) find_threshold(mykeys, kb, extra, lane, T, need);
+    write_selection(mykeys, kb, extra, T, need, lane, block, Lq, Lk, sink, ids + ((size_t)h * qb + i) * n_ids, n_ids,
+                    mask ? mask + ((size_t)h * qb + i) * kb : nullptr);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Fast mode: the score GEMM on tcgen05, the exact scores only where the selection could differ.
+// ---------------------------------------------------------------------------------------------
+// Every score S = <qh_i, kh_j> is first computed on the tensor cores from the split operands
+// x = hi + lo (hi = x with its 13 low mantissa bits cleared, exact in tf32; lo = x - hi, exact in
+// fp32) as lo.hi + hi.lo + hi.hi (kind::tf32, fp32 accumulate), which leaves out lo.lo and the
+// truncation of lo: |fast - S| <= 3 * 2^-20 * sum|q_e k_e| from the split, plus the accumulation's
+// own rounding (at most one 2^-23-relative truncation of the running sum per K=8 instruction,
+// 24 instructions for R = 64: below 2^-15 * sum|q_e k_e|). The exact mode's chain of R fmaf is
+// within R * 2^-24 * sum|q_e k_e| of S. With sum|q_e k_e| <= |q| |k_j| (Cauchy-Schwarz), every
+// exact score lies within
+//     eps_j = FAST_BOUND * |q| * |k_j| + FAST_ABS,   FAST_BOUND = 2^-13 (over 3x the sum above),
+// of its fast score (FAST_ABS covers tf32 denormals flushed to zero). A query block's selection
+// from the fast scores is therefore the exact mode's whenever its threshold T is not tied and
+// min over selected (fast - eps) > max over the unselected candidates (fast + eps): then every
+// exact score of a selected block exceeds every exact score of an unselected one. Any other
+// query block (and any with a non-finite value) is scored again in exact fp32 with the exact
+// mode's arithmetic and selected by the exact mode's code, so the ids are bit-identical to it.
+constexpr float FAST_BOUND = 1.0f / 8192.0f;
+constexpr float FAST_ABS = 7.8886091e-31f;   // 2^-100
+constexpr int TC_TILE = 128;                 // query blocks (M) and key blocks (N) of a score tile
+constexpr uint32_t TC_REGION = TC_TILE * 128;   // one 128-byte K slice (32 fp32) of a 128-row tile
+constexpr int FAST_WARPS = 4;                // query blocks (one warp each) per select_fast CTA
+
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Instruction descriptor for kind::tf32 with fp32 D, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+    return (1u << 4)                       // D format: f32
+           | (2u << 7)                     // A format: tf32
+           | (2u << 10)                    // B format: tf32
+           | ((uint32_t)(N >> 3) << 17)    // N / 8
+           | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+__device__ __forceinline__ void split_tf32(float4 x, float4 &hi, float4 &lo) {
+    hi.x = __uint_as_float(__float_as_uint(x.x) & 0xffffe000u);
+    hi.y = __uint_as_float(__float_as_uint(x.y) & 0xffffe000u);
+    hi.z = __uint_as_float(__float_as_uint(x.z) & 0xffffe000u);
+    hi.w = __uint_as_float(__float_as_uint(x.w) & 0xffffe000u);
+    lo = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+}
+
+// grid (kbr / 64, ceil(qb / 128), H), TC_THREADS threads: the fast scores of query blocks
+// [m0, m0 + 128) x key blocks [n0, n0 + 64) of head h into sfast [H][qb][kbr], and (from the first
+// query tile) the norms |kh_j| into kn [H][kbr].
+//   1. cp.async copies every 16-byte chunk of the fp32 projections straight to its place in the
+//      UMMA K-major 128-byte-swizzle layout (a tile is R / 32 regions of rows x 128 B; chunk c of
+//      row r sits at chunk c ^ (r & 7)); rows past qb / kb are zero-filled. All copies are in
+//      flight together.
+//   2. Each thread splits the chunks it copied: hi in place, lo = x - hi to the lo tile.
+//   3. One elected thread issues the 3 * R / 8 MMAs (M = 128, N = 64, K = 8) into a 64-column
+//      TMEM accumulator.
+//   4. Warp w reads TMEM lanes 32 (w % 4) .. +31, columns 32 (w / 4) .. +31, into a padded
+//      staging tile in the (now free) A tiles' shared memory; thread r < 128 then sends row r
+//      (256 B) to sfast with one bulk copy.
+constexpr int TC_THREADS = 256;
+constexpr int TC_N = 64;                             // key blocks per score tile
+constexpr uint32_t TC_STAGE_ROW = TC_N * 4 + 16;     // padded staging row: conflict-free 16-byte stores
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+template <int R>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+score_tc_kernel(const float *__restrict__ qh, const float *__restrict__ kh, int kh_ld, int qb, int kb, int kbr,
+                float *__restrict__ sfast, float *__restrict__ kn, int *status) {
+    constexpr int NREG = R / 32, C4N = R / 4;
+    constexpr uint32_t A_BYTES = NREG * TC_TILE * 128, B_BYTES = NREG * TC_N * 128;
+    constexpr uint32_t B_REGION = TC_N * 128;
+    extern __shared__ uint8_t smr_raw[];
+    uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *a_hi = smr, *a_lo = smr + A_BYTES, *b_hi = smr + 2 * A_BYTES, *b_lo = smr + 2 * A_BYTES + B_BYTES;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smr + 2 * A_BYTES + 2 * B_BYTES);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bar + 2);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int h = blockIdx.z, m0 = blockIdx.y * TC_TILE, n0 = blockIdx.x * TC_N;
+    if (tid == 0) {
+        mbar_init(smem_u32(bar), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
     }
-    // ascending compaction of forced | above T | the first `need` ties at T
-    int32_t *out = ids + ((size_t)h * qb + i) * n_ids;
-    int pos = 0, taken = 0;
-    for (int j0 = 0; j0 < kb; j0 += 32) {
-        const int j = j0 + lane;
-        const uint32_t key = j < kb ? mykeys[j] : 0u;
-        const bool tie = extra > 0 && j < kb && key == T;
-        const unsigned tb = __ballot_sync(0xffffffffu, tie);
-        const bool keep_tie = tie && taken + __popc(tb & ((1u << lane) - 1u)) < need;
-        taken += __popc(tb);
-        const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && key > T) || keep_tie);
-        const unsigned bal = __ballot_sync(0xffffffffu, sel);
-        const int off = pos + __popc(bal & ((1u << lane) - 1u));
-        if (sel && off < n_ids) out[off] = j;
-        if (mask && j < kb) mask[((size_t)h * qb + i) * kb + j] = sel ? 1 : 0;
-        pos += __popc(bal);
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tslot), TC_N);
+        tmem_relinquish();
     }
+    // 1. chunk x of the A tile (x < 128 * C4N) is row x / C4N, float4 x % C4N; then the B tile
+    constexpr int NA = TC_TILE * C4N / TC_THREADS, NB = TC_N * C4N / TC_THREADS;
+    const float4 *q4 = reinterpret_cast<const float4 *>(qh) + (size_t)h * qb * C4N;
+    const float4 *k4 = reinterpret_cast<const float4 *>(kh) + (size_t)h * kh_ld * C4N;
+    auto a_off = [](int row, int c4) -> uint32_t {
+        return (uint32_t)(c4 >> 3) * (TC_TILE * 128) + (uint32_t)row * 128 + ((uint32_t)((c4 & 7) ^ (row & 7)) << 4);
+    };
+    auto b_off = [](int row, int c4) -> uint32_t {
+        return (uint32_t)(c4 >> 3) * B_REGION + (uint32_t)row * 128 + ((uint32_t)((c4 & 7) ^ (row & 7)) << 4);
+    };
+#pragma unroll
+    for (int u = 0; u < NA; ++u) {
+        const int x = tid + u * TC_THREADS, row = x / C4N, c4 = x % C4N;
+        const bool in = m0 + row < qb;
+        cp_async16(smem_u32(a_hi) + a_off(row, c4), q4 + (size_t)(in ? m0 + row : 0) * C4N + c4, in ? 16u : 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+        const int x = tid + u * TC_THREADS, row = x / C4N, c4 = x % C4N;
+        const bool in = n0 + row < kb;
+        cp_async16(smem_u32(b_hi) + b_off(row, c4), k4 + (size_t)(in ? n0 + row : 0) * C4N + c4, in ? 16u : 0u);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    // 2. split the chunks this thread copied (its own writes: no barrier needed before)
+#pragma unroll
+    for (int u = 0; u < NA; ++u) {
+        const int x = tid + u * TC_THREADS;
+        const uint32_t off = a_off(x / C4N, x % C4N);
+        float4 hi, lo;
+        split_tf32(*reinterpret_cast<const float4 *>(a_hi + off), hi, lo);
+        *reinterpret_cast<float4 *>(a_hi + off) = hi;
+        *reinterpret_cast<float4 *>(a_lo + off) = lo;
+    }
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+        const int x = tid + u * TC_THREADS, row = x / C4N;
+        const uint32_t off = b_off(row, x % C4N);
+        const float4 v = *reinterpret_cast<const float4 *>(b_hi + off);
+        float4 hi, lo;
+        split_tf32(v, hi, lo);
+        *reinterpret_cast<float4 *>(b_hi + off) = hi;
+        *reinterpret_cast<float4 *>(b_lo + off) = lo;
+        float ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, v.w * v.w)));
+#pragma unroll
+        for (int o = C4N >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (blockIdx.y == 0 && x % C4N == 0) kn[(size_t)h * kbr + n0 + row] = sqrtf(ss);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the stores above, to the MMA
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(tslot);
+    // 3.
+    if (warp == 0) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_tf32_f32(TC_TILE, TC_N);
+            const uint32_t ah = smem_u32(a_hi), al = smem_u32(a_lo), bh = smem_u32(b_hi), bl = smem_u32(b_lo);
+            uint32_t acc = 0;
+#pragma unroll 1
+            for (int pass = 0; pass < 3; ++pass) {   // lo.hi, hi.lo, then hi.hi
+                const uint32_t a = pass == 0 ? al : ah, b = pass == 1 ? bl : bh;
+#pragma unroll
+                for (int kk = 0; kk < R / 8; ++kk) {
+                    const uint32_t ka = (uint32_t)(kk >> 2) * (TC_TILE * 128) + (uint32_t)(kk & 3) * 32;
+                    const uint32_t kb_ = (uint32_t)(kk >> 2) * B_REGION + (uint32_t)(kk & 3) * 32;
+                    mma_tf32_ss(tmem, smem_desc_sw128(a + ka, 16, 1024), smem_desc_sw128(b + kb_, 16, 1024), idesc,
+                                acc);
+                    acc = 1;
+                }
+            }
+            tc_commit(smem_u32(bar));
+        }
+        __syncwarp();
+    }
+    bool ok = mbar_wait(smem_u32(bar), 0, abort_flag);
+    tc_fence_after();
+    // 4. (the MMAs have completed: the A tiles are free for the staging rows)
+    uint8_t *stage = smr;
+    if (ok) {
+        const int r = 32 * (warp & 3) + (tid & 31), c0 = 32 * (warp >> 2);
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0, v);
+        tmem_wait_ld();
+        tmem_ld_fence32(v);
+        float4 *dst = reinterpret_cast<float4 *>(stage + (uint32_t)r * TC_STAGE_ROW + c0 * 4);
+#pragma unroll
+        for (int x = 0; x < 8; ++x) dst[x] = make_float4(v[4 * x], v[4 * x + 1], v[4 * x + 2], v[4 * x + 3]);
+    } else {
+        if (tid == 0) report(status, SS_DEV_TIMEOUT);
+        volatile int never = 0;
+        mbar_wait(smem_u32(bar), 0, &never);   // the MMAs still own the accumulator (bounded)
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the staging rows, to the bulk copies
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, TC_N);
+    if (ok && tid < TC_TILE && m0 + tid < qb) {
+        float *g = sfast + ((size_t)h * qb + m0 + tid) * kbr + n0;
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(g),
+                     "r"(smem_u32(stage + (uint32_t)tid * TC_STAGE_ROW)), "r"((uint32_t)(TC_N * 4))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // before the CTA's memory is released
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float ordered_to_float(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
+}
+
+// The exact mode's score of key block j for the query projections sq (one fmaf chain in ascending
+// e, -0 -> +0), as its order-preserving key; `nonfinite` set for NaN / inf.
+__device__ __forceinline__ uint32_t exact_key(const float *sq, const float4 *krow, int R, bool &nonfinite) {
+    const float4 *sq4 = reinterpret_cast<const float4 *>(sq);
+    float4 kv[16];   // R <= 64: the whole row's loads in flight together
+#pragma unroll
+    for (int e4 = 0; e4 < 16; ++e4)
+        if (e4 < R / 4) kv[e4] = __ldg(krow + e4);
+    float a = 0.f;
+#pragma unroll
+    for (int e4 = 0; e4 < 16; ++e4) {
+        if (e4 < R / 4) {
+            const float4 qv = sq4[e4];
+            a = __fmaf_rn(qv.x, kv[e4].x, a);
+            a = __fmaf_rn(qv.y, kv[e4].y, a);
+            a = __fmaf_rn(qv.z, kv[e4].z, a);
+            a = __fmaf_rn(qv.w, kv[e4].w, a);
+        }
+    }
+    if (a == 0.f) a = 0.f;
+    nonfinite |= !isfinite(a);
+    return ordered_bits(a);
+}
+
+// Warp-wide count of keys >= c (or > c when strict) over NK keys per lane in registers.
+template <int NK>
+__device__ __forceinline__ int count_keys(const uint32_t (&kr)[NK], uint32_t c, bool strict) {
+    int n4[4] = {0, 0, 0, 0};   // independent partial counts keep the add chains short
+#pragma unroll
+    for (int u = 0; u < NK; ++u) n4[u & 3] += strict ? (kr[u] > c) : (kr[u] >= c);
+    return (int)__reduce_add_sync(0xffffffffu, (unsigned)((n4[0] + n4[1]) + (n4[2] + n4[3])));
+}
+
+// The threshold of the exact mode's selection from keys in registers: T with need = the keys
+// equal to T to keep (lowest indices first), by bisection on the order-preserving bits. The
+// search stops as soon as exactly `extra` keys are >= the candidate: those are then the `extra`
+// largest with no tie across the boundary, the set the full search selects.
+template <int NK>
+__device__ __forceinline__ void threshold_regs(const uint32_t (&kr)[NK], int extra, uint32_t &T, int &need) {
+    T = 0u;
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = T | (1u << bit);
+        const int c = count_keys(kr, cand, false);
+        if (c >= extra) {
+            T = cand;
+            if (c == extra) break;
+        }
+    }
+    need = extra - count_keys(kr, T, true);
+}
+
+// grid ceil(H * qb / FAST_WARPS), 32 * FAST_WARPS threads; NK keys per lane (kb <= 32 * NK): warp w
+// of the grid selects for query block (h, i) = (w / qb, w % qb), its keys in registers (key block
+// j = lane + 32 u in kr[u]). Dynamic shared memory: the query projections [FAST_WARPS][R] fp32,
+// then [FAST_WARPS][32] block indices.
+// With t the exact mode's threshold search run on the fast keys (t lies between the (extra+1)-th
+// and the extra-th largest fast score) and e = 2 * max_j eps_j over the query block's candidates,
+// every candidate is
+//   in        if fast > t + e: any block that could precede it in the exact order (higher exact
+//             score, or equal and lower index) has fast >= fast_j - e > t, and at most `extra`
+//             blocks have fast > t;
+//   out       if fast < t - e: the >= `extra` blocks with fast >= t all precede it;
+//   uncertain otherwise.
+// The selection is `in` plus the best r = extra - |in| uncertain blocks in the exact order: all of
+// them when r equals their count, none when r = 0, else the uncertain blocks (up to 32) get exact
+// scores, one per lane, ranked by (exact key descending, index ascending). A query block with
+// more uncertain blocks than that, or any non-finite value, is scored again in full with the
+// exact mode's arithmetic and selected by its rule. `scores` (optional) receives the fast scores;
+// `rescored` (optional) counts the query blocks that needed any exact score.
+template <int NK>
+__global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
+    const float *__restrict__ qh, const float *__restrict__ kh, int kh_ld, const float *__restrict__ sfast,
+    const float *__restrict__ kn, int H, int qb, int kb, int kbr, int R, int block, int Lq, int Lk, int sink,
+    int extra, int32_t *__restrict__ ids, int n_ids, uint8_t *__restrict__ mask, float *__restrict__ scores,
+    int *rescored, int *status) {
+    extern __shared__ __align__(16) uint8_t smr[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned lt = (1u << lane) - 1u;
+    const int gw = blockIdx.x * FAST_WARPS + warp;   // = h * qb + i
+    if (gw >= H * qb) return;
+    const int h = gw / qb;
+    float *sq = reinterpret_cast<float *>(smr) + warp * R;
+    int *uidx = reinterpret_cast<int *>(reinterpret_cast<float *>(smr) + FAST_WARPS * R) + warp * 32;
+    const float4 *khh = reinterpret_cast<const float4 *>(kh + (size_t)h * kh_ld * R);
+    const float *srow = sfast + (size_t)gw * kbr;
+    const float *knh = kn + (size_t)h * kbr;
+    uint32_t kr[NK];
+    float kv[NK];
+#pragma unroll
+    for (int u = 0; u < NK; ++u) {
+        const int j = lane + 32 * u;
+        kr[u] = j < kb ? __float_as_uint(srow[j]) : 0u;
+        kv[u] = j < kb ? knh[j] : 0.f;
+    }
+    float qn2 = 0.f;
+    for (int e = lane; e < R; e += 32) {
+        const float x = qh[(size_t)gw * R + e];
+        sq[e] = x;
+        qn2 = fmaf(x, x, qn2);
+    }
+    qn2 = warp_sum(qn2);
+    bool bad = !(qn2 <= 3.0e38f);   // also NaN
+    float knmax = 0.f;
+#pragma unroll
+    for (int u = 0; u < NK; ++u) {
+        const int j = lane + 32 * u;
+        if (j < kb) {
+            const float sv = __uint_as_float(kr[u]);
+            if (scores) scores[(size_t)gw * kb + j] = sv;
+            bad |= !isfinite(sv);
+            const bool forced = is_forced(j, block, Lq, Lk, sink);
+            kr[u] = forced ? 0u : ordered_bits(sv == 0.f ? 0.f : sv);
+            if (!forced) knmax = fmaxf(knmax, kv[u]);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) knmax = fmaxf(knmax, __shfl_xor_sync(0xffffffffu, knmax, o));
+    bool full = __any_sync(0xffffffffu, bad);
+    __syncwarp();   // sq
+    int32_t *out = ids + (size_t)gw * n_ids;
+    uint8_t *mrow = mask ? mask + (size_t)gw * kb : nullptr;
+    bool touched = false;
+    if (extra > 0 && !full) {
+        uint32_t T;
+        int need;
+        threshold_regs(kr, extra, T, need);
+        const float t = ordered_to_float(T);
+        const float e = 2.f * fmaf(FAST_BOUND * sqrtf(qn2), knmax, FAST_ABS);
+        const float up = t + e, dn = t - e;
+        full = !(e <= 1.0e38f);
+        int nin = 0, nu = 0;
+#pragma unroll
+        for (int u = 0; u < NK; ++u) {
+            const float sv = ordered_to_float(kr[u]);
+            const bool cand = kr[u] != 0u;
+            nin += __popc(__ballot_sync(0xffffffffu, cand && sv > up));
+            const unsigned b = __ballot_sync(0xffffffffu, cand && sv >= dn && sv <= up);
+            const int pos = nu + __popc(b & lt);
+            if (((b >> lane) & 1u) && pos < 32) uidx[pos] = lane + 32 * u;
+            nu += __popc(b);
+        }
+        const int r = extra - nin;
+        const bool take_all = r == nu, take_none = r == 0;
+        unsigned takemask = 0u;
+        if (!full && !take_all && !take_none) {
+            if (nu > 32) {
+                full = true;
+            } else {
+                __syncwarp();   // uidx
+                touched = true;
+                const int j = lane < nu ? uidx[lane] : 0;
+                bool nonfinite = false;
+                const uint32_t ek = lane < nu ? exact_key(sq, khh + (size_t)j * (R / 4), R, nonfinite) : 0u;
+                if (__any_sync(0xffffffffu, nonfinite)) {
+                    full = true;
+                } else {
+                    int rank = 0;
+                    for (int x = 0; x < nu; ++x) {
+                        const uint32_t kx = __shfl_sync(0xffffffffu, ek, x);
+                        const int jx = __shfl_sync(0xffffffffu, j, x);
+                        rank += kx > ek || (kx == ek && jx < j);
+                    }
+                    takemask = __ballot_sync(0xffffffffu, lane < nu && rank < r);
+                }
+            }
+        }
+        if (!full) {
+            int pos_u = 0, opos = 0;
+#pragma unroll
+            for (int u = 0; u < NK; ++u) {
+                const int j = lane + 32 * u;
+                const float sv = ordered_to_float(kr[u]);
+                const bool cand = kr[u] != 0u;
+                const bool unc = cand && sv >= dn && sv <= up;
+                const unsigned b = __ballot_sync(0xffffffffu, unc);
+                const int upos = pos_u + __popc(b & lt);
+                pos_u += __popc(b);
+                const bool take = take_all || (!take_none && upos < 32 && ((takemask >> upos) & 1u));
+                const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (cand && sv > up) || (unc && take));
+                const unsigned bal = __ballot_sync(0xffffffffu, sel);
+                const int off = opos + __popc(bal & lt);
+                if (sel && off < n_ids) out[off] = j;
+                if (mrow && j < kb) mrow[j] = sel ? 1 : 0;
+                opos += __popc(bal);
+            }
+        }
+    }
+    if (full || extra == 0) {
+        // the exact mode: every key block scored with its arithmetic (only to select when extra > 0,
+        // and always to flag non-finite scores as it does), then its threshold and ordered compaction
+        uint32_t T = 0xffffffffu;
+        int need = 0;
+        if (full) {
+            bool nonfinite = false;
+#pragma unroll
+            for (int u = 0; u < NK; ++u) {   // unrolled: kr stays in registers
+                const int j = lane + 32 * u;
+                if (j < kb) {
+                    const uint32_t key = exact_key(sq, khh + (size_t)j * (R / 4), R, nonfinite);
+                    kr[u] = is_forced(j, block, Lq, Lk, sink) ? 0u : key;
+                }
+            }
+            if (__any_sync(0xffffffffu, nonfinite) && lane == 0) report(status, SS_DEV_NONFINITE);
+            touched = true;
+            if (extra > 0) threshold_regs(kr, extra, T, need);
+        }
+        int taken = 0, opos = 0;
+#pragma unroll
+        for (int u = 0; u < NK; ++u) {
+            const int j = lane + 32 * u;
+            const bool tie = extra > 0 && j < kb && kr[u] == T;
+            const unsigned tb = __ballot_sync(0xffffffffu, tie);
+            const bool keep_tie = tie && taken + __popc(tb & lt) < need;
+            taken += __popc(tb);
+            const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && kr[u] > T) || keep_tie);
+            const unsigned bal = __ballot_sync(0xffffffffu, sel);
+            const int off = opos + __popc(bal & lt);
+            if (sel && off < n_ids) out[off] = j;
+            if (mrow && j < kb) mrow[j] = sel ? 1 : 0;
+            opos += __popc(bal);
+        }
+    }
+    if (touched && rescored && lane == 0) atomicAdd(rescored, 1);
 }
 
 }  // namespace router
@@ -370,6 +823,10 @@ int router_prepare(int device) {
     if (e != cudaSuccess) return (int)e;
     e = cudaFuncSetAttribute(router::score_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return (int)e;
+    e = cudaFuncSetAttribute(router::score_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaFuncSetAttribute(router::score_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return (int)e;
     int nsm = 0;
     e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
     if (e != cudaSuccess) return (int)e;
@@ -385,21 +842,39 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // score_select in shared memory and the row count of the key projections
 static int kb_padded(int kb) { return (kb + 3) & ~3; }
 
+// key-block count rounded up to the fast mode's score tile (128): the row stride of its scores
+static int kb_tiles(int kb) { return (kb + router::TC_TILE - 1) / router::TC_TILE * router::TC_TILE; }
+
+// Workspace: query projections [H][qb][R], key projections [H][kbp][R] (when no caller table),
+// then for the fast mode its scores [H][qb][kbr] and key norms [H][kbr] (kbr = kb_tiles(kb)).
 struct RouterLayout {
-    size_t qh, kh, total;
+    size_t qh, kh, total, sf, kn, total_fast;
 };
 
 static RouterLayout router_layout(int H, int Lq, int Lk, int R, int block) {
     const size_t qb = (size_t)((Lq + block - 1) / block);
-    const size_t kbp = (size_t)kb_padded((Lk + block - 1) / block);
+    const int kb = (Lk + block - 1) / block;
+    const size_t kbp = (size_t)kb_padded(kb), kbr = (size_t)kb_tiles(kb);
     RouterLayout L;
     L.qh = 0;
     L.kh = align256(L.qh + 4 * (size_t)H * qb * R);
     L.total = align256(L.kh + 4 * (size_t)H * R * kbp);
+    L.sf = L.total;
+    L.kn = align256(L.sf + 4 * (size_t)H * qb * kbr);
+    L.total_fast = align256(L.kn + 4 * (size_t)H * kbr);
     return L;
 }
 
 size_t router_workspace_size(int H, int Lq, int Lk, int R, int block) { return router_layout(H, Lq, Lk, R, block).total; }
+size_t router_fast_workspace_size(int H, int Lq, int Lk, int R, int block) {
+    return router_layout(H, Lq, Lk, R, block).total_fast;
+}
+
+static size_t tc_smem(int R) {
+    return 1024 + 2 * (size_t)(R / 32) * (router::TC_TILE + router::TC_N) * 128 + 64;
+}
+constexpr int FAST_MAX_KB = 2048;   // 64 keys per lane
+static size_t fast_smem(int R) { return (size_t)router::FAST_WARPS * ((size_t)R + 32) * 4; }
 
 static int count_forced(int Lq, int Lk, int block, int sink) {
     const int kb = (Lk + block - 1) / block;
@@ -432,7 +907,7 @@ int router_check(const void *q, const void *k, const float *wq, const float *wk,
 // pool_project_kernel: blocks per CTA tile chosen as the fewest that keep the grid within one wave.
 static int pool_launch(int device, const void *q, const void *k, const float *wq, const float *wk, int H, int Lq,
                        int Lk, int R, int block, bool with_q, float *qh, float *kh, int kh_ld, int kj0, int kj1,
-                       int *status, cudaStream_t st, int krow0 = 0) {
+                       int *status, cudaStream_t st, int krow0 = 0, KvRing ring = KvRing()) {
     const int qb = with_q ? (Lq + block - 1) / block : 0, nk = kj1 - kj0;
     if (qb + nk <= 0) return 0;
     const int nsm = g_router_sms[device] > 0 ? g_router_sms[device] : 148;
@@ -442,18 +917,17 @@ static int pool_launch(int device, const void *q, const void *k, const float *wq
     const int nw = pp_warps(R, block);
     CUtensorMap tmq, tmk;
     const uint64_t row_bytes = (uint64_t)H * router::D * 2;
-    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)(Lk - krow0), row_bytes, router::D,
-                                 (uint32_t)block))
+    if (encode_tmap_2d_bf16_rows(&tmk, k, (uint64_t)H * router::D, (uint64_t)(ring.phys_rows(Lk) - krow0), row_bytes,
+                                 router::D, 64u))
         return SS_ERR_DRIVER;
     if (with_q) {
-        if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D,
-                                     (uint32_t)block))
+        if (encode_tmap_2d_bf16_rows(&tmq, q, (uint64_t)H * router::D, (uint64_t)Lq, row_bytes, router::D, 64u))
             return SS_ERR_DRIVER;
     } else {
         tmq = tmk;   // no query tiles: the map is never read
     }
     router::pool_project_kernel<<<dim3(tq + tk, H), 32 * nw, pp_smem(R, block, nw), st>>>(
-        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kh_ld, kj0, kj1, krow0, status);
+        tmq, tmk, H, Lq, Lk, block, R, tq, bg, wq, wk, qh, kh, kh_ld, kj0, kj1, krow0, ring, status);
     return (int)cudaGetLastError();
 }
 
@@ -464,7 +938,7 @@ static int pool_launch(int device, const void *q, const void *k, const float *wq
 int router_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
                   int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores,
                   uint8_t *ws, int *status, cudaStream_t st, float *kh_ext = nullptr, int kh_ld_ext = 0,
-                  int n_cached = 0, int krow0 = 0) {
+                  int n_cached = 0, int krow0 = 0, KvRing ring = KvRing()) {
     const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block, kbp = kb_padded(kb);
     int device;
     cudaError_t e = cudaGetDevice(&device);
@@ -476,11 +950,54 @@ int router_launch(const void *q, const void *k, const float *wq, const float *wk
     float *kh = kh_ext ? kh_ext : reinterpret_cast<float *>(ws + L.kh);
     const int kh_ld = kh_ext ? kh_ld_ext : kbp;
     rc = pool_launch(device, q, k, wq, wk, H, Lq, Lk, R, block, true, qh, kh, kh_ld, kh_ext ? n_cached : 0, kb,
-                     status, st, krow0);
+                     status, st, krow0, ring);
     if (rc) return rc;
     router::score_select_kernel<<<dim3((qb + router::ROWS - 1) / router::ROWS, H), router::SS_THREADS,
                                   select_smem(kbp, R), st>>>(qh, kh, kh_ld, qb, kb, kbp, R, block, Lq, Lk, sink_tokens,
                                                              extra, ids, n_ids, mask, scores, status);
+    return (int)cudaGetLastError();
+}
+
+// router_launch in the fast mode: pooling as there, then score_tc_kernel and select_fast_kernel
+// (the fast scores and key norms in the workspace's fast-mode part). R must be 32 or 64.
+int router_fast_launch(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk, int R,
+                       int block, int sink_tokens, int extra, int32_t *ids, int n_ids, uint8_t *mask, float *scores,
+                       int *rescored, uint8_t *ws, int *status, cudaStream_t st, float *kh_ext, int kh_ld_ext,
+                       int n_cached, int krow0, KvRing ring = KvRing()) {
+    const int qb = (Lq + block - 1) / block, kb = (Lk + block - 1) / block, kbp = kb_padded(kb), kbr = kb_tiles(kb);
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    int rc = router_prepare(device);
+    if (rc) return rc;
+    const RouterLayout L = router_layout(H, Lq, Lk, R, block);
+    float *qh = reinterpret_cast<float *>(ws + L.qh);
+    float *kh = kh_ext ? kh_ext : reinterpret_cast<float *>(ws + L.kh);
+    const int kh_ld = kh_ext ? kh_ld_ext : kbp;
+    float *sf = reinterpret_cast<float *>(ws + L.sf), *kn = reinterpret_cast<float *>(ws + L.kn);
+    rc = pool_launch(device, q, k, wq, wk, H, Lq, Lk, R, block, true, qh, kh, kh_ld, kh_ext ? n_cached : 0, kb,
+                     status, st, krow0, ring);
+    if (rc) return rc;
+    const dim3 tg(kbr / router::TC_N, (qb + router::TC_TILE - 1) / router::TC_TILE, H);
+    if (R == 64)
+        router::score_tc_kernel<64><<<tg, router::TC_THREADS, tc_smem(R), st>>>(qh, kh, kh_ld, qb, kb, kbr, sf, kn,
+                                                                              status);
+    else
+        router::score_tc_kernel<32><<<tg, router::TC_THREADS, tc_smem(R), st>>>(qh, kh, kh_ld, qb, kb, kbr, sf, kn,
+                                                                              status);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    const int rows = H * qb, grid = (rows + router::FAST_WARPS - 1) / router::FAST_WARPS;
+    const size_t sm = fast_smem(R);
+#define SS_SELECT_FAST(NK)                                                                                           \
+    router::select_fast_kernel<NK><<<grid, 32 * router::FAST_WARPS, sm, st>>>(                                        \
+        qh, kh, kh_ld, sf, kn, H, qb, kb, kbr, R, block, Lq, Lk, sink_tokens, extra, ids, n_ids, mask, scores, rescored, \
+        status)
+    if (kb <= 256) SS_SELECT_FAST(8);
+    else if (kb <= 512) SS_SELECT_FAST(16);
+    else if (kb <= 1024) SS_SELECT_FAST(32);
+    else SS_SELECT_FAST(64);
+#undef SS_SELECT_FAST
     return (int)cudaGetLastError();
 }
 
@@ -540,7 +1057,7 @@ extern "C" int ss_router_noalloc(const void *q, const void *k, const float *wq, 
 
 extern "C" int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes) {
     if (!bytes || H <= 0 || Lq <= 0 || Lk <= 0 || R <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
-    *bytes = ss::router_workspace_size(H, Lq, Lk, R, block);
+    *bytes = ss::router_fast_workspace_size(H, Lq, Lk, R, block);   // enough for both modes
     return 0;
 }
 
@@ -591,4 +1108,90 @@ extern "C" int ss_router_cached(const void *q, const void *k, int k_row0, const 
     return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
                              static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream), kh,
                              kh_rows, n_cached, k_row0);
+}
+
+extern "C" int ss_router_fast(const void *q, const void *k, int k_row0, const float *wq, const float *wk, int H, int Lq,
+                              int Lk, int R, int block, int sink_tokens, int extra, float *kh, int kh_rows,
+                              int n_cached, int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *rescored,
+                              void *workspace, size_t workspace_bytes, int *status, void *stream) {
+    int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
+    if (rc) return rc;
+    if (R != 32 && R != 64) return SS_ERR_SHAPE;
+    if (!workspace) return SS_ERR_POINTER;
+    const int kb = (Lk + block - 1) / block;
+    if (kh) {
+        if (kh_rows < kb || n_cached < 0 || n_cached > kb) return SS_ERR_SHAPE;
+        if (k_row0 < 0 || k_row0 > n_cached * block || k_row0 >= Lk) return SS_ERR_SHAPE;
+        if (reinterpret_cast<uintptr_t>(kh) & 15u) return SS_ERR_POINTER;
+    } else if (n_cached != 0 || k_row0 != 0) {
+        return SS_ERR_SHAPE;
+    }
+    if (workspace_bytes < ss::router_fast_workspace_size(H, Lq, Lk, R, block)) return SS_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return SS_ERR_POINTER;
+    if (kb > ss::FAST_MAX_KB)   // beyond the fast selector's keys in registers: the exact kernels
+        return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
+                                 static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream), kh,
+                                 kh ? kh_rows : 0, n_cached, k_row0);
+    return ss::router_fast_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
+                                  rescored, static_cast<uint8_t *>(workspace), status, static_cast<cudaStream_t>(stream),
+                                  kh, kh_rows, n_cached, k_row0);
+}
+
+extern "C" int ss_router_pool_keys_ring(const void *k, const float *wk, int H, int Lk, int R, int block, int j0,
+                                        int j1, float *kh, int kh_rows, int ring_sink, int ring_cap, int ring_head,
+                                        int *status, void *stream) {
+    using namespace ss;
+    KvRing ring;
+    ring.S = ring_sink;
+    ring.C = ring_cap;
+    ring.head = ring_head;
+    if (ring_cap <= 0 || ring_check(ring, Lk)) return SS_ERR_SHAPE;
+    if (!k || !wk || !kh) return SS_ERR_POINTER;
+    if (H <= 0 || H > 65535 || Lk <= 0 || R <= 0 || R > router::MAX_R || (R % 16) || (block != 64 && block != 128))
+        return SS_ERR_SHAPE;
+    const int kb = (Lk + block - 1) / block;
+    if (j0 < 0 || j1 < j0 || j1 > kb || kh_rows < kb) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(wk) | reinterpret_cast<uintptr_t>(kh)) & 15u)
+        return SS_ERR_POINTER;
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    int rc = router_prepare(device);
+    if (rc) return rc;
+    return pool_launch(device, nullptr, k, nullptr, wk, H, 0, Lk, R, block, false, nullptr, kh, kh_rows, j0, j1,
+                       status, static_cast<cudaStream_t>(stream), 0, ring);
+}
+
+extern "C" int ss_router_ring(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk,
+                              int R, int block, int sink_tokens, int extra, float *kh, int kh_rows, int n_cached,
+                              int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *rescored, int fast,
+                              int ring_sink, int ring_cap, int ring_head, void *workspace, size_t workspace_bytes,
+                              int *status, void *stream) {
+    ss::KvRing ring;
+    ring.S = ring_sink;
+    ring.C = ring_cap;
+    ring.head = ring_head;
+    if (ring_cap <= 0 || ss::ring_check(ring, Lk)) return SS_ERR_SHAPE;
+    int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
+    if (rc) return rc;
+    if (!workspace) return SS_ERR_POINTER;
+    const int kb = (Lk + block - 1) / block;
+    if (kh) {
+        if (kh_rows < kb || n_cached < 0 || n_cached > kb) return SS_ERR_SHAPE;
+        if (reinterpret_cast<uintptr_t>(kh) & 15u) return SS_ERR_POINTER;
+    } else if (n_cached != 0) {
+        return SS_ERR_SHAPE;
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 255u) return SS_ERR_POINTER;
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (fast && kb <= ss::FAST_MAX_KB) {
+        if (R != 32 && R != 64) return SS_ERR_SHAPE;
+        if (workspace_bytes < ss::router_fast_workspace_size(H, Lq, Lk, R, block)) return SS_ERR_WORKSPACE;
+        return ss::router_fast_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores,
+                                      rescored, ws, status, st, kh, kh ? kh_rows : 0, n_cached, 0, ring);
+    }
+    if (workspace_bytes < ss::router_workspace_size(H, Lq, Lk, R, block)) return SS_ERR_WORKSPACE;
+    return ss::router_launch(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids, mask, scores, ws,
+                             status, st, kh, kh ? kh_rows : 0, n_cached, 0, ring);
 }

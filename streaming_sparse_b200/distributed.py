@@ -257,7 +257,7 @@ class KVShardedAttention:
         c = self.sparse.config
         return ops.route(q, self.k_tail, self.sparse.wq, self.sparse.wk, block=self.block, extra=self.extra,
                          sink_tokens=c.sink_tokens, workspace=self.ws, keys=self.keys, n_cached=self.n_hist,
-                         k_row0=self.row0)
+                         k_row0=self.row0, fast=c.fast)
 
     def __call__(self, q: torch.Tensor, k_chunk: torch.Tensor, v_chunk: torch.Tensor,
                  out: torch.Tensor | None = None) -> torch.Tensor:

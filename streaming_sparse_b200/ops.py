@@ -149,7 +149,9 @@ def router_workspace_bytes(H: int, Lq: int, Lk: int, R: int = 64, block: int = 6
 
 def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, return_mask: bool = False,
           return_scores: bool = False, workspace: Workspace | None = None, out: torch.Tensor | None = None,
-          validate: bool = False, keys: RouterKeys | None = None, n_cached: int = 0, k_row0: int = 0):
+          validate: bool = False, keys: RouterKeys | None = None, n_cached: int = 0, k_row0: int = 0,
+          fast: bool = False, rescored: torch.Tensor | None = None, ring: Ring | None = None,
+          Lk: int | None = None):
     """Block ids per (head, query block): forced blocks plus the ``extra`` best-scoring others.
 
     q [Lq,H,128] bf16 (current chunk), k [Lk,H,128] bf16 (visible window, current chunk last),
@@ -161,11 +163,22 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
     pooled, their projections written into the table. The ids are those of the uncached call.
     ``k_row0`` (with ``keys``): k holds only the window rows [k_row0, Lk), k_row0 <= n_cached*block
     (a KV-sharded rank: the tail of the window, the history before it represented by ``keys``).
+
+    ``fast`` (R = 32 or 64): the block scores on the tensor cores (``ss_router_fast``), with the
+    query blocks whose selection the error bound cannot settle scored again in exact fp32; the ids
+    and mask are bit-identical to the exact mode, ``return_scores`` gives the tensor-core scores.
+    ``rescored`` (int32 [1] on the device, fast mode): incremented once per query block scored
+    again. ``ring`` (with ``Lk``, the window's rows): k is a ring cache [S + C + 64, H, 128]
+    (``ss_router_ring``); the result is that of the call on the window's rows in order.
     """
     q = _tokens(q, "q")
     k = _tokens(k, "k")
     Lq, H, _ = q.shape
-    Lk = k.shape[0] + k_row0
+    _require((ring is None) == (Lk is None), "Lk goes with ring")
+    if ring is None:
+        Lk = k.shape[0] + k_row0
+    else:
+        _require(k_row0 == 0 and k.shape[0] == ring.phys_rows(), "a ring cache k holds S + C + 64 rows, k_row0 = 0")
     _require(k_row0 == 0 or (keys is not None and 0 <= k_row0 <= n_cached * block), "k_row0 needs keys covering it")
     _require(k.shape[1] == H and k.device == q.device, "q/k head count or device mismatch")
     _require(wq.shape == wk.shape and wq.dim() == 3 and wq.shape[0] == H and wq.shape[1] == HEAD_DIM,
@@ -183,14 +196,33 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
     mask = torch.empty((H, qb, kb), dtype=torch.uint8, device=q.device) if return_mask else None
     scores = torch.empty((H, qb, kb), dtype=torch.float32, device=q.device) if return_scores else None
     status = DeviceStatus.word(q.device)
-    if keys is None:
+    if keys is not None:
+        _require(keys.block == block and keys.R == R and keys.kh.shape[0] == H and keys.kh.device == q.device,
+                 "RouterKeys geometry differs from this call")
+        _require(0 <= n_cached <= kb and keys.kh.shape[1] >= kb, "n_cached or RouterKeys rows out of range")
+    if ring is not None:
+        _require(not fast or R in (32, 64), "the fast router needs R = 32 or 64")
+        rc = lib().ss_router_ring(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra,
+                                  _p(keys.kh) if keys is not None else None,
+                                  keys.kh.shape[1] if keys is not None else 0, int(n_cached), _p(ids), n_ids,
+                                  _p(mask), _p(scores), _p(rescored), int(bool(fast)), ring.sink, ring.cap, ring.head,
+                                  _p(scratch), nbytes, _p(status), _stream(q.device))
+        check(rc, "ss_router_ring")
+    elif fast:
+        _require(R in (32, 64), "the fast router needs R = 32 or 64")
+        _require(rescored is None or (rescored.dtype == torch.int32 and rescored.device == q.device),
+                 "rescored must be an int32 device tensor")
+        rc = lib().ss_router_fast(_p(q), _p(k), int(k_row0), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra,
+                                  _p(keys.kh) if keys is not None else None,
+                                  keys.kh.shape[1] if keys is not None else 0, int(n_cached), _p(ids), n_ids,
+                                  _p(mask), _p(scores), _p(rescored), _p(scratch), nbytes, _p(status),
+                                  _stream(q.device))
+        check(rc, "ss_router_fast")
+    elif keys is None:
         rc = lib().ss_router(_p(q), _p(k), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra, _p(ids), n_ids,
                              _p(mask), _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
         check(rc, "ss_router")
     else:
-        _require(keys.block == block and keys.R == R and keys.kh.shape[0] == H and keys.kh.device == q.device,
-                 "RouterKeys geometry differs from this call")
-        _require(0 <= n_cached <= kb and keys.kh.shape[1] >= kb, "n_cached or RouterKeys rows out of range")
         rc = lib().ss_router_cached(_p(q), _p(k), int(k_row0), _p(wq), _p(wk), H, Lq, Lk, R, block, sink_tokens, extra,
                                     _p(keys.kh), keys.kh.shape[1], int(n_cached), _p(ids), n_ids, _p(mask),
                                     _p(scores), _p(scratch), nbytes, _p(status), _stream(q.device))
@@ -241,18 +273,30 @@ def history_blocks(Lq: int, Lk: int, block: int) -> int:
     return (Lk - Lq) // block
 
 
-def pool_keys(k, wk, keys: RouterKeys, *, j0: int = 0, j1: int | None = None) -> None:
+def pool_keys(k, wk, keys: RouterKeys, *, j0: int = 0, j1: int | None = None, ring: Ring | None = None,
+              Lk: int | None = None) -> None:
     """Pool and project key blocks [j0, j1) of the window k [Lk,H,128] into ``keys.kh``
-    (``ss_router_pool_keys``)."""
+    (``ss_router_pool_keys``). With ``ring``: k is a ring cache [S + C + 64, H, 128] holding a
+    window of ``Lk`` rows (``ss_router_pool_keys_ring``)."""
     k = _tokens(k, "k")
-    Lk, H, _ = k.shape
+    H = k.shape[1]
+    _require((ring is None) == (Lk is None), "Lk goes with ring")
+    if ring is None:
+        Lk = k.shape[0]
+    else:
+        _require(k.shape[0] == ring.phys_rows(), "k rows do not match the ring")
     wk = wk.to(device=k.device, dtype=torch.float32).contiguous()
     _require(wk.shape == (H, HEAD_DIM, keys.R), f"wk must be [H,128,{keys.R}]")
     kb = nblocks(Lk, keys.block)
     j1 = kb if j1 is None else j1
     _require(0 <= j0 <= j1 <= kb and keys.kh.shape[0] == H and keys.kh.shape[1] >= kb, "key range or table size")
-    rc = lib().ss_router_pool_keys(_p(k), _p(wk), H, Lk, keys.R, keys.block, j0, j1, _p(keys.kh), keys.kh.shape[1],
-                                   _p(DeviceStatus.word(k.device)), _stream(k.device))
+    st = _p(DeviceStatus.word(k.device))
+    if ring is None:
+        rc = lib().ss_router_pool_keys(_p(k), _p(wk), H, Lk, keys.R, keys.block, j0, j1, _p(keys.kh), keys.kh.shape[1],
+                                       st, _stream(k.device))
+    else:
+        rc = lib().ss_router_pool_keys_ring(_p(k), _p(wk), H, Lk, keys.R, keys.block, j0, j1, _p(keys.kh),
+                                            keys.kh.shape[1], ring.sink, ring.cap, ring.head, st, _stream(k.device))
     check(rc, "ss_router_pool_keys")
 
 
@@ -282,19 +326,26 @@ def attention_workspace_bytes(H: int, Lq: int) -> int:
 def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = None,
                      out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False,
                      out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False,
-                     workspace: Workspace | None = None, split: bool = True):
+                     workspace: Workspace | None = None, split: bool = True, ring: Ring | None = None,
+                     Lk: int | None = None):
     """softmax(scale q K_S^T) V_S over the valid tokens of the blocks in ids[h, t // block].
 
     q [Lq,H,128], k/v [Lk,H,128] bf16; ids int32 [H, ceil(Lq/block), n] (entries < 0 ignored).
     Returns out [Lq,H,128] in ``out_dtype`` (bf16 or fp32), plus the natural-log LSE [H,Lq] fp32
     when ``return_lse``. With ``split`` (default) a problem of fewer 128-row tiles than twice the
     SMs splits its tiles across the SMs (``ss_attention_ws``, workspace from ``workspace``).
+    ``ring`` (with ``Lk``, the window's rows): k/v are a ring cache [S + C + 64, H, 128]
+    (``ss_attention_ring``).
     """
     q = _tokens(q, "q")
     k = _tokens(k, "k")
     v = _tokens(v, "v")
     Lq, H, D = q.shape
-    Lk = k.shape[0]
+    _require((ring is None) == (Lk is None), "Lk goes with ring")
+    if ring is None:
+        Lk = k.shape[0]
+    else:
+        _require(k.shape[0] == ring.phys_rows(), "k/v rows do not match the ring")
     _require(v.shape == k.shape and k.shape[1] == H, "k/v shape mismatch")
     _require(ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 3, "ids must be int32 CUDA [H,qb,n]")
     _require(ids.shape[0] == H and ids.shape[1] == nblocks(Lq, block), f"ids must be [H,{nblocks(Lq, block)},n]")
@@ -308,7 +359,14 @@ def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = Non
         lse = torch.empty((H, Lq), dtype=torch.float32, device=q.device)
     status = DeviceStatus.word(q.device)
     nws = attention_workspace_bytes(H, Lq) if split else 0
-    if nws:
+    if ring is not None:
+        ws = _ws(workspace, q.device).tensor("attention_split", (max(nws, 256),), q.device, torch.uint8)
+        rc = lib().ss_attention_ring(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
+                                     1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
+                                     _p(status), ring.sink, ring.cap, ring.head, _p(ws) if nws else None, nws,
+                                     _stream(q.device))
+        check(rc, "ss_attention_ring")
+    elif nws:
         ws = _ws(workspace, q.device).tensor("attention_split", (nws,), q.device, torch.uint8)
         rc = lib().ss_attention_ws(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
                                    1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
@@ -388,6 +446,61 @@ def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end
                                ctypes.byref(new_end), _stream(kc.device))
     check(rc, "ss_cache_append")
     return new_end.value
+
+
+class Ring(tuple):
+    """Geometry of a ring-buffer KV cache: (sink rows S, ring rows C, head). Window row t >= S lives
+    at physical row S + ((t - S + head) mod C); see ``ss_router_ring`` in include/ssparse.h."""
+
+    def __new__(cls, sink: int, cap: int, head: int):
+        return super().__new__(cls, (int(sink), int(cap), int(head)))
+
+    @property
+    def sink(self) -> int:
+        return self[0]
+
+    @property
+    def cap(self) -> int:
+        return self[1]
+
+    @property
+    def head(self) -> int:
+        return self[2]
+
+    def phys_rows(self) -> int:
+        return self[0] + self[1] + 64
+
+
+def cache_append_ring(k_cache, v_cache, k_new, v_new, *, cap: int, local_attn: bool, global_end: int,
+                      local_end: int, current_start: int, sink_tokens: int, ring: Ring) -> tuple[int, int]:
+    """``cache_append`` on a ring cache [S + C + 64, H, 128] (``ss_cache_append_ring``): the same
+    window, but a roll only moves the ring's head. Returns (new local end, new head)."""
+    kc = k_cache[0] if k_cache.dim() == 4 else k_cache
+    vc = v_cache[0] if v_cache.dim() == 4 else v_cache
+    kn = k_new[0] if k_new.dim() == 4 else k_new
+    vn = v_new[0] if v_new.dim() == 4 else v_new
+    for name, t in (("k_cache", kc), ("v_cache", vc), ("k_new", kn), ("v_new", vn)):
+        _require(t.is_cuda and t.dtype == torch.bfloat16 and t.shape[-1] == HEAD_DIM, f"{name}: bf16 CUDA [...,128]")
+    _require(kc.is_contiguous() and vc.is_contiguous() and kc.shape == vc.shape, "caches must be contiguous and equal")
+    _require(ring.sink == sink_tokens and kc.shape[0] == ring.phys_rows(), "cache rows do not match the ring")
+    H = kc.shape[1]
+    _require(kn.shape == vn.shape and kn.shape[1] == H and kn.stride() == vn.stride(), "k_new/v_new mismatch")
+    _require(kn.stride(2) == 1 and kn.stride(1) == HEAD_DIM, "k_new rows must be [H,128] contiguous")
+    new_end, new_head = ctypes.c_int64(), ctypes.c_int()
+    rc = lib().ss_cache_append_ring(_p(kc), _p(vc), int(cap), H, _p(kn), _p(vn), kn.stride(0), kn.shape[0],
+                                    int(bool(local_attn)), int(global_end), int(local_end), int(current_start),
+                                    int(sink_tokens), ring.cap, ring.head, ctypes.byref(new_end),
+                                    ctypes.byref(new_head), _stream(kc.device))
+    check(rc, "ss_cache_append_ring")
+    return new_end.value, new_head.value
+
+
+def ring_refresh(k_cache, v_cache, ring: Ring) -> None:
+    """Rewrite a ring cache's copy of the sink's last S mod 64 rows (``ss_cache_ring_refresh``)."""
+    kc = k_cache[0] if k_cache.dim() == 4 else k_cache
+    vc = v_cache[0] if v_cache.dim() == 4 else v_cache
+    rc = lib().ss_cache_ring_refresh(_p(kc), _p(vc), kc.shape[1], ring.sink, ring.cap, ring.head, _stream(kc.device))
+    check(rc, "ss_cache_ring_refresh")
 
 
 def rope_shift(src: torch.Tensor, dst: torch.Tensor, phase: torch.Tensor) -> torch.Tensor:

@@ -27,7 +27,8 @@ class RouterConfig:
     """Block size and budget of the learned block router.
 
     Exactly one of ``topk`` (fixed count outside the forced set) or ``density`` is used;
-    ``rule`` picks how ``density`` becomes a count (see ``ops.budget``).
+    ``rule`` picks how ``density`` becomes a count (see ``ops.budget``). ``fast`` scores the blocks
+    on the tensor cores (``ops.route(..., fast=True)``; same ids, proj_dim 32 or 64).
     """
 
     block: int = 64
@@ -36,6 +37,7 @@ class RouterConfig:
     rule: str = "total"
     sink_tokens: int = 0
     proj_dim: int = 64
+    fast: bool = False
 
     def extra(self, Lq: int, Lk: int) -> int:
         kb = ops.nblocks(Lk, self.block)
@@ -90,13 +92,17 @@ class SparseAttention:
         for its rows, and the table is marked valid for this window's history afterwards."""
         Lq, Lk = q.shape[-3], k.shape[-3]
         c = self.config
+        ring = cache.ring if cache is not None and cache.ring_mode else None
+        if ring is not None:   # k is the ring cache's physical rows
+            Lk = cache.window_rows()
         if cache is None:
             return ops.route(q, k, self.wq, self.wk, block=c.block, extra=c.extra(Lq, Lk), sink_tokens=c.sink_tokens,
-                             workspace=self.workspace, validate=self.validate)
+                             workspace=self.workspace, validate=self.validate, fast=c.fast)
         keys = cache.router_keys(c.block, self.wq.shape[2])
         tag = cache.history_tag()
         ids = ops.route(q, k, self.wq, self.wk, block=c.block, extra=c.extra(Lq, Lk), sink_tokens=c.sink_tokens,
-                        workspace=self.workspace, validate=self.validate, keys=keys, n_cached=keys.cached(tag))
+                        workspace=self.workspace, validate=self.validate, keys=keys, n_cached=keys.cached(tag),
+                        fast=c.fast, ring=ring, Lk=Lk if ring is not None else None)
         keys.mark(tag, ops.history_blocks(Lq, Lk, c.block))
         return ids
 
@@ -112,15 +118,17 @@ class SparseAttention:
         """q [Lq,H,D], k/v [Lk,H,D] bf16 -> [Lq,H,D] bf16. ``cache``: the ``KVCache`` whose window
         k/v are (found among the attached caches when not given)."""
         Lq, H, _ = q.shape
-        Lk = k.shape[0]
-        if Lk < Lq:
-            raise ValueError("the KV window must contain the current chunk (Lk >= Lq)")
         if cache is None:
             cache = self.cache_of(k)
+        ring = cache.ring if cache is not None and cache.ring_mode else None
+        Lk = cache.window_rows() if ring is not None else k.shape[0]
+        if Lk < Lq:
+            raise ValueError("the KV window must contain the current chunk (Lk >= Lq)")
         ids = self._dense_ids(H, Lq, Lk, q.device) if self.dense else self.route(q, k, cache)
         self.last_ids = ids
         self.calls += 1
-        return ops.sparse_attention(q, k, v, ids, block=self.config.block, out=out, validate=self.validate)
+        return ops.sparse_attention(q, k, v, ids, block=self.config.block, out=out, validate=self.validate, ring=ring,
+                                    Lk=Lk if ring is not None else None)
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *args, **kwargs) -> torch.Tensor:
         if args or kwargs:

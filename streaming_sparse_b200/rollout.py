@@ -42,6 +42,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .cache import KVCache
+from .plugin import _PATCH_FLAG as _PLUGIN_FLAG
 
 HEAD_DIM = 128
 
@@ -229,7 +230,7 @@ class Block(nn.Module):
             v = torch.empty_like(q)
             ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, k, v)
             cache.append(k, v, current_start)
-        kw, vw = cache.window()
+        kw, vw = _window_for(cache)
         y = _module_attention()(q[None], kw[None], vw[None])[0]
         ops.gate_residual(x, self.o(y.reshape(n, d)), gate=em[:, 2], frame_tokens=ft)
 
@@ -266,7 +267,7 @@ class Block(nn.Module):
         k = apply_rope(rms_norm(k, self.norm_k, cfg.eps).view(n, H, HEAD_DIM), *rope)
         v = v.contiguous().view(n, H, HEAD_DIM)
         cache.append(k, v, current_start)
-        kw, vw = cache.window()
+        kw, vw = _window_for(cache)
         y = _module_attention()(q[None], kw[None], vw[None])[0]
         x = x + gate(self.o(y.reshape(n, d)), e[2])
 
@@ -285,6 +286,14 @@ class Block(nn.Module):
 def _module_attention():
     # looked up at call time so that a plugin that swapped the module symbol is seen
     return globals()["attention"]
+
+
+def _window_for(cache: KVCache):
+    """The K/V window handed to the module's attention: a ring cache's physical rows go only to the
+    sparse plugin (which follows the ring); any other attention gets the window in order."""
+    if cache.ring_mode and not getattr(_module_attention(), _PLUGIN_FLAG, False):
+        return cache.window_logical()
+    return cache.window()
 
 
 class CausalWanDiT(nn.Module):
