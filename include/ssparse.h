@@ -86,9 +86,13 @@ int ss_prepare_device(void);
 /* Router: mean-pooled query/key blocks -> per-head projections -> block scores -> top-k.       */
 /* ------------------------------------------------------------------------------------------ */
 
-/* Bytes of workspace ss_router, ss_router_cached and ss_router_fast need for these sizes
- * (R = projection width, 64 in the reference). */
+/* Bytes of workspace ss_router and ss_router_cached need for these sizes (R = projection width,
+ * 64 in the reference). */
 int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes);
+
+/* Bytes of workspace ss_router_fast (and ss_router_ring with fast != 0) needs: the exact mode's
+ * workspace followed by the tensor-core scores and key norms. */
+int ss_router_fast_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes);
 
 /* Route one chunk-layer.
  *   q       [Lq][H][128] bf16, the current chunk's queries (RoPE applied)
@@ -144,7 +148,7 @@ int ss_router_cached(const void *q, const void *k, int k_row0, const float *wq, 
  *   kh      may be NULL (with n_cached = k_row0 = 0): every key block pooled into the workspace
  *   scores  (optional) receives the tensor-core scores
  *   rescored (optional) device int, incremented once per query block scored again
- *   workspace  ss_router_workspace_bytes for these sizes (the fast mode's scores live there too)
+ *   workspace  ss_router_fast_workspace_bytes for these sizes (the fast mode's scores live there too)
  * Replaces the tensor-core projection and score GEMM of the reference's Triton router
  * (migration/unified_router/opt8/projection.py:4-14, `_coarse` in migration/unified_router/
  * opt16/route.py:34-47) with its top-k (`_top`, :49-55). */

@@ -31,6 +31,7 @@ SIGNATURES = {
     "ss_version": ([], _I),
     "ss_prepare_device": ([], _I),
     "ss_router_workspace_bytes": ([_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)], _I),
+    "ss_router_fast_workspace_bytes": ([_I, _I, _I, _I, _I, ctypes.POINTER(_SZ)], _I),
     "ss_router": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _SZ, _P, _P], _I),
     "ss_router_noalloc": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P, _P, _P], _I),
     "ss_router_pool_keys": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P], _I),

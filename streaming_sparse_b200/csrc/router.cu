@@ -243,12 +243,94 @@ __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb,
     need = extra - count(T, true);   // ties at T to keep, >= 1
 }
 
-// select_threshold with the keys per lane chosen by the key-block count.
-__device__ __forceinline__ void find_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t &T,
-                                               int &need) {
-    if (kb <= 256) select_threshold<8>(mykeys, kb, extra, lane, T, need);
-    else if (kb <= 512) select_threshold<16>(mykeys, kb, extra, lane, T, need);
-    else if (kb <= 1024) select_threshold<32>(mykeys, kb, extra, lane, T, need);
+// Exclusive prefix sum of v over the warp's lanes (and the total in *total).
+__device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int *total) {
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    *total = __shfl_sync(0xffffffffu, x, 31);
+    return x - v;
+}
+
+// The threshold of the exact mode's selection (as select_threshold: T = the extra-th largest
+// nonzero key, need = the keys equal to T to keep) by a most-significant-digit radix select over
+// the keys in registers: four passes of 8 bits, each a histogram of the next digit of the keys
+// that match the digits found so far (shared-memory counts of one warp, hist[256]), scanned from
+// the top digit down to the bin holding the rank still sought. Four passes instead of 32
+// bisection steps; the result is the same T, and rank left at the end is `need`.
+template <int NK>
+__device__ __forceinline__ void threshold_radix(const uint32_t (&kr)[NK], int extra, uint32_t *hist, int lane,
+                                                uint32_t &T, int &need) {
+    uint32_t prefix = 0u, pmask = 0u;
+    int rank = extra;   // rank, from the top, of the key sought among those matching prefix
+#pragma unroll 1
+    for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) hist[lane + 32 * b] = 0u;
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < NK; ++u)
+            if (kr[u] != 0u && (kr[u] & pmask) == prefix) atomicAdd(&hist[(kr[u] >> shift) & 255u], 1u);
+        __syncwarp();
+        // lane l holds bins 255 - 8l down to 248 - 8l
+        uint32_t c[8];
+        int sum = 0;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            c[b] = hist[255 - 8 * lane - b];
+            sum += (int)c[b];
+        }
+        int total;
+        const int above = warp_exclusive_scan(sum, lane, &total);   // keys in higher bins
+        const bool mine = above < rank && rank <= above + sum;
+        const int owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+        int digit = 0, before = 0;
+        if (mine) {
+            int acc = above;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                if (acc + (int)c[b] >= rank) {
+                    digit = 255 - 8 * lane - b;
+                    before = acc;
+                    break;
+                }
+                acc += (int)c[b];
+            }
+        }
+        digit = __shfl_sync(0xffffffffu, digit, owner);
+        before = __shfl_sync(0xffffffffu, before, owner);
+        prefix |= (uint32_t)digit << shift;
+        pmask |= 255u << shift;
+        rank -= before;
+        __syncwarp();   // the histogram is cleared by the next pass
+    }
+    T = prefix;
+    need = rank;
+}
+
+template <int NK>
+__device__ __forceinline__ void radix_from_smem(const uint32_t *mykeys, int kb, int extra, uint32_t *hist, int lane,
+                                                uint32_t &T, int &need) {
+    uint32_t kr[NK];
+#pragma unroll
+    for (int u = 0; u < NK; ++u) {
+        const int j = lane + 32 * u;
+        kr[u] = j < kb ? mykeys[j] : 0u;
+    }
+    threshold_radix(kr, extra, hist, lane, T, need);
+}
+
+// The selection threshold of one query block's keys (in shared memory), run by one warp: a radix
+// select over the keys in registers up to 1024 key blocks (hist: the warp's 256 counts), the
+// bisection from shared memory beyond.
+__device__ __forceinline__ void find_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t *hist,
+                                               uint32_t &T, int &need) {
+    if (kb <= 256) radix_from_smem<8>(mykeys, kb, extra, hist, lane, T, need);
+    else if (kb <= 512) radix_from_smem<16>(mykeys, kb, extra, hist, lane, T, need);
+    else if (kb <= 1024) radix_from_smem<32>(mykeys, kb, extra, hist, lane, T, need);
     else select_threshold<0>(mykeys, kb, extra, lane, T, need);
 }
 
@@ -343,9 +425,10 @@ __global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *_
     const int i = i0 + warp;
     if (warp >= ROWS || i >= qb) return;
     const uint32_t *mykeys = keys + (size_t)warp * kbp;
+    uint32_t *hist = keys + (size_t)ROWS * kbp + warp * 256;
     uint32_t T = 0xffffffffu;
     int need = 0;
-    if (extra > 0) find_threshold(mykeys, kb, extra, lane, T, need);
+    if (extra > 0) find_threshold(mykeys, kb, extra, lane, hist, T, need);
     write_selection(mykeys, kb, extra, T, need, lane, block, Lq, Lk, sink, ids + ((size_t)h * qb + i) * n_ids, n_ids,
                     mask ? mask + ((size_t)h * qb + i) * kb : nullptr);
 }
@@ -585,37 +668,12 @@ __device__ __forceinline__ uint32_t exact_key(const float *sq, const float4 *kro
     return ordered_bits(a);
 }
 
-// Warp-wide count of keys >= c (or > c when strict) over NK keys per lane in registers.
-template <int NK>
-__device__ __forceinline__ int count_keys(const uint32_t (&kr)[NK], uint32_t c, bool strict) {
-    int n4[4] = {0, 0, 0, 0};   // independent partial counts keep the add chains short
-#pragma unroll
-    for (int u = 0; u < NK; ++u) n4[u & 3] += strict ? (kr[u] > c) : (kr[u] >= c);
-    return (int)__reduce_add_sync(0xffffffffu, (unsigned)((n4[0] + n4[1]) + (n4[2] + n4[3])));
-}
-
-// The threshold of the exact mode's selection from keys in registers: T with need = the keys
-// equal to T to keep (lowest indices first), by bisection on the order-preserving bits. The
-// search stops as soon as exactly `extra` keys are >= the candidate: those are then the `extra`
-// largest with no tie across the boundary, the set the full search selects.
-template <int NK>
-__device__ __forceinline__ void threshold_regs(const uint32_t (&kr)[NK], int extra, uint32_t &T, int &need) {
-    T = 0u;
-    for (int bit = 31; bit >= 0; --bit) {
-        const uint32_t cand = T | (1u << bit);
-        const int c = count_keys(kr, cand, false);
-        if (c >= extra) {
-            T = cand;
-            if (c == extra) break;
-        }
-    }
-    need = extra - count_keys(kr, T, true);
-}
-
-// grid ceil(H * qb / FAST_WARPS), 32 * FAST_WARPS threads; NK keys per lane (kb <= 32 * NK): warp w
-// of the grid selects for query block (h, i) = (w / qb, w % qb), its keys in registers (key block
-// j = lane + 32 u in kr[u]). Dynamic shared memory: the query projections [FAST_WARPS][R] fp32,
-// then [FAST_WARPS][32] block indices.
+// grid ceil(H * qb / FAST_WARPS), 32 * FAST_WARPS threads; NK keys per lane (kb <= 32 * NK, the
+// fast scores' row stride kbr a multiple of 32 * NK): warp w of the grid selects for query block
+// (h, i) = (w / qb, w % qb), lane l holding key blocks j = NK l + u in kr[u] (ascending block order
+// runs lane by lane, so an ordered compaction is one prefix sum of per-lane counts). Dynamic
+// shared memory: the query projections [FAST_WARPS][R] fp32, [FAST_WARPS][32] block indices, then
+// [FAST_WARPS][256] radix histogram counts.
 // With t the exact mode's threshold search run on the fast keys (t lies between the (extra+1)-th
 // and the extra-th largest fast score) and e = 2 * max_j eps_j over the query block's candidates,
 // every candidate is
@@ -638,22 +696,29 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
     int *rescored, int *status) {
     extern __shared__ __align__(16) uint8_t smr[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const unsigned lt = (1u << lane) - 1u;
     const int gw = blockIdx.x * FAST_WARPS + warp;   // = h * qb + i
     if (gw >= H * qb) return;
-    const int h = gw / qb;
+    const int h = gw / qb, jl = NK * lane;
     float *sq = reinterpret_cast<float *>(smr) + warp * R;
     int *uidx = reinterpret_cast<int *>(reinterpret_cast<float *>(smr) + FAST_WARPS * R) + warp * 32;
+    uint32_t *hist = reinterpret_cast<uint32_t *>(reinterpret_cast<int *>(reinterpret_cast<float *>(smr) +
+                                                                          FAST_WARPS * R) + FAST_WARPS * 32) + warp * 256;
     const float4 *khh = reinterpret_cast<const float4 *>(kh + (size_t)h * kh_ld * R);
-    const float *srow = sfast + (size_t)gw * kbr;
-    const float *knh = kn + (size_t)h * kbr;
+    const float4 *srow4 = reinterpret_cast<const float4 *>(sfast + (size_t)gw * kbr + jl);
+    const float4 *knh4 = reinterpret_cast<const float4 *>(kn + (size_t)h * kbr + jl);
     uint32_t kr[NK];
     float kv[NK];
 #pragma unroll
-    for (int u = 0; u < NK; ++u) {
-        const int j = lane + 32 * u;
-        kr[u] = j < kb ? __float_as_uint(srow[j]) : 0u;
-        kv[u] = j < kb ? knh[j] : 0.f;
+    for (int x = 0; x < NK / 4; ++x) {
+        const float4 a = srow4[x], b = knh4[x];
+        kr[4 * x] = __float_as_uint(a.x);
+        kr[4 * x + 1] = __float_as_uint(a.y);
+        kr[4 * x + 2] = __float_as_uint(a.z);
+        kr[4 * x + 3] = __float_as_uint(a.w);
+        kv[4 * x] = b.x;
+        kv[4 * x + 1] = b.y;
+        kv[4 * x + 2] = b.z;
+        kv[4 * x + 3] = b.w;
     }
     float qn2 = 0.f;
     for (int e = lane; e < R; e += 32) {
@@ -666,15 +731,15 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
     float knmax = 0.f;
 #pragma unroll
     for (int u = 0; u < NK; ++u) {
-        const int j = lane + 32 * u;
+        const int j = jl + u;
+        const float sv = __uint_as_float(kr[u]);
         if (j < kb) {
-            const float sv = __uint_as_float(kr[u]);
             if (scores) scores[(size_t)gw * kb + j] = sv;
             bad |= !isfinite(sv);
-            const bool forced = is_forced(j, block, Lq, Lk, sink);
-            kr[u] = forced ? 0u : ordered_bits(sv == 0.f ? 0.f : sv);
-            if (!forced) knmax = fmaxf(knmax, kv[u]);
         }
+        const bool cand = j < kb && !is_forced(j, block, Lq, Lk, sink);
+        kr[u] = cand ? ordered_bits(sv == 0.f ? 0.f : sv) : 0u;
+        if (cand) knmax = fmaxf(knmax, kv[u]);
     }
     for (int o = 16; o > 0; o >>= 1) knmax = fmaxf(knmax, __shfl_xor_sync(0xffffffffu, knmax, o));
     bool full = __any_sync(0xffffffffu, bad);
@@ -685,22 +750,22 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
     if (extra > 0 && !full) {
         uint32_t T;
         int need;
-        threshold_regs(kr, extra, T, need);
+        threshold_radix(kr, extra, hist, lane, T, need);
         const float t = ordered_to_float(T);
         const float e = 2.f * fmaf(FAST_BOUND * sqrtf(qn2), knmax, FAST_ABS);
         const float up = t + e, dn = t - e;
         full = !(e <= 1.0e38f);
-        int nin = 0, nu = 0;
+        int nin_l = 0, nu_l = 0;
 #pragma unroll
         for (int u = 0; u < NK; ++u) {
             const float sv = ordered_to_float(kr[u]);
             const bool cand = kr[u] != 0u;
-            nin += __popc(__ballot_sync(0xffffffffu, cand && sv > up));
-            const unsigned b = __ballot_sync(0xffffffffu, cand && sv >= dn && sv <= up);
-            const int pos = nu + __popc(b & lt);
-            if (((b >> lane) & 1u) && pos < 32) uidx[pos] = lane + 32 * u;
-            nu += __popc(b);
+            nin_l += cand && sv > up;
+            nu_l += cand && sv >= dn && sv <= up;
         }
+        const int nin = (int)__reduce_add_sync(0xffffffffu, (unsigned)nin_l);
+        int nu;
+        const int ubase = warp_exclusive_scan(nu_l, lane, &nu);
         const int r = extra - nin;
         const bool take_all = r == nu, take_none = r == 0;
         unsigned takemask = 0u;
@@ -708,6 +773,12 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
             if (nu > 32) {
                 full = true;
             } else {
+                int k = ubase;
+#pragma unroll
+                for (int u = 0; u < NK; ++u) {
+                    const float sv = ordered_to_float(kr[u]);
+                    if (kr[u] != 0u && sv >= dn && sv <= up) uidx[k++] = jl + u;
+                }
                 __syncwarp();   // uidx
                 touched = true;
                 const int j = lane < nu ? uidx[lane] : 0;
@@ -727,36 +798,44 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
             }
         }
         if (!full) {
-            int pos_u = 0, opos = 0;
+            // selected: forced, in, and the taken uncertain ones; then the ordered compaction
+            uint64_t selbits = 0u;   // bit u: key block jl + u selected
+            int k = ubase;
 #pragma unroll
             for (int u = 0; u < NK; ++u) {
-                const int j = lane + 32 * u;
+                const int j = jl + u;
                 const float sv = ordered_to_float(kr[u]);
                 const bool cand = kr[u] != 0u;
                 const bool unc = cand && sv >= dn && sv <= up;
-                const unsigned b = __ballot_sync(0xffffffffu, unc);
-                const int upos = pos_u + __popc(b & lt);
-                pos_u += __popc(b);
-                const bool take = take_all || (!take_none && upos < 32 && ((takemask >> upos) & 1u));
-                const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (cand && sv > up) || (unc && take));
-                const unsigned bal = __ballot_sync(0xffffffffu, sel);
-                const int off = opos + __popc(bal & lt);
-                if (sel && off < n_ids) out[off] = j;
-                if (mrow && j < kb) mrow[j] = sel ? 1 : 0;
-                opos += __popc(bal);
+                const bool take = unc && (take_all || (!take_none && k < 32 && ((takemask >> k) & 1u)));
+                k += unc;
+                const bool sel = j < kb && ((!cand && is_forced(j, block, Lq, Lk, sink)) || (cand && sv > up) || take);
+                selbits |= (uint64_t)sel << u;
+            }
+            int total;
+            int o = warp_exclusive_scan(__popcll(selbits), lane, &total);
+#pragma unroll
+            for (int u = 0; u < NK; ++u) {
+                const int j = jl + u;
+                if ((selbits >> u) & 1u) {
+                    if (o < n_ids) out[o] = j;
+                    ++o;
+                }
+                if (mrow && j < kb) mrow[j] = (uint8_t)((selbits >> u) & 1u);
             }
         }
     }
     if (full || extra == 0) {
         // the exact mode: every key block scored with its arithmetic (only to select when extra > 0,
-        // and always to flag non-finite scores as it does), then its threshold and ordered compaction
+        // and always to flag non-finite scores as it does), then its threshold and its ordered
+        // compaction with the ties at T kept from the lowest index
         uint32_t T = 0xffffffffu;
         int need = 0;
         if (full) {
             bool nonfinite = false;
 #pragma unroll
             for (int u = 0; u < NK; ++u) {   // unrolled: kr stays in registers
-                const int j = lane + 32 * u;
+                const int j = jl + u;
                 if (j < kb) {
                     const uint32_t key = exact_key(sq, khh + (size_t)j * (R / 4), R, nonfinite);
                     kr[u] = is_forced(j, block, Lq, Lk, sink) ? 0u : key;
@@ -764,22 +843,33 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
             }
             if (__any_sync(0xffffffffu, nonfinite) && lane == 0) report(status, SS_DEV_NONFINITE);
             touched = true;
-            if (extra > 0) threshold_regs(kr, extra, T, need);
+            if (extra > 0) threshold_radix(kr, extra, hist, lane, T, need);
         }
-        int taken = 0, opos = 0;
+        int ties_l = 0;
+#pragma unroll
+        for (int u = 0; u < NK; ++u) ties_l += extra > 0 && jl + u < kb && kr[u] == T;
+        int ties;
+        int tie_rank = warp_exclusive_scan(ties_l, lane, &ties);
+        uint64_t selbits = 0u;   // bit u: key block jl + u selected
 #pragma unroll
         for (int u = 0; u < NK; ++u) {
-            const int j = lane + 32 * u;
+            const int j = jl + u;
             const bool tie = extra > 0 && j < kb && kr[u] == T;
-            const unsigned tb = __ballot_sync(0xffffffffu, tie);
-            const bool keep_tie = tie && taken + __popc(tb & lt) < need;
-            taken += __popc(tb);
+            const bool keep_tie = tie && tie_rank < need;
+            tie_rank += tie;
             const bool sel = j < kb && (is_forced(j, block, Lq, Lk, sink) || (extra > 0 && kr[u] > T) || keep_tie);
-            const unsigned bal = __ballot_sync(0xffffffffu, sel);
-            const int off = opos + __popc(bal & lt);
-            if (sel && off < n_ids) out[off] = j;
-            if (mrow && j < kb) mrow[j] = sel ? 1 : 0;
-            opos += __popc(bal);
+            selbits |= (uint64_t)sel << u;
+        }
+        int total;
+        int o = warp_exclusive_scan(__popcll(selbits), lane, &total);
+#pragma unroll
+        for (int u = 0; u < NK; ++u) {
+            const int j = jl + u;
+            if ((selbits >> u) & 1u) {
+                if (o < n_ids) out[o] = j;
+                ++o;
+            }
+            if (mrow && j < kb) mrow[j] = (uint8_t)((selbits >> u) & 1u);
         }
     }
     if (touched && rescored && lane == 0) atomicAdd(rescored, 1);
@@ -802,7 +892,7 @@ static size_t pp_smem(int R, int block, int nw) {
 }
 
 static size_t select_smem(int kb, int R) {
-    return (size_t)R * router::ROWS * 4 + (size_t)router::ROWS * kb * 4 + 16;
+    return (size_t)R * router::ROWS * 4 + (size_t)router::ROWS * kb * 4 + (size_t)router::ROWS * 256 * 4 + 16;
 }
 
 static int g_router_configured[SS_MAX_DEVICES] = {0};
@@ -842,8 +932,9 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // score_select in shared memory and the row count of the key projections
 static int kb_padded(int kb) { return (kb + 3) & ~3; }
 
-// key-block count rounded up to the fast mode's score tile (128): the row stride of its scores
-static int kb_tiles(int kb) { return (kb + router::TC_TILE - 1) / router::TC_TILE * router::TC_TILE; }
+// the fast mode's score row stride: 32 lanes x the selector's keys per lane (256, 512, 1024, 2048),
+// so a lane's keys are whole float4s of one row
+static int kb_tiles(int kb) { return kb <= 256 ? 256 : kb <= 512 ? 512 : kb <= 1024 ? 1024 : 2048; }
 
 // Workspace: query projections [H][qb][R], key projections [H][kbp][R] (when no caller table),
 // then for the fast mode its scores [H][qb][kbr] and key norms [H][kbr] (kbr = kb_tiles(kb)).
@@ -874,7 +965,7 @@ static size_t tc_smem(int R) {
     return 1024 + 2 * (size_t)(R / 32) * (router::TC_TILE + router::TC_N) * 128 + 64;
 }
 constexpr int FAST_MAX_KB = 2048;   // 64 keys per lane
-static size_t fast_smem(int R) { return (size_t)router::FAST_WARPS * ((size_t)R + 32) * 4; }
+static size_t fast_smem(int R) { return (size_t)router::FAST_WARPS * ((size_t)R + 32 + 256) * 4; }
 
 static int count_forced(int Lq, int Lk, int block, int sink) {
     const int kb = (Lk + block - 1) / block;
@@ -1057,7 +1148,13 @@ extern "C" int ss_router_noalloc(const void *q, const void *k, const float *wq, 
 
 extern "C" int ss_router_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes) {
     if (!bytes || H <= 0 || Lq <= 0 || Lk <= 0 || R <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
-    *bytes = ss::router_fast_workspace_size(H, Lq, Lk, R, block);   // enough for both modes
+    *bytes = ss::router_workspace_size(H, Lq, Lk, R, block);
+    return 0;
+}
+
+extern "C" int ss_router_fast_workspace_bytes(int H, int Lq, int Lk, int R, int block, size_t *bytes) {
+    if (!bytes || H <= 0 || Lq <= 0 || Lk <= 0 || R <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
+    *bytes = ss::router_fast_workspace_size(H, Lq, Lk, R, block);   // the exact mode's part, then the fast scores
     return 0;
 }
 

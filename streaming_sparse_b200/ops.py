@@ -141,9 +141,10 @@ class DeviceStatus:
 # router
 # ----------------------------------------------------------------------------------------------
 
-def router_workspace_bytes(H: int, Lq: int, Lk: int, R: int = 64, block: int = 64) -> int:
+def router_workspace_bytes(H: int, Lq: int, Lk: int, R: int = 64, block: int = 64, fast: bool = False) -> int:
     n = ctypes.c_size_t()
-    check(lib().ss_router_workspace_bytes(H, Lq, Lk, R, block, ctypes.byref(n)), "ss_router_workspace_bytes")
+    fn = lib().ss_router_fast_workspace_bytes if fast else lib().ss_router_workspace_bytes
+    check(fn(H, Lq, Lk, R, block, ctypes.byref(n)), "ss_router_workspace_bytes")
     return n.value
 
 
@@ -189,8 +190,8 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
     qb, kb = nblocks(Lq, block), nblocks(Lk, block)
     n_ids = forced_count(Lq, Lk, block, sink_tokens) + extra
     ws = _ws(workspace, q.device)
-    nbytes = router_workspace_bytes(H, Lq, Lk, R, block)
-    scratch = ws.tensor("router", (nbytes,), q.device, torch.uint8)
+    nbytes = router_workspace_bytes(H, Lq, Lk, R, block, fast=fast)
+    scratch = ws.tensor("router_fast" if fast else "router", (nbytes,), q.device, torch.uint8)
     ids = out if out is not None else torch.empty((H, qb, n_ids), dtype=torch.int32, device=q.device)
     _require(ids.shape == (H, qb, n_ids) and ids.dtype == torch.int32 and ids.is_contiguous(), "bad ids buffer")
     mask = torch.empty((H, qb, kb), dtype=torch.uint8, device=q.device) if return_mask else None
