@@ -51,7 +51,7 @@ def peaks():
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention launch at config 2,
 # from the ncu capture summarised in profiles/attention_sm100_config2.md (same command given there).
-ATTN_TRAFFIC_BYTES = 229491200
+ATTN_TRAFFIC_BYTES = 295373056
 ATTN_TRAFFIC_SOURCE = "ncu --set full capture of one config-2 attention launch (profiles/attention_sm100_config2.md)"
 
 
@@ -317,6 +317,9 @@ def hbm_kernels_bench(dev, args, hbm_gbs: float) -> dict:
     * ``cache_append_roll``: a chunk write into a full rolling window (config 4: 22 frames of
       1560 tokens with a 1-frame sink, 4680-token chunk): 28080 rows shifted left by 4680 in six
       copies, then the chunk written; (28080 + 4680) rows x 3 KB x (K, V) read + written.
+    * ``cache_append_ring_roll``: the same roll on a ring-buffer cache: the ring's head moves by
+      4680 rows and only the chunk (with at most 64 mirrored rows and the sink's last 24 rows
+      repeated before the head) is written.
     * ``lse_merge_8``: the KV-sharded merge of 8 partial outputs (fp32 [8, 4680, 12, 128] + LSE)
       into bf16, the combine step of 8-GPU KV-block sharding.
     * ``anchor_rebase``: one layer's anchor rebase (1560 canonical key rows copied into the
@@ -355,7 +358,39 @@ def hbm_kernels_bench(dev, args, hbm_gbs: float) -> dict:
     nbytes = (rolled + n) * row_bytes * 2 * 2
     out["cache_append_roll"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
                                 "frac": nbytes / (us * 1e-6) / 1e9 / hbm_gbs, "launches": rolled // evicted + 1}
-    del caches, chunks
+
+    # ---- the same roll on a ring-buffer cache: the head moves, only the chunk (plus the mirrored
+    # rows and the sink's copy before the head) is written
+    ring0 = ops.Ring(sink, cap - sink + 64, 10 * n % (cap - sink + 64))
+    rcaches = [(torch.randn((ring0.phys_rows(), H, D), generator=gen, device=dev).to(torch.bfloat16),
+                torch.randn((ring0.phys_rows(), H, D), generator=gen, device=dev).to(torch.bfloat16)) for _ in range(2)]
+
+    def ring_roll(i):
+        (kc, vc), (kn, vn) = rcaches[i % 2], chunks[i % 2]
+        return ops.cache_append_ring(kc, vc, kn, vn, cap=cap, local_attn=True, global_end=g_end, local_end=cap,
+                                     current_start=g_end, sink_tokens=sink, ring=ring0)
+
+    def window_of(kc, r):
+        t = torch.arange(cap, device=dev)
+        rows = torch.where(t < r.sink, t, r.sink + torch.remainder(t - r.sink + r.head, r.cap))
+        return kc.index_select(0, rows)
+
+    kc, vc = rcaches[0]
+    before = window_of(kc, ring0)
+    want_k = torch.cat((before[:sink], before[sink + evicted:], chunks[0][0]))
+    _, head = ring_roll(0)
+    torch.cuda.synchronize()
+    assert torch.equal(window_of(kc, ops.Ring(sink, ring0.cap, head)), want_k), "ring roll differs from the window roll"
+    del before, want_k
+    us = _graph_us(ring_roll, 2, args.steps)
+    a = sink % 64
+    rows_written = n + min(n, 64) + a + 64   # chunk, mirrored rows (at most 64), sink copy (+ its mirror, at most)
+    nbytes = (n + a) * row_bytes * 2 * 2     # read + written, K and V: the chunk and the sink's copy
+    out["cache_append_ring_roll"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9,
+                                     "frac": nbytes / (us * 1e-6) / 1e9 / hbm_gbs,
+                                     "rows_written_max": rows_written,
+                                     "vs_shift_bytes": out["cache_append_roll"]["bytes"]}
+    del caches, chunks, rcaches
 
     # ---- 8-part LSE merge
     P = 8
@@ -836,6 +871,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         q, k, v, wq, wk = sets[s]
         ops.route(q, k, wq, wk, block=BLOCK, extra=extra, workspace=ws, out=ids_buf[s])
 
+    fast_ids = [torch.empty_like(b) for b in ids_buf]
+
+    def route_fast(s):   # the tensor-core router mode (same ids), timed beside the exact one
+        q, k, v, wq, wk = sets[s]
+        ops.route(q, k, wq, wk, block=BLOCK, extra=extra, workspace=ws, out=fast_ids[s], keys=keys[s],
+                  n_cached=n_hist, fast=True)
+
     def attend(s):
         q, k, v, wq, wk = sets[s]
         ops.sparse_attention(q, k, v, ids_buf[s], block=BLOCK, out=out)
@@ -850,8 +892,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     cached_ids = [b.clone() for b in ids_buf]
     for s in range(2):
         route_uncached(s)
+        route_fast(s)
     torch.cuda.synchronize()
     assert all(torch.equal(a, b) for a, b in zip(cached_ids, ids_buf)), "cached route differs from the full route"
+    fast_equal = all(torch.equal(a, b) for a, b in zip(cached_ids, fast_ids))
+    assert fast_equal, "the fast router's ids differ from the exact router's"
     flops = [effective_flops(b.cpu().numpy()) for b in ids_buf]
     # router FLOPs (reported separately): pooled projections + block-score GEMM
     qb, kb = math.ceil(LQ / BLOCK), math.ceil(LK / BLOCK)
@@ -860,9 +905,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # one CUDA graph per (stage, input set): a step replays the router graph (after the commit
     # graph on the set's every fourth call: a chunk's four denoising calls share one commit), then
     # the attention graph
-    g_commit, g_route, g_attn, g_full = [], [], [], []
+    g_commit, g_route, g_attn, g_full, g_fast = [], [], [], [], []
     for s in range(2):
-        for fn, lst in ((commit, g_commit), (route, g_route), (attend, g_attn), (route_uncached, g_full)):
+        for fn, lst in ((commit, g_commit), (route, g_route), (attend, g_attn), (route_uncached, g_full),
+                        (route_fast, g_fast)):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn(s)
@@ -917,7 +963,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     commit_us = 1e3 * _replay_ms(g_commit, 20)
     route_full_us = 1e3 * _replay_ms(g_full, 20)
     route_cached_us = 1e3 * _replay_ms(g_route, 20)
-    del g_commit, g_full
+    route_fast_us = 1e3 * _replay_ms(g_fast, 20)
+    del g_commit, g_full, g_fast
 
     # ---- e2e: the public plugin call with host buffers (pinned), copies inside the timed region
     sparse = SparseAttention(sets[0][3], sets[0][4], RouterConfig(density=DENSITY), workspace=ws)
@@ -1038,7 +1085,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "clocks": clk.summary(),
         "us_per_chunk_layer": r(1e3 * elapsed_ms / args.steps),
         "attention_us": r(1e3 * att_avg), "router_us": r(1e3 * statistics.mean(rt_ms)),
-        "router": {"cached_us": r(route_cached_us), "commit_pool_us": r(commit_us), "full_us": r(route_full_us)},
+        "router": {"cached_us": r(route_cached_us), "commit_pool_us": r(commit_us), "full_us": r(route_full_us),
+                   "fast_cached_us": r(route_fast_us), "fast_ids_equal": fast_equal},
+        "roll": {"shift_us": r(hbm_k["cache_append_roll"]["us"]), "shift_mb": r(hbm_k["cache_append_roll"]["bytes"] / 1e6),
+                 "ring_us": r(hbm_k["cache_append_ring_roll"]["us"]),
+                 "ring_mb": r(hbm_k["cache_append_ring_roll"]["bytes"] / 1e6)},
         "effective_gflop": r(statistics.mean(flops) / 1e9), "router_gflop": r(router_flops / 1e9, 3),
         "e2e_streaming": {"value": r(streaming["value"]), "ms_per_step": r(streaming["ms_per_step"], 3),
                           "h2d_bytes_per_step": streaming["h2d_bytes_per_step"]},

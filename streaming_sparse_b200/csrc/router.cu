@@ -255,82 +255,12 @@ __device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int *total) 
     return x - v;
 }
 
-// The threshold of the exact mode's selection (as select_threshold: T = the extra-th largest
-// nonzero key, need = the keys equal to T to keep) by a most-significant-digit radix select over
-// the keys in registers: four passes of 8 bits, each a histogram of the next digit of the keys
-// that match the digits found so far (shared-memory counts of one warp, hist[256]), scanned from
-// the top digit down to the bin holding the rank still sought. Four passes instead of 32
-// bisection steps; the result is the same T, and rank left at the end is `need`.
-template <int NK>
-__device__ __forceinline__ void threshold_radix(const uint32_t (&kr)[NK], int extra, uint32_t *hist, int lane,
-                                                uint32_t &T, int &need) {
-    uint32_t prefix = 0u, pmask = 0u;
-    int rank = extra;   // rank, from the top, of the key sought among those matching prefix
-#pragma unroll 1
-    for (int shift = 24; shift >= 0; shift -= 8) {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) hist[lane + 32 * b] = 0u;
-        __syncwarp();
-#pragma unroll
-        for (int u = 0; u < NK; ++u)
-            if (kr[u] != 0u && (kr[u] & pmask) == prefix) atomicAdd(&hist[(kr[u] >> shift) & 255u], 1u);
-        __syncwarp();
-        // lane l holds bins 255 - 8l down to 248 - 8l
-        uint32_t c[8];
-        int sum = 0;
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            c[b] = hist[255 - 8 * lane - b];
-            sum += (int)c[b];
-        }
-        int total;
-        const int above = warp_exclusive_scan(sum, lane, &total);   // keys in higher bins
-        const bool mine = above < rank && rank <= above + sum;
-        const int owner = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
-        int digit = 0, before = 0;
-        if (mine) {
-            int acc = above;
-#pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                if (acc + (int)c[b] >= rank) {
-                    digit = 255 - 8 * lane - b;
-                    before = acc;
-                    break;
-                }
-                acc += (int)c[b];
-            }
-        }
-        digit = __shfl_sync(0xffffffffu, digit, owner);
-        before = __shfl_sync(0xffffffffu, before, owner);
-        prefix |= (uint32_t)digit << shift;
-        pmask |= 255u << shift;
-        rank -= before;
-        __syncwarp();   // the histogram is cleared by the next pass
-    }
-    T = prefix;
-    need = rank;
-}
-
-template <int NK>
-__device__ __forceinline__ void radix_from_smem(const uint32_t *mykeys, int kb, int extra, uint32_t *hist, int lane,
-                                                uint32_t &T, int &need) {
-    uint32_t kr[NK];
-#pragma unroll
-    for (int u = 0; u < NK; ++u) {
-        const int j = lane + 32 * u;
-        kr[u] = j < kb ? mykeys[j] : 0u;
-    }
-    threshold_radix(kr, extra, hist, lane, T, need);
-}
-
-// The selection threshold of one query block's keys (in shared memory), run by one warp: a radix
-// select over the keys in registers up to 1024 key blocks (hist: the warp's 256 counts), the
-// bisection from shared memory beyond.
-__device__ __forceinline__ void find_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t *hist,
-                                               uint32_t &T, int &need) {
-    if (kb <= 256) radix_from_smem<8>(mykeys, kb, extra, hist, lane, T, need);
-    else if (kb <= 512) radix_from_smem<16>(mykeys, kb, extra, hist, lane, T, need);
-    else if (kb <= 1024) radix_from_smem<32>(mykeys, kb, extra, hist, lane, T, need);
+// select_threshold with the keys per lane chosen by the key-block count.
+__device__ __forceinline__ void find_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t &T,
+                                               int &need) {
+    if (kb <= 256) select_threshold<8>(mykeys, kb, extra, lane, T, need);
+    else if (kb <= 512) select_threshold<16>(mykeys, kb, extra, lane, T, need);
+    else if (kb <= 1024) select_threshold<32>(mykeys, kb, extra, lane, T, need);
     else select_threshold<0>(mykeys, kb, extra, lane, T, need);
 }
 
@@ -425,10 +355,9 @@ __global__ void __launch_bounds__(SS_THREADS) score_select_kernel(const float *_
     const int i = i0 + warp;
     if (warp >= ROWS || i >= qb) return;
     const uint32_t *mykeys = keys + (size_t)warp * kbp;
-    uint32_t *hist = keys + (size_t)ROWS * kbp + warp * 256;
     uint32_t T = 0xffffffffu;
     int need = 0;
-    if (extra > 0) find_threshold(mykeys, kb, extra, lane, hist, T, need);
+    if (extra > 0) find_threshold(mykeys, kb, extra, lane, T, need);
     write_selection(mykeys, kb, extra, T, need, lane, block, Lq, Lk, sink, ids + ((size_t)h * qb + i) * n_ids, n_ids,
                     mask ? mask + ((size_t)h * qb + i) * kb : nullptr);
 }
@@ -668,12 +597,40 @@ __device__ __forceinline__ uint32_t exact_key(const float *sq, const float4 *kro
     return ordered_bits(a);
 }
 
+// Warp-wide count of keys >= c (or > c when strict) over NK keys per lane in registers.
+template <int NK>
+__device__ __forceinline__ int count_keys(const uint32_t (&kr)[NK], uint32_t c, bool strict) {
+    int n4[4] = {0, 0, 0, 0};   // independent partial counts keep the add chains short
+#pragma unroll
+    for (int u = 0; u < NK; ++u) n4[u & 3] += strict ? (kr[u] > c) : (kr[u] >= c);
+    return (int)__reduce_add_sync(0xffffffffu, (unsigned)((n4[0] + n4[1]) + (n4[2] + n4[3])));
+}
+
+// The threshold of the exact mode's selection from keys in registers: T with need = the keys
+// equal to T to keep (lowest indices first), by bisection on the order-preserving bits. The
+// search stops as soon as exactly `extra` keys are >= the candidate: those are then the `extra`
+// largest with no tie across the boundary, the set the full search selects. (A radix select with
+// shared-memory histograms measured slower here: most keys share their top digits, so the
+// histogram atomics serialise.)
+template <int NK>
+__device__ __forceinline__ void threshold_regs(const uint32_t (&kr)[NK], int extra, uint32_t &T, int &need) {
+    T = 0u;
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = T | (1u << bit);
+        const int c = count_keys(kr, cand, false);
+        if (c >= extra) {
+            T = cand;
+            if (c == extra) break;
+        }
+    }
+    need = extra - count_keys(kr, T, true);
+}
+
 // grid ceil(H * qb / FAST_WARPS), 32 * FAST_WARPS threads; NK keys per lane (kb <= 32 * NK, the
 // fast scores' row stride kbr a multiple of 32 * NK): warp w of the grid selects for query block
 // (h, i) = (w / qb, w % qb), lane l holding key blocks j = NK l + u in kr[u] (ascending block order
 // runs lane by lane, so an ordered compaction is one prefix sum of per-lane counts). Dynamic
-// shared memory: the query projections [FAST_WARPS][R] fp32, [FAST_WARPS][32] block indices, then
-// [FAST_WARPS][256] radix histogram counts.
+// shared memory: the query projections [FAST_WARPS][R] fp32, then [FAST_WARPS][32] block indices.
 // With t the exact mode's threshold search run on the fast keys (t lies between the (extra+1)-th
 // and the extra-th largest fast score) and e = 2 * max_j eps_j over the query block's candidates,
 // every candidate is
@@ -701,8 +658,6 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
     const int h = gw / qb, jl = NK * lane;
     float *sq = reinterpret_cast<float *>(smr) + warp * R;
     int *uidx = reinterpret_cast<int *>(reinterpret_cast<float *>(smr) + FAST_WARPS * R) + warp * 32;
-    uint32_t *hist = reinterpret_cast<uint32_t *>(reinterpret_cast<int *>(reinterpret_cast<float *>(smr) +
-                                                                          FAST_WARPS * R) + FAST_WARPS * 32) + warp * 256;
     const float4 *khh = reinterpret_cast<const float4 *>(kh + (size_t)h * kh_ld * R);
     const float4 *srow4 = reinterpret_cast<const float4 *>(sfast + (size_t)gw * kbr + jl);
     const float4 *knh4 = reinterpret_cast<const float4 *>(kn + (size_t)h * kbr + jl);
@@ -750,7 +705,7 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
     if (extra > 0 && !full) {
         uint32_t T;
         int need;
-        threshold_radix(kr, extra, hist, lane, T, need);
+        threshold_regs(kr, extra, T, need);
         const float t = ordered_to_float(T);
         const float e = 2.f * fmaf(FAST_BOUND * sqrtf(qn2), knmax, FAST_ABS);
         const float up = t + e, dn = t - e;
@@ -843,7 +798,7 @@ __global__ void __launch_bounds__(32 * FAST_WARPS) select_fast_kernel(
             }
             if (__any_sync(0xffffffffu, nonfinite) && lane == 0) report(status, SS_DEV_NONFINITE);
             touched = true;
-            if (extra > 0) threshold_radix(kr, extra, hist, lane, T, need);
+            if (extra > 0) threshold_regs(kr, extra, T, need);
         }
         int ties_l = 0;
 #pragma unroll
@@ -892,7 +847,7 @@ static size_t pp_smem(int R, int block, int nw) {
 }
 
 static size_t select_smem(int kb, int R) {
-    return (size_t)R * router::ROWS * 4 + (size_t)router::ROWS * kb * 4 + (size_t)router::ROWS * 256 * 4 + 16;
+    return (size_t)R * router::ROWS * 4 + (size_t)router::ROWS * kb * 4 + 16;
 }
 
 static int g_router_configured[SS_MAX_DEVICES] = {0};
@@ -965,7 +920,7 @@ static size_t tc_smem(int R) {
     return 1024 + 2 * (size_t)(R / 32) * (router::TC_TILE + router::TC_N) * 128 + 64;
 }
 constexpr int FAST_MAX_KB = 2048;   // 64 keys per lane
-static size_t fast_smem(int R) { return (size_t)router::FAST_WARPS * ((size_t)R + 32 + 256) * 4; }
+static size_t fast_smem(int R) { return (size_t)router::FAST_WARPS * ((size_t)R + 32) * 4; }
 
 static int count_forced(int Lq, int Lk, int block, int sink) {
     const int kb = (Lk + block - 1) / block;
