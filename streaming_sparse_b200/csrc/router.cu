@@ -213,7 +213,10 @@ __device__ __forceinline__ uint32_t ordered_bits(float f) {
 
 // Threshold of one query block's selection: T = the extra-th largest candidate key (bisection on
 // the order-preserving bits) and `need` = how many keys equal to T are kept, run by one warp. NK
-// keys per lane are held in registers (NK = 0: read from shared memory at every step).
+// keys per lane are held in registers (NK = 0: read from shared memory at every step). The search
+// stops early once exactly `extra` keys are >= the candidate: T is then not necessarily a key, but
+// {key >= T} is the same `extra` keys the full search keeps (its T is their minimum, with all of
+// its ties among them).
 template <int NK>
 __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb, int extra, int lane, uint32_t &T,
                                                  int &need) {
@@ -238,9 +241,13 @@ __device__ __forceinline__ void select_threshold(const uint32_t *mykeys, int kb,
     T = 0u;
     for (int bit = 31; bit >= 0; --bit) {
         const uint32_t cand = T | (1u << bit);
-        if (count(cand, false) >= extra) T = cand;
+        const int c = count(cand, false);
+        if (c >= extra) {
+            T = cand;
+            if (c == extra) break;   // exactly `extra` keys >= cand: they are the selection, no tie across it
+        }
     }
-    need = extra - count(T, true);   // ties at T to keep, >= 1
+    need = extra - count(T, true);   // ties at T to keep (all keys equal to T when the search stopped early)
 }
 
 // Exclusive prefix sum of v over the warp's lanes (and the total in *total).
