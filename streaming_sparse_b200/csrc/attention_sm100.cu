@@ -69,12 +69,13 @@ constexpr uint32_t OFF_BAR = 0;
 constexpr int NBAR = 32;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;  // flags and counters
 constexpr uint32_t OFF_TILES = OFF_MISC + 64;      // Tile table [MAXT]
+constexpr uint32_t OFF_TINFO = OFF_TILES + MAXT * 16;  // prologue: per candidate tile 4 ints
 constexpr uint32_t OFF_XCH = 1024;                 // log-sum-exp merge: [2 wg][m, l][128 rows]
 constexpr uint32_t OFF_RING = OFF_XCH + 2 * 2 * 128 * 4;  // 1024-aligned
 constexpr uint32_t SMEM_LIMIT = 232448;            // 227 KB opt-in maximum per CTA
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TMEM_S = 0, TMEM_P = 128, TMEM_Q = 192, TMEM_O = 256;
-static_assert(OFF_TILES + MAXT * 16 <= OFF_XCH, "table space");
+static_assert(OFF_TINFO + MAXT * 16 <= OFF_XCH, "table space");
 static_assert(OFF_RING % 1024 == 0, "ring alignment");
 
 enum Bar {
@@ -184,35 +185,27 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 // Ascending compaction of the set bits of word(w) (w < nwords) into sub-block entries, run by
 // one warp; sub-block k of the output is stored by put(k, entry). Returns the number written.
 template <class W, class M, class P>
-__device__ __forceinline__ int compact(int nwords, int block, int Lk, const KvRing &ring, int lane, W &&word,
-                                       M &&maskof, P &&put) {
+__device__ __forceinline__ void compact(int nwords, int block, int Lk, const KvRing &ring, int lane, W &&word,
+                                        M &&maskof, P &&put) {
+    // the set bits of word(0), word(1), ... in ascending block order: lane l takes bit l of each
+    // word, its rank among the word's set bits is the popcount of the bits below it
     const int per = block / 64;
+    const uint32_t below = (1u << lane) - 1u;
     int carry = 0;
-    for (int w0 = 0; w0 < nwords; w0 += 32) {
-        const int w = w0 + lane;
-        uint32_t u = w < nwords ? word(w) : 0u;
-        const int cnt = __popc(u) * per;
-        int incl = cnt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        int pos = carry + incl - cnt;
-        while (u) {
-            const int bit = __ffs(u) - 1;
-            u &= u - 1;
-            const int j = w * 32 + bit;
-            const uint32_t m = maskof(w, bit);
+    for (int w = 0; w < nwords; ++w) {
+        const uint32_t u = word(w);
+        if ((u >> lane) & 1u) {
+            const int j = w * 32 + lane;
+            const uint32_t m = maskof(w, lane);
+            const int pos = carry + __popc(u & below) * per;
             for (int s = 0; s < per; ++s) {
                 const int t0 = j * block + s * 64;
                 const int valid = min(64, max(0, Lk - t0));
-                put(pos++, entry((uint32_t)ring.sub_row(t0), (uint32_t)valid, m));
+                put(pos + s, entry((uint32_t)ring.sub_row(t0), (uint32_t)valid, m));
             }
         }
-        carry += __shfl_sync(0xffffffffu, incl, 31);
+        carry += __popc(u) * per;
     }
-    return carry;
 }
 
 __device__ __forceinline__ int warp_count_bits(int nwords, int lane, int per, const uint32_t *a, const uint32_t *b,
@@ -385,7 +378,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         }
     }
     __syncthreads();
-    if (warp == 0) {
+    {
         // Per tile, the union's sub-blocks, padded to a whole, even number (>= 2) of steps. A
         // 64-row half of the tile runs on two fixed SM sub-partitions (TMEM lane quarters), so a
         // step whose sub-blocks only one half selected keeps the other half's sub-partitions
@@ -396,61 +389,86 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
         // start of a tile reads K/V that the head's other tiles (and warp 3's L2 prefetch) have
         // already brought into L2. Order: both (an even count), the pairs, the unpaired rest, the
         // odd "both" sub-block if there is one; each group ascending.
+        // Built in three passes over the warps: the piece counts (one warp per tile), the list
+        // offsets and tile table (warp 0), the entries (one warp per tile and group).
         uint32_t *sub = reinterpret_cast<uint32_t *>(steps);
-        int pos = 0;   // sub-blocks written
-        int nout = 0;  // table entries (pieces with steps)
-        for (int lt = 0; lt < ntc; ++lt) {
+        int *tinfo = reinterpret_cast<int *>(smem + OFF_TINFO);   // per tile: A only, B only, both, offset
+        const int per = p.block / 64;
+        for (int lt = warp; lt < ntc; lt += NTHREADS / 32) {
             const uint32_t *A = bm + (2 * lt) * p.nwords, *B = A + p.nwords;
-            const int per = p.block / 64;
+            const int na = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0xffffffffu);   // A only
+            const int nb = warp_count_bits(p.nwords, lane, per, B, A, 0u, 0xffffffffu);   // B only
+            const int nboth = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0u);         // both
+            if (lane == 0) {
+                tinfo[4 * lt] = na;
+                tinfo[4 * lt + 1] = nb;
+                tinfo[4 * lt + 2] = nboth;
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int pos = 0;   // sub-blocks before the tile's list
+            int nout = 0;  // table entries (pieces with steps)
+            for (int lt = 0; lt < ntc; ++lt) {
+                const int n = tinfo[4 * lt] + tinfo[4 * lt + 1] + tinfo[4 * lt + 2];
+                const int padded = max(4, (n + 3) & ~3);
+                if (lane == 0) tinfo[4 * lt + 3] = pos;
+                // the steps this CTA runs: the whole list, or in split mode its share of the tile's
+                // step pairs (the same cut for every CTA holding a piece of the tile)
+                const int t = cand_tile(lt), tsteps = padded / 2;
+                int s0 = 0, s1 = tsteps, slot = -1;
+                if (p.split) {
+                    const long g0 = (long)t * p.G, u0 = (long)blockIdx.x * p.T;
+                    const long a = max(u0, g0) - g0, b = min(u0 + p.T, g0 + p.G) - g0;
+                    if (a > 0 || b < p.G) {
+                        const long pairs = tsteps / 2;
+                        s0 = 2 * (int)(a * pairs / p.G);
+                        s1 = 2 * (int)(b * pairs / p.G);
+                        slot = split_slot((int)blockIdx.x, t, p.T, p.G);
+                    }
+                }
+                if (s1 > s0) {
+                    if (lane == 0) {
+                        Tile tl;
+                        tl.first = pos / 2 + s0;
+                        tl.n = s1 - s0;
+                        tl.tile = t;
+                        tl.slot = slot;
+                        tiles[nout] = tl;
+                    }
+                    ++nout;
+                } else {   // a piece without steps: an empty partial for the merge
+                    for (int r = lane; r < 128; r += 32) p.ws_lse[(size_t)slot * 128 + r] = -INFINITY;
+                }
+                pos += padded;
+            }
+            if (lane == 0) *nt_slot = nout;
+        }
+        __syncthreads();
+        for (int job = warp; job < 3 * ntc; job += NTHREADS / 32) {
+            const int lt = job / 3, grp = job % 3;
+            const uint32_t *A = bm + (2 * lt) * p.nwords, *B = A + p.nwords;
             auto maskof = [&](int w, int bit) -> uint32_t {
                 if (!pairq) return 3u;
                 return ((A[w] >> bit) & 1u) | (((B[w] >> bit) & 1u) << 1);
             };
-            const int na = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0xffffffffu);   // A only
-            const int nb = warp_count_bits(p.nwords, lane, per, B, A, 0u, 0xffffffffu);   // B only
-            const int nboth = warp_count_bits(p.nwords, lane, per, A, B, 0u, 0u);         // both
+            const int na = tinfo[4 * lt], nb = tinfo[4 * lt + 1], nboth = tinfo[4 * lt + 2];
             const int mp = min(na, nb), nb2 = nboth & ~1;
             const int n = na + nb + nboth;
-            uint32_t *base = sub + pos;
-            compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & B[w]; }, maskof,
-                    [&](int k, uint32_t e) { base[k < nb2 ? k : n - 1] = e; });
-            compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
-                    [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k : mp + k)] = e; });
-            compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
-                    [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k + 1 : mp + k)] = e; });
-            const int padded = max(4, (n + 3) & ~3);
-            for (int k = n + lane; k < padded; k += 32) sub[pos + k] = entry(0u, 0u, 0u);
-            // the steps this CTA runs: the whole list, or in split mode its share of the tile's
-            // step pairs (the same cut for every CTA holding a piece of the tile)
-            const int t = cand_tile(lt), tsteps = padded / 2;
-            int s0 = 0, s1 = tsteps, slot = -1;
-            if (p.split) {
-                const long g0 = (long)t * p.G, u0 = (long)blockIdx.x * p.T;
-                const long a = max(u0, g0) - g0, b = min(u0 + p.T, g0 + p.G) - g0;
-                if (a > 0 || b < p.G) {
-                    const long pairs = tsteps / 2;
-                    s0 = 2 * (int)(a * pairs / p.G);
-                    s1 = 2 * (int)(b * pairs / p.G);
-                    slot = split_slot((int)blockIdx.x, t, p.T, p.G);
-                }
+            uint32_t *base = sub + tinfo[4 * lt + 3];
+            if (grp == 0) {
+                compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & B[w]; }, maskof,
+                        [&](int k, uint32_t e) { base[k < nb2 ? k : n - 1] = e; });
+                const int padded = max(4, (n + 3) & ~3);
+                for (int k = n + lane; k < padded; k += 32) base[k] = entry(0u, 0u, 0u);
+            } else if (grp == 1) {
+                compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
+                        [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k : mp + k)] = e; });
+            } else {
+                compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
+                        [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k + 1 : mp + k)] = e; });
             }
-            if (s1 > s0) {
-                if (lane == 0) {
-                    Tile tl;
-                    tl.first = pos / 2 + s0;
-                    tl.n = s1 - s0;
-                    tl.tile = t;
-                    tl.slot = slot;
-                    tiles[nout] = tl;
-                }
-                ++nout;
-            } else {   // a piece without steps: an empty partial for the merge
-                for (int r = lane; r < 128; r += 32) p.ws_lse[(size_t)slot * 128 + r] = -INFINITY;
-            }
-            pos += padded;
-            __syncwarp();
         }
-        if (lane == 0) *nt_slot = nout;
     }
     tc_fence_before();
     __syncthreads();
