@@ -584,6 +584,11 @@ def rollout_bench(dev, args, world: int):
     ms_d, ok_d = res["dense"]
     frames = cfg.frames * world
     c4 = rollout4_bench(dev, args) if world == 1 else None
+    if c4 is not None:
+        c4r = rollout4_bench(dev, args, ring=True)
+        c4["ring_cache"] = {"value": c4r["value"], "ms_per_rollout": c4r["ms_per_rollout"],
+                            "latents_equal": bool(torch.equal(c4r.pop("latents"), c4["latents"]))}
+        c4.pop("latents")
     return {"metric": "latent frames/s (config 3 rollout, all streams)", "value": frames / (ms_s * 1e-3),
             "unit": "frames/s", "streams": world, "frames_per_stream": cfg.frames, "ms_per_rollout": ms_s,
             "dense_value": frames / (ms_d * 1e-3), "dense_ms_per_rollout": ms_d, "speedup_vs_dense": ms_d / ms_s,
@@ -598,16 +603,17 @@ def rollout_bench(dev, args, world: int):
             "config4_long_horizon": c4}
 
 
-def rollout4_bench(dev, args):
+def rollout4_bench(dev, args, ring: bool = False):
     """Config 4's stream on one GPU: 120 latent frames in 40 chunks through a rolling window of 21
     frames + 1 sink frame (34320 tokens), 128-token router blocks at 10 % of the unforced blocks;
     the window rolls on every chunk's first call from chunk 7 on. One timed rollout after an eager
     warm-up and a capture run (routed only; the dense model is timed by
-    `python -m streaming_sparse_b200.rollout --config4 --dense`)."""
+    `python -m streaming_sparse_b200.rollout --config4 --dense`). ``ring``: the layers' KV caches
+    as ring buffers (a roll moves the head; heads in device memory under graph replay)."""
     from streaming_sparse_b200 import rollout as R
     from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
 
-    cfg = R.WanConfig(frames=120, cache_frames=22, local_attn_frames=22, sink_frames=1)
+    cfg = R.WanConfig(frames=120, cache_frames=22, local_attn_frames=22, sink_frames=1, ring_cache=ring)
     model = R.build_model(cfg, device=dev, seed=0)
     g = torch.Generator(device=dev)
     noise = torch.randn((cfg.frames, cfg.in_dim, cfg.latent_h, cfg.latent_w), device=dev, generator=g.manual_seed(3))
@@ -625,7 +631,8 @@ def rollout4_bench(dev, args):
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
     res = {"value": cfg.frames / (ms * 1e-3), "unit": "frames/s", "ms_per_rollout": ms, "frames": cfg.frames,
-           "graphs": len(ro._graph), "finite": bool(torch.isfinite(out).all())}
+           "graphs": len(ro._graph), "finite": bool(torch.isfinite(out).all()), "ring_cache": ring,
+           "latents": out}
     ro.release_graphs()
     del ro, model
     torch.cuda.empty_cache()
@@ -1097,7 +1104,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "frames_s": r(rollout["value"], 2), "dense_frames_s": r(rollout["dense_value"], 2),
             "streams": rollout["streams"],
             "config4_frames_s": None if rollout["config4_long_horizon"] is None else
-            r(rollout["config4_long_horizon"]["value"], 2)},
+            r(rollout["config4_long_horizon"]["value"], 2),
+            "config4_ring_frames_s": None if rollout["config4_long_horizon"] is None else
+            r(rollout["config4_long_horizon"]["ring_cache"]["value"], 2)},
         "configs_frac": None if other is None else {o["short"]: [r(o["us"]), r(o["frac_of_peak"], 3)] for o in other},
         "sharded": None if sharded is None else {
             "c4_1gpu_us": r(sharded["single_gpu_us"]),

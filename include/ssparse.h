@@ -167,6 +167,9 @@ int ss_router_fast(const void *q, const void *k, int k_row0, const float *wq, co
  * ring_head - S mod 64 .. ring_head - 1, so that every 64-row sub-block of the window is one
  * contiguous physical range (kept by ss_cache_append_ring / ss_cache_ring_refresh). Physical rows:
  * S + C + 64; the window (Lk rows, starting at the cache's row 0) needs Lk - S + S mod 64 <= C.
+ * ring_head_dev (optional, device int): where the head lives for calls captured in a CUDA graph.
+ * When it is given the kernels read the head from it at run time (ring_head must still be the
+ * current head, for the host checks), and ss_cache_append_ring moves it on after its copies.
  * The reference's paged store advances the same kind of cursor over whole pages
  * (`PageStore.commit`: write = sink + (end - sink) % (history_pages - sink),
  * local_experiments/review_v1/runtime.py:38-46); here it runs per token, because the frames
@@ -176,7 +179,7 @@ int ss_router_fast(const void *q, const void *k, int k_row0, const float *wq, co
 /* ss_router_pool_keys over a ring cache k (S + C + 64 rows). */
 int ss_router_pool_keys_ring(const void *k, const float *wk, int H, int Lk, int R, int block, int j0, int j1,
                              float *kh, int kh_rows, int ring_sink, int ring_cap, int ring_head,
-                             int *status, void *stream);
+                             const int *ring_head_dev, int *status, void *stream);
 
 /* The router over a ring cache k: the exact mode (fast = 0, ss_router / ss_router_cached) or the
  * tensor-core mode (fast != 0, ss_router_fast), the first n_cached key blocks' projections from kh
@@ -185,7 +188,7 @@ int ss_router_ring(const void *q, const void *k, const float *wq, const float *w
                    int H, int Lq, int Lk, int R, int block, int sink_tokens, int extra,
                    float *kh, int kh_rows, int n_cached,
                    int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *rescored, int fast,
-                   int ring_sink, int ring_cap, int ring_head,
+                   int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
                    void *workspace, size_t workspace_bytes, int *status, void *stream);
 
 /* Bytes of the static device array used by ss_router_noalloc (8 MiB per device that loads the
@@ -254,7 +257,7 @@ int ss_attention_ws(const void *q, const void *k, const void *v, const int32_t *
 int ss_attention_ring(const void *q, const void *k, const void *v, const int32_t *ids,
                       int H, int Lq, int Lk, int block, int n_ids, float scale,
                       void *out, int out_dtype, float *lse, int *status,
-                      int ring_sink, int ring_cap, int ring_head,
+                      int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
                       void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------------------ */
@@ -340,13 +343,13 @@ int ss_cache_append(void *k_cache, void *v_cache, int cap, int H,
 int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H,
                          const void *k_new, const void *v_new, int64_t new_stride, int n_new,
                          int local_attn, int64_t global_end, int64_t local_end,
-                         int64_t current_start, int sink_tokens, int ring_cap, int ring_head,
+                         int64_t current_start, int sink_tokens, int ring_cap, int ring_head, int *ring_head_dev,
                          int64_t *out_local_end, int *out_ring_head, void *stream);
 
 /* Rewrite the copy of the sink's last sink_tokens mod 64 rows before the ring's head (and its
  * mirrored rows), after the sink rows changed outside ss_cache_append_ring (an anchor rebase). */
 int ss_cache_ring_refresh(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap, int ring_head,
-                          void *stream);
+                          const int *ring_head_dev, void *stream);
 
 /* Rotate the first `pairs` complex pairs (elements 2p, 2p+1) of every head of rows [0, n) of a
  * key tensor [n][H][128] bf16 by phase[p] = (cos, sin) (float64 [pairs][2], device memory):

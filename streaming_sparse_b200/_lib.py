@@ -39,13 +39,13 @@ SIGNATURES = {
                           _P], _I),
     "ss_router_fast": ([_P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I, _P, _P, _P, _P, _SZ,
                         _P, _P], _I),
-    "ss_router_pool_keys_ring": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P], _I),
+    "ss_router_pool_keys_ring": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P], _I),
     "ss_router_ring": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _I,
-                        _P, _SZ, _P, _P], _I),
-    "ss_attention_ring": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _I, _I, _I, _P, _SZ, _P], _I),
-    "ss_cache_append_ring": ([_P, _P, _I, _I, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _I, _I, _I,
+                        _P, _P, _SZ, _P, _P], _I),
+    "ss_attention_ring": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _I, _I, _I, _P, _P, _SZ, _P], _I),
+    "ss_cache_append_ring": ([_P, _P, _I, _I, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _I, _I, _I, _P,
                               ctypes.POINTER(_I64), ctypes.POINTER(_I), _P], _I),
-    "ss_cache_ring_refresh": ([_P, _P, _I, _I, _I, _I, _P], _I),
+    "ss_cache_ring_refresh": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
     "ss_ipc_handle": ([_P, _P, ctypes.POINTER(_SZ)], _I),
     "ss_ipc_open": ([_P, _SZ, ctypes.POINTER(_P)], _I),
     "ss_ipc_close": ([_P, _SZ], _I),

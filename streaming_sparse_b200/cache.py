@@ -100,7 +100,10 @@ class KVCache:
             S = self.sink_tokens
             if S >= capacity:
                 raise ValueError("the sink must leave room for the ring")
-            self.ring = Ring(S, capacity - S + 64, 0)
+            # the head on the host (host checks, the window's order) and in device memory (what the
+            # kernels follow, so that captured CUDA graphs see later rolls)
+            self._ring_head_dev = torch.zeros(1, dtype=torch.int32, device=device)
+            self.ring = Ring(S, capacity - S + 64, 0, self._ring_head_dev)
             rows = self.ring.phys_rows()
         self.k = torch.zeros((1, rows, num_heads, head_dim), device=device, dtype=dtype)
         self.v = torch.zeros_like(self.k)
@@ -146,13 +149,15 @@ class KVCache:
                                         local_attn=self.local_attn_size != -1, sink_tokens=self.sink_tokens,
                                         max_attention_size=self.max_attention_size)
         end = current_start + n
-        rolls, _, local_end = self.write_plan(n, current_start)
+        rolls, evicted, local_end = self.write_plan(n, current_start)
         if local_end - n < 0 or local_end > self.capacity:
             raise ValueError(f"chunk rows [{local_end - n}, {local_end}) fall outside the {self.capacity}-slot cache")
         self.local_end, self.global_end = local_end, end
         self.commits += 1
         if rolls:
             self.epoch += 1
+            if self.ring_mode:   # the device head moves in the append's own kernels
+                self.ring = self.ring.with_head((self.ring.head + evicted) % self.ring.cap)
         return vis
 
     def window_start(self, local_end: int | None = None) -> int:
@@ -181,14 +186,14 @@ class KVCache:
     def append(self, k_new: torch.Tensor, v_new: torch.Tensor, current_start: int):
         """Write a chunk (post-RoPE K, V: [n,H,D] or [1,n,H,D]); returns (visible positions, history)."""
         n = k_new.shape[-3]
-        old_global, old_local = self.global_end, self.local_end
+        old_global, old_local, old_ring = self.global_end, self.local_end, self.ring
         vis = self.advance(n, current_start)
         if self.ring_mode:
             new_end, head = cache_append_ring(self.k, self.v, k_new, v_new, cap=self.capacity,
                                               local_attn=self.local_attn_size != -1, global_end=old_global,
                                               local_end=old_local, current_start=current_start,
-                                              sink_tokens=self.sink_tokens, ring=self.ring)
-            self.ring = Ring(self.ring.sink, self.ring.cap, head)
+                                              sink_tokens=self.sink_tokens, ring=old_ring)
+            assert head == self.ring.head
         else:
             new_end = cache_append(self.k, self.v, k_new, v_new, local_attn=self.local_attn_size != -1,
                                    global_end=old_global, local_end=old_local, current_start=current_start,
@@ -212,7 +217,8 @@ class KVCache:
         """Device copy of the K/V rows in use and the index state (see ``restore``)."""
         n = self.k.shape[1] if self.ring_mode else self.local_end
         return {"k": self.k[0, :n].clone(), "v": self.v[0, :n].clone(), "global_end": self.global_end,
-                "local_end": self.local_end, "commits": self.commits, "ring": self.ring,
+                "local_end": self.local_end, "commits": self.commits,
+                "ring": self.ring.head if self.ring_mode else None,
                 "positions": None if self.positions is None else self.positions.flat.copy()}
 
     def restore(self, snap: dict) -> None:
@@ -225,7 +231,8 @@ class KVCache:
         self.k[0, :n].copy_(snap["k"])
         self.v[0, :n].copy_(snap["v"])
         if self.ring_mode:
-            self.ring = snap["ring"]
+            self.ring = self.ring.with_head(snap["ring"])
+            self._ring_head_dev.fill_(snap["ring"])
         self.global_end, self.local_end, self.commits = snap["global_end"], le, snap["commits"]
         self.epoch += 1
         if self.positions is not None and snap["positions"] is not None:
@@ -256,7 +263,8 @@ class KVCache:
         """Empty the cache (index state only; rows are overwritten by the next writes)."""
         self.global_end = self.local_end = 0
         if self.ring_mode:
-            self.ring = Ring(self.ring.sink, self.ring.cap, 0)
+            self.ring = self.ring.with_head(0)
+            self._ring_head_dev.zero_()
         self.epoch += 1
         if self.positions is not None:
             self.positions.flat[:] = -1

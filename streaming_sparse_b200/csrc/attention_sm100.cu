@@ -445,6 +445,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             if (lane == 0) *nt_slot = nout;
         }
         __syncthreads();
+        const KvRing ring = p.ring.resolved();
         for (int job = warp; job < 3 * ntc; job += NTHREADS / 32) {
             const int lt = job / 3, grp = job % 3;
             const uint32_t *A = bm + (2 * lt) * p.nwords, *B = A + p.nwords;
@@ -457,15 +458,15 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             const int n = na + nb + nboth;
             uint32_t *base = sub + tinfo[4 * lt + 3];
             if (grp == 0) {
-                compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & B[w]; }, maskof,
+                compact(p.nwords, p.block, p.Lk, ring, lane, [&](int w) { return A[w] & B[w]; }, maskof,
                         [&](int k, uint32_t e) { base[k < nb2 ? k : n - 1] = e; });
                 const int padded = max(4, (n + 3) & ~3);
                 for (int k = n + lane; k < padded; k += 32) base[k] = entry(0u, 0u, 0u);
             } else if (grp == 1) {
-                compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
+                compact(p.nwords, p.block, p.Lk, ring, lane, [&](int w) { return A[w] & ~B[w]; }, maskof,
                         [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k : mp + k)] = e; });
             } else {
-                compact(p.nwords, p.block, p.Lk, p.ring, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
+                compact(p.nwords, p.block, p.Lk, ring, lane, [&](int w) { return B[w] & ~A[w]; }, maskof,
                         [&](int k, uint32_t e) { base[nb2 + (k < mp ? 2 * k + 1 : mp + k)] = e; });
             }
         }
@@ -1088,12 +1089,13 @@ extern "C" int ss_attention_ws(const void *q, const void *k, const void *v, cons
 
 extern "C" int ss_attention_ring(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq,
                                  int Lk, int block, int n_ids, float scale, void *out, int out_dtype, float *lse,
-                                 int *status, int ring_sink, int ring_cap, int ring_head, void *workspace,
-                                 size_t workspace_bytes, void *stream) {
+                                 int *status, int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
+                                 void *workspace, size_t workspace_bytes, void *stream) {
     ss::KvRing ring;
     ring.S = ring_sink;
     ring.C = ring_cap;
     ring.head = ring_head;
+    ring.head_dev = ring_head_dev;
     if (ring_cap <= 0) return SS_ERR_SHAPE;
     return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status, workspace,
                                 workspace_bytes, static_cast<cudaStream_t>(stream), ring);

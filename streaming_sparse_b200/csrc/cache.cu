@@ -190,6 +190,48 @@ static int ring_refresh_tail(__nv_bfloat16 *kc, __nv_bfloat16 *vc, int H, int S,
                       ((int64_t)head - a + C) % C, a, st);
 }
 
+// The same writes with the ring's head in device memory (so that a captured CUDA graph places rows
+// by the head at replay time): n rows (K and V, source rows src_stride_vec uint4 apart) go to ring
+// rows (off + i + head') mod C, and once more to S + C + that row when it is below 64, where
+// head' = (*head_dev + evicted) mod C is the head after this call's roll (evicted = 0 without one).
+__global__ void __launch_bounds__(256) ring_rows_kernel(const uint4 *__restrict__ sk, const uint4 *__restrict__ sv,
+                                                        int64_t src_stride_vec, uint4 *__restrict__ dk,
+                                                        uint4 *__restrict__ dv, int S, int C, int64_t off, int n,
+                                                        int row_vec, const int *head_dev, int evicted) {
+    const int head = (int)(((int64_t)*head_dev + evicted) % C);
+    const int64_t total = (int64_t)n * row_vec;
+    for (int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; x < total; x += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = x / row_vec, c = x % row_vec;
+        const int64_t pos = ((off + i + head) % C + C) % C;
+        const uint4 a = __ldcs(sk + i * src_stride_vec + c), b = __ldcs(sv + i * src_stride_vec + c);
+        dk[(S + pos) * row_vec + c] = a;
+        dv[(S + pos) * row_vec + c] = b;
+        if (pos < 64) {
+            dk[(S + C + pos) * row_vec + c] = a;
+            dv[(S + C + pos) * row_vec + c] = b;
+        }
+    }
+}
+
+__global__ void ring_head_advance_kernel(int *head_dev, int evicted, int C) {
+    *head_dev = (int)(((int64_t)*head_dev + evicted) % C);
+}
+
+static int ring_rows_launch(const __nv_bfloat16 *sk, const __nv_bfloat16 *sv, int64_t src_stride, __nv_bfloat16 *kc,
+                            __nv_bfloat16 *vc, int H, int S, int C, int64_t off, int n, const int *head_dev,
+                            int evicted, cudaStream_t st) {
+    if (n <= 0) return 0;
+    const int row_vec = H * D / 8;
+    CopyGeometry geo;
+    int rc = copy_geometry(&geo);
+    if (rc) return rc;
+    const int64_t total = (int64_t)n * row_vec;
+    const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, (int64_t)geo.sms * 8);
+    ring_rows_kernel<<<blocks, 256, 0, st>>>((const uint4 *)sk, (const uint4 *)sv, src_stride / 8, (uint4 *)kc,
+                                            (uint4 *)vc, S, C, off, n, row_vec, head_dev, evicted);
+    return (int)cudaGetLastError();
+}
+
 }  // namespace cache
 }  // namespace ss
 
@@ -264,8 +306,8 @@ extern "C" int ss_cache_append(void *k_cache, void *v_cache, int cap, int H, con
 extern "C" int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H, const void *k_new,
                                     const void *v_new, int64_t new_stride, int n_new, int local_attn,
                                     int64_t global_end, int64_t local_end, int64_t current_start, int sink_tokens,
-                                    int ring_cap, int ring_head, int64_t *out_local_end, int *out_ring_head,
-                                    void *stream) {
+                                    int ring_cap, int ring_head, int *ring_head_dev, int64_t *out_local_end,
+                                    int *out_ring_head, void *stream) {
     using namespace ss;
     if (!k_cache || !v_cache || !k_new || !v_new || !out_local_end || !out_ring_head) return SS_ERR_POINTER;
     if (cap <= 0 || H <= 0 || n_new <= 0 || n_new > cap || sink_tokens < 0 || sink_tokens > cap || global_end < 0 ||
@@ -282,12 +324,14 @@ extern "C" int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H
     const int64_t current_end = current_start + n_new;
     int64_t new_local_end;
     int head = ring_head;
+    int evicted_rows = 0;
     if (local_attn && current_end > global_end && n_new + local_end > cap) {
         // the roll: the window's rows after the sink move down by `evicted`, which in the ring is
         // only its head moving on by that many rows
         const int64_t evicted = n_new + local_end - cap;
         if (local_end - evicted - S < 0) return SS_ERR_SHAPE;   // cache too small for the sink and the chunk
         head = (int)(((int64_t)head + evicted) % C);
+        evicted_rows = (int)evicted;
         new_local_end = local_end + current_end - global_end - evicted;
     } else {
         new_local_end = local_end + current_end - global_end;
@@ -301,25 +345,49 @@ extern "C" int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H
     int rc = 0;
     if (ns > 0) rc = cache::launch_copy(kn, vn, new_stride, kc + start * row, vc + start * row, row, ns, H, st);
     if (rc) return rc;
-    if (n_new > ns) {
-        const int64_t t0 = start + ns;   // first window row of the chunk at or after S
-        rc = cache::ring_write(kn + ns * new_stride, vn + ns * new_stride, new_stride, kc, vc, H, S, C,
-                               (t0 - S + head) % C, n_new - ns, st);
+    const int64_t t0 = start + ns;   // first window row of the chunk at or after S
+    if (ring_head_dev) {
+        // the head in device memory: rows placed by kernels that read it, then the head moved on
+        if (n_new > ns) {
+            rc = cache::ring_rows_launch(kn + ns * new_stride, vn + ns * new_stride, new_stride, kc, vc, H, S, C,
+                                         t0 - S, (int)(n_new - ns), ring_head_dev, evicted_rows, st);
+            if (rc) return rc;
+        }
+        const int a = S % 64;   // the sink's copy before the new head, after the chunk (it may hold sink rows)
+        rc = cache::ring_rows_launch(kc + (int64_t)(S - a) * row, vc + (int64_t)(S - a) * row, row, kc, vc, H, S, C,
+                                     -a, a, ring_head_dev, evicted_rows, st);
+        if (rc) return rc;
+        if (evicted_rows) {
+            cache::ring_head_advance_kernel<<<1, 1, 0, st>>>(ring_head_dev, evicted_rows, C);
+            if ((rc = (int)cudaGetLastError())) return rc;
+        }
+    } else {
+        if (n_new > ns) {
+            rc = cache::ring_write(kn + ns * new_stride, vn + ns * new_stride, new_stride, kc, vc, H, S, C,
+                                   (t0 - S + head) % C, n_new - ns, st);
+            if (rc) return rc;
+        }
+        rc = cache::ring_refresh_tail(kc, vc, H, S, C, head, st);   // after the chunk: it may hold the sink's rows
         if (rc) return rc;
     }
-    rc = cache::ring_refresh_tail(kc, vc, H, S, C, head, st);   // after the chunk: it may hold the sink's rows
-    if (rc) return rc;
     *out_local_end = new_local_end;
     *out_ring_head = head;
     return 0;
 }
 
 extern "C" int ss_cache_ring_refresh(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap, int ring_head,
-                                     void *stream) {
+                                     const int *ring_head_dev, void *stream) {
     using namespace ss;
     if (!k_cache || !v_cache) return SS_ERR_POINTER;
     if (H <= 0 || sink_tokens < 0 || ring_cap < 64 || ring_head < 0 || ring_head >= ring_cap) return SS_ERR_SHAPE;
     if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) return SS_ERR_POINTER;
-    return cache::ring_refresh_tail(static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), H,
-                                    sink_tokens, ring_cap, ring_head, static_cast<cudaStream_t>(stream));
+    __nv_bfloat16 *kc = static_cast<__nv_bfloat16 *>(k_cache), *vc = static_cast<__nv_bfloat16 *>(v_cache);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (ring_head_dev) {
+        const int a = sink_tokens % 64;
+        const int64_t row = (int64_t)H * cache::D;
+        return cache::ring_rows_launch(kc + (int64_t)(sink_tokens - a) * row, vc + (int64_t)(sink_tokens - a) * row,
+                                       row, kc, vc, H, sink_tokens, ring_cap, -a, a, ring_head_dev, 0, st);
+    }
+    return cache::ring_refresh_tail(kc, vc, H, sink_tokens, ring_cap, ring_head, st);
 }

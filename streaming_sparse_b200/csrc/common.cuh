@@ -255,6 +255,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // C = 0 means a plain contiguous window (physical row = window row).
 struct KvRing {
     int S = 0, C = 0, head = 0;
+    const int *head_dev = nullptr;   // when set, the head is read from device memory (graph replays)
+    // this ring with the head from device memory when it lives there
+    __device__ __forceinline__ KvRing resolved() const {
+        KvRing r = *this;
+        if (head_dev) r.head = *head_dev;
+        return r;
+    }
     // physical row of the first row of the 64-row sub-block starting at window row t0 (t0 % 64 == 0)
     __host__ __device__ __forceinline__ int sub_row(int t0) const {
         if (C == 0 || t0 + 64 <= S) return t0;

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(PP_MAX_WARPS * 32, 1)
 pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k, int H, int Lq,
                     int Lk, int block, int R, int tiles_q, int bg, const float *__restrict__ wq,
                     const float *__restrict__ wk, float *__restrict__ qh, float *__restrict__ kh, int kh_ld,
-                    int kj0, int kj1, int krow0, KvRing ring, int *status) {
+                    int kj0, int kj1, int krow0, KvRing ring_arg, int *status) {
     extern __shared__ uint8_t smr_raw[];
     uint8_t *smr = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smr_raw) + 1023) & ~uintptr_t(1023));
     const int nw = blockDim.x / 32;
@@ -104,6 +104,7 @@ pool_project_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     float4 *md = smean + w * D;
     const CUtensorMap *tm = isq ? &tm_q : &tm_k;
     const int row0 = isq ? 0 : krow0;   // window row of the tensor map's first row
+    const KvRing ring = ring_arg.resolved();
     if (tid == 0) {
         *abort_flag = 0;
         for (int i = 0; i <= nw; ++i) mbar_init(smem_u32(mb + i), 1);
@@ -1198,12 +1199,13 @@ extern "C" int ss_router_fast(const void *q, const void *k, int k_row0, const fl
 
 extern "C" int ss_router_pool_keys_ring(const void *k, const float *wk, int H, int Lk, int R, int block, int j0,
                                         int j1, float *kh, int kh_rows, int ring_sink, int ring_cap, int ring_head,
-                                        int *status, void *stream) {
+                                        const int *ring_head_dev, int *status, void *stream) {
     using namespace ss;
     KvRing ring;
     ring.S = ring_sink;
     ring.C = ring_cap;
     ring.head = ring_head;
+    ring.head_dev = ring_head_dev;
     if (ring_cap <= 0 || ring_check(ring, Lk)) return SS_ERR_SHAPE;
     if (!k || !wk || !kh) return SS_ERR_POINTER;
     if (H <= 0 || H > 65535 || Lk <= 0 || R <= 0 || R > router::MAX_R || (R % 16) || (block != 64 && block != 128))
@@ -1224,12 +1226,13 @@ extern "C" int ss_router_pool_keys_ring(const void *k, const float *wk, int H, i
 extern "C" int ss_router_ring(const void *q, const void *k, const float *wq, const float *wk, int H, int Lq, int Lk,
                               int R, int block, int sink_tokens, int extra, float *kh, int kh_rows, int n_cached,
                               int32_t *ids, int n_ids, uint8_t *mask, float *scores, int *rescored, int fast,
-                              int ring_sink, int ring_cap, int ring_head, void *workspace, size_t workspace_bytes,
-                              int *status, void *stream) {
+                              int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev, void *workspace,
+                              size_t workspace_bytes, int *status, void *stream) {
     ss::KvRing ring;
     ring.S = ring_sink;
     ring.C = ring_cap;
     ring.head = ring_head;
+    ring.head_dev = ring_head_dev;
     if (ring_cap <= 0 || ss::ring_check(ring, Lk)) return SS_ERR_SHAPE;
     int rc = ss::router_check(q, k, wq, wk, H, Lq, Lk, R, block, sink_tokens, extra, ids, n_ids);
     if (rc) return rc;

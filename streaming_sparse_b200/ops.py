@@ -207,7 +207,7 @@ def route(q, k, wq, wk, *, block: int = 64, extra: int, sink_tokens: int = 0, re
                                   _p(keys.kh) if keys is not None else None,
                                   keys.kh.shape[1] if keys is not None else 0, int(n_cached), _p(ids), n_ids,
                                   _p(mask), _p(scores), _p(rescored), int(bool(fast)), ring.sink, ring.cap, ring.head,
-                                  _p(scratch), nbytes, _p(status), _stream(q.device))
+                                  ring.dev_ptr(), _p(scratch), nbytes, _p(status), _stream(q.device))
         check(rc, "ss_router_ring")
     elif fast:
         _require(R in (32, 64), "the fast router needs R = 32 or 64")
@@ -297,7 +297,8 @@ def pool_keys(k, wk, keys: RouterKeys, *, j0: int = 0, j1: int | None = None, ri
                                        st, _stream(k.device))
     else:
         rc = lib().ss_router_pool_keys_ring(_p(k), _p(wk), H, Lk, keys.R, keys.block, j0, j1, _p(keys.kh),
-                                            keys.kh.shape[1], ring.sink, ring.cap, ring.head, st, _stream(k.device))
+                                            keys.kh.shape[1], ring.sink, ring.cap, ring.head, ring.dev_ptr(), st,
+                                            _stream(k.device))
     check(rc, "ss_router_pool_keys")
 
 
@@ -364,8 +365,8 @@ def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = Non
         ws = _ws(workspace, q.device).tensor("attention_split", (max(nws, 256),), q.device, torch.uint8)
         rc = lib().ss_attention_ring(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, _p(out),
                                      1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
-                                     _p(status), ring.sink, ring.cap, ring.head, _p(ws) if nws else None, nws,
-                                     _stream(q.device))
+                                     _p(status), ring.sink, ring.cap, ring.head, ring.dev_ptr(),
+                                     _p(ws) if nws else None, nws, _stream(q.device))
         check(rc, "ss_attention_ring")
     elif nws:
         ws = _ws(workspace, q.device).tensor("attention_split", (nws,), q.device, torch.uint8)
@@ -451,10 +452,20 @@ def cache_append(k_cache, v_cache, k_new, v_new, *, local_attn: bool, global_end
 
 class Ring(tuple):
     """Geometry of a ring-buffer KV cache: (sink rows S, ring rows C, head). Window row t >= S lives
-    at physical row S + ((t - S + head) mod C); see ``ss_router_ring`` in include/ssparse.h."""
+    at physical row S + ((t - S + head) mod C); see ``ss_router_ring`` in include/ssparse.h.
+    ``head_dev`` (optional int32 [1] device tensor) holds the same head in device memory: the
+    kernels then read it at run time, so calls captured in a CUDA graph follow later rolls."""
 
-    def __new__(cls, sink: int, cap: int, head: int):
-        return super().__new__(cls, (int(sink), int(cap), int(head)))
+    def __new__(cls, sink: int, cap: int, head: int, head_dev: torch.Tensor | None = None):
+        r = super().__new__(cls, (int(sink), int(cap), int(head)))
+        r.head_dev = head_dev
+        return r
+
+    def with_head(self, head: int) -> "Ring":
+        return Ring(self[0], self[1], head, self.head_dev)
+
+    def dev_ptr(self):
+        return None if self.head_dev is None else self.head_dev.data_ptr()
 
     @property
     def sink(self) -> int:
@@ -490,7 +501,7 @@ def cache_append_ring(k_cache, v_cache, k_new, v_new, *, cap: int, local_attn: b
     new_end, new_head = ctypes.c_int64(), ctypes.c_int()
     rc = lib().ss_cache_append_ring(_p(kc), _p(vc), int(cap), H, _p(kn), _p(vn), kn.stride(0), kn.shape[0],
                                     int(bool(local_attn)), int(global_end), int(local_end), int(current_start),
-                                    int(sink_tokens), ring.cap, ring.head, ctypes.byref(new_end),
+                                    int(sink_tokens), ring.cap, ring.head, ring.dev_ptr(), ctypes.byref(new_end),
                                     ctypes.byref(new_head), _stream(kc.device))
     check(rc, "ss_cache_append_ring")
     return new_end.value, new_head.value
@@ -500,7 +511,8 @@ def ring_refresh(k_cache, v_cache, ring: Ring) -> None:
     """Rewrite a ring cache's copy of the sink's last S mod 64 rows (``ss_cache_ring_refresh``)."""
     kc = k_cache[0] if k_cache.dim() == 4 else k_cache
     vc = v_cache[0] if v_cache.dim() == 4 else v_cache
-    rc = lib().ss_cache_ring_refresh(_p(kc), _p(vc), kc.shape[1], ring.sink, ring.cap, ring.head, _stream(kc.device))
+    rc = lib().ss_cache_ring_refresh(_p(kc), _p(vc), kc.shape[1], ring.sink, ring.cap, ring.head, ring.dev_ptr(),
+                                     _stream(kc.device))
     check(rc, "ss_cache_ring_refresh")
 
 
@@ -614,6 +626,7 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None
 __all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "RouterKeys", "pool_keys",
            "history_blocks", "sparse_attention", "exact",
            "attention_max_ids", "attention_workspace_bytes", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
+           "Ring", "cache_append_ring", "ring_refresh",
            "rope_shift", "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
 
 # keep the status-bit names importable from here

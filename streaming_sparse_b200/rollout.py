@@ -68,6 +68,7 @@ class WanConfig:
     cache_frames: int = 21        # KV cache capacity in frames
     local_attn_frames: int = -1   # rolling window in frames (-1: global cache, no eviction)
     sink_frames: int = 0          # frames kept at the front when the window rolls
+    ring_cache: bool = False      # KV caches as ring buffers (a roll moves a head, not the window)
 
     @property
     def frame_tokens(self) -> int:
@@ -416,7 +417,7 @@ class Rollout:
         cfg = self.cfg
         self.caches = [KVCache(cfg.cache_frames * cfg.frame_tokens, cfg.num_heads, HEAD_DIM,
                                frame_tokens=cfg.frame_tokens, local_attn_size=cfg.local_attn_frames,
-                               sink_size=cfg.sink_frames, device=dev, track_positions=False)
+                               sink_size=cfg.sink_frames, device=dev, track_positions=False, ring=cfg.ring_cache)
                        for _ in range(cfg.num_layers)]
         self.device = dev
         self._rope = {}

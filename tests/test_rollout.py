@@ -224,3 +224,38 @@ def test_rollout_with_a_short_last_chunk():
     assert torch.isfinite(eager).all() and ro.caches[0].local_end == 7 * 64
     assert (replayed - eager).abs().max() < 1e-2
     ro.release_graphs()
+
+
+@pytest.mark.gpu
+def test_ring_cache_rollout_equals_shifting_cache():
+    """The rolling-window rollout with ring-buffer caches (heads in device memory, so replayed
+    graphs follow every roll) gives the shifting caches' latents bit for bit, eager and replayed.
+    48-token frames: the sink frame ends inside a 64-row sub-block, so its copy before the head is
+    exercised too."""
+    import dataclasses
+
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+
+    dev = torch.device("cuda:0")
+    base = R.WanConfig(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_dim=64, text_len=16, latent_h=16,
+                       latent_w=12, frames=15, cache_frames=7, local_attn_frames=7, sink_frames=1)
+    g = torch.Generator(device=dev)
+    noise = torch.randn(base.frames, 16, 16, 12, device=dev, generator=g.manual_seed(3))
+    text = torch.randn(10, base.text_dim, device=dev, generator=g.manual_seed(4))
+    runs = {}
+    for ring in (False, True):
+        cfg = dataclasses.replace(base, ring_cache=ring)
+        m = R.build_model(cfg, device=dev)
+        wq, wk = init_router_weights(cfg.num_heads, device=dev)
+        sp = SparseAttention(wq, wk, RouterConfig(density=0.5, sink_tokens=cfg.frame_tokens))
+        ro = R.Rollout(m, sparse=sp, graphs=True)
+        eager = ro.run(noise, text, generator=g.manual_seed(5))
+        ro.run(noise, text, generator=g.manual_seed(5))                 # captures
+        replayed = ro.run(noise, text, generator=g.manual_seed(5))
+        runs[ring] = (eager, replayed)
+        if ring:
+            c = ro.caches[0]
+            assert c.ring.head != 0 and int(c.ring.head_dev.item()) == c.ring.head
+        ro.release_graphs()
+    assert torch.equal(runs[True][0], runs[False][0])
+    assert torch.equal(runs[True][1], runs[False][1])
