@@ -351,6 +351,12 @@ int ss_cache_append_ring(void *k_cache, void *v_cache, int cap, int H,
 int ss_cache_ring_refresh(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap, int ring_head,
                           const int *ring_head_dev, void *stream);
 
+/* After a ring write placed by the device head (ss_qkv_norm_rope_ring): when the write rolled
+ * (evicted > 0) or wrote sink rows (refresh != 0), the sink's last sink_tokens mod 64 rows are
+ * repeated before the head after the roll; then the head moves on by evicted. */
+int ss_cache_ring_commit(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap,
+                         int *ring_head_dev, int evicted, int refresh, void *stream);
+
 /* Rotate the first `pairs` complex pairs (elements 2p, 2p+1) of every head of rows [0, n) of a
  * key tensor [n][H][128] bf16 by phase[p] = (cos, sin) (float64 [pairs][2], device memory):
  * float64 products and sums, then double -> float -> bf16. src rows at stride src_ld elements,
@@ -373,6 +379,16 @@ int ss_qkv_norm_rope(const void *qkv, int64_t qkv_ld, int n, int H, const void *
                      const void *norm_k, float eps, const float *cos_t, const float *sin_t,
                      void *q_out, int64_t q_ld, void *k_out, void *v_out, int64_t kv_ld,
                      void *stream);
+
+/* ss_qkv_norm_rope writing k and v into a ring-buffer cache (see ss_router_ring): row r goes to
+ * the physical row of window row t0 + r with the head (*ring_head_dev + evicted) mod C, the head
+ * after this write's roll, and once more among the mirrored rows when its ring row is below 64.
+ * Follow it with ss_cache_ring_commit (same evicted). */
+int ss_qkv_norm_rope_ring(const void *qkv, int64_t qkv_ld, int n, int H, const void *norm_q,
+                          const void *norm_k, float eps, const float *cos_t, const float *sin_t,
+                          void *q_out, int64_t q_ld, void *k_cache, void *v_cache, int64_t kv_ld,
+                          int ring_sink, int ring_cap, int64_t t0, const int *ring_head_dev, int evicted,
+                          void *stream);
 
 /* LayerNorm of the n rows of x [n][d] bf16 (no affine, fp32 statistics, rounded to bf16), then
  * EITHER modulation with the row's frame f = row / frame_tokens:

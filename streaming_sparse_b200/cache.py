@@ -201,6 +201,24 @@ class KVCache:
         assert new_end == self.local_end
         return vis
 
+    def write_qkv(self, qkv, norm_q, norm_k, eps: float, cos, sin, q_out, current_start: int):
+        """A ring cache's counterpart of ``reserve`` + the fused projection: q/k RMSNorm + RoPE from
+        ``qkv`` with k and v written straight into the ring rows of this write, placed by the
+        device head (so a captured CUDA graph stays right after later rolls), then the sink's copy
+        and the head updated when the write rolled; advances the index state like ``append``."""
+        from .ops import qkv_norm_rope_ring, ring_commit
+        if not self.ring_mode:
+            raise RuntimeError("write_qkv is for ring caches; use reserve() on a shifting cache")
+        n = q_out.shape[0]
+        rolls, evicted, local_end = self.write_plan(n, current_start)
+        start = local_end - n
+        old_ring = self.ring
+        self.advance(n, current_start)
+        ev = evicted if rolls else 0
+        qkv_norm_rope_ring(qkv, norm_q, norm_k, eps, cos, sin, q_out, self.k, self.v, ring=old_ring, t0=start,
+                           evicted=ev)
+        ring_commit(self.k, self.v, old_ring, evicted=ev, refresh=start < self.sink_tokens)
+
     def reserve(self, n: int, current_start: int):
         """Claim the rows a chunk of n tokens occupies, for a producer that writes them itself.
 

@@ -391,3 +391,26 @@ extern "C" int ss_cache_ring_refresh(void *k_cache, void *v_cache, int H, int si
     }
     return cache::ring_refresh_tail(kc, vc, H, sink_tokens, ring_cap, ring_head, st);
 }
+
+extern "C" int ss_cache_ring_commit(void *k_cache, void *v_cache, int H, int sink_tokens, int ring_cap,
+                                    int *ring_head_dev, int evicted, int refresh, void *stream) {
+    using namespace ss;
+    if (!k_cache || !v_cache || !ring_head_dev) return SS_ERR_POINTER;
+    if (H <= 0 || sink_tokens < 0 || ring_cap < 64 || evicted < 0) return SS_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u) return SS_ERR_POINTER;
+    __nv_bfloat16 *kc = static_cast<__nv_bfloat16 *>(k_cache), *vc = static_cast<__nv_bfloat16 *>(v_cache);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = 0;
+    if (refresh || evicted) {   // the sink's copy before the head after this write
+        const int a = sink_tokens % 64;
+        const int64_t row = (int64_t)H * cache::D;
+        rc = cache::ring_rows_launch(kc + (int64_t)(sink_tokens - a) * row, vc + (int64_t)(sink_tokens - a) * row, row,
+                                     kc, vc, H, sink_tokens, ring_cap, -a, a, ring_head_dev, evicted, st);
+        if (rc) return rc;
+    }
+    if (evicted) {
+        cache::ring_head_advance_kernel<<<1, 1, 0, st>>>(ring_head_dev, evicted, ring_cap);
+        rc = (int)cudaGetLastError();
+    }
+    return rc;
+}

@@ -73,13 +73,24 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float2 *red) {
     return s;
 }
 
+// Where row r of the k/v output goes: row r (C = 0), or in a ring-buffer cache the physical row
+// of window row t0 + r (the sink's rows in place, the rest at S + ((t - S + head) mod C) with
+// head = (*head_dev + evicted) mod C, the head after this write's roll), written once more at
+// S + C + that ring row when it is below 64 (the ring's mirrored rows).
+struct RingRows {
+    int S = 0, C = 0;
+    int64_t t0 = 0;
+    const int *head_dev = nullptr;
+    int evicted = 0;
+};
+
 // One CTA per token row of width d = H * 128: q = rope(bf16(bf16(q * rq) * wq)), same for k,
-// v copied; q to q_out, k and v to k_out / v_out (cache rows).
+// v copied; q to q_out, k and v to k_out / v_out (cache rows, placed by rr).
 __global__ void __launch_bounds__(1024) qkv_norm_rope_kernel(
     const __nv_bfloat16 *__restrict__ qkv, int64_t ld, int d, const __nv_bfloat16 *__restrict__ wq,
     const __nv_bfloat16 *__restrict__ wk, float eps, const float *__restrict__ cos_t,
     const float *__restrict__ sin_t, __nv_bfloat16 *__restrict__ q_out, int64_t q_ld,
-    __nv_bfloat16 *__restrict__ k_out, __nv_bfloat16 *__restrict__ v_out, int64_t kv_ld) {
+    __nv_bfloat16 *__restrict__ k_out, __nv_bfloat16 *__restrict__ v_out, int64_t kv_ld, RingRows rr) {
     __shared__ float2 red[32];
     const int64_t row = blockIdx.x;
     const int t = threadIdx.x;
@@ -123,8 +134,25 @@ __global__ void __launch_bounds__(1024) qkv_norm_rope_kernel(
         ko[2 * j + 1] = __fadd_rn(__fmul_rn(k[2 * j], sn), __fmul_rn(k[2 * j + 1], c));
     }
     *reinterpret_cast<uint4 *>(q_out + row * q_ld + t * VEC) = pack8(qo);
-    *reinterpret_cast<uint4 *>(k_out + row * kv_ld + t * VEC) = pack8(ko);
-    *reinterpret_cast<uint4 *>(v_out + row * kv_ld + t * VEC) = vv;
+    int64_t krow = row, mrow = -1;
+    if (rr.C) {
+        const int64_t tw = rr.t0 + row;
+        if (tw < rr.S) {
+            krow = tw;
+        } else {
+            const int64_t head = ((int64_t)*rr.head_dev + rr.evicted) % rr.C;
+            const int64_t pos = ((tw - rr.S + head) % rr.C + rr.C) % rr.C;
+            krow = rr.S + pos;
+            if (pos < 64) mrow = (int64_t)rr.S + rr.C + pos;
+        }
+    }
+    const uint4 kk = pack8(ko);
+    *reinterpret_cast<uint4 *>(k_out + krow * kv_ld + t * VEC) = kk;
+    *reinterpret_cast<uint4 *>(v_out + krow * kv_ld + t * VEC) = vv;
+    if (mrow >= 0) {
+        *reinterpret_cast<uint4 *>(k_out + mrow * kv_ld + t * VEC) = kk;
+        *reinterpret_cast<uint4 *>(v_out + mrow * kv_ld + t * VEC) = vv;
+    }
 }
 
 // One CTA per token row of width d. LayerNorm (two passes over the registers: mean, then the
@@ -328,7 +356,38 @@ extern "C" int ss_qkv_norm_rope(const void *qkv, int64_t qkv_ld, int n, int H, c
     dit::qkv_norm_rope_kernel<<<n, dit::row_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16 *>(qkv), qkv_ld, d, static_cast<const __nv_bfloat16 *>(norm_q),
         static_cast<const __nv_bfloat16 *>(norm_k), eps, cos_t, sin_t, static_cast<__nv_bfloat16 *>(q_out), q_ld,
-        static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(v_out), kv_ld);
+        static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(v_out), kv_ld, dit::RingRows());
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ss_qkv_norm_rope_ring(const void *qkv, int64_t qkv_ld, int n, int H, const void *norm_q,
+                                     const void *norm_k, float eps, const float *cos_t, const float *sin_t,
+                                     void *q_out, int64_t q_ld, void *k_cache, void *v_cache, int64_t kv_ld,
+                                     int ring_sink, int ring_cap, int64_t t0, const int *ring_head_dev, int evicted,
+                                     void *stream) {
+    using namespace ss;
+    if (!qkv || !norm_q || !norm_k || !cos_t || !sin_t || !q_out || !k_cache || !v_cache || !ring_head_dev)
+        return SS_ERR_POINTER;
+    const int d = H * dit::HD;
+    if (n < 0 || H <= 0 || d / dit::VEC > 1024 || qkv_ld < 3 * (int64_t)d || q_ld < d || kv_ld < d ||
+        (qkv_ld % dit::VEC) || (q_ld % dit::VEC) || (kv_ld % dit::VEC))
+        return SS_ERR_SHAPE;
+    if (ring_sink < 0 || ring_cap < 64 || t0 < 0 || evicted < 0 || t0 + n > (int64_t)ring_sink + ring_cap)
+        return SS_ERR_SHAPE;
+    if (dit::misaligned(qkv) || dit::misaligned(norm_q) || dit::misaligned(norm_k) || dit::misaligned(q_out) ||
+        dit::misaligned(k_cache) || dit::misaligned(v_cache) || dit::misaligned(cos_t) || dit::misaligned(sin_t))
+        return SS_ERR_POINTER;
+    if (n == 0) return 0;
+    dit::RingRows rr;
+    rr.S = ring_sink;
+    rr.C = ring_cap;
+    rr.t0 = t0;
+    rr.head_dev = ring_head_dev;
+    rr.evicted = evicted;
+    dit::qkv_norm_rope_kernel<<<n, dit::row_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16 *>(qkv), qkv_ld, d, static_cast<const __nv_bfloat16 *>(norm_q),
+        static_cast<const __nv_bfloat16 *>(norm_k), eps, cos_t, sin_t, static_cast<__nv_bfloat16 *>(q_out), q_ld,
+        static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), kv_ld, rr);
     return (int)cudaGetLastError();
 }
 

@@ -570,6 +570,41 @@ def qkv_norm_rope(qkv: torch.Tensor, norm_q: torch.Tensor, norm_k: torch.Tensor,
     return q_out
 
 
+def qkv_norm_rope_ring(qkv: torch.Tensor, norm_q: torch.Tensor, norm_k: torch.Tensor, eps: float, cos: torch.Tensor,
+                       sin: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                       ring: Ring, t0: int, evicted: int) -> torch.Tensor:
+    """``qkv_norm_rope`` with k and v written into a ring-buffer cache [S + C + 64, H, 128] at the
+    rows of window rows t0 .. t0 + n - 1, placed by the device head moved on by ``evicted``
+    (``ss_qkv_norm_rope_ring``; ``ring.head_dev`` required). Follow it with ``ring_commit``."""
+    n, H = q_out.shape[0], q_out.shape[1]
+    d = H * HEAD_DIM
+    kc = k_cache[0] if k_cache.dim() == 4 else k_cache
+    vc = v_cache[0] if v_cache.dim() == 4 else v_cache
+    _require(ring.head_dev is not None, "the ring's head must live in device memory")
+    _require(qkv.dtype == torch.bfloat16 and qkv.dim() == 2 and qkv.shape[0] == n, "qkv: bf16 [n, 3d]")
+    ld = _rows(qkv, "qkv", 3 * d)
+    _require(q_out.dtype == torch.bfloat16 and q_out.shape == (n, H, HEAD_DIM) and q_out.stride(2) == 1 and
+             q_out.stride(1) == HEAD_DIM, "q_out: bf16 [n, H, 128] rows")
+    _require(kc.is_contiguous() and vc.is_contiguous() and kc.shape == vc.shape and kc.shape[0] == ring.phys_rows()
+             and kc.shape[1] == H, "caches must be contiguous ring caches of the ring's geometry")
+    rc = lib().ss_qkv_norm_rope_ring(_p(qkv), ld, n, H, _p(norm_q), _p(norm_k), float(eps), _p(cos), _p(sin),
+                                     _p(q_out), q_out.stride(0), _p(kc), _p(vc), kc.stride(0), ring.sink, ring.cap,
+                                     int(t0), ring.dev_ptr(), int(evicted), _stream(qkv.device))
+    check(rc, "ss_qkv_norm_rope_ring")
+    return q_out
+
+
+def ring_commit(k_cache, v_cache, ring: Ring, *, evicted: int, refresh: bool) -> None:
+    """After ``qkv_norm_rope_ring``: the sink's copy before the new head (when the write rolled or
+    wrote sink rows), then the device head moved on by ``evicted`` (``ss_cache_ring_commit``)."""
+    kc = k_cache[0] if k_cache.dim() == 4 else k_cache
+    vc = v_cache[0] if v_cache.dim() == 4 else v_cache
+    _require(ring.head_dev is not None, "the ring's head must live in device memory")
+    rc = lib().ss_cache_ring_commit(_p(kc), _p(vc), kc.shape[1], ring.sink, ring.cap, ring.dev_ptr(), int(evicted),
+                                    int(bool(refresh)), _stream(kc.device))
+    check(rc, "ss_cache_ring_commit")
+
+
 def adaln(x: torch.Tensor, *, eps: float, shift: torch.Tensor | None = None, scale: torch.Tensor | None = None,
           frame_tokens: int = 0, weight: torch.Tensor | None = None, bias: torch.Tensor | None = None,
           out: torch.Tensor | None = None) -> torch.Tensor:
@@ -626,7 +661,7 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None
 __all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "RouterKeys", "pool_keys",
            "history_blocks", "sparse_attention", "exact",
            "attention_max_ids", "attention_workspace_bytes", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
-           "Ring", "cache_append_ring", "ring_refresh",
+           "Ring", "cache_append_ring", "ring_refresh", "qkv_norm_rope_ring", "ring_commit",
            "rope_shift", "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]
 
 # keep the status-bit names importable from here

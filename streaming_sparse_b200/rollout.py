@@ -226,6 +226,8 @@ class Block(nn.Module):
         rows = cache.reserve(n, current_start)
         if rows is not None:
             ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, rows[0], rows[1])
+        elif cache.ring_mode:   # straight into the ring rows, placed by the head in device memory
+            cache.write_qkv(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, current_start)
         else:   # the write rolls the window: stage k/v, then the cache kernel rolls and writes
             k = torch.empty_like(q)
             v = torch.empty_like(q)
