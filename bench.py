@@ -1114,7 +1114,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "merge_share": r(sharded["kv"]["merge_share"], 3), "ids_equal": sharded["kv"]["ids_equal"],
                    "max_abs": r(sharded["kv"]["max_abs"], 5), "nmse": sharded["kv"]["nmse"]},
             "heads": {"us": r(sharded["heads"]["us"]), "x": r(sharded["heads"]["speedup_vs_1gpu"], 2),
-                      "bit_exact": sharded["heads"]["bit_exact"]}},
+                      "bit_exact": sharded["heads"]["bit_exact"], "max_abs": r(sharded["heads"]["max_abs"], 5),
+                      "nmse": sharded["heads"]["nmse"]}},
     }
     print(json.dumps(line), flush=True)
 
