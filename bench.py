@@ -51,7 +51,7 @@ def peaks():
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention launch at config 2,
 # from the ncu capture summarised in profiles/attention_sm100_config2.md (same command given there).
-ATTN_TRAFFIC_BYTES = 295373056
+ATTN_TRAFFIC_BYTES = 297295104
 ATTN_TRAFFIC_SOURCE = "ncu --set full capture of one config-2 attention launch (profiles/attention_sm100_config2.md)"
 
 
