@@ -650,6 +650,8 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
       (flag barrier + one merge kernel).
     * ``heads``: head sharding, each rank routing and attending over its heads, then one NCCL
       all_gather of the outputs.
+    * ``heads_fused``: the same heads, the gather fused into the attention: the kernel's epilogue
+      stores every output row into all ranks' buffers over NVLink, then a flag barrier.
     Each is checked once against the single-GPU output (router ids bit for bit for ``kv``; max-abs,
     mean-abs and NMSE of the output), then timed as CUDA-graph replays (two calls per graph),
     max over ranks. ``merge_share``: the part of a KV-sharded call that a graph without the
@@ -742,6 +744,21 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
     heads["us"] = graph_us(lambda: (hs(hq, hk, hv), hs(hq, hk, hv)))
     heads["speedup_vs_1gpu"] = single / heads["us"]
     res["heads"] = heads
+
+    # ---- heads, the gather fused into the attention (epilogue stores to every rank's buffer)
+    hf = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg),
+                              H, Lq=lq, device=dev)
+    fout = hf(hq, hk, hv).clone()
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    fused = dict(err(fout), equals_all_gather=bool(torch.equal(fout, hout)))
+    fused["us"] = graph_us(lambda: (hf(hq, hk, hv), hf(hq, hk, hv)))
+    fused["speedup_vs_1gpu"] = single / fused["us"]
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    dist.barrier()
+    hf.close()
+    res["heads_fused"] = fused
     del shard, hs
     torch.cuda.empty_cache()
     return res
@@ -1115,7 +1132,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "max_abs": r(sharded["kv"]["max_abs"], 5), "nmse": sharded["kv"]["nmse"]},
             "heads": {"us": r(sharded["heads"]["us"]), "x": r(sharded["heads"]["speedup_vs_1gpu"], 2),
                       "bit_exact": sharded["heads"]["bit_exact"], "max_abs": r(sharded["heads"]["max_abs"], 5),
-                      "nmse": sharded["heads"]["nmse"]}},
+                      "nmse": sharded["heads"]["nmse"]},
+            "heads_fused": {"us": r(sharded["heads_fused"]["us"]), "x": r(sharded["heads_fused"]["speedup_vs_1gpu"], 2),
+                            "equals_all_gather": sharded["heads_fused"]["equals_all_gather"],
+                            "max_abs": r(sharded["heads_fused"]["max_abs"], 5)}},
     }
     print(json.dumps(line), flush=True)
 

@@ -314,6 +314,24 @@ int ss_lse_merge_peers(const void *const *o_parts, const float *const *lse_parts
                        int H, int Lq, int row0, int row1, void *out, int out_dtype, float *lse_out,
                        void *stream);
 
+/* Head sharding: ss_attention_ws over this rank's H heads (global heads h0 .. h0 + H - 1 of
+ * out_heads) whose output rows go straight into all P ranks' [Lq][out_heads][128] buffers
+ * (outs[p], this rank's own and the others' opened with ss_ipc_open; out_dtype 0 = bf16, 1 =
+ * fp32; 32-byte aligned): row t of local head h is stored at element ((t * out_heads) + h0 + h) *
+ * 128 of every outs[p], by the attention kernel's epilogue (and the split merge), so the
+ * all-gather of the heads' outputs travels over NVLink inside the attention instead of after it.
+ * lse (optional) is this rank's [H][Lq]. After a ss_peer_barrier on every rank, each rank's buffer
+ * holds every head's rows. 1 <= P <= SS_MAX_PEERS, 0 <= h0, h0 + H <= out_heads. ring_cap > 0:
+ * k, v are a ring cache of this rank's heads (as ss_attention_ring); ring_cap = 0: the window's
+ * rows in order (the other ring arguments ignored). Replaces, per
+ * rank, the reference's attention(q, k, v) call of the patched model
+ * (self_forcing_adapter.py:109) on a head slice plus an all-gather of the slices. */
+int ss_attention_heads(const void *q, const void *k, const void *v, const int32_t *ids,
+                       int H, int Lq, int Lk, int block, int n_ids, float scale,
+                       void *const *outs, int P, int out_heads, int h0, int out_dtype, float *lse,
+                       int *status, int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
+                       void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------------------------ */
 /* KV cache append / evict.                                                                    */
 /* ------------------------------------------------------------------------------------------ */

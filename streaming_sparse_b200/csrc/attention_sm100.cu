@@ -120,10 +120,19 @@ struct Ring {
     }
 };
 
+// Where the output rows go: row r of head h (this call's head numbering) is stored at element
+// ((r * heads) + h0 + h) * D of every p[d], d < n. A plain call: n = 1 and heads = H, h0 = 0 (the
+// caller's [Lq, H, D] buffer). Head sharding: p[] are every rank's [Lq, heads, D] buffers (this
+// rank's and the peers' mapped with CUDA IPC), so the epilogue's stores are the all-gather.
+struct OutRows {
+    void *p[SS_MAX_PEERS];
+    int n, heads, h0;
+};
+
 struct Params {
     const __nv_bfloat16 *q;
     const int32_t *ids;
-    void *out;
+    OutRows out;
     float *lse;
     int *status;
     int H, Lq, Lk, block, n_ids, qb, kb, ntiles, nwords, T, G, tmax, step_cap, out_fp32;
@@ -306,6 +315,8 @@ __device__ __forceinline__ bool mma_issuer(uint32_t tmem, uint32_t sRing, uint32
     return ok;
 }
 
+// NDST: the most output buffers a row is stored to (1, or SS_MAX_PEERS for head sharding).
+template <int NDST>
 __global__ void __launch_bounds__(NTHREADS, 1)
 sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const Params p) {
@@ -705,18 +716,38 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                     p.ws_lse[(size_t)tl.slot * 128 + r] =
                         L > 0.f ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
             } else if (live) {
+                const size_t off = ((size_t)row * p.out.heads + p.out.h0 + h) * D + 64 * wg;
                 if (p.out_fp32) {
-                    float *dst = reinterpret_cast<float *>(p.out) + ((size_t)row * p.H + h) * D + 64 * wg;
 #pragma unroll
-                    for (int x = 0; x < 8; ++x) st_v8(dst + 8 * x, reinterpret_cast<const uint32_t *>(res + 8 * x));
-                } else {
-                    __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out) + ((size_t)row * p.H + h) * D + 64 * wg;
+                    for (int d = 0; d < NDST; ++d) {
+                        if (NDST == 1 || d < p.out.n) {
+                            float *dst = reinterpret_cast<float *>(p.out.p[d]) + off;
+#pragma unroll
+                            for (int x = 0; x < 8; ++x)
+                                st_v8(dst + 8 * x, reinterpret_cast<const uint32_t *>(res + 8 * x));
+                        }
+                    }
+                } else if (NDST == 1) {
+                    __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out.p[0]) + off;
 #pragma unroll
                     for (int x = 0; x < 4; ++x) {
                         uint32_t w[8];
 #pragma unroll
                         for (int y = 0; y < 8; ++y) w[y] = pack_bf16x2(res[16 * x + 2 * y], res[16 * x + 2 * y + 1]);
                         st_v8(dst + 16 * x, w);
+                    }
+                } else {
+                    // packed once, then stored to this rank's buffer and over NVLink to the peers'
+                    uint32_t w[32];
+#pragma unroll
+                    for (int y = 0; y < 32; ++y) w[y] = pack_bf16x2(res[2 * y], res[2 * y + 1]);
+#pragma unroll
+                    for (int d = 0; d < NDST; ++d) {
+                        if (d < p.out.n) {
+                            __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out.p[d]) + off;
+#pragma unroll
+                            for (int x = 0; x < 4; ++x) st_v8(dst + 16 * x, w + 8 * x);
+                        }
                     }
                 }
                 if (p.lse && wg == 0)
@@ -839,7 +870,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
 constexpr int MERGE_MAXP = MAXSPLIT_PIECES;
 __global__ void __launch_bounds__(256) split_merge_kernel(const float *__restrict__ ws_o,
                                                           const float *__restrict__ ws_lse, int T, int G, int ntiles,
-                                                          int H, int Lq, void *out, int out_fp32, float *lse) {
+                                                          int H, int Lq, OutRows out, int out_fp32, float *lse) {
     const int t = blockIdx.x;
     const int ca = (int)(((long)t * G) / T), cb = (int)(((long)(t + 1) * G - 1) / T);
     if (ca == cb) return;                       // the whole tile is one CTA's: already written
@@ -877,13 +908,17 @@ __global__ void __launch_bounds__(256) split_merge_kernel(const float *__restric
         }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    const size_t base = ((size_t)row * H + h) * D + quad * 4;
-    if (out_fp32) {
-        reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + base)[0] =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    } else {
-        reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out) + base)[0] =
-            make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+    const size_t base = ((size_t)row * out.heads + out.h0 + h) * D + quad * 4;
+#pragma unroll
+    for (int d = 0; d < SS_MAX_PEERS; ++d) {
+        if (d >= out.n) break;
+        if (out_fp32) {
+            reinterpret_cast<float4 *>(reinterpret_cast<float *>(out.p[d]) + base)[0] =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        } else {
+            reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(out.p[d]) + base)[0] =
+                make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+        }
     }
     if (lse && quad == 0) lse[(size_t)h * Lq + row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
 }
@@ -923,8 +958,11 @@ int attention_prepare(int device) {
     if (rc) return rc;
     std::lock_guard<std::mutex> lock(g_attn_mutex);
     if (g_attn_configured[device] && g_attn_ctx[device] == ctx) return 0;
-    cudaError_t e = cudaFuncSetAttribute(attn::sparse_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)attn::SMEM_LIMIT);
+    cudaError_t e = cudaFuncSetAttribute(attn::sparse_attention_kernel<1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn::SMEM_LIMIT);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaFuncSetAttribute(attn::sparse_attention_kernel<SS_MAX_PEERS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn::SMEM_LIMIT);
     if (e != cudaSuccess) return (int)e;
     int nsm = 0;
     e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
@@ -974,14 +1012,33 @@ int ring_check(const KvRing &r, int Lk) {
 
 static int attention_launch(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq, int Lk,
                             int block, int n_ids, float scale, void *out, int out_dtype, float *lse, int *status,
-                            void *ws, size_t ws_bytes, cudaStream_t stream, KvRing ring = KvRing()) {
-    if (!q || !k || !v || !ids || !out) return SS_ERR_POINTER;
+                            void *ws, size_t ws_bytes, cudaStream_t stream, KvRing ring = KvRing(),
+                            const attn::OutRows *dst = nullptr) {
+    if (!q || !k || !v || !ids || (!out && !dst)) return SS_ERR_POINTER;
     if (H <= 0 || Lq <= 0 || Lk <= 0 || n_ids <= 0 || (block != 64 && block != 128)) return SS_ERR_SHAPE;
     if (Lk >= (1 << 20) - 128 || (long)Lq * H * attn::D >= (1L << 31) || (long)Lk * H * attn::D >= (1L << 31))
         return SS_ERR_SHAPE;
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15u)
         return SS_ERR_POINTER;
-    if (reinterpret_cast<uintptr_t>(out) & 31u) return SS_ERR_POINTER;   // 32-byte row stores
+    attn::OutRows rows;
+    if (dst) {
+        rows = *dst;
+        if (rows.n < 1 || rows.n > SS_MAX_PEERS || rows.h0 < 0 || rows.heads < rows.h0 + H) return SS_ERR_SHAPE;
+        if ((long)Lq * rows.heads * attn::D >= (1L << 31)) return SS_ERR_SHAPE;
+    } else {
+        rows.n = 1;
+        rows.p[0] = out;
+        rows.heads = H;
+        rows.h0 = 0;
+    }
+    for (int d = 0; d < SS_MAX_PEERS; ++d) {
+        if (d >= rows.n) {
+            rows.p[d] = nullptr;
+            continue;
+        }
+        if (!rows.p[d]) return SS_ERR_POINTER;
+        if (reinterpret_cast<uintptr_t>(rows.p[d]) & 31u) return SS_ERR_POINTER;   // 32-byte row stores
+    }
     if (out_dtype != 0 && out_dtype != 1) return SS_ERR_SHAPE;
     if (ring_check(ring, Lk)) return SS_ERR_SHAPE;
     if (ws && (reinterpret_cast<uintptr_t>(ws) & 255u)) return SS_ERR_POINTER;
@@ -997,7 +1054,7 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
     attn::Params prm;
     prm.q = static_cast<const __nv_bfloat16 *>(q);
     prm.ids = ids;
-    prm.out = out;
+    prm.out = rows;
     prm.lse = lse;
     prm.status = status;
     prm.H = H;
@@ -1047,14 +1104,18 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
 
     CUtensorMap tk, tv;
     const uint64_t row_bytes = (uint64_t)H * attn::D * 2;
-    const uint64_t rows = (uint64_t)ring.phys_rows(Lk);
-    if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, rows, row_bytes, 64, 64)) return SS_ERR_DRIVER;
-    if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, rows, row_bytes, 64, 64)) return SS_ERR_DRIVER;
+    const uint64_t kv_rows = (uint64_t)ring.phys_rows(Lk);
+    if (encode_tmap_2d_bf16(&tk, k, (uint64_t)H * attn::D, kv_rows, row_bytes, 64, 64)) return SS_ERR_DRIVER;
+    if (encode_tmap_2d_bf16(&tv, v, (uint64_t)H * attn::D, kv_rows, row_bytes, 64, 64)) return SS_ERR_DRIVER;
 
-    attn::sparse_attention_kernel<<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem, stream>>>(tk, tv, prm);
+    if (rows.n == 1)
+        attn::sparse_attention_kernel<1><<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem, stream>>>(tk, tv, prm);
+    else
+        attn::sparse_attention_kernel<SS_MAX_PEERS>
+            <<<dim3((unsigned)G), attn::NTHREADS, (size_t)smem, stream>>>(tk, tv, prm);
     if (prm.split)
         attn::split_merge_kernel<<<dim3((unsigned)prm.T, 16), 256, 0, stream>>>(prm.ws_o, prm.ws_lse, prm.T, G,
-                                                                                 prm.ntiles, H, Lq, out, out_dtype, lse);
+                                                                                 prm.ntiles, H, Lq, rows, out_dtype, lse);
     return (int)cudaGetLastError();
 }
 
@@ -1099,4 +1160,27 @@ extern "C" int ss_attention_ring(const void *q, const void *k, const void *v, co
     if (ring_cap <= 0) return SS_ERR_SHAPE;
     return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status, workspace,
                                 workspace_bytes, static_cast<cudaStream_t>(stream), ring);
+}
+
+extern "C" int ss_attention_heads(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq,
+                                  int Lk, int block, int n_ids, float scale, void *const *outs, int P, int out_heads,
+                                  int h0, int out_dtype, float *lse, int *status, int ring_sink, int ring_cap,
+                                  int ring_head, const int *ring_head_dev, void *workspace, size_t workspace_bytes,
+                                  void *stream) {
+    if (!outs) return SS_ERR_POINTER;
+    if (P < 1 || P > SS_MAX_PEERS) return SS_ERR_SHAPE;
+    ss::KvRing ring;
+    if (ring_cap > 0) {
+        ring.S = ring_sink;
+        ring.C = ring_cap;
+        ring.head = ring_head;
+        ring.head_dev = ring_head_dev;
+    }
+    ss::attn::OutRows rows;
+    rows.n = P;
+    rows.heads = out_heads;
+    rows.h0 = h0;
+    for (int d = 0; d < SS_MAX_PEERS; ++d) rows.p[d] = d < P ? outs[d] : nullptr;
+    return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, nullptr, out_dtype, lse, status,
+                                workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ring, &rows);
 }

@@ -8,8 +8,10 @@ used here for KV-block sharding.
 
 * streams (replicas): every rank runs its own stream; no collective at all.
 * heads: rank r owns a contiguous range of heads. Router and attention are per head, so the
-  call itself needs no exchange; ``gather_heads`` assembles the full [Lq,H,D] output for the
-  o-projection (one all_gather).
+  call itself needs no exchange; the full [Lq,H,D] output for the o-projection is assembled
+  either by ``gather_heads`` (one NCCL all_gather after the attention) or, fused, by the
+  attention kernel itself: its epilogue stores every output row into all ranks' output buffers
+  over NVLink (``ss_attention_heads``), and a flag barrier ends the call.
 * KV blocks (``KVShardedAttention``): rank r stores only the window blocks j with
   ``j % world == r`` (block-cyclic, which spreads the always-kept sink and current-chunk blocks
   evenly), packed into a local window. The history's pooled key projections are computed by
@@ -62,16 +64,73 @@ def gather_heads(local: torch.Tensor, H: int, group=None) -> torch.Tensor:
 
 
 class HeadShardedAttention:
-    """Routed sparse attention over this rank's heads; ``gather`` returns all heads."""
+    """Routed sparse attention over this rank's heads; ``gather`` returns all heads.
 
-    def __init__(self, sparse_local, H: int, group=None):
+    Without ``Lq`` the heads are gathered with one NCCL all_gather after the attention. With
+    ``Lq`` (the chunk length of every call) and ``device``, the gather is fused into the
+    attention: each rank's [2, Lq, H, D] output buffer is mapped by every other rank (CUDA IPC),
+    the attention kernel's epilogue stores each output row of this rank's heads into all ranks'
+    buffers over NVLink (``ss_attention_heads``), and a flag barrier (``ss_peer_barrier``) ends the
+    call. Calls alternate between the two slots; the returned view stays valid until the call
+    after next (pass ``out`` for a copy). No host synchronisation: a call can be captured in a
+    CUDA graph (capture calls in pairs). Every rank makes the same calls in the same order."""
+
+    def __init__(self, sparse_local, H: int, group=None, Lq: int | None = None, device=None):
         self.sparse = sparse_local    # SparseAttention built with this rank's head slice of wq/wk
         self.H = H
         self.group = group
+        self.peer = None
+        if Lq is not None:
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+            if self.world > 8:
+                raise ValueError("the fused head gather takes at most 8 ranks")
+            self.h0, self.h1 = head_range(H, self.rank, self.world)
+            self.Lq = Lq
+            self.device = torch.device(device)
+            self.peer = PeerBuffers({"out": ((2, Lq, H, ops.HEAD_DIM), torch.bfloat16),
+                                     "flags": ((self.world,), torch.int32)}, self.device, group)
+            self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.slot_bytes = Lq * H * ops.HEAD_DIM * 2
+            self.ws = ops.Workspace()
+            self.calls = 0
 
-    def __call__(self, q_local, k_local, v_local, gather: bool = True):
-        out = self.sparse.forward_one(q_local, k_local, v_local)
-        return gather_heads(out, self.H, self.group) if gather else out
+    def __call__(self, q_local, k_local, v_local, gather: bool = True, out: torch.Tensor | None = None):
+        if self.peer is None or not gather:
+            res = self.sparse.forward_one(q_local, k_local, v_local)
+            res = gather_heads(res, self.H, self.group) if gather else res
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
+        Lq, h, _ = q_local.shape
+        assert Lq == self.Lq and h == self.h1 - self.h0, "q_local must be this rank's heads of an Lq-row chunk"
+        sp = self.sparse
+        cache = sp.cache_of(k_local)
+        ring = cache.ring if cache is not None and cache.ring_mode else None
+        Lk = cache.window_rows() if ring is not None else k_local.shape[0]
+        ids = sp._dense_ids(h, Lq, Lk, q_local.device) if sp.dense else sp.route(q_local, k_local, cache)
+        sp.last_ids = ids
+        sp.calls += 1
+        slot = self.calls % 2
+        ops.sparse_attention_heads(q_local, k_local, v_local, ids,
+                                   [p + slot * self.slot_bytes for p in self.peer.ptrs["out"]], out_heads=self.H,
+                                   h0=self.h0, block=sp.config.block, workspace=self.ws, ring=ring,
+                                   Lk=Lk if ring is not None else None)
+        stream = ops._stream(self.device)
+        status = ops.DeviceStatus.word(self.device)
+        check(lib().ss_peer_barrier(_ptr_array(self.peer.ptrs["flags"]), self.rank, self.world, ops._p(self.epoch),
+                                    ops._p(status), stream), "ss_peer_barrier")
+        self.calls += 1
+        res = self.peer.local["out"][slot]
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
 
 # ----------------------------------------------------------------------------------------------

@@ -384,6 +384,45 @@ def sparse_attention(q, k, v, ids, *, block: int = 64, scale: float | None = Non
     return (out, lse) if return_lse else out
 
 
+def sparse_attention_heads(q, k, v, ids, outs, *, out_heads: int, h0: int, block: int = 64,
+                           scale: float | None = None, out_dtype: torch.dtype = torch.bfloat16,
+                           workspace: Workspace | None = None, validate: bool = False, ring: Ring | None = None,
+                           Lk: int | None = None) -> None:
+    """``sparse_attention`` over one rank's heads (global heads h0 .. h0 + H - 1 of ``out_heads``)
+    whose output rows go into every buffer of ``outs``: device addresses (ints) of the ranks'
+    [Lq, out_heads, 128] ``out_dtype`` buffers, this rank's own and the peers' mapped ones
+    (``ss_attention_heads``). The kernel's epilogue stores each row to all of them, so a peer
+    barrier after the call completes the all-gather of the heads. ``ring`` (with ``Lk``): k/v are
+    a ring cache of this rank's heads, as in ``sparse_attention``."""
+    q = _tokens(q, "q")
+    k = _tokens(k, "k")
+    v = _tokens(v, "v")
+    Lq, H, D = q.shape
+    _require((ring is None) == (Lk is None), "Lk goes with ring")
+    if ring is None:
+        Lk = k.shape[0]
+    else:
+        _require(k.shape[0] == ring.phys_rows(), "k/v rows do not match the ring")
+    _require(v.shape == k.shape and k.shape[1] == H, "k/v shape mismatch")
+    _require(ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 3, "ids must be int32 CUDA [H,qb,n]")
+    _require(ids.shape[0] == H and ids.shape[1] == nblocks(Lq, block), f"ids must be [H,{nblocks(Lq, block)},n]")
+    ids = ids.contiguous()
+    _require(out_dtype in (torch.bfloat16, torch.float32), "out_dtype must be bf16 or fp32")
+    _require(1 <= len(outs) <= 8 and 0 <= h0 and h0 + H <= out_heads, "bad output buffers")
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    arr = (ctypes.c_void_p * len(outs))(*outs)
+    nws = attention_workspace_bytes(H, Lq)
+    ws = _ws(workspace, q.device).tensor("attention_split", (max(nws, 256),), q.device, torch.uint8)
+    status = DeviceStatus.word(q.device)
+    rs = (ring.sink, ring.cap, ring.head, ring.dev_ptr()) if ring is not None else (0, 0, 0, None)
+    rc = lib().ss_attention_heads(_p(q), _p(k), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale, arr,
+                                  len(outs), out_heads, h0, 1 if out_dtype == torch.float32 else 0, None, _p(status),
+                                  *rs, _p(ws) if nws else None, nws, _stream(q.device))
+    check(rc, "ss_attention_heads")
+    if validate:
+        DeviceStatus.check(q.device)
+
+
 def exact(q, k, v, ids, workspace: Workspace | None = None):
     """Reference mirror: q/k/v [1,N,H,D] bf16, ids [H, N//64, count] -> (O fp32 [1,N,H,D], lse [H,N])."""
     ws = _ws(workspace, q.device)
@@ -659,7 +698,7 @@ def gate_residual(x: torch.Tensor, y: torch.Tensor, *, gate: torch.Tensor | None
 
 
 __all__ = ["Workspace", "DeviceStatus", "route", "router_workspace_bytes", "RouterKeys", "pool_keys",
-           "history_blocks", "sparse_attention", "exact",
+           "history_blocks", "sparse_attention", "sparse_attention_heads", "exact",
            "attention_max_ids", "attention_workspace_bytes", "lse_merge", "merge", "cache_append", "budget", "forced_count", "nblocks",
            "Ring", "cache_append_ring", "ring_refresh", "qkv_norm_rope_ring", "ring_commit",
            "rope_shift", "qkv_norm_rope", "adaln", "rms_norm", "gate_residual"]

@@ -1,6 +1,8 @@
 """The multi-GPU layouts on real GPUs: NCCL ranks (one process per GPU, spawned), KV-block sharding
 (each rank stores its own blocks, the history keys all-gathered at commit, the partials merged
-over peer memory) and head sharding with the all_gather, each against the single-GPU result.
+over peer memory) and head sharding with the all_gather, each against the single-GPU result; the
+fused head gather (the attention epilogue storing every rank's heads into all ranks' buffers over
+NVLink) against the all_gather, bit for bit, through both output slots and in the split mode.
 Skipped where fewer than two GPUs are visible."""
 import datetime
 import os
@@ -52,10 +54,25 @@ def _worker(rank, world, port, q_out):
         ids = shard.last_ids.cpu().numpy()
         hs = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg),
                                   H)(head_shard(q, rank, world), head_shard(k, rank, world), head_shard(v, rank, world))
+        fused_ok = []
+        # (Lq, Lk): 16 tiles per rank, and 150 (the split mode, one to two tiles per SM)
+        for lq, lk in ((LQ, LK), (9600, 12800)):
+            g = torch.Generator().manual_seed(lq)
+            fq, fk, fv = (torch.randn((n, H, 128), generator=g).bfloat16().to(dev) for n in (lq, lk, lk))
+            sps = [SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg)
+                   for _ in range(2)]
+            args = (head_shard(fq, rank, world), head_shard(fk, rank, world), head_shard(fv, rank, world))
+            want = HeadShardedAttention(sps[0], H)(*args)
+            fused = HeadShardedAttention(sps[1], H, Lq=lq, device=dev)
+            got = [fused(*args).clone() for _ in range(3)]       # both output slots, then the first again
+            torch.cuda.synchronize()
+            fused_ok.append(all(torch.equal(x, want) for x in got))
+            dist.barrier()
+            fused.close()
         torch.cuda.synchronize()
         ops.DeviceStatus.check(dev)
         same = all(torch.equal(outs[0], o_) for o_ in outs[1:])
-        q_out.put((rank, (outs[0].float().cpu().numpy(), ids, same), hs.float().cpu().numpy()))
+        q_out.put((rank, (outs[0].float().cpu().numpy(), ids, same, fused_ok), hs.float().cpu().numpy()))
         dist.barrier()
         shard.close()
         dist.destroy_process_group()
@@ -95,7 +112,8 @@ def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
     sp = SparseAttention(wq, wk, RouterConfig(density=0.25))
     whole = sp(q[None], k[None], v[None])[0].float().cpu().numpy()
     whole_ids = sp.last_ids.cpu().numpy()
-    for rank, ((kv, ids, same), hs) in results.items():
+    for rank, ((kv, ids, same, fused_ok), hs) in results.items():
+        assert fused_ok == [True, True], f"rank {rank}: fused head gather differs from the all_gather"
         np.testing.assert_array_equal(ids, whole_ids)          # the sharded router: same ids, bit for bit
         assert same                                            # repeated calls through both partial slots
         assert_attention_close(kv, whole)                       # KV-block shards merged by LSE
