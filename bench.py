@@ -646,8 +646,13 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
 
     * ``kv``: KV-block sharding. Each rank stores its own blocks, the history keys are pooled by
       their owners and all-gathered at commit (outside the timed region, once per chunk), and a
-      call routes, attends over the rank's blocks and merges all ranks' partials over peer memory
-      (flag barrier + one merge kernel).
+      call routes, attends over the rank's blocks with the epilogue pushing each partial row to
+      the rank that owns it, then every rank's merge kernel (after a flag barrier it makes
+      itself) merges its own rows and stores them into all ranks' outputs, and a second barrier
+      ends the call. ``kv_pull``: the same call with the partials pulled over peer memory by one
+      merge kernel per rank (every row). Both are timed as ``attend`` (route, attention,
+      exchange), as the single-GPU call finds the chunk already in its window; writing the
+      chunk's rows into the shards (``write_chunk``) is reported beside it.
     * ``heads``: head sharding, each rank routing and attending over its heads, then one NCCL
       all_gather of the outputs.
     * ``heads_fused``: the same heads, the gather fused into the attention: the kernel's epilogue
@@ -709,30 +714,39 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
            "single_gpu_us": single}
 
     # ---- KV blocks
-    shard = KVShardedAttention(SparseAttention(wq, wk, cfg), lq, lk, dev)
-    shard.commit(k, v)
     c0 = lk - lq
     kc, vc = k[c0:].clone(), v[c0:].clone()
-    out = shard(q, kc, vc)
-    torch.cuda.synchronize()
-    ops.DeviceStatus.check(dev)
-    kv = dict(err(out), ids_equal=bool(torch.equal(shard.last_ids, whole_ids)))
     ob = torch.empty_like(q)
-    kv["us"] = graph_us(lambda: (shard(q, kc, vc, out=ob), shard(q, kc, vc, out=ob)))
+    lo, ll = torch.empty_like(q), torch.empty((H, lq), dtype=torch.float32, device=dev)
+    for exchange in ("push", "pull"):
+        shard = KVShardedAttention(SparseAttention(wq, wk, cfg), lq, lk, dev, exchange=exchange)
+        shard.commit(k, v)
+        out = shard(q, kc, vc).clone()
+        torch.cuda.synchronize()
+        ops.DeviceStatus.check(dev)
+        kv = dict(err(out), ids_equal=bool(torch.equal(shard.last_ids, whole_ids)))
+        # timed: route + attention + exchange over the window as written (the single-GPU call
+        # likewise finds the chunk in its window); the chunk's write into the shards apart
+        if exchange == "push":
+            kv["us"] = graph_us(lambda: (shard.attend(q), shard.attend(q)))
+            kv["write_chunk_us"] = graph_us(lambda: (shard.write_chunk(kc, vc), shard.write_chunk(kc, vc)))
+            push_out = out
+        else:
+            kv["us"] = graph_us(lambda: (shard.attend(q, out=ob), shard.attend(q, out=ob)))
+            kv["equals_push"] = bool(torch.equal(out, push_out))
 
-    def local_part():
-        ids = shard.route(q)
-        ops.sparse_attention(q, shard.k_local[:shard.Lk_local], shard.v_local[:shard.Lk_local],
-                             local_ids(ids, rank, world), block=block, return_lse=True,
-                             out=shard.peer.local["o"][0], lse=shard.peer.local["lse"][0])
-    kv["local_us"] = graph_us(lambda: (local_part(), local_part()))
-    kv["merge_share"] = max(0.0, 1.0 - kv["local_us"] / kv["us"])
-    kv["speedup_vs_1gpu"] = single / kv["us"]
-    torch.cuda.synchronize()
-    ops.DeviceStatus.check(dev)
-    dist.barrier()
-    shard.close()
-    res["kv"] = kv
+            def local_part():
+                ids = shard.route(q)
+                ops.sparse_attention(q, shard.k_local[:shard.Lk_local], shard.v_local[:shard.Lk_local],
+                                     local_ids(ids, rank, world), block=block, return_lse=True, out=lo, lse=ll)
+            kv["local_us"] = graph_us(lambda: (local_part(), local_part()))
+            kv["merge_share"] = max(0.0, 1.0 - kv["local_us"] / kv["us"])
+        kv["speedup_vs_1gpu"] = single / kv["us"]
+        torch.cuda.synchronize()
+        ops.DeviceStatus.check(dev)
+        dist.barrier()
+        shard.close()
+        res["kv" if exchange == "push" else "kv_pull"] = kv
 
     # ---- heads
     sph = SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg)
@@ -1128,8 +1142,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "sharded": None if sharded is None else {
             "c4_1gpu_us": r(sharded["single_gpu_us"]),
             "kv": {"us": r(sharded["kv"]["us"]), "x": r(sharded["kv"]["speedup_vs_1gpu"], 2),
-                   "merge_share": r(sharded["kv"]["merge_share"], 3), "ids_equal": sharded["kv"]["ids_equal"],
+                   "write_chunk_us": r(sharded["kv"]["write_chunk_us"]), "ids_equal": sharded["kv"]["ids_equal"],
                    "max_abs": r(sharded["kv"]["max_abs"], 5), "nmse": sharded["kv"]["nmse"]},
+            "kv_pull": {"us": r(sharded["kv_pull"]["us"]), "x": r(sharded["kv_pull"]["speedup_vs_1gpu"], 2),
+                        "merge_share": r(sharded["kv_pull"]["merge_share"], 3),
+                        "equals_push": sharded["kv_pull"]["equals_push"]},
             "heads": {"us": r(sharded["heads"]["us"]), "x": r(sharded["heads"]["speedup_vs_1gpu"], 2),
                       "bit_exact": sharded["heads"]["bit_exact"], "max_abs": r(sharded["heads"]["max_abs"], 5),
                       "nmse": sharded["heads"]["nmse"]},

@@ -314,6 +314,33 @@ int ss_lse_merge_peers(const void *const *o_parts, const float *const *lse_parts
                        int H, int Lq, int row0, int row1, void *out, int out_dtype, float *lse_out,
                        void *stream);
 
+/* KV-block sharding with the exchange fused into the kernels. Rank `slot` of P stores the window
+ * blocks j with j % P == slot, packed in order into its k, v (Lk rows: local block j / P); ids
+ * are the window's block ids as the router gives them (every rank the same), and the kernel keeps
+ * this rank's. It attends over them (ss_attention_ws arguments) and its epilogue stores each partial row straight into
+ * the buffers of the rank that owns the row: row t belongs to rank d = t / rows (rows * P >= Lq)
+ * and goes to o_parts[d] [P][rows][H][128] (part_dtype 0 = bf16, 1 = fp32; 32-byte aligned) at
+ * [slot][t - d * rows], its natural-log LSE to lse_parts[d] [P][H][rows] at [slot][h][t - d *
+ * rows] (-inf where the rank saw no token). o_parts / lse_parts: every rank's buffers, this
+ * rank's own and the others' opened with ss_ipc_open. After a ss_peer_barrier, rank d merges its
+ * rows from its own memory with ss_lse_merge_gather. */
+int ss_attention_kv_parts(const void *q, const void *k, const void *v, const int32_t *ids,
+                          int H, int Lq, int Lk, int block, int n_ids, float scale,
+                          void *const *o_parts, float *const *lse_parts, int P, int rows, int slot,
+                          int part_dtype, int *status, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* ss_lse_merge_peers whose merged rows are stored into each of outs[0 .. n_out) (device pointers,
+ * this GPU's or peers', 16-byte aligned; row r of the parts goes to row r of every outs[d]), so a
+ * rank merging the rows it owns also delivers them to every rank. n_out <= SS_MAX_PEERS.
+ * flags (optional, NULL = none): the merge is first preceded by the barrier of ss_peer_barrier
+ * over the P ranks (flags, rank, epoch, status as there), so that the partials the peers pushed
+ * before it are visible: one warp posts the epoch, and the merge's CTAs wait for the peers'
+ * posts before they read. With row0 == row1 only the barrier runs. */
+int ss_lse_merge_gather(const void *const *o_parts, const float *const *lse_parts, int P, int part_dtype,
+                        int H, int Lq, int row0, int row1, void *const *outs, int n_out, int out_dtype,
+                        int *const *flags, int rank, int *epoch, int *status, void *stream);
+
 /* Head sharding: ss_attention_ws over this rank's H heads (global heads h0 .. h0 + H - 1 of
  * out_heads) whose output rows go straight into all P ranks' [Lq][out_heads][128] buffers
  * (outs[p], this rank's own and the others' opened with ss_ipc_open; out_dtype 0 = bf16, 1 =

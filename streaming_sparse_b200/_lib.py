@@ -54,6 +54,8 @@ SIGNATURES = {
     "ss_ipc_close": ([_P, _SZ], _I),
     "ss_peer_barrier": ([_P, _I, _I, _P, _P, _P], _I),
     "ss_lse_merge_peers": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _P, _P], _I),
+    "ss_attention_kv_parts": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _I, _I, _I, _I, _P, _P, _SZ, _P], _I),
+    "ss_lse_merge_gather": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, _I, _I, _P, _I, _P, _P, _P], _I),
     "ss_attention_heads": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P,
                             _SZ, _P], _I),
     "ss_attention": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P], _I),

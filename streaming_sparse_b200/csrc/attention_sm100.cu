@@ -124,9 +124,13 @@ struct Ring {
 // ((r * heads) + h0 + h) * D of every p[d], d < n. A plain call: n = 1 and heads = H, h0 = 0 (the
 // caller's [Lq, H, D] buffer). Head sharding: p[] are every rank's [Lq, heads, D] buffers (this
 // rank's and the peers' mapped with CUDA IPC), so the epilogue's stores are the all-gather.
+// Owner mode (rows > 0, KV-block sharding): row r belongs to rank d = r / rows and goes to p[d]
+// only, a [n][rows][heads][D] partial buffer, at slot `slot` (this rank), local row r - d * rows;
+// its LSE goes to lse[d], [n][heads][rows] -- the epilogue's stores are the reduce-scatter.
 struct OutRows {
     void *p[SS_MAX_PEERS];
-    int n, heads, h0;
+    float *lse[SS_MAX_PEERS];
+    int n, heads, h0, rows, slot;
 };
 
 struct Params {
@@ -144,6 +148,9 @@ struct Params {
     int split;
     float *ws_o, *ws_lse;
     KvRing ring;   // where K/V rows live (C = 0: the window's rows in order)
+    // ids name window blocks of which this rank stores those with id % own_n == own_r, packed in
+    // order (local block id / own_n); own_n = 1: the ids are the k/v blocks themselves
+    int own_n, own_r;
 };
 
 // Pieces of one tile at most in split mode: the grid has at most 8 CTAs per tile, and a tile
@@ -383,7 +390,12 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
             const int t = cand_tile(lt), h = t / p.ntiles, tile = t % p.ntiles;
             const int qblk = pairq ? 2 * tile + half : tile;
             if (qblk >= p.qb) continue;
-            const int a = p.ids[((size_t)h * p.qb + qblk) * p.n_ids + i];
+            int a = p.ids[((size_t)h * p.qb + qblk) * p.n_ids + i];
+            if (p.own_n > 1 && a >= 0) {
+                // KV-block sharding: window block a is stored by rank a % own_n, as local block a / own_n
+                if ((int)((unsigned)a % (unsigned)p.own_n) != p.own_r) continue;
+                a = (int)((unsigned)a / (unsigned)p.own_n);
+            }
             if (a >= p.kb) *badid_flag = 1;
             else if (a >= 0) atomicOr(&bm[(2 * lt + half) * p.nwords + (a >> 5)], 1u << (a & 31));
         }
@@ -716,11 +728,26 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                     p.ws_lse[(size_t)tl.slot * 128 + r] =
                         L > 0.f ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
             } else if (live) {
-                const size_t off = ((size_t)row * p.out.heads + p.out.h0 + h) * D + 64 * wg;
+                size_t off = ((size_t)row * p.out.heads + p.out.h0 + h) * D + 64 * wg;
+                int d_lo = 0, d_hi = NDST;     // destinations [d_lo, d_hi) of those below p.out.n
+                if (NDST > 1 && p.out.rows > 0) {
+                    // owner mode: the row goes to its owner's buffer only, at slot p.out.slot
+                    const int d = row / p.out.rows, rl = row - d * p.out.rows;
+                    off = (((size_t)p.out.slot * p.out.rows + rl) * p.out.heads + p.out.h0 + h) * D + 64 * wg;
+                    d_lo = d;
+                    d_hi = d + 1;
+                    if (wg == 0) {
+                        const float l_row = L > 0.f ? (M + __log2f(L)) * 0.69314718055994530942f : -INFINITY;
+                        const size_t li = ((size_t)p.out.slot * p.out.heads + p.out.h0 + h) * p.out.rows + rl;
+#pragma unroll
+                        for (int i = 0; i < NDST; ++i)
+                            if (i == d) p.out.lse[i][li] = l_row;
+                    }
+                }
                 if (p.out_fp32) {
 #pragma unroll
                     for (int d = 0; d < NDST; ++d) {
-                        if (NDST == 1 || d < p.out.n) {
+                        if (NDST == 1 || (d >= d_lo && d < d_hi && d < p.out.n)) {
                             float *dst = reinterpret_cast<float *>(p.out.p[d]) + off;
 #pragma unroll
                             for (int x = 0; x < 8; ++x)
@@ -743,7 +770,7 @@ sparse_attention_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_c
                     for (int y = 0; y < 32; ++y) w[y] = pack_bf16x2(res[2 * y], res[2 * y + 1]);
 #pragma unroll
                     for (int d = 0; d < NDST; ++d) {
-                        if (d < p.out.n) {
+                        if (d >= d_lo && d < d_hi && d < p.out.n) {
                             __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.out.p[d]) + off;
 #pragma unroll
                             for (int x = 0; x < 4; ++x) st_v8(dst + 16 * x, w + 8 * x);
@@ -908,10 +935,26 @@ __global__ void __launch_bounds__(256) split_merge_kernel(const float *__restric
         }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    const size_t base = ((size_t)row * out.heads + out.h0 + h) * D + quad * 4;
+    size_t base = ((size_t)row * out.heads + out.h0 + h) * D + quad * 4;
+    int d_lo = 0;
+    int d_hi = out.n;
+    if (out.rows > 0) {   // owner mode (see OutRows)
+        const int d = row / out.rows, rl = row - d * out.rows;
+        base = (((size_t)out.slot * out.rows + rl) * out.heads + out.h0 + h) * D + quad * 4;
+        d_lo = d;
+        d_hi = d + 1;
+        if (quad == 0) {
+            const float l_row = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+            const size_t li = ((size_t)out.slot * out.heads + out.h0 + h) * out.rows + rl;
+#pragma unroll
+            for (int i = 0; i < SS_MAX_PEERS; ++i)
+                if (i == d) out.lse[i][li] = l_row;
+        }
+    }
 #pragma unroll
     for (int d = 0; d < SS_MAX_PEERS; ++d) {
-        if (d >= out.n) break;
+        if (d >= d_hi) break;
+        if (d < d_lo) continue;
         if (out_fp32) {
             reinterpret_cast<float4 *>(reinterpret_cast<float *>(out.p[d]) + base)[0] =
                 make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
@@ -1024,20 +1067,31 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
     if (dst) {
         rows = *dst;
         if (rows.n < 1 || rows.n > SS_MAX_PEERS || rows.h0 < 0 || rows.heads < rows.h0 + H) return SS_ERR_SHAPE;
-        if ((long)Lq * rows.heads * attn::D >= (1L << 31)) return SS_ERR_SHAPE;
+        if (rows.rows < 0 || (rows.rows > 0 && ((long)rows.rows * rows.n < Lq || rows.slot < 0 ||
+                                                rows.slot >= rows.n)))
+            return SS_ERR_SHAPE;
+        if ((long)std::max(Lq, rows.n * rows.rows) * rows.heads * attn::D >= (1L << 31)) return SS_ERR_SHAPE;
     } else {
         rows.n = 1;
         rows.p[0] = out;
         rows.heads = H;
         rows.h0 = 0;
+        rows.rows = 0;
+        rows.slot = 0;
     }
     for (int d = 0; d < SS_MAX_PEERS; ++d) {
         if (d >= rows.n) {
             rows.p[d] = nullptr;
+            rows.lse[d] = nullptr;
             continue;
         }
         if (!rows.p[d]) return SS_ERR_POINTER;
         if (reinterpret_cast<uintptr_t>(rows.p[d]) & 31u) return SS_ERR_POINTER;   // 32-byte row stores
+        if (rows.rows > 0) {
+            if (!rows.lse[d] || (reinterpret_cast<uintptr_t>(rows.lse[d]) & 3u)) return SS_ERR_POINTER;
+        } else {
+            rows.lse[d] = nullptr;
+        }
     }
     if (out_dtype != 0 && out_dtype != 1) return SS_ERR_SHAPE;
     if (ring_check(ring, Lk)) return SS_ERR_SHAPE;
@@ -1070,6 +1124,12 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
     prm.split = 0;
     prm.ws_o = prm.ws_lse = nullptr;
     prm.ring = ring;
+    prm.own_n = 1;
+    prm.own_r = 0;
+    if (rows.rows > 0) {   // owner mode: the ids are the window's, this rank stores blocks j % n == slot
+        prm.own_n = rows.n;
+        prm.own_r = rows.slot;
+    }
     const int nsm = g_num_sms[device] > 0 ? g_num_sms[device] : 148;
     const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)prm.kb) : 2L * std::min(n_ids, prm.kb);
     int G;
@@ -1180,7 +1240,32 @@ extern "C" int ss_attention_heads(const void *q, const void *k, const void *v, c
     rows.n = P;
     rows.heads = out_heads;
     rows.h0 = h0;
-    for (int d = 0; d < SS_MAX_PEERS; ++d) rows.p[d] = d < P ? outs[d] : nullptr;
+    rows.rows = 0;
+    rows.slot = 0;
+    for (int d = 0; d < SS_MAX_PEERS; ++d) {
+        rows.p[d] = d < P ? outs[d] : nullptr;
+        rows.lse[d] = nullptr;
+    }
     return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, nullptr, out_dtype, lse, status,
                                 workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ring, &rows);
+}
+
+extern "C" int ss_attention_kv_parts(const void *q, const void *k, const void *v, const int32_t *ids, int H, int Lq,
+                                     int Lk, int block, int n_ids, float scale, void *const *o_parts,
+                                     float *const *lse_parts, int P, int rows, int slot, int part_dtype,
+                                     int *status, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!o_parts || !lse_parts) return SS_ERR_POINTER;
+    if (P < 1 || P > SS_MAX_PEERS || rows <= 0) return SS_ERR_SHAPE;
+    ss::attn::OutRows dst;
+    dst.n = P;
+    dst.heads = H;
+    dst.h0 = 0;
+    dst.rows = rows;
+    dst.slot = slot;
+    for (int d = 0; d < SS_MAX_PEERS; ++d) {
+        dst.p[d] = d < P ? o_parts[d] : nullptr;
+        dst.lse[d] = d < P ? lse_parts[d] : nullptr;
+    }
+    return ss::attention_launch(q, k, v, ids, H, Lq, Lk, block, n_ids, scale, nullptr, part_dtype, nullptr, status,
+                                workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ss::KvRing(), &dst);
 }

@@ -17,9 +17,14 @@ used here for KV-block sharding.
   evenly), packed into a local window. The history's pooled key projections are computed by
   their owners and all-gathered once per commit; every rank then routes with the same exact-fp32
   router (bit-identical ids everywhere), pooling the current chunk itself from the window's tail.
-  Each rank attends over its own selected blocks into buffers the other ranks have mapped (CUDA
-  IPC), and one kernel per rank (``ss_lse_merge_peers``, after the flag barrier
-  ``ss_peer_barrier``) reads all partials over NVLink and writes the merged rows.
+  Exchange "push" (default): rank d owns query rows [d*rows, (d+1)*rows); each rank's attention
+  epilogue stores every partial row (and its LSE) over NVLink into the owner's buffers
+  (``ss_attention_kv_parts``, a reduce-scatter inside the attention); after a flag barrier each
+  rank merges its own rows from its own memory and stores them into every rank's output
+  (``ss_lse_merge_gather``, an all-gather inside the merge); a second barrier ends the call.
+  Exchange "pull": each rank attends into buffers the other ranks have mapped (CUDA IPC), and one
+  kernel per rank (``ss_lse_merge_peers``, after the flag barrier ``ss_peer_barrier``) reads all
+  partials over NVLink and writes the merged rows.
 """
 from __future__ import annotations
 
@@ -250,15 +255,26 @@ class KVShardedAttention:
     migration/unified_router/opt23/pipeline.py:22-29). ``__call__(q, k_chunk, v_chunk)`` is one
     routed chunk-layer call: every rank passes the same chunk (its q/k/v come from the replicated
     activations) and gets the merged bf16 output [Lq, H, D]. A call has no host synchronisation
-    and can be captured in a CUDA graph (capture calls in pairs: they alternate between two
-    partial buffers); every rank makes the same calls in the same order.
+    and can be captured in a CUDA graph (capture calls in pairs: with ``exchange="pull"`` they
+    alternate between two partial buffers); every rank makes the same calls in the same order.
+
+    ``exchange="push"`` needs one buffer set: a rank's attention of call i+1 writes into a peer's
+    partials only after the second barrier of call i, which the peer posts after its merge of
+    call i has read them, and a peer's merge of call i+1 writes this rank's output only after the
+    first barrier of call i+1, which this rank posts after the work it enqueued before the call.
+    The returned output (a view of the mapped buffer) stays valid until the next call; pass
+    ``out`` for a copy.
     """
 
-    def __init__(self, sparse, Lq: int, Lk: int, device, group=None, part_dtype=torch.bfloat16):
+    def __init__(self, sparse, Lq: int, Lk: int, device, group=None, part_dtype=torch.bfloat16,
+                 exchange: str = "push"):
         self.sparse, self.group = sparse, group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         if self.world > 8:
             raise ValueError("the peer merge takes at most 8 ranks")
+        if exchange not in ("push", "pull"):
+            raise ValueError("exchange is 'push' or 'pull'")
+        self.exchange = exchange
         c = sparse.config
         self.block, self.Lq, self.Lk = c.block, Lq, Lk
         self.H = sparse.wq.shape[0]
@@ -281,11 +297,29 @@ class KVShardedAttention:
         self.keys = ops.RouterKeys(self.H, Lk, block=self.block, R=self.R, device=device)
         self.ws = ops.Workspace()
         self.part_fp32 = part_dtype == torch.float32
-        self.peer = PeerBuffers({"o": ((2, Lq, self.H, D), part_dtype), "lse": ((2, self.H, Lq), torch.float32),
-                                 "flags": ((self.world,), torch.int32)}, device, group)
-        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)   # advanced by the barrier kernel
-        self.o_bytes = Lq * self.H * D * (4 if self.part_fp32 else 2)
-        self.lse_bytes = self.H * Lq * 4
+        esz = 4 if self.part_fp32 else 2
+        if exchange == "pull":
+            self.peer = PeerBuffers({"o": ((2, Lq, self.H, D), part_dtype), "lse": ((2, self.H, Lq), torch.float32),
+                                     "flags": ((self.world,), torch.int32)}, device, group)
+            self.o_bytes = Lq * self.H * D * esz
+            self.lse_bytes = self.H * Lq * 4
+        else:
+            # rank d owns output rows [d * rows, (d + 1) * rows): its "o" / "lse" hold every rank's
+            # partial of those rows (slot = the writing rank), its "out" the merged output
+            self.rows_per_rank = -(-Lq // self.world)
+            self.row_lo = min(Lq, self.rank * self.rows_per_rank)
+            self.row_hi = min(Lq, self.row_lo + self.rows_per_rank)
+            self.peer = PeerBuffers({"o": ((self.world, self.rows_per_rank, self.H, D), part_dtype),
+                                     "lse": ((self.world, self.H, self.rows_per_rank), torch.float32),
+                                     "out": ((Lq, self.H, D), torch.bfloat16),
+                                     "flags": ((self.world,), torch.int32)}, device, group)
+            self.peer.local["lse"].fill_(float("-inf"))    # slots of ranks that store no block stay empty
+            torch.cuda.synchronize(device)
+            dist.barrier(group=group)
+            self.o_slot_bytes = self.rows_per_rank * self.H * D * esz
+            self.lse_slot_bytes = self.H * self.rows_per_rank * 4
+            self.out_row_bytes = self.H * D * 2
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)   # advanced by the barrier kernels
         self.calls = 0
         self.device = device
         self.last_ids = None
@@ -318,17 +352,31 @@ class KVShardedAttention:
                          sink_tokens=c.sink_tokens, workspace=self.ws, keys=self.keys, n_cached=self.n_hist,
                          k_row0=self.row0, fast=c.fast)
 
-    def __call__(self, q: torch.Tensor, k_chunk: torch.Tensor, v_chunk: torch.Tensor,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-        Lq, H, D = q.shape
-        assert Lq == self.Lq and k_chunk.shape == q.shape and v_chunk.shape == q.shape
-        # this rank's rows of the chunk into its local window; the whole chunk into the tail
+    def write_chunk(self, k_chunk: torch.Tensor, v_chunk: torch.Tensor) -> None:
+        """The chunk's k/v rows this rank stores into its local window, the whole chunk into the
+        router's tail (the cache write of a denoising call, which a single-GPU cache makes in its
+        append)."""
+        assert k_chunk.shape == (self.Lq, self.H, ops.HEAD_DIM) and v_chunk.shape == k_chunk.shape
         if self.chunk_dst.numel():
             self.k_local.index_copy_(0, self.chunk_dst, k_chunk.index_select(0, self.chunk_src))
             self.v_local.index_copy_(0, self.chunk_dst, v_chunk.index_select(0, self.chunk_src))
-        self.k_tail[self.Lk - Lq - self.row0:].copy_(k_chunk)
+        self.k_tail[self.Lk - self.Lq - self.row0:].copy_(k_chunk)
+
+    def __call__(self, q: torch.Tensor, k_chunk: torch.Tensor, v_chunk: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        """``write_chunk`` then ``attend``."""
+        self.write_chunk(k_chunk, v_chunk)
+        return self.attend(q, out)
+
+    def attend(self, q: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Route and attend the chunk's queries over the window as last written, merged over the
+        ranks."""
+        Lq, H, D = q.shape
+        assert Lq == self.Lq and H == self.H
         ids = self.route(q)                        # identical on every rank (exact-fp32 router)
         self.last_ids = ids
+        if self.exchange == "push":
+            return self._call_push(q, ids, out)
         slot = self.calls % 2
         o_part = self.peer.local["o"][slot]
         lse_part = self.peer.local["lse"][slot]
@@ -353,6 +401,42 @@ class KVShardedAttention:
               "ss_lse_merge_peers")
         self.calls += 1
         return out
+
+    def _call_push(self, q, ids, out):
+        """Attention whose epilogue stores each partial row into its owner's slot for this rank
+        (the reduce-scatter), a barrier, each rank's merge of its own rows from its own memory with
+        the merged rows stored into every rank's output (the all-gather), a barrier."""
+        Lq, H, D = q.shape
+        stream = ops._stream(self.device)
+        status = ops.DeviceStatus.word(self.device)
+        dtype = 1 if self.part_fp32 else 0
+        if self.Lk_local:
+            # the window's ids: the kernel keeps the blocks this rank stores (j % world == rank)
+            nws = ops.attention_workspace_bytes(H, Lq)
+            ws = self.ws.tensor("attention_split", (max(nws, 256),), self.device, torch.uint8)
+            check(lib().ss_attention_kv_parts(ops._p(q), ops._p(self.k_local), ops._p(self.v_local), ops._p(ids), H,
+                                              Lq, self.Lk_local, self.block, ids.shape[2], 1.0 / D ** 0.5,
+                                              _ptr_array(self.peer.ptrs["o"]), _ptr_array(self.peer.ptrs["lse"]),
+                                              self.world, self.rows_per_rank, self.rank, dtype, ops._p(status),
+                                              ops._p(ws) if nws else None, nws, stream), "ss_attention_kv_parts")
+        # the first barrier is made by the merge kernel itself, before it reads the pushed partials
+        flags = _ptr_array(self.peer.ptrs["flags"])
+        o0, l0 = self.peer.ptrs["o"][self.rank], self.peer.ptrs["lse"][self.rank]
+        o_parts = _ptr_array([o0 + p * self.o_slot_bytes for p in range(self.world)])
+        lse_parts = _ptr_array([l0 + p * self.lse_slot_bytes for p in range(self.world)])
+        check(lib().ss_lse_merge_gather(o_parts, lse_parts, self.world, dtype, H, self.rows_per_rank, 0,
+                                        self.row_hi - self.row_lo,
+                                        _ptr_array(self.peer.ptrs["out"], self.row_lo * self.out_row_bytes),
+                                        self.world, 0, flags, self.rank, ops._p(self.epoch), ops._p(status), stream),
+              "ss_lse_merge_gather")
+        check(lib().ss_peer_barrier(flags, self.rank, self.world, ops._p(self.epoch), ops._p(status), stream),
+              "ss_peer_barrier")
+        self.calls += 1
+        res = self.peer.local["out"]
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
 
     def close(self):
         self.peer.close()

@@ -1,6 +1,7 @@
 """The multi-GPU layouts on real GPUs: NCCL ranks (one process per GPU, spawned), KV-block sharding
-(each rank stores its own blocks, the history keys all-gathered at commit, the partials merged
-over peer memory) and head sharding with the all_gather, each against the single-GPU result; the
+(each rank stores its own blocks, the history keys all-gathered at commit, the partials pushed
+to their rows' owners by the attention epilogue and merged there, or pulled and merged over peer
+memory) and head sharding with the all_gather, each against the single-GPU result; the
 fused head gather (the attention epilogue storing every rank's heads into all ranks' buffers over
 NVLink) against the all_gather, bit for bit, through both output slots and in the split mode.
 Skipped where fewer than two GPUs are visible."""
@@ -47,11 +48,19 @@ def _worker(rank, world, port, q_out):
         from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
         q, k, v, wq, wk = (t.to(dev) for t in _inputs())
         cfg = RouterConfig(density=0.25)
-        shard = KVShardedAttention(SparseAttention(wq, wk, cfg), LQ, LK, dev)
-        shard.commit(k, v)
         c0 = LK - LQ
-        outs = [shard(q, k[c0:], v[c0:]) for _ in range(3)]      # both partial slots, then the first again
-        ids = shard.last_ids.cpu().numpy()
+        outs_by = {}
+        for exchange in ("push", "pull"):
+            shard = KVShardedAttention(SparseAttention(wq, wk, cfg), LQ, LK, dev, exchange=exchange)
+            shard.commit(k, v)
+            # three calls: with "pull" both partial slots, then the first again
+            outs_by[exchange] = [shard(q, k[c0:], v[c0:]).clone() for _ in range(3)]
+            ids = shard.last_ids.cpu().numpy()
+            torch.cuda.synchronize()
+            dist.barrier()
+            shard.close()
+        outs = outs_by["push"]
+        push_eq_pull = all(torch.equal(a, b) for a, b in zip(outs_by["push"], outs_by["pull"]))
         hs = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg),
                                   H)(head_shard(q, rank, world), head_shard(k, rank, world), head_shard(v, rank, world))
         fused_ok = []
@@ -72,9 +81,9 @@ def _worker(rank, world, port, q_out):
         torch.cuda.synchronize()
         ops.DeviceStatus.check(dev)
         same = all(torch.equal(outs[0], o_) for o_ in outs[1:])
-        q_out.put((rank, (outs[0].float().cpu().numpy(), ids, same, fused_ok), hs.float().cpu().numpy()))
+        q_out.put((rank, (outs[0].float().cpu().numpy(), ids, same and push_eq_pull, fused_ok),
+                   hs.float().cpu().numpy()))
         dist.barrier()
-        shard.close()
         dist.destroy_process_group()
     except Exception as e:   # report to the parent instead of hanging it
         q_out.put((rank, repr(e), None))
@@ -115,6 +124,6 @@ def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
     for rank, ((kv, ids, same, fused_ok), hs) in results.items():
         assert fused_ok == [True, True], f"rank {rank}: fused head gather differs from the all_gather"
         np.testing.assert_array_equal(ids, whole_ids)          # the sharded router: same ids, bit for bit
-        assert same                                            # repeated calls through both partial slots
+        assert same                                            # repeated calls; push == pull, bit for bit
         assert_attention_close(kv, whole)                       # KV-block shards merged by LSE
         np.testing.assert_array_equal(hs, whole)               # heads are independent: identical bits
