@@ -603,13 +603,18 @@ def rollout_bench(dev, args, world: int):
             "config4_long_horizon": c4}
 
 
-def rollout4_bench(dev, args, ring: bool = False):
+def rollout4_bench(dev, args, ring: bool = False, head_parallel: bool = False):
     """Config 4's stream on one GPU: 120 latent frames in 40 chunks through a rolling window of 21
     frames + 1 sink frame (34320 tokens), 128-token router blocks at 10 % of the unforced blocks;
     the window rolls on every chunk's first call from chunk 7 on. One timed rollout after an eager
     warm-up and a capture run (routed only; the dense model is timed by
     `python -m streaming_sparse_b200.rollout --config4 --dense`). ``ring``: the layers' KV caches
-    as ring buffers (a roll moves the head; heads in device memory under graph replay)."""
+    as ring buffers (a roll moves the head; heads in device memory under graph replay).
+    ``head_parallel`` (under torchrun): the same stream with every layer's attention split by
+    heads over the ranks (each rank's caches hold its heads; the fused head gather returns all
+    heads to every rank; the rest of the model runs on every rank), timed between barriers, max
+    over ranks."""
+    import torch.distributed as dist
     from streaming_sparse_b200 import rollout as R
     from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
 
@@ -620,20 +625,28 @@ def rollout4_bench(dev, args, ring: bool = False):
     text = torch.randn((cfg.text_len, cfg.text_dim), device=dev, generator=g.manual_seed(4))
     wq, wk = init_router_weights(cfg.num_heads, device=dev)
     sp = SparseAttention(wq, wk, RouterConfig(block=128, density=0.10, rule="rest", sink_tokens=cfg.frame_tokens))
-    ro = R.Rollout(model, sparse=sp, graphs=True)
+    ro = R.Rollout(model, sparse=sp, graphs=True, head_parallel=head_parallel)
     for _ in range(2):
         ro.run(noise, text, generator=g.manual_seed(5))
     torch.cuda.synchronize()
+    if head_parallel:
+        dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     out = ro.run(noise, text, generator=g.manual_seed(5))
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
+    if head_parallel:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
     res = {"value": cfg.frames / (ms * 1e-3), "unit": "frames/s", "ms_per_rollout": ms, "frames": cfg.frames,
            "graphs": len(ro._graph), "finite": bool(torch.isfinite(out).all()), "ring_cache": ring,
            "latents": out}
-    ro.release_graphs()
+    ro.close()
+    if head_parallel:
+        dist.barrier()
     del ro, model
     torch.cuda.empty_cache()
     return res
@@ -657,6 +670,10 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
       all_gather of the outputs.
     * ``heads_fused``: the same heads, the gather fused into the attention: the kernel's epilogue
       stores every output row into all ranks' buffers over NVLink, then a flag barrier.
+    * ``stream4_heads`` (unless ``--no-rollout``): config 4's whole stream (120 frames) with every
+      layer's attention split by heads this way, frames/s max over ranks; rank 0 also runs the
+      stream on one GPU for the ratio and the latents' difference (split-mode tiles at 6 heads
+      per rank merge in fp32, so the latents agree to rounding, not bit for bit).
     Each is checked once against the single-GPU output (router ids bit for bit for ``kv``; max-abs,
     mean-abs and NMSE of the output), then timed as CUDA-graph replays (two calls per graph),
     max over ranks. ``merge_share``: the part of a KV-sharded call that a graph without the
@@ -774,6 +791,21 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
     hf.close()
     res["heads_fused"] = fused
     del shard, hs
+    torch.cuda.empty_cache()
+
+    # ---- config 4's stream, every layer's attention split by heads (fused gather)
+    if not args.no_rollout:
+        hp = rollout4_bench(dev, args, ring=True, head_parallel=True)
+        stream = {"frames_s": hp["value"], "ms_per_rollout": hp["ms_per_rollout"], "finite": hp["finite"]}
+        if rank == 0:   # the same stream on one GPU, same box, for the ratio and the latents
+            one = rollout4_bench(dev, args, ring=True)
+            d = (hp["latents"].float() - one["latents"].float()).abs()
+            stream.update(single_frames_s=one["value"], speedup_vs_1gpu=hp["value"] / one["value"],
+                          latents_max_abs=float(d.max()), latents_mean_abs=float(d.mean()))
+            del one
+        del hp
+        dist.barrier()
+        res["stream4_heads"] = stream
     torch.cuda.empty_cache()
     return res
 
@@ -1152,7 +1184,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                       "nmse": sharded["heads"]["nmse"]},
             "heads_fused": {"us": r(sharded["heads_fused"]["us"]), "x": r(sharded["heads_fused"]["speedup_vs_1gpu"], 2),
                             "equals_all_gather": sharded["heads_fused"]["equals_all_gather"],
-                            "max_abs": r(sharded["heads_fused"]["max_abs"], 5)}},
+                            "max_abs": r(sharded["heads_fused"]["max_abs"], 5)},
+            "stream4_heads": sharded.get("stream4_heads") and {
+                k_: (r(v_, 3) if isinstance(v_, float) else v_) for k_, v_ in sharded["stream4_heads"].items()}},
     }
     print(json.dumps(line), flush=True)
 

@@ -435,6 +435,16 @@ int ss_qkv_norm_rope_ring(const void *qkv, int64_t qkv_ld, int n, int H, const v
                           int ring_sink, int ring_cap, int64_t t0, const int *ring_head_dev, int evicted,
                           void *stream);
 
+/* Head sharding: ss_qkv_norm_rope (ring_cap = 0) or ss_qkv_norm_rope_ring (ring_cap > 0) over
+ * the H heads of qkv -- the RMSNorm still over the whole width H*128 -- writing only heads h0 ..
+ * h0 + nh - 1: to q_out [n][nh][128] (row stride q_ld) and to k/v rows of nh heads (row stride
+ * kv_ld), so a rank's cache holds its own heads only. */
+int ss_qkv_norm_rope_heads(const void *qkv, int64_t qkv_ld, int n, int H, const void *norm_q,
+                           const void *norm_k, float eps, const float *cos_t, const float *sin_t, int h0, int nh,
+                           void *q_out, int64_t q_ld, void *k_out, void *v_out, int64_t kv_ld,
+                           int ring_sink, int ring_cap, int64_t t0, const int *ring_head_dev, int evicted,
+                           void *stream);
+
 /* LayerNorm of the n rows of x [n][d] bf16 (no affine, fp32 statistics, rounded to bf16), then
  * EITHER modulation with the row's frame f = row / frame_tokens:
  *     out = bf16(ln * (1 + scale[f*mod_ld + c]) + shift[f*mod_ld + c])   (shift/scale fp32)

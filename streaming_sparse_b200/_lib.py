@@ -48,6 +48,8 @@ SIGNATURES = {
     "ss_cache_ring_refresh": ([_P, _P, _I, _I, _I, _I, _P, _P], _I),
     "ss_qkv_norm_rope_ring": ([_P, _I64, _I, _I, _P, _P, _F, _P, _P, _P, _I64, _P, _P, _I64, _I, _I, _I64, _P, _I,
                                _P], _I),
+    "ss_qkv_norm_rope_heads": ([_P, _I64, _I, _I, _P, _P, _F, _P, _P, _I, _I, _P, _I64, _P, _P, _I64, _I, _I, _I64,
+                                _P, _I, _P], _I),
     "ss_cache_ring_commit": ([_P, _P, _I, _I, _I, _P, _I, _I, _P], _I),
     "ss_ipc_handle": ([_P, _P, ctypes.POINTER(_SZ)], _I),
     "ss_ipc_open": ([_P, _SZ, ctypes.POINTER(_P)], _I),

@@ -88,6 +88,9 @@ class KVCache:
                  local_attn_size: int = -1, sink_size: int = 0, device="cuda", dtype=torch.bfloat16,
                  track_positions: bool = True, ring: bool = False):
         self.capacity, self.H, self.D = capacity, num_heads, head_dim
+        # first model head this cache holds (head-parallel models: a rank's caches hold the heads
+        # head0 .. head0 + H - 1 of the model's)
+        self.head0 = 0
         self.frame_tokens = frame_tokens
         self.local_attn_size, self.sink_size = local_attn_size, sink_size
         self.max_attention_size = 32760 if local_attn_size == -1 else local_attn_size * frame_tokens
@@ -201,11 +204,13 @@ class KVCache:
         assert new_end == self.local_end
         return vis
 
-    def write_qkv(self, qkv, norm_q, norm_k, eps: float, cos, sin, q_out, current_start: int):
+    def write_qkv(self, qkv, norm_q, norm_k, eps: float, cos, sin, q_out, current_start: int,
+                  model_heads: int | None = None):
         """A ring cache's counterpart of ``reserve`` + the fused projection: q/k RMSNorm + RoPE from
         ``qkv`` with k and v written straight into the ring rows of this write, placed by the
         device head (so a captured CUDA graph stays right after later rolls), then the sink's copy
-        and the head updated when the write rolled; advances the index state like ``append``."""
+        and the head updated when the write rolled; advances the index state like ``append``.
+        ``model_heads``: qkv holds that many heads, of which this cache stores head0 .. head0 + H - 1."""
         from .ops import qkv_norm_rope_ring, ring_commit
         if not self.ring_mode:
             raise RuntimeError("write_qkv is for ring caches; use reserve() on a shifting cache")
@@ -216,7 +221,7 @@ class KVCache:
         self.advance(n, current_start)
         ev = evicted if rolls else 0
         qkv_norm_rope_ring(qkv, norm_q, norm_k, eps, cos, sin, q_out, self.k, self.v, ring=old_ring, t0=start,
-                           evicted=ev)
+                           evicted=ev, model_heads=model_heads, h0=self.head0)
         ring_commit(self.k, self.v, old_ring, evicted=ev, refresh=start < self.sink_tokens)
 
     def reserve(self, n: int, current_start: int):

@@ -90,7 +90,8 @@ __global__ void __launch_bounds__(1024) qkv_norm_rope_kernel(
     const __nv_bfloat16 *__restrict__ qkv, int64_t ld, int d, const __nv_bfloat16 *__restrict__ wq,
     const __nv_bfloat16 *__restrict__ wk, float eps, const float *__restrict__ cos_t,
     const float *__restrict__ sin_t, __nv_bfloat16 *__restrict__ q_out, int64_t q_ld,
-    __nv_bfloat16 *__restrict__ k_out, __nv_bfloat16 *__restrict__ v_out, int64_t kv_ld, RingRows rr) {
+    __nv_bfloat16 *__restrict__ k_out, __nv_bfloat16 *__restrict__ v_out, int64_t kv_ld, RingRows rr, int c0,
+    int c1) {
     __shared__ float2 red[32];
     const int64_t row = blockIdx.x;
     const int t = threadIdx.x;
@@ -110,7 +111,10 @@ __global__ void __launch_bounds__(1024) qkv_norm_rope_kernel(
         }
     }
     const float2 s = block_sum2(sq, sk, red);
-    if (!active) return;
+    // the norm is over the whole row; only the columns [c0, c1) (whole heads) are written, at
+    // column t * VEC - c0 of the outputs
+    if (!active || t * VEC < c0 || t * VEC >= c1) return;
+    const int oc = t * VEC - c0;
     const float rq = rsqrtf(__fadd_rn(__fdiv_rn(s.x, (float)d), eps));
     const float rk = rsqrtf(__fadd_rn(__fdiv_rn(s.y, (float)d), eps));
     float w_q[VEC], w_k[VEC];
@@ -133,7 +137,7 @@ __global__ void __launch_bounds__(1024) qkv_norm_rope_kernel(
         ko[2 * j] = __fsub_rn(__fmul_rn(k[2 * j], c), __fmul_rn(k[2 * j + 1], sn));
         ko[2 * j + 1] = __fadd_rn(__fmul_rn(k[2 * j], sn), __fmul_rn(k[2 * j + 1], c));
     }
-    *reinterpret_cast<uint4 *>(q_out + row * q_ld + t * VEC) = pack8(qo);
+    *reinterpret_cast<uint4 *>(q_out + row * q_ld + oc) = pack8(qo);
     int64_t krow = row, mrow = -1;
     if (rr.C) {
         const int64_t tw = rr.t0 + row;
@@ -147,11 +151,11 @@ __global__ void __launch_bounds__(1024) qkv_norm_rope_kernel(
         }
     }
     const uint4 kk = pack8(ko);
-    *reinterpret_cast<uint4 *>(k_out + krow * kv_ld + t * VEC) = kk;
-    *reinterpret_cast<uint4 *>(v_out + krow * kv_ld + t * VEC) = vv;
+    *reinterpret_cast<uint4 *>(k_out + krow * kv_ld + oc) = kk;
+    *reinterpret_cast<uint4 *>(v_out + krow * kv_ld + oc) = vv;
     if (mrow >= 0) {
-        *reinterpret_cast<uint4 *>(k_out + mrow * kv_ld + t * VEC) = kk;
-        *reinterpret_cast<uint4 *>(v_out + mrow * kv_ld + t * VEC) = vv;
+        *reinterpret_cast<uint4 *>(k_out + mrow * kv_ld + oc) = kk;
+        *reinterpret_cast<uint4 *>(v_out + mrow * kv_ld + oc) = vv;
     }
 }
 
@@ -356,7 +360,7 @@ extern "C" int ss_qkv_norm_rope(const void *qkv, int64_t qkv_ld, int n, int H, c
     dit::qkv_norm_rope_kernel<<<n, dit::row_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16 *>(qkv), qkv_ld, d, static_cast<const __nv_bfloat16 *>(norm_q),
         static_cast<const __nv_bfloat16 *>(norm_k), eps, cos_t, sin_t, static_cast<__nv_bfloat16 *>(q_out), q_ld,
-        static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(v_out), kv_ld, dit::RingRows());
+        static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(v_out), kv_ld, dit::RingRows(), 0, d);
     return (int)cudaGetLastError();
 }
 
@@ -387,7 +391,42 @@ extern "C" int ss_qkv_norm_rope_ring(const void *qkv, int64_t qkv_ld, int n, int
     dit::qkv_norm_rope_kernel<<<n, dit::row_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16 *>(qkv), qkv_ld, d, static_cast<const __nv_bfloat16 *>(norm_q),
         static_cast<const __nv_bfloat16 *>(norm_k), eps, cos_t, sin_t, static_cast<__nv_bfloat16 *>(q_out), q_ld,
-        static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), kv_ld, rr);
+        static_cast<__nv_bfloat16 *>(k_cache), static_cast<__nv_bfloat16 *>(v_cache), kv_ld, rr, 0, d);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int ss_qkv_norm_rope_heads(const void *qkv, int64_t qkv_ld, int n, int H, const void *norm_q,
+                                      const void *norm_k, float eps, const float *cos_t, const float *sin_t, int h0,
+                                      int nh, void *q_out, int64_t q_ld, void *k_out, void *v_out, int64_t kv_ld,
+                                      int ring_sink, int ring_cap, int64_t t0, const int *ring_head_dev, int evicted,
+                                      void *stream) {
+    using namespace ss;
+    if (!qkv || !norm_q || !norm_k || !cos_t || !sin_t || !q_out || !k_out || !v_out) return SS_ERR_POINTER;
+    const int d = H * dit::HD;
+    if (n < 0 || H <= 0 || d / dit::VEC > 1024 || h0 < 0 || nh <= 0 || h0 + nh > H || qkv_ld < 3 * (int64_t)d ||
+        q_ld < (int64_t)nh * dit::HD || kv_ld < (int64_t)nh * dit::HD || (qkv_ld % dit::VEC) || (q_ld % dit::VEC) ||
+        (kv_ld % dit::VEC))
+        return SS_ERR_SHAPE;
+    dit::RingRows rr;
+    if (ring_cap > 0) {
+        if (!ring_head_dev) return SS_ERR_POINTER;
+        if (ring_sink < 0 || ring_cap < 64 || t0 < 0 || evicted < 0 || t0 + n > (int64_t)ring_sink + ring_cap)
+            return SS_ERR_SHAPE;
+        rr.S = ring_sink;
+        rr.C = ring_cap;
+        rr.t0 = t0;
+        rr.head_dev = ring_head_dev;
+        rr.evicted = evicted;
+    }
+    if (dit::misaligned(qkv) || dit::misaligned(norm_q) || dit::misaligned(norm_k) || dit::misaligned(q_out) ||
+        dit::misaligned(k_out) || dit::misaligned(v_out) || dit::misaligned(cos_t) || dit::misaligned(sin_t))
+        return SS_ERR_POINTER;
+    if (n == 0) return 0;
+    dit::qkv_norm_rope_kernel<<<n, dit::row_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16 *>(qkv), qkv_ld, d, static_cast<const __nv_bfloat16 *>(norm_q),
+        static_cast<const __nv_bfloat16 *>(norm_k), eps, cos_t, sin_t, static_cast<__nv_bfloat16 *>(q_out), q_ld,
+        static_cast<__nv_bfloat16 *>(k_out), static_cast<__nv_bfloat16 *>(v_out), kv_ld, rr, h0 * dit::HD,
+        (h0 + nh) * dit::HD);
     return (int)cudaGetLastError();
 }
 

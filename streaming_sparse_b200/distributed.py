@@ -80,7 +80,7 @@ class HeadShardedAttention:
     after next (pass ``out`` for a copy). No host synchronisation: a call can be captured in a
     CUDA graph (capture calls in pairs). Every rank makes the same calls in the same order."""
 
-    def __init__(self, sparse_local, H: int, group=None, Lq: int | None = None, device=None):
+    def __init__(self, sparse_local, H: int, group=None, Lq: int | None = None, device=None, slots: int = 2):
         self.sparse = sparse_local    # SparseAttention built with this rank's head slice of wq/wk
         self.H = H
         self.group = group
@@ -90,9 +90,10 @@ class HeadShardedAttention:
             if self.world > 8:
                 raise ValueError("the fused head gather takes at most 8 ranks")
             self.h0, self.h1 = head_range(H, self.rank, self.world)
-            self.Lq = Lq
+            self.Lq = Lq               # the most query rows of a call
+            self.slots = slots
             self.device = torch.device(device)
-            self.peer = PeerBuffers({"out": ((2, Lq, H, ops.HEAD_DIM), torch.bfloat16),
+            self.peer = PeerBuffers({"out": ((slots, Lq, H, ops.HEAD_DIM), torch.bfloat16),
                                      "flags": ((self.world,), torch.int32)}, self.device, group)
             self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
             self.slot_bytes = Lq * H * ops.HEAD_DIM * 2
@@ -108,7 +109,7 @@ class HeadShardedAttention:
                 return out
             return res
         Lq, h, _ = q_local.shape
-        assert Lq == self.Lq and h == self.h1 - self.h0, "q_local must be this rank's heads of an Lq-row chunk"
+        assert Lq <= self.Lq and h == self.h1 - self.h0, "q_local must be this rank's heads of at most Lq rows"
         sp = self.sparse
         cache = sp.cache_of(k_local)
         ring = cache.ring if cache is not None and cache.ring_mode else None
@@ -116,7 +117,7 @@ class HeadShardedAttention:
         ids = sp._dense_ids(h, Lq, Lk, q_local.device) if sp.dense else sp.route(q_local, k_local, cache)
         sp.last_ids = ids
         sp.calls += 1
-        slot = self.calls % 2
+        slot = self.calls % self.slots
         ops.sparse_attention_heads(q_local, k_local, v_local, ids,
                                    [p + slot * self.slot_bytes for p in self.peer.ptrs["out"]], out_heads=self.H,
                                    h0=self.h0, block=sp.config.block, workspace=self.ws, ring=ring,
@@ -126,7 +127,7 @@ class HeadShardedAttention:
         check(lib().ss_peer_barrier(_ptr_array(self.peer.ptrs["flags"]), self.rank, self.world, ops._p(self.epoch),
                                     ops._p(status), stream), "ss_peer_barrier")
         self.calls += 1
-        res = self.peer.local["out"][slot]
+        res = self.peer.local["out"][slot][:Lq]
         if out is not None:
             out.copy_(res)
             return out
@@ -136,6 +137,46 @@ class HeadShardedAttention:
         if self.peer is not None:
             self.peer.close()
             self.peer = None
+
+
+class HeadParallelAttention:
+    """The attention a head-parallel model's plugin calls: every layer hands this rank's heads
+    (q [1, n, h, D] and the layer's cache window of h heads) and gets all heads [1, n, H, D] back
+    through that layer's fused head gather (``HeadShardedAttention``). Built from the full-model
+    ``SparseAttention``: the router weights are sliced to this rank's heads.
+
+    Each layer has one output buffer. Layer l's buffer is written again only in the next model
+    call, after every rank has passed the barriers of the layers in between, and a rank posts
+    each of those after the o-projection that read layer l's output -- so with two or more layers
+    one buffer per layer is enough (one layer takes two, alternating). Attributes not set here
+    (``config``, ``wq``, ``dense``, ``attach`` ...) are the local ``SparseAttention``'s."""
+
+    def __init__(self, sparse_full, caches, Lq: int, device, group=None):
+        from .plugin import SparseAttention
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        H = sparse_full.wq.shape[0]
+        local = SparseAttention(head_shard(sparse_full.wq, rank, world, 0), head_shard(sparse_full.wk, rank, world, 0),
+                                sparse_full.config, validate=sparse_full.validate)
+        object.__setattr__(self, "local", local)
+        slots = 1 if len(caches) >= 2 else 2
+        object.__setattr__(self, "layers", {id(c): HeadShardedAttention(local, H, group, Lq=Lq, device=device,
+                                                                         slots=slots) for c in caches})
+
+    def __getattr__(self, name):
+        return getattr(self.local, name)
+
+    def __setattr__(self, name, value):
+        setattr(self.local, name, value)
+
+    def __call__(self, q, k, v):
+        cache = self.local.cache_of(k[0])
+        if cache is None or id(cache) not in self.layers:
+            raise ValueError("k is not the window of one of this model's caches")
+        return self.layers[id(cache)](q[0], k[0], v[0])[None]
+
+    def close(self):
+        for hs in self.layers.values():
+            hs.close()
 
 
 # ----------------------------------------------------------------------------------------------

@@ -583,14 +583,19 @@ def _rows(t: torch.Tensor, name: str, width: int) -> int:
 
 
 def qkv_norm_rope(qkv: torch.Tensor, norm_q: torch.Tensor, norm_k: torch.Tensor, eps: float, cos: torch.Tensor,
-                  sin: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor) -> torch.Tensor:
+                  sin: torch.Tensor, q_out: torch.Tensor, k_out: torch.Tensor, v_out: torch.Tensor, *,
+                  model_heads: int | None = None, h0: int = 0) -> torch.Tensor:
     """q/k RMSNorm + weight + 3-D RoPE, v copied, from one fused projection (`ss_qkv_norm_rope`).
 
     qkv [n, >=3d] bf16 (q | k | v columns, d = H*128); norm_q/norm_k [d] bf16; cos/sin [n, 64]
     fp32; q_out [n, H, 128] bf16; k_out/v_out [n, H, 128] bf16 with equal row strides (for
-    example the cache rows of the chunk). Returns q_out.
+    example the cache rows of the chunk). Returns q_out. ``model_heads`` (head sharding): qkv holds
+    all ``model_heads`` heads (the norm runs over the whole width) and only heads h0 .. h0 + h - 1
+    are written, h = q_out.shape[1] (``ss_qkv_norm_rope_heads``).
     """
     n, H = q_out.shape[0], q_out.shape[1]
+    if model_heads is not None:
+        return _qkv_heads(qkv, norm_q, norm_k, eps, cos, sin, q_out, k_out, v_out, model_heads, h0)
     d = H * HEAD_DIM
     _require(qkv.dtype == torch.bfloat16 and qkv.dim() == 2 and qkv.shape[0] == n, "qkv: bf16 [n, 3d]")
     ld = _rows(qkv, "qkv", 3 * d)
@@ -609,16 +614,56 @@ def qkv_norm_rope(qkv: torch.Tensor, norm_q: torch.Tensor, norm_k: torch.Tensor,
     return q_out
 
 
+def _qkv_heads(qkv, norm_q, norm_k, eps, cos, sin, q_out, k_out, v_out, model_heads: int, h0: int,
+               ring: Ring | None = None, t0: int = 0, evicted: int = 0) -> torch.Tensor:
+    """``ss_qkv_norm_rope_heads``: the norm over all ``model_heads`` heads of qkv, heads
+    h0 .. h0 + h - 1 written to q_out [n, h, 128] and k_out / v_out (rows of h heads, plain or a
+    ring cache)."""
+    n, h = q_out.shape[0], q_out.shape[1]
+    d = model_heads * HEAD_DIM
+    _require(qkv.dtype == torch.bfloat16 and qkv.dim() == 2 and qkv.shape[0] == n, "qkv: bf16 [n, 3d]")
+    _require(0 <= h0 and h0 + h <= model_heads, "head range outside the model's heads")
+    ld = _rows(qkv, "qkv", 3 * d)
+    _require(q_out.dtype == torch.bfloat16 and q_out.stride(2) == 1 and q_out.stride(1) == HEAD_DIM,
+             "q_out: bf16 [n, h, 128] rows")
+    for name, t in (("k_out", k_out), ("v_out", v_out)):
+        _require(t.dtype == torch.bfloat16 and t.shape[1:] == (h, HEAD_DIM) and t.stride(2) == 1 and
+                 t.stride(1) == HEAD_DIM, f"{name}: bf16 [rows, h, 128]")
+    _require(k_out.stride(0) == v_out.stride(0), "k_out and v_out must share a row stride")
+    for name, t in (("norm_q", norm_q), ("norm_k", norm_k)):
+        _require(t.dtype == torch.bfloat16 and t.is_contiguous() and t.numel() == d, f"{name}: bf16 [{d}]")
+    for name, t in (("cos", cos), ("sin", sin)):
+        _require(t.dtype == torch.float32 and t.is_contiguous() and t.shape == (n, HEAD_DIM // 2),
+                 f"{name}: fp32 [n, 64]")
+    if ring is not None:
+        _require(ring.head_dev is not None, "the ring's head must live in device memory")
+        _require(k_out.is_contiguous() and v_out.is_contiguous() and k_out.shape[0] == ring.phys_rows(),
+                 "caches must be contiguous ring caches of the ring's geometry")
+        rs = (ring.sink, ring.cap, int(t0), ring.dev_ptr(), int(evicted))
+    else:
+        _require(k_out.shape[0] == n and v_out.shape[0] == n, "k_out / v_out: the chunk's n rows")
+        rs = (0, 0, 0, None, 0)
+    rc = lib().ss_qkv_norm_rope_heads(_p(qkv), ld, n, model_heads, _p(norm_q), _p(norm_k), float(eps), _p(cos),
+                                      _p(sin), h0, h, _p(q_out), q_out.stride(0), _p(k_out), _p(v_out),
+                                      k_out.stride(0), *rs, _stream(qkv.device))
+    check(rc, "ss_qkv_norm_rope_heads")
+    return q_out
+
+
 def qkv_norm_rope_ring(qkv: torch.Tensor, norm_q: torch.Tensor, norm_k: torch.Tensor, eps: float, cos: torch.Tensor,
                        sin: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
-                       ring: Ring, t0: int, evicted: int) -> torch.Tensor:
+                       ring: Ring, t0: int, evicted: int, model_heads: int | None = None, h0: int = 0) -> torch.Tensor:
     """``qkv_norm_rope`` with k and v written into a ring-buffer cache [S + C + 64, H, 128] at the
     rows of window rows t0 .. t0 + n - 1, placed by the device head moved on by ``evicted``
-    (``ss_qkv_norm_rope_ring``; ``ring.head_dev`` required). Follow it with ``ring_commit``."""
+    (``ss_qkv_norm_rope_ring``; ``ring.head_dev`` required). Follow it with ``ring_commit``.
+    ``model_heads`` / ``h0``: as in ``qkv_norm_rope`` (a cache of h0 .. h0 + h - 1)."""
     n, H = q_out.shape[0], q_out.shape[1]
     d = H * HEAD_DIM
     kc = k_cache[0] if k_cache.dim() == 4 else k_cache
     vc = v_cache[0] if v_cache.dim() == 4 else v_cache
+    if model_heads is not None:
+        return _qkv_heads(qkv, norm_q, norm_k, eps, cos, sin, q_out, kc, vc, model_heads, h0, ring=ring, t0=t0,
+                          evicted=evicted)
     _require(ring.head_dev is not None, "the ring's head must live in device memory")
     _require(qkv.dtype == torch.bfloat16 and qkv.dim() == 2 and qkv.shape[0] == n, "qkv: bf16 [n, 3d]")
     ld = _rows(qkv, "qkv", 3 * d)

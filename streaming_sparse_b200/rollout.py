@@ -222,16 +222,21 @@ class Block(nn.Module):
 
         h = ops.adaln(x, eps=cfg.eps, shift=em[:, 0], scale=em[:, 1], frame_tokens=ft)
         qkv = self.qkv(h)
-        q = torch.empty((n, H, HEAD_DIM), device=x.device, dtype=x.dtype)
+        # a head-parallel rank's cache holds heads head0 .. head0 + cache.H - 1: q, k and v of
+        # those heads only (the q/k RMSNorm still over the whole width)
+        nh = cache.H
+        part = dict(model_heads=H, h0=cache.head0) if nh != H else {}
+        q = torch.empty((n, nh, HEAD_DIM), device=x.device, dtype=x.dtype)
         rows = cache.reserve(n, current_start)
         if rows is not None:
-            ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, rows[0], rows[1])
+            ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, rows[0], rows[1], **part)
         elif cache.ring_mode:   # straight into the ring rows, placed by the head in device memory
-            cache.write_qkv(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, current_start)
+            cache.write_qkv(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, current_start,
+                            model_heads=H if part else None)
         else:   # the write rolls the window: stage k/v, then the cache kernel rolls and writes
             k = torch.empty_like(q)
             v = torch.empty_like(q)
-            ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, k, v)
+            ops.qkv_norm_rope(qkv, self.norm_q, self.norm_k, cfg.eps, rope[0], rope[1], q, k, v, **part)
             cache.append(k, v, current_start)
         kw, vw = _window_for(cache)
         y = _module_attention()(q[None], kw[None], vw[None])[0]
@@ -410,17 +415,32 @@ class Rollout:
     """
 
     def __init__(self, model: CausalWanDiT, sparse=None, scheduler: FlowMatch | None = None, graphs: bool = False,
-                 fused: bool = True):
+                 fused: bool = True, head_parallel: bool = False, group=None):
         self.model = model
         self.cfg = model.cfg
         self.sparse = sparse
         self.sched = scheduler or FlowMatch()
         dev = next(model.parameters()).device
         cfg = self.cfg
-        self.caches = [KVCache(cfg.cache_frames * cfg.frame_tokens, cfg.num_heads, HEAD_DIM,
+        h0, nh = 0, cfg.num_heads
+        if head_parallel:
+            import torch.distributed as dist
+
+            from .distributed import head_range
+            if sparse is None or not fused:
+                raise ValueError("a head-parallel rollout runs the sparse plugin with the fused kernels")
+            h0, h1 = head_range(cfg.num_heads, dist.get_rank(group), dist.get_world_size(group))
+            nh = h1 - h0
+        self.caches = [KVCache(cfg.cache_frames * cfg.frame_tokens, nh, HEAD_DIM,
                                frame_tokens=cfg.frame_tokens, local_attn_size=cfg.local_attn_frames,
                                sink_size=cfg.sink_frames, device=dev, track_positions=False, ring=cfg.ring_cache)
                        for _ in range(cfg.num_layers)]
+        for c in self.caches:
+            c.head0 = h0
+        self.head_parallel = head_parallel
+        if head_parallel:
+            from .distributed import HeadParallelAttention
+            self.sparse = HeadParallelAttention(sparse, self.caches, cfg.chunk_tokens, dev, group)
         self.device = dev
         self._rope = {}
         self.graphs = graphs
@@ -550,6 +570,12 @@ class Rollout:
         self._graph.clear()
         self._pool = None
         self._rope_in.clear()
+
+    def close(self):
+        """Release the graphs and, for a head-parallel rollout, the peer mappings (every rank)."""
+        self.release_graphs()
+        if self.head_parallel:
+            self.sparse.close()
 
 
 def build_model(cfg: WanConfig = WanConfig(), device="cuda", seed: int = 0) -> CausalWanDiT:

@@ -127,3 +127,97 @@ def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
         assert same                                            # repeated calls; push == pull, bit for bit
         assert_attention_close(kv, whole)                       # KV-block shards merged by LSE
         np.testing.assert_array_equal(hs, whole)               # heads are independent: identical bits
+
+
+def _rollout_cfg(ring: bool):
+    from streaming_sparse_b200 import rollout as R
+    return R.WanConfig(dim=512, ffn_dim=1024, num_heads=4, num_layers=2, text_dim=64, text_len=16, latent_h=16,
+                       latent_w=12, frames=12, cache_frames=7, local_attn_frames=7, sink_frames=1, ring_cache=ring)
+
+
+def _rollout_inputs(cfg, dev):
+    g = torch.Generator(device=dev)
+    noise = torch.randn(cfg.frames, 16, cfg.latent_h, cfg.latent_w, device=dev, generator=g.manual_seed(3))
+    text = torch.randn(10, cfg.text_dim, device=dev, generator=g.manual_seed(4))
+    return noise, text, g
+
+
+def _run_rollout(cfg, dev, head_parallel: bool):
+    """Eager run, then capture, then replay; returns (eager, replayed) latents on the CPU."""
+    from streaming_sparse_b200 import rollout as R
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention, init_router_weights
+    m = R.build_model(cfg, device=dev)
+    wq, wk = init_router_weights(cfg.num_heads, device=dev)
+    sp = SparseAttention(wq, wk, RouterConfig(density=0.5, sink_tokens=cfg.frame_tokens))
+    ro = R.Rollout(m, sparse=sp, graphs=True, head_parallel=head_parallel)
+    noise, text, g = _rollout_inputs(cfg, dev)
+    eager = ro.run(noise, text, generator=g.manual_seed(5))
+    ro.run(noise, text, generator=g.manual_seed(5))            # captures
+    replayed = ro.run(noise, text, generator=g.manual_seed(5))
+    torch.cuda.synchronize()
+    res = (eager.float().cpu(), replayed.float().cpu())
+    ro.close()
+    return res
+
+
+def _rollout_worker(rank, world, port, q_out):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        from streaming_sparse_b200 import ops
+        runs = {}
+        for ring in (False, True):
+            runs[ring] = _run_rollout(_rollout_cfg(ring), dev, head_parallel=True)
+            dist.barrier()
+        ops.DeviceStatus.check(dev)
+        q_out.put((rank, runs))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:   # report to the parent instead of hanging it
+        q_out.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_head_parallel_rollout_on_two_gpus_matches_one_gpu():
+    """Config 4's stream shape in miniature (rolling window with a sink frame, shifting and ring
+    caches) with the attention split by heads over two GPUs: each rank's caches hold its two of
+    the four heads, the fused kernel writes only those, and every layer's attention output
+    reaches both ranks through the fused head gather. No tile is split at this size, so every
+    head's arithmetic is the single GPU's: the latents are equal bit for bit, eager and replayed
+    from CUDA graphs."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rollout_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in procs:
+            rank, runs = q_out.get(timeout=300)
+            results[rank] = runs
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=30)
+    assert len(results) == 2
+    for rank, runs in results.items():
+        assert not isinstance(runs, str), f"rank {rank}: {runs}"
+    dev = torch.device("cuda:0")
+    for ring in (False, True):
+        eager, replayed = _run_rollout(_rollout_cfg(ring), dev, head_parallel=False)
+        for rank in (0, 1):
+            hp_eager, hp_replayed = results[rank][ring]
+            assert torch.isfinite(hp_eager).all()
+            assert torch.equal(hp_eager, eager), f"ring={ring} rank {rank}: eager latents differ"
+            assert torch.equal(hp_replayed, replayed), f"ring={ring} rank {rank}: replayed latents differ"
