@@ -674,10 +674,14 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
       layer's attention split by heads this way, frames/s max over ranks; rank 0 also runs the
       stream on one GPU for the ratio and the latents' difference (split-mode tiles at 6 heads
       per rank merge in fp32, so the latents agree to rounding, not bit for bit).
+    * ``c5_98280``: config 5's longest window (98280 tokens, 64-token blocks, 10 %), KV push and
+      fused heads.
     Each is checked once against the single-GPU output (router ids bit for bit for ``kv``; max-abs,
     mean-abs and NMSE of the output), then timed as CUDA-graph replays (two calls per graph),
-    max over ranks. ``merge_share``: the part of a KV-sharded call that a graph without the
-    barrier and merge does not take."""
+    max over ranks. The KV-sharded speed-ups are against the one-GPU call that also routes with
+    the history keys pooled at commit (``single_gpu_cached_us``); the head-sharded ones against
+    the plain one-GPU call (both route the whole window per call). ``merge_share``: the part of a
+    KV-sharded call that a graph without the barrier and merge does not take."""
     import torch.distributed as dist
     from streaming_sparse_b200 import ops
     from streaming_sparse_b200.distributed import HeadShardedAttention, KVShardedAttention, head_shard, local_ids
@@ -727,8 +731,25 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
 
     o1 = torch.empty_like(q)
     single = graph_us(lambda: (sp.forward_one(q, k, v, out=o1), sp.forward_one(q, k, v, out=o1)))
+
+    def cached_single(q_, k_, v_, cfg_, sink_):
+        """us of the one-GPU call with the history keys pooled at commit (as the KV-sharded ranks
+        route): cached route + attention."""
+        lq_, lk_ = q_.shape[0], k_.shape[0]
+        keys = ops.RouterKeys(H, lk_, block=cfg_.block, device=dev)
+        nh = ops.history_blocks(lq_, lk_, cfg_.block)
+        ops.pool_keys(k_, wk, keys, j0=0, j1=nh)
+        ws1, o_ = ops.Workspace(), torch.empty_like(q_)
+
+        def call():
+            ids = ops.route(q_, k_, wq, wk, block=cfg_.block, extra=cfg_.extra(lq_, lk_), sink_tokens=sink_,
+                            workspace=ws1, keys=keys, n_cached=nh)
+            ops.sparse_attention(q_, k_, v_, ids, block=cfg_.block, out=o_, workspace=ws1)
+        return graph_us(lambda: (call(), call()))
+
+    single_cached = cached_single(q, k, v, cfg, sink)
     res = {"config": "config4 chunk-layer: 4680 q x 34320 KV (21 frames + 1 sink frame), b128, 10% of unforced",
-           "single_gpu_us": single}
+           "single_gpu_us": single, "single_gpu_cached_us": single_cached}
 
     # ---- KV blocks
     c0 = lk - lq
@@ -758,7 +779,8 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
                                      local_ids(ids, rank, world), block=block, return_lse=True, out=lo, lse=ll)
             kv["local_us"] = graph_us(lambda: (local_part(), local_part()))
             kv["merge_share"] = max(0.0, 1.0 - kv["local_us"] / kv["us"])
-        kv["speedup_vs_1gpu"] = single / kv["us"]
+        # against the one-GPU call that also routes with the keys pooled at commit
+        kv["speedup_vs_1gpu"] = single_cached / kv["us"]
         torch.cuda.synchronize()
         ops.DeviceStatus.check(dev)
         dist.barrier()
@@ -791,6 +813,46 @@ def sharded_bench(dev, args, rank: int, world: int) -> dict:
     hf.close()
     res["heads_fused"] = fused
     del shard, hs
+    torch.cuda.empty_cache()
+
+    # ---- config 5's longest window (98280 tokens, 64-token blocks, 10 %): KV push, fused heads
+    lq5, lk5 = 4680, 98280
+    cfg5 = RouterConfig(block=64, density=0.10)
+    g5 = torch.Generator().manual_seed(505)
+    q5, k5, v5 = (torch.randn((n, H, D), generator=g5).bfloat16().to(dev) for n in (lq5, lk5, lk5))
+    sp5 = SparseAttention(wq, wk, cfg5)
+    whole5 = sp5.forward_one(q5, k5, v5)
+    ids5 = sp5.last_ids.clone()
+    o5 = torch.empty_like(q5)
+    c5 = {"config": "config5 chunk-layer: 4680 q x 98280 KV, b64, 10%",
+          "single_gpu_us": graph_us(lambda: (sp5.forward_one(q5, k5, v5, out=o5), sp5.forward_one(q5, k5, v5, out=o5))),
+          "single_gpu_cached_us": cached_single(q5, k5, v5, cfg5, 0)}
+    sh5 = KVShardedAttention(SparseAttention(wq, wk, cfg5), lq5, lk5, dev)
+    sh5.commit(k5, v5)                     # the whole window, the chunk's rows included
+    out5 = sh5.attend(q5).clone()
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    c5["kv"] = {"us": graph_us(lambda: (sh5.attend(q5), sh5.attend(q5))),
+                "ids_equal": bool(torch.equal(sh5.last_ids, ids5)),
+                "max_abs": float((out5.float() - whole5.float()).abs().max())}
+    c5["kv"]["speedup_vs_1gpu"] = c5["single_gpu_cached_us"] / c5["kv"]["us"]
+    torch.cuda.synchronize()
+    dist.barrier()
+    sh5.close()
+    hf5 = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg5),
+                               H, Lq=lq5, device=dev)
+    a5 = (head_shard(q5, rank, world), head_shard(k5, rank, world), head_shard(v5, rank, world))
+    hout5 = hf5(*a5).clone()
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    c5["heads_fused"] = {"us": graph_us(lambda: (hf5(*a5), hf5(*a5))),
+                         "max_abs": float((hout5.float() - whole5.float()).abs().max())}
+    c5["heads_fused"]["speedup_vs_1gpu"] = c5["single_gpu_us"] / c5["heads_fused"]["us"]
+    torch.cuda.synchronize()
+    dist.barrier()
+    hf5.close()
+    res["c5_98280"] = c5
+    del sp5, sh5, hf5, q5, k5, v5, a5, whole5
     torch.cuda.empty_cache()
 
     # ---- config 4's stream, every layer's attention split by heads (fused gather)
@@ -1172,7 +1234,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             r(rollout["config4_long_horizon"]["ring_cache"]["value"], 2)},
         "configs_frac": None if other is None else {o["short"]: [r(o["us"]), r(o["frac_of_peak"], 3)] for o in other},
         "sharded": None if sharded is None else {
-            "c4_1gpu_us": r(sharded["single_gpu_us"]),
+            "c4_1gpu_us": r(sharded["single_gpu_us"]), "c4_1gpu_cached_us": r(sharded["single_gpu_cached_us"]),
             "kv": {"us": r(sharded["kv"]["us"]), "x": r(sharded["kv"]["speedup_vs_1gpu"], 2),
                    "write_chunk_us": r(sharded["kv"]["write_chunk_us"]), "ids_equal": sharded["kv"]["ids_equal"],
                    "max_abs": r(sharded["kv"]["max_abs"], 5), "nmse": sharded["kv"]["nmse"]},
@@ -1185,6 +1247,13 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "heads_fused": {"us": r(sharded["heads_fused"]["us"]), "x": r(sharded["heads_fused"]["speedup_vs_1gpu"], 2),
                             "equals_all_gather": sharded["heads_fused"]["equals_all_gather"],
                             "max_abs": r(sharded["heads_fused"]["max_abs"], 5)},
+            "c5_98280": {"1gpu_us": r(sharded["c5_98280"]["single_gpu_us"]),
+                         "1gpu_cached_us": r(sharded["c5_98280"]["single_gpu_cached_us"]),
+                         "kv_us": r(sharded["c5_98280"]["kv"]["us"]),
+                         "kv_x": r(sharded["c5_98280"]["kv"]["speedup_vs_1gpu"], 2),
+                         "kv_ids_equal": sharded["c5_98280"]["kv"]["ids_equal"],
+                         "heads_fused_us": r(sharded["c5_98280"]["heads_fused"]["us"]),
+                         "heads_fused_x": r(sharded["c5_98280"]["heads_fused"]["speedup_vs_1gpu"], 2)},
             "stream4_heads": sharded.get("stream4_heads") and {
                 k_: (r(v_, 3) if isinstance(v_, float) else v_) for k_, v_ in sharded["stream4_heads"].items()}},
     }

@@ -3,7 +3,8 @@
 to their rows' owners by the attention epilogue and merged there, or pulled and merged over peer
 memory) and head sharding with the all_gather, each against the single-GPU result; the
 fused head gather (the attention epilogue storing every rank's heads into all ranks' buffers over
-NVLink) against the all_gather, bit for bit, through both output slots and in the split mode.
+NVLink) against the all_gather, bit for bit, through both output slots, in the split mode and
+with an uneven head split.
 Skipped where fewer than two GPUs are visible."""
 import datetime
 import os
@@ -64,15 +65,17 @@ def _worker(rank, world, port, q_out):
         hs = HeadShardedAttention(SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg),
                                   H)(head_shard(q, rank, world), head_shard(k, rank, world), head_shard(v, rank, world))
         fused_ok = []
-        # (Lq, Lk): 16 tiles per rank, and 150 (the split mode, one to two tiles per SM)
-        for lq, lk in ((LQ, LK), (9600, 12800)):
-            g = torch.Generator().manual_seed(lq)
-            fq, fk, fv = (torch.randn((n, H, 128), generator=g).bfloat16().to(dev) for n in (lq, lk, lk))
-            sps = [SparseAttention(head_shard(wq, rank, world, 0), head_shard(wk, rank, world, 0), cfg)
+        # (Lq, Lk, heads): 16 tiles per rank; 150 (the split mode, one to two tiles per SM); and
+        # 3 heads, split 2 + 1 (uneven ranks, as 12 heads over 8 GPUs)
+        for lq, lk, nh in ((LQ, LK, H), (9600, 12800, H), (LQ, LK, 3)):
+            g = torch.Generator().manual_seed(lq + nh)
+            fq, fk, fv = (torch.randn((n, nh, 128), generator=g).bfloat16().to(dev) for n in (lq, lk, lk))
+            hwq, hwk = wq[:nh].contiguous(), wk[:nh].contiguous()
+            sps = [SparseAttention(head_shard(hwq, rank, world, 0), head_shard(hwk, rank, world, 0), cfg)
                    for _ in range(2)]
             args = (head_shard(fq, rank, world), head_shard(fk, rank, world), head_shard(fv, rank, world))
-            want = HeadShardedAttention(sps[0], H)(*args)
-            fused = HeadShardedAttention(sps[1], H, Lq=lq, device=dev)
+            want = HeadShardedAttention(sps[0], nh)(*args)
+            fused = HeadShardedAttention(sps[1], nh, Lq=lq, device=dev)
             got = [fused(*args).clone() for _ in range(3)]       # both output slots, then the first again
             torch.cuda.synchronize()
             fused_ok.append(all(torch.equal(x, want) for x in got))
@@ -122,7 +125,7 @@ def test_kv_and_head_sharding_on_two_gpus_match_one_gpu():
     whole = sp(q[None], k[None], v[None])[0].float().cpu().numpy()
     whole_ids = sp.last_ids.cpu().numpy()
     for rank, ((kv, ids, same, fused_ok), hs) in results.items():
-        assert fused_ok == [True, True], f"rank {rank}: fused head gather differs from the all_gather"
+        assert fused_ok == [True, True, True], f"rank {rank}: fused head gather differs from the all_gather"
         np.testing.assert_array_equal(ids, whole_ids)          # the sharded router: same ids, bit for bit
         assert same                                            # repeated calls; push == pull, bit for bit
         assert_attention_close(kv, whole)                       # KV-block shards merged by LSE
