@@ -205,6 +205,14 @@ def local_rows(Lk: int, block: int, rank: int, world: int) -> torch.Tensor:
     return rows[rows < Lk]
 
 
+def owner_rows(Lq: int, rank: int, world: int) -> tuple[int, int, int]:
+    """Query rows [lo, hi) whose merged output rank ``rank`` owns under the push exchange, and
+    the row count of every owner's buffers (ceil(Lq / world)); row t belongs to rank t // rows."""
+    rows = -(-Lq // world)
+    lo = min(Lq, rank * rows)
+    return lo, min(Lq, lo + rows), rows
+
+
 def shard_ids(ids: torch.Tensor, rank: int, world: int) -> torch.Tensor:
     """Keep the block ids this rank owns (window numbering); others become -1."""
     own = (ids >= 0) & (torch.remainder(ids, world) == rank)
@@ -347,9 +355,7 @@ class KVShardedAttention:
         else:
             # rank d owns output rows [d * rows, (d + 1) * rows): its "o" / "lse" hold every rank's
             # partial of those rows (slot = the writing rank), its "out" the merged output
-            self.rows_per_rank = -(-Lq // self.world)
-            self.row_lo = min(Lq, self.rank * self.rows_per_rank)
-            self.row_hi = min(Lq, self.row_lo + self.rows_per_rank)
+            self.row_lo, self.row_hi, self.rows_per_rank = owner_rows(Lq, self.rank, self.world)
             self.peer = PeerBuffers({"o": ((self.world, self.rows_per_rank, self.H, D), part_dtype),
                                      "lse": ((self.world, self.H, self.rows_per_rank), torch.float32),
                                      "out": ((Lq, self.H, D), torch.bfloat16),

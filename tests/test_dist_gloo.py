@@ -1,5 +1,7 @@
-"""Multi-rank host logic on CPU (gloo, world sizes 2 and 3): LSE merge of KV-block shards and the head
-all_gather, with the per-rank partial attention computed by the CPU oracle in the test."""
+"""Multi-rank host logic on CPU (gloo, world sizes 2 and 3): LSE merge of KV-block shards (every
+partial to every rank, and the push exchange: partial rows to their owners, merged rows to
+everyone) and the head all_gather, with the per-rank partial attention computed by the CPU oracle
+in the test."""
 import math
 import os
 import socket
@@ -80,6 +82,39 @@ def kv_shard_rank(rank, world):
     return o.lse_merge(np.stack([p_[0] for p_ in parts]), np.stack([p_[1] for p_ in parts]))
 
 
+def kv_push_rank(rank, world):
+    """The push exchange of KVShardedAttention restated: this rank's partial (as kv_shard_rank)
+    goes to the owners of its rows, slot = this rank (the attention epilogue's stores into the
+    owners' [world][rows][H][D] and [world][H][rows] buffers); each owner merges its rows from its
+    slots and every rank gathers the merged rows (the merge's stores into every rank's output)."""
+    from streaming_sparse_b200.distributed import local_ids, local_rows, owner_rows
+    o, q, k, v, ids = _inputs()
+    Lq, H = q.shape[0], q.shape[1]
+    rows = local_rows(k.shape[0], 64, rank, world).numpy()
+    part, lse = o.attention(q, k[rows], v[rows], local_ids(torch.from_numpy(ids), rank, world).numpy(), 64)
+    lse = np.where(np.isnan(lse), -np.inf, lse)
+    part = np.where(np.isneginf(lse).T[:, :, None], 0.0, part)
+    _, _, n = owner_rows(Lq, rank, world)
+    # what this rank pushes to each owner d: rows [lo_d, hi_d) at local rows 0 .. hi_d - lo_d
+    pushes = []
+    for d in range(world):
+        lo, hi, _ = owner_rows(Lq, d, world)
+        o_buf = np.zeros((n, H, 128), np.float32)
+        l_buf = np.full((H, n), -np.inf, np.float32)
+        o_buf[:hi - lo] = part[lo:hi]
+        l_buf[:, :hi - lo] = lse[:, lo:hi]
+        pushes.append((o_buf, l_buf))
+    everyone = [None] * world
+    dist.all_gather_object(everyone, pushes)
+    lo, hi, _ = owner_rows(Lq, rank, world)
+    o_slots = np.stack([everyone[src][rank][0] for src in range(world)])      # [world][rows][H][D]
+    l_slots = np.stack([everyone[src][rank][1] for src in range(world)])      # [world][H][rows]
+    merged, merged_lse = o.lse_merge(o_slots[:, :hi - lo], l_slots[:, :, :hi - lo])
+    gathered = [None] * world
+    dist.all_gather_object(gathered, (merged, merged_lse))
+    return np.concatenate([g_[0] for g_ in gathered]), np.concatenate([g_[1] for g_ in gathered], axis=1)
+
+
 def kv_keys_rank(rank, world):
     """Every rank pools the history blocks it owns from its local window; the all-gathered tables
     assembled into window order must equal the projections of the whole window's blocks."""
@@ -121,6 +156,28 @@ def test_kv_sharded_lse_merge_equals_full(world):
     for r in range(world):
         np.testing.assert_allclose(res[r][0], ref, rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(res[r][1], ref_lse, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_kv_sharded_push_exchange_equals_full(world):
+    """130 query rows over 3 owners: 44 + 44 + 42 (the last owner's buffers partly unused)."""
+    res = _run(kv_push_rank, world)
+    o, q, k, v, ids = _inputs()
+    ref, ref_lse = o.attention(q, k, v, ids, 64)
+    for r in range(world):
+        np.testing.assert_allclose(res[r][0], ref, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(res[r][1], ref_lse, rtol=1e-6, atol=1e-6)
+
+
+def test_owner_rows():
+    from streaming_sparse_b200.distributed import owner_rows
+    assert [owner_rows(130, r, 3) for r in range(3)] == [(0, 44, 44), (44, 88, 44), (88, 130, 44)]
+    assert [owner_rows(4680, r, 8)[:2] for r in range(8)][-1] == (4095, 4680)
+    assert owner_rows(3, 3, 4) == (3, 3, 1)          # more owners than rows: an empty range
+    for world in (1, 2, 3, 4, 8):
+        spans = [owner_rows(4680, r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == 4680
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
 
 
 @pytest.mark.parametrize("world", [2, 3, 8])
