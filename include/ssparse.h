@@ -238,9 +238,10 @@ int ss_attention(const void *q, const void *k, const void *v, const int32_t *ids
 /* Largest n_ids ss_attention accepts for these sizes (its block lists live in shared memory). */
 int ss_attention_max_ids(int Lk, int block, int *max_ids);
 
-/* ss_attention with a caller workspace that balances a problem of one to two tiles per SM: when
- * the 128-row tiles (ceil(Lq/128) * H) are at least as many as the SMs and fewer than twice as
- * many, each CTA takes an equal share of the tiles' work, a tile shared by several CTAs is cut at its step list, every piece leaves
+/* ss_attention with a caller workspace that balances a problem of one to two tiles per SM, or of
+ * half a tile per SM or less: when the 128-row tiles (ceil(Lq/128) * H) are at least as many as
+ * the SMs and fewer than twice as many, or at most half as many (and long enough that a piece
+ * keeps 8 steps), each CTA takes an equal share of the tiles' work, a tile shared by several CTAs is cut at its step list, every piece leaves
  * its normalised partial and LSE in the workspace, and a second kernel merges the pieces (the
  * arithmetic of ss_lse_merge). Larger problems run exactly as ss_attention. Same arguments and
  * results as ss_attention (within fp32 rounding of the merge for split tiles). workspace:

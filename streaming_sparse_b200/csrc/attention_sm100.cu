@@ -1037,9 +1037,10 @@ constexpr int MAXSPLIT = 8;
 static_assert(attn::MAXSPLIT_PIECES >= MAXSPLIT + 1, "pieces per tile");
 
 // Measured on B200 (kernel alone): 156 tiles 77.8 -> 74.9 us and 222 tiles 144.9 -> 136.2 us with
-// the split, but 111 tiles 74.1 -> 86.5 us: below one tile per SM each piece's fixed start-up and
-// epilogue cost outweighs the balance gained, so only between one and two tiles per SM.
-static bool split_wanted(int T, int nsm) { return T >= nsm && T < 2 * nsm; }
+// the split; at half a tile per SM or less every tile is cut in two or more equal pieces, config 4
+// with 74 tiles 71.1 -> 52.3 us; in between a piece's fixed start-up, epilogue and merge cost more
+// than the balance gained (111 tiles 71.9 -> 76.9 us), so those run whole.
+static bool split_wanted(int T, int nsm) { return (T >= nsm && T < 2 * nsm) || 2 * T <= nsm; }
 static int split_grid(int T, int nsm) { return std::min(nsm, MAXSPLIT * T); }
 static size_t split_ws_bytes(int G) { return (size_t)2 * G * 128 * (attn::D + 1) * sizeof(float); }
 
@@ -1134,10 +1135,13 @@ static int attention_launch(const void *q, const void *k, const void *v, const i
     const long sb_tile = (block == 64) ? std::min(2L * n_ids, (long)prm.kb) : 2L * std::min(n_ids, prm.kb);
     int G;
     if (ws && split_wanted(prm.T, nsm)) {
-        // split mode: every CTA's units meet at most ceil(T/G) + 1 tiles
+        // split mode: every CTA's units meet at most ceil(T/G) + 1 tiles; below one tile per SM
+        // only where a piece keeps at least 8 steps of the longest list (short lists run whole)
         G = split_grid(prm.T, nsm);
         const int tmax = (prm.T + G - 1) / G + 1;
-        if (ws_bytes >= split_ws_bytes(G) && attention_smem_for(prm.kb, block, n_ids, tmax) <= (long)attn::SMEM_LIMIT) {
+        const bool pieces_long = prm.T >= nsm || attention_tile_steps(sb_tile) * prm.T >= 8L * G;
+        if (pieces_long && ws_bytes >= split_ws_bytes(G) &&
+            attention_smem_for(prm.kb, block, n_ids, tmax) <= (long)attn::SMEM_LIMIT) {
             prm.split = 1;
             prm.tmax = tmax;
             prm.ws_o = static_cast<float *>(ws);

@@ -290,11 +290,13 @@ def test_attention_many_tiles_per_cta(oracle, Lq, Lk, H, n):
 @pytest.mark.parametrize("Lq,Lk,H,block,n", [
     (1560, 6240, 12, 64, 49),       # config 1's shape: 156 tiles on 148 SMs
     (4680, 34320, 6, 128, 72),      # config 4 with 6 heads (a 2-way head shard): 222 tiles
+    (4680, 34320, 2, 128, 72),      # config 4 with 2 heads (8-way head shard): 74 tiles, two CTAs each
+    (4680, 34320, 1, 128, 72),      # 1 head: 37 tiles, four CTAs each
     (3600, 6000, 10, 64, 2),        # 290 tiles with two-step lists: pieces without steps
     (3650, 3000, 10, 128, 3),       # partial last tile of every head, 128-token blocks
 ])
 def test_split_tiles_match_unsplit_and_oracle(oracle, Lq, Lk, H, block, n):
-    """ss_attention_ws on problems of one to two tiles per SM (tiles cut across CTAs,
+    """ss_attention_ws on problems of one to two tiles per SM or half a tile per SM or less (tiles cut across CTAs,
     pieces merged by log-sum-exp) against ss_attention (whole tiles) and, with the north-star
     tolerance, against the float64 oracle; fp32 output and LSE too, twice in a row (the
     workspace keeps nothing between calls)."""
