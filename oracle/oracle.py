@@ -280,3 +280,119 @@ def rope_shift(keys: np.ndarray, tokens: int, phase: np.ndarray) -> np.ndarray:
     rot[..., 0::2], rot[..., 1::2] = re, im
     out[..., :tokens, :, :2 * pairs] = bf16_round(rot.astype(np.float32))
     return out
+
+
+# ----------------------------------------------------------------------------------------------
+# INT8-QK sparse attention (SpargeAttn-style path)
+# ----------------------------------------------------------------------------------------------
+# Restates migration/unified_router/opt23/attention.py: ``_quant`` (:6-14, K per 64-token page and
+# head) and ``_shared`` with INT8=True (:30-58: Q per G-row group and head, quantised in the
+# kernel; logits = int32 dot * (qs * ks[page]) * log2(e)/sqrt(128); base-2 online softmax; P cast to
+# V's type for the P.V product), used with G = 32 by opt24/pipeline.py:24-25 and opt24/sparge.py.
+
+QUANT_PAGE = 64      # K rows sharing one scale (one page)
+QUANT_QGROUP = 32    # Q rows sharing one scale
+
+
+def quant_rows(x: np.ndarray, rows: int):
+    """x [L,H,D] (float32 holding the bf16 values) -> (x_i8 [L,H,D] int8, scale [H,ceil(L/rows)] fp32).
+
+    Per group of ``rows`` consecutive rows and per head: scale = max(max|x| / 127, 1e-10) in fp32,
+    x_i8 = round-half-even(x / scale) with an IEEE fp32 divide (opt23/attention.py:10-13,37-39).
+    Rows past L count as zeros in their group's maximum.
+    """
+    x = np.asarray(x, np.float32)
+    L, H, D = x.shape
+    n = -(-L // rows)
+    pad = np.zeros((n * rows, H, D), np.float32)
+    pad[:L] = x
+    g = pad.reshape(n, rows, H, D)
+    amax = np.abs(g).max(axis=(1, 3))                                     # [n,H]
+    s = np.maximum(amax / np.float32(127.0), np.float32(1e-10)).astype(np.float32)
+    xi = np.rint(g / s[:, None, :, None]).astype(np.int8)
+    return xi.reshape(n * rows, H, D)[:L].copy(), np.ascontiguousarray(s.T)
+
+
+def i8_logit_scale(scale: float) -> np.float32:
+    """fp32 multiplier of the scaled int32 logits: scale * log2(e), rounded once to fp32."""
+    return np.float32(float(np.float32(scale)) * 1.4426950408889634)
+
+
+def i8_logits(qi_rows, qs_rows, ki_tok, ks_tok, c):
+    """fp32 base-2 logits of ``_shared`` (:47-48): ((int32 dot) * (qs * ks)) * c, each product rounded."""
+    dot = qi_rows.astype(np.int32) @ ki_tok.astype(np.int32).T            # exact (|dot| < 2^24)
+    t = (qs_rows[:, None].astype(np.float32) * ks_tok[None, :].astype(np.float32)).astype(np.float32)
+    return ((dot.astype(np.float32) * t).astype(np.float32) * np.float32(c)).astype(np.float32)
+
+
+def attention_i8(q, k_i8, ks, v, ids, block: int, scale: float | None = None, heads=None, qblocks=None):
+    """INT8-QK block-sparse attention with this library's layouts, exact softmax in float64.
+
+    q [Lq,H,D] (bf16 values), k_i8 [Lk,H,D] int8 and ks [H,ceil(Lk/64)] from ``quant_rows(k, 64)``,
+    v [Lk,H,D], ids [H,qb,K] block ids of ``block`` tokens (<0 ignored). Q is quantised per 32-row
+    group. Returns (out [Lq,H,D], lse [H,Lq]) in float64 (natural-log LSE); skipped rows are NaN.
+    """
+    q = np.asarray(q, np.float32)
+    Lq, H, D = q.shape
+    Lk = k_i8.shape[0]
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    c = i8_logit_scale(scale)
+    qi, qs = quant_rows(q, QUANT_QGROUP)
+    qb = nblocks(Lq, block)
+    out = np.full((Lq, H, D), np.nan)
+    lse = np.full((H, Lq), np.nan)
+    for h in (range(H) if heads is None else heads):
+        for i in (range(qb) if qblocks is None else qblocks):
+            r0, r1 = i * block, min(Lq, (i + 1) * block)
+            tok = selected_tokens(ids[h, i], Lk, block)
+            if len(tok) == 0:
+                out[r0:r1, h], lse[h, r0:r1] = 0.0, -np.inf
+                continue
+            rows = np.arange(r0, r1)
+            y = i8_logits(qi[rows, h], qs[h, rows // QUANT_QGROUP], k_i8[tok, h], ks[h, tok // QUANT_PAGE], c)
+            z = y.astype(np.float64)
+            m = z.max(axis=1, keepdims=True)
+            p = np.exp2(z - m)
+            s = p.sum(axis=1, keepdims=True)
+            out[r0:r1, h] = (p @ np.asarray(v[tok, h], np.float64)) / s
+            lse[h, r0:r1] = (m[:, 0] + np.log2(s[:, 0])) * math.log(2.0)
+    return out, lse
+
+
+def shared_i8_tiles(q, k_i8, ks, v, pages, group: int = QUANT_QGROUP, c=None, p_dtype=np.float16):
+    """The ``_shared`` kernel's own loop (opt23/attention.py:30-58, INT8=True, SPLITS=1), in its
+    layouts: q [H,N,D], k_i8 [H,NK,D], ks [H,B], v [H,NK,D], pages [H,T,KEEP] 64-token page ids per
+    ``group``-row tile, visited in list order; P rounded to ``p_dtype`` (V's type) before P.V, fp32
+    accumulation. Returns out [H,N,D] float32. Used to pin the restatement to the golden vectors."""
+    q = np.asarray(q, np.float32)
+    H, N, D = q.shape
+    NK = k_i8.shape[1]
+    c = np.float32(0.12751743082459617) if c is None else np.float32(c)
+    out = np.zeros((H, N, D), np.float32)
+    for h in range(H):
+        for t in range(pages.shape[1]):
+            rows = np.arange(t * group, min(N, (t + 1) * group))
+            qt = np.zeros((group, D), np.float32)
+            qt[:len(rows)] = q[h, rows]
+            qi, qs = quant_rows(qt[:, None, :], group)
+            m = np.full(group, -np.inf, np.float32)
+            den = np.zeros(group, np.float32)
+            acc = np.zeros((group, D), np.float32)
+            for page in pages[h, t]:
+                ki = page * QUANT_PAGE + np.arange(QUANT_PAGE)
+                valid = ki < NK
+                kk = np.zeros((QUANT_PAGE, D), np.int8)
+                kk[valid] = k_i8[h, ki[valid]]
+                y = i8_logits(qi[:, 0], np.full(group, qs[0, 0], np.float32), kk,
+                              np.full(QUANT_PAGE, ks[h, page], np.float32), c)
+                y = np.where(valid[None, :], y, np.float32(-np.inf))
+                nm = np.maximum(m, y.max(axis=1))
+                al = np.exp2(m - nm).astype(np.float32)
+                pr = np.exp2(y - nm[:, None]).astype(np.float32)
+                vv = np.zeros((QUANT_PAGE, D), np.float32)
+                vv[valid] = v[h, ki[valid]]
+                acc = (acc * al[:, None] + pr.astype(p_dtype).astype(np.float32) @ vv).astype(np.float32)
+                den = (den * al + pr.sum(axis=1)).astype(np.float32)
+                m = nm
+            out[h, rows] = (acc / den[:, None])[:len(rows)]
+    return out
