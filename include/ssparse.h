@@ -32,6 +32,9 @@
  *   ss_attention   <- exact(q,k,v,ids,workspace) (local_experiments/video_runtime_v1/attention.py:15-24)
  *                     wrapping _attn_fwd (local_experiments/gap_exact_round_kernel.py:4-137), and the
  *                     sm_80 C ABI `run` (local_experiments/video_runtime_v1/csrc/fixed15_attention.cu:407-409)
+ *   ss_quant_k_pages, ss_attention_i8 <- the INT8-QK path: `_quant` and `_shared` with INT8=True
+ *                     (migration/unified_router/opt23/attention.py:6-58), called by the Sparge
+ *                     pipeline (migration/unified_router/opt24/pipeline.py:23-25, sparge.py:38-43)
  *   ss_lse_merge   <- merge (local_experiments/video_runtime_v1/attention.py:40-45),
  *                     _merge_restore (migration/unified_router/opt21/attention.py:7-15)
  *   ss_cache_append<- the cache roll + write in CausalWanSelfAttention.forward
@@ -260,6 +263,30 @@ int ss_attention_ring(const void *q, const void *k, const void *v, const int32_t
                       void *out, int out_dtype, float *lse, int *status,
                       int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
                       void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------------------------ */
+/* INT8-QK block-sparse attention (the reference's SpargeAttn-style path).                      */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Quantise the key pages [p0, p1) of the window k [Lk][H][128] bf16 (page p = tokens
+ * [64p, 64p + 64), the last page possibly partial): per page and head, scale = max(max|k| / 127,
+ * 1e-10) in fp32 and k_i8 = round-half-even(k / scale) (IEEE divide) into k_i8 [Lk][H][128] int8,
+ * the scale into ks [H][ceil(Lk/64)] fp32. Replaces `_quant` / `Quantized.history` / `.current`
+ * (migration/unified_router/opt23/attention.py:6-28): history pages are quantised once per commit,
+ * the pages the current chunk touches per call. k and k_i8 16-byte aligned. */
+int ss_quant_k_pages(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8, float *ks, void *stream);
+
+/* ss_attention with the scores taken in int8: q [Lq][H][128] bf16 is quantised per 32-row group
+ * and head inside the kernel (the scale rule of ss_quant_k_pages), the logits are the exact int32
+ * dot products with k_i8 times (q scale * ks[page]) times scale * log2(e) (fp32, rounded after each
+ * product), softmax in base 2, P rounded to bf16 for the P.V product (fp32 accumulation), v bf16.
+ * ids, block, n_ids, out (0 = bf16, 1 = fp32), lse (natural log, optional) and status as in
+ * ss_attention; out, q, k_i8, v 16-byte aligned; at most 4096 pages (Lk <= 262144). Replaces the
+ * INT8 attention of migration/unified_router/opt23/attention.py:30-58 (`_shared`, INT8=True) and
+ * the Sparge call of opt24/sparge.py:38-43 / opt24/pipeline.py:23-25. Plain (non-ring) windows. */
+int ss_attention_i8(const void *q, const int8_t *k_i8, const float *ks, const void *v, const int32_t *ids,
+                    int H, int Lq, int Lk, int block, int n_ids, float scale,
+                    void *out, int out_dtype, float *lse, int *status, void *stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial attention results.                                             */

@@ -320,7 +320,8 @@ def i8_logit_scale(scale: float) -> np.float32:
 
 def i8_logits(qi_rows, qs_rows, ki_tok, ks_tok, c):
     """fp32 base-2 logits of ``_shared`` (:47-48): ((int32 dot) * (qs * ks)) * c, each product rounded."""
-    dot = qi_rows.astype(np.int32) @ ki_tok.astype(np.int32).T            # exact (|dot| < 2^24)
+    # integer dot products, exact in float64 (|dot| <= 127 * 127 * 128 < 2^24) and so in fp32
+    dot = qi_rows.astype(np.float64) @ ki_tok.astype(np.float64).T
     t = (qs_rows[:, None].astype(np.float32) * ks_tok[None, :].astype(np.float32)).astype(np.float32)
     return ((dot.astype(np.float32) * t).astype(np.float32) * np.float32(c)).astype(np.float32)
 

@@ -7,6 +7,7 @@ namespace ss {
 
 int attention_prepare(int device);
 int router_prepare(int device);
+int attention_i8_prepare(int device);
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -51,6 +52,21 @@ int encode_tmap_2d_bf16_rows(CUtensorMap *map, const void *base, uint64_t inner,
     return encode_2d_bf16(map, base, inner, outer, row_stride_bytes, box_inner, box_outer, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// 2-D uint8 tensor map over a row-major [outer][inner] view (int8 data), 128-byte swizzle.
+int encode_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                      uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return SS_ERR_DRIVER;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_stride_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : SS_ERR_DRIVER;
+}
+
 using CtxGetCurrentFn = CUresult (*)(CUcontext *);
 
 // The calling thread's current CUDA context (nullptr if none), through the driver entry point so
@@ -81,6 +97,8 @@ extern "C" int ss_prepare_device(void) {
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return (int)e;
     int rc = ss::attention_prepare(device);
+    if (rc) return rc;
+    rc = ss::attention_i8_prepare(device);
     if (rc) return rc;
     return ss::router_prepare(device);
 }

@@ -423,6 +423,71 @@ def sparse_attention_heads(q, k, v, ids, outs, *, out_heads: int, h0: int, block
         DeviceStatus.check(q.device)
 
 
+PAGE_TOKENS = 64
+
+
+def quant_pages(Lk: int) -> int:
+    """Key pages (64 tokens, the last one possibly partial) of a window of Lk tokens."""
+    return (Lk + PAGE_TOKENS - 1) // PAGE_TOKENS
+
+
+def quant_k_pages(k, *, p0: int = 0, p1: int | None = None, k_i8: torch.Tensor | None = None,
+                  ks: torch.Tensor | None = None):
+    """Quantise key pages [p0, p1) of k [Lk,H,128] bf16 to int8 (``ss_quant_k_pages``).
+
+    Returns (k_i8 [Lk,H,128] int8, ks [H,ceil(Lk/64)] fp32); pass the previous buffers to update
+    only some pages (history pages once per commit, the current chunk's pages per call, as
+    ``Quantized.history`` / ``.current`` of migration/unified_router/opt23/attention.py:16-28).
+    """
+    k = _tokens(k, "k")
+    Lk, H, _ = k.shape
+    npg = quant_pages(Lk)
+    p1 = npg if p1 is None else p1
+    if k_i8 is None:
+        k_i8 = torch.empty((Lk, H, HEAD_DIM), dtype=torch.int8, device=k.device)
+    if ks is None:
+        ks = torch.empty((H, npg), dtype=torch.float32, device=k.device)
+    _require(k_i8.shape == k.shape and k_i8.dtype == torch.int8 and k_i8.is_contiguous(), "bad k_i8 buffer")
+    _require(ks.shape == (H, npg) and ks.dtype == torch.float32 and ks.is_contiguous(), "bad ks buffer")
+    rc = lib().ss_quant_k_pages(_p(k), H, Lk, p0, p1, _p(k_i8), _p(ks), _stream(k.device))
+    check(rc, "ss_quant_k_pages")
+    return k_i8, ks
+
+
+def sparse_attention_i8(q, k_i8, ks, v, ids, *, block: int = 64, scale: float | None = None,
+                        out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False,
+                        out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False):
+    """INT8-QK block-sparse attention (``ss_attention_i8``): ``sparse_attention`` with the scores
+    taken from int8 Q (32-row groups, quantised in the kernel) and int8 K pages (``quant_k_pages``),
+    as the reference's INT8 path (migration/unified_router/opt23/attention.py:30-58)."""
+    q = _tokens(q, "q")
+    v = _tokens(v, "v")
+    Lq, H, D = q.shape
+    Lk = v.shape[0]
+    _require(k_i8.is_cuda and k_i8.dtype == torch.int8 and k_i8.shape == v.shape and k_i8.is_contiguous(),
+             "k_i8 must be int8 CUDA [Lk,H,128] like v")
+    _require(ks.is_cuda and ks.dtype == torch.float32 and ks.shape == (H, quant_pages(Lk)) and ks.is_contiguous(),
+             f"ks must be fp32 CUDA [H,{quant_pages(Lk)}]")
+    _require(ids.is_cuda and ids.dtype == torch.int32 and ids.dim() == 3, "ids must be int32 CUDA [H,qb,n]")
+    _require(ids.shape[0] == H and ids.shape[1] == nblocks(Lq, block), f"ids must be [H,{nblocks(Lq, block)},n]")
+    ids = ids.contiguous()
+    _require(out_dtype in (torch.bfloat16, torch.float32), "out_dtype must be bf16 or fp32")
+    scale = 1.0 / math.sqrt(D) if scale is None else float(scale)
+    if out is None:
+        out = torch.empty((Lq, H, D), dtype=out_dtype, device=q.device)
+    _require(out.shape == (Lq, H, D) and out.dtype == out_dtype and out.is_contiguous(), "bad out buffer")
+    if return_lse and lse is None:
+        lse = torch.empty((H, Lq), dtype=torch.float32, device=q.device)
+    status = DeviceStatus.word(q.device)
+    rc = lib().ss_attention_i8(_p(q), _p(k_i8), _p(ks), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale,
+                               _p(out), 1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
+                               _p(status), _stream(q.device))
+    check(rc, "ss_attention_i8")
+    if validate:
+        DeviceStatus.check(q.device)
+    return (out, lse) if return_lse else out
+
+
 def exact(q, k, v, ids, workspace: Workspace | None = None):
     """Reference mirror: q/k/v [1,N,H,D] bf16, ids [H, N//64, count] -> (O fp32 [1,N,H,D], lse [H,N])."""
     ws = _ws(workspace, q.device)

@@ -9,7 +9,7 @@ here unmodified under Triton's CPU interpreter (TRITON_INTERPRET=1), with one su
 interpreter cannot call libdevice, so ``nearbyint`` (round half to even) is replaced by an exact
 round-half-even written with floor. V is passed as fp16, the type the reference's Sparge path
 gives it (opt24/sparge.py:41 ``self.v=self.pv.half()``): the interpreter's P.V product does not
-handle bf16. Pages are made window-global by passing SEG = (number of pages) * 64, so page p covers
+handle bf16. V is drawn in bf16 (tiny values zeroed), so its values are exact in both types. Pages are made window-global by passing SEG = (number of pages) * 64, so page p covers
 tokens [64p, 64p + 64), as in this library.
 
 The reference is read, never modified, and is not needed at test time (the .npz is committed).
@@ -53,7 +53,9 @@ def main():
     k = torch.randn((H, NK, 128), generator=g).bfloat16()
     k[1, 64:128] = 0                                 # an all-zero page: scale clamps to 1e-10
     k[0, :7, :5] *= 40                               # outliers set a page's scale
-    v = torch.randn((H, NK, 128), generator=g).half()
+    v = torch.randn((H, NK, 128), generator=g).bfloat16()
+    v[v.abs() < 1e-3] = 0                           # every value exact in both bf16 and fp16
+    v = v.half()
     q = torch.randn((H, N, 128), generator=g).bfloat16()
     q[0, 32:64] = 0                                  # an all-zero query group
     q[1, :32] *= 3
