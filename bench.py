@@ -18,7 +18,8 @@ self-attention layer, next to the same model with dense attention; and ``other_c
 ``--no-configs``): router + attention at the shapes of configs 1, 4 and a grid of config 5;
 ``hbm_kernels``: the rolling cache append, the 8-part LSE merge and the anchor rebase, each alone;
 ``e2e`` (the plugin call with the whole KV window uploaded from the host every step) and
-``e2e_streaming`` (the window resident in a KVCache, only the chunk's q/k/v uploaded per step).
+``e2e_streaming`` (the window resident in a KVCache, only the chunk's q/k/v uploaded per step);
+``int8_qk`` (unless ``--no-int8``): the INT8-QK attention path on config 2's inputs and ids.
 """
 from __future__ import annotations
 
@@ -961,6 +962,70 @@ def e2e_streaming_bench(dev, sets, sparse, flops, args, world: int, stream) -> d
                    "resident across calls"}
 
 
+def int8_bench(dev, sets, ids_buf, flops, args, peak) -> dict:
+    """The INT8-QK path (migration/unified_router/opt23/attention.py, INT8=True) at
+    config 2 on the bench's own inputs and router ids: the history's key pages quantised once per
+    commit, the pages the current chunk touches quantised per call, then ss_attention_i8. Each stage
+    is one CUDA graph per input set, replayed alternately (two 215 MB sets, > L2); its output is
+    compared with the bf16 kernel's on the same ids (the difference is the int8 rounding of Q and K)."""
+    from streaming_sparse_b200 import ops
+    npg = ops.quant_pages(LK)
+    p_cur = (LK - LQ) // 64                       # first page holding a current-chunk token
+    qk = [ops.quant_k_pages(s_[1]) for s_ in sets]
+    out8 = [torch.empty((LQ, H, D), dtype=torch.bfloat16, device=dev) for _ in sets]
+    ws = ops.Workspace()
+
+    def commit(s):
+        ops.quant_k_pages(sets[s][1], p0=0, p1=p_cur, k_i8=qk[s][0], ks=qk[s][1])
+
+    def quant_chunk(s):
+        ops.quant_k_pages(sets[s][1], p0=p_cur, p1=npg, k_i8=qk[s][0], ks=qk[s][1])
+
+    def attend(s):
+        q, k, v, _, _ = sets[s]
+        ops.sparse_attention_i8(q, qk[s][0], qk[s][1], v, ids_buf[s], block=BLOCK, out=out8[s], workspace=ws)
+
+    for s in range(2):
+        commit(s), quant_chunk(s), attend(s)
+    torch.cuda.synchronize()
+    ops.DeviceStatus.check(dev)
+    graphs = {}
+    for name, fn in (("commit", commit), ("quant_chunk", quant_chunk), ("attend", attend)):
+        graphs[name] = []
+        for s in range(2):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn(s)
+            graphs[name].append(g)
+    n = max(10, min(args.steps, 100))
+    res = {}
+    for name, gs in graphs.items():
+        for i in range(max(3, args.warmup)):
+            gs[i % 2].replay()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        torch.cuda.synchronize()
+        for i in range(n):
+            evs[i][0].record()
+            gs[i % 2].replay()
+            evs[i][1].record()
+        torch.cuda.synchronize()
+        res[name] = statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e3
+    ref = torch.empty((LQ, H, D), dtype=torch.float32, device=dev)
+    dif = []
+    for s in range(2):
+        q, k, v, _, _ = sets[s]
+        ops.sparse_attention(q, k, v, ids_buf[s], block=BLOCK, out=ref, out_dtype=torch.float32)
+        d = out8[s].float() - ref
+        dif.append((float(d.abs().max()), float((d * d).sum() / (ref * ref).sum())))
+    eff = statistics.mean(flops)
+    tf = eff / (res["attend"] * 1e-6) / 1e12
+    return {"attention_us": res["attend"], "quant_chunk_us": res["quant_chunk"], "commit_quant_us": res["commit"],
+            "pieces_workspace_bytes": ops.attention_i8_workspace_bytes(H, LQ),
+            "tflops": tf, "frac_of_peak": tf / peak, "step_tflops": eff / ((res["attend"] + res["quant_chunk"]) * 1e-6) / 1e12,
+            "vs_bf16_max_abs": max(x[0] for x in dif), "vs_bf16_nmse": max(x[1] for x in dif),
+            "kernel": "ss::i8::attention_i8_kernel (tcgen05.mma kind::i8 scores, kind::f16 P.V)"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch.distributed as dist
     from streaming_sparse_b200 import ops
@@ -1170,6 +1235,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     _, hbm_gbs, _ = peaks()
     hbm_k = hbm_kernels_bench(dev, args, hbm_gbs)
 
+    # ---- the INT8-QK path on the same inputs and ids
+    int8 = None if args.no_int8 else int8_bench(dev, sets, ids_buf, flops, args, peaks()[0])
+
     # ---- config 4's chunk-layer split over the GPUs (KV blocks / heads), N > 1
     sharded = sharded_bench(dev, args, rank, world) if world > 1 and not args.no_sharded else None
 
@@ -1189,7 +1257,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # Detail records first, one JSON object per line; the last line is the bench line proper,
     # short enough that a reader keeping only the tail of stdout still sees every headline figure.
     details = {"e2e_streaming": streaming, "cache_append": dict(cache, hbm_peak_gbs=hbm, frac=cache["gbs"] / hbm),
-               "hbm_kernels": hbm_k, "rollout": rollout, "other_configs": other, "sharded": sharded}
+               "hbm_kernels": hbm_k, "rollout": rollout, "other_configs": other, "sharded": sharded, "int8_qk": int8}
     for name, rec in details.items():
         if rec is not None:
             print(json.dumps({"detail": name, "record": rec}), flush=True)
@@ -1232,6 +1300,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             r(rollout["config4_long_horizon"]["value"], 2),
             "config4_ring_frames_s": None if rollout["config4_long_horizon"] is None else
             r(rollout["config4_long_horizon"]["ring_cache"]["value"], 2)},
+        "int8_qk": None if int8 is None else {
+            "attention_us": r(int8["attention_us"]), "quant_chunk_us": r(int8["quant_chunk_us"]),
+            "tflops": r(int8["tflops"]), "frac": r(int8["frac_of_peak"], 3),
+            "vs_bf16_nmse": int8["vs_bf16_nmse"]},
         "configs_frac": None if other is None else {o["short"]: [r(o["us"]), r(o["frac_of_peak"], 3)] for o in other},
         "sharded": None if sharded is None else {
             "c4_1gpu_us": r(sharded["single_gpu_us"]), "c4_1gpu_cached_us": r(sharded["single_gpu_cached_us"]),
@@ -1270,6 +1342,7 @@ def main():
     ap.add_argument("--ref-pairs", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rollout", action="store_true", help="skip the config-3 rollout measurement")
+    ap.add_argument("--no-int8", action="store_true", help="skip the INT8-QK path measurement")
     ap.add_argument("--no-configs", action="store_true", help="skip the per-shape measurements of configs 1, 4, 5")
     ap.add_argument("--no-sharded", action="store_true", help="skip the KV-block / head sharded config-4 chunk-layer")
     ap.add_argument("--only-hbm-kernels", action="store_true",

@@ -64,7 +64,8 @@ SIGNATURES = {
     "ss_attention_max_ids": ([_I, _I, ctypes.POINTER(_I)], _I),
     "ss_attention_workspace_bytes": ([_I, _I, ctypes.POINTER(_SZ)], _I),
     "ss_quant_k_pages": ([_P, _I, _I, _I, _I, _P, _P, _P], _I),
-    "ss_attention_i8": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P], _I),
+    "ss_attention_i8_workspace_bytes": ([_I, _I, ctypes.POINTER(_SZ)], _I),
+    "ss_attention_i8": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _SZ, _P], _I),
     "ss_attention_ws": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _SZ, _P], _I),
     "ss_lse_merge": ([_P, _P, _I, _I, _I, _P, _I, _P, _P], _I),
     "ss_cache_append": ([_P, _P, _I, _I, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _I, ctypes.POINTER(_I64), _P], _I),

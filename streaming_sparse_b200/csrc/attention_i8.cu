@@ -22,6 +22,7 @@
 // blocks' pages in ascending order, each with a bit per query block, and a row ignores the pages
 // its own block did not select. Every wait is bounded; on expiry SS_DEV_TIMEOUT is reported, loads
 // and MMAs in flight are drained and TMEM is freed.
+#include <climits>
 #include <mutex>
 
 #include "common.cuh"
@@ -68,6 +69,9 @@ struct Params {
     int *status;
     int H, Lq, Lk, block, n_ids, nqb, nkb, npages, out_fp32;
     float c;   // scale * log2(e)
+    int pieces;        // > 1: CTA z of a tile takes steps [z n / pieces, (z + 1) n / pieces)
+    float *ws_o;       // pieces > 1: [pieces][Lq][H][128] fp32 normalised partials
+    float *ws_lse;     //             [pieces][H][Lq] natural-log LSE (-inf: no token)
 };
 
 // D[tmem] (+)= A[smem] * B[smem], kind::i8 (s8 inputs, s32 accumulate)
@@ -91,6 +95,7 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 __device__ __forceinline__ bool warp_all(bool ok) { return __all_sync(0xffffffffu, ok); }
+
 
 // A wait that ignores the abort flag (used only to drain work this CTA itself issued).
 __device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity) {
@@ -181,7 +186,11 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         if (lane == 0) misc[1] = (uint32_t)base;
     }
     __syncthreads();
-    const int n = (int)misc[1];
+    const int n_all = (int)misc[1];
+    const int z = blockIdx.z;
+    const int s_lo = (int)(((long)z * n_all) / p.pieces), s_hi = (int)(((long)(z + 1) * n_all) / p.pieces);
+    const int n = s_hi - s_lo;                  // this CTA's steps: list[s_lo .. s_hi)
+    const uint32_t *steps = list + s_lo;
     const uint32_t tmem = misc[0];
     const uint32_t sQ = sbase + OFF_Q;
 
@@ -233,69 +242,92 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         const float *ksh = p.ks + (size_t)h * p.npages;
         float m_run = -INFINITY, l = 0.f;
         bool ok = true;
-        float ks_next = n > 0 ? __ldg(ksh + (list[0] & 0xFFFFu)) : 0.f;
+        float ks_next = n > 0 ? __ldg(ksh + (steps[0] & 0xFFFFu)) : 0.f;
         for (int s = 0; s < n && ok; ++s) {
-            const uint32_t e = list[s];
+            const uint32_t e = steps[s];
             const int page = (int)(e & 0xFFFFu);
             const bool sel = (e >> (16 + qi)) & 1u;
             const float ksv = ks_next;
-            if (s + 1 < n) ks_next = __ldg(ksh + (list[s + 1] & 0xFFFFu));
+            if (s + 1 < n) ks_next = __ldg(ksh + (steps[s + 1] & 0xFFFFu));
             const int b = s & 1;
             ok = warp_all(mbar_wait(bar(S_FULL + b), (s >> 1) & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            float sv[64];
-            tmem_ld32(lane_base + 64 * b, sv);
-            tmem_ld32(lane_base + 64 * b + 32, sv + 32);
-            tmem_wait_ld();
-            tmem_ld_fence32(sv);
-            tmem_ld_fence32(sv + 32);
-            const int nvalid = min(PAGE, p.Lk - page * PAGE);
-            const float t = __fmul_rn(qs, ksv);
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-                const float y = __fmul_rn(__fmul_rn((float)__float_as_int(sv[j]), t), p.c);
-                sv[j] = (sel && j < nvalid) ? y : -INFINITY;
-                mx = fmaxf(mx, sv[j]);
-            }
-            // raise the running maximum only when it grows by more than 8 (P stays <= 256)
-            float alpha = 1.f;
-            const bool raise = mx > m_run + 8.f;
-            if (raise) {
-                if (m_run != -INFINITY) alpha = ex2(m_run - mx);
-                m_run = mx;
-            }
-            if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                // O holds PV(0 .. s-1): wait for the last one, then rescale this warp's rows
-                ok = warp_all(mbar_wait(bar(PV_DONE + ((s - 1) & 1)), ((s - 1) >> 1) & 1, abort_flag));
-                if (!ok) break;
-                tc_fence_after();
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    float ov[32];
-                    tmem_ld32(lane_base + TMEM_O + 32 * cc, ov);
-                    tmem_wait_ld();
-                    tmem_ld_fence32(ov);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) ov[j] *= alpha;
-                    tmem_st32(lane_base + TMEM_O + 32 * cc, ov);
-                    tmem_wait_st();
-                    tmem_st_fence32(ov);
-                }
-                l *= alpha;
-            }
             uint32_t pk[32];
-            float sum = 0.f;
-            const bool any = m_run != -INFINITY;
+            if (sel) {   // warp-uniform: a warp's 32 rows lie in one query block
+                float sv[64];
+                tmem_ld32(lane_base + 64 * b, sv);
+                tmem_ld32(lane_base + 64 * b + 32, sv + 32);
+                tmem_wait_ld();
+                tmem_ld_fence32(sv);
+                tmem_ld_fence32(sv + 32);
+                const int nvalid = min(PAGE, p.Lk - page * PAGE);
+                // logit = score * tc with tc = (qs * ks) * scale * log2(e) > 0, so the row's largest
+                // logit comes from its largest integer score
+                const float tc = __fmul_rn(__fmul_rn(qs, ksv), p.c);
+                int smax = INT_MIN;
+                if (nvalid == PAGE) {   // every page but a window's last: no bounds in the loops
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float p0 = any ? ex2(sv[2 * j] - m_run) : 0.f;
-                const float p1 = any ? ex2(sv[2 * j + 1] - m_run) : 0.f;
-                sum += p0 + p1;
-                pk[j] = pack_bf16x2(p0, p1);
+                    for (int j = 0; j < 63; j += 2)
+                        smax = __vimax3_s32(smax, __float_as_int(sv[j]), __float_as_int(sv[j + 1]));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 64; ++j)
+                        if (j < nvalid) smax = max(smax, __float_as_int(sv[j]));
+                }
+                const float mx = __fmul_rn((float)smax, tc);
+                // raise the running maximum only when it grows by more than 8 (P stays <= 256)
+                float alpha = 1.f;
+                if (mx > m_run + 8.f) {
+                    if (m_run != -INFINITY) alpha = ex2(m_run - mx);
+                    m_run = mx;
+                }
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    // O holds PV(0 .. s-1): wait for the last one, then rescale this warp's rows
+                    ok = warp_all(mbar_wait(bar(PV_DONE + ((s - 1) & 1)), ((s - 1) >> 1) & 1, abort_flag));
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        float ov[32];
+                        tmem_ld32(lane_base + TMEM_O + 32 * cc, ov);
+                        tmem_wait_ld();
+                        tmem_ld_fence32(ov);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) ov[j] *= alpha;
+                        tmem_st32(lane_base + TMEM_O + 32 * cc, ov);
+                        tmem_wait_st();
+                        tmem_st_fence32(ov);
+                    }
+                    l *= alpha;
+                }
+                const float neg = -m_run;
+                float sum0 = 0.f, sum1 = 0.f;
+                if (nvalid == PAGE) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float p0 = ex2(fmaf((float)__float_as_int(sv[2 * j]), tc, neg));
+                        const float p1 = ex2(fmaf((float)__float_as_int(sv[2 * j + 1]), tc, neg));
+                        sum0 += p0;
+                        sum1 += p1;
+                        pk[j] = pack_bf16x2(p0, p1);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float p0 = 2 * j < nvalid ? ex2(fmaf((float)__float_as_int(sv[2 * j]), tc, neg)) : 0.f;
+                        const float p1 =
+                            2 * j + 1 < nvalid ? ex2(fmaf((float)__float_as_int(sv[2 * j + 1]), tc, neg)) : 0.f;
+                        sum0 += p0;
+                        sum1 += p1;
+                        pk[j] = pack_bf16x2(p0, p1);
+                    }
+                }
+                l += sum0 + sum1;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) pk[j] = 0u;
             }
-            l += sum;
             tmem_st32(lane_base + 64 * b, reinterpret_cast<const float *>(pk));
             tmem_wait_st();
             tmem_st_fence32(reinterpret_cast<const float *>(pk));
@@ -317,7 +349,13 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 #pragma unroll
                     for (int j = 0; j < 32; ++j) ov[j] = 0.f;
                 }
-                if (live) {
+                if (live && p.pieces > 1) {
+                    float4 *dst = reinterpret_cast<float4 *>(p.ws_o + (((size_t)z * p.Lq + row) * p.H + h) * D + 32 * cc);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        dst[j] = make_float4(ov[4 * j] * inv, ov[4 * j + 1] * inv, ov[4 * j + 2] * inv,
+                                             ov[4 * j + 3] * inv);
+                } else if (live) {
                     if (p.out_fp32) {
                         float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) +
                                                                  ((size_t)row * p.H + h) * D + 32 * cc);
@@ -337,8 +375,9 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
                     }
                 }
             }
-            if (live && p.lse)
-                p.lse[(size_t)h * p.Lq + row] = l > 0.f ? (m_run + __log2f(l)) * 0.6931471805599453f : -INFINITY;
+            const float lse_row = l > 0.f ? (m_run + __log2f(l)) * 0.6931471805599453f : -INFINITY;
+            if (live && p.pieces > 1) p.ws_lse[((size_t)z * p.H + h) * p.Lq + row] = lse_row;
+            else if (live && p.lse) p.lse[(size_t)h * p.Lq + row] = lse_row;
         }
         if (!ok) report(p.status, SS_DEV_TIMEOUT);
     } else if (warp == 4) {
@@ -351,7 +390,7 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
                 ok = warp_all(mbar_wait(bar(KV_EMPTY + st), ((s / NSTAGE) - 1) & 1, abort_flag));
                 if (!ok) break;
             }
-            const int page = (int)(list[s] & 0xFFFFu);
+            const int page = (int)(steps[s] & 0xFFFFu);
             if (elect_one()) {
                 const uint32_t dst = sbase + OFF_STAGE + (uint32_t)st * STAGE_BYTES;
                 mbar_arrive_expect_tx(bar(KV_FULL + st), STAGE_BYTES);
@@ -479,6 +518,7 @@ quant_k_pages_kernel(const __nv_bfloat16 *k, int H, int Lk, int p0, int npages, 
 static std::mutex g_i8_mutex;
 static int g_i8_configured[SS_MAX_DEVICES];
 static void *g_i8_ctx[SS_MAX_DEVICES];
+static int g_i8_nsm[SS_MAX_DEVICES];
 
 int attention_i8_prepare(int device) {
     if (device < 0 || device >= SS_MAX_DEVICES) return SS_ERR_DEVICE;
@@ -490,10 +530,31 @@ int attention_i8_prepare(int device) {
     cudaError_t e = cudaFuncSetAttribute(i8::attention_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)i8::SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
+    int nsm = 0;
+    e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return (int)e;
+    g_i8_nsm[device] = nsm;
     g_i8_ctx[device] = ctx;
     g_i8_configured[device] = 1;
     return 0;
 }
+
+// Pieces per tile (1-4): the fewest that minimise the waves of two-CTA-per-SM slots a tile-time
+// each, e.g. 444 tiles on 148 SMs: whole tiles take 2 waves, halves 3 waves of half a tile (1.5).
+static int i8_pieces(long T, int nsm) {
+    const long slots = 2L * nsm;
+    int best = 1;
+    double cost = (double)((T + slots - 1) / slots);
+    for (int P = 2; P <= 4; ++P) {
+        const double c = (double)((P * T + slots - 1) / slots) / P;
+        if (c < cost - 1e-9) {
+            cost = c;
+            best = P;
+        }
+    }
+    return best;
+}
+static size_t i8_ws_bytes(int P, int H, int Lq) { return (size_t)P * Lq * H * (i8::D + 1) * sizeof(float); }
 
 int encode_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
@@ -513,9 +574,21 @@ extern "C" int ss_quant_k_pages(const void *k, int H, int Lk, int p0, int p1, in
     return (int)cudaGetLastError();
 }
 
+extern "C" int ss_attention_i8_workspace_bytes(int H, int Lq, size_t *bytes) {
+    if (!bytes || H <= 0 || Lq <= 0) return SS_ERR_SHAPE;
+    int device;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return (int)e;
+    int rc = ss::attention_i8_prepare(device);
+    if (rc) return rc;
+    const int P = ss::i8_pieces((long)((Lq + 127) / 128) * H, ss::g_i8_nsm[device]);
+    *bytes = P > 1 ? ss::i8_ws_bytes(P, H, Lq) : 0;
+    return 0;
+}
+
 extern "C" int ss_attention_i8(const void *q, const int8_t *k_i8, const float *ks, const void *v, const int32_t *ids,
                                int H, int Lq, int Lk, int block, int n_ids, float scale, void *out, int out_dtype,
-                               float *lse, int *status, void *stream) {
+                               float *lse, int *status, void *workspace, size_t workspace_bytes, void *stream) {
     using namespace ss::i8;
     if (!q || !k_i8 || !ks || !v || !ids || !out) return SS_ERR_POINTER;
     if (H <= 0 || Lq <= 0 || Lk <= 0 || n_ids <= 0 || (block != 64 && block != 128) || H > 65535) return SS_ERR_SHAPE;
@@ -549,14 +622,22 @@ extern "C" int ss_attention_i8(const void *q, const int8_t *k_i8, const float *k
     prm.npages = npages;
     prm.out_fp32 = out_dtype;
     prm.c = (float)((double)scale * 1.4426950408889634);
+    const unsigned ntiles = (unsigned)((Lq + 127) / 128);
+    int P = workspace ? ss::i8_pieces((long)ntiles * H, ss::g_i8_nsm[device]) : 1;
+    if (P > 1 && workspace_bytes < ss::i8_ws_bytes(P, H, Lq)) return SS_ERR_WORKSPACE;
+    if (P > 1 && (reinterpret_cast<uintptr_t>(workspace) & 255u)) return SS_ERR_POINTER;
+    prm.pieces = P;
+    prm.ws_o = P > 1 ? static_cast<float *>(workspace) : nullptr;
+    prm.ws_lse = P > 1 ? prm.ws_o + (size_t)P * Lq * H * D : nullptr;
 
     CUtensorMap tk, tv;
     if (ss::encode_tmap_2d_u8(&tk, k_i8, (uint64_t)H * D, (uint64_t)Lk, (uint64_t)H * D, 128, PAGE))
         return SS_ERR_DRIVER;
     if (ss::encode_tmap_2d_bf16(&tv, v, (uint64_t)H * D, (uint64_t)Lk, (uint64_t)H * D * 2, 64, PAGE))
         return SS_ERR_DRIVER;
-    const unsigned ntiles = (unsigned)((Lq + 127) / 128);
-    attention_i8_kernel<<<dim3(ntiles, (unsigned)H), NTHREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tk, tv,
-                                                                                                                prm);
-    return (int)cudaGetLastError();
+    attention_i8_kernel<<<dim3(ntiles, (unsigned)H, (unsigned)P), NTHREADS, SMEM_BYTES,
+                          static_cast<cudaStream_t>(stream)>>>(tk, tv, prm);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || P == 1) return (int)e;
+    return ss_lse_merge(prm.ws_o, prm.ws_lse, P, H, Lq, out, out_dtype, lse, stream);
 }

@@ -454,12 +454,22 @@ def quant_k_pages(k, *, p0: int = 0, p1: int | None = None, k_i8: torch.Tensor |
     return k_i8, ks
 
 
+def attention_i8_workspace_bytes(H: int, Lq: int) -> int:
+    """Workspace bytes ss_attention_i8 uses to split tiles on the current device (0: never splits)."""
+    n = ctypes.c_size_t(0)
+    check(lib().ss_attention_i8_workspace_bytes(H, Lq, ctypes.byref(n)), "ss_attention_i8_workspace_bytes")
+    return int(n.value)
+
+
 def sparse_attention_i8(q, k_i8, ks, v, ids, *, block: int = 64, scale: float | None = None,
                         out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False,
-                        out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False):
+                        out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False,
+                        workspace: Workspace | None = None, split: bool = True):
     """INT8-QK block-sparse attention (``ss_attention_i8``): ``sparse_attention`` with the scores
     taken from int8 Q (32-row groups, quantised in the kernel) and int8 K pages (``quant_k_pages``),
-    as the reference's INT8 path (migration/unified_router/opt23/attention.py:30-58)."""
+    as the reference's INT8 path (migration/unified_router/opt23/attention.py:30-58). With ``split``
+    (default) a problem that would leave a partial wave cuts its tiles into equal pieces merged by
+    LSE (workspace from ``workspace``)."""
     q = _tokens(q, "q")
     v = _tokens(v, "v")
     Lq, H, D = q.shape
@@ -479,9 +489,11 @@ def sparse_attention_i8(q, k_i8, ks, v, ids, *, block: int = 64, scale: float | 
     if return_lse and lse is None:
         lse = torch.empty((H, Lq), dtype=torch.float32, device=q.device)
     status = DeviceStatus.word(q.device)
+    nws = attention_i8_workspace_bytes(H, Lq) if split else 0
+    ws = _ws(workspace, q.device).tensor("attention_i8_split", (nws,), q.device, torch.uint8) if nws else None
     rc = lib().ss_attention_i8(_p(q), _p(k_i8), _p(ks), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale,
                                _p(out), 1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
-                               _p(status), _stream(q.device))
+                               _p(status), _p(ws), nws, _stream(q.device))
     check(rc, "ss_attention_i8")
     if validate:
         DeviceStatus.check(q.device)

@@ -23,11 +23,11 @@ def _quant(k):
     return k_i8.cpu().numpy(), ks.cpu().numpy()
 
 
-def _attend_i8(q, k, v, ids, block, out_dtype=torch.bfloat16):
+def _attend_i8(q, k, v, ids, block, out_dtype=torch.bfloat16, split=True):
     from streaming_sparse_b200 import ops
     k_i8, ks = ops.quant_k_pages(k.to(DEV))
     out, lse = ops.sparse_attention_i8(q.to(DEV), k_i8, ks, v.to(DEV), torch.as_tensor(ids).to(DEV), block=block,
-                                       out_dtype=out_dtype, return_lse=True, validate=True)
+                                       out_dtype=out_dtype, return_lse=True, validate=True, split=split)
     torch.cuda.synchronize()
     return out.float().cpu().numpy(), lse.cpu().numpy(), k_i8.cpu().numpy(), ks.cpu().numpy()
 
@@ -85,11 +85,14 @@ def test_golden_reference_kernel():
     (64, 4096, 1, 64, 64, 0, torch.float32),      # every block listed: 64 steps
     (1, 65, 1, 64, 2, 0, torch.float32),          # one query row, a 1-token last page
 ])
-def test_attention_i8_random_lists(Lq, Lk, H, block, n, pad, out_dtype):
+@pytest.mark.parametrize("split", [True, False])
+def test_attention_i8_random_lists(Lq, Lk, H, block, n, pad, out_dtype, split):
+    """split: these small problems cut every tile into pieces (some of them empty) merged by LSE;
+    without it each tile is one CTA."""
     q, k, v = qkv(13, Lq, Lk, H)
     rng = np.random.default_rng(Lq + Lk)
     ids = _random_ids(rng, H, oracle.nblocks(Lq, block), oracle.nblocks(Lk, block), n, pad)
-    out, lse, ki, ks = _attend_i8(q, k, v, ids, block, out_dtype)
+    out, lse, ki, ks = _attend_i8(q, k, v, ids, block, out_dtype, split)
     ref, ref_lse = oracle.attention_i8(np32(q), ki, ks, np32(v), ids, block)
     assert_attention_close(out, ref)
     assert np.abs(lse - ref_lse).max() <= 2e-3
@@ -103,10 +106,11 @@ def test_attention_i8_routed_and_empty_lists():
     wq, wk = router_weights(17, H)
     ids = ops.route(q.to(DEV), k.to(DEV), wq.to(DEV), wk.to(DEV), block=64, extra=3, validate=True).cpu().numpy()
     ids[1, 2] = -1
-    out, lse, ki, ks = _attend_i8(q, k, v, ids, 64, torch.float32)
-    ref, ref_lse = oracle.attention_i8(np32(q), ki, ks, np32(v), ids, 64)
-    assert np.all(out[128:192, 1] == 0) and np.all(np.isneginf(lse[1, 128:192]))
-    assert_attention_close(out, ref)
+    for split in (True, False):
+        out, lse, ki, ks = _attend_i8(q, k, v, ids, 64, torch.float32, split)
+        ref, ref_lse = oracle.attention_i8(np32(q), ki, ks, np32(v), ids, 64)
+        assert np.all(out[128:192, 1] == 0) and np.all(np.isneginf(lse[1, 128:192]))
+        assert_attention_close(out, ref)
 
 
 def test_attention_i8_config2_sampled():
@@ -132,3 +136,8 @@ def test_attention_i8_config2_sampled():
     assert_attention_close(got, ref)
     d = (out - dense).abs()
     assert float(d.mean()) < 5e-3, float(d.mean())
+    # 444 tiles: the default call cuts them in pieces (each piece rounds P against its own running
+    # maximum); the whole-tile call meets the same bound
+    whole = ops.sparse_attention_i8(qd, k_i8, ks, vd, ids, block=64, out_dtype=torch.float32, split=False)
+    assert ops.attention_i8_workspace_bytes(H, Lq) > 0
+    assert_attention_close(whole.cpu().numpy(), ref)
