@@ -96,6 +96,23 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 }
 __device__ __forceinline__ bool warp_all(bool ok) { return __all_sync(0xffffffffu, ok); }
 
+// two fp32 lanes in one 64-bit register: fma.rn.f32x2 / add.rn.f32x2 (two IEEE operations each)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float f2_lo(uint64_t x) { return __uint_as_float((uint32_t)x); }
+__device__ __forceinline__ float f2_hi(uint64_t x) { return __uint_as_float((uint32_t)(x >> 32)); }
+
 
 // A wait that ignores the abort flag (used only to drain work this CTA itself issued).
 __device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity) {
@@ -303,15 +320,25 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
                 }
                 const float neg = -m_run;
                 float sum0 = 0.f, sum1 = 0.f;
-                if (nvalid == PAGE) {
+                if (nvalid == PAGE) {   // packed: one fma and one add instruction per two scores
+                    const uint64_t tc2 = f2_pack(tc, tc), nb2 = f2_pack(neg, neg);
+                    uint64_t sa = 0ull, sb = 0ull;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float p0 = ex2(fmaf((float)__float_as_int(sv[2 * j]), tc, neg));
-                        const float p1 = ex2(fmaf((float)__float_as_int(sv[2 * j + 1]), tc, neg));
-                        sum0 += p0;
-                        sum1 += p1;
-                        pk[j] = pack_bf16x2(p0, p1);
+                    for (int c = 0; c < 64; c += 4) {
+                        const uint64_t x0 = f2_fma(f2_pack((float)__float_as_int(sv[c]), (float)__float_as_int(sv[c + 1])),
+                                                   tc2, nb2);
+                        const uint64_t x1 = f2_fma(
+                            f2_pack((float)__float_as_int(sv[c + 2]), (float)__float_as_int(sv[c + 3])), tc2, nb2);
+                        const float p0 = ex2(f2_lo(x0)), p1 = ex2(f2_hi(x0));
+                        const float p2 = ex2(f2_lo(x1)), p3 = ex2(f2_hi(x1));
+                        sa = f2_add(sa, f2_pack(p0, p1));
+                        sb = f2_add(sb, f2_pack(p2, p3));
+                        pk[c >> 1] = pack_bf16x2(p0, p1);
+                        pk[(c >> 1) + 1] = pack_bf16x2(p2, p3);
                     }
+                    const uint64_t st2 = f2_add(sa, sb);
+                    sum0 = f2_lo(st2);
+                    sum1 = f2_hi(st2);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
