@@ -28,7 +28,10 @@ class RouterConfig:
 
     Exactly one of ``topk`` (fixed count outside the forced set) or ``density`` is used;
     ``rule`` picks how ``density`` becomes a count (see ``ops.budget``). ``fast`` scores the blocks
-    on the tensor cores (``ops.route(..., fast=True)``; same ids, proj_dim 32 or 64).
+    on the tensor cores (``ops.route(..., fast=True)``; same ids, proj_dim 32 or 64). ``int8`` runs
+    the attention on the INT8-QK path (``ops.sparse_attention_i8``; the reference's
+    ``attention(..., int8=True)``, migration/unified_router/opt23/attention.py:60-69), plain
+    (non-ring) windows only.
     """
 
     block: int = 64
@@ -38,6 +41,7 @@ class RouterConfig:
     sink_tokens: int = 0
     proj_dim: int = 64
     fast: bool = False
+    int8: bool = False
 
     def extra(self, Lq: int, Lk: int) -> int:
         kb = ops.nblocks(Lk, self.block)
@@ -69,6 +73,7 @@ class SparseAttention:
         self.last_ids = None
         self.calls = 0
         self._caches = {}           # k-cache storage address -> attached KVCache
+        self._i8 = {}               # id(KVCache) -> [k_i8, ks, (history tag, Lk)] of the INT8-QK path
 
     def attach(self, cache) -> None:
         """Let calls whose k is this ``KVCache``'s visible window reuse its history's pooled key
@@ -106,6 +111,28 @@ class SparseAttention:
         keys.mark(tag, ops.history_blocks(Lq, Lk, c.block))
         return ids
 
+    def int8_keys(self, q: torch.Tensor, k: torch.Tensor, cache=None):
+        """int8 key pages and their scales for the window k (``ops.quant_k_pages``). With ``cache``
+        (the ``KVCache`` whose window is k), pages wholly before the current chunk are quantised
+        once per history tag and window length, as the reference's ``Quantized.history`` runs once
+        per commit (migration/unified_router/opt23/pipeline.py); the current chunk's pages on every
+        call."""
+        Lq, Lk, H = q.shape[0], k.shape[0], k.shape[1]
+        npg = ops.quant_pages(Lk)
+        if cache is None:
+            k_i8 = self.workspace.tensor("k_i8", tuple(k.shape), k.device, torch.int8)
+            ks = self.workspace.tensor("k_i8_scales", (H, npg), k.device, torch.float32)
+            return ops.quant_k_pages(k, k_i8=k_i8, ks=ks)
+        key = (cache.history_tag(), Lk)
+        ent = self._i8.get(id(cache))
+        if ent is None or ent[0].shape != k.shape:
+            ent = self._i8[id(cache)] = [torch.empty(k.shape, dtype=torch.int8, device=k.device),
+                                         torch.empty((H, npg), dtype=torch.float32, device=k.device), None]
+        p0 = (Lk - Lq) // ops.PAGE_TOKENS if ent[2] == key else 0
+        ops.quant_k_pages(k, p0=p0, k_i8=ent[0], ks=ent[1])
+        ent[2] = key
+        return ent[0], ent[1]
+
     def _dense_ids(self, H: int, Lq: int, Lk: int, device) -> torch.Tensor:
         c = self.config
         qb, kb = ops.nblocks(Lq, c.block), ops.nblocks(Lk, c.block)
@@ -127,6 +154,12 @@ class SparseAttention:
         ids = self._dense_ids(H, Lq, Lk, q.device) if self.dense else self.route(q, k, cache)
         self.last_ids = ids
         self.calls += 1
+        if self.config.int8:
+            if ring is not None:
+                raise ValueError("the INT8-QK path takes plain (non-ring) KV windows")
+            k_i8, ks = self.int8_keys(q, k, cache)
+            return ops.sparse_attention_i8(q, k_i8, ks, v, ids, block=self.config.block, out=out,
+                                           validate=self.validate, workspace=self.workspace)
         return ops.sparse_attention(q, k, v, ids, block=self.config.block, out=out, validate=self.validate, ring=ring,
                                     Lk=Lk if ring is not None else None)
 

@@ -141,3 +141,44 @@ def test_attention_i8_config2_sampled():
     whole = ops.sparse_attention_i8(qd, k_i8, ks, vd, ids, block=64, out_dtype=torch.float32, split=False)
     assert ops.attention_i8_workspace_bytes(H, Lq) > 0
     assert_attention_close(whole.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("local,sink,block", [(-1, 0, 64), (5, 1, 128)])
+def test_plugin_int8_stream_reuses_history_pages(local, sink, block):
+    """RouterConfig(int8=True) through a KVCache stream (three calls per chunk, each rewriting the
+    chunk's rows; a roll of the window; an anchor rebase): the attached plugin quantises the
+    history's pages once per window and equals, bit for bit, a plugin that quantises every page on
+    every call; both stay within the int8 rounding of the bf16 path."""
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.cache import KVCache
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
+    H, ftok, fpc, chunks = 2, 300, 2, 5
+    cap = (local if local != -1 else fpc * chunks) * ftok
+    cache = KVCache(cap, num_heads=H, frame_tokens=ftok, local_attn_size=local, sink_size=sink, device=DEV)
+    wq, wk = router_weights(12, H)
+    cfg = RouterConfig(block=block, density=0.3, rule="rest" if sink else "total", sink_tokens=sink * ftok, int8=True)
+    sp = SparseAttention(wq.to(DEV), wk.to(DEV), cfg)
+    ref = SparseAttention(wq.to(DEV), wk.to(DEV), cfg)      # never attached: quantises every page per call
+    bf = SparseAttention(wq.to(DEV), wk.to(DEV), RouterConfig(block=block, density=0.3, rule=cfg.rule,
+                                                             sink_tokens=cfg.sink_tokens))
+    sp.attach(cache)
+    g = torch.Generator().manual_seed(4)
+    n = fpc * ftok
+    for c in range(chunks):
+        for step in range(3):
+            kn = torch.randn((n, H, 128), generator=g).bfloat16().to(DEV)
+            vn = torch.randn((n, H, 128), generator=g).bfloat16().to(DEV)
+            q = torch.randn((n, H, 128), generator=g).bfloat16().to(DEV)
+            cache.append(kn, vn, c * n)
+            if c == 3 and step == 1 and sink:
+                cache.save_anchor()
+                cache.rebase_anchor(1)
+            kw, vw = cache.window()
+            got = sp.forward_one(q, kw, vw).clone()
+            want = ref.forward_one(q, kw, vw)
+            dense = bf.forward_one(q, kw, vw)
+            torch.cuda.synchronize()
+            assert torch.equal(got, want), (c, step)
+            d = (got.float() - dense.float())
+            assert float((d * d).sum() / (dense.float() ** 2).sum()) < 2e-3
+    ops.DeviceStatus.check(DEV)
