@@ -117,3 +117,21 @@ def test_host_argument_errors(lib):
     end = ctypes.c_int64()
     assert lib.ss_cache_append(fake, fake, 24, 1, fake, fake, 128, 30, 1, 0, 0, 0, 4, ctypes.byref(end), None) == 1001
     assert lib.ss_cache_append(fake, fake, 24, 1, fake, fake, 100, 12, 1, 0, 0, 0, 4, ctypes.byref(end), None) == 1001
+    # INT8-QK path: page ranges past the window, null and misaligned pointers, more pages than the
+    # kernel's page list holds (4096), unsupported block size and output type
+    assert lib.ss_quant_k_pages(fake, 12, 32760, 0, 513, fake, fake, None) == 1001
+    assert lib.ss_quant_k_pages(fake, 12, 32760, 10, 5, fake, fake, None) == 1001
+    assert lib.ss_quant_k_pages(None, 12, 32760, 0, 512, fake, fake, None) == 1002
+    assert lib.ss_quant_k_pages(odd, 12, 32760, 0, 512, fake, fake, None) == 1002
+    assert lib.ss_quant_k_pages(fake, 12, 32760, 7, 7, fake, fake, None) == 0        # empty range: nothing launched
+    sz = ctypes.c_size_t(0)
+    assert lib.ss_attention_i8(fake, fake, fake, fake, fake, 12, 4680, 4096 * 64 + 1, 64, 4, 0.1, fake, 0, None, None,
+                               None, sz, None) == 1001
+    assert lib.ss_attention_i8(fake, fake, fake, fake, fake, 12, 4680, 32760, 96, 4, 0.1, fake, 0, None, None,
+                               None, sz, None) == 1001
+    assert lib.ss_attention_i8(fake, fake, fake, fake, fake, 12, 4680, 32760, 64, 4, 0.1, fake, 2, None, None,
+                               None, sz, None) == 1001
+    assert lib.ss_attention_i8(fake, fake, fake, fake, fake, 12, 4680, 32760, 64, 4, 0.1, odd, 0, None, None,
+                               None, sz, None) == 1002
+    assert lib.ss_attention_i8(fake, None, fake, fake, fake, 12, 4680, 32760, 64, 4, 0.1, fake, 0, None, None,
+                               None, sz, None) == 1002

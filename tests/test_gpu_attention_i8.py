@@ -182,3 +182,25 @@ def test_plugin_int8_stream_reuses_history_pages(local, sink, block):
             d = (got.float() - dense.float())
             assert float((d * d).sum() / (dense.float() ** 2).sum()) < 2e-3
     ops.DeviceStatus.check(DEV)
+
+
+@pytest.mark.parametrize("block,density", [(64, 0.05), (128, 0.5)])
+def test_attention_i8_config5_long_window(block, density):
+    """Config 5's longest window (98280 tokens = 1536 pages, 4680 queries): the largest page lists
+    the benched shapes give a tile, two heads, sampled query blocks against the oracle."""
+    from streaming_sparse_b200 import ops
+    Lq, Lk, H = 4680, 98280, 2
+    q, k, v = qkv(31, Lq, Lk, H)
+    wq, wk = router_weights(31, H)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    kb = oracle.nblocks(Lk, block)
+    extra = ops.budget(kb, ops.forced_count(Lq, Lk, block), density=density)
+    ids = ops.route(qd, kd, wq.to(DEV), wk.to(DEV), block=block, extra=extra, validate=True)
+    k_i8, ks = ops.quant_k_pages(kd)
+    out = ops.sparse_attention_i8(qd, k_i8, ks, vd, ids, block=block, out_dtype=torch.float32, validate=True)
+    torch.cuda.synchronize()
+    nqb = oracle.nblocks(Lq, block)
+    qblocks = sorted({0, nqb // 3, nqb // 2, nqb - 1})
+    ref, _ = oracle.attention_i8(np32(q), k_i8.cpu().numpy(), ks.cpu().numpy(), np32(v), ids.cpu().numpy(), block,
+                                 qblocks=qblocks)
+    assert_attention_close(out.cpu().numpy(), ref)
