@@ -283,7 +283,8 @@ int ss_quant_k_pages(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8,
  * ids, block, n_ids, out (0 = bf16, 1 = fp32), lse (natural log, optional) and status as in
  * ss_attention; out, q, k_i8, v 16-byte aligned; at most 4096 pages (Lk <= 262144). Replaces the
  * INT8 attention of migration/unified_router/opt23/attention.py:30-58 (`_shared`, INT8=True) and
- * the Sparge call of opt24/sparge.py:38-43 / opt24/pipeline.py:23-25. Plain (non-ring) windows.
+ * the Sparge call of opt24/sparge.py:38-43 / opt24/pipeline.py:23-25. Plain windows (ring caches:
+ * ss_attention_i8_ring).
  * workspace (optional, 256-byte aligned, ss_attention_i8_workspace_bytes bytes; NULL = none): when
  * the 128-row tiles would leave a partial wave (two CTAs per SM), each tile's step list is cut into
  * 2-4 equal pieces whose normalised partials and LSEs go to the workspace and are combined by the
@@ -294,6 +295,19 @@ int ss_attention_i8(const void *q, const int8_t *k_i8, const float *ks, const vo
                     int H, int Lq, int Lk, int block, int n_ids, float scale,
                     void *out, int out_dtype, float *lse, int *status,
                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* The INT8-QK path over a ring cache (ring arguments as in ss_router_ring): k (bf16), k_i8 and v
+ * hold the ring's physical rows (S + C + 64 each); a page is a 64-row range of window rows, which
+ * the ring keeps contiguous, so its int8 rows sit where its bf16 rows sit. Same results, bit for
+ * bit, as the plain-window calls on the same window. Replaces the same reference code as the plain
+ * entry points, over the ring cursor of local_experiments/review_v1/runtime.py:38-46. */
+int ss_quant_k_pages_ring(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8, float *ks,
+                          int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev, void *stream);
+int ss_attention_i8_ring(const void *q, const int8_t *k_i8, const float *ks, const void *v, const int32_t *ids,
+                         int H, int Lq, int Lk, int block, int n_ids, float scale,
+                         void *out, int out_dtype, float *lse, int *status,
+                         int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
+                         void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial attention results.                                             */

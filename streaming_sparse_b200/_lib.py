@@ -66,6 +66,9 @@ SIGNATURES = {
     "ss_quant_k_pages": ([_P, _I, _I, _I, _I, _P, _P, _P], _I),
     "ss_attention_i8_workspace_bytes": ([_I, _I, ctypes.POINTER(_SZ)], _I),
     "ss_attention_i8": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _SZ, _P], _I),
+    "ss_quant_k_pages_ring": ([_P, _I, _I, _I, _I, _P, _P, _I, _I, _I, _P, _P], _I),
+    "ss_attention_i8_ring": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _I, _I, _I, _P, _P, _SZ,
+                              _P], _I),
     "ss_attention_ws": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _SZ, _P], _I),
     "ss_lse_merge": ([_P, _P, _I, _I, _I, _P, _I, _P, _P], _I),
     "ss_cache_append": ([_P, _P, _I, _I, _P, _P, _I64, _I, _I, _I64, _I64, _I64, _I, ctypes.POINTER(_I64), _P], _I),

@@ -33,6 +33,7 @@ namespace i8 {
 constexpr int D = 128;
 constexpr int PAGE = 64;
 constexpr int QGROUP = 32;
+static_assert(QGROUP == 32, "a query scale group is one warp's 32 rows");
 constexpr int NSTAGE = 3;
 constexpr int MAX_PAGES = 4096;
 constexpr int NTHREADS = 192;
@@ -72,6 +73,7 @@ struct Params {
     int pieces;        // > 1: CTA z of a tile takes steps [z n / pieces, (z + 1) n / pieces)
     float *ws_o;       // pieces > 1: [pieces][Lq][H][128] fp32 normalised partials
     float *ws_lse;     //             [pieces][H][Lq] natural-log LSE (-inf: no token)
+    KvRing ring;       // k_i8 / v as a ring cache (C = 0: a plain window); a page is one 64-row range
 };
 
 // D[tmem] (+)= A[smem] * B[smem], kind::i8 (s8 inputs, s32 accumulate)
@@ -411,6 +413,7 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
         // ---------------- TMA producer ----------------
         int issued = 0;
         bool ok = true;
+        const KvRing rg = p.ring.resolved();
         for (int s = 0; s < n; ++s) {
             const int st = s % NSTAGE;
             if (s >= NSTAGE) {
@@ -421,9 +424,10 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
             if (elect_one()) {
                 const uint32_t dst = sbase + OFF_STAGE + (uint32_t)st * STAGE_BYTES;
                 mbar_arrive_expect_tx(bar(KV_FULL + st), STAGE_BYTES);
-                tma_load_2d(dst, &tm_k, h * D, page * PAGE, bar(KV_FULL + st));
-                tma_load_2d(dst + K_BYTES, &tm_v, h * D, page * PAGE, bar(KV_FULL + st));
-                tma_load_2d(dst + K_BYTES + V_REGION, &tm_v, h * D + 64, page * PAGE, bar(KV_FULL + st));
+                const int y = rg.sub_row(page * PAGE);   // the page's first physical row
+                tma_load_2d(dst, &tm_k, h * D, y, bar(KV_FULL + st));
+                tma_load_2d(dst + K_BYTES, &tm_v, h * D, y, bar(KV_FULL + st));
+                tma_load_2d(dst + K_BYTES + V_REGION, &tm_v, h * D + 64, y, bar(KV_FULL + st));
             }
             __syncwarp();
             issued = s + 1;
@@ -497,11 +501,12 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
 // dims 32 (t%4) .. +32.
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
-quant_k_pages_kernel(const __nv_bfloat16 *k, int H, int Lk, int p0, int npages, int8_t *ki, float *ks) {
+quant_k_pages_kernel(const __nv_bfloat16 *k, int H, int Lk, int p0, int npages, int8_t *ki, float *ks, KvRing ring) {
     __shared__ float red[8];
     const int pg = p0 + blockIdx.x, h = blockIdx.y;
-    const int t = threadIdx.x, row = pg * PAGE + (t >> 2), d0 = 32 * (t & 3);
-    const bool live = row < Lk;
+    const int t = threadIdx.x, d0 = 32 * (t & 3);
+    const bool live = pg * PAGE + (t >> 2) < Lk;
+    const int row = ring.resolved().sub_row(pg * PAGE) + (t >> 2);   // physical row (a ring keeps pages contiguous)
     float x[32];
     const uint4 *src = reinterpret_cast<const uint4 *>(k + ((size_t)(live ? row : 0) * H + h) * D + d0);
 #pragma unroll
@@ -588,17 +593,38 @@ int encode_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64
 
 }  // namespace ss
 
-extern "C" int ss_quant_k_pages(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8, float *ks, void *stream) {
+namespace ss {
+
+static int quant_launch(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8, float *ks, cudaStream_t stream,
+                        KvRing ring) {
     if (!k || !k_i8 || !ks) return SS_ERR_POINTER;
-    const int npages = (Lk + ss::i8::PAGE - 1) / ss::i8::PAGE;
+    const int npages = (Lk + i8::PAGE - 1) / i8::PAGE;
     if (H <= 0 || Lk <= 0 || p0 < 0 || p1 > npages || p0 > p1 || H > 65535) return SS_ERR_SHAPE;
-    if ((long)Lk * H * ss::i8::D >= (1L << 31)) return SS_ERR_SHAPE;
+    if (ring_check(ring, Lk) || ring.phys_rows(Lk) * H * i8::D >= (1L << 31)) return SS_ERR_SHAPE;
     if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(k_i8)) & 15u) return SS_ERR_POINTER;
     if (reinterpret_cast<uintptr_t>(ks) & 3u) return SS_ERR_POINTER;
     if (p0 == p1) return 0;
-    ss::i8::quant_k_pages_kernel<<<dim3((unsigned)(p1 - p0), (unsigned)H), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __nv_bfloat16 *>(k), H, Lk, p0, npages, k_i8, ks);
+    i8::quant_k_pages_kernel<<<dim3((unsigned)(p1 - p0), (unsigned)H), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(k), H, Lk, p0, npages, k_i8, ks, ring);
     return (int)cudaGetLastError();
+}
+
+}  // namespace ss
+
+extern "C" int ss_quant_k_pages(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8, float *ks, void *stream) {
+    return ss::quant_launch(k, H, Lk, p0, p1, k_i8, ks, static_cast<cudaStream_t>(stream), ss::KvRing());
+}
+
+extern "C" int ss_quant_k_pages_ring(const void *k, int H, int Lk, int p0, int p1, int8_t *k_i8, float *ks,
+                                     int ring_sink, int ring_cap, int ring_head, const int *ring_head_dev,
+                                     void *stream) {
+    ss::KvRing ring;
+    ring.S = ring_sink;
+    ring.C = ring_cap;
+    ring.head = ring_head;
+    ring.head_dev = ring_head_dev;
+    if (ring_cap <= 0) return SS_ERR_SHAPE;
+    return ss::quant_launch(k, H, Lk, p0, p1, k_i8, ks, static_cast<cudaStream_t>(stream), ring);
 }
 
 extern "C" int ss_attention_i8_workspace_bytes(int H, int Lq, size_t *bytes) {
@@ -613,15 +639,20 @@ extern "C" int ss_attention_i8_workspace_bytes(int H, int Lq, size_t *bytes) {
     return 0;
 }
 
-extern "C" int ss_attention_i8(const void *q, const int8_t *k_i8, const float *ks, const void *v, const int32_t *ids,
+namespace ss {
+
+static int attention_i8_launch(const void *q, const int8_t *k_i8, const float *ks, const void *v, const int32_t *ids,
                                int H, int Lq, int Lk, int block, int n_ids, float scale, void *out, int out_dtype,
-                               float *lse, int *status, void *workspace, size_t workspace_bytes, void *stream) {
+                               float *lse, int *status, void *workspace, size_t workspace_bytes, void *stream,
+                               KvRing ring) {
     using namespace ss::i8;
     if (!q || !k_i8 || !ks || !v || !ids || !out) return SS_ERR_POINTER;
     if (H <= 0 || Lq <= 0 || Lk <= 0 || n_ids <= 0 || (block != 64 && block != 128) || H > 65535) return SS_ERR_SHAPE;
     if (out_dtype != 0 && out_dtype != 1) return SS_ERR_SHAPE;
     const int npages = (Lk + PAGE - 1) / PAGE;
-    if (npages > MAX_PAGES || (long)Lq * H * D >= (1L << 31) || (long)Lk * H * D >= (1L << 31)) return SS_ERR_SHAPE;
+    if (npages > MAX_PAGES || (long)Lq * H * D >= (1L << 31)) return SS_ERR_SHAPE;
+    if (ring_check(ring, Lk) || ring.phys_rows(Lk) * H * D >= (1L << 31)) return SS_ERR_SHAPE;
+    const uint64_t kv_rows = (uint64_t)ring.phys_rows(Lk);
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_i8) | reinterpret_cast<uintptr_t>(v) |
          reinterpret_cast<uintptr_t>(out)) & 15u)
         return SS_ERR_POINTER;
@@ -649,6 +680,7 @@ extern "C" int ss_attention_i8(const void *q, const int8_t *k_i8, const float *k
     prm.npages = npages;
     prm.out_fp32 = out_dtype;
     prm.c = (float)((double)scale * 1.4426950408889634);
+    prm.ring = ring;
     const unsigned ntiles = (unsigned)((Lq + 127) / 128);
     int P = workspace ? ss::i8_pieces((long)ntiles * H, ss::g_i8_nsm[device]) : 1;
     if (P > 1 && workspace_bytes < ss::i8_ws_bytes(P, H, Lq)) return SS_ERR_WORKSPACE;
@@ -658,13 +690,37 @@ extern "C" int ss_attention_i8(const void *q, const int8_t *k_i8, const float *k
     prm.ws_lse = P > 1 ? prm.ws_o + (size_t)P * Lq * H * D : nullptr;
 
     CUtensorMap tk, tv;
-    if (ss::encode_tmap_2d_u8(&tk, k_i8, (uint64_t)H * D, (uint64_t)Lk, (uint64_t)H * D, 128, PAGE))
+    if (ss::encode_tmap_2d_u8(&tk, k_i8, (uint64_t)H * D, kv_rows, (uint64_t)H * D, 128, PAGE))
         return SS_ERR_DRIVER;
-    if (ss::encode_tmap_2d_bf16(&tv, v, (uint64_t)H * D, (uint64_t)Lk, (uint64_t)H * D * 2, 64, PAGE))
+    if (ss::encode_tmap_2d_bf16(&tv, v, (uint64_t)H * D, kv_rows, (uint64_t)H * D * 2, 64, PAGE))
         return SS_ERR_DRIVER;
     attention_i8_kernel<<<dim3(ntiles, (unsigned)H, (unsigned)P), NTHREADS, SMEM_BYTES,
                           static_cast<cudaStream_t>(stream)>>>(tk, tv, prm);
     e = cudaGetLastError();
     if (e != cudaSuccess || P == 1) return (int)e;
     return ss_lse_merge(prm.ws_o, prm.ws_lse, P, H, Lq, out, out_dtype, lse, stream);
+}
+
+}  // namespace ss
+
+extern "C" int ss_attention_i8(const void *q, const int8_t *k_i8, const float *ks, const void *v, const int32_t *ids,
+                               int H, int Lq, int Lk, int block, int n_ids, float scale, void *out, int out_dtype,
+                               float *lse, int *status, void *workspace, size_t workspace_bytes, void *stream) {
+    return ss::attention_i8_launch(q, k_i8, ks, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status,
+                                   workspace, workspace_bytes, stream, ss::KvRing());
+}
+
+extern "C" int ss_attention_i8_ring(const void *q, const int8_t *k_i8, const float *ks, const void *v,
+                                    const int32_t *ids, int H, int Lq, int Lk, int block, int n_ids, float scale,
+                                    void *out, int out_dtype, float *lse, int *status, int ring_sink, int ring_cap,
+                                    int ring_head, const int *ring_head_dev, void *workspace, size_t workspace_bytes,
+                                    void *stream) {
+    ss::KvRing ring;
+    ring.S = ring_sink;
+    ring.C = ring_cap;
+    ring.head = ring_head;
+    ring.head_dev = ring_head_dev;
+    if (ring_cap <= 0) return SS_ERR_SHAPE;
+    return ss::attention_i8_launch(q, k_i8, ks, v, ids, H, Lq, Lk, block, n_ids, scale, out, out_dtype, lse, status,
+                                   workspace, workspace_bytes, stream, ring);
 }

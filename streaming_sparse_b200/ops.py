@@ -432,15 +432,22 @@ def quant_pages(Lk: int) -> int:
 
 
 def quant_k_pages(k, *, p0: int = 0, p1: int | None = None, k_i8: torch.Tensor | None = None,
-                  ks: torch.Tensor | None = None):
+                  ks: torch.Tensor | None = None, ring: "Ring | None" = None, Lk: int | None = None):
     """Quantise key pages [p0, p1) of k [Lk,H,128] bf16 to int8 (``ss_quant_k_pages``).
 
     Returns (k_i8 [Lk,H,128] int8, ks [H,ceil(Lk/64)] fp32); pass the previous buffers to update
     only some pages (history pages once per commit, the current chunk's pages per call, as
     ``Quantized.history`` / ``.current`` of migration/unified_router/opt23/attention.py:16-28).
+    ``ring`` (with ``Lk``, the window's rows): k is a ring cache's physical rows and k_i8 gets the
+    same rows (``ss_quant_k_pages_ring``).
     """
     k = _tokens(k, "k")
-    Lk, H, _ = k.shape
+    _require((ring is None) == (Lk is None), "Lk goes with ring")
+    H = k.shape[1]
+    if ring is None:
+        Lk = k.shape[0]
+    else:
+        _require(k.shape[0] == ring.phys_rows(), "k rows do not match the ring")
     npg = quant_pages(Lk)
     p1 = npg if p1 is None else p1
     if k_i8 is None:
@@ -449,7 +456,11 @@ def quant_k_pages(k, *, p0: int = 0, p1: int | None = None, k_i8: torch.Tensor |
         ks = torch.empty((H, npg), dtype=torch.float32, device=k.device)
     _require(k_i8.shape == k.shape and k_i8.dtype == torch.int8 and k_i8.is_contiguous(), "bad k_i8 buffer")
     _require(ks.shape == (H, npg) and ks.dtype == torch.float32 and ks.is_contiguous(), "bad ks buffer")
-    rc = lib().ss_quant_k_pages(_p(k), H, Lk, p0, p1, _p(k_i8), _p(ks), _stream(k.device))
+    if ring is None:
+        rc = lib().ss_quant_k_pages(_p(k), H, Lk, p0, p1, _p(k_i8), _p(ks), _stream(k.device))
+    else:
+        rc = lib().ss_quant_k_pages_ring(_p(k), H, Lk, p0, p1, _p(k_i8), _p(ks), ring.sink, ring.cap, ring.head,
+                                         ring.dev_ptr(), _stream(k.device))
     check(rc, "ss_quant_k_pages")
     return k_i8, ks
 
@@ -464,16 +475,22 @@ def attention_i8_workspace_bytes(H: int, Lq: int) -> int:
 def sparse_attention_i8(q, k_i8, ks, v, ids, *, block: int = 64, scale: float | None = None,
                         out_dtype: torch.dtype = torch.bfloat16, return_lse: bool = False,
                         out: torch.Tensor | None = None, lse: torch.Tensor | None = None, validate: bool = False,
-                        workspace: Workspace | None = None, split: bool = True):
+                        workspace: Workspace | None = None, split: bool = True, ring: "Ring | None" = None,
+                        Lk: int | None = None):
     """INT8-QK block-sparse attention (``ss_attention_i8``): ``sparse_attention`` with the scores
     taken from int8 Q (32-row groups, quantised in the kernel) and int8 K pages (``quant_k_pages``),
     as the reference's INT8 path (migration/unified_router/opt23/attention.py:30-58). With ``split``
     (default) a problem that would leave a partial wave cuts its tiles into equal pieces merged by
-    LSE (workspace from ``workspace``)."""
+    LSE (workspace from ``workspace``). ``ring`` (with ``Lk``): k_i8 and v are a ring cache's
+    physical rows (``ss_attention_i8_ring``)."""
     q = _tokens(q, "q")
     v = _tokens(v, "v")
     Lq, H, D = q.shape
-    Lk = v.shape[0]
+    _require((ring is None) == (Lk is None), "Lk goes with ring")
+    if ring is None:
+        Lk = v.shape[0]
+    else:
+        _require(v.shape[0] == ring.phys_rows(), "v rows do not match the ring")
     _require(k_i8.is_cuda and k_i8.dtype == torch.int8 and k_i8.shape == v.shape and k_i8.is_contiguous(),
              "k_i8 must be int8 CUDA [Lk,H,128] like v")
     _require(ks.is_cuda and ks.dtype == torch.float32 and ks.shape == (H, quant_pages(Lk)) and ks.is_contiguous(),
@@ -491,9 +508,15 @@ def sparse_attention_i8(q, k_i8, ks, v, ids, *, block: int = 64, scale: float | 
     status = DeviceStatus.word(q.device)
     nws = attention_i8_workspace_bytes(H, Lq) if split else 0
     ws = _ws(workspace, q.device).tensor("attention_i8_split", (nws,), q.device, torch.uint8) if nws else None
-    rc = lib().ss_attention_i8(_p(q), _p(k_i8), _p(ks), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale,
-                               _p(out), 1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
-                               _p(status), _p(ws), nws, _stream(q.device))
+    if ring is None:
+        rc = lib().ss_attention_i8(_p(q), _p(k_i8), _p(ks), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2], scale,
+                                   _p(out), 1 if out_dtype == torch.float32 else 0, _p(lse) if return_lse else None,
+                                   _p(status), _p(ws), nws, _stream(q.device))
+    else:
+        rc = lib().ss_attention_i8_ring(_p(q), _p(k_i8), _p(ks), _p(v), _p(ids), H, Lq, Lk, block, ids.shape[2],
+                                        scale, _p(out), 1 if out_dtype == torch.float32 else 0,
+                                        _p(lse) if return_lse else None, _p(status), ring.sink, ring.cap, ring.head,
+                                        ring.dev_ptr(), _p(ws), nws, _stream(q.device))
     check(rc, "ss_attention_i8")
     if validate:
         DeviceStatus.check(q.device)

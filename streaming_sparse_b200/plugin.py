@@ -30,8 +30,8 @@ class RouterConfig:
     ``rule`` picks how ``density`` becomes a count (see ``ops.budget``). ``fast`` scores the blocks
     on the tensor cores (``ops.route(..., fast=True)``; same ids, proj_dim 32 or 64). ``int8`` runs
     the attention on the INT8-QK path (``ops.sparse_attention_i8``; the reference's
-    ``attention(..., int8=True)``, migration/unified_router/opt23/attention.py:60-69), plain
-    (non-ring) windows only.
+    ``attention(..., int8=True)``, migration/unified_router/opt23/attention.py:60-69), on plain
+    windows and ring caches.
     """
 
     block: int = 64
@@ -117,7 +117,9 @@ class SparseAttention:
         once per history tag and window length, as the reference's ``Quantized.history`` runs once
         per commit (migration/unified_router/opt23/pipeline.py); the current chunk's pages on every
         call."""
-        Lq, Lk, H = q.shape[0], k.shape[0], k.shape[1]
+        ring = cache.ring if cache is not None and cache.ring_mode else None
+        Lq, H = q.shape[0], k.shape[1]
+        Lk = cache.window_rows() if ring is not None else k.shape[0]
         npg = ops.quant_pages(Lk)
         if cache is None:
             k_i8 = self.workspace.tensor("k_i8", tuple(k.shape), k.device, torch.int8)
@@ -128,8 +130,11 @@ class SparseAttention:
         if ent is None or ent[0].shape != k.shape:
             ent = self._i8[id(cache)] = [torch.empty(k.shape, dtype=torch.int8, device=k.device),
                                          torch.empty((H, npg), dtype=torch.float32, device=k.device), None]
+        if ent[1].shape != (H, npg):
+            ent[1] = torch.empty((H, npg), dtype=torch.float32, device=k.device)
+            ent[2] = None
         p0 = (Lk - Lq) // ops.PAGE_TOKENS if ent[2] == key else 0
-        ops.quant_k_pages(k, p0=p0, k_i8=ent[0], ks=ent[1])
+        ops.quant_k_pages(k, p0=p0, k_i8=ent[0], ks=ent[1], ring=ring, Lk=Lk if ring is not None else None)
         ent[2] = key
         return ent[0], ent[1]
 
@@ -155,11 +160,10 @@ class SparseAttention:
         self.last_ids = ids
         self.calls += 1
         if self.config.int8:
-            if ring is not None:
-                raise ValueError("the INT8-QK path takes plain (non-ring) KV windows")
             k_i8, ks = self.int8_keys(q, k, cache)
             return ops.sparse_attention_i8(q, k_i8, ks, v, ids, block=self.config.block, out=out,
-                                           validate=self.validate, workspace=self.workspace)
+                                           validate=self.validate, workspace=self.workspace, ring=ring,
+                                           Lk=Lk if ring is not None else None)
         return ops.sparse_attention(q, k, v, ids, block=self.config.block, out=out, validate=self.validate, ring=ring,
                                     Lk=Lk if ring is not None else None)
 

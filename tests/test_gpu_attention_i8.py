@@ -204,3 +204,39 @@ def test_attention_i8_config5_long_window(block, density):
     ref, _ = oracle.attention_i8(np32(q), k_i8.cpu().numpy(), ks.cpu().numpy(), np32(v), ids.cpu().numpy(), block,
                                  qblocks=qblocks)
     assert_attention_close(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("block", [64, 128])
+def test_plugin_int8_ring_cache_equals_shifting_cache(block):
+    """RouterConfig(int8=True) streaming through a ring-buffer KVCache (a roll moves the head) and
+    through the shifting cache: the int8 keys, scales and outputs are the same, bit for bit, at
+    every call, over rolls of the window."""
+    from streaming_sparse_b200 import ops
+    from streaming_sparse_b200.cache import KVCache
+    from streaming_sparse_b200.plugin import RouterConfig, SparseAttention
+    H, ftok, local, sink = 2, 300, 5, 1
+    cfg = RouterConfig(block=block, density=0.3, rule="rest", sink_tokens=sink * ftok, int8=True)
+    wq, wk = (w.to(DEV) for w in router_weights(16, H))
+    caches = [KVCache(local * ftok, H, 128, frame_tokens=ftok, local_attn_size=local, sink_size=sink, device=DEV,
+                      ring=r) for r in (False, True)]
+    sps = [SparseAttention(wq, wk, cfg) for _ in caches]
+    for sp, cache in zip(sps, caches):
+        sp.attach(cache)
+    g = torch.Generator().manual_seed(2)
+    n = 2 * ftok
+    for c in range(8):
+        for _ in range(2):
+            kn = torch.randn((n, H, 128), generator=g).bfloat16().to(DEV)
+            vn = torch.randn((n, H, 128), generator=g).bfloat16().to(DEV)
+            q = torch.randn((n, H, 128), generator=g).bfloat16().to(DEV)
+            outs = []
+            for sp, cache in zip(sps, caches):
+                cache.append(kn, vn, c * n)
+                kw, vw = cache.window()
+                outs.append(sp(q[None], kw[None], vw[None]))
+            torch.cuda.synchronize()
+            assert torch.equal(sps[0].last_ids, sps[1].last_ids)
+            assert torch.equal(outs[0], outs[1]), c
+            assert torch.equal(sps[0]._i8[id(caches[0])][1], sps[1]._i8[id(caches[1])][1])   # page scales
+    assert caches[1].ring.head != 0
+    ops.DeviceStatus.check(DEV)
