@@ -12,7 +12,10 @@ gives it (opt24/sparge.py:41 ``self.v=self.pv.half()``): the interpreter's P.V p
 handle bf16. V is drawn in bf16 (tiny values zeroed), so its values are exact in both types. Pages are made window-global by passing SEG = (number of pages) * 64, so page p covers
 tokens [64p, 64p + 64), as in this library.
 
-The reference is read, never modified, and is not needed at test time (the .npz is committed).
+Two fixtures: int8_qk.npz (64-token routing blocks, one page each) and int8_qk_b128.npz (the same
+keys and values, 128-token routing blocks of two pages each, 256 queries).
+
+The reference is read, never modified, and is not needed at test time (the .npz files are committed).
 """
 import argparse
 import importlib
@@ -80,6 +83,26 @@ def main():
         k=k.float().numpy(), v=v.float().numpy(), q=q.float().numpy(), k_i8=ki.numpy(), ks=ks.numpy(),
         page_lists=lists, tiles=tiles, out=out.numpy(), group=np.int32(G))
     print("wrote int8_qk.npz", out.abs().mean().item())
+
+    # 128-token routing blocks: block id b covers pages 2b and 2b + 1 (the last block's second page
+    # lies past the window and is dropped), so a 128-row query block's page list is its blocks'
+    # pages; its four 32-row tiles share that list
+    g2 = torch.Generator().manual_seed(128)
+    N2 = 256
+    q2 = torch.randn((H, N2, 128), generator=g2).bfloat16()
+    blocks = np.array([[[0, 2], [1, 2]], [[1, 2], [0, 2]]], np.int32)        # [H, 2 query blocks, 2]: 3 pages each
+    plists = np.zeros((H, 2, 3), np.int32)
+    for h in range(H):
+        for b in range(2):
+            pg = [2 * x + u for x in blocks[h, b] for u in range(2) if 2 * x + u < pages]
+            plists[h, b] = pg
+    tiles2 = np.repeat(plists, 4, axis=1)                                       # [H, 8, 3]
+    out2 = torch.zeros((H, N2, 128), dtype=torch.float32)
+    att._shared[(N2 // G, H, 1)](q2, ki, v, ks, torch.from_numpy(tiles2), out2, out2, N2, NK, pages, G, N2 // G, 3, 1,
+                                 True, SEG, num_warps=4)
+    np.savez_compressed(os.path.join(OUT, "int8_qk_b128.npz"), q=q2.float().numpy(), block_lists=blocks,
+                        tiles=tiles2, out=out2.numpy())
+    print("wrote int8_qk_b128.npz", out2.abs().mean().item())
 
 
 if __name__ == "__main__":

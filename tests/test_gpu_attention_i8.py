@@ -78,6 +78,18 @@ def test_golden_reference_kernel():
     assert err.max() <= 1e-2 and err.mean() <= 1e-3, (err.max(), err.mean())
 
 
+def test_golden_reference_kernel_128_token_blocks():
+    """The reference kernel's output with 128-token routing blocks (int8_qk_b128.npz)."""
+    g, g2 = np.load(GOLD), np.load(GOLD.replace("int8_qk.npz", "int8_qk_b128.npz"))
+    k = torch.from_numpy(g["k"].transpose(1, 0, 2).copy()).bfloat16()
+    v = torch.from_numpy(g["v"].transpose(1, 0, 2).copy()).bfloat16()
+    q = torch.from_numpy(g2["q"].transpose(1, 0, 2).copy()).bfloat16()
+    out, _, ki, ks = _attend_i8(q, k, v, g2["block_lists"], 128, torch.float32)
+    assert np.array_equal(ki, g["k_i8"].transpose(1, 0, 2))
+    err = np.abs(out - g2["out"].transpose(1, 0, 2))
+    assert err.max() <= 1e-2 and err.mean() <= 1e-3, (err.max(), err.mean())
+
+
 @pytest.mark.parametrize("Lq,Lk,H,block,n,pad,out_dtype", [
     (100, 333, 2, 64, 3, 2, torch.bfloat16),      # partial tile, partial last page, -1 padding
     (256, 1024, 3, 64, 7, 0, torch.float32),      # two full tiles, fp32 out

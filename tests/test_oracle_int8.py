@@ -50,3 +50,16 @@ def test_quant_rounds_half_to_even():
     xi, s = oracle.quant_rows(x, 32)
     assert s[0, 0] == 1.0
     assert list(xi[0, 0, :6]) == [127, 0, 2, 2, 0, -2]
+
+
+def test_128_token_blocks_match_reference_kernel():
+    """int8_qk_b128.npz: the same int8 keys, 128-token routing blocks (two pages per block id, the
+    window's last block one page): the kernel loop restatement and the library-layout oracle with
+    block = 128 against the reference kernel's output."""
+    g, g2 = _g(), np.load(GOLD.replace("int8_qk.npz", "int8_qk_b128.npz"))
+    out = oracle.shared_i8_tiles(g2["q"], g["k_i8"], g["ks"], g["v"], g2["tiles"], int(g["group"]))
+    assert np.abs(out - g2["out"]).max() <= 2e-6
+    q, k_i8, v = g2["q"].transpose(1, 0, 2), g["k_i8"].transpose(1, 0, 2), g["v"].transpose(1, 0, 2)
+    ref, _ = oracle.attention_i8(q, k_i8, g["ks"], v, g2["block_lists"], 128)
+    err = np.abs(ref - g2["out"].transpose(1, 0, 2))
+    assert err.max() <= 2e-3 and err.mean() <= 2e-4
