@@ -286,9 +286,15 @@ attention_i8_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_const
                 const float tc = __fmul_rn(__fmul_rn(qs, ksv), p.c);
                 int smax = INT_MIN;
                 if (nvalid == PAGE) {   // every page but a window's last: no bounds in the loops
+                    int m0 = INT_MIN, m1 = INT_MIN, m2 = INT_MIN, m3 = INT_MIN;   // four independent chains
 #pragma unroll
-                    for (int j = 0; j < 63; j += 2)
-                        smax = __vimax3_s32(smax, __float_as_int(sv[j]), __float_as_int(sv[j + 1]));
+                    for (int j = 0; j < 64; j += 8) {
+                        m0 = __vimax3_s32(m0, __float_as_int(sv[j]), __float_as_int(sv[j + 1]));
+                        m1 = __vimax3_s32(m1, __float_as_int(sv[j + 2]), __float_as_int(sv[j + 3]));
+                        m2 = __vimax3_s32(m2, __float_as_int(sv[j + 4]), __float_as_int(sv[j + 5]));
+                        m3 = __vimax3_s32(m3, __float_as_int(sv[j + 6]), __float_as_int(sv[j + 7]));
+                    }
+                    smax = max(__vimax3_s32(m0, m1, m2), m3);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 64; ++j)
