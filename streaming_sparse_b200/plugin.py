@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import importlib
 import math
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -73,7 +74,9 @@ class SparseAttention:
         self.last_ids = None
         self.calls = 0
         self._caches = {}           # k-cache storage address -> attached KVCache
-        self._i8 = {}               # id(KVCache) -> [k_i8, ks, (history tag, Lk)] of the INT8-QK path
+        # KVCache -> [k_i8, ks, (history tag, Lk)] of the INT8-QK path, held weakly: a cache that is
+        # gone takes its entry along, so a new cache at the same address starts from nothing
+        self._i8 = weakref.WeakKeyDictionary()
 
     def attach(self, cache) -> None:
         """Let calls whose k is this ``KVCache``'s visible window reuse its history's pooled key
@@ -126,9 +129,9 @@ class SparseAttention:
             ks = self.workspace.tensor("k_i8_scales", (H, npg), k.device, torch.float32)
             return ops.quant_k_pages(k, k_i8=k_i8, ks=ks)
         key = (cache.history_tag(), Lk)
-        ent = self._i8.get(id(cache))
+        ent = self._i8.get(cache)
         if ent is None or ent[0].shape != k.shape:
-            ent = self._i8[id(cache)] = [torch.empty(k.shape, dtype=torch.int8, device=k.device),
+            ent = self._i8[cache] = [torch.empty(k.shape, dtype=torch.int8, device=k.device),
                                          torch.empty((H, npg), dtype=torch.float32, device=k.device), None]
         if ent[1].shape != (H, npg):
             ent[1] = torch.empty((H, npg), dtype=torch.float32, device=k.device)

@@ -249,6 +249,6 @@ def test_plugin_int8_ring_cache_equals_shifting_cache(block):
             torch.cuda.synchronize()
             assert torch.equal(sps[0].last_ids, sps[1].last_ids)
             assert torch.equal(outs[0], outs[1]), c
-            assert torch.equal(sps[0]._i8[id(caches[0])][1], sps[1]._i8[id(caches[1])][1])   # page scales
+            assert torch.equal(sps[0]._i8[caches[0]][1], sps[1]._i8[caches[1]][1])   # page scales
     assert caches[1].ring.head != 0
     ops.DeviceStatus.check(DEV)
